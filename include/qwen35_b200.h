@@ -1,0 +1,279 @@
+/*
+ * qwen35_b200.h — C ABI of the B200 (sm_100a) Qwen3.5 fused inference hot path.
+ *
+ * Drop-in boundary for the reference project's fused operator layer,
+ * qwen35_fused/kernels.py, and for the decode/prefill loop its integration patches into the
+ * Hugging Face model (qwen35_fused/integration.py, qwen35_fused/graph.py). Each entry point
+ * names the reference interface it replaces as `file:line`.
+ *
+ * Conventions (mirroring kernels.py:16-21 and the wrappers):
+ *   - every tensor argument is a device pointer to a contiguous row-major buffer;
+ *     "bf16" means IEEE bfloat16 stored as uint16_t;
+ *   - `stream` is a cudaStream_t (NULL = legacy default stream); work is enqueued on it,
+ *     nothing synchronises the host, and no entry point allocates device memory:
+ *     scratch ("workspace") is caller-provided, sized by the matching *_workspace_size();
+ *   - lengths and positions that change from step to step are read from device int64
+ *     scalars, so a captured CUDA graph stays valid across steps (graph.py:50-79);
+ *   - return value: Q35_OK, or an error code with a message from q35_last_error().
+ *     Q35_EINVAL is what the reference reports as ValueError (bad shape / layout).
+ */
+#ifndef QWEN35_B200_H
+#define QWEN35_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  Q35_OK = 0,
+  Q35_EINVAL = 1,   /* invalid argument (reference: ValueError) */
+  Q35_ECUDA = 2,    /* CUDA launch / runtime error */
+  Q35_ETIMEOUT = 3, /* a bounded device-side wait gave up */
+  Q35_ENOTSUP = 4   /* shape outside what the kernels are built for */
+};
+
+/* Message of the last failing call on this host thread. */
+const char* q35_last_error(void);
+/* ABI version of this library (bumped on any signature change). */
+int q35_abi_version(void);
+
+/* ---------------------------------------------------------------- norms & activations */
+
+/* kernels.py:44 rms_norm — out = bf16(x * rsqrt(mean(x^2) + eps) * (1 + w)), per row. */
+int q35_rms_norm(const void* x, const void* weight, void* out, int64_t rows, int64_t width,
+                 float eps, void* stream);
+
+/* kernels.py:85 residual_add_rms_norm — r' = bf16(r + u); n = rms_norm(r'). */
+int q35_residual_add_rms_norm(const void* residual, const void* update, const void* weight,
+                              void* residual_out, void* norm_out, int64_t rows, int64_t width,
+                              float eps, void* stream);
+
+/* kernels.py:139 gated_rms_norm — bf16(bf16(bf16(norm(x)) * w) * silu(gate)), plain weight. */
+int q35_gated_rms_norm(const void* x, const void* gate, const void* weight, void* out,
+                       int64_t rows, int64_t width, float eps, void* stream);
+
+/* kernels.py:170 silu_and_mul — packed [rows, 2*width] -> [rows, width]. */
+int q35_silu_and_mul(const void* packed, void* out, int64_t rows, int64_t width, void* stream);
+
+/* kernels.py:276 sigmoid_mul — bf16(x * bf16(sigmoid(gate))). */
+int q35_sigmoid_mul(const void* x, const void* gate, void* out, int64_t n, void* stream);
+
+/* kernels.py:312 attention_gate_mul — x [rows, hidden] times sigmoid of the gate half of each
+ * packed Q|gate head block (packed row stride `packed_stride`). */
+int q35_attention_gate_mul(const void* x, const void* packed, void* out, int64_t rows,
+                           int64_t hidden, int64_t packed_stride, int64_t head_dim, void* stream);
+
+/* Embedding gather (integration.py:402-403, embed_tokens): out[i] = table[ids[i]]. */
+int q35_embedding(const int64_t* ids, const void* table, void* out, int64_t n, int64_t vocab,
+                  int64_t width, void* stream);
+
+/* ---------------------------------------------------------------- decode GEMVs */
+
+/* kernels.py:232 ppu_swiglu_gemv — x [k] times packed [gate; up] weight [2*n_out, k]:
+ * out[n] = bf16(bf16(silu(bf16(g_n))) * bf16(u_n)). */
+int q35_swiglu_gemv(const void* x, const void* packed_weight, void* out, int64_t n_out,
+                    int64_t k, void* stream);
+
+/* Fused batch-1 decode GEMV used by the decoder loop (integration.py:245, 298, 183-185, 272,
+ * 359 as F.linear / ppu_swiglu_gemv, with the residual_add_rms_norm of :478-499 folded in).
+ * Prologue builds the input vector in shared memory; epilogue writes the result. */
+enum {
+  Q35_PRO_PLAIN = 0, /* x = input[k] */
+  Q35_PRO_NORM = 1,  /* x = rms_norm(input[k], norm_weight) */
+  Q35_PRO_EMBED = 2  /* x = rms_norm(embed[token[0]], norm_weight); the raw row -> resid_out */
+};
+enum {
+  Q35_EPI_STORE = 0,    /* out[n] = bf16(y_n) */
+  Q35_EPI_RESIDUAL = 1, /* resid_out[n] = bf16(resid_out[n] + bf16(y_n)) (in place) */
+  Q35_EPI_SWIGLU = 2    /* rows n and n + n_out are gate/up: out[n] = SwiGLU */
+};
+typedef struct {
+  const void* weight;       /* bf16 [rows, k], or int8 [rows, k] when int8 != 0 */
+  const float* w_scale;     /* int8 only: fp32 per-row scale [rows] */
+  const void* input;        /* bf16 [k] (PLAIN / NORM) */
+  const void* norm_weight;  /* bf16 [k] (NORM / EMBED) */
+  const int64_t* token;     /* EMBED: device token id */
+  const void* embed;        /* EMBED: bf16 [vocab, k] */
+  void* resid_out;          /* EMBED: receives the raw embedding row; RESIDUAL: updated in place */
+  void* out;                /* bf16 [n_out] (STORE / SWIGLU) */
+  int64_t n_out;            /* outputs (rows, or rows/2 for SWIGLU) */
+  int64_t k;                /* reduction length (fast paths for 2048 and 6144) */
+  int64_t vocab;            /* EMBED: rows of embed; token ids are clamped into [0, vocab) */
+  int32_t prologue;
+  int32_t epilogue;
+  int32_t int8;             /* 1 = A8W8: per-token int8 activation, int32 accumulation */
+  float eps;
+} q35_gemv_desc;
+int q35_gemv(const q35_gemv_desc* d, void* stream);
+
+/* kernels.py:1146 lm_head_argmax — token[b] = argmax_v bf16(hidden[b] . weight[v]), lowest v on
+ * ties, in one launch. With norm_weight != NULL the hidden row is rms_norm'ed first (the final
+ * norm of integration.py:494-499 fused in). Workspace: q35_lm_head_workspace_size(batch) bytes,
+ * zeroed once by the caller; every call leaves it zeroed again. */
+size_t q35_lm_head_workspace_size(int64_t batch);
+int q35_lm_head_argmax(const void* hidden, const void* norm_weight, const void* weight,
+                       int64_t* token_out, int64_t batch, int64_t vocab, int64_t hidden_size,
+                       float eps, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------- A8W8 */
+
+/* explore_runtime_quantization.py:143-155 (weights) and :167-172 (activations): per-row
+ * symmetric int8, scale = amax|x| / 127 (1 for an all-zero row), q = clamp(rne(x / s), +-127). */
+int q35_quantize_rows(const void* x, int8_t* q, float* scale, int64_t rows, int64_t width,
+                      void* stream);
+
+/* explore_runtime_quantization.py:161-181 (PPUA8W8Linear.forward with acext int8_gemm):
+ * out = bf16((float(qx @ qw^T) * s_x) * s_w), qx/s_x from q35_quantize_rows(x).
+ * Workspace: q35_a8w8_linear_workspace_size(m, k) bytes. */
+size_t q35_a8w8_linear_workspace_size(int64_t m, int64_t k);
+int q35_a8w8_linear(const void* x, const int8_t* qw, const float* w_scale, void* out, int64_t m,
+                    int64_t n, int64_t k, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Exact int32 accumulation of an int8 GEMM, acc = qx [m,k] @ qw [n,k]^T (bit-exactness probe). */
+int q35_int8_gemm_i32(const int8_t* qx, const int8_t* qw, int32_t* acc, int64_t m, int64_t n,
+                      int64_t k, void* stream);
+
+/* ---------------------------------------------------------------- prefill GEMM */
+
+/* Dense prefill projection C = A [m,k] @ W [n,k]^T, bf16 in, fp32 accumulate (integration.py:183,
+ * 245, 298 F.linear; :185, 272, 359 down/out/o proj). Epilogues as the decode GEMV:
+ * STORE -> out [m,n]; RESIDUAL -> resid [m,n] += (bf16 rounding both); SWIGLU -> W rows
+ * [0,n) are gate and [n,2n) up, out [m,n] = SwiGLU. */
+int q35_gemm_bf16(const void* a, const void* w, void* out, int64_t m, int64_t n, int64_t k,
+                  int32_t epilogue, void* stream);
+
+/* ---------------------------------------------------------------- attention */
+
+/* kernels.py:507 qgkv_norm_rope — packed [B, L, 2*Hq*D + 2*Hkv*D] -> q [B,Hq,L,D] and K/V written
+ * to k_out/v_out [B, Hkv, kv_len, D] at row offset *cache_start (NULL = 0). cos/sin [B,L,rot]. */
+int q35_qgkv_norm_rope(const void* packed, const void* q_weight, const void* k_weight,
+                       const void* cos, const void* sin, void* q_out, void* k_out, void* v_out,
+                       const int64_t* cache_start, int64_t batch, int64_t seq_len,
+                       int64_t q_heads, int64_t kv_heads, int64_t dim, int64_t rotary_dim,
+                       int64_t kv_len, float eps, void* stream);
+
+/* kernels.py:1031 gqa_decode_attention — q [B,H,1,D] over cache [B,Hkv,cache_len,D] with the
+ * valid prefix *valid_length (device, includes the current token) -> out [B,1,H*D] bf16.
+ * FP32 online softmax, split-KV with an in-kernel combine. Batch >= 1 (reference: batch 1). */
+size_t q35_gqa_decode_workspace_size(int64_t batch, int64_t heads, int64_t kv_heads,
+                                     int64_t head_dim, int64_t cache_len);
+int q35_gqa_decode_attention(const void* q, const void* cache_k, const void* cache_v,
+                             const int64_t* valid_length, float scale, void* out, int64_t batch,
+                             int64_t heads, int64_t kv_heads, int64_t head_dim, int64_t cache_len,
+                             void* workspace, size_t workspace_bytes, void* stream);
+
+/* Fused decode attention layer step (integration.py:298-359 for L == 1): from the packed QGKV
+ * projection output [B, 5120] it does Q/K RMSNorm + partial RoPE at position *rope_pos, writes
+ * K/V at row *cache_len, attends over rows [0, *cache_len] and multiplies by sigmoid(gate):
+ * out [B, Hq*D]. Does not advance *cache_len (the decoder does once per step). */
+size_t q35_attn_decode_workspace_size(int64_t batch, int64_t q_heads, int64_t kv_heads,
+                                      int64_t head_dim, int64_t cache_len);
+int q35_attn_decode(const void* packed, const void* q_weight, const void* k_weight,
+                    const float* inv_freq, void* cache_k, void* cache_v, const int64_t* cache_len,
+                    const int64_t* rope_pos, void* out, int64_t batch, int64_t q_heads,
+                    int64_t kv_heads, int64_t head_dim, int64_t rotary_dim, int64_t max_len,
+                    float eps, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Causal prefill attention (integration.py:360-372, SDPA with a causal mask): q [B,Hq,L,D],
+ * keys/values [B,Hkv,kv_len,D] (rows [0, q_offset + L) valid) -> out [B, L, Hq*D] bf16, FP32
+ * softmax. Query i attends keys j <= q_offset + i. */
+int q35_prefill_attention(const void* q, const void* k, const void* v, void* out, int64_t batch,
+                          int64_t q_heads, int64_t kv_heads, int64_t seq_len, int64_t kv_len,
+                          int64_t q_offset, int64_t head_dim, float scale, void* stream);
+
+/* ---------------------------------------------------------------- Gated DeltaNet */
+
+/* kernels.py:659 causal_conv1d_fused — x [B,L,in_stride] (first `channels` columns), weight
+ * [channels, K], state [B, channels, K] updated in place; out [B, L, channels] = SiLU(conv). */
+int q35_causal_conv1d(const void* x, const void* weight, void* state, void* out, int64_t batch,
+                      int64_t seq_len, int64_t in_stride, int64_t channels, int64_t kernel_size,
+                      void* stream);
+
+/* kernels.py:854 delta_recurrent_fused — sequential gated delta rule over L tokens.
+ * qkv [B,L,3*H*D] (conv output), packed [B,L,packed_stride] holding [qkv|z|a|b],
+ * state [B,H,D,D] fp32 in place; out [B,L,H,D] bf16. */
+int q35_delta_recurrent(const void* qkv, const void* packed, const void* a_log,
+                        const void* dt_bias, float* state, void* out, int64_t batch,
+                        int64_t seq_len, int64_t heads, int64_t dim, int64_t packed_stride,
+                        void* stream);
+
+/* Fused DeltaNet decode step (integration.py:245-272 for L == 1): conv update + SiLU, q/k L2
+ * norm, gated delta step on the fp32 state, gated RMSNorm with z. packed [B, packed_stride]
+ * -> out [B, H*D] bf16 (input of out_proj). */
+int q35_delta_decode(const void* packed, const void* conv_weight, void* conv_state,
+                     const void* a_log, const void* dt_bias, const void* norm_weight,
+                     float* state, void* out, int64_t batch, int64_t heads, int64_t dim,
+                     int64_t packed_stride, float eps, void* stream);
+
+/* ---------------------------------------------------------------- decoder loop */
+
+/* One layer of the text model as packed device tensors (integration.py:69-140 packing). */
+typedef struct {
+  int32_t kind;              /* 0 = Gated DeltaNet, 1 = full attention */
+  const void* in_ln;         /* bf16 [H] input_layernorm (1 + w) */
+  const void* post_ln;       /* bf16 [H] post_attention_layernorm */
+  const void* mix_in;        /* packed [qkv|z|a|b] [delta_rows, H] or [Q|G..|K|V] [qgkv_rows, H] */
+  const float* mix_in_scale; /* A8W8 per-row scales (NULL for bf16) */
+  const void* mix_out;       /* out_proj / o_proj [H, 2048] */
+  const float* mix_out_scale;
+  const void* gate_up;       /* [2I, H] */
+  const float* gate_up_scale;
+  const void* down;          /* [H, I] */
+  const float* down_scale;
+  const void* conv_w;        /* DeltaNet: bf16 [conv_dim, K] */
+  const void* a_log;         /* bf16 [heads] */
+  const void* dt_bias;       /* bf16 [heads] */
+  const void* gnorm;         /* bf16 [dv] gated norm weight */
+  void* conv_state;          /* bf16 [B, conv_dim, K] */
+  float* rec_state;          /* fp32 [B, heads, dk, dv] */
+  const void* q_norm;        /* attention: bf16 [D] */
+  const void* k_norm;
+  void* k_cache;             /* bf16 [B, Hkv, max_len, D] */
+  void* v_cache;
+} q35_layer_desc;
+
+typedef struct {
+  int32_t n_layers, hidden, intermediate, vocab;
+  int32_t q_heads, kv_heads, head_dim, rotary_dim;
+  int32_t lin_heads, lin_dk, lin_dv, conv_kernel, delta_rows;
+  int32_t max_len;        /* KV cache rows */
+  int32_t max_prefill;    /* longest prefill the workspace is sized for */
+  int32_t a8w8;
+  float eps;
+  const q35_layer_desc* layers;
+  const void* embed;      /* bf16 [vocab, H], tied LM head */
+  const void* final_norm; /* bf16 [H] */
+  const float* inv_freq;  /* fp32 [rotary_dim / 2] RoPE inverse frequencies */
+  int64_t* token;         /* device [1]: token fed to the next decode step / last greedy token */
+  int64_t* cache_len;     /* device: rows already in the KV cache */
+  int64_t* rope_pos;      /* device: RoPE position of the next token */
+  int64_t* token_log;     /* optional device ring [log_len]: decode tokens by step (may be NULL) */
+  int64_t* log_pos;       /* device counter into token_log */
+  int32_t log_len;
+  int32_t use_pdl;        /* launch decode kernels with programmatic dependent launch */
+  void* workspace;
+  size_t workspace_bytes;
+} q35_decoder_desc;
+
+typedef struct q35_decoder q35_decoder;
+
+size_t q35_decoder_workspace_size(const q35_decoder_desc* desc);
+int q35_decoder_create(const q35_decoder_desc* desc, q35_decoder** out);
+void q35_decoder_destroy(q35_decoder* dec);
+/* Prefill `length` token ids (device int64) from an empty cache (evaluation_wrapper.py:354-363):
+ * all layers, caches/states filled, greedy first token -> *token; cache_len = rope_pos = length. */
+int q35_decoder_prefill(q35_decoder* dec, const int64_t* ids, int64_t length, void* stream);
+/* One greedy decode step (graph.py:51-79 body): consumes *token, appends to caches, writes the
+ * next greedy token to *token (and token_log), advances cache_len / rope_pos. */
+int q35_decoder_decode_step(q35_decoder* dec, void* stream);
+/* Number of kernels one decode step launches (for launch accounting). */
+int q35_decoder_kernels_per_step(const q35_decoder* dec);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QWEN35_B200_H */

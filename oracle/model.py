@@ -184,15 +184,15 @@ class OracleDecoder:
         return (tokens, margins) if return_margins else tokens
 
     def teacher_forced_top1(self, prompt: torch.Tensor, forced: list[int]):
-        """Top-1 and top-1/top-2 margin at every step when fed ``forced`` tokens."""
+        """At every step, fed ``forced`` tokens: ``(oracle top-1, its BF16 logit, the BF16 logit
+        of the forced token)``."""
         self.reset(prompt.shape[0])
         h = self.forward(prompt)[:, -1]
         out = []
         for step in range(len(forced)):
             logits = ops.linear(h, self.embed).float()[0]
             top = int(ops.lm_head_argmax(h, self.embed)[0, 0])
-            t2 = torch.topk(logits, 2).values
-            out.append((top, float(t2[0] - t2[1])))
+            out.append((top, float(logits[top]), float(logits[forced[step]])))
             if step + 1 < len(forced):
                 h = self.forward(torch.tensor([[forced[step]]]))[:, -1]
         return out

@@ -1,0 +1,619 @@
+// Gated GQA attention for Qwen3.5 (reference: kernels.py:419-573 qgkv_norm_rope, 940-1090
+// gqa_decode_attention, 285-333 attention_gate_mul; integration.py:282-380).
+//
+// * qgkv_norm_rope: one CTA per (batch, token); thread d owns dimension d of every head, so the
+//   per-head RMSNorm reductions and the RoPE partner exchange stay in shared memory.
+// * decode attention: split-KV over the cache rows with all G = Hq/Hkv query heads of one KV
+//   head in the same CTA (K/V are read once per group, not once per query head); FP32 online
+//   softmax per warp, merged per CTA, then the last CTA of each (batch, KV head) combines the
+//   splits (atomic ticket; no second launch) and applies the sigmoid output gate. The fused
+//   variant also performs the Q/K norm + RoPE and the cache write of the current token, so a
+//   whole decode attention layer (minus the projections) is one kernel.
+// * prefill attention: causal, FP32 CUDA-core tiles (64 queries x 64 keys per step).
+#include <cfloat>
+
+#include "common.cuh"
+
+using namespace q35;
+
+namespace {
+
+constexpr int kD = 256;  // head_dim of every Qwen3.5 attention layer
+
+// RoPE factors for dimension d at position pos: cos/sin rounded to BF16 as the HF rotary
+// embedding returns them (cat(freqs, freqs); FP32 angle = pos * inv_freq).
+Q35_DEV void rope_cs(int d, int half, float pos, const float* inv_freq, float& c, float& s) {
+  const float ang = pos * inv_freq[d % half];
+  float sn, cs;
+  sincosf(ang, &sn, &cs);
+  c = rbf(cs);
+  s = rbf(sn);
+}
+
+// Apply partial RoPE to a normed head held in shared memory (kernels.py:455-472).
+Q35_DEV float rope_apply(const float* normed, int d, int rot, float c, float s) {
+  if (d >= rot) return normed[d];
+  const int half = rot / 2;
+  const float partner = d < half ? -normed[d + half] : normed[d - half];
+  return rbf(rbf(normed[d] * c) + rbf(partner * s));
+}
+
+// ============================================================================ qgkv_norm_rope
+template <bool TABLE>
+__global__ void __launch_bounds__(kD) qgkv_rope_kernel(
+    const bf16* __restrict__ packed, const bf16* __restrict__ qw, const bf16* __restrict__ kw,
+    const bf16* __restrict__ cos_t, const bf16* __restrict__ sin_t, const float* __restrict__ inv_freq,
+    int64_t pos_base, bf16* __restrict__ q_out, bf16* __restrict__ k_out, bf16* __restrict__ v_out,
+    const int64_t* __restrict__ cache_start, int L, int Hq, int Hkv, int rot, int kv_len, float eps) {
+  __shared__ float normed[kD];
+  __shared__ float red[kD / 32];
+  const int bt = blockIdx.x;  // b * L + t
+  const int b = bt / L, t = bt - b * L;
+  const int d = threadIdx.x;
+  const int stride = 2 * Hq * kD + 2 * Hkv * kD;
+  const bf16* row = packed + (int64_t)bt * stride;
+  const int64_t start = cache_start ? *cache_start : 0;
+  float c = 1.f, s = 0.f;
+  if (d < rot) {
+    if (TABLE) {
+      c = bf2f(cos_t[(int64_t)bt * rot + d]);
+      s = bf2f(sin_t[(int64_t)bt * rot + d]);
+    } else {
+      rope_cs(d, rot / 2, (float)(pos_base + start + t), inv_freq, c, s);
+    }
+  }
+  for (int h = 0; h < Hq + Hkv; ++h) {
+    const bool is_q = h < Hq;
+    const int off = is_q ? h * 2 * kD : 2 * Hq * kD + (h - Hq) * kD;
+    const float x = bf2f(row[off + d]);
+    const float var = block_sum<kD / 32>(x * x, red) / (float)kD;
+    const float w = bf2f(is_q ? qw[d] : kw[d]);
+    normed[d] = rbf(x * rsqrt_ieee(var + eps) * (1.0f + w));
+    __syncthreads();
+    const float y = rope_apply(normed, d, rot, c, s);
+    if (is_q) {
+      q_out[(((int64_t)b * Hq + h) * L + t) * kD + d] = f2bf(y);
+    } else if (start + t >= 0 && start + t < kv_len) {  // device-side start: never write past the cache
+      const int kh = h - Hq;
+      const int64_t o = (((int64_t)b * Hkv + kh) * kv_len + start + t) * kD + d;
+      k_out[o] = f2bf(y);
+      v_out[o] = row[2 * Hq * kD + Hkv * kD + kh * kD + d];
+    }
+    __syncthreads();
+  }
+}
+
+// ============================================================================ decode attention
+struct DecodeParams {
+  const bf16* packed;    // fused: [B, stride] projection output
+  const bf16* qw;
+  const bf16* kw;
+  const float* inv_freq;
+  const int64_t* rope_pos;
+  const bf16* q_in;      // API: [B, Hq, D]
+  bf16* cache_k;         // [B, Hkv, max_len, D]
+  bf16* cache_v;
+  const int64_t* len;    // fused: rows already cached (new token goes to row *len); API: valid rows
+  bf16* out;             // [B, Hq*D]
+  float* part;           // [B*Hkv*S*G] x (D + 2)
+  unsigned* tickets;     // [B*Hkv]
+  int Hq, Hkv, max_len, S, rot;
+  float scale, eps;
+};
+
+constexpr int kAttnThreads = 256;
+constexpr int kAttnWarps = 8;
+
+template <int G, bool FUSED>
+__global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(DecodeParams p) {
+  __shared__ __align__(16) float qf[G][kD];     // scaled final queries
+  __shared__ __align__(16) float kn[kD];        // fused: current token key (final) / scratch
+  __shared__ __align__(16) float vn[kD];
+  __shared__ float wm[kAttnWarps][G], wl[kAttnWarps][G];
+  __shared__ __align__(16) float wacc[kAttnWarps][G][kD];
+  __shared__ float red[kAttnWarps][G + 1];
+  __shared__ unsigned ticket_s;
+
+  const int s = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
+  const int S = p.S, Hkv = p.Hkv, Hq = p.Hq;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int d = threadIdx.x;  // kAttnThreads == kD
+  const int64_t kv_base = ((int64_t)b * Hkv + g) * p.max_len * kD;
+
+  pdl_wait();
+  pdl_launch_dependents();
+  const int64_t len = *p.len;
+  int n_rows;  // cache rows to attend from the cache
+  if (FUSED) {
+    n_rows = (int)len;
+    const int stride = 2 * Hq * kD + 2 * Hkv * kD;
+    const bf16* row = p.packed + (int64_t)b * stride;
+    // raw values
+    float x[G + 1];
+#pragma unroll
+    for (int hh = 0; hh < G; ++hh) x[hh] = bf2f(row[(g * G + hh) * 2 * kD + d]);
+    x[G] = bf2f(row[2 * Hq * kD + g * kD + d]);
+    const float v_raw = bf2f(row[2 * Hq * kD + Hkv * kD + g * kD + d]);
+    // G+1 simultaneous block reductions of x^2
+#pragma unroll
+    for (int i = 0; i <= G; ++i) {
+      const float ws = warp_sum(x[i] * x[i]);
+      if (lane == 0) red[warp][i] = ws;
+    }
+    __syncthreads();
+    float c = 1.f, sn = 0.f;
+    if (d < p.rot) rope_cs(d, p.rot / 2, (float)(*p.rope_pos), p.inv_freq, c, sn);
+    const float wq = bf2f(p.qw[d]), wk = bf2f(p.kw[d]);
+    for (int i = 0; i <= G; ++i) {
+      float tot = 0.f;
+#pragma unroll
+      for (int w = 0; w < kAttnWarps; ++w) tot += red[w][i];
+      const float r = rsqrt_ieee(tot / (float)kD + p.eps);
+      const float nrm = rbf(x[i] * r * (1.0f + (i < G ? wq : wk)));
+      kn[d] = nrm;  // scratch: normed head i
+      __syncthreads();
+      const float y = rope_apply(kn, d, p.rot, c, sn);
+      __syncthreads();
+      if (i < G) {
+        qf[i][d] = y * p.scale;
+      } else {
+        kn[d] = y;
+        vn[d] = v_raw;
+        if (s == 0 && len < p.max_len) {
+          p.cache_k[kv_base + len * kD + d] = f2bf(y);
+          p.cache_v[kv_base + len * kD + d] = f2bf(v_raw);
+        }
+      }
+    }
+  } else {
+    n_rows = (int)len;
+#pragma unroll
+    for (int hh = 0; hh < G; ++hh)
+      qf[hh][d] = bf2f(p.q_in[((int64_t)b * Hq + g * G + hh) * kD + d]) * p.scale;
+  }
+  if (n_rows > p.max_len) n_rows = p.max_len;
+  if (n_rows < 0) n_rows = 0;
+  __syncthreads();
+
+  // ---- this CTA's rows of the cache
+  const int chunk = (n_rows + S - 1) / S;
+  const int r0 = s * chunk;
+  const int r1 = min(r0 + chunk, n_rows);
+  float m[G], l[G], acc[G][8];
+#pragma unroll
+  for (int hh = 0; hh < G; ++hh) {
+    m[hh] = -FLT_MAX;
+    l[hh] = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[hh][j] = 0.f;
+  }
+  float q8[G][8];
+#pragma unroll
+  for (int hh = 0; hh < G; ++hh)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) q8[hh][j] = qf[hh][lane * 8 + j];
+
+  auto process = [&](const float kf[8], const float vf[8]) {
+    float sc[G];
+#pragma unroll
+    for (int hh = 0; hh < G; ++hh) {
+      float a = 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) a = fmaf(q8[hh][j], kf[j], a);
+      sc[hh] = warp_sum(a);
+    }
+#pragma unroll
+    for (int hh = 0; hh < G; ++hh) {
+      const float mn = fmaxf(m[hh], sc[hh]);
+      const float alpha = expf(m[hh] - mn);
+      const float pr = expf(sc[hh] - mn);
+      l[hh] = l[hh] * alpha + pr;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[hh][j] = acc[hh][j] * alpha + pr * vf[j];
+      m[hh] = mn;
+    }
+  };
+
+  const bf16* Kb = p.cache_k + kv_base;
+  const bf16* Vb = p.cache_v + kv_base;
+  int r = r0 + warp;
+  uint4 kc = make_uint4(0, 0, 0, 0), vc = make_uint4(0, 0, 0, 0);
+  if (r < r1) {
+    kc = *reinterpret_cast<const uint4*>(Kb + (int64_t)r * kD + lane * 8);
+    vc = *reinterpret_cast<const uint4*>(Vb + (int64_t)r * kD + lane * 8);
+  }
+  for (; r < r1; r += kAttnWarps) {
+    const int rn = r + kAttnWarps;
+    uint4 kn2 = make_uint4(0, 0, 0, 0), vn2 = make_uint4(0, 0, 0, 0);
+    if (rn < r1) {
+      kn2 = *reinterpret_cast<const uint4*>(Kb + (int64_t)rn * kD + lane * 8);
+      vn2 = *reinterpret_cast<const uint4*>(Vb + (int64_t)rn * kD + lane * 8);
+    }
+    float kf[8], vf[8];
+    unpack_bf16x8(kc, kf);
+    unpack_bf16x8(vc, vf);
+    process(kf, vf);
+    kc = kn2;
+    vc = vn2;
+  }
+  if (FUSED && s == S - 1 && warp == 0) {  // the current token, from registers/shared memory
+    float kf[8], vf[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      kf[j] = kn[lane * 8 + j];
+      vf[j] = vn[lane * 8 + j];
+    }
+    process(kf, vf);
+  }
+
+  // ---- merge the warps of this CTA
+  if (lane == 0) {
+#pragma unroll
+    for (int hh = 0; hh < G; ++hh) {
+      wm[warp][hh] = m[hh];
+      wl[warp][hh] = l[hh];
+    }
+  }
+#pragma unroll
+  for (int hh = 0; hh < G; ++hh)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) wacc[warp][hh][lane * 8 + j] = acc[hh][j];
+  __syncthreads();
+  const int slot0 = (((b * Hkv + g) * S) + s) * G;
+#pragma unroll
+  for (int hh = 0; hh < G; ++hh) {
+    float M = -FLT_MAX;
+#pragma unroll
+    for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, wm[w][hh]);
+    float Lsum = 0.f, A = 0.f;
+#pragma unroll
+    for (int w = 0; w < kAttnWarps; ++w) {
+      const float e = (wl[w][hh] > 0.f) ? expf(wm[w][hh] - M) : 0.f;
+      Lsum += wl[w][hh] * e;
+      A += wacc[w][hh][d] * e;
+    }
+    float* slot = p.part + (int64_t)(slot0 + hh) * (kD + 2);
+    slot[d] = A;
+    if (d == 0) {
+      slot[kD] = M;
+      slot[kD + 1] = Lsum;
+    }
+  }
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) ticket_s = atomicAdd(&p.tickets[b * Hkv + g], 1u);
+  __syncthreads();
+  if (ticket_s != (unsigned)(S - 1)) return;
+  __threadfence();
+
+  // ---- last CTA of this (batch, KV head): combine the splits, gate, store
+  for (int hh = 0; hh < G; ++hh) {
+    const int base = ((b * Hkv + g) * S) * G + hh;
+    float M = -FLT_MAX;
+    for (int j = 0; j < S; ++j) {
+      const float* slot = p.part + (int64_t)(base + j * G) * (kD + 2);
+      if (__ldcg(slot + kD + 1) > 0.f) M = fmaxf(M, __ldcg(slot + kD));
+    }
+    float Lsum = 0.f, A = 0.f;
+    for (int j = 0; j < S; ++j) {
+      const float* slot = p.part + (int64_t)(base + j * G) * (kD + 2);
+      const float lj = __ldcg(slot + kD + 1);
+      if (lj > 0.f) {
+        const float e = expf(__ldcg(slot + kD) - M);
+        Lsum += lj * e;
+        A += __ldcg(slot + d) * e;
+      }
+    }
+    const float o = Lsum > 0.f ? rbf(A / Lsum) : 0.f;
+    const int h = g * G + hh;
+    if (FUSED) {
+      const int stride = 2 * Hq * kD + 2 * Hkv * kD;
+      const float gate = bf2f(p.packed[(int64_t)b * stride + h * 2 * kD + kD + d]);
+      p.out[((int64_t)b * Hq + h) * kD + d] = f2bf(o * rbf(sigmoid_f(gate)));
+    } else {
+      p.out[((int64_t)b * Hq + h) * kD + d] = f2bf(o);
+    }
+  }
+  if (threadIdx.x == 0) atomicExch(&p.tickets[b * Hkv + g], 0u);
+}
+
+int choose_splits(int64_t batch, int64_t kv_heads, int64_t cache_len) {
+  int64_t s = (2 * kNumSMs + batch * kv_heads - 1) / (batch * kv_heads);
+  const int64_t cap = (cache_len + 15) / 16;
+  if (s > cap) s = cap;
+  if (s > 128) s = 128;
+  if (s < 1) s = 1;
+  return (int)s;
+}
+
+size_t decode_ws(int64_t batch, int64_t heads, int64_t kv_heads, int64_t cache_len) {
+  const int S = choose_splits(batch, kv_heads, cache_len);
+  const size_t parts = (size_t)batch * heads * S * (kD + 2) * sizeof(float);
+  const size_t tickets = (size_t)batch * kv_heads * sizeof(unsigned);
+  return ((tickets + 255) & ~(size_t)255) + parts;
+}
+
+template <bool FUSED>
+int launch_decode(DecodeParams p, int64_t batch, int G, void* ws, cudaStream_t st, bool pdl) {
+  p.tickets = static_cast<unsigned*>(ws);
+  const size_t tickets = (size_t)batch * p.Hkv * sizeof(unsigned);
+  p.part = reinterpret_cast<float*>(static_cast<char*>(ws) + ((tickets + 255) & ~(size_t)255));
+  dim3 grid(p.S, p.Hkv, (unsigned)batch);
+  cudaError_t e;
+  switch (G) {
+    case 1: e = q35_launch(attn_decode_kernel<1, FUSED>, grid, dim3(kAttnThreads), 0, st, pdl, p); break;
+    case 2: e = q35_launch(attn_decode_kernel<2, FUSED>, grid, dim3(kAttnThreads), 0, st, pdl, p); break;
+    case 4: e = q35_launch(attn_decode_kernel<4, FUSED>, grid, dim3(kAttnThreads), 0, st, pdl, p); break;
+    default: return q35_fail(Q35_ENOTSUP, "decode attention: group size %d unsupported", G);
+  }
+  if (e != cudaSuccess) return q35_fail(Q35_ECUDA, "decode attention launch: %s", cudaGetErrorString(e));
+  return Q35_OK;
+}
+
+// ============================================================================ prefill attention
+// One CTA = 64 queries of one head; 256 threads as a 16 x 16 grid. Scores for a 64 x 64 tile:
+// thread (ty, tx) owns query rows ty*4..+3 and key columns tx*4..+3. Output: rows ty*4..+3,
+// dims tx*16..+15. K is staged transposed so the score loop reads shared memory conflict-free.
+constexpr int kPQ = 64, kPK = 64;
+
+__global__ void __launch_bounds__(256) prefill_attn_kernel(const bf16* __restrict__ Q, const bf16* __restrict__ K,
+                                                          const bf16* __restrict__ V, bf16* __restrict__ O,
+                                                          int Hq, int Hkv, int L, int kv_len, int q_offset,
+                                                          float scale) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  bf16* Qs = reinterpret_cast<bf16*>(smem);                 // [64][256]
+  bf16* Kt = Qs + kPQ * kD;                                 // [256][64] transposed
+  bf16* Vs = Kt + kD * kPK;                                 // [64][256]
+  float* Ps = reinterpret_cast<float*>(Vs + kPK * kD);      // [64][65]
+  const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int G = Hq / Hkv, kvh = h / G;
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+  const int q0 = qt * kPQ;
+  const bf16* Qg = Q + (((int64_t)b * Hq + h) * L) * kD;
+  const bf16* Kg = K + (((int64_t)b * Hkv + kvh) * kv_len) * kD;
+  const bf16* Vg = V + (((int64_t)b * Hkv + kvh) * kv_len) * kD;
+  for (int i = threadIdx.x; i < kPQ * kD / 8; i += 256) {
+    const int rr = i / (kD / 8), cc = (i % (kD / 8)) * 8;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (q0 + rr < L) v = *reinterpret_cast<const uint4*>(Qg + (int64_t)(q0 + rr) * kD + cc);
+    *reinterpret_cast<uint4*>(Qs + rr * kD + cc) = v;
+  }
+  float m[4], l[4], acc[4][16];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    m[i] = -FLT_MAX;
+    l[i] = 0.f;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) acc[i][j] = 0.f;
+  }
+  const int last_q = min(q0 + kPQ, L) - 1 + q_offset;  // highest key any row here may see
+  const int n_kt = last_q / kPK + 1;
+  for (int kt = 0; kt < n_kt; ++kt) {
+    const int k0 = kt * kPK;
+    __syncthreads();
+    for (int i = threadIdx.x; i < kPK * kD / 8; i += 256) {
+      const int rr = i / (kD / 8), cc = (i % (kD / 8)) * 8;
+      uint4 kv = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
+      if (k0 + rr < kv_len) {
+        kv = *reinterpret_cast<const uint4*>(Kg + (int64_t)(k0 + rr) * kD + cc);
+        vv = *reinterpret_cast<const uint4*>(Vg + (int64_t)(k0 + rr) * kD + cc);
+      }
+      const bf16* kp = reinterpret_cast<const bf16*>(&kv);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) Kt[(cc + j) * kPK + rr] = kp[j];
+      *reinterpret_cast<uint4*>(Vs + rr * kD + cc) = vv;
+    }
+    __syncthreads();
+    float sc[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) sc[i][j] = 0.f;
+    for (int dd = 0; dd < kD; dd += 2) {
+      float qv[4][2], kv[2][4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const __nv_bfloat162 q2 = *reinterpret_cast<const __nv_bfloat162*>(Qs + (ty * 4 + i) * kD + dd);
+        qv[i][0] = __low2float(q2);
+        qv[i][1] = __high2float(q2);
+      }
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const uint2 k4 = *reinterpret_cast<const uint2*>(Kt + (dd + e) * kPK + tx * 4);
+        kv[e][0] = __uint_as_float(k4.x << 16);
+        kv[e][1] = __uint_as_float(k4.x & 0xffff0000u);
+        kv[e][2] = __uint_as_float(k4.y << 16);
+        kv[e][3] = __uint_as_float(k4.y & 0xffff0000u);
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) sc[i][j] = fmaf(qv[i][0], kv[0][j], fmaf(qv[i][1], kv[1][j], sc[i][j]));
+    }
+    // causal mask + online softmax (row max/sum over the 16 tx lanes of this row group)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int qi = q0 + ty * 4 + i + q_offset;
+      float mx = -FLT_MAX;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int kj = k0 + tx * 4 + j;
+        sc[i][j] = (kj <= qi && kj < kv_len) ? sc[i][j] * scale : -FLT_MAX;
+        mx = fmaxf(mx, sc[i][j]);
+      }
+#pragma unroll
+      for (int o = 1; o < 16; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      const float mn = fmaxf(m[i], mx);
+      const float alpha = (m[i] == -FLT_MAX) ? 0.f : expf(m[i] - mn);
+      float rs = 0.f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float pr = (sc[i][j] == -FLT_MAX) ? 0.f : expf(sc[i][j] - mn);
+        Ps[(ty * 4 + i) * 65 + tx * 4 + j] = pr;
+        rs += pr;
+      }
+#pragma unroll
+      for (int o = 1; o < 16; o <<= 1) rs += __shfl_xor_sync(0xffffffffu, rs, o);
+      l[i] = l[i] * alpha + rs;
+      m[i] = mn;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) acc[i][j] *= alpha;
+    }
+    __syncthreads();
+    for (int c = 0; c < kPK; ++c) {
+      float vv[16];
+      const uint4* vp = reinterpret_cast<const uint4*>(Vs + c * kD + tx * 16);
+      unpack_bf16x8(vp[0], vv);
+      unpack_bf16x8(vp[1], vv + 8);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float pr = Ps[(ty * 4 + i) * 65 + c];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) acc[i][j] = fmaf(pr, vv[j], acc[i][j]);
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int qi = q0 + ty * 4 + i;
+    if (qi >= L) continue;
+    const float inv = l[i] > 0.f ? 1.0f / l[i] : 0.f;
+    __align__(16) bf16 o[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) o[j] = f2bf(acc[i][j] * inv);
+    bf16* dst = O + (((int64_t)b * L + qi) * Hq + h) * kD + tx * 16;
+    reinterpret_cast<uint4*>(dst)[0] = reinterpret_cast<const uint4*>(o)[0];
+    reinterpret_cast<uint4*>(dst)[1] = reinterpret_cast<const uint4*>(o)[1];
+  }
+}
+
+}  // namespace
+
+// ------------------------------------------------------------------------------------ C ABI
+extern "C" int q35_qgkv_norm_rope(const void* packed, const void* q_weight, const void* k_weight,
+                                  const void* cos, const void* sin, void* q_out, void* k_out, void* v_out,
+                                  const int64_t* cache_start, int64_t batch, int64_t seq_len,
+                                  int64_t q_heads, int64_t kv_heads, int64_t dim, int64_t rotary_dim,
+                                  int64_t kv_len, float eps, void* stream) {
+  Q35_REQUIRE(packed && q_weight && k_weight && cos && sin && q_out && k_out && v_out,
+              "qgkv_norm_rope: null pointer");
+  Q35_REQUIRE(dim == kD, "qgkv_norm_rope: head dim %lld unsupported (256)", (long long)dim);
+  Q35_REQUIRE(rotary_dim > 0 && rotary_dim <= dim && rotary_dim % 2 == 0, "qgkv_norm_rope: bad rotary_dim");
+  Q35_REQUIRE(batch >= 0 && seq_len >= 0 && q_heads > 0 && kv_heads > 0 && kv_len >= seq_len,
+              "qgkv_norm_rope: bad shape");
+  if (batch * seq_len == 0) return Q35_OK;
+  qgkv_rope_kernel<true><<<(unsigned)(batch * seq_len), kD, 0, (cudaStream_t)stream>>>(
+      (const bf16*)packed, (const bf16*)q_weight, (const bf16*)k_weight, (const bf16*)cos, (const bf16*)sin,
+      nullptr, 0, (bf16*)q_out, (bf16*)k_out, (bf16*)v_out, cache_start, (int)seq_len, (int)q_heads,
+      (int)kv_heads, (int)rotary_dim, (int)kv_len, eps);
+  return q35_check_launch("qgkv_norm_rope");
+}
+
+// Prefill variant used by the decoder: RoPE from positions cache_start + t (text tokens).
+int q35_qgkv_rope_positions_launch(const void* packed, const void* q_weight, const void* k_weight,
+                                   const float* inv_freq, void* q_out, void* k_out, void* v_out,
+                                   const int64_t* cache_start, int64_t batch, int64_t seq_len, int64_t q_heads,
+                                   int64_t kv_heads, int64_t rotary_dim, int64_t kv_len, float eps,
+                                   cudaStream_t stream) {
+  qgkv_rope_kernel<false><<<(unsigned)(batch * seq_len), kD, 0, stream>>>(
+      (const bf16*)packed, (const bf16*)q_weight, (const bf16*)k_weight, nullptr, nullptr, inv_freq, 0,
+      (bf16*)q_out, (bf16*)k_out, (bf16*)v_out, cache_start, (int)seq_len, (int)q_heads, (int)kv_heads,
+      (int)rotary_dim, (int)kv_len, eps);
+  return q35_check_launch("qgkv_rope_positions");
+}
+
+extern "C" size_t q35_gqa_decode_workspace_size(int64_t batch, int64_t heads, int64_t kv_heads,
+                                                int64_t head_dim, int64_t cache_len) {
+  (void)head_dim;
+  return decode_ws(batch, heads, kv_heads, cache_len);
+}
+
+extern "C" int q35_gqa_decode_attention(const void* q, const void* cache_k, const void* cache_v,
+                                        const int64_t* valid_length, float scale, void* out, int64_t batch,
+                                        int64_t heads, int64_t kv_heads, int64_t head_dim, int64_t cache_len,
+                                        void* workspace, size_t workspace_bytes, void* stream) {
+  Q35_REQUIRE(q && cache_k && cache_v && valid_length && out && workspace, "gqa_decode_attention: null pointer");
+  Q35_REQUIRE(head_dim == kD, "gqa_decode_attention: head dim %lld unsupported (256)", (long long)head_dim);
+  Q35_REQUIRE(batch >= 1 && kv_heads >= 1 && heads % kv_heads == 0 && cache_len >= 1,
+              "gqa_decode_attention: head layout does not match cache");
+  Q35_REQUIRE(workspace_bytes >= decode_ws(batch, heads, kv_heads, cache_len),
+              "gqa_decode_attention: workspace too small");
+  DecodeParams p = {};
+  p.q_in = (const bf16*)q;
+  p.cache_k = (bf16*)cache_k;
+  p.cache_v = (bf16*)cache_v;
+  p.len = valid_length;
+  p.out = (bf16*)out;
+  p.Hq = (int)heads;
+  p.Hkv = (int)kv_heads;
+  p.max_len = (int)cache_len;
+  p.S = choose_splits(batch, kv_heads, cache_len);
+  p.scale = scale;
+  return launch_decode<false>(p, batch, (int)(heads / kv_heads), workspace, (cudaStream_t)stream, false);
+}
+
+int q35_attn_decode_launch(const void* packed, const void* q_weight, const void* k_weight, const float* inv_freq,
+                           void* cache_k, void* cache_v, const int64_t* cache_len, const int64_t* rope_pos,
+                           void* out, int64_t batch, int64_t q_heads, int64_t kv_heads, int64_t rotary_dim,
+                           int64_t max_len, float eps, void* workspace, cudaStream_t stream, bool pdl) {
+  DecodeParams p = {};
+  p.packed = (const bf16*)packed;
+  p.qw = (const bf16*)q_weight;
+  p.kw = (const bf16*)k_weight;
+  p.inv_freq = inv_freq;
+  p.rope_pos = rope_pos;
+  p.cache_k = (bf16*)cache_k;
+  p.cache_v = (bf16*)cache_v;
+  p.len = cache_len;
+  p.out = (bf16*)out;
+  p.Hq = (int)q_heads;
+  p.Hkv = (int)kv_heads;
+  p.max_len = (int)max_len;
+  p.S = choose_splits(batch, kv_heads, max_len);
+  p.rot = (int)rotary_dim;
+  p.scale = 1.0f / sqrtf((float)kD);
+  p.eps = eps;
+  return launch_decode<true>(p, batch, (int)(q_heads / kv_heads), workspace, stream, pdl);
+}
+
+extern "C" size_t q35_attn_decode_workspace_size(int64_t batch, int64_t q_heads, int64_t kv_heads,
+                                                 int64_t head_dim, int64_t cache_len) {
+  (void)head_dim;
+  return decode_ws(batch, q_heads, kv_heads, cache_len);
+}
+
+extern "C" int q35_attn_decode(const void* packed, const void* q_weight, const void* k_weight,
+                               const float* inv_freq, void* cache_k, void* cache_v, const int64_t* cache_len,
+                               const int64_t* rope_pos, void* out, int64_t batch, int64_t q_heads,
+                               int64_t kv_heads, int64_t head_dim, int64_t rotary_dim, int64_t max_len, float eps,
+                               void* workspace, size_t workspace_bytes, void* stream) {
+  Q35_REQUIRE(packed && q_weight && k_weight && inv_freq && cache_k && cache_v && cache_len && rope_pos && out &&
+                  workspace,
+              "attn_decode: null pointer");
+  Q35_REQUIRE(head_dim == kD, "attn_decode: head dim must be 256");
+  Q35_REQUIRE(batch >= 1 && kv_heads >= 1 && q_heads % kv_heads == 0 && max_len >= 1 && rotary_dim % 2 == 0 &&
+                  rotary_dim <= head_dim,
+              "attn_decode: bad shape");
+  Q35_REQUIRE(workspace_bytes >= decode_ws(batch, q_heads, kv_heads, max_len), "attn_decode: workspace too small");
+  return q35_attn_decode_launch(packed, q_weight, k_weight, inv_freq, cache_k, cache_v, cache_len, rope_pos, out,
+                                batch, q_heads, kv_heads, rotary_dim, max_len, eps, workspace, (cudaStream_t)stream,
+                                false);
+}
+
+extern "C" int q35_prefill_attention(const void* q, const void* k, const void* v, void* out, int64_t batch,
+                                     int64_t q_heads, int64_t kv_heads, int64_t seq_len, int64_t kv_len,
+                                     int64_t q_offset, int64_t head_dim, float scale, void* stream) {
+  Q35_REQUIRE(q && k && v && out, "prefill_attention: null pointer");
+  Q35_REQUIRE(head_dim == kD, "prefill_attention: head dim must be 256");
+  Q35_REQUIRE(batch >= 0 && seq_len >= 0 && kv_heads >= 1 && q_heads % kv_heads == 0 && q_offset >= 0 &&
+                  kv_len >= q_offset + seq_len,
+              "prefill_attention: bad shape");
+  if (batch * seq_len == 0) return Q35_OK;
+  const size_t smem = (size_t)(kPQ * kD + kD * kPK + kPK * kD) * sizeof(bf16) + (size_t)kPQ * 65 * sizeof(float);
+  cudaFuncSetAttribute(prefill_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  dim3 grid((unsigned)((seq_len + kPQ - 1) / kPQ), (unsigned)q_heads, (unsigned)batch);
+  prefill_attn_kernel<<<grid, 256, smem, (cudaStream_t)stream>>>((const bf16*)q, (const bf16*)k, (const bf16*)v,
+                                                                 (bf16*)out, (int)q_heads, (int)kv_heads,
+                                                                 (int)seq_len, (int)kv_len, (int)q_offset, scale);
+  return q35_check_launch("prefill_attention");
+}

@@ -1,0 +1,158 @@
+// Shared device helpers for the Qwen3.5 sm_100a kernels.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <utility>
+
+#include "qwen35_b200.h"
+
+#define Q35_DEV __device__ __forceinline__
+
+typedef __nv_bfloat16 bf16;
+
+namespace q35 {
+
+constexpr int kNumSMs = 148;
+
+Q35_DEV float bf2f(bf16 x) { return __bfloat162float(x); }
+Q35_DEV bf16 f2bf(float x) { return __float2bfloat16_rn(x); }
+Q35_DEV float rbf(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+// SiLU / sigmoid exactly as the reference kernels write them (kernels.py:135, 166, 272).
+Q35_DEV float silu_f(float x) { return x / (1.0f + expf(-x)); }
+Q35_DEV float sigmoid_f(float x) { return 1.0f / (1.0f + expf(-x)); }
+// IEEE square root and division (no approximate rsqrt), closest to torch.rsqrt on the CPU.
+Q35_DEV float rsqrt_ieee(float x) { return 1.0f / sqrtf(x); }
+
+Q35_DEV float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+Q35_DEV float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Block-wide sum; every thread gets the result. `red` needs NWARPS floats.
+template <int NWARPS>
+Q35_DEV float block_sum(float v, float* red) {
+  v = warp_sum(v);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  float t = 0.f;
+#pragma unroll
+  for (int i = 0; i < NWARPS; ++i) t += red[i];
+  return t;
+}
+template <int NWARPS>
+Q35_DEV float block_max(float v, float* red) {
+  v = warp_max(v);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  float t = red[0];
+#pragma unroll
+  for (int i = 1; i < NWARPS; ++i) t = fmaxf(t, red[i]);
+  return t;
+}
+
+// 16-byte read-only streaming load: weights are touched once per step, keep them out of L1.
+Q35_DEV uint4 ld_stream(const void* p) {
+  uint4 r;
+  asm("ld.global.nc.L1::no_allocate.L2::256B.v4.u32 {%0,%1,%2,%3}, [%4];"
+      : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+      : "l"(p));
+  return r;
+}
+
+Q35_DEV void unpack_bf16x8(const uint4& u, float f[8]) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    f[2 * i] = __uint_as_float(w[i] << 16);
+    f[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+  }
+}
+
+Q35_DEV float dot_bf16x8(const uint4& a, const uint4& b, float acc) {
+  float fa[8], fb[8];
+  unpack_bf16x8(a, fa);
+  unpack_bf16x8(b, fb);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) acc = fmaf(fa[i], fb[i], acc);
+  return acc;
+}
+
+Q35_DEV int dot_i8x16(const uint4& a, const uint4& b, int acc) {
+  acc = __dp4a((int)a.x, (int)b.x, acc);
+  acc = __dp4a((int)a.y, (int)b.y, acc);
+  acc = __dp4a((int)a.z, (int)b.z, acc);
+  acc = __dp4a((int)a.w, (int)b.w, acc);
+  return acc;
+}
+
+// Symmetric int8 quantisation of one value given its row scale: clamp(rne(x / s), -127, 127).
+Q35_DEV int quant_i8(float x, float s) {
+  int q = __float2int_rn(__fdiv_rn(x, s));
+  return max(-127, min(127, q));
+}
+
+// Programmatic dependent launch: wait for the producer grid's writes / let the consumer start.
+Q35_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+Q35_DEV void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// Order-preserving 32-bit key of a float (larger float -> larger key); -0 folds onto +0.
+Q35_DEV uint32_t float_order_key(float f) {
+  if (f == 0.0f) f = 0.0f;
+  uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+}  // namespace q35
+
+// Per-step device counters the decoder's last kernel advances (cache rows, RoPE position, token log).
+struct q35_step_counters {
+  int64_t* cache_len;
+  int64_t* rope_pos;
+  int64_t* token_log;
+  int64_t* log_pos;
+  int log_len;
+};
+
+// Host-side error reporting shared by every entry point.
+int q35_fail(int code, const char* fmt, ...);
+int q35_check_launch(const char* what);
+
+#define Q35_REQUIRE(cond, ...)                         \
+  do {                                                 \
+    if (!(cond)) return q35_fail(Q35_EINVAL, __VA_ARGS__); \
+  } while (0)
+
+#define Q35_ALIGNED(p, n) ((((uintptr_t)(p)) % (n)) == 0)
+
+// Launch with optional programmatic dependent launch (PDL): the kernel may start while the
+// previous kernel on the stream drains; it must call pdl_wait() before touching that kernel's
+// outputs. Without the attribute pdl_wait()/pdl_launch_dependents() are no-ops.
+template <typename... KArgs, typename... Args>
+static inline cudaError_t q35_launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                                     cudaStream_t stream, bool pdl, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}

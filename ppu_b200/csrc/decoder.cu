@@ -1,0 +1,317 @@
+// The Qwen3.5 text-decoder loop on the device (reference: the patched text-model forward,
+// qwen35_fused/integration.py:390-504; the greedy step of qwen35_fused/graph.py:51-79; the
+// prefill + first token of evaluation_wrapper.py:354-365).
+//
+// Decode step (batch 1), per layer five launches:
+//   in-projection GEMV   (prologue: RMSNorm of the residual, or embedding gather at layer 0)
+//   mixer                (DeltaNet: conv + recurrent step + gated norm | attention: norm/RoPE/
+//                         cache write/split-KV attention/gate), one kernel each
+//   out-projection GEMV  (epilogue: residual add in place)
+//   gate/up GEMV         (prologue: post-attention RMSNorm; epilogue: SwiGLU)
+//   down GEMV            (epilogue: residual add)
+// then the LM head with the final norm fused in, greedy top-1, and the step counters advanced
+// by its last CTA: 5 * layers + 1 kernels, all on one stream, optionally chained with
+// programmatic dependent launch so each kernel's weight prefetch overlaps its predecessor.
+#include <cstring>
+#include <vector>
+
+#include "common.cuh"
+
+int q35_gemv_launch(const q35_gemv_desc* d, cudaStream_t s, bool pdl);
+int q35_lm_head_launch(const void* hidden, const void* norm_weight, const void* weight, int64_t* token_out,
+                       int64_t vocab, int64_t k, float eps, void* ws, cudaStream_t s, bool pdl,
+                       const q35_step_counters* adv);
+int q35_attn_decode_launch(const void* packed, const void* q_weight, const void* k_weight, const float* inv_freq,
+                           void* cache_k, void* cache_v, const int64_t* cache_len, const int64_t* rope_pos,
+                           void* out, int64_t batch, int64_t q_heads, int64_t kv_heads, int64_t rotary_dim,
+                           int64_t max_len, float eps, void* workspace, cudaStream_t stream, bool pdl);
+int q35_delta_decode_launch(const void* packed, const void* conv_weight, void* conv_state, const void* a_log,
+                            const void* dt_bias, const void* norm_weight, float* state, void* out, int64_t batch,
+                            int64_t heads, int64_t packed_stride, float eps, cudaStream_t stream, bool pdl);
+int q35_gemm_launch(const void* a, const void* w, void* out, int64_t m, int64_t n, int64_t k, int epi, bool int8,
+                    const float* sx, const float* sw, cudaStream_t s);
+int q35_quantize_rows_launch(const void* x, int8_t* q, float* scale, int64_t rows, int64_t width, cudaStream_t s);
+int q35_qgkv_rope_positions_launch(const void* packed, const void* q_weight, const void* k_weight,
+                                   const float* inv_freq, void* q_out, void* k_out, void* v_out,
+                                   const int64_t* cache_start, int64_t batch, int64_t seq_len, int64_t q_heads,
+                                   int64_t kv_heads, int64_t rotary_dim, int64_t kv_len, float eps,
+                                   cudaStream_t stream);
+int q35_gated_rms_strided_launch(const void* x, const void* gate, int gate_group, int64_t gate_stride,
+                                 const void* weight, void* out, int64_t rows, int64_t width, float eps,
+                                 cudaStream_t stream);
+int q35_set_counters_launch(int64_t* a, int64_t* b, int64_t value, cudaStream_t stream);
+size_t q35_attn_decode_workspace_size(int64_t batch, int64_t q_heads, int64_t kv_heads, int64_t head_dim,
+                                      int64_t cache_len);
+
+namespace {
+
+struct Carve {
+  char* base;
+  size_t off = 0;
+  template <typename T>
+  T* take(size_t count) {
+    off = (off + 255) & ~(size_t)255;
+    T* p = reinterpret_cast<T*>(base ? base + off : nullptr);
+    off += count * sizeof(T);
+    return p;
+  }
+};
+
+struct Buffers {
+  // decode
+  bf16* resid;
+  bf16* mix_in_out;   // projection output [max(delta_rows, qgkv_rows)]
+  bf16* mix_out;      // mixer output [max(value_dim, q_heads*head_dim)]
+  bf16* act;          // SwiGLU output [intermediate]
+  void* attn_ws;
+  void* lm_ws;
+  // prefill
+  bf16* p_resid;      // [L, H]
+  bf16* p_norm;       // [L, H]
+  bf16* p_packed;     // [L, max rows]
+  bf16* p_conv;       // [L, conv_dim]
+  bf16* p_core;       // [L, value_dim] / q [Hq, L, D]
+  bf16* p_attn;       // [L, Hq*D]
+  bf16* p_mix;        // [L, max(value_dim, Hq*D)]
+  bf16* p_act;        // [L, I]
+  int8_t* p_q8;       // [L, max(H, I, mix width)]
+  float* p_sx;        // [L]
+};
+
+Buffers carve(const q35_decoder_desc& d, void* base, size_t* total) {
+  Carve c{static_cast<char*>(base)};
+  Buffers b;
+  const int64_t rows_in = d.delta_rows > 2 * d.q_heads * d.head_dim + 2 * d.kv_heads * d.head_dim
+                              ? d.delta_rows
+                              : 2 * d.q_heads * d.head_dim + 2 * d.kv_heads * d.head_dim;
+  const int64_t mixw = (int64_t)d.lin_heads * d.lin_dv > (int64_t)d.q_heads * d.head_dim
+                           ? (int64_t)d.lin_heads * d.lin_dv
+                           : (int64_t)d.q_heads * d.head_dim;
+  const int64_t conv_dim = (int64_t)d.lin_heads * (2 * d.lin_dk + d.lin_dv);
+  const int64_t L = d.max_prefill;
+  b.lm_ws = c.take<char>(256);  // LM head ticket + key (must start zeroed)
+  b.resid = c.take<bf16>(d.hidden);
+  b.mix_in_out = c.take<bf16>(rows_in);
+  b.mix_out = c.take<bf16>(mixw);
+  b.act = c.take<bf16>(d.intermediate);
+  b.attn_ws = c.take<char>(q35_attn_decode_workspace_size(1, d.q_heads, d.kv_heads, d.head_dim, d.max_len));
+  b.p_resid = c.take<bf16>(L * d.hidden);
+  b.p_norm = c.take<bf16>(L * d.hidden);
+  b.p_packed = c.take<bf16>(L * rows_in);
+  b.p_conv = c.take<bf16>(L * conv_dim);
+  b.p_core = c.take<bf16>(L * mixw);
+  b.p_attn = c.take<bf16>(L * mixw);
+  b.p_mix = c.take<bf16>(L * mixw);
+  b.p_act = c.take<bf16>(L * d.intermediate);
+  int64_t qw = d.hidden > d.intermediate ? d.hidden : d.intermediate;
+  if (mixw > qw) qw = mixw;
+  b.p_q8 = c.take<int8_t>(L * qw);
+  b.p_sx = c.take<float>(L);
+  *total = c.off + 256;
+  return b;
+}
+
+}  // namespace
+
+struct q35_decoder {
+  q35_decoder_desc d;
+  std::vector<q35_layer_desc> layers;
+  Buffers buf;
+};
+
+extern "C" size_t q35_decoder_workspace_size(const q35_decoder_desc* desc) {
+  if (!desc) return 0;
+  size_t total = 0;
+  carve(*desc, nullptr, &total);
+  return total;
+}
+
+extern "C" int q35_decoder_create(const q35_decoder_desc* desc, q35_decoder** out) {
+  Q35_REQUIRE(desc && out && desc->layers && desc->n_layers > 0, "decoder_create: bad descriptor");
+  const q35_decoder_desc& d = *desc;
+  Q35_REQUIRE(d.embed && d.final_norm && d.inv_freq && d.token && d.cache_len && d.rope_pos,
+              "decoder_create: missing model/state pointer");
+  Q35_REQUIRE(d.head_dim == 256 && d.lin_dk == 128 && d.lin_dv == 128 && d.conv_kernel == 4,
+              "decoder_create: kernels are built for head dims 256 / 128 and conv kernel 4");
+  Q35_REQUIRE(d.hidden % 16 == 0 && d.intermediate % 16 == 0 && d.max_len > 0 && d.max_prefill > 0,
+              "decoder_create: bad sizes");
+  Q35_REQUIRE(d.workspace && d.workspace_bytes >= q35_decoder_workspace_size(desc),
+              "decoder_create: workspace too small (%zu < %zu)", d.workspace_bytes, q35_decoder_workspace_size(desc));
+  for (int i = 0; i < d.n_layers; ++i) {
+    const q35_layer_desc& L = d.layers[i];
+    Q35_REQUIRE(L.in_ln && L.post_ln && L.mix_in && L.mix_out && L.gate_up && L.down, "layer %d: missing weight", i);
+    Q35_REQUIRE(!d.a8w8 || (L.mix_in_scale && L.mix_out_scale && L.gate_up_scale && L.down_scale),
+                "layer %d: A8W8 scales missing", i);
+    if (L.kind == 0)
+      Q35_REQUIRE(L.conv_w && L.a_log && L.dt_bias && L.gnorm && L.conv_state && L.rec_state,
+                  "layer %d: DeltaNet tensors missing", i);
+    else
+      Q35_REQUIRE(L.q_norm && L.k_norm && L.k_cache && L.v_cache, "layer %d: attention tensors missing", i);
+  }
+  q35_decoder* dec = new q35_decoder();
+  dec->d = d;
+  dec->layers.assign(d.layers, d.layers + d.n_layers);
+  dec->d.layers = dec->layers.data();
+  size_t total = 0;
+  dec->buf = carve(d, d.workspace, &total);
+  *out = dec;
+  return Q35_OK;
+}
+
+extern "C" void q35_decoder_destroy(q35_decoder* dec) { delete dec; }
+
+extern "C" int q35_decoder_kernels_per_step(const q35_decoder* dec) { return dec ? 5 * dec->d.n_layers + 1 : 0; }
+
+#define Q35_TRY(x)          \
+  do {                      \
+    int _rc = (x);          \
+    if (_rc) return _rc;    \
+  } while (0)
+
+extern "C" int q35_decoder_decode_step(q35_decoder* dec, void* stream) {
+  Q35_REQUIRE(dec, "decode_step: null decoder");
+  const q35_decoder_desc& d = dec->d;
+  const Buffers& B = dec->buf;
+  cudaStream_t s = (cudaStream_t)stream;
+  const bool pdl = d.use_pdl != 0;
+  const bool q8 = d.a8w8 != 0;
+  const int qgkv_rows = 2 * d.q_heads * d.head_dim + 2 * d.kv_heads * d.head_dim;
+  for (int i = 0; i < d.n_layers; ++i) {
+    const q35_layer_desc& L = dec->layers[i];
+    const bool delta = L.kind == 0;
+    q35_gemv_desc g = {};
+    // in-projection (+ residual norm / embedding)
+    g.weight = L.mix_in;
+    g.w_scale = L.mix_in_scale;
+    g.input = B.resid;
+    g.norm_weight = L.in_ln;
+    g.token = d.token;
+    g.embed = d.embed;
+    g.vocab = d.vocab;
+    g.resid_out = B.resid;
+    g.out = B.mix_in_out;
+    g.n_out = delta ? d.delta_rows : qgkv_rows;
+    g.k = d.hidden;
+    g.prologue = (i == 0) ? Q35_PRO_EMBED : Q35_PRO_NORM;
+    g.epilogue = Q35_EPI_STORE;
+    g.int8 = q8;
+    g.eps = d.eps;
+    Q35_TRY(q35_gemv_launch(&g, s, pdl));
+    // mixer
+    if (delta) {
+      Q35_TRY(q35_delta_decode_launch(B.mix_in_out, L.conv_w, L.conv_state, L.a_log, L.dt_bias, L.gnorm,
+                                      L.rec_state, B.mix_out, 1, d.lin_heads, d.delta_rows, d.eps, s, pdl));
+    } else {
+      Q35_TRY(q35_attn_decode_launch(B.mix_in_out, L.q_norm, L.k_norm, d.inv_freq, L.k_cache, L.v_cache,
+                                     d.cache_len, d.rope_pos, B.mix_out, 1, d.q_heads, d.kv_heads, d.rotary_dim,
+                                     d.max_len, d.eps, B.attn_ws, s, pdl));
+    }
+    // out-projection + residual
+    g = q35_gemv_desc{};
+    g.weight = L.mix_out;
+    g.w_scale = L.mix_out_scale;
+    g.input = B.mix_out;
+    g.resid_out = B.resid;
+    g.n_out = d.hidden;
+    g.k = delta ? d.lin_heads * d.lin_dv : d.q_heads * d.head_dim;
+    g.prologue = Q35_PRO_PLAIN;
+    g.epilogue = Q35_EPI_RESIDUAL;
+    g.int8 = q8;
+    g.eps = d.eps;
+    Q35_TRY(q35_gemv_launch(&g, s, pdl));
+    // gate/up + SwiGLU
+    g = q35_gemv_desc{};
+    g.weight = L.gate_up;
+    g.w_scale = L.gate_up_scale;
+    g.input = B.resid;
+    g.norm_weight = L.post_ln;
+    g.out = B.act;
+    g.n_out = d.intermediate;
+    g.k = d.hidden;
+    g.prologue = Q35_PRO_NORM;
+    g.epilogue = Q35_EPI_SWIGLU;
+    g.int8 = q8;
+    g.eps = d.eps;
+    Q35_TRY(q35_gemv_launch(&g, s, pdl));
+    // down + residual
+    g = q35_gemv_desc{};
+    g.weight = L.down;
+    g.w_scale = L.down_scale;
+    g.input = B.act;
+    g.resid_out = B.resid;
+    g.n_out = d.hidden;
+    g.k = d.intermediate;
+    g.prologue = Q35_PRO_PLAIN;
+    g.epilogue = Q35_EPI_RESIDUAL;
+    g.int8 = q8;
+    g.eps = d.eps;
+    Q35_TRY(q35_gemv_launch(&g, s, pdl));
+  }
+  q35_step_counters adv = {d.cache_len, d.rope_pos, d.token_log, d.log_pos, d.log_len};
+  return q35_lm_head_launch(B.resid, d.final_norm, d.embed, d.token, d.vocab, d.hidden, d.eps, B.lm_ws, s, pdl, &adv);
+}
+
+extern "C" int q35_decoder_prefill(q35_decoder* dec, const int64_t* ids, int64_t length, void* stream) {
+  Q35_REQUIRE(dec && ids, "prefill: null argument");
+  const q35_decoder_desc& d = dec->d;
+  Q35_REQUIRE(length >= 1 && length <= d.max_prefill && length < d.max_len,
+              "prefill: length %lld outside [1, %d] (cache %d)", (long long)length, d.max_prefill, d.max_len);
+  const Buffers& B = dec->buf;
+  cudaStream_t s = (cudaStream_t)stream;
+  const bool q8 = d.a8w8 != 0;
+  const int64_t H = d.hidden, I = d.intermediate, Lt = length;
+  const int64_t qgkv_rows = 2 * d.q_heads * d.head_dim + 2 * d.kv_heads * d.head_dim;
+  const int64_t conv_dim = (int64_t)d.lin_heads * (2 * d.lin_dk + d.lin_dv);
+  const int64_t vdim = (int64_t)d.lin_heads * d.lin_dv;
+  const int64_t adim = (int64_t)d.q_heads * d.head_dim;
+
+  // Projection helper: bf16 GEMM, or per-token int8 quantisation + int8 GEMM for A8W8.
+  auto proj = [&](const bf16* x, int64_t k, const void* w, const float* sw, void* out, int64_t n, int epi) -> int {
+    if (!q8) return q35_gemm_launch(x, w, out, Lt, n, k, epi, false, nullptr, nullptr, s);
+    int rc = q35_quantize_rows_launch(x, B.p_q8, B.p_sx, Lt, k, s);
+    if (rc) return rc;
+    return q35_gemm_launch(B.p_q8, w, out, Lt, n, k, epi, true, B.p_sx, sw, s);
+  };
+
+  // fresh cache: zero the recurrent/conv states (the KV rows past `length` are never read)
+  for (int i = 0; i < d.n_layers; ++i) {
+    const q35_layer_desc& L = dec->layers[i];
+    if (L.kind == 0) {
+      if (cudaMemsetAsync(L.rec_state, 0, (size_t)d.lin_heads * d.lin_dk * d.lin_dv * sizeof(float), s) !=
+              cudaSuccess ||
+          cudaMemsetAsync(L.conv_state, 0, (size_t)conv_dim * d.conv_kernel * sizeof(bf16), s) != cudaSuccess)
+        return q35_fail(Q35_ECUDA, "prefill: state reset failed");
+    }
+  }
+  Q35_TRY(q35_set_counters_launch(d.cache_len, d.rope_pos, 0, s));
+  Q35_TRY(q35_embedding(ids, d.embed, B.p_resid, Lt, d.vocab, H, s));
+  for (int i = 0; i < d.n_layers; ++i) {
+    const q35_layer_desc& L = dec->layers[i];
+    Q35_TRY(q35_rms_norm(B.p_resid, L.in_ln, B.p_norm, Lt, H, d.eps, s));
+    if (L.kind == 0) {
+      Q35_TRY(proj(B.p_norm, H, L.mix_in, L.mix_in_scale, B.p_packed, d.delta_rows, Q35_EPI_STORE));
+      Q35_TRY(q35_causal_conv1d(B.p_packed, L.conv_w, L.conv_state, B.p_conv, 1, Lt, d.delta_rows, conv_dim,
+                                d.conv_kernel, s));
+      Q35_TRY(q35_delta_recurrent(B.p_conv, B.p_packed, L.a_log, L.dt_bias, L.rec_state, B.p_core, 1, Lt,
+                                  d.lin_heads, d.lin_dk, d.delta_rows, s));
+      Q35_TRY(q35_gated_rms_strided_launch(B.p_core, B.p_packed + conv_dim, d.lin_heads, d.delta_rows, L.gnorm,
+                                           B.p_mix, Lt * d.lin_heads, d.lin_dv, d.eps, s));
+      Q35_TRY(proj(B.p_mix, vdim, L.mix_out, L.mix_out_scale, B.p_resid, H, Q35_EPI_RESIDUAL));
+    } else {
+      Q35_TRY(proj(B.p_norm, H, L.mix_in, L.mix_in_scale, B.p_packed, qgkv_rows, Q35_EPI_STORE));
+      Q35_TRY(q35_qgkv_rope_positions_launch(B.p_packed, L.q_norm, L.k_norm, d.inv_freq, B.p_core, L.k_cache,
+                                             L.v_cache, nullptr, 1, Lt, d.q_heads, d.kv_heads, d.rotary_dim,
+                                             d.max_len, d.eps, s));
+      Q35_TRY(q35_prefill_attention(B.p_core, L.k_cache, L.v_cache, B.p_attn, 1, d.q_heads, d.kv_heads, Lt,
+                                    d.max_len, 0, d.head_dim, 1.0f / sqrtf((float)d.head_dim), s));
+      Q35_TRY(q35_attention_gate_mul(B.p_attn, B.p_packed, B.p_mix, Lt, adim, qgkv_rows, d.head_dim, s));
+      Q35_TRY(proj(B.p_mix, adim, L.mix_out, L.mix_out_scale, B.p_resid, H, Q35_EPI_RESIDUAL));
+    }
+    Q35_TRY(q35_rms_norm(B.p_resid, L.post_ln, B.p_norm, Lt, H, d.eps, s));
+    Q35_TRY(proj(B.p_norm, H, L.gate_up, L.gate_up_scale, B.p_act, I, Q35_EPI_SWIGLU));
+    Q35_TRY(proj(B.p_act, I, L.down, L.down_scale, B.p_resid, H, Q35_EPI_RESIDUAL));
+  }
+  Q35_TRY(q35_lm_head_launch(B.p_resid + (Lt - 1) * H, d.final_norm, d.embed, d.token, d.vocab, H, d.eps, B.lm_ws,
+                             s, false, nullptr));
+  return q35_set_counters_launch(d.cache_len, d.rope_pos, Lt, s);
+}

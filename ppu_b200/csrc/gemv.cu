@@ -1,0 +1,598 @@
+// Batch-1 decode GEMVs and the fused LM-head top-1 (reference: kernels.py:183-263, 1093-1185;
+// F.linear at integration.py:183-185, 245, 272, 298, 359).
+//
+// Design (HBM-bound weight streaming, no tensor cores):
+//  * one warp owns U output units per iteration; each lane streams 16-byte chunks of the unit's
+//    weight row(s) with ld.global.nc.L1::no_allocate, so a warp keeps U*rows*K*esize bytes in
+//    flight; the first group's loads are issued before the prologue (and before the PDL wait),
+//    later groups are prefetched before the reduction of the current one;
+//  * the prologue builds the input vector in shared memory: plain copy, RMSNorm(1+w) of the
+//    residual (folding the reference's residual_add_rms_norm into the consumer), or embedding
+//    gather + RMSNorm; for A8W8 it also quantises the vector per token to int8;
+//  * BF16 dot products accumulate in FP32; int8 dot products use dp4a with exact int32
+//    accumulation and an exact integer warp reduction;
+//  * epilogues: store, in-place residual add (bf16(r + bf16(y))), SwiGLU over row pairs
+//    (n, n + n_out), or top-1 with a packed 64-bit (value, index) atomicMax and a last-CTA
+//    finish that writes the token and re-zeroes the workspace.
+#include <cfloat>
+
+#include "common.cuh"
+
+using namespace q35;
+
+namespace {
+
+constexpr int kWarps = 8;
+constexpr int kThreads = kWarps * 32;
+
+struct GemvParams {
+  const void* weight;
+  const float* w_scale;
+  const bf16* input;
+  const bf16* norm_w;
+  const int64_t* token;
+  const bf16* embed;
+  bf16* resid;
+  bf16* out;
+  int n_out;
+  int k;       // runtime K (generic kernel)
+  int vocab;   // embedding rows (EMBED prologue clamp)
+  float eps;
+};
+
+// ---------------------------------------------------------------------------------------------
+// Prologue: x (bf16, [k]) into shared memory, optional per-token int8 quantisation.
+template <int PRO, bool INT8>
+Q35_DEV void build_input(const GemvParams& p, int k, bf16* xs, int8_t* xq, float* sx_out,
+                         float* red) {
+  const bf16* src = p.input;
+  if (PRO == Q35_PRO_EMBED) {
+    int64_t t = *p.token;
+    t = t < 0 ? 0 : (t >= p.vocab ? p.vocab - 1 : t);
+    src = p.embed + t * (int64_t)k;
+  }
+  const int nv = k >> 3;
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < nv; i += kThreads) {
+    const uint4 v = reinterpret_cast<const uint4*>(src)[i];
+    if (PRO == Q35_PRO_EMBED && blockIdx.x == 0) reinterpret_cast<uint4*>(p.resid)[i] = v;
+    reinterpret_cast<uint4*>(xs)[i] = v;
+    if (PRO != Q35_PRO_PLAIN) {
+      float f[8];
+      unpack_bf16x8(v, f);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss += f[j] * f[j];
+    }
+  }
+  if (PRO != Q35_PRO_PLAIN) {
+    const float var = block_sum<kWarps>(ss, red) / (float)k;
+    const float r = rsqrt_ieee(var + p.eps);
+    for (int i = threadIdx.x; i < nv; i += kThreads) {
+      float f[8], w[8];
+      unpack_bf16x8(reinterpret_cast<const uint4*>(xs)[i], f);
+      unpack_bf16x8(reinterpret_cast<const uint4*>(p.norm_w)[i], w);
+      __align__(16) bf16 o[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[j] = f2bf(f[j] * r * (1.0f + w[j]));
+      reinterpret_cast<uint4*>(xs)[i] = *reinterpret_cast<const uint4*>(o);
+    }
+  }
+  if (INT8) {
+    __syncthreads();
+    float amax = 0.f;
+    for (int i = threadIdx.x; i < k; i += kThreads) amax = fmaxf(amax, fabsf(bf2f(xs[i])));
+    amax = block_max<kWarps>(amax, red);
+    const float s = amax > 0.f ? amax / 127.0f : 1.0f;
+    for (int i = threadIdx.x; i < k; i += kThreads) xq[i] = (int8_t)quant_i8(bf2f(xs[i]), s);
+    if (threadIdx.x == 0) *sx_out = s;
+  }
+  __syncthreads();
+}
+
+Q35_DEV int warp_sum_i(int v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+template <int EPI, bool INT8>
+Q35_DEV void epilogue(const GemvParams& p, int unit, float y0, float y1) {
+  // y0/y1: dequantised (or fp32) results for rows unit / unit + n_out.
+  if (EPI == Q35_EPI_STORE) {
+    p.out[unit] = f2bf(y0);
+  } else if (EPI == Q35_EPI_RESIDUAL) {
+    p.resid[unit] = f2bf(bf2f(p.resid[unit]) + rbf(y0));
+  } else {
+    const float g = rbf(y0), u = rbf(y1);
+    p.out[unit] = f2bf(rbf(silu_f(g)) * u);
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// Fast path: compile-time K. A warp's unit group is streamed in SEG segments of CHS 16-byte
+// chunks per lane (at most 16 chunks = 64 registers in flight per thread); segment i+1 is
+// loaded before segment i is consumed.
+template <int K, bool INT8, int RPU>
+struct FastShape {
+  static constexpr int ES = INT8 ? 1 : 2;
+  static constexpr int CHT = K * ES / 512;                       // chunks per row per lane
+  static constexpr int SEG = (RPU * CHT > 16) ? (RPU * CHT + 15) / 16 : 1;
+  static constexpr int CHS = CHT / SEG;                          // chunks per segment
+  static constexpr int U = (SEG == 1) ? ((16 / (RPU * CHT)) < 1 ? 1 : 16 / (RPU * CHT)) : 1;
+  static_assert(K * ES % 512 == 0, "K must fill whole warp-wide 16-byte chunks");
+  static_assert(CHT % SEG == 0, "segments must split a row evenly");
+};
+
+template <int K, int PRO, int EPI, bool INT8>
+__global__ void __launch_bounds__(kThreads) gemv_fast_kernel(GemvParams p) {
+  constexpr int RPU = (EPI == Q35_EPI_SWIGLU) ? 2 : 1;
+  using Sh = FastShape<K, INT8, RPU>;
+  constexpr int ES = Sh::ES, SEG = Sh::SEG, CHS = Sh::CHS, U = Sh::U;
+  __shared__ __align__(16) bf16 xs[K];
+  __shared__ __align__(16) int8_t xq[INT8 ? K : 16];
+  __shared__ float red[kWarps];
+  __shared__ float sx_s;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_out = p.n_out;
+  const int ngroups = (n_out + U - 1) / U;
+  const int gstride = gridDim.x * kWarps;
+  const int g0 = blockIdx.x * kWarps + warp;
+  const int n_iter = (g0 < ngroups) ? ((ngroups - 1 - g0) / gstride + 1) * SEG : 0;
+  const char* W = static_cast<const char*>(p.weight);
+
+  uint4 wr[U][RPU][CHS];
+  auto load = [&](int it) {
+    const int grp = g0 + (it / SEG) * gstride, seg = it % SEG;
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int unit = grp * U + u;
+#pragma unroll
+      for (int r = 0; r < RPU; ++r) {
+        const int64_t row = unit + (int64_t)r * n_out;
+        const char* base = W + row * (int64_t)(K * ES) + (seg * CHS * 32 + lane) * 16;
+#pragma unroll
+        for (int c = 0; c < CHS; ++c)
+          wr[u][r][c] = (unit < n_out) ? ld_stream(base + c * 512) : make_uint4(0, 0, 0, 0);
+      }
+    }
+  };
+  if (n_iter > 0) load(0);
+  pdl_wait();
+  pdl_launch_dependents();
+  build_input<PRO, INT8>(p, K, xs, xq, &sx_s, red);
+  const float sx = INT8 ? sx_s : 1.0f;
+
+  float accf[U][RPU];
+  int acci[U][RPU];
+  for (int it = 0; it < n_iter; ++it) {
+    const int seg = it % SEG;
+    const int g = g0 + (it / SEG) * gstride;
+    if (seg == 0) {
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+#pragma unroll
+        for (int r = 0; r < RPU; ++r) {
+          accf[u][r] = 0.f;
+          acci[u][r] = 0;
+        }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+#pragma unroll
+      for (int r = 0; r < RPU; ++r) {
+#pragma unroll
+        for (int c = 0; c < CHS; ++c) {
+          const int xi = (seg * CHS + c) * 32 + lane;
+          if (INT8)
+            acci[u][r] = dot_i8x16(wr[u][r][c], reinterpret_cast<const uint4*>(xq)[xi], acci[u][r]);
+          else
+            accf[u][r] = dot_bf16x8(wr[u][r][c], reinterpret_cast<const uint4*>(xs)[xi], accf[u][r]);
+        }
+      }
+    if (it + 1 < n_iter) load(it + 1);
+    if (seg != SEG - 1) continue;
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int unit = g * U + u;
+      float y[RPU];
+#pragma unroll
+      for (int r = 0; r < RPU; ++r) {
+        if (INT8) {
+          const int tot = warp_sum_i(acci[u][r]);
+          const int64_t row = unit + (int64_t)r * n_out;
+          y[r] = ((float)tot * sx) * ((unit < n_out) ? p.w_scale[row] : 0.f);
+        } else {
+          y[r] = warp_sum(accf[u][r]);
+        }
+      }
+      if (lane == 0 && unit < n_out) epilogue<EPI, INT8>(p, unit, y[0], RPU > 1 ? y[RPU - 1] : 0.f);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// Generic path: runtime K (multiple of 8, or of 16 for int8); x in dynamic shared memory.
+template <int PRO, int EPI, bool INT8>
+__global__ void __launch_bounds__(kThreads) gemv_any_kernel(GemvParams p) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  __shared__ float red[kWarps];
+  __shared__ float sx_s;
+  const int k = p.k;
+  bf16* xs = reinterpret_cast<bf16*>(smem_raw);
+  int8_t* xq = reinterpret_cast<int8_t*>(smem_raw + ((2 * k + 15) & ~15));
+  pdl_wait();
+  pdl_launch_dependents();
+  build_input<PRO, INT8>(p, k, xs, xq, &sx_s, red);
+  const float sx = INT8 ? sx_s : 1.0f;
+  constexpr int RPU = (EPI == Q35_EPI_SWIGLU) ? 2 : 1;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int unit = blockIdx.x * kWarps + warp; unit < p.n_out; unit += gridDim.x * kWarps) {
+    float y[2] = {0.f, 0.f};
+#pragma unroll
+    for (int r = 0; r < RPU; ++r) {
+      const int64_t row = unit + (int64_t)r * p.n_out;
+      if (INT8) {
+        const int8_t* wrow = static_cast<const int8_t*>(p.weight) + row * k;
+        int a = 0;
+        for (int c = lane; c < k / 16; c += 32)
+          a = dot_i8x16(ld_stream(wrow + 16 * c), reinterpret_cast<const uint4*>(xq)[c], a);
+        y[r] = ((float)warp_sum_i(a) * sx) * p.w_scale[row];
+      } else {
+        const bf16* wrow = static_cast<const bf16*>(p.weight) + row * k;
+        float a = 0.f;
+        for (int c = lane; c < k / 8; c += 32)
+          a = dot_bf16x8(ld_stream(wrow + 8 * c), reinterpret_cast<const uint4*>(xs)[c], a);
+        y[r] = warp_sum(a);
+      }
+    }
+    if (lane == 0) epilogue<EPI, INT8>(p, unit, y[0], y[1]);
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// LM head: GEMV over the tied embedding with a fused greedy top-1 (kernels.py:1093-1185).
+struct LmWorkspace {
+  unsigned long long key;
+  unsigned int count;
+  unsigned int pad;
+};
+
+struct LmParams {
+  q35_step_counters adv;  // optional: advanced by the last CTA after the token is written
+  const bf16* hidden;
+  const bf16* norm_w;  // nullptr: hidden is already normalised
+  const bf16* weight;
+  int64_t* token_out;
+  LmWorkspace* ws;
+  int vocab;
+  int k;
+  float eps;
+};
+
+Q35_DEV unsigned long long top1_key(float v, int idx) {
+  return ((unsigned long long)float_order_key(v) << 32) | (unsigned long long)(0xFFFFFFFFu - (uint32_t)idx);
+}
+
+Q35_DEV void lm_finish(const LmParams& p, float best_v, int best_i, float* red_v, int* red_i) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) {
+    red_v[warp] = best_v;
+    red_i[warp] = best_i;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float bv = red_v[0];
+    int bi = red_i[0];
+    for (int w = 1; w < kWarps; ++w)
+      if (red_v[w] > bv || (red_v[w] == bv && red_i[w] < bi)) {
+        bv = red_v[w];
+        bi = red_i[w];
+      }
+    if (bi != 0x7fffffff) atomicMax(&p.ws->key, top1_key(bv, bi));
+    __threadfence();
+    const unsigned prev = atomicAdd(&p.ws->count, 1u);
+    if (prev == gridDim.x - 1) {
+      __threadfence();
+      const unsigned long long key = atomicExch(&p.ws->key, 0ull);
+      atomicExch(&p.ws->count, 0u);
+      const int64_t tok = (key == 0ull) ? 0 : (int64_t)(0xFFFFFFFFu - (uint32_t)(key & 0xFFFFFFFFull));
+      p.token_out[0] = tok;
+      if (p.adv.cache_len) *p.adv.cache_len += 1;
+      if (p.adv.rope_pos) *p.adv.rope_pos += 1;
+      if (p.adv.token_log && p.adv.log_pos && p.adv.log_len > 0) {
+        const int64_t pos = *p.adv.log_pos;
+        p.adv.token_log[pos % p.adv.log_len] = tok;
+        *p.adv.log_pos = pos + 1;
+      }
+    }
+  }
+}
+
+template <int K, bool NORM>
+__global__ void __launch_bounds__(kThreads) lm_head_fast_kernel(LmParams p) {
+  constexpr int CH = K * 2 / 512;
+  constexpr int U = 16 / CH < 1 ? 1 : 16 / CH;
+  __shared__ __align__(16) bf16 xs[K];
+  __shared__ float red[kWarps];
+  __shared__ float red_v[kWarps];
+  __shared__ int red_i[kWarps];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int ngroups = (p.vocab + U - 1) / U;
+  const int gstride = gridDim.x * kWarps;
+  int g = blockIdx.x * kWarps + warp;
+  const char* W = reinterpret_cast<const char*>(p.weight);
+  uint4 wr[U][CH];
+  auto load_group = [&](int grp) {
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int row = grp * U + u;
+      const char* base = W + (int64_t)row * (K * 2) + lane * 16;
+#pragma unroll
+      for (int c = 0; c < CH; ++c)
+        wr[u][c] = (row < p.vocab) ? ld_stream(base + c * 512) : make_uint4(0, 0, 0, 0);
+    }
+  };
+  if (g < ngroups) load_group(g);
+  pdl_wait();
+  pdl_launch_dependents();
+  {
+    GemvParams gp = {};
+    gp.input = p.hidden;
+    gp.norm_w = p.norm_w;
+    gp.eps = p.eps;
+    if (NORM)
+      build_input<Q35_PRO_NORM, false>(gp, K, xs, nullptr, nullptr, red);
+    else
+      build_input<Q35_PRO_PLAIN, false>(gp, K, xs, nullptr, nullptr, red);
+  }
+  float best_v = -FLT_MAX;
+  int best_i = 0x7fffffff;
+  for (; g < ngroups; g += gstride) {
+    float acc[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      float a = 0.f;
+#pragma unroll
+      for (int c = 0; c < CH; ++c)
+        a = dot_bf16x8(wr[u][c], reinterpret_cast<const uint4*>(xs)[lane + 32 * c], a);
+      acc[u] = a;
+    }
+    const int gn = g + gstride;
+    if (gn < ngroups) load_group(gn);
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const float v = rbf(warp_sum(acc[u]));  // eager materialises BF16 logits (kernels.py:1119-1121)
+      const int row = g * U + u;
+      if (row < p.vocab && v > best_v) {
+        best_v = v;
+        best_i = row;
+      }
+    }
+  }
+  lm_finish(p, best_v, best_i, red_v, red_i);
+}
+
+template <bool NORM>
+__global__ void __launch_bounds__(kThreads) lm_head_any_kernel(LmParams p) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  __shared__ float red[kWarps];
+  __shared__ float red_v[kWarps];
+  __shared__ int red_i[kWarps];
+  bf16* xs = reinterpret_cast<bf16*>(smem_raw);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  pdl_wait();
+  pdl_launch_dependents();
+  {
+    GemvParams gp = {};
+    gp.input = p.hidden;
+    gp.norm_w = p.norm_w;
+    gp.eps = p.eps;
+    if (NORM)
+      build_input<Q35_PRO_NORM, false>(gp, p.k, xs, nullptr, nullptr, red);
+    else
+      build_input<Q35_PRO_PLAIN, false>(gp, p.k, xs, nullptr, nullptr, red);
+  }
+  float best_v = -FLT_MAX;
+  int best_i = 0x7fffffff;
+  for (int row = blockIdx.x * kWarps + warp; row < p.vocab; row += gridDim.x * kWarps) {
+    const bf16* wrow = p.weight + (int64_t)row * p.k;
+    float a = 0.f;
+    for (int c = lane; c < p.k / 8; c += 32)
+      a = dot_bf16x8(ld_stream(wrow + 8 * c), reinterpret_cast<const uint4*>(xs)[c], a);
+    const float v = rbf(warp_sum(a));
+    if (v > best_v) {
+      best_v = v;
+      best_i = row;
+    }
+  }
+  lm_finish(p, best_v, best_i, red_v, red_i);
+}
+
+// ---------------------------------------------------------------------------------------------
+// Grid choice: at most `max_ctas` resident CTAs; among grids of whole-SM multiples pick the one
+// whose last round of unit groups is the fullest (less tail imbalance between warps).
+int choose_grid(int ngroups, int max_ctas) {
+  const int need = (ngroups + kWarps - 1) / kWarps;
+  if (need <= max_ctas) return need < 1 ? 1 : need;
+  int best = max_ctas;
+  double best_eff = 0.0;
+  for (int ctas = kNumSMs / 2; ctas <= max_ctas; ctas += kNumSMs / 2) {
+    const long warps = (long)ctas * kWarps;
+    const long rounds = (ngroups + warps - 1) / warps;
+    const double eff = (double)ngroups / (double)(rounds * warps);
+    if (eff > best_eff + 1e-3 || (eff > best_eff - 1e-3 && ctas > best)) {
+      best_eff = eff;
+      best = ctas;
+    }
+  }
+  return best;
+}
+
+template <typename KernelT>
+int resident_ctas(KernelT kernel, size_t dyn_smem) {
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kThreads, dyn_smem) != cudaSuccess ||
+      per_sm < 1)
+    per_sm = 1;
+  return per_sm * kNumSMs;
+}
+
+template <int K, int PRO, int EPI, bool INT8>
+int launch_fast(const GemvParams& p, cudaStream_t s, bool pdl) {
+  using Sh = FastShape<K, INT8, (EPI == Q35_EPI_SWIGLU) ? 2 : 1>;
+  static int max_ctas = 0;
+  if (!max_ctas) max_ctas = resident_ctas(gemv_fast_kernel<K, PRO, EPI, INT8>, 0);
+  const int ngroups = (p.n_out + Sh::U - 1) / Sh::U;
+  const int grid = choose_grid(ngroups, max_ctas);
+  cudaError_t e = q35_launch(gemv_fast_kernel<K, PRO, EPI, INT8>, dim3(grid), dim3(kThreads), 0, s, pdl, p);
+  if (e != cudaSuccess) return q35_fail(Q35_ECUDA, "gemv launch: %s", cudaGetErrorString(e));
+  return Q35_OK;
+}
+
+template <int PRO, int EPI, bool INT8>
+int launch_any(const GemvParams& p, cudaStream_t s, bool pdl) {
+  const size_t smem = ((2 * (size_t)p.k + 15) & ~(size_t)15) + (INT8 ? (size_t)p.k : 0);
+  if (smem > 200 * 1024) return q35_fail(Q35_ENOTSUP, "gemv: k=%d too large", p.k);
+  if (smem > 48 * 1024)
+    cudaFuncSetAttribute(gemv_any_kernel<PRO, EPI, INT8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  const int grid = choose_grid(p.n_out, 2 * kNumSMs);
+  cudaError_t e = q35_launch(gemv_any_kernel<PRO, EPI, INT8>, dim3(grid), dim3(kThreads), smem, s, pdl, p);
+  if (e != cudaSuccess) return q35_fail(Q35_ECUDA, "gemv launch: %s", cudaGetErrorString(e));
+  return Q35_OK;
+}
+
+template <int PRO, int EPI, bool INT8>
+int dispatch_k(const GemvParams& p, cudaStream_t s, bool pdl) {
+  if (p.k == 2048) return launch_fast<2048, PRO, EPI, INT8>(p, s, pdl);
+  if constexpr (EPI != Q35_EPI_SWIGLU && PRO == Q35_PRO_PLAIN) {
+    if (p.k == 6144) return launch_fast<6144, PRO, EPI, INT8>(p, s, pdl);
+  }
+  return launch_any<PRO, EPI, INT8>(p, s, pdl);
+}
+
+template <int PRO, int EPI>
+int dispatch_int8(const GemvParams& p, bool int8, cudaStream_t s, bool pdl) {
+  return int8 ? dispatch_k<PRO, EPI, true>(p, s, pdl) : dispatch_k<PRO, EPI, false>(p, s, pdl);
+}
+
+template <int PRO>
+int dispatch_epi(const GemvParams& p, int epi, bool int8, cudaStream_t s, bool pdl) {
+  switch (epi) {
+    case Q35_EPI_STORE: return dispatch_int8<PRO, Q35_EPI_STORE>(p, int8, s, pdl);
+    case Q35_EPI_RESIDUAL: return dispatch_int8<PRO, Q35_EPI_RESIDUAL>(p, int8, s, pdl);
+    case Q35_EPI_SWIGLU: return dispatch_int8<PRO, Q35_EPI_SWIGLU>(p, int8, s, pdl);
+  }
+  return q35_fail(Q35_EINVAL, "gemv: bad epilogue %d", epi);
+}
+
+}  // namespace
+
+// Shared with decoder.cu.
+int q35_gemv_launch(const q35_gemv_desc* d, cudaStream_t s, bool pdl) {
+  Q35_REQUIRE(d && d->weight, "gemv: null descriptor / weight");
+  Q35_REQUIRE(d->n_out > 0 && d->k > 0 && d->k % (d->int8 ? 16 : 8) == 0, "gemv: bad shape n=%lld k=%lld",
+              (long long)d->n_out, (long long)d->k);
+  Q35_REQUIRE(!d->int8 || d->w_scale, "gemv: int8 weights need w_scale");
+  Q35_REQUIRE(Q35_ALIGNED(d->weight, 16), "gemv: weight must be 16-byte aligned");
+  Q35_REQUIRE(d->prologue == Q35_PRO_EMBED ? (d->token && d->embed && d->resid_out && d->norm_weight)
+                                           : (d->input != nullptr),
+              "gemv: prologue inputs missing");
+  Q35_REQUIRE(d->prologue != Q35_PRO_NORM || d->norm_weight, "gemv: norm weight missing");
+  Q35_REQUIRE(d->epilogue == Q35_EPI_RESIDUAL ? d->resid_out != nullptr : d->out != nullptr,
+              "gemv: output missing");
+  GemvParams p = {};
+  p.weight = d->weight;
+  p.w_scale = d->w_scale;
+  p.input = static_cast<const bf16*>(d->input);
+  p.norm_w = static_cast<const bf16*>(d->norm_weight);
+  p.token = d->token;
+  p.embed = static_cast<const bf16*>(d->embed);
+  p.resid = static_cast<bf16*>(d->resid_out);
+  p.out = static_cast<bf16*>(d->out);
+  p.n_out = (int)d->n_out;
+  p.k = (int)d->k;
+  p.vocab = d->vocab > 0 ? (int)d->vocab : (1 << 30);
+  p.eps = d->eps;
+  const bool int8 = d->int8 != 0;
+  switch (d->prologue) {
+    case Q35_PRO_PLAIN: return dispatch_epi<Q35_PRO_PLAIN>(p, d->epilogue, int8, s, pdl);
+    case Q35_PRO_NORM: return dispatch_epi<Q35_PRO_NORM>(p, d->epilogue, int8, s, pdl);
+    case Q35_PRO_EMBED: return dispatch_epi<Q35_PRO_EMBED>(p, d->epilogue, int8, s, pdl);
+  }
+  return q35_fail(Q35_EINVAL, "gemv: bad prologue %d", d->prologue);
+}
+
+int q35_lm_head_launch(const void* hidden, const void* norm_weight, const void* weight,
+                       int64_t* token_out, int64_t vocab, int64_t k, float eps, void* ws,
+                       cudaStream_t s, bool pdl, const q35_step_counters* adv) {
+  LmParams p = {};
+  if (adv) p.adv = *adv;
+  p.hidden = static_cast<const bf16*>(hidden);
+  p.norm_w = static_cast<const bf16*>(norm_weight);
+  p.weight = static_cast<const bf16*>(weight);
+  p.token_out = token_out;
+  p.ws = static_cast<LmWorkspace*>(ws);
+  p.vocab = (int)vocab;
+  p.k = (int)k;
+  p.eps = eps;
+  cudaError_t e;
+  if (k == 2048) {
+    static int max_norm = 0, max_plain = 0;
+    if (!max_norm) max_norm = resident_ctas(lm_head_fast_kernel<2048, true>, 0);
+    if (!max_plain) max_plain = resident_ctas(lm_head_fast_kernel<2048, false>, 0);
+    const int ngroups = (int)((vocab + 1) / 2);
+    if (norm_weight)
+      e = q35_launch(lm_head_fast_kernel<2048, true>, dim3(choose_grid(ngroups, max_norm)), dim3(kThreads), 0, s,
+                     pdl, p);
+    else
+      e = q35_launch(lm_head_fast_kernel<2048, false>, dim3(choose_grid(ngroups, max_plain)), dim3(kThreads), 0,
+                     s, pdl, p);
+  } else {
+    const size_t smem = 2 * (size_t)k;
+    if (smem > 200 * 1024) return q35_fail(Q35_ENOTSUP, "lm_head: hidden size %lld too large", (long long)k);
+    auto kern = norm_weight ? lm_head_any_kernel<true> : lm_head_any_kernel<false>;
+    if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    const int grid = choose_grid((int)vocab, 2 * kNumSMs);
+    e = q35_launch(kern, dim3(grid), dim3(kThreads), smem, s, pdl, p);
+  }
+  if (e != cudaSuccess) return q35_fail(Q35_ECUDA, "lm_head launch: %s", cudaGetErrorString(e));
+  return Q35_OK;
+}
+
+extern "C" int q35_gemv(const q35_gemv_desc* d, void* stream) {
+  return q35_gemv_launch(d, (cudaStream_t)stream, false);
+}
+
+extern "C" int q35_swiglu_gemv(const void* x, const void* packed_weight, void* out, int64_t n_out,
+                               int64_t k, void* stream) {
+  Q35_REQUIRE(x && packed_weight && out, "swiglu_gemv: null pointer");
+  q35_gemv_desc d = {};
+  d.weight = packed_weight;
+  d.input = x;
+  d.out = out;
+  d.n_out = n_out;
+  d.k = k;
+  d.prologue = Q35_PRO_PLAIN;
+  d.epilogue = Q35_EPI_SWIGLU;
+  return q35_gemv_launch(&d, (cudaStream_t)stream, false);
+}
+
+extern "C" size_t q35_lm_head_workspace_size(int64_t batch) {
+  return (size_t)(batch < 1 ? 1 : batch) * sizeof(LmWorkspace);
+}
+
+extern "C" int q35_lm_head_argmax(const void* hidden, const void* norm_weight, const void* weight,
+                                  int64_t* token_out, int64_t batch, int64_t vocab,
+                                  int64_t hidden_size, float eps, void* workspace,
+                                  size_t workspace_bytes, void* stream) {
+  Q35_REQUIRE(hidden && weight && token_out && workspace, "lm_head_argmax: null pointer");
+  Q35_REQUIRE(batch == 1, "lm_head_argmax: batch %lld unsupported (batch 1, as kernels.py:1155)",
+              (long long)batch);
+  Q35_REQUIRE(vocab > 0 && vocab < (1ll << 31) && hidden_size > 0 && hidden_size % 8 == 0,
+              "lm_head_argmax: bad shape");
+  Q35_REQUIRE(workspace_bytes >= q35_lm_head_workspace_size(batch), "lm_head_argmax: workspace too small");
+  Q35_REQUIRE(Q35_ALIGNED(weight, 16) && Q35_ALIGNED(hidden, 16), "lm_head_argmax: 16-byte alignment");
+  return q35_lm_head_launch(hidden, norm_weight, weight, token_out, vocab, hidden_size, eps, workspace,
+                            (cudaStream_t)stream, false, nullptr);
+}

@@ -1,0 +1,215 @@
+// Row norms and elementwise activations (reference: qwen35_fused/kernels.py:24-333).
+//
+// One CTA per row for the 2048-wide norms (the reduction stays on chip); one warp per row for
+// the 128-wide gated norm; vectorised grid-stride loops for the elementwise ops.
+#include "common.cuh"
+
+using namespace q35;
+
+namespace {
+
+constexpr int kRowThreads = 256;
+
+// rows x width RMSNorm(1+w), optional residual add first (kernels.py:24-112).
+template <bool ADD>
+__global__ void __launch_bounds__(kRowThreads) rms_rows_kernel(const bf16* __restrict__ x,
+                                                               const bf16* __restrict__ upd,
+                                                               const bf16* __restrict__ w,
+                                                               bf16* __restrict__ resid_out,
+                                                               bf16* __restrict__ out, int width,
+                                                               float eps) {
+  __shared__ float red[kRowThreads / 32];
+  const int64_t row = blockIdx.x;
+  const bf16* xr = x + row * width;
+  const bf16* ur = ADD ? upd + row * width : nullptr;
+  float ss = 0.f;
+  for (int c = threadIdx.x; c < width; c += kRowThreads) {
+    float v = bf2f(xr[c]);
+    if (ADD) {
+      v = rbf(v + bf2f(ur[c]));
+      resid_out[row * width + c] = f2bf(v);
+    }
+    ss += v * v;
+  }
+  const float var = block_sum<kRowThreads / 32>(ss, red) / (float)width;
+  const float r = rsqrt_ieee(var + eps);
+  for (int c = threadIdx.x; c < width; c += kRowThreads) {
+    float v = bf2f(xr[c]);
+    if (ADD) v = rbf(v + bf2f(ur[c]));
+    out[row * width + c] = f2bf(v * r * (1.0f + bf2f(w[c])));
+  }
+}
+
+// One warp per row: bf16(bf16(bf16(norm(x)) * w) * silu(gate)) (kernels.py:115-155).
+// Gate row r starts at gate + (r / gate_group) * gate_stride + (r % gate_group) * width, so the z
+// block of a packed projection ([L, rows] with `gate_group` heads per token) is read in place.
+__global__ void gated_rms_kernel(const bf16* __restrict__ x, const bf16* __restrict__ gate,
+                                 const bf16* __restrict__ w, bf16* __restrict__ out, int64_t rows,
+                                 int width, float eps, int gate_group, int64_t gate_stride) {
+  const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const bf16* xr = x + row * width;
+  const bf16* gr = gate + (row / gate_group) * gate_stride + (row % gate_group) * width;
+  float ss = 0.f;
+  for (int c = lane; c < width; c += 32) {
+    float v = bf2f(xr[c]);
+    ss += v * v;
+  }
+  const float r = rsqrt_ieee(warp_sum(ss) / (float)width + eps);
+  for (int c = lane; c < width; c += 32) {
+    const float nrm = rbf(bf2f(xr[c]) * r);
+    const float wt = rbf(nrm * bf2f(w[c]));
+    out[row * width + c] = f2bf(wt * silu_f(bf2f(gr[c])));
+  }
+}
+
+__global__ void silu_mul_kernel(const bf16* __restrict__ packed, bf16* __restrict__ out,
+                                int64_t rows, int64_t width) {
+  const int64_t total = rows * width;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / width, c = i - r * width;
+    const float g = bf2f(packed[r * 2 * width + c]);
+    const float u = bf2f(packed[r * 2 * width + width + c]);
+    out[i] = f2bf(rbf(silu_f(g)) * u);
+  }
+}
+
+__global__ void sigmoid_mul_kernel(const bf16* __restrict__ x, const bf16* __restrict__ gate,
+                                   bf16* __restrict__ out, int64_t n) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x)
+    out[i] = f2bf(bf2f(x[i]) * rbf(sigmoid_f(bf2f(gate[i]))));
+}
+
+__global__ void attn_gate_kernel(const bf16* __restrict__ x, const bf16* __restrict__ packed,
+                                 bf16* __restrict__ out, int64_t rows, int64_t hidden,
+                                 int64_t stride, int64_t head_dim) {
+  const int64_t total = rows * hidden;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / hidden, c = i - r * hidden;
+    const int64_t h = c / head_dim, d = c - h * head_dim;
+    const float g = bf2f(packed[r * stride + h * 2 * head_dim + head_dim + d]);
+    out[i] = f2bf(bf2f(x[i]) * rbf(sigmoid_f(g)));
+  }
+}
+
+__global__ void embedding_kernel(const int64_t* __restrict__ ids, const bf16* __restrict__ table,
+                                 bf16* __restrict__ out, int64_t n, int64_t vocab, int64_t width) {
+  const int64_t row = blockIdx.x;
+  if (row >= n) return;
+  int64_t id = ids[row];
+  id = id < 0 ? 0 : (id >= vocab ? vocab - 1 : id);  // clamp: never read outside the table
+  const uint4* src = reinterpret_cast<const uint4*>(table + id * width);
+  uint4* dst = reinterpret_cast<uint4*>(out + row * width);
+  for (int64_t c = threadIdx.x; c < width / 8; c += blockDim.x) dst[c] = src[c];
+}
+
+int grid_for(int64_t n, int threads) {
+  int64_t g = (n + threads - 1) / threads;
+  if (g > 8 * kNumSMs) g = 8 * kNumSMs;
+  return (int)(g < 1 ? 1 : g);
+}
+
+}  // namespace
+
+extern "C" int q35_rms_norm(const void* x, const void* weight, void* out, int64_t rows,
+                            int64_t width, float eps, void* stream) {
+  Q35_REQUIRE(x && weight && out, "rms_norm: null pointer");
+  Q35_REQUIRE(rows >= 0 && width > 0 && width <= 65536, "rms_norm: bad shape rows=%lld width=%lld",
+              (long long)rows, (long long)width);
+  if (rows == 0) return Q35_OK;
+  rms_rows_kernel<false><<<(unsigned)rows, kRowThreads, 0, (cudaStream_t)stream>>>(
+      (const bf16*)x, nullptr, (const bf16*)weight, nullptr, (bf16*)out, (int)width, eps);
+  return q35_check_launch("rms_norm");
+}
+
+extern "C" int q35_residual_add_rms_norm(const void* residual, const void* update,
+                                         const void* weight, void* residual_out, void* norm_out,
+                                         int64_t rows, int64_t width, float eps, void* stream) {
+  Q35_REQUIRE(residual && update && weight && residual_out && norm_out,
+              "residual_add_rms_norm: null pointer");
+  Q35_REQUIRE(rows >= 0 && width > 0 && width <= 65536, "residual_add_rms_norm: bad shape");
+  if (rows == 0) return Q35_OK;
+  rms_rows_kernel<true><<<(unsigned)rows, kRowThreads, 0, (cudaStream_t)stream>>>(
+      (const bf16*)residual, (const bf16*)update, (const bf16*)weight, (bf16*)residual_out,
+      (bf16*)norm_out, (int)width, eps);
+  return q35_check_launch("residual_add_rms_norm");
+}
+
+extern "C" int q35_gated_rms_norm(const void* x, const void* gate, const void* weight, void* out,
+                                  int64_t rows, int64_t width, float eps, void* stream) {
+  Q35_REQUIRE(x && gate && weight && out, "gated_rms_norm: null pointer");
+  Q35_REQUIRE(rows >= 0 && width > 0, "gated_rms_norm: bad shape");
+  if (rows == 0) return Q35_OK;
+  const int rows_per_block = 8;
+  gated_rms_kernel<<<(unsigned)((rows + rows_per_block - 1) / rows_per_block), 32 * rows_per_block, 0,
+                     (cudaStream_t)stream>>>((const bf16*)x, (const bf16*)gate,
+                                             (const bf16*)weight, (bf16*)out, rows, (int)width, eps,
+                                             1, width);
+  return q35_check_launch("gated_rms_norm");
+}
+
+int q35_gated_rms_strided_launch(const void* x, const void* gate, int gate_group, int64_t gate_stride,
+                                 const void* weight, void* out, int64_t rows, int64_t width, float eps,
+                                 cudaStream_t stream) {
+  if (rows == 0) return Q35_OK;
+  const int rows_per_block = 8;
+  gated_rms_kernel<<<(unsigned)((rows + rows_per_block - 1) / rows_per_block), 32 * rows_per_block, 0,
+                     stream>>>((const bf16*)x, (const bf16*)gate, (const bf16*)weight, (bf16*)out, rows,
+                               (int)width, eps, gate_group, gate_stride);
+  return q35_check_launch("gated_rms_strided");
+}
+
+__global__ void set_counters_kernel(int64_t* a, int64_t* b, int64_t value) {
+  if (a) *a = value;
+  if (b) *b = value;
+}
+
+int q35_set_counters_launch(int64_t* a, int64_t* b, int64_t value, cudaStream_t stream) {
+  set_counters_kernel<<<1, 1, 0, stream>>>(a, b, value);
+  return q35_check_launch("set_counters");
+}
+
+extern "C" int q35_silu_and_mul(const void* packed, void* out, int64_t rows, int64_t width,
+                                void* stream) {
+  Q35_REQUIRE(packed && out && rows >= 0 && width > 0, "silu_and_mul: bad argument");
+  if (rows == 0) return Q35_OK;
+  silu_mul_kernel<<<grid_for(rows * width, 256), 256, 0, (cudaStream_t)stream>>>(
+      (const bf16*)packed, (bf16*)out, rows, width);
+  return q35_check_launch("silu_and_mul");
+}
+
+extern "C" int q35_sigmoid_mul(const void* x, const void* gate, void* out, int64_t n,
+                               void* stream) {
+  Q35_REQUIRE(x && gate && out && n >= 0, "sigmoid_mul: bad argument");
+  if (n == 0) return Q35_OK;
+  sigmoid_mul_kernel<<<grid_for(n, 256), 256, 0, (cudaStream_t)stream>>>(
+      (const bf16*)x, (const bf16*)gate, (bf16*)out, n);
+  return q35_check_launch("sigmoid_mul");
+}
+
+extern "C" int q35_attention_gate_mul(const void* x, const void* packed, void* out, int64_t rows,
+                                      int64_t hidden, int64_t packed_stride, int64_t head_dim,
+                                      void* stream) {
+  Q35_REQUIRE(x && packed && out, "attention_gate_mul: null pointer");
+  Q35_REQUIRE(rows >= 0 && head_dim > 0 && hidden % head_dim == 0 && packed_stride >= 2 * hidden,
+              "attention_gate_mul: bad shape");
+  if (rows == 0) return Q35_OK;
+  attn_gate_kernel<<<grid_for(rows * hidden, 256), 256, 0, (cudaStream_t)stream>>>(
+      (const bf16*)x, (const bf16*)packed, (bf16*)out, rows, hidden, packed_stride, head_dim);
+  return q35_check_launch("attention_gate_mul");
+}
+
+extern "C" int q35_embedding(const int64_t* ids, const void* table, void* out, int64_t n,
+                             int64_t vocab, int64_t width, void* stream) {
+  Q35_REQUIRE(ids && table && out && n >= 0 && vocab > 0 && width % 8 == 0,
+              "embedding: bad argument");
+  Q35_REQUIRE(Q35_ALIGNED(table, 16) && Q35_ALIGNED(out, 16), "embedding: 16-byte alignment");
+  if (n == 0) return Q35_OK;
+  embedding_kernel<<<(unsigned)n, 128, 0, (cudaStream_t)stream>>>(ids, (const bf16*)table,
+                                                                 (bf16*)out, n, vocab, width);
+  return q35_check_launch("embedding");
+}

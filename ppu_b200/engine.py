@@ -1,0 +1,251 @@
+"""Device-resident Qwen3.5 text decoder driven through the C ABI decoder loop.
+
+``Qwen35Engine`` packs a Hugging Face-named weight dict the way qwen35_fused/integration.py
+packs the model (integration.py:69-140: [qkv|z|a|b] for DeltaNet, [Q|gate..|K|V] for attention,
+[gate; up] for the MLP), optionally quantises the M/F/L projection groups to A8W8 with the CUDA
+quantiser, allocates the static KV cache, DeltaNet conv/recurrent states and one workspace, and
+creates a ``q35_decoder``. Prefill and each greedy decode step are single C calls on the current
+stream; ``capture`` records decode steps into a CUDA graph (qwen35_fused/graph.py).
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+import time
+
+import torch
+
+from . import lib as L
+from .config import Qwen35Dims
+
+BF16 = torch.bfloat16
+
+
+def rope_inv_freq(rotary_dim: int, theta: float) -> torch.Tensor:
+    """HF Qwen3_5TextRotaryEmbedding.compute_default_rope_parameters, in FP32."""
+    exponent = torch.arange(0, rotary_dim, 2, dtype=torch.int64).to(torch.float32) / rotary_dim
+    return 1.0 / (theta ** exponent)
+
+
+def cache_bucket(input_len: int, max_new_tokens: int) -> int:
+    """Static-cache length bucket of evaluation_wrapper.py:340-341."""
+    need = input_len + max_new_tokens + 1
+    return max(512, (need + 127) // 128 * 128)
+
+
+class Qwen35Engine:
+    def __init__(self, weights: dict, dims: Qwen35Dims = Qwen35Dims(), *, a8w8: bool = False,
+                 max_len: int = 2048, max_prefill: int = 1024, device="cuda", use_pdl: bool = True,
+                 log_len: int = 4096, release_source: bool = False):
+        L.load()
+        dev = torch.device(device)
+        if dev.type != "cuda":
+            raise ValueError("Qwen35Engine runs on a CUDA device only")
+        self.dims = dims
+        self.device = dev
+        self.a8w8 = a8w8
+        self.max_len = max_len
+        self.max_prefill = min(max_prefill, max_len - 1)
+        self._keep: list[torch.Tensor] = []
+
+        def w(name):
+            t = weights[name]
+            if release_source:
+                weights[name] = None
+            return t.to(device=dev, dtype=BF16).contiguous()
+
+        d = dims
+        self.layer_descs = (L.LayerDesc * d.layers)()
+        self.conv_states, self.rec_states, self.k_caches, self.v_caches = [], [], [], []
+        self.layer_tensors = []
+        for i, kind in enumerate(d.layer_types):
+            p = f"model.layers.{i}."
+            T: dict[str, torch.Tensor] = {
+                "in_ln": w(p + "input_layernorm.weight"),
+                "post_ln": w(p + "post_attention_layernorm.weight"),
+                "gate_up": torch.cat((w(p + "mlp.gate_proj.weight"), w(p + "mlp.up_proj.weight")), 0).contiguous(),
+                "down": w(p + "mlp.down_proj.weight"),
+            }
+            ld = self.layer_descs[i]
+            if kind == "linear_attention":
+                la = p + "linear_attn."
+                packed = torch.cat((w(la + "in_proj_qkv.weight"), w(la + "in_proj_z.weight"),
+                                    w(la + "in_proj_a.weight"), w(la + "in_proj_b.weight")), 0)
+                pad = d.delta_rows - packed.shape[0]
+                if pad:
+                    packed = torch.cat((packed, packed.new_zeros(pad, packed.shape[1])), 0)
+                T["mix_in"] = packed.contiguous()
+                T["mix_out"] = w(la + "out_proj.weight")
+                T["conv_w"] = w(la + "conv1d.weight").reshape(d.conv_dim, d.conv_kernel).contiguous()
+                T["a_log"] = w(la + "A_log")
+                T["dt_bias"] = w(la + "dt_bias")
+                T["gnorm"] = w(la + "norm.weight")
+                T["conv_state"] = torch.zeros(1, d.conv_dim, d.conv_kernel, device=dev, dtype=BF16)
+                T["rec_state"] = torch.zeros(1, d.lin_heads, d.lin_dk, d.lin_dv, device=dev, dtype=torch.float32)
+                self.conv_states.append(T["conv_state"])
+                self.rec_states.append(T["rec_state"])
+                ld.kind = 0
+            else:
+                sa = p + "self_attn."
+                T["mix_in"] = torch.cat((w(sa + "q_proj.weight"), w(sa + "k_proj.weight"),
+                                         w(sa + "v_proj.weight")), 0).contiguous()
+                T["mix_out"] = w(sa + "o_proj.weight")
+                T["q_norm"] = w(sa + "q_norm.weight")
+                T["k_norm"] = w(sa + "k_norm.weight")
+                T["k_cache"] = torch.zeros(1, d.kv_heads, max_len, d.head_dim, device=dev, dtype=BF16)
+                T["v_cache"] = torch.zeros_like(T["k_cache"])
+                self.k_caches.append(T["k_cache"])
+                self.v_caches.append(T["v_cache"])
+                ld.kind = 1
+            if a8w8:
+                for key in ("mix_in", "mix_out", "gate_up", "down"):
+                    q, s = self._quantize(T[key])
+                    T[key] = q
+                    T[key + "_scale"] = s
+            for key in ("in_ln", "post_ln", "mix_in", "mix_out", "gate_up", "down", "conv_w", "a_log", "dt_bias",
+                        "gnorm", "conv_state", "rec_state", "q_norm", "k_norm", "k_cache", "v_cache",
+                        "mix_in_scale", "mix_out_scale", "gate_up_scale", "down_scale"):
+                if key in T:
+                    setattr(ld, key, T[key].data_ptr())
+            self.layer_tensors.append(T)
+        self.embed = w("model.embed_tokens.weight")
+        self.final_norm = w("model.norm.weight")
+        self.inv_freq = rope_inv_freq(d.rotary_dim, d.rope_theta).to(dev)
+        self.token = torch.zeros(1, device=dev, dtype=torch.int64)
+        self.cache_len = torch.zeros(1, device=dev, dtype=torch.int64)
+        self.rope_pos = torch.zeros(1, device=dev, dtype=torch.int64)
+        self.log_len = log_len
+        self.token_log = torch.zeros(max(log_len, 1), device=dev, dtype=torch.int64)
+        self.log_pos = torch.zeros(1, device=dev, dtype=torch.int64)
+
+        desc = L.DecoderDesc()
+        desc.n_layers, desc.hidden, desc.intermediate, desc.vocab = d.layers, d.hidden, d.intermediate, d.vocab
+        desc.q_heads, desc.kv_heads, desc.head_dim, desc.rotary_dim = d.q_heads, d.kv_heads, d.head_dim, d.rotary_dim
+        desc.lin_heads, desc.lin_dk, desc.lin_dv = d.lin_heads, d.lin_dk, d.lin_dv
+        desc.conv_kernel, desc.delta_rows = d.conv_kernel, d.delta_rows
+        desc.max_len, desc.max_prefill, desc.a8w8, desc.eps = max_len, self.max_prefill, int(a8w8), d.eps
+        desc.layers = self.layer_descs
+        desc.embed, desc.final_norm, desc.inv_freq = self.embed.data_ptr(), self.final_norm.data_ptr(), \
+            self.inv_freq.data_ptr()
+        desc.token, desc.cache_len, desc.rope_pos = self.token.data_ptr(), self.cache_len.data_ptr(), \
+            self.rope_pos.data_ptr()
+        desc.token_log = self.token_log.data_ptr() if log_len > 0 else None
+        desc.log_pos = self.log_pos.data_ptr()
+        desc.log_len = log_len
+        desc.use_pdl = int(use_pdl)
+        size = L.load().q35_decoder_workspace_size(C.byref(desc))
+        self.workspace = torch.zeros(size, device=dev, dtype=torch.uint8)
+        desc.workspace, desc.workspace_bytes = self.workspace.data_ptr(), size
+        self.desc = desc
+        handle = C.c_void_p()
+        L.check(L.load().q35_decoder_create(C.byref(desc), C.byref(handle)), "q35_decoder_create")
+        self.handle = handle
+        self.kernels_per_step = L.load().q35_decoder_kernels_per_step(handle)
+        self._graphs: dict[int, torch.cuda.CUDAGraph] = {}
+
+    def __del__(self):
+        h = getattr(self, "handle", None)
+        if h is not None and h.value:
+            try:
+                L.load().q35_decoder_destroy(h)
+            except Exception:
+                pass
+
+    def _quantize(self, w: torch.Tensor):
+        q = torch.empty(w.shape, device=w.device, dtype=torch.int8)
+        s = torch.empty(w.shape[0], device=w.device, dtype=torch.float32)
+        L.call("q35_quantize_rows", w.data_ptr(), q.data_ptr(), s.data_ptr(), w.shape[0], w.shape[1],
+               L.stream_of(w.device))
+        return q, s
+
+    # ------------------------------------------------------------------ steps
+    def prefill(self, ids: torch.Tensor) -> torch.Tensor:
+        """Prefill device token ids ``[L]`` from an empty cache; the greedy first token lands in
+        ``self.token`` (returned, on device)."""
+        ids = ids.reshape(-1)
+        if ids.device != self.device or ids.dtype != torch.int64:
+            raise ValueError("prefill expects int64 token ids on the engine's device")
+        n = ids.numel()
+        if n > self.max_prefill:
+            raise ValueError(f"prompt of {n} tokens exceeds max_prefill={self.max_prefill}")
+        L.check(L.load().q35_decoder_prefill(self.handle, ids.data_ptr(), n, L.stream_of(self.device)),
+                "q35_decoder_prefill")
+        return self.token
+
+    def decode_step(self) -> torch.Tensor:
+        """One greedy decode step on the current stream (reads/writes ``self.token``)."""
+        L.check(L.load().q35_decoder_decode_step(self.handle, L.stream_of(self.device)), "q35_decoder_decode_step")
+        return self.token
+
+    def capture(self, steps: int = 1) -> torch.cuda.CUDAGraph:
+        """CUDA graph of ``steps`` consecutive decode steps (graph.py:50-79)."""
+        if steps in self._graphs:
+            return self._graphs[steps]
+        side = torch.cuda.Stream(self.device)
+        side.wait_stream(torch.cuda.current_stream(self.device))
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(side):
+            with torch.cuda.graph(g, stream=side):
+                for _ in range(steps):
+                    self.decode_step()
+        torch.cuda.current_stream(self.device).wait_stream(side)
+        self._graphs[steps] = g
+        return g
+
+    # ------------------------------------------------------------------ state
+    def snapshot(self) -> dict:
+        """Copies of every piece of mutable decoding state (for restoring after warm-up)."""
+        return {"conv": [t.clone() for t in self.conv_states], "rec": [t.clone() for t in self.rec_states],
+                "k": [t.clone() for t in self.k_caches], "v": [t.clone() for t in self.v_caches],
+                "token": self.token.clone(), "cache_len": self.cache_len.clone(), "rope_pos": self.rope_pos.clone()}
+
+    def restore(self, snap: dict) -> None:
+        for dst, src in zip(self.conv_states, snap["conv"]):
+            dst.copy_(src)
+        for dst, src in zip(self.rec_states, snap["rec"]):
+            dst.copy_(src)
+        for dst, src in zip(self.k_caches, snap["k"]):
+            dst.copy_(src)
+        for dst, src in zip(self.v_caches, snap["v"]):
+            dst.copy_(src)
+        self.token.copy_(snap["token"])
+        self.cache_len.copy_(snap["cache_len"])
+        self.rope_pos.copy_(snap["rope_pos"])
+
+    # ------------------------------------------------------------------ generation
+    def generate(self, prompt_ids, max_new_tokens: int, *, eos_ids=(), use_graph: bool = True,
+                 graph_steps: int = 1):
+        """Greedy generation from host token ids, mirroring evaluation_wrapper.py:307-441:
+        H2D copy of the prompt, prefill, first token read on the host (TTFT), then one decode
+        step per token with a host read of each token (EOS check). Returns
+        ``(tokens, ttft_s, elapsed_s)``."""
+        eos = set(int(e) for e in eos_ids)
+        host = torch.as_tensor(prompt_ids, dtype=torch.int64).reshape(-1)
+        if not host.is_pinned():
+            host = host.pin_memory()
+        start = time.perf_counter()
+        ids = host.to(self.device, non_blocking=True)
+        self.prefill(ids)
+        tokens = [int(self.token.item())]
+        first_at = time.perf_counter()
+        graph = self.capture(graph_steps) if (use_graph and max_new_tokens > 1) else None
+        while len(tokens) < max_new_tokens and tokens[-1] not in eos:
+            if graph is not None:
+                graph.replay()
+                if graph_steps == 1:
+                    new = [int(self.token.item())]
+                else:
+                    pos = int(self.log_pos.item())
+                    idx = [(pos - graph_steps + j) % self.log_len for j in range(graph_steps)]
+                    new = [int(v) for v in self.token_log[idx].tolist()]
+            else:
+                self.decode_step()
+                new = [int(self.token.item())]
+            for t in new:
+                if len(tokens) >= max_new_tokens:
+                    break
+                tokens.append(t)
+                if t in eos:
+                    break
+        end = time.perf_counter()
+        return tokens, first_at - start, end - start

@@ -1,0 +1,384 @@
+"""Drop-in replacement for the reference's ``qwen35_fused.kernels`` (text-decoder operators).
+
+Same function names, keyword-only arguments, output shapes and ``ValueError`` checks as
+qwen35_fused/kernels.py; every call launches hand-written sm_100a CUDA through the C ABI
+(``include/qwen35_b200.h``) on the current stream. Outputs are allocated with ``torch.empty``
+from PyTorch's caching allocator (so calls stay CUDA-graph capturable); the K/V cache, conv
+state and recurrent state are updated in place exactly where the reference does so.
+Triton tile knobs (``block_n``, ``block_k``, ``block_v``, ``splits``) are accepted and ignored.
+
+Added beyond the reference: ``quantize_rows`` / ``a8w8_linear`` / ``int8_gemm`` (the A8W8
+linear of explore_runtime_quantization.py:129-181), ``gemm`` (prefill projection with fused
+epilogues), ``fused_gemv`` (decode GEMV with fused norm / residual / SwiGLU), ``attn_decode`` and
+``delta_decode`` (one-kernel decode mixers), and a batch dimension for ``gqa_decode_attention``.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import lib as L
+
+BF16 = torch.bfloat16
+
+
+def _rows_and_width(x: torch.Tensor) -> tuple[int, int]:
+    """kernels.py:16-21."""
+    if not x.is_cuda:
+        raise ValueError("fused kernels require a CUDA tensor")
+    if not x.is_contiguous():
+        raise ValueError("fused kernels require contiguous input")
+    return x.numel() // x.shape[-1], x.shape[-1]
+
+
+def _need_bf16(*ts: torch.Tensor) -> None:
+    for t in ts:
+        if t.dtype != BF16:
+            raise ValueError(f"expected bfloat16 tensor, got {t.dtype}")
+
+
+def _s(t: torch.Tensor) -> int:
+    return L.stream_of(t.device)
+
+
+# ---------------------------------------------------------------------------- norms / activations
+def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
+    """Qwen3.5 RMSNorm: FP32 reduction and direct BF16 output (kernels.py:44-53)."""
+    rows, width = _rows_and_width(x)
+    if weight.numel() != width:
+        raise ValueError(f"weight has {weight.numel()} values, expected {width}")
+    _need_bf16(x, weight)
+    out = torch.empty_like(x)
+    L.call("q35_rms_norm", L.ptr(x), L.ptr(weight.contiguous()), L.ptr(out), rows, width, eps, _s(x))
+    return out
+
+
+def residual_add_rms_norm(residual, update, weight, eps: float = 1e-6):
+    """Return ``(residual + update, RMSNorm(residual + update))`` in one launch (kernels.py:85-112)."""
+    if residual.shape != update.shape or residual.dtype != update.dtype:
+        raise ValueError("residual and update must have identical shape and dtype")
+    rows, width = _rows_and_width(residual)
+    if not update.is_contiguous():
+        raise ValueError("update must be contiguous")
+    _need_bf16(residual, weight)
+    residual_out = torch.empty_like(residual)
+    norm_out = torch.empty_like(residual)
+    L.call("q35_residual_add_rms_norm", L.ptr(residual), L.ptr(update), L.ptr(weight.contiguous()),
+           L.ptr(residual_out), L.ptr(norm_out), rows, width, eps, _s(residual))
+    return residual_out, norm_out
+
+
+def gated_rms_norm(x, gate, weight, eps: float = 1e-6):
+    """Qwen3.5 gated RMSNorm with eager-compatible intermediate rounding (kernels.py:139-155)."""
+    if x.shape != gate.shape:
+        raise ValueError("x and gate must have identical shape")
+    rows, width = _rows_and_width(x)
+    if not gate.is_contiguous():
+        raise ValueError("gate must be contiguous")
+    _need_bf16(x, gate, weight)
+    out = torch.empty_like(x)
+    L.call("q35_gated_rms_norm", L.ptr(x), L.ptr(gate), L.ptr(weight.contiguous()), L.ptr(out), rows, width,
+           eps, _s(x))
+    return out
+
+
+def silu_and_mul(packed: torch.Tensor) -> torch.Tensor:
+    """Apply SiLU to the first half and multiply the second half (kernels.py:170-180)."""
+    rows, packed_width = _rows_and_width(packed)
+    if packed_width % 2:
+        raise ValueError("packed last dimension must be even")
+    _need_bf16(packed)
+    width = packed_width // 2
+    out = torch.empty((*packed.shape[:-1], width), device=packed.device, dtype=packed.dtype)
+    L.call("q35_silu_and_mul", L.ptr(packed), L.ptr(out), rows, width, _s(packed))
+    return out
+
+
+def sigmoid_mul(x: torch.Tensor, gate: torch.Tensor) -> torch.Tensor:
+    """kernels.py:276-282."""
+    if x.shape != gate.shape or not x.is_contiguous() or not gate.is_contiguous():
+        raise ValueError("x and gate must be contiguous tensors with identical shape")
+    _rows_and_width(x)
+    _need_bf16(x, gate)
+    out = torch.empty_like(x)
+    L.call("q35_sigmoid_mul", L.ptr(x), L.ptr(gate), L.ptr(out), x.numel(), _s(x))
+    return out
+
+
+def attention_gate_mul(x: torch.Tensor, packed_qgkv: torch.Tensor, head_dim: int) -> torch.Tensor:
+    """Multiply attention output by a gate stored inside packed QGKV output (kernels.py:312-333)."""
+    if not x.is_contiguous() or not packed_qgkv.is_contiguous():
+        raise ValueError("attention gate tensors must be contiguous")
+    hidden = x.shape[-1]
+    if packed_qgkv.shape[:-1] != x.shape[:-1]:
+        raise ValueError("attention output and packed projection rows do not match")
+    _rows_and_width(x)
+    _need_bf16(x, packed_qgkv)
+    out = torch.empty_like(x)
+    rows = x.numel() // hidden
+    L.call("q35_attention_gate_mul", L.ptr(x), L.ptr(packed_qgkv), L.ptr(out), rows, hidden,
+           packed_qgkv.shape[-1], head_dim, _s(x))
+    return out
+
+
+# ---------------------------------------------------------------------------- GEMV / GEMM
+def ppu_swiglu_gemv(x: torch.Tensor, packed_weight: torch.Tensor, *, block_n: int = 8) -> torch.Tensor:
+    """Decode-only packed gate/up projection with fused SwiGLU (kernels.py:232-263)."""
+    if x.ndim != 3 or x.shape[:2] != (1, 1) or x.dtype != BF16:
+        raise ValueError("SwiGLU GEMV expects BF16 x[1,1,K]")
+    if packed_weight.ndim != 2 or packed_weight.shape[0] % 2:
+        raise ValueError("packed SwiGLU weight must have shape [2N,K]")
+    if packed_weight.shape[1] != x.shape[-1] or packed_weight.dtype != x.dtype:
+        raise ValueError("SwiGLU GEMV input and weight dimensions do not match")
+    if not x.is_contiguous() or not packed_weight.is_contiguous():
+        raise ValueError("SwiGLU GEMV tensors must be contiguous")
+    if not x.is_cuda:
+        raise ValueError("fused kernels require a CUDA tensor")
+    if block_n not in (2, 4, 8):
+        raise ValueError("SwiGLU GEMV block_n must be 2, 4 or 8")
+    n = packed_weight.shape[0] // 2
+    out = torch.empty((1, 1, n), device=x.device, dtype=x.dtype)
+    L.call("q35_swiglu_gemv", L.ptr(x), L.ptr(packed_weight), L.ptr(out), n, x.shape[-1], _s(x))
+    return out
+
+
+def fused_gemv(weight, x=None, *, prologue=L.PRO_PLAIN, epilogue=L.EPI_STORE, norm_weight=None, w_scale=None,
+               token=None, embed=None, resid=None, n_out=None, eps: float = 1e-6):
+    """Batch-1 decode GEMV with the decoder's fused prologue/epilogue (``q35_gemv``).
+
+    Returns the output vector (STORE / SWIGLU) or the updated ``resid`` (RESIDUAL / EMBED)."""
+    int8 = weight.dtype == torch.int8
+    k = weight.shape[1]
+    rows = weight.shape[0]
+    if n_out is None:
+        n_out = rows // 2 if epilogue == L.EPI_SWIGLU else rows
+    out = None
+    if epilogue != L.EPI_RESIDUAL:
+        out = torch.empty(n_out, device=weight.device, dtype=BF16)
+    d = L.GemvDesc(weight=L.ptr(weight), w_scale=L.ptr(w_scale), input=L.ptr(x), norm_weight=L.ptr(norm_weight),
+                   token=L.ptr(token), embed=L.ptr(embed), resid_out=L.ptr(resid), out=L.ptr(out), n_out=n_out, k=k,
+                   vocab=0 if embed is None else embed.shape[0], prologue=prologue, epilogue=epilogue,
+                   int8=int(int8), eps=eps)
+    L.check(L.load().q35_gemv(L.C.byref(d), L.stream_of(weight.device)), "q35_gemv")
+    return out if out is not None else resid
+
+
+def gemm(a: torch.Tensor, weight: torch.Tensor, *, epilogue=L.EPI_STORE, out=None) -> torch.Tensor:
+    """Prefill projection ``a [M,K] @ weight [N,K]^T`` (bf16; RESIDUAL adds into ``out`` in place)."""
+    _need_bf16(a, weight)
+    m, k = a.reshape(-1, a.shape[-1]).shape
+    n = weight.shape[0] // 2 if epilogue == L.EPI_SWIGLU else weight.shape[0]
+    if epilogue == L.EPI_RESIDUAL:
+        if out is None:
+            raise ValueError("RESIDUAL epilogue needs the residual tensor as `out`")
+    elif out is None:
+        out = torch.empty((*a.shape[:-1], n), device=a.device, dtype=BF16)
+    L.call("q35_gemm_bf16", L.ptr(a), L.ptr(weight), L.ptr(out), m, n, k, epilogue, _s(a))
+    return out
+
+
+# ---------------------------------------------------------------------------- A8W8
+def quantize_rows(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Per-row symmetric int8 (explore_runtime_quantization.py:143-155 / vllm per-token)."""
+    rows, width = _rows_and_width(x)
+    _need_bf16(x)
+    q = torch.empty(x.shape, device=x.device, dtype=torch.int8)
+    scale = torch.empty((*x.shape[:-1], 1), device=x.device, dtype=torch.float32)
+    L.call("q35_quantize_rows", L.ptr(x), L.ptr(q), L.ptr(scale), rows, width, _s(x))
+    return q, scale
+
+
+def int8_gemm(qx: torch.Tensor, qw: torch.Tensor) -> torch.Tensor:
+    """Exact int32 ``qx @ qw^T``."""
+    m, k = qx.reshape(-1, qx.shape[-1]).shape
+    acc = torch.empty((m, qw.shape[0]), device=qx.device, dtype=torch.int32)
+    L.call("q35_int8_gemm_i32", L.ptr(qx), L.ptr(qw), L.ptr(acc), m, qw.shape[0], k, _s(qx))
+    return acc
+
+
+def a8w8_linear(x: torch.Tensor, qw: torch.Tensor, w_scale: torch.Tensor) -> torch.Tensor:
+    """Dynamic per-token A8W8 linear: ``bf16((float(q_x q_w^T) * s_x) * s_w)``."""
+    _rows_and_width(x)
+    _need_bf16(x)
+    m, k = x.reshape(-1, x.shape[-1]).shape
+    n = qw.shape[0]
+    if m == 1:
+        out = fused_gemv(qw, x.reshape(-1).contiguous(), w_scale=w_scale.reshape(-1).contiguous())
+        return out.reshape(*x.shape[:-1], n)
+    size = L.load().q35_a8w8_linear_workspace_size(m, k)
+    ws = torch.empty(size, device=x.device, dtype=torch.uint8)
+    out = torch.empty((*x.shape[:-1], n), device=x.device, dtype=BF16)
+    L.call("q35_a8w8_linear", L.ptr(x), L.ptr(qw), L.ptr(w_scale), L.ptr(out), m, n, k, L.ptr(ws), size, _s(x))
+    return out
+
+
+# ---------------------------------------------------------------------------- attention
+def qgkv_norm_rope(packed_qgkv, q_weight, k_weight, cos, sin, *, q_heads, kv_heads, dim, rotary_dim,
+                   cache_key=None, cache_value=None, cache_start=None):
+    """Layout packed Q+gate/K/V and fuse Q/K RMSNorm with partial RoPE (kernels.py:507-573)."""
+    if not packed_qgkv.is_contiguous():
+        raise ValueError("packed QGKV must be contiguous")
+    batch, seq_len, packed_width = packed_qgkv.shape
+    expected = 2 * q_heads * dim + 2 * kv_heads * dim
+    if packed_width != expected:
+        raise ValueError(f"packed QGKV width {packed_width}, expected {expected}")
+    cos = cos.to(BF16).contiguous()
+    sin = sin.to(BF16).contiguous()
+    if cos.shape != (batch, seq_len, rotary_dim) or sin.shape != cos.shape:
+        raise ValueError(f"RoPE shape {tuple(cos.shape)}, expected {(batch, seq_len, rotary_dim)}")
+    _rows_and_width(packed_qgkv)
+    q = torch.empty((batch, q_heads, seq_len, dim), device=packed_qgkv.device, dtype=packed_qgkv.dtype)
+    if cache_key is not None:
+        if cache_value is None or cache_start is None:
+            raise ValueError("cache key, value and start must be provided together")
+        if cache_key.shape[:2] != (batch, kv_heads) or cache_key.shape[-1] != dim:
+            raise ValueError("static K cache shape does not match QGKV")
+        if cache_value.shape != cache_key.shape:
+            raise ValueError("static K/V cache shapes must match")
+        k, v = cache_key, cache_value
+        kv_len = cache_key.shape[-2]
+        start = cache_start if cache_start.dtype == torch.int64 else cache_start.to(torch.int64)
+    else:
+        k = torch.empty((batch, kv_heads, seq_len, dim), device=packed_qgkv.device, dtype=packed_qgkv.dtype)
+        v = torch.empty_like(k)
+        kv_len = seq_len
+        start = None
+    L.call("q35_qgkv_norm_rope", L.ptr(packed_qgkv), L.ptr(q_weight.contiguous()), L.ptr(k_weight.contiguous()),
+           L.ptr(cos), L.ptr(sin), L.ptr(q), L.ptr(k), L.ptr(v), L.ptr(start), batch, seq_len, q_heads, kv_heads,
+           dim, rotary_dim, kv_len, 1e-6, _s(packed_qgkv))
+    return q, k, v
+
+
+def gqa_decode_attention(q, cache_keys, cache_values, valid_length, scale: float, *, splits: int = 4,
+                         block_n: int = 64):
+    """One decode attention step over a static cache (kernels.py:1031-1090); batch >= 1 here.
+
+    ``q [B,H,1,D]``, caches ``[B,KVH,L,D]``, ``valid_length`` a device scalar including the
+    current token. Returns ``[B, 1, H*D]``."""
+    if q.ndim != 4 or q.shape[2] != 1:
+        raise ValueError("GQA decode attention expects q[B,H,1,D]")
+    if cache_keys.ndim != 4 or cache_keys.shape[0] != q.shape[0]:
+        raise ValueError("static K cache must be [B,KVH,L,D]")
+    if cache_values.shape != cache_keys.shape:
+        raise ValueError("static K/V cache shapes must match")
+    if not q.is_contiguous() or not cache_keys.is_contiguous() or not cache_values.is_contiguous():
+        raise ValueError("GQA decode attention tensors must be contiguous")
+    batch, heads, head_dim = q.shape[0], q.shape[1], q.shape[3]
+    kv_heads, cache_len = cache_keys.shape[1], cache_keys.shape[2]
+    if head_dim != cache_keys.shape[3] or heads % kv_heads:
+        raise ValueError("GQA decode attention head layout does not match cache")
+    n_valid = valid_length.reshape(-1)[:1].to(torch.int64)
+    size = L.load().q35_gqa_decode_workspace_size(batch, heads, kv_heads, head_dim, cache_len)
+    ws = torch.empty(size, device=q.device, dtype=torch.uint8)
+    ws[:256].zero_()
+    out = torch.empty((batch, 1, heads * head_dim), device=q.device, dtype=q.dtype)
+    L.call("q35_gqa_decode_attention", L.ptr(q), L.ptr(cache_keys), L.ptr(cache_values), L.ptr(n_valid), scale,
+           L.ptr(out), batch, heads, kv_heads, head_dim, cache_len, L.ptr(ws), size, _s(q))
+    return out
+
+
+def attn_decode(packed, q_weight, k_weight, inv_freq, cache_key, cache_value, cache_len, rope_pos, *, q_heads,
+                kv_heads, rotary_dim, eps: float = 1e-6):
+    """Whole decode attention mixer in one kernel: ``packed [B, 2HqD+2HkvD]`` -> gated ``[B, Hq*D]``.
+
+    Writes the token's K/V at row ``cache_len`` (not advanced here)."""
+    batch = packed.shape[0]
+    dim = cache_key.shape[-1]
+    max_len = cache_key.shape[2]
+    size = L.load().q35_attn_decode_workspace_size(batch, q_heads, kv_heads, dim, max_len)
+    ws = torch.empty(size, device=packed.device, dtype=torch.uint8)
+    ws[:256].zero_()
+    out = torch.empty((batch, q_heads * dim), device=packed.device, dtype=BF16)
+    L.call("q35_attn_decode", L.ptr(packed), L.ptr(q_weight), L.ptr(k_weight), L.ptr(inv_freq), L.ptr(cache_key),
+           L.ptr(cache_value), L.ptr(cache_len), L.ptr(rope_pos), L.ptr(out), batch, q_heads, kv_heads, dim,
+           rotary_dim, max_len, eps, L.ptr(ws), size, _s(packed))
+    return out
+
+
+def prefill_attention(q, k, v, scale: float, q_offset: int = 0) -> torch.Tensor:
+    """Causal GQA attention ``q [B,Hq,L,D]`` over ``k/v [B,Hkv,S,D]`` -> ``[B, L, Hq*D]``."""
+    b, hq, length, dim = q.shape
+    out = torch.empty((b, length, hq * dim), device=q.device, dtype=BF16)
+    L.call("q35_prefill_attention", L.ptr(q), L.ptr(k), L.ptr(v), L.ptr(out), b, hq, k.shape[1], length,
+           k.shape[2], q_offset, dim, scale, _s(q))
+    return out
+
+
+# ---------------------------------------------------------------------------- DeltaNet
+def causal_conv1d_fused(x: torch.Tensor, weight: torch.Tensor, state: torch.Tensor) -> torch.Tensor:
+    """Causal depthwise conv + SiLU, updating ``state`` in place (kernels.py:659-710)."""
+    if x.ndim != 3 or weight.ndim != 2 or state.ndim != 3:
+        raise ValueError("expected x[B,L,C], weight[C,K], state[B,C,K]")
+    if not x.is_contiguous() or not weight.is_contiguous() or not state.is_contiguous():
+        raise ValueError("causal conv tensors must be contiguous")
+    batch, seq_len, input_stride = x.shape
+    channels, kernel_size = weight.shape
+    if input_stride < channels or state.shape != (batch, channels, kernel_size):
+        raise ValueError("causal conv shapes do not match")
+    _rows_and_width(x)
+    out = torch.empty((batch, seq_len, channels), device=x.device, dtype=x.dtype)
+    L.call("q35_causal_conv1d", L.ptr(x), L.ptr(weight), L.ptr(state), L.ptr(out), batch, seq_len, input_stride,
+           channels, kernel_size, _s(x))
+    return out
+
+
+def delta_recurrent_fused(qkv, packed_projection, a_log, dt_bias, state, *, block_v: int = 8,
+                          precompute_factors: bool = False):
+    """Sequential gated-delta recurrence for prefill and decode; ``state`` updated in place
+    (kernels.py:854-937). ``qkv [B,L,3HD]``; ``packed_projection`` holds ``[qkv,z,a,b]``."""
+    if qkv.ndim != 3 or packed_projection.ndim != 3 or state.ndim != 4:
+        raise ValueError("invalid delta recurrent tensor rank")
+    if not qkv.is_contiguous() or not packed_projection.is_contiguous() or not state.is_contiguous():
+        raise ValueError("delta recurrent tensors must be contiguous")
+    batch, seq_len, qkv_width = qkv.shape
+    _, heads, dim, value_dim = state.shape
+    if dim != value_dim or qkv_width != 3 * heads * dim:
+        raise ValueError("delta recurrent dimensions do not match")
+    packed_width = packed_projection.shape[-1]
+    need = qkv_width + heads * dim + 2 * heads
+    if packed_width < need:
+        raise ValueError(f"packed projection width {packed_width} is smaller than {need}")
+    if state.dtype != torch.float32:
+        raise ValueError("recurrent state must be float32")
+    _rows_and_width(qkv)
+    out = torch.empty((batch, seq_len, heads, dim), device=qkv.device, dtype=qkv.dtype)
+    L.call("q35_delta_recurrent", L.ptr(qkv), L.ptr(packed_projection), L.ptr(a_log.contiguous()),
+           L.ptr(dt_bias.contiguous()), L.ptr(state), L.ptr(out), batch, seq_len, heads, dim, packed_width, _s(qkv))
+    return out
+
+
+def delta_decode(packed, conv_weight, conv_state, a_log, dt_bias, norm_weight, state, *, eps: float = 1e-6):
+    """Whole DeltaNet decode mixer in one kernel: ``packed [B, rows]`` -> ``[B, H*Dv]`` (gated-normed)."""
+    batch = packed.shape[0]
+    heads, dim = state.shape[1], state.shape[2]
+    out = torch.empty((batch, heads * dim), device=packed.device, dtype=BF16)
+    L.call("q35_delta_decode", L.ptr(packed), L.ptr(conv_weight), L.ptr(conv_state), L.ptr(a_log), L.ptr(dt_bias),
+           L.ptr(norm_weight), L.ptr(state), L.ptr(out), batch, heads, dim, packed.shape[-1], eps, _s(packed))
+    return out
+
+
+# ---------------------------------------------------------------------------- LM head
+def lm_head_argmax(hidden: torch.Tensor, weight: torch.Tensor, *, block_n: int = 16, block_k: int = 128,
+                   norm_weight: torch.Tensor | None = None, eps: float = 1e-6) -> torch.Tensor:
+    """Greedy token id without materialising the BF16 logits (kernels.py:1146-1185); int64 [1,1]."""
+    if hidden.shape != (1, weight.shape[1]) or hidden.dtype != BF16:
+        raise ValueError("lm_head_argmax supports BF16 batch=1 hidden vectors")
+    if not hidden.is_contiguous() or not weight.is_contiguous():
+        raise ValueError("LM head tensors must be contiguous")
+    if not hidden.is_cuda:
+        raise ValueError("fused kernels require a CUDA tensor")
+    vocab, hidden_size = weight.shape
+    size = L.load().q35_lm_head_workspace_size(1)
+    ws = torch.zeros(max(size, 16), device=hidden.device, dtype=torch.uint8)
+    out = torch.empty((1, 1), device=hidden.device, dtype=torch.int64)
+    L.call("q35_lm_head_argmax", L.ptr(hidden), L.ptr(norm_weight), L.ptr(weight), L.ptr(out), 1, vocab,
+           hidden_size, eps, L.ptr(ws), size, _s(hidden))
+    return out
+
+
+__all__ = [
+    "rms_norm", "residual_add_rms_norm", "gated_rms_norm", "silu_and_mul", "ppu_swiglu_gemv", "sigmoid_mul",
+    "attention_gate_mul", "qgkv_norm_rope", "causal_conv1d_fused", "delta_recurrent_fused",
+    "gqa_decode_attention", "lm_head_argmax", "quantize_rows", "int8_gemm", "a8w8_linear", "gemm",
+    "fused_gemv", "attn_decode", "prefill_attention", "delta_decode",
+]

@@ -1,0 +1,43 @@
+"""Shared comparison helpers for the parity tests."""
+
+import pytest
+import torch
+
+BF16 = torch.bfloat16
+
+
+def ulp_diff(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    """Distance in BF16 ulps (at the larger magnitude) between two tensors."""
+    a32, b32 = a.float().cpu(), b.float().cpu()
+    mag = torch.maximum(a32.abs(), b32.abs()).clamp_min(1e-30)
+    ulp = torch.exp2(torch.floor(torch.log2(mag)) - 7)
+    return (a32 - b32).abs() / ulp
+
+
+def rel_err(a: torch.Tensor, b: torch.Tensor) -> float:
+    a32, b32 = a.float().cpu(), b.float().cpu()
+    return float((a32 - b32).norm() / b32.norm().clamp_min(1e-30))
+
+
+def assert_bf16_close(actual, expected, *, max_ulp=1.0, max_frac=0.02, rel=1e-2):
+    """Tolerance for BF16 outputs of the same rounding sequence: at most `max_ulp` BF16 ulps
+    apart (FP32 summation order / transcendental differences), on at most `max_frac` of the
+    elements, and a relative Frobenius error within `rel` (the 1e-2 bound for BF16 paths)."""
+    assert tuple(actual.shape) == tuple(expected.shape), (actual.shape, expected.shape)
+    d = ulp_diff(actual, expected)
+    assert float(d.max()) <= max_ulp, f"max ulp diff {float(d.max())}"
+    assert float((d > 0).float().mean()) <= max_frac, f"mismatch fraction {float((d > 0).float().mean())}"
+    assert rel_err(actual, expected) <= rel
+
+
+def gen(seed: int) -> torch.Generator:
+    g = torch.Generator()
+    g.manual_seed(seed)
+    return g
+
+
+def randn(*shape, seed=0, scale=1.0, dtype=BF16):
+    return (torch.randn(*shape, generator=gen(seed)) * scale).to(dtype)
+
+
+requires_cuda = pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a CUDA device")
