@@ -20,24 +20,6 @@ namespace {
 
 constexpr int kD = 256;  // head_dim of every Qwen3.5 attention layer
 
-// RoPE factors for dimension d at position pos: cos/sin rounded to BF16 as the HF rotary
-// embedding returns them (cat(freqs, freqs); FP32 angle = pos * inv_freq).
-Q35_DEV void rope_cs(int d, int half, float pos, const float* inv_freq, float& c, float& s) {
-  const float ang = pos * inv_freq[d % half];
-  float sn, cs;
-  sincosf(ang, &sn, &cs);
-  c = rbf(cs);
-  s = rbf(sn);
-}
-
-// Apply partial RoPE to a normed head held in shared memory (kernels.py:455-472).
-Q35_DEV float rope_apply(const float* normed, int d, int rot, float c, float s) {
-  if (d >= rot) return normed[d];
-  const int half = rot / 2;
-  const float partner = d < half ? -normed[d + half] : normed[d - half];
-  return rbf(rbf(normed[d] * c) + rbf(partner * s));
-}
-
 // ============================================================================ qgkv_norm_rope
 template <bool TABLE>
 __global__ void __launch_bounds__(kD) qgkv_rope_kernel(
@@ -81,273 +63,6 @@ __global__ void __launch_bounds__(kD) qgkv_rope_kernel(
     }
     __syncthreads();
   }
-}
-
-// ============================================================================ decode attention
-struct DecodeParams {
-  const bf16* packed;    // fused: [B, stride] projection output
-  const bf16* qw;
-  const bf16* kw;
-  const float* inv_freq;
-  const int64_t* rope_pos;
-  const bf16* q_in;      // API: [B, Hq, D]
-  bf16* cache_k;         // [B, Hkv, max_len, D]
-  bf16* cache_v;
-  const int64_t* len;    // fused: rows already cached (new token goes to row *len); API: valid rows
-  bf16* out;             // [B, Hq*D]
-  float* part;           // [B*Hkv*S*G] x (D + 2)
-  unsigned* tickets;     // [B*Hkv]
-  int Hq, Hkv, max_len, S, rot;
-  float scale, eps;
-};
-
-constexpr int kAttnThreads = 256;
-constexpr int kAttnWarps = 8;
-
-template <int G, bool FUSED>
-__global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(DecodeParams p) {
-  __shared__ __align__(16) float qf[G][kD];     // scaled final queries
-  __shared__ __align__(16) float kn[kD];        // fused: current token key (final) / scratch
-  __shared__ __align__(16) float vn[kD];
-  __shared__ float wm[kAttnWarps][G], wl[kAttnWarps][G];
-  __shared__ __align__(16) float wacc[kAttnWarps][G][kD];
-  __shared__ float red[kAttnWarps][G + 1];
-  __shared__ unsigned ticket_s;
-
-  const int s = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
-  const int S = p.S, Hkv = p.Hkv, Hq = p.Hq;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int d = threadIdx.x;  // kAttnThreads == kD
-  const int64_t kv_base = ((int64_t)b * Hkv + g) * p.max_len * kD;
-
-  pdl_wait();
-  pdl_launch_dependents();
-  const int64_t len = *p.len;
-  int n_rows;  // cache rows to attend from the cache
-  if (FUSED) {
-    n_rows = (int)len;
-    const int stride = 2 * Hq * kD + 2 * Hkv * kD;
-    const bf16* row = p.packed + (int64_t)b * stride;
-    // raw values
-    float x[G + 1];
-#pragma unroll
-    for (int hh = 0; hh < G; ++hh) x[hh] = bf2f(row[(g * G + hh) * 2 * kD + d]);
-    x[G] = bf2f(row[2 * Hq * kD + g * kD + d]);
-    const float v_raw = bf2f(row[2 * Hq * kD + Hkv * kD + g * kD + d]);
-    // G+1 simultaneous block reductions of x^2
-#pragma unroll
-    for (int i = 0; i <= G; ++i) {
-      const float ws = warp_sum(x[i] * x[i]);
-      if (lane == 0) red[warp][i] = ws;
-    }
-    __syncthreads();
-    float c = 1.f, sn = 0.f;
-    if (d < p.rot) rope_cs(d, p.rot / 2, (float)(*p.rope_pos), p.inv_freq, c, sn);
-    const float wq = bf2f(p.qw[d]), wk = bf2f(p.kw[d]);
-    for (int i = 0; i <= G; ++i) {
-      float tot = 0.f;
-#pragma unroll
-      for (int w = 0; w < kAttnWarps; ++w) tot += red[w][i];
-      const float r = rsqrt_ieee(tot / (float)kD + p.eps);
-      const float nrm = rbf(x[i] * r * (1.0f + (i < G ? wq : wk)));
-      kn[d] = nrm;  // scratch: normed head i
-      __syncthreads();
-      const float y = rope_apply(kn, d, p.rot, c, sn);
-      __syncthreads();
-      if (i < G) {
-        qf[i][d] = y * p.scale;
-      } else {
-        kn[d] = y;
-        vn[d] = v_raw;
-        if (s == 0 && len < p.max_len) {
-          p.cache_k[kv_base + len * kD + d] = f2bf(y);
-          p.cache_v[kv_base + len * kD + d] = f2bf(v_raw);
-        }
-      }
-    }
-  } else {
-    n_rows = (int)len;
-#pragma unroll
-    for (int hh = 0; hh < G; ++hh)
-      qf[hh][d] = bf2f(p.q_in[((int64_t)b * Hq + g * G + hh) * kD + d]) * p.scale;
-  }
-  if (n_rows > p.max_len) n_rows = p.max_len;
-  if (n_rows < 0) n_rows = 0;
-  __syncthreads();
-
-  // ---- this CTA's rows of the cache
-  const int chunk = (n_rows + S - 1) / S;
-  const int r0 = s * chunk;
-  const int r1 = min(r0 + chunk, n_rows);
-  float m[G], l[G], acc[G][8];
-#pragma unroll
-  for (int hh = 0; hh < G; ++hh) {
-    m[hh] = -FLT_MAX;
-    l[hh] = 0.f;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) acc[hh][j] = 0.f;
-  }
-  float q8[G][8];
-#pragma unroll
-  for (int hh = 0; hh < G; ++hh)
-#pragma unroll
-    for (int j = 0; j < 8; ++j) q8[hh][j] = qf[hh][lane * 8 + j];
-
-  auto process = [&](const float kf[8], const float vf[8]) {
-    float sc[G];
-#pragma unroll
-    for (int hh = 0; hh < G; ++hh) {
-      float a = 0.f;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) a = fmaf(q8[hh][j], kf[j], a);
-      sc[hh] = warp_sum(a);
-    }
-#pragma unroll
-    for (int hh = 0; hh < G; ++hh) {
-      const float mn = fmaxf(m[hh], sc[hh]);
-      const float alpha = expf(m[hh] - mn);
-      const float pr = expf(sc[hh] - mn);
-      l[hh] = l[hh] * alpha + pr;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) acc[hh][j] = acc[hh][j] * alpha + pr * vf[j];
-      m[hh] = mn;
-    }
-  };
-
-  const bf16* Kb = p.cache_k + kv_base;
-  const bf16* Vb = p.cache_v + kv_base;
-  int r = r0 + warp;
-  uint4 kc = make_uint4(0, 0, 0, 0), vc = make_uint4(0, 0, 0, 0);
-  if (r < r1) {
-    kc = *reinterpret_cast<const uint4*>(Kb + (int64_t)r * kD + lane * 8);
-    vc = *reinterpret_cast<const uint4*>(Vb + (int64_t)r * kD + lane * 8);
-  }
-  for (; r < r1; r += kAttnWarps) {
-    const int rn = r + kAttnWarps;
-    uint4 kn2 = make_uint4(0, 0, 0, 0), vn2 = make_uint4(0, 0, 0, 0);
-    if (rn < r1) {
-      kn2 = *reinterpret_cast<const uint4*>(Kb + (int64_t)rn * kD + lane * 8);
-      vn2 = *reinterpret_cast<const uint4*>(Vb + (int64_t)rn * kD + lane * 8);
-    }
-    float kf[8], vf[8];
-    unpack_bf16x8(kc, kf);
-    unpack_bf16x8(vc, vf);
-    process(kf, vf);
-    kc = kn2;
-    vc = vn2;
-  }
-  if (FUSED && s == S - 1 && warp == 0) {  // the current token, from registers/shared memory
-    float kf[8], vf[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      kf[j] = kn[lane * 8 + j];
-      vf[j] = vn[lane * 8 + j];
-    }
-    process(kf, vf);
-  }
-
-  // ---- merge the warps of this CTA
-  if (lane == 0) {
-#pragma unroll
-    for (int hh = 0; hh < G; ++hh) {
-      wm[warp][hh] = m[hh];
-      wl[warp][hh] = l[hh];
-    }
-  }
-#pragma unroll
-  for (int hh = 0; hh < G; ++hh)
-#pragma unroll
-    for (int j = 0; j < 8; ++j) wacc[warp][hh][lane * 8 + j] = acc[hh][j];
-  __syncthreads();
-  const int slot0 = (((b * Hkv + g) * S) + s) * G;
-#pragma unroll
-  for (int hh = 0; hh < G; ++hh) {
-    float M = -FLT_MAX;
-#pragma unroll
-    for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, wm[w][hh]);
-    float Lsum = 0.f, A = 0.f;
-#pragma unroll
-    for (int w = 0; w < kAttnWarps; ++w) {
-      const float e = (wl[w][hh] > 0.f) ? expf(wm[w][hh] - M) : 0.f;
-      Lsum += wl[w][hh] * e;
-      A += wacc[w][hh][d] * e;
-    }
-    float* slot = p.part + (int64_t)(slot0 + hh) * (kD + 2);
-    slot[d] = A;
-    if (d == 0) {
-      slot[kD] = M;
-      slot[kD + 1] = Lsum;
-    }
-  }
-  __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) ticket_s = atomicAdd(&p.tickets[b * Hkv + g], 1u);
-  __syncthreads();
-  if (ticket_s != (unsigned)(S - 1)) return;
-  __threadfence();
-
-  // ---- last CTA of this (batch, KV head): combine the splits, gate, store
-  for (int hh = 0; hh < G; ++hh) {
-    const int base = ((b * Hkv + g) * S) * G + hh;
-    float M = -FLT_MAX;
-    for (int j = 0; j < S; ++j) {
-      const float* slot = p.part + (int64_t)(base + j * G) * (kD + 2);
-      if (__ldcg(slot + kD + 1) > 0.f) M = fmaxf(M, __ldcg(slot + kD));
-    }
-    float Lsum = 0.f, A = 0.f;
-    for (int j = 0; j < S; ++j) {
-      const float* slot = p.part + (int64_t)(base + j * G) * (kD + 2);
-      const float lj = __ldcg(slot + kD + 1);
-      if (lj > 0.f) {
-        const float e = expf(__ldcg(slot + kD) - M);
-        Lsum += lj * e;
-        A += __ldcg(slot + d) * e;
-      }
-    }
-    const float o = Lsum > 0.f ? rbf(A / Lsum) : 0.f;
-    const int h = g * G + hh;
-    if (FUSED) {
-      const int stride = 2 * Hq * kD + 2 * Hkv * kD;
-      const float gate = bf2f(p.packed[(int64_t)b * stride + h * 2 * kD + kD + d]);
-      p.out[((int64_t)b * Hq + h) * kD + d] = f2bf(o * rbf(sigmoid_f(gate)));
-    } else {
-      p.out[((int64_t)b * Hq + h) * kD + d] = f2bf(o);
-    }
-  }
-  if (threadIdx.x == 0) atomicExch(&p.tickets[b * Hkv + g], 0u);
-}
-
-int choose_splits(int64_t batch, int64_t kv_heads, int64_t cache_len) {
-  int64_t s = (2 * kNumSMs + batch * kv_heads - 1) / (batch * kv_heads);
-  const int64_t cap = (cache_len + 15) / 16;
-  if (s > cap) s = cap;
-  if (s > 128) s = 128;
-  if (s < 1) s = 1;
-  return (int)s;
-}
-
-size_t decode_ws(int64_t batch, int64_t heads, int64_t kv_heads, int64_t cache_len) {
-  const int S = choose_splits(batch, kv_heads, cache_len);
-  const size_t parts = (size_t)batch * heads * S * (kD + 2) * sizeof(float);
-  const size_t tickets = (size_t)batch * kv_heads * sizeof(unsigned);
-  return ((tickets + 255) & ~(size_t)255) + parts;
-}
-
-template <bool FUSED>
-int launch_decode(DecodeParams p, int64_t batch, int G, void* ws, cudaStream_t st, bool pdl) {
-  p.tickets = static_cast<unsigned*>(ws);
-  const size_t tickets = (size_t)batch * p.Hkv * sizeof(unsigned);
-  p.part = reinterpret_cast<float*>(static_cast<char*>(ws) + ((tickets + 255) & ~(size_t)255));
-  dim3 grid(p.S, p.Hkv, (unsigned)batch);
-  cudaError_t e;
-  switch (G) {
-    case 1: e = q35_launch(attn_decode_kernel<1, FUSED>, grid, dim3(kAttnThreads), 0, st, pdl, p); break;
-    case 2: e = q35_launch(attn_decode_kernel<2, FUSED>, grid, dim3(kAttnThreads), 0, st, pdl, p); break;
-    case 4: e = q35_launch(attn_decode_kernel<4, FUSED>, grid, dim3(kAttnThreads), 0, st, pdl, p); break;
-    default: return q35_fail(Q35_ENOTSUP, "decode attention: group size %d unsupported", G);
-  }
-  if (e != cudaSuccess) return q35_fail(Q35_ECUDA, "decode attention launch: %s", cudaGetErrorString(e));
-  return Q35_OK;
 }
 
 // ============================================================================ prefill attention
@@ -520,84 +235,6 @@ int q35_qgkv_rope_positions_launch(const void* packed, const void* q_weight, con
       (bf16*)q_out, (bf16*)k_out, (bf16*)v_out, cache_start, (int)seq_len, (int)q_heads, (int)kv_heads,
       (int)rotary_dim, (int)kv_len, eps);
   return q35_check_launch("qgkv_rope_positions");
-}
-
-extern "C" size_t q35_gqa_decode_workspace_size(int64_t batch, int64_t heads, int64_t kv_heads,
-                                                int64_t head_dim, int64_t cache_len) {
-  (void)head_dim;
-  return decode_ws(batch, heads, kv_heads, cache_len);
-}
-
-extern "C" int q35_gqa_decode_attention(const void* q, const void* cache_k, const void* cache_v,
-                                        const int64_t* valid_length, float scale, void* out, int64_t batch,
-                                        int64_t heads, int64_t kv_heads, int64_t head_dim, int64_t cache_len,
-                                        void* workspace, size_t workspace_bytes, void* stream) {
-  Q35_REQUIRE(q && cache_k && cache_v && valid_length && out && workspace, "gqa_decode_attention: null pointer");
-  Q35_REQUIRE(head_dim == kD, "gqa_decode_attention: head dim %lld unsupported (256)", (long long)head_dim);
-  Q35_REQUIRE(batch >= 1 && kv_heads >= 1 && heads % kv_heads == 0 && cache_len >= 1,
-              "gqa_decode_attention: head layout does not match cache");
-  Q35_REQUIRE(workspace_bytes >= decode_ws(batch, heads, kv_heads, cache_len),
-              "gqa_decode_attention: workspace too small");
-  DecodeParams p = {};
-  p.q_in = (const bf16*)q;
-  p.cache_k = (bf16*)cache_k;
-  p.cache_v = (bf16*)cache_v;
-  p.len = valid_length;
-  p.out = (bf16*)out;
-  p.Hq = (int)heads;
-  p.Hkv = (int)kv_heads;
-  p.max_len = (int)cache_len;
-  p.S = choose_splits(batch, kv_heads, cache_len);
-  p.scale = scale;
-  return launch_decode<false>(p, batch, (int)(heads / kv_heads), workspace, (cudaStream_t)stream, false);
-}
-
-int q35_attn_decode_launch(const void* packed, const void* q_weight, const void* k_weight, const float* inv_freq,
-                           void* cache_k, void* cache_v, const int64_t* cache_len, const int64_t* rope_pos,
-                           void* out, int64_t batch, int64_t q_heads, int64_t kv_heads, int64_t rotary_dim,
-                           int64_t max_len, float eps, void* workspace, cudaStream_t stream, bool pdl) {
-  DecodeParams p = {};
-  p.packed = (const bf16*)packed;
-  p.qw = (const bf16*)q_weight;
-  p.kw = (const bf16*)k_weight;
-  p.inv_freq = inv_freq;
-  p.rope_pos = rope_pos;
-  p.cache_k = (bf16*)cache_k;
-  p.cache_v = (bf16*)cache_v;
-  p.len = cache_len;
-  p.out = (bf16*)out;
-  p.Hq = (int)q_heads;
-  p.Hkv = (int)kv_heads;
-  p.max_len = (int)max_len;
-  p.S = choose_splits(batch, kv_heads, max_len);
-  p.rot = (int)rotary_dim;
-  p.scale = 1.0f / sqrtf((float)kD);
-  p.eps = eps;
-  return launch_decode<true>(p, batch, (int)(q_heads / kv_heads), workspace, stream, pdl);
-}
-
-extern "C" size_t q35_attn_decode_workspace_size(int64_t batch, int64_t q_heads, int64_t kv_heads,
-                                                 int64_t head_dim, int64_t cache_len) {
-  (void)head_dim;
-  return decode_ws(batch, q_heads, kv_heads, cache_len);
-}
-
-extern "C" int q35_attn_decode(const void* packed, const void* q_weight, const void* k_weight,
-                               const float* inv_freq, void* cache_k, void* cache_v, const int64_t* cache_len,
-                               const int64_t* rope_pos, void* out, int64_t batch, int64_t q_heads,
-                               int64_t kv_heads, int64_t head_dim, int64_t rotary_dim, int64_t max_len, float eps,
-                               void* workspace, size_t workspace_bytes, void* stream) {
-  Q35_REQUIRE(packed && q_weight && k_weight && inv_freq && cache_k && cache_v && cache_len && rope_pos && out &&
-                  workspace,
-              "attn_decode: null pointer");
-  Q35_REQUIRE(head_dim == kD, "attn_decode: head dim must be 256");
-  Q35_REQUIRE(batch >= 1 && kv_heads >= 1 && q_heads % kv_heads == 0 && max_len >= 1 && rotary_dim % 2 == 0 &&
-                  rotary_dim <= head_dim,
-              "attn_decode: bad shape");
-  Q35_REQUIRE(workspace_bytes >= decode_ws(batch, q_heads, kv_heads, max_len), "attn_decode: workspace too small");
-  return q35_attn_decode_launch(packed, q_weight, k_weight, inv_freq, cache_k, cache_v, cache_len, rope_pos, out,
-                                batch, q_heads, kv_heads, rotary_dim, max_len, eps, workspace, (cudaStream_t)stream,
-                                false);
 }
 
 extern "C" int q35_prefill_attention(const void* q, const void* k, const void* v, void* out, int64_t batch,

@@ -109,6 +109,25 @@ Q35_DEV int quant_i8(float x, float s) {
 Q35_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 Q35_DEV void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
+// RoPE factors for dimension d at position pos: cos/sin rounded to BF16 as the HF rotary
+// embedding returns them (cat(freqs, freqs); FP32 angle = pos * inv_freq).
+Q35_DEV void rope_cs(int d, int half, float pos, const float* inv_freq, float& c, float& s) {
+  const float ang = pos * inv_freq[d % half];
+  float sn, cs;
+  sincosf(ang, &sn, &cs);
+  c = rbf(cs);
+  s = rbf(sn);
+}
+
+// Partial RoPE of a normed head held in shared memory, with the BF16 rounding of each partial
+// product of the eager path (kernels.py:455-472).
+Q35_DEV float rope_apply(const float* normed, int d, int rot, float c, float s) {
+  if (d >= rot) return normed[d];
+  const int half = rot / 2;
+  const float partner = d < half ? -normed[d + half] : normed[d - half];
+  return rbf(rbf(normed[d] * c) + rbf(partner * s));
+}
+
 // Order-preserving 32-bit key of a float (larger float -> larger key); -0 folds onto +0.
 Q35_DEV uint32_t float_order_key(float f) {
   if (f == 0.0f) f = 0.0f;

@@ -1,0 +1,410 @@
+// Split-KV GQA decode attention (reference: kernels.py:940-1090 gqa_decode_attention, the decode
+// branch of integration.py:343-359, and kernels.py:285-333 attention_gate_mul).
+//
+// One CTA = one (batch, KV head, split of cache rows) with all G = Hq/Hkv query heads of that KV
+// head, so each K/V row is read from HBM once per group (the reference reads it once per query
+// head). Warps stride over the split's rows with an FP32 online softmax per head; the CTA merges
+// its warps and writes one (max, sum, un-normalised output) partial per head. The last CTA of a
+// (batch, KV head) — elected by an atomic ticket, no second launch — combines the partials with
+// all 8 warps, normalises, rounds to BF16 and (fused variant) multiplies by BF16(sigmoid(gate)).
+//
+// The fused variant is the whole decode attention mixer: Q/K RMSNorm(1+w) and partial RoPE of the
+// current token (positions from device scalars), its K/V written to the cache row *len, and the
+// current token attended from registers, so nothing waits on the cache write.
+#include <cfloat>
+
+#include "common.cuh"
+
+using namespace q35;
+
+namespace {
+
+constexpr int kD = 256;
+constexpr int kThreads = 256;
+constexpr int kWarps = 8;
+constexpr int kMaxSplits = 128;
+constexpr int kRowsPerSplit = 64;
+
+struct DecodeParams {
+  const bf16* packed;    // fused: [B, stride] projection output
+  const bf16* qw;
+  const bf16* kw;
+  const float* inv_freq;
+  const int64_t* rope_pos;
+  const bf16* q_in;      // API: [B, Hq, D]
+  bf16* cache_k;         // [B, Hkv, max_len, D]
+  bf16* cache_v;
+  const int64_t* len;    // fused: rows already cached (new token -> row *len); API: valid rows
+  bf16* out;             // [B, Hq*D]
+  float* part;           // [B*Hkv*S*G][D]
+  float* part_ml;        // [B*Hkv*S*G][2]
+  unsigned* tickets;     // [B*Hkv]
+  int Hq, Hkv, max_len, S, rot;
+  float scale, eps;
+};
+
+template <int G, bool FUSED>
+__global__ void __launch_bounds__(kThreads) attn_decode_kernel(DecodeParams p) {
+  __shared__ __align__(16) float qf[G][kD];
+  __shared__ __align__(16) float nrm[FUSED ? G + 1 : 1][kD];
+  __shared__ __align__(16) float kn[kD];
+  __shared__ __align__(16) float vn[kD];
+  __shared__ float wm[kWarps][G], wl[kWarps][G];
+  __shared__ __align__(16) float wacc[kWarps][G][kD];
+  __shared__ float red[kWarps][G + 1];
+  __shared__ float cm[kMaxSplits][G];
+  __shared__ float cls[G];
+  __shared__ unsigned ticket_s;
+
+  const int s = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
+  const int S = p.S, Hkv = p.Hkv, Hq = p.Hq;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int d = threadIdx.x;  // kThreads == kD
+  const int64_t kv_base = ((int64_t)b * Hkv + g) * p.max_len * kD;
+
+  pdl_wait();
+  pdl_launch_dependents();
+  const int64_t len = *p.len;
+  if (FUSED) {
+    const int stride = 2 * Hq * kD + 2 * Hkv * kD;
+    const bf16* row = p.packed + (int64_t)b * stride;
+    float x[G + 1];
+#pragma unroll
+    for (int hh = 0; hh < G; ++hh) x[hh] = bf2f(row[(g * G + hh) * 2 * kD + d]);
+    x[G] = bf2f(row[2 * Hq * kD + g * kD + d]);
+    const float v_raw = bf2f(row[2 * Hq * kD + Hkv * kD + g * kD + d]);
+#pragma unroll
+    for (int i = 0; i <= G; ++i) {
+      const float ws = warp_sum(x[i] * x[i]);
+      if (lane == 0) red[warp][i] = ws;
+    }
+    float c = 1.f, sn = 0.f;
+    if (d < p.rot) rope_cs(d, p.rot / 2, (float)(*p.rope_pos), p.inv_freq, c, sn);
+    const float wq = bf2f(p.qw[d]), wk = bf2f(p.kw[d]);
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i <= G; ++i) {
+      float tot = 0.f;
+#pragma unroll
+      for (int w = 0; w < kWarps; ++w) tot += red[w][i];
+      const float r = rsqrt_ieee(tot / (float)kD + p.eps);
+      nrm[i][d] = rbf(x[i] * r * (1.0f + (i < G ? wq : wk)));
+    }
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < G; ++i) qf[i][d] = rope_apply(nrm[i], d, p.rot, c, sn) * p.scale;
+    const float kr = rope_apply(nrm[G], d, p.rot, c, sn);
+    kn[d] = kr;
+    vn[d] = v_raw;
+    if (s == 0 && len >= 0 && len < p.max_len) {
+      p.cache_k[kv_base + len * kD + d] = f2bf(kr);
+      p.cache_v[kv_base + len * kD + d] = f2bf(v_raw);
+    }
+  } else {
+#pragma unroll
+    for (int hh = 0; hh < G; ++hh) qf[hh][d] = bf2f(p.q_in[((int64_t)b * Hq + g * G + hh) * kD + d]) * p.scale;
+  }
+  int n_rows = (int)(len < 0 ? 0 : (len > p.max_len ? p.max_len : len));
+  __syncthreads();
+
+  // ---- this CTA's rows of the cache (FP32 online softmax per warp and head)
+  const int chunk = (n_rows + S - 1) / S;
+  const int r0 = s * chunk;
+  const int r1 = min(r0 + chunk, n_rows);
+  float m[G], l[G], acc[G][8], q8[G][8];
+#pragma unroll
+  for (int hh = 0; hh < G; ++hh) {
+    m[hh] = -FLT_MAX;
+    l[hh] = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      acc[hh][j] = 0.f;
+      q8[hh][j] = qf[hh][lane * 8 + j];
+    }
+  }
+  auto process = [&](const float kf[8], const float vf[8]) {
+    float sc[G];
+#pragma unroll
+    for (int hh = 0; hh < G; ++hh) {
+      float a = 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) a = fmaf(q8[hh][j], kf[j], a);
+      sc[hh] = warp_sum(a);
+    }
+#pragma unroll
+    for (int hh = 0; hh < G; ++hh) {
+      const float mn = fmaxf(m[hh], sc[hh]);
+      const float alpha = expf(m[hh] - mn);
+      const float pr = expf(sc[hh] - mn);
+      l[hh] = l[hh] * alpha + pr;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[hh][j] = acc[hh][j] * alpha + pr * vf[j];
+      m[hh] = mn;
+    }
+  };
+  const bf16* Kb = p.cache_k + kv_base;
+  const bf16* Vb = p.cache_v + kv_base;
+  int r = r0 + warp;
+  uint4 kc = make_uint4(0, 0, 0, 0), vc = make_uint4(0, 0, 0, 0);
+  if (r < r1) {
+    kc = *reinterpret_cast<const uint4*>(Kb + (int64_t)r * kD + lane * 8);
+    vc = *reinterpret_cast<const uint4*>(Vb + (int64_t)r * kD + lane * 8);
+  }
+  for (; r < r1; r += kWarps) {
+    const int rn = r + kWarps;
+    uint4 kn2 = make_uint4(0, 0, 0, 0), vn2 = make_uint4(0, 0, 0, 0);
+    if (rn < r1) {
+      kn2 = *reinterpret_cast<const uint4*>(Kb + (int64_t)rn * kD + lane * 8);
+      vn2 = *reinterpret_cast<const uint4*>(Vb + (int64_t)rn * kD + lane * 8);
+    }
+    float kf[8], vf[8];
+    unpack_bf16x8(kc, kf);
+    unpack_bf16x8(vc, vf);
+    process(kf, vf);
+    kc = kn2;
+    vc = vn2;
+  }
+  if (FUSED && s == S - 1 && warp == kWarps - 1) {  // the current token, from shared memory
+    float kf[8], vf[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      kf[j] = kn[lane * 8 + j];
+      vf[j] = vn[lane * 8 + j];
+    }
+    process(kf, vf);
+  }
+
+  // ---- merge this CTA's warps into one partial per head
+  if (lane == 0) {
+#pragma unroll
+    for (int hh = 0; hh < G; ++hh) {
+      wm[warp][hh] = m[hh];
+      wl[warp][hh] = l[hh];
+    }
+  }
+#pragma unroll
+  for (int hh = 0; hh < G; ++hh) {
+    float4* dst = reinterpret_cast<float4*>(&wacc[warp][hh][lane * 8]);
+    dst[0] = make_float4(acc[hh][0], acc[hh][1], acc[hh][2], acc[hh][3]);
+    dst[1] = make_float4(acc[hh][4], acc[hh][5], acc[hh][6], acc[hh][7]);
+  }
+  __syncthreads();
+  const int base = ((b * Hkv + g) * S) * G;
+#pragma unroll
+  for (int hh = 0; hh < G; ++hh) {
+    float M = -FLT_MAX;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w)
+      if (wl[w][hh] > 0.f) M = fmaxf(M, wm[w][hh]);
+    float Ls = 0.f, A = 0.f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) {
+      const float e = (wl[w][hh] > 0.f) ? expf(wm[w][hh] - M) : 0.f;
+      Ls += wl[w][hh] * e;
+      A += wacc[w][hh][d] * e;
+    }
+    const int slot = base + s * G + hh;
+    p.part[(int64_t)slot * kD + d] = A;
+    if (d == 0) {
+      p.part_ml[2 * slot] = M;
+      p.part_ml[2 * slot + 1] = Ls;
+    }
+  }
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) ticket_s = atomicAdd(&p.tickets[b * Hkv + g], 1u);
+  __syncthreads();
+  if (ticket_s != (unsigned)(S - 1)) return;
+  __threadfence();
+
+  // ---- last CTA: combine the S partials of each head with all warps
+  for (int i = threadIdx.x; i < S * G; i += kThreads) {
+    const float mi = __ldcg(p.part_ml + 2 * (base + i));
+    const float li = __ldcg(p.part_ml + 2 * (base + i) + 1);
+    cm[i / G][i % G] = li > 0.f ? mi : -INFINITY;  // empty split: zero weight
+  }
+  __syncthreads();
+  if (threadIdx.x < G) {
+    const int hh = threadIdx.x;
+    float M = -FLT_MAX;
+    for (int j = 0; j < S; ++j) M = fmaxf(M, cm[j][hh]);
+    float Ls = 0.f;
+    for (int j = 0; j < S; ++j) {
+      const float li = __ldcg(p.part_ml + 2 * (base + j * G + hh) + 1);
+      const float e = (cm[j][hh] == -INFINITY) ? 0.f : expf(cm[j][hh] - M);
+      cm[j][hh] = e;
+      Ls += li * e;
+    }
+    cls[hh] = Ls;
+  }
+  __syncthreads();
+  float a8[G][8];
+#pragma unroll
+  for (int hh = 0; hh < G; ++hh)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) a8[hh][j] = 0.f;
+#pragma unroll 2
+  for (int j = warp; j < S; j += kWarps) {
+#pragma unroll
+    for (int hh = 0; hh < G; ++hh) {
+      const float wgt = cm[j][hh];
+      const float4* src = reinterpret_cast<const float4*>(p.part + (int64_t)(base + j * G + hh) * kD + lane * 8);
+      const float4 u0 = __ldcg(src), u1 = __ldcg(src + 1);
+      a8[hh][0] += wgt * u0.x;
+      a8[hh][1] += wgt * u0.y;
+      a8[hh][2] += wgt * u0.z;
+      a8[hh][3] += wgt * u0.w;
+      a8[hh][4] += wgt * u1.x;
+      a8[hh][5] += wgt * u1.y;
+      a8[hh][6] += wgt * u1.z;
+      a8[hh][7] += wgt * u1.w;
+    }
+  }
+#pragma unroll
+  for (int hh = 0; hh < G; ++hh) {
+    float4* dst = reinterpret_cast<float4*>(&wacc[warp][hh][lane * 8]);
+    dst[0] = make_float4(a8[hh][0], a8[hh][1], a8[hh][2], a8[hh][3]);
+    dst[1] = make_float4(a8[hh][4], a8[hh][5], a8[hh][6], a8[hh][7]);
+  }
+  __syncthreads();
+#pragma unroll
+  for (int hh = 0; hh < G; ++hh) {
+    float A = 0.f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) A += wacc[w][hh][d];
+    const float o = cls[hh] > 0.f ? rbf(A / cls[hh]) : 0.f;
+    const int h = g * G + hh;
+    if (FUSED) {
+      const int stride = 2 * Hq * kD + 2 * Hkv * kD;
+      const float gate = bf2f(p.packed[(int64_t)b * stride + h * 2 * kD + kD + d]);
+      p.out[((int64_t)b * Hq + h) * kD + d] = f2bf(o * rbf(sigmoid_f(gate)));
+    } else {
+      p.out[((int64_t)b * Hq + h) * kD + d] = f2bf(o);
+    }
+  }
+  if (threadIdx.x == 0) atomicExch(&p.tickets[b * Hkv + g], 0u);
+}
+
+int choose_splits(int64_t batch, int64_t kv_heads, int64_t cache_len) {
+  int64_t s = (cache_len + kRowsPerSplit - 1) / kRowsPerSplit;  // >= 64 rows per CTA
+  const int64_t fill = (2 * kNumSMs + batch * kv_heads - 1) / (batch * kv_heads);
+  if (s > fill) s = fill;
+  if (s > kMaxSplits) s = kMaxSplits;
+  return (int)(s < 1 ? 1 : s);
+}
+
+struct WsLayout {
+  size_t tickets, ml, part, total;
+};
+
+WsLayout ws_layout(int64_t batch, int64_t heads, int64_t kv_heads, int64_t cache_len) {
+  const int S = choose_splits(batch, kv_heads, cache_len);
+  const size_t slots = (size_t)batch * heads * S;
+  WsLayout w;
+  w.tickets = 0;
+  w.ml = 256;
+  w.part = w.ml + ((slots * 2 * sizeof(float) + 255) & ~(size_t)255);
+  w.total = w.part + slots * kD * sizeof(float);
+  return w;
+}
+
+template <bool FUSED>
+int launch_decode(DecodeParams p, int64_t batch, int G, void* ws, cudaStream_t st, bool pdl) {
+  const WsLayout w = ws_layout(batch, p.Hq, p.Hkv, p.max_len);
+  if ((size_t)batch * p.Hkv * sizeof(unsigned) > w.ml) return q35_fail(Q35_ENOTSUP, "decode attention: batch too large");
+  char* base = static_cast<char*>(ws);
+  p.tickets = reinterpret_cast<unsigned*>(base + w.tickets);
+  p.part_ml = reinterpret_cast<float*>(base + w.ml);
+  p.part = reinterpret_cast<float*>(base + w.part);
+  dim3 grid(p.S, p.Hkv, (unsigned)batch);
+  cudaError_t e;
+  switch (G) {
+    case 1: e = q35_launch(attn_decode_kernel<1, FUSED>, grid, dim3(kThreads), 0, st, pdl, p); break;
+    case 2: e = q35_launch(attn_decode_kernel<2, FUSED>, grid, dim3(kThreads), 0, st, pdl, p); break;
+    case 4: e = q35_launch(attn_decode_kernel<4, FUSED>, grid, dim3(kThreads), 0, st, pdl, p); break;
+    default: return q35_fail(Q35_ENOTSUP, "decode attention: group size %d unsupported (1, 2, 4)", G);
+  }
+  if (e != cudaSuccess) return q35_fail(Q35_ECUDA, "decode attention launch: %s", cudaGetErrorString(e));
+  return Q35_OK;
+}
+
+}  // namespace
+
+extern "C" size_t q35_gqa_decode_workspace_size(int64_t batch, int64_t heads, int64_t kv_heads, int64_t head_dim,
+                                                int64_t cache_len) {
+  (void)head_dim;
+  return ws_layout(batch, heads, kv_heads, cache_len).total;
+}
+
+extern "C" int q35_gqa_decode_attention(const void* q, const void* cache_k, const void* cache_v,
+                                        const int64_t* valid_length, float scale, void* out, int64_t batch,
+                                        int64_t heads, int64_t kv_heads, int64_t head_dim, int64_t cache_len,
+                                        void* workspace, size_t workspace_bytes, void* stream) {
+  Q35_REQUIRE(q && cache_k && cache_v && valid_length && out && workspace, "gqa_decode_attention: null pointer");
+  Q35_REQUIRE(head_dim == kD, "gqa_decode_attention: head dim %lld unsupported (256)", (long long)head_dim);
+  Q35_REQUIRE(batch >= 1 && batch <= 64 && kv_heads >= 1 && heads % kv_heads == 0 && cache_len >= 1,
+              "gqa_decode_attention: head layout does not match cache");
+  Q35_REQUIRE(workspace_bytes >= ws_layout(batch, heads, kv_heads, cache_len).total,
+              "gqa_decode_attention: workspace too small");
+  DecodeParams p = {};
+  p.q_in = (const bf16*)q;
+  p.cache_k = (bf16*)cache_k;
+  p.cache_v = (bf16*)cache_v;
+  p.len = valid_length;
+  p.out = (bf16*)out;
+  p.Hq = (int)heads;
+  p.Hkv = (int)kv_heads;
+  p.max_len = (int)cache_len;
+  p.S = choose_splits(batch, kv_heads, cache_len);
+  p.scale = scale;
+  return launch_decode<false>(p, batch, (int)(heads / kv_heads), workspace, (cudaStream_t)stream, false);
+}
+
+int q35_attn_decode_launch(const void* packed, const void* q_weight, const void* k_weight, const float* inv_freq,
+                           void* cache_k, void* cache_v, const int64_t* cache_len, const int64_t* rope_pos,
+                           void* out, int64_t batch, int64_t q_heads, int64_t kv_heads, int64_t rotary_dim,
+                           int64_t max_len, float eps, void* workspace, cudaStream_t stream, bool pdl) {
+  DecodeParams p = {};
+  p.packed = (const bf16*)packed;
+  p.qw = (const bf16*)q_weight;
+  p.kw = (const bf16*)k_weight;
+  p.inv_freq = inv_freq;
+  p.rope_pos = rope_pos;
+  p.cache_k = (bf16*)cache_k;
+  p.cache_v = (bf16*)cache_v;
+  p.len = cache_len;
+  p.out = (bf16*)out;
+  p.Hq = (int)q_heads;
+  p.Hkv = (int)kv_heads;
+  p.max_len = (int)max_len;
+  p.S = choose_splits(batch, kv_heads, max_len);
+  p.rot = (int)rotary_dim;
+  p.scale = 1.0f / sqrtf((float)kD);
+  p.eps = eps;
+  return launch_decode<true>(p, batch, (int)(q_heads / kv_heads), workspace, stream, pdl);
+}
+
+extern "C" size_t q35_attn_decode_workspace_size(int64_t batch, int64_t q_heads, int64_t kv_heads, int64_t head_dim,
+                                                 int64_t cache_len) {
+  (void)head_dim;
+  return ws_layout(batch, q_heads, kv_heads, cache_len).total;
+}
+
+extern "C" int q35_attn_decode(const void* packed, const void* q_weight, const void* k_weight, const float* inv_freq,
+                               void* cache_k, void* cache_v, const int64_t* cache_len, const int64_t* rope_pos,
+                               void* out, int64_t batch, int64_t q_heads, int64_t kv_heads, int64_t head_dim,
+                               int64_t rotary_dim, int64_t max_len, float eps, void* workspace,
+                               size_t workspace_bytes, void* stream) {
+  Q35_REQUIRE(packed && q_weight && k_weight && inv_freq && cache_k && cache_v && cache_len && rope_pos && out &&
+                  workspace,
+              "attn_decode: null pointer");
+  Q35_REQUIRE(head_dim == kD, "attn_decode: head dim must be 256");
+  Q35_REQUIRE(batch >= 1 && batch <= 64 && kv_heads >= 1 && q_heads % kv_heads == 0 && max_len >= 1 &&
+                  rotary_dim % 2 == 0 && rotary_dim <= head_dim,
+              "attn_decode: bad shape");
+  Q35_REQUIRE(workspace_bytes >= ws_layout(batch, q_heads, kv_heads, max_len).total,
+              "attn_decode: workspace too small");
+  return q35_attn_decode_launch(packed, q_weight, k_weight, inv_freq, cache_k, cache_v, cache_len, rope_pos, out,
+                                batch, q_heads, kv_heads, rotary_dim, max_len, eps, workspace, (cudaStream_t)stream,
+                                false);
+}

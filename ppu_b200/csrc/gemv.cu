@@ -110,21 +110,22 @@ Q35_DEV void epilogue(const GemvParams& p, int unit, float y0, float y1) {
 
 // ---------------------------------------------------------------------------------------------
 // Fast path: compile-time K. A warp's unit group is streamed in SEG segments of CHS 16-byte
-// chunks per lane (at most 16 chunks = 64 registers in flight per thread); segment i+1 is
-// loaded before segment i is consumed.
+// chunks per lane (at most 8 chunks = 32 registers in flight per thread, 16 warps per SM);
+// segment i+1 is loaded before segment i is consumed.
 template <int K, bool INT8, int RPU>
 struct FastShape {
   static constexpr int ES = INT8 ? 1 : 2;
   static constexpr int CHT = K * ES / 512;                       // chunks per row per lane
-  static constexpr int SEG = (RPU * CHT > 16) ? (RPU * CHT + 15) / 16 : 1;
+  static constexpr int BUDGET = 8;                               // 16-byte chunks in flight per lane
+  static constexpr int SEG = (RPU * CHT > BUDGET) ? (RPU * CHT + BUDGET - 1) / BUDGET : 1;
   static constexpr int CHS = CHT / SEG;                          // chunks per segment
-  static constexpr int U = (SEG == 1) ? ((16 / (RPU * CHT)) < 1 ? 1 : 16 / (RPU * CHT)) : 1;
+  static constexpr int U = (SEG == 1) ? ((BUDGET / (RPU * CHT)) < 1 ? 1 : BUDGET / (RPU * CHT)) : 1;
   static_assert(K * ES % 512 == 0, "K must fill whole warp-wide 16-byte chunks");
   static_assert(CHT % SEG == 0, "segments must split a row evenly");
 };
 
 template <int K, int PRO, int EPI, bool INT8>
-__global__ void __launch_bounds__(kThreads) gemv_fast_kernel(GemvParams p) {
+__global__ void __launch_bounds__(kThreads, 2) gemv_fast_kernel(GemvParams p) {
   constexpr int RPU = (EPI == Q35_EPI_SWIGLU) ? 2 : 1;
   using Sh = FastShape<K, INT8, RPU>;
   constexpr int ES = Sh::ES, SEG = Sh::SEG, CHS = Sh::CHS, U = Sh::U;
@@ -158,6 +159,9 @@ __global__ void __launch_bounds__(kThreads) gemv_fast_kernel(GemvParams p) {
     }
   };
   if (n_iter > 0) load(0);
+  if (PRO != Q35_PRO_PLAIN)  // norm weights are constants: warm L2 while the producer drains
+    for (int i = threadIdx.x; i < K / 64; i += kThreads)
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(p.norm_w + 64 * i));
   pdl_wait();
   pdl_launch_dependents();
   build_input<PRO, INT8>(p, K, xs, xq, &sx_s, red);
@@ -312,7 +316,7 @@ Q35_DEV void lm_finish(const LmParams& p, float best_v, int best_i, float* red_v
 template <int K, bool NORM>
 __global__ void __launch_bounds__(kThreads) lm_head_fast_kernel(LmParams p) {
   constexpr int CH = K * 2 / 512;
-  constexpr int U = 16 / CH < 1 ? 1 : 16 / CH;
+  constexpr int U = 16 / CH < 1 ? 1 : 16 / CH;  // 1 CTA/SM streaming 2 rows per warp: ~94% of HBM
   __shared__ __align__(16) bf16 xs[K];
   __shared__ float red[kWarps];
   __shared__ float red_v[kWarps];
@@ -413,15 +417,20 @@ __global__ void __launch_bounds__(kThreads) lm_head_any_kernel(LmParams p) {
 // Grid choice: at most `max_ctas` resident CTAs; among grids of whole-SM multiples pick the one
 // whose last round of unit groups is the fullest (less tail imbalance between warps).
 int choose_grid(int ngroups, int max_ctas) {
+  // Every round of unit groups costs about the same, so the best grid among the resident sizes
+  // (at least half of the machine) is the one with the fewest rounds, then the fullest last
+  // round, then the most CTAs. E.g. 6144 groups over 296 resident CTAs: 256 CTAs -> 3 full rounds.
   const int need = (ngroups + kWarps - 1) / kWarps;
   if (need <= max_ctas) return need < 1 ? 1 : need;
   int best = max_ctas;
+  long best_rounds = 1L << 40;
   double best_eff = 0.0;
-  for (int ctas = kNumSMs / 2; ctas <= max_ctas; ctas += kNumSMs / 2) {
+  for (int ctas = max_ctas; ctas >= (max_ctas + 1) / 2; --ctas) {
     const long warps = (long)ctas * kWarps;
     const long rounds = (ngroups + warps - 1) / warps;
     const double eff = (double)ngroups / (double)(rounds * warps);
-    if (eff > best_eff + 1e-3 || (eff > best_eff - 1e-3 && ctas > best)) {
+    if (rounds < best_rounds || (rounds == best_rounds && eff > best_eff + 1e-9)) {
+      best_rounds = rounds;
       best_eff = eff;
       best = ctas;
     }
@@ -541,7 +550,7 @@ int q35_lm_head_launch(const void* hidden, const void* norm_weight, const void* 
     static int max_norm = 0, max_plain = 0;
     if (!max_norm) max_norm = resident_ctas(lm_head_fast_kernel<2048, true>, 0);
     if (!max_plain) max_plain = resident_ctas(lm_head_fast_kernel<2048, false>, 0);
-    const int ngroups = (int)((vocab + 1) / 2);
+    const int ngroups = (int)((vocab + 1) / 2);  // two rows per warp iteration at K = 2048
     if (norm_weight)
       e = q35_launch(lm_head_fast_kernel<2048, true>, dim3(choose_grid(ngroups, max_norm)), dim3(kThreads), 0, s,
                      pdl, p);

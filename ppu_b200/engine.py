@@ -41,6 +41,8 @@ class Qwen35Engine:
         dev = torch.device(device)
         if dev.type != "cuda":
             raise ValueError("Qwen35Engine runs on a CUDA device only")
+        if dev.index is None:
+            dev = torch.device("cuda", torch.cuda.current_device())
         self.dims = dims
         self.device = dev
         self.a8w8 = a8w8
@@ -163,8 +165,10 @@ class Qwen35Engine:
         """Prefill device token ids ``[L]`` from an empty cache; the greedy first token lands in
         ``self.token`` (returned, on device)."""
         ids = ids.reshape(-1)
-        if ids.device != self.device or ids.dtype != torch.int64:
-            raise ValueError("prefill expects int64 token ids on the engine's device")
+        if not ids.is_cuda or ids.dtype != torch.int64:
+            raise ValueError("prefill expects int64 token ids on a CUDA device")
+        if ids.device != self.device:
+            ids = ids.to(self.device)
         n = ids.numel()
         if n > self.max_prefill:
             raise ValueError(f"prompt of {n} tokens exceeds max_prefill={self.max_prefill}")

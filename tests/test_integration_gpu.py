@@ -1,0 +1,118 @@
+"""Drop-in surface: apply_fusions on a Transformers Qwen3.5 model, GreedyDecodeGraph over a
+StaticCache, and VLMModel.generate_with_metrics, all checked against the CPU oracle."""
+
+import pytest
+import torch
+
+from oracle.model import OracleDecoder, bf16_ulp
+from ppu_b200.config import FusionConfig, Qwen35Dims
+from ppu_b200.evaluation_wrapper import GenerationConfig, GenerationResult, VLMModel, compute_throughput
+from ppu_b200.synthetic import make_prompt, make_weights
+
+pytestmark = pytest.mark.gpu
+
+# Smallest shape the kernels are built for: attention head 256, linear-attention heads 128.
+TINY = Qwen35Dims(vocab=1024, hidden=512, intermediate=1024, layers=4, q_heads=2, kv_heads=1, lin_heads=2)
+
+
+def _hf_model(dims, weights):
+    from transformers.models.qwen3_5 import modeling_qwen3_5 as hf
+
+    cfg = hf.Qwen3_5TextConfig(
+        vocab_size=dims.vocab, hidden_size=dims.hidden, intermediate_size=dims.intermediate,
+        num_hidden_layers=dims.layers, num_attention_heads=dims.q_heads, num_key_value_heads=dims.kv_heads,
+        head_dim=dims.head_dim, linear_num_key_heads=dims.lin_heads, linear_num_value_heads=dims.lin_heads,
+        linear_key_head_dim=dims.lin_dk, linear_value_head_dim=dims.lin_dv, tie_word_embeddings=True,
+        rope_parameters={"rope_type": "default", "rope_theta": dims.rope_theta, "partial_rotary_factor": 0.25,
+                         "mrope_section": list(dims.mrope_section), "mrope_interleaved": True})
+    model = hf.Qwen3_5ForCausalLM(cfg).to(torch.bfloat16)
+    model.load_state_dict({k: v for k, v in weights.items()}, strict=False)
+    model.lm_head.weight = model.model.embed_tokens.weight
+    return model.cuda().eval()
+
+
+def _assert_greedy_ok(weights, dims, prompt, tokens, a8w8=False):
+    ref = OracleDecoder(weights, dims, a8w8=a8w8, max_cache_len=512).teacher_forced_top1(prompt, tokens)
+    for tok, (top, top_val, tok_val) in zip(tokens, ref):
+        assert tok == top or tok_val >= top_val - bf16_ulp(top_val), (tokens, [r[0] for r in ref])
+
+
+@pytest.mark.parametrize("a8w8", [False, True])
+def test_apply_fusions_static_cache_graph(a8w8):
+    from transformers.cache_utils import StaticCache
+
+    from ppu_b200.graph import GreedyDecodeGraph
+    from ppu_b200.integration import apply_fusions
+    from ppu_b200.kernels import lm_head_argmax
+
+    w = make_weights(TINY, seed=21)
+    prompt = make_prompt(TINY, 37, seed=22)
+    model = _hf_model(TINY, w)
+    stats = apply_fusions(model, FusionConfig(a8w8=a8w8))
+    assert stats["delta"] == 3 and stats["attention"] == 1 and stats["mlp"] == 4
+    cache = StaticCache(config=model.config, max_cache_len=512)
+    with torch.inference_mode():
+        out = model.model(input_ids=prompt.cuda(), past_key_values=cache, use_cache=True, return_dict=True)
+        tok = lm_head_argmax(out.last_hidden_state[:, -1, :].contiguous(), model.lm_head.weight)
+        tokens = [int(tok)]
+        pos = torch.full((4, 1, 1), prompt.shape[1], device="cuda", dtype=torch.int64)
+        runner = GreedyDecodeGraph(model, cache, tok, pos, steps=1)
+        for _ in range(8):
+            tokens.append(int(runner.replay().item()))
+    _assert_greedy_ok(w, TINY, prompt, tokens, a8w8=a8w8)
+
+
+def test_apply_fusions_dynamic_cache_eager_decode():
+    from ppu_b200.integration import apply_fusions
+    from ppu_b200.kernels import lm_head_argmax
+
+    w = make_weights(TINY, seed=31)
+    prompt = make_prompt(TINY, 20, seed=32)
+    model = _hf_model(TINY, w)
+    apply_fusions(model)
+    with torch.inference_mode():
+        out = model.model(input_ids=prompt.cuda(), use_cache=True, return_dict=True)
+        cache = out.past_key_values
+        tok = lm_head_argmax(out.last_hidden_state[:, -1, :].contiguous(), model.lm_head.weight)
+        tokens = [int(tok)]
+        for _ in range(5):
+            out = model.model(input_ids=tok, past_key_values=cache, use_cache=True, return_dict=True)
+            tok = lm_head_argmax(out.last_hidden_state[:, -1, :].contiguous(), model.lm_head.weight)
+            tokens.append(int(tok))
+    _assert_greedy_ok(w, TINY, prompt, tokens)
+
+
+def test_vlmmodel_synthetic_backend():
+    dims = Qwen35Dims(layers=4, vocab=4096)
+    vm = VLMModel(backend="synthetic", dims=dims, seed=5, max_len=512, max_prefill=256)
+    assert vm.backend_name == "synthetic"
+    prompt = make_prompt(dims, 100, seed=6)[0].tolist()
+    res = vm.generate_with_metrics(image=None, prompt=prompt, choices={"A": "x"},
+                                   generation_config=GenerationConfig(max_new_tokens=12), sample_id="s0")
+    assert isinstance(res, GenerationResult) and res.token_count == 12
+    assert 0 < res.ttft_seconds < res.elapsed_seconds
+    assert compute_throughput(res) > 0
+    tokens = [int(t) for t in res.text.split()]
+    w = make_weights(dims, seed=5)
+    _assert_greedy_ok(w, dims, torch.tensor([prompt]), tokens)
+    # a second request reuses the engine, the cache and the captured graph
+    res2 = vm.generate_with_metrics(image=None, prompt=prompt, generation_config=GenerationConfig(max_new_tokens=12))
+    assert res2.text == res.text
+
+
+def test_vlmmodel_transformers_backend(tmp_path):
+    w = make_weights(TINY, seed=41)
+    model = _hf_model(TINY, w)
+    model.save_pretrained(tmp_path)
+    vm = VLMModel(str(tmp_path), backend="transformers")
+    prompt = make_prompt(TINY, 30, seed=42)[0].tolist()
+    res = vm.generate_with_metrics(image=None, prompt=prompt, generation_config=GenerationConfig(max_new_tokens=6))
+    assert res.meta["backend"] == "transformers-b200-fused" and res.token_count == 6
+    _assert_greedy_ok(w, TINY, torch.tensor([prompt]), [int(t) for t in res.text.split()])
+
+
+def test_dummy_backend_matches_reference_contract():
+    vm = VLMModel(backend="dummy")
+    res = vm.generate_with_metrics(image=None, prompt="q", choices={"A": "a", "B": "b"},
+                                   generation_config=GenerationConfig(max_new_tokens=8), sample_id="x")
+    assert res.meta["backend"] == "dummy" and res.text.startswith("Answer: ")
