@@ -145,6 +145,21 @@ int q35_int8_gemm_i32(const int8_t* qx, const int8_t* qw, int32_t* acc, int64_t 
 int q35_gemm_bf16(const void* a, const void* w, void* out, int64_t m, int64_t n, int64_t k,
                   int32_t epilogue, void* stream);
 
+/* The same projection on the 5th-generation tensor cores: TMA-fed 128 x 256 tiles accumulated
+ * by tcgen05.mma in TMEM (kind::f16). k must be a multiple of 64, n of 8. */
+int q35_gemm_tc(const void* a, const void* w, void* out, int64_t m, int64_t n, int64_t k,
+                int32_t epilogue, void* stream);
+
+/* A8W8 prefill projection on tcgen05 (kind::i8, exact int32 accumulation in TMEM) with the
+ * dequantisation bf16((float(acc) * sx[m]) * sw[n]) and the epilogue fused (k multiple of 128).
+ * qa/sx come from q35_quantize_rows (explore_runtime_quantization.py:161-181). */
+int q35_gemm_tc_a8w8(const int8_t* qa, const float* sx, const int8_t* qw, const float* sw, void* out,
+                     int64_t m, int64_t n, int64_t k, int32_t epilogue, void* stream);
+
+/* Error word of the tensor-core kernels: non-zero when a bounded pipeline wait gave up (the
+ * kernel then finished without hanging). Reading it synchronises and clears it. */
+int q35_tc_error(void);
+
 /* ---------------------------------------------------------------- attention */
 
 /* kernels.py:507 qgkv_norm_rope — packed [B, L, 2*Hq*D + 2*Hkv*D] -> q [B,Hq,L,D] and K/V written
@@ -254,6 +269,7 @@ typedef struct {
   int64_t* log_pos;       /* device counter into token_log */
   int32_t log_len;
   int32_t use_pdl;        /* launch decode kernels with programmatic dependent launch */
+  int32_t prefill_tc;     /* prefill projections on tcgen05 (1) or warp-level MMA (0) */
   void* workspace;
   size_t workspace_bytes;
 } q35_decoder_desc;

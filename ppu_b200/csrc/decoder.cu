@@ -30,6 +30,8 @@ int q35_delta_decode_launch(const void* packed, const void* conv_weight, void* c
                             int64_t heads, int64_t packed_stride, float eps, cudaStream_t stream, bool pdl);
 int q35_gemm_launch(const void* a, const void* w, void* out, int64_t m, int64_t n, int64_t k, int epi, bool int8,
                     const float* sx, const float* sw, cudaStream_t s);
+int q35_gemm_tc_launch(const void* a, const void* w, void* out, int64_t m, int64_t n, int64_t k, int epi, bool int8,
+                       const float* sx, const float* sw, cudaStream_t s);
 int q35_quantize_rows_launch(const void* x, int8_t* q, float* scale, int64_t rows, int64_t width, cudaStream_t s);
 int q35_qgkv_rope_positions_launch(const void* packed, const void* q_weight, const void* k_weight,
                                    const float* inv_freq, void* q_out, void* k_out, void* v_out,
@@ -265,12 +267,17 @@ extern "C" int q35_decoder_prefill(q35_decoder* dec, const int64_t* ids, int64_t
   const int64_t vdim = (int64_t)d.lin_heads * d.lin_dv;
   const int64_t adim = (int64_t)d.q_heads * d.head_dim;
 
-  // Projection helper: bf16 GEMM, or per-token int8 quantisation + int8 GEMM for A8W8.
+  // Projection helper: bf16 GEMM, or per-token int8 quantisation + int8 GEMM for A8W8; tcgen05
+  // tiles when enabled (K must fill the 128-byte slabs), warp-level MMA otherwise.
   auto proj = [&](const bf16* x, int64_t k, const void* w, const float* sw, void* out, int64_t n, int epi) -> int {
-    if (!q8) return q35_gemm_launch(x, w, out, Lt, n, k, epi, false, nullptr, nullptr, s);
+    const bool tc = d.prefill_tc && (k * (q8 ? 1 : 2)) % 128 == 0 && n % 8 == 0;
+    if (!q8)
+      return tc ? q35_gemm_tc_launch(x, w, out, Lt, n, k, epi, false, nullptr, nullptr, s)
+                : q35_gemm_launch(x, w, out, Lt, n, k, epi, false, nullptr, nullptr, s);
     int rc = q35_quantize_rows_launch(x, B.p_q8, B.p_sx, Lt, k, s);
     if (rc) return rc;
-    return q35_gemm_launch(B.p_q8, w, out, Lt, n, k, epi, true, B.p_sx, sw, s);
+    return tc ? q35_gemm_tc_launch(B.p_q8, w, out, Lt, n, k, epi, true, B.p_sx, sw, s)
+              : q35_gemm_launch(B.p_q8, w, out, Lt, n, k, epi, true, B.p_sx, sw, s);
   };
 
   // fresh cache: zero the recurrent/conv states (the KV rows past `length` are never read)

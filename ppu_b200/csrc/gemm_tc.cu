@@ -1,0 +1,356 @@
+// Prefill projections on the 5th-generation tensor cores (tcgen05 + TMEM + TMA), sm_100a.
+//
+// C[M, N] = A[M, K] . W[N, K]^T with BF16 inputs / FP32 accumulation (kind::f16), or int8 inputs /
+// exact int32 accumulation (kind::i8, A8W8). One CTA computes a 128 x 256 tile:
+//   warp 0 lane 0  TMA producer: A box 128 x 128 B and W box 256 x 128 B per stage (128-byte
+//                  swizzle, K-major), 4-stage ring guarded by full/empty mbarriers;
+//   warp 1 lane 0  MMA issuer: 4 x tcgen05.mma (K = 16 bf16 / 32 int8 each) per stage into a
+//                  128 x 256 FP32/S32 accumulator in TMEM; tcgen05.commit frees the stage;
+//   warps 0-3      epilogue: tcgen05.ld 32 columns at a time from the warp's 32 TMEM lanes,
+//                  dequantise (int8), and store / add to the residual / apply SwiGLU.
+// SwiGLU tiles load W rows [o0, o0+128) (gate) and [N+o0, N+o0+128) (up) as the two halves of
+// the 256-row B tile, so gate and up of an output sit 128 TMEM columns apart.
+// No cluster multicast anywhere (loads are per CTA). Every mbarrier wait is bounded by a clock
+// budget; a wait that gives up records an error code in q35_tc_error and lets the CTA finish.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include "common.cuh"
+
+using namespace q35;
+
+__device__ int q35_tc_error_word = 0;
+
+namespace {
+
+constexpr int BM = 128, BN = 256, BKB = 128;  // tile rows, tile cols, K bytes per stage
+constexpr int kStages = 4;
+constexpr int kABytes = BM * BKB;             // 16 KB
+constexpr int kBBytes = BN * BKB;             // 32 KB
+constexpr int kThreads = 128;
+constexpr long long kWaitBudget = 4000000000LL;  // ~2 s at 2 GHz
+
+struct TcParams {
+  void* out;          // bf16 [M, N] or int32 (RAW)
+  bf16* resid;        // RESIDUAL: [M, N] updated in place
+  const float* sx;    // int8: [M]
+  const float* sw;    // int8: [Nw]
+  int M, N, K;        // K in elements
+};
+
+Q35_DEV uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+Q35_DEV bool mbar_wait(uint32_t bar, uint32_t parity) {
+  const long long t0 = clock64();
+  while (true) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    if (ok) return true;
+    if (clock64() - t0 > kWaitBudget) return false;
+  }
+}
+
+Q35_DEV void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+Q35_DEV void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+Q35_DEV void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+      "l"(map), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+
+// K-major operand tile with 128-byte swizzle: 8-row core groups 1024 bytes apart (SBO), version 1.
+Q35_DEV uint64_t smem_desc(uint32_t addr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((addr >> 4) & 0x3FFF);          // start address
+  d |= (uint64_t)1 << 16;                         // leading byte offset (unused for swizzled K-major)
+  d |= (uint64_t)(1024 >> 4) << 32;               // stride byte offset
+  d |= (uint64_t)1 << 46;                         // descriptor version (sm100)
+  d |= (uint64_t)2 << 61;                         // SWIZZLE_128B
+  return d;
+}
+
+template <bool INT8>
+Q35_DEV void mma(uint32_t tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
+  if (INT8)
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem),
+        "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
+        : "memory");
+  else
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem),
+        "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+Q35_DEV void mma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+Q35_DEV void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+Q35_DEV void report(int code) { atomicCAS(&q35_tc_error_word, 0, code); }
+
+template <bool INT8, int EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, TcParams p) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  unsigned char* sA = smem;
+  unsigned char* sB = smem + kStages * kABytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + kStages * kBBytes);  // full[S], empty[S], done
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kStages + 1);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m0 = blockIdx.y * BM;
+  const int col0 = blockIdx.x * (EPI == Q35_EPI_SWIGLU ? BN / 2 : BN);  // first output column
+  const int n_k = p.K / (BKB / (INT8 ? 1 : 2));
+  const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + kStages), done = smem_u32(bars + 2 * kStages);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(full0 + 8 * s, 1);
+      mbar_init(empty0 + 8 * s, 1);
+    }
+    mbar_init(done, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(BN)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0 && lane == 0) {
+    // ---------------- TMA producer
+    for (int kt = 0; kt < n_k; ++kt) {
+      const int s = kt % kStages, r = kt / kStages;
+      if (r > 0 && !mbar_wait(empty0 + 8 * s, (r - 1) & 1)) {
+        report(1);
+        break;
+      }
+      mbar_expect_tx(full0 + 8 * s, kABytes + kBBytes);
+      const int kx = kt * (BKB / (INT8 ? 1 : 2));
+      tma_load_2d(smem_u32(sA + s * kABytes), &tmA, kx, m0, full0 + 8 * s);
+      if (EPI == Q35_EPI_SWIGLU) {
+        tma_load_2d(smem_u32(sB + s * kBBytes), &tmB, kx, col0, full0 + 8 * s);
+        tma_load_2d(smem_u32(sB + s * kBBytes + kBBytes / 2), &tmB, kx, p.N + col0, full0 + 8 * s);
+      } else {
+        tma_load_2d(smem_u32(sB + s * kBBytes), &tmB, kx, col0, full0 + 8 * s);
+      }
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ---------------- MMA issuer
+    // instruction descriptor: D fp32 (1) / s32 (2); A, B bf16 (1) / signed int8 (1); K-major;
+    // N = 256 (>> 3 at bit 17), M = 128 (>> 4 at bit 24)
+    const uint32_t idesc = ((INT8 ? 2u : 1u) << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
+                           ((uint32_t)(BM >> 4) << 24);
+    bool ok = true;
+    for (int kt = 0; kt < n_k && ok; ++kt) {
+      const int s = kt % kStages, r = kt / kStages;
+      if (!mbar_wait(full0 + 8 * s, r & 1)) {
+        report(2);
+        ok = false;
+        break;
+      }
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const uint32_t a0 = smem_u32(sA + s * kABytes), b0 = smem_u32(sB + s * kBBytes);
+#pragma unroll
+      for (int k = 0; k < BKB / 32; ++k)  // 32 bytes of K per MMA
+        mma<INT8>(tmem, smem_desc(a0 + 32 * k), smem_desc(b0 + 32 * k), idesc, (kt > 0 || k > 0) ? 1u : 0u);
+      mma_commit(empty0 + 8 * s);
+    }
+    mma_commit(done);
+  }
+  __syncwarp();
+
+  // ---------------- epilogue: warp w owns TMEM lanes / tile rows [32w, 32w + 32)
+  const bool ready = mbar_wait(done, 0);
+  if (!ready) report(3);
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const int row = m0 + warp * 32 + lane;
+  const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
+  if (ready) {
+    const int ncols = (EPI == Q35_EPI_SWIGLU) ? BN / 2 : BN;
+    for (int c = 0; c < ncols; c += 32) {
+      uint32_t v[32], u[32];
+      tmem_ld32(trow + c, v);
+      if (EPI == Q35_EPI_SWIGLU) tmem_ld32(trow + BN / 2 + c, u);
+      if (row >= p.M) continue;
+      const int gc = col0 + c;
+      float y[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        if (INT8) {
+          const int col = gc + j;
+          y[j] = (col < p.N) ? ((float)(int)v[j] * p.sx[row]) * p.sw[col] : 0.f;
+        } else {
+          y[j] = __uint_as_float(v[j]);
+        }
+      }
+      if (EPI == Q35_EPI_SWIGLU) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          float up;
+          if (INT8) {
+            const int col = gc + j;
+            up = (col < p.N) ? ((float)(int)u[j] * p.sx[row]) * p.sw[p.N + col] : 0.f;
+          } else {
+            up = __uint_as_float(u[j]);
+          }
+          y[j] = rbf(silu_f(rbf(y[j]))) * rbf(up);
+        }
+      }
+      bf16* dst = (EPI == Q35_EPI_RESIDUAL ? p.resid : static_cast<bf16*>(p.out)) + (int64_t)row * p.N + gc;
+      if (gc + 32 <= p.N) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          __align__(16) bf16 o[8];
+          if (EPI == Q35_EPI_RESIDUAL) {
+            const uint4 rv = *reinterpret_cast<const uint4*>(dst + 8 * q);
+            float rf[8];
+            unpack_bf16x8(rv, rf);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) o[j] = f2bf(rf[j] + rbf(y[8 * q + j]));
+          } else {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) o[j] = f2bf(y[8 * q + j]);
+          }
+          *reinterpret_cast<uint4*>(dst + 8 * q) = *reinterpret_cast<const uint4*>(o);
+        }
+      } else {
+        for (int j = 0; j < 32 && gc + j < p.N; ++j) {
+          if (EPI == Q35_EPI_RESIDUAL)
+            dst[j] = f2bf(bf2f(dst[j]) + rbf(y[j]));
+          else
+            dst[j] = f2bf(y[j]);
+        }
+      }
+    }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == 1)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(BN) : "memory");
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q;
+    void* f = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+  }
+  return fn;
+}
+
+// 2-D K-major map: rows x k elements, box = (128 bytes of K) x box_rows, 128-byte swizzle.
+bool make_map(CUtensorMap* m, const void* ptr, uint64_t rows, uint64_t k, uint32_t box_rows, bool int8) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  const uint64_t esz = int8 ? 1 : 2;
+  cuuint64_t dims[2] = {k, rows};
+  cuuint64_t strides[1] = {k * esz};
+  cuuint32_t box[2] = {(cuuint32_t)(BKB / esz), box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(m, int8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims,
+            strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+constexpr size_t kSmem = 1024 + (size_t)kStages * (kABytes + kBBytes) + 256;
+
+template <bool INT8, int EPI>
+int launch_tc(const void* a, const void* w, const TcParams& p, cudaStream_t s) {
+  CUtensorMap ma, mb;
+  const uint64_t wrows = (EPI == Q35_EPI_SWIGLU) ? 2 * (uint64_t)p.N : (uint64_t)p.N;
+  if (!make_map(&ma, a, p.M, p.K, BM, INT8) ||
+      !make_map(&mb, w, wrows, p.K, EPI == Q35_EPI_SWIGLU ? BN / 2 : BN, INT8))
+    return q35_fail(Q35_ECUDA, "gemm_tc: tensor map encoding failed");
+  cudaFuncSetAttribute(gemm_tc_kernel<INT8, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmem);
+  const int cols_per_tile = (EPI == Q35_EPI_SWIGLU) ? BN / 2 : BN;
+  dim3 grid((unsigned)((p.N + cols_per_tile - 1) / cols_per_tile), (unsigned)((p.M + BM - 1) / BM));
+  gemm_tc_kernel<INT8, EPI><<<grid, kThreads, kSmem, s>>>(ma, mb, p);
+  return q35_check_launch("gemm_tc");
+}
+
+}  // namespace
+
+// Used by the decoder prefill and q35_gemm_tc: tensor-core projection with fused epilogue.
+int q35_gemm_tc_launch(const void* a, const void* w, void* out, int64_t m, int64_t n, int64_t k, int epi, bool int8,
+                       const float* sx, const float* sw, cudaStream_t s) {
+  Q35_REQUIRE(a && w && out, "gemm_tc: null pointer");
+  Q35_REQUIRE(m >= 1 && n >= 1 && k >= 1 && (k * (int8 ? 1 : 2)) % BKB == 0,
+              "gemm_tc: k=%lld must fill 128-byte K slabs", (long long)k);
+  Q35_REQUIRE(Q35_ALIGNED(a, 16) && Q35_ALIGNED(w, 16) && Q35_ALIGNED(out, 16), "gemm_tc: 16-byte alignment");
+  Q35_REQUIRE(n % 8 == 0, "gemm_tc: n must be a multiple of 8");
+  Q35_REQUIRE(!int8 || (sx && sw), "gemm_tc: int8 needs scales");
+  Q35_REQUIRE(epi == Q35_EPI_STORE || epi == Q35_EPI_RESIDUAL || epi == Q35_EPI_SWIGLU, "gemm_tc: bad epilogue");
+  TcParams p;
+  p.out = out;
+  p.resid = static_cast<bf16*>(out);
+  p.sx = sx;
+  p.sw = sw;
+  p.M = (int)m;
+  p.N = (int)n;
+  p.K = (int)k;
+  if (int8) {
+    switch (epi) {
+      case Q35_EPI_STORE: return launch_tc<true, Q35_EPI_STORE>(a, w, p, s);
+      case Q35_EPI_RESIDUAL: return launch_tc<true, Q35_EPI_RESIDUAL>(a, w, p, s);
+      default: return launch_tc<true, Q35_EPI_SWIGLU>(a, w, p, s);
+    }
+  }
+  switch (epi) {
+    case Q35_EPI_STORE: return launch_tc<false, Q35_EPI_STORE>(a, w, p, s);
+    case Q35_EPI_RESIDUAL: return launch_tc<false, Q35_EPI_RESIDUAL>(a, w, p, s);
+    default: return launch_tc<false, Q35_EPI_SWIGLU>(a, w, p, s);
+  }
+}
+
+extern "C" int q35_gemm_tc(const void* a, const void* w, void* out, int64_t m, int64_t n, int64_t k,
+                           int32_t epilogue, void* stream) {
+  return q35_gemm_tc_launch(a, w, out, m, n, k, epilogue, false, nullptr, nullptr, (cudaStream_t)stream);
+}
+
+extern "C" int q35_gemm_tc_a8w8(const int8_t* qa, const float* sx, const int8_t* qw, const float* sw, void* out,
+                                int64_t m, int64_t n, int64_t k, int32_t epilogue, void* stream) {
+  return q35_gemm_tc_launch(qa, qw, out, m, n, k, epilogue, true, sx, sw, (cudaStream_t)stream);
+}
+
+extern "C" int q35_tc_error(void) {
+  int v = 0, zero = 0;
+  if (cudaMemcpyFromSymbol(&v, q35_tc_error_word, sizeof(int)) != cudaSuccess) return -1;
+  if (v) cudaMemcpyToSymbol(q35_tc_error_word, &zero, sizeof(int));
+  return v;
+}

@@ -163,8 +163,9 @@ def fused_gemv(weight, x=None, *, prologue=L.PRO_PLAIN, epilogue=L.EPI_STORE, no
     return out if out is not None else resid
 
 
-def gemm(a: torch.Tensor, weight: torch.Tensor, *, epilogue=L.EPI_STORE, out=None) -> torch.Tensor:
-    """Prefill projection ``a [M,K] @ weight [N,K]^T`` (bf16; RESIDUAL adds into ``out`` in place)."""
+def gemm(a: torch.Tensor, weight: torch.Tensor, *, epilogue=L.EPI_STORE, out=None, tc: bool = False) -> torch.Tensor:
+    """Prefill projection ``a [M,K] @ weight [N,K]^T`` (bf16; RESIDUAL adds into ``out`` in place).
+    ``tc=True`` runs the tcgen05/TMEM kernel, otherwise the warp-level MMA kernel."""
     _need_bf16(a, weight)
     m, k = a.reshape(-1, a.shape[-1]).shape
     n = weight.shape[0] // 2 if epilogue == L.EPI_SWIGLU else weight.shape[0]
@@ -173,8 +174,23 @@ def gemm(a: torch.Tensor, weight: torch.Tensor, *, epilogue=L.EPI_STORE, out=Non
             raise ValueError("RESIDUAL epilogue needs the residual tensor as `out`")
     elif out is None:
         out = torch.empty((*a.shape[:-1], n), device=a.device, dtype=BF16)
-    L.call("q35_gemm_bf16", L.ptr(a), L.ptr(weight), L.ptr(out), m, n, k, epilogue, _s(a))
+    L.call("q35_gemm_tc" if tc else "q35_gemm_bf16", L.ptr(a), L.ptr(weight), L.ptr(out), m, n, k, epilogue, _s(a))
     return out
+
+
+def gemm_a8w8_tc(qa, sx, qw, sw, *, epilogue=L.EPI_STORE, out=None) -> torch.Tensor:
+    """A8W8 prefill projection on tcgen05: int8 ``qa [M,K]`` / ``qw [N,K]`` with row scales."""
+    m, k = qa.shape
+    n = qw.shape[0] // 2 if epilogue == L.EPI_SWIGLU else qw.shape[0]
+    if out is None:
+        out = torch.empty((m, n), device=qa.device, dtype=BF16)
+    L.call("q35_gemm_tc_a8w8", L.ptr(qa), L.ptr(sx), L.ptr(qw), L.ptr(sw), L.ptr(out), m, n, k, epilogue, _s(qa))
+    return out
+
+
+def tc_error() -> int:
+    """Error word of the tensor-core kernels (0 = every bounded wait completed)."""
+    return int(L.load().q35_tc_error())
 
 
 # ---------------------------------------------------------------------------- A8W8

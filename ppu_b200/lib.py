@@ -47,7 +47,7 @@ class DecoderDesc(C.Structure):
         ("max_len", I32), ("max_prefill", I32), ("a8w8", I32), ("eps", F32),
         ("layers", C.POINTER(LayerDesc)), ("embed", P), ("final_norm", P), ("inv_freq", P),
         ("token", P), ("cache_len", P), ("rope_pos", P), ("token_log", P), ("log_pos", P),
-        ("log_len", I32), ("use_pdl", I32), ("workspace", P), ("workspace_bytes", SZ),
+        ("log_len", I32), ("use_pdl", I32), ("prefill_tc", I32), ("workspace", P), ("workspace_bytes", SZ),
     ]
 
 
@@ -70,6 +70,9 @@ _SIGS = {
     "q35_a8w8_linear": (INT, [P, P, P, P, I64, I64, I64, P, SZ, P]),
     "q35_int8_gemm_i32": (INT, [P, P, P, I64, I64, I64, P]),
     "q35_gemm_bf16": (INT, [P, P, P, I64, I64, I64, I32, P]),
+    "q35_gemm_tc": (INT, [P, P, P, I64, I64, I64, I32, P]),
+    "q35_gemm_tc_a8w8": (INT, [P, P, P, P, P, I64, I64, I64, I32, P]),
+    "q35_tc_error": (INT, []),
     "q35_qgkv_norm_rope": (INT, [P, P, P, P, P, P, P, P, P, I64, I64, I64, I64, I64, I64, I64, F32, P]),
     "q35_gqa_decode_workspace_size": (SZ, [I64, I64, I64, I64, I64]),
     "q35_gqa_decode_attention": (INT, [P, P, P, P, F32, P, I64, I64, I64, I64, I64, P, SZ, P]),

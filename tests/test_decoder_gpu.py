@@ -15,7 +15,7 @@ from ppu_b200.config import Qwen35Dims
 from ppu_b200.engine import Qwen35Engine
 from ppu_b200.synthetic import make_prompt, make_weights
 
-from .helpers import rel_err
+from .helpers import assert_bf16_close, rel_err
 
 pytestmark = pytest.mark.gpu
 
@@ -71,7 +71,8 @@ def test_prefill_state_matches_oracle():
     eng.prefill(prompt[0].cuda())
     torch.cuda.synchronize()
     for c_gpu, c_ref in zip(eng.conv_states, oracle.conv_state):
-        assert torch.equal(c_gpu.cpu(), c_ref)
+        # the conv state holds raw projection outputs of the last 4 tokens (GEMM results)
+        assert_bf16_close(c_gpu.cpu(), c_ref, max_ulp=1, max_frac=0.02)
     for s_gpu, s_ref in zip(eng.rec_states, oracle.rec_state):
         assert rel_err(s_gpu, s_ref) < 1e-2
     for v_gpu, v_ref in zip(eng.v_caches, oracle.v_cache):

@@ -93,7 +93,7 @@ def test_vlmmodel_synthetic_backend():
     assert 0 < res.ttft_seconds < res.elapsed_seconds
     assert compute_throughput(res) > 0
     tokens = [int(t) for t in res.text.split()]
-    w = make_weights(dims, seed=5)
+    w = {k: v.cpu() for k, v in make_weights(dims, seed=5, device="cuda").items()}  # the backend seeds on device
     _assert_greedy_ok(w, dims, torch.tensor([prompt]), tokens)
     # a second request reuses the engine, the cache and the captured graph
     res2 = vm.generate_with_metrics(image=None, prompt=prompt, generation_config=GenerationConfig(max_new_tokens=12))
