@@ -23,7 +23,7 @@ constexpr int kD = 256;
 constexpr int kThreads = 256;
 constexpr int kWarps = 8;
 constexpr int kMaxSplits = 128;
-constexpr int kRowsPerSplit = 64;
+constexpr int kRowsPerSplit = 32;
 
 struct DecodeParams {
   const bf16* packed;    // fused: [B, stride] projection output
@@ -144,25 +144,28 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(DecodeParams p) {
   };
   const bf16* Kb = p.cache_k + kv_base;
   const bf16* Vb = p.cache_v + kv_base;
-  int r = r0 + warp;
-  uint4 kc = make_uint4(0, 0, 0, 0), vc = make_uint4(0, 0, 0, 0);
-  if (r < r1) {
-    kc = *reinterpret_cast<const uint4*>(Kb + (int64_t)r * kD + lane * 8);
-    vc = *reinterpret_cast<const uint4*>(Vb + (int64_t)r * kD + lane * 8);
-  }
-  for (; r < r1; r += kWarps) {
-    const int rn = r + kWarps;
-    uint4 kn2 = make_uint4(0, 0, 0, 0), vn2 = make_uint4(0, 0, 0, 0);
-    if (rn < r1) {
-      kn2 = *reinterpret_cast<const uint4*>(Kb + (int64_t)rn * kD + lane * 8);
-      vn2 = *reinterpret_cast<const uint4*>(Vb + (int64_t)rn * kD + lane * 8);
+  // Each warp takes rows r0 + warp, r0 + warp + 8, ...; kRowBatch of them are loaded together so
+  // their HBM latencies overlap (the online softmax then consumes them in order).
+  constexpr int kRowBatch = 4;
+  for (int rb = r0 + warp; rb < r1; rb += kWarps * kRowBatch) {
+    uint4 kc[kRowBatch], vc[kRowBatch];
+#pragma unroll
+    for (int i = 0; i < kRowBatch; ++i) {
+      const int r = rb + i * kWarps;
+      kc[i] = vc[i] = make_uint4(0, 0, 0, 0);
+      if (r < r1) {
+        kc[i] = *reinterpret_cast<const uint4*>(Kb + (int64_t)r * kD + lane * 8);
+        vc[i] = *reinterpret_cast<const uint4*>(Vb + (int64_t)r * kD + lane * 8);
+      }
     }
-    float kf[8], vf[8];
-    unpack_bf16x8(kc, kf);
-    unpack_bf16x8(vc, vf);
-    process(kf, vf);
-    kc = kn2;
-    vc = vn2;
+#pragma unroll
+    for (int i = 0; i < kRowBatch; ++i) {
+      if (rb + i * kWarps >= r1) break;
+      float kf[8], vf[8];
+      unpack_bf16x8(kc[i], kf);
+      unpack_bf16x8(vc[i], vf);
+      process(kf, vf);
+    }
   }
   if (FUSED && s == S - 1 && warp == kWarps - 1) {  // the current token, from shared memory
     float kf[8], vf[8];

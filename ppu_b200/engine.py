@@ -36,7 +36,7 @@ def cache_bucket(input_len: int, max_new_tokens: int) -> int:
 class Qwen35Engine:
     def __init__(self, weights: dict, dims: Qwen35Dims = Qwen35Dims(), *, a8w8: bool = False,
                  max_len: int = 2048, max_prefill: int = 1024, device="cuda", use_pdl: bool = True,
-                 prefill_tc: bool = False, log_len: int = 4096, release_source: bool = False):
+                 prefill_tc: bool = True, log_len: int = 4096, release_source: bool = False):
         L.load()
         dev = torch.device(device)
         if dev.type != "cuda":

@@ -19,7 +19,7 @@ def rel_err(a: torch.Tensor, b: torch.Tensor) -> float:
     return float((a32 - b32).norm() / b32.norm().clamp_min(1e-30))
 
 
-def assert_bf16_close(actual, expected, *, max_ulp=1.0, max_frac=0.02, rel=1e-2, floor_rel=1e-3):
+def assert_bf16_close(actual, expected, *, max_ulp=1.0, max_frac=0.02, rel=1e-2, floor_rel=2.0 ** -6):
     """Tolerance for BF16 outputs of the same rounding sequence: at most `max_ulp` BF16 ulps
     apart (FP32 summation order / transcendental differences), on at most `max_frac` of the
     elements, and a relative Frobenius error within `rel` (the 1e-2 bound for BF16 paths).
