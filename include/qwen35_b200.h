@@ -109,6 +109,14 @@ typedef struct {
 } q35_gemv_desc;
 int q35_gemv(const q35_gemv_desc* d, void* stream);
 
+/* Weight-streaming strategy of the K = 2048 / 6144 decode GEMVs (process-wide, default BULK):
+ * BULK stages weights through shared memory with bulk asynchronous copies issued before the
+ * programmatic-dependent-launch wait; REGISTERS streams 16-byte loads into registers. */
+enum { Q35_GEMV_BULK = 0, Q35_GEMV_REGISTERS = 1 };
+int q35_set_gemv_variant(int variant);
+/* Error word of the bulk GEMV (non-zero when a bounded copy wait gave up); reading clears it. */
+int q35_gemv_error(void);
+
 /* kernels.py:1146 lm_head_argmax — token[b] = argmax_v bf16(hidden[b] . weight[v]), lowest v on
  * ties, in one launch. With norm_weight != NULL the hidden row is rms_norm'ed first (the final
  * norm of integration.py:494-499 fused in). Workspace: q35_lm_head_workspace_size(batch) bytes,
@@ -215,6 +223,17 @@ int q35_delta_recurrent(const void* qkv, const void* packed, const void* a_log,
                         int64_t seq_len, int64_t heads, int64_t dim, int64_t packed_stride,
                         void* stream);
 
+/* The same recurrence in chunked (WY / UT-transform) form, chunk 64, FP32 throughout — the
+ * algorithm of HF torch_chunk_gated_delta_rule — used for prefill: chunk-local factors for all
+ * chunks in parallel, then one pass over the chunks per (head, 16 value columns). Same inputs,
+ * outputs and in-place state update as q35_delta_recurrent; workspace from
+ * q35_delta_chunked_workspace_size. */
+size_t q35_delta_chunked_workspace_size(int64_t batch, int64_t heads, int64_t seq_len);
+int q35_delta_chunked(const void* qkv, const void* packed, const void* a_log, const void* dt_bias,
+                      float* state, void* out, int64_t batch, int64_t seq_len, int64_t heads,
+                      int64_t dim, int64_t packed_stride, void* workspace, size_t workspace_bytes,
+                      void* stream);
+
 /* Fused DeltaNet decode step (integration.py:245-272 for L == 1): conv update + SiLU, q/k L2
  * norm, gated delta step on the fp32 state, gated RMSNorm with z. packed [B, packed_stride]
  * -> out [B, H*D] bf16 (input of out_proj). */
@@ -270,6 +289,7 @@ typedef struct {
   int32_t log_len;
   int32_t use_pdl;        /* launch decode kernels with programmatic dependent launch */
   int32_t prefill_tc;     /* prefill projections on tcgen05 (1) or warp-level MMA (0) */
+  int32_t prefill_delta;  /* prefill DeltaNet scan: 0 = chunked WY form, 1 = sequential */
   void* workspace;
   size_t workspace_bytes;
 } q35_decoder_desc;

@@ -42,6 +42,10 @@ int q35_gated_rms_strided_launch(const void* x, const void* gate, int gate_group
                                  const void* weight, void* out, int64_t rows, int64_t width, float eps,
                                  cudaStream_t stream);
 int q35_set_counters_launch(int64_t* a, int64_t* b, int64_t value, cudaStream_t stream);
+size_t q35_delta_chunk_workspace_bytes(int64_t batch, int64_t heads, int64_t max_len);
+int q35_delta_chunked_launch(const void* qkv, const void* packed, const void* a_log, const void* dt_bias, float* state,
+                             void* out, int64_t batch, int64_t seq_len, int64_t heads, int64_t packed_stride,
+                             float* ws, cudaStream_t s);
 size_t q35_attn_decode_workspace_size(int64_t batch, int64_t q_heads, int64_t kv_heads, int64_t head_dim,
                                       int64_t cache_len);
 
@@ -78,6 +82,7 @@ struct Buffers {
   bf16* p_act;        // [L, I]
   int8_t* p_q8;       // [L, max(H, I, mix width)]
   float* p_sx;        // [L]
+  float* p_chunk;     // chunked DeltaNet factors for one layer
 };
 
 Buffers carve(const q35_decoder_desc& d, void* base, size_t* total) {
@@ -109,6 +114,7 @@ Buffers carve(const q35_decoder_desc& d, void* base, size_t* total) {
   if (mixw > qw) qw = mixw;
   b.p_q8 = c.take<int8_t>(L * qw);
   b.p_sx = c.take<float>(L);
+  b.p_chunk = c.take<float>(q35_delta_chunk_workspace_bytes(1, d.lin_heads, L) / sizeof(float));
   *total = c.off + 256;
   return b;
 }
@@ -299,8 +305,12 @@ extern "C" int q35_decoder_prefill(q35_decoder* dec, const int64_t* ids, int64_t
       Q35_TRY(proj(B.p_norm, H, L.mix_in, L.mix_in_scale, B.p_packed, d.delta_rows, Q35_EPI_STORE));
       Q35_TRY(q35_causal_conv1d(B.p_packed, L.conv_w, L.conv_state, B.p_conv, 1, Lt, d.delta_rows, conv_dim,
                                 d.conv_kernel, s));
-      Q35_TRY(q35_delta_recurrent(B.p_conv, B.p_packed, L.a_log, L.dt_bias, L.rec_state, B.p_core, 1, Lt,
-                                  d.lin_heads, d.lin_dk, d.delta_rows, s));
+      if (d.prefill_delta == 0)
+        Q35_TRY(q35_delta_chunked_launch(B.p_conv, B.p_packed, L.a_log, L.dt_bias, L.rec_state, B.p_core, 1, Lt,
+                                         d.lin_heads, d.delta_rows, B.p_chunk, s));
+      else
+        Q35_TRY(q35_delta_recurrent(B.p_conv, B.p_packed, L.a_log, L.dt_bias, L.rec_state, B.p_core, 1, Lt,
+                                    d.lin_heads, d.lin_dk, d.delta_rows, s));
       Q35_TRY(q35_gated_rms_strided_launch(B.p_core, B.p_packed + conv_dim, d.lin_heads, d.delta_rows, L.gnorm,
                                            B.p_mix, Lt * d.lin_heads, d.lin_dv, d.eps, s));
       Q35_TRY(proj(B.p_mix, vdim, L.mix_out, L.mix_out_scale, B.p_resid, H, Q35_EPI_RESIDUAL));

@@ -471,11 +471,18 @@ int launch_any(const GemvParams& p, cudaStream_t s, bool pdl) {
   return Q35_OK;
 }
 
+#include "gemv_bulk.cuh"
+
+int g_gemv_variant = Q35_GEMV_BULK;
+
 template <int PRO, int EPI, bool INT8>
 int dispatch_k(const GemvParams& p, cudaStream_t s, bool pdl) {
-  if (p.k == 2048) return launch_fast<2048, PRO, EPI, INT8>(p, s, pdl);
+  const bool bulk = g_gemv_variant == Q35_GEMV_BULK;
+  if (p.k == 2048)
+    return bulk ? launch_bulk<2048, PRO, EPI, INT8>(p, s, pdl) : launch_fast<2048, PRO, EPI, INT8>(p, s, pdl);
   if constexpr (EPI != Q35_EPI_SWIGLU && PRO == Q35_PRO_PLAIN) {
-    if (p.k == 6144) return launch_fast<6144, PRO, EPI, INT8>(p, s, pdl);
+    if (p.k == 6144)
+      return bulk ? launch_bulk<6144, PRO, EPI, INT8>(p, s, pdl) : launch_fast<6144, PRO, EPI, INT8>(p, s, pdl);
   }
   return launch_any<PRO, EPI, INT8>(p, s, pdl);
 }
@@ -567,6 +574,19 @@ int q35_lm_head_launch(const void* hidden, const void* norm_weight, const void* 
   }
   if (e != cudaSuccess) return q35_fail(Q35_ECUDA, "lm_head launch: %s", cudaGetErrorString(e));
   return Q35_OK;
+}
+
+extern "C" int q35_set_gemv_variant(int variant) {
+  Q35_REQUIRE(variant == Q35_GEMV_BULK || variant == Q35_GEMV_REGISTERS, "gemv variant %d unknown", variant);
+  g_gemv_variant = variant;
+  return Q35_OK;
+}
+
+extern "C" int q35_gemv_error(void) {
+  int v = 0, zero = 0;
+  if (cudaMemcpyFromSymbol(&v, q35_gemv_error_word, sizeof(int)) != cudaSuccess) return -1;
+  if (v) cudaMemcpyToSymbol(q35_gemv_error_word, &zero, sizeof(int));
+  return v;
 }
 
 extern "C" int q35_gemv(const q35_gemv_desc* d, void* stream) {

@@ -36,7 +36,7 @@ def cache_bucket(input_len: int, max_new_tokens: int) -> int:
 class Qwen35Engine:
     def __init__(self, weights: dict, dims: Qwen35Dims = Qwen35Dims(), *, a8w8: bool = False,
                  max_len: int = 2048, max_prefill: int = 1024, device="cuda", use_pdl: bool = True,
-                 prefill_tc: bool = True, log_len: int = 4096, release_source: bool = False):
+                 prefill_tc: bool = True, prefill_chunked: bool = True, log_len: int = 4096, release_source: bool = False):
         L.load()
         dev = torch.device(device)
         if dev.type != "cuda":
@@ -136,6 +136,7 @@ class Qwen35Engine:
         desc.log_len = log_len
         desc.use_pdl = int(use_pdl)
         desc.prefill_tc = int(prefill_tc)
+        desc.prefill_delta = 0 if prefill_chunked else 1
         size = L.load().q35_decoder_workspace_size(C.byref(desc))
         self.workspace = torch.zeros(size, device=dev, dtype=torch.uint8)
         desc.workspace, desc.workspace_bytes = self.workspace.data_ptr(), size

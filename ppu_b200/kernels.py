@@ -363,6 +363,22 @@ def delta_recurrent_fused(qkv, packed_projection, a_log, dt_bias, state, *, bloc
     return out
 
 
+def delta_chunked_fused(qkv, packed_projection, a_log, dt_bias, state):
+    """``delta_recurrent_fused`` in chunked WY form (chunk 64, FP32): same inputs/outputs and
+    in-place state update; the algorithm of HF torch_chunk_gated_delta_rule (prefill)."""
+    batch, seq_len, qkv_width = qkv.shape
+    _, heads, dim, _ = state.shape
+    if qkv_width != 3 * heads * dim or not qkv.is_contiguous() or not packed_projection.is_contiguous():
+        raise ValueError("delta chunked tensors do not match")
+    out = torch.empty((batch, seq_len, heads, dim), device=qkv.device, dtype=qkv.dtype)
+    size = L.load().q35_delta_chunked_workspace_size(batch, heads, seq_len)
+    ws = torch.empty(max(size, 16), device=qkv.device, dtype=torch.uint8)
+    L.call("q35_delta_chunked", L.ptr(qkv), L.ptr(packed_projection), L.ptr(a_log.contiguous()),
+           L.ptr(dt_bias.contiguous()), L.ptr(state), L.ptr(out), batch, seq_len, heads, dim,
+           packed_projection.shape[-1], L.ptr(ws), size, _s(qkv))
+    return out
+
+
 def delta_decode(packed, conv_weight, conv_state, a_log, dt_bias, norm_weight, state, *, eps: float = 1e-6):
     """Whole DeltaNet decode mixer in one kernel: ``packed [B, rows]`` -> ``[B, H*Dv]`` (gated-normed)."""
     batch = packed.shape[0]
@@ -396,5 +412,5 @@ __all__ = [
     "rms_norm", "residual_add_rms_norm", "gated_rms_norm", "silu_and_mul", "ppu_swiglu_gemv", "sigmoid_mul",
     "attention_gate_mul", "qgkv_norm_rope", "causal_conv1d_fused", "delta_recurrent_fused",
     "gqa_decode_attention", "lm_head_argmax", "quantize_rows", "int8_gemm", "a8w8_linear", "gemm",
-    "fused_gemv", "attn_decode", "prefill_attention", "delta_decode",
+    "fused_gemv", "attn_decode", "prefill_attention", "delta_decode", "delta_chunked_fused",
 ]

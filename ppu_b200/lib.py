@@ -13,6 +13,7 @@ LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libqwen35_b200.so"
 Q35_OK, Q35_EINVAL, Q35_ECUDA, Q35_ETIMEOUT, Q35_ENOTSUP = 0, 1, 2, 3, 4
 PRO_PLAIN, PRO_NORM, PRO_EMBED = 0, 1, 2
 EPI_STORE, EPI_RESIDUAL, EPI_SWIGLU = 0, 1, 2
+Q35_GEMV_BULK, Q35_GEMV_REGISTERS = 0, 1
 
 P = C.c_void_p
 I64 = C.c_int64
@@ -47,7 +48,7 @@ class DecoderDesc(C.Structure):
         ("max_len", I32), ("max_prefill", I32), ("a8w8", I32), ("eps", F32),
         ("layers", C.POINTER(LayerDesc)), ("embed", P), ("final_norm", P), ("inv_freq", P),
         ("token", P), ("cache_len", P), ("rope_pos", P), ("token_log", P), ("log_pos", P),
-        ("log_len", I32), ("use_pdl", I32), ("prefill_tc", I32), ("workspace", P), ("workspace_bytes", SZ),
+        ("log_len", I32), ("use_pdl", I32), ("prefill_tc", I32), ("prefill_delta", I32), ("workspace", P), ("workspace_bytes", SZ),
     ]
 
 
@@ -63,6 +64,8 @@ _SIGS = {
     "q35_embedding": (INT, [P, P, P, I64, I64, I64, P]),
     "q35_swiglu_gemv": (INT, [P, P, P, I64, I64, P]),
     "q35_gemv": (INT, [C.POINTER(GemvDesc), P]),
+    "q35_set_gemv_variant": (INT, [INT]),
+    "q35_gemv_error": (INT, []),
     "q35_lm_head_workspace_size": (SZ, [I64]),
     "q35_lm_head_argmax": (INT, [P, P, P, P, I64, I64, I64, F32, P, SZ, P]),
     "q35_quantize_rows": (INT, [P, P, P, I64, I64, P]),
@@ -82,6 +85,8 @@ _SIGS = {
     "q35_causal_conv1d": (INT, [P, P, P, P, I64, I64, I64, I64, I64, P]),
     "q35_delta_recurrent": (INT, [P, P, P, P, P, P, I64, I64, I64, I64, I64, P]),
     "q35_delta_decode": (INT, [P, P, P, P, P, P, P, P, I64, I64, I64, I64, F32, P]),
+    "q35_delta_chunked_workspace_size": (SZ, [I64, I64, I64]),
+    "q35_delta_chunked": (INT, [P, P, P, P, P, P, I64, I64, I64, I64, I64, P, SZ, P]),
     "q35_decoder_workspace_size": (SZ, [C.POINTER(DecoderDesc)]),
     "q35_decoder_create": (INT, [C.POINTER(DecoderDesc), C.POINTER(P)]),
     "q35_decoder_destroy": (None, [P]),
