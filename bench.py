@@ -46,6 +46,9 @@ def parse():
     ap.add_argument("--new-tokens", type=int, default=32)
     ap.add_argument("--a8w8", action="store_true", help="int8 weights / per-token int8 activations (M/F/L groups)")
     ap.add_argument("--no-pdl", action="store_true")
+    ap.add_argument("--gemv", default="bulk", choices=["bulk", "registers"],
+                    help="decode GEMV weight streaming: shared-memory bulk copies or register loads")
+    ap.add_argument("--prefill-delta", default="chunked", choices=["chunked", "sequential"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
 
@@ -196,9 +199,10 @@ def main():
 
     dims = Qwen35Dims()
     P, T = args.prompt_len, args.new_tokens
+    L.call("q35_set_gemv_variant", L.Q35_GEMV_BULK if args.gemv == "bulk" else L.Q35_GEMV_REGISTERS)
     weights = make_weights(dims, seed=0, device=dev)
     eng = Qwen35Engine(weights, dims, a8w8=args.a8w8, max_len=cache_bucket(P, T), max_prefill=P, device=dev,
-                       use_pdl=not args.no_pdl)
+                       use_pdl=not args.no_pdl, prefill_chunked=args.prefill_delta == "chunked")
     gate_up_w = [t["gate_up"] for t in eng.layer_tensors]
     post_ln = [t["post_ln"] for t in eng.layer_tensors]
     gate_up_s = [t.get("gate_up_scale") for t in eng.layer_tensors]
@@ -305,6 +309,7 @@ def main():
             "model": "Qwen3.5-2B-shape text decoder (24 layers, 3xGatedDeltaNet:1xGQA, hidden 2048, vocab 248320)",
             "global_batch": world, "seq_len": P, "parallelism": f"request-parallel replicas x{world}",
             "a8w8": args.a8w8, "pdl": not args.no_pdl, "cuda_graph": "1 decode step per replay",
+            "gemv": args.gemv, "prefill_delta": args.prefill_delta, "prefill_gemm": "tcgen05",
             "l2": "weights 3.8 GB per step >> 126 MB L2 (no flush needed)",
         },
         "ttft_ms": round(prefill_ms / args.steps, 3),
@@ -312,7 +317,7 @@ def main():
         "step_hbm": {"bytes_per_token": bytes_tok, "achieved_gbs": round(bytes_tok * value / world / 1e9, 1),
                      "peak_gbs": hbm_peak, "frac": round(bytes_tok * value / world / 1e9 / hbm_peak, 4),
                      "peak_kind": peak_kind},
-        "roofline": {"kernel": "gemv_fast<2048,NORM,SWIGLU> (gate/up + RMSNorm + SwiGLU)", "bound": "hbm",
+        "roofline": {"kernel": f"gemv_{args.gemv}<2048,NORM,SWIGLU> (gate/up + RMSNorm + SwiGLU)", "bound": "hbm",
                      "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
                      "frac": round(achieved / hbm_peak, 4), "traffic": traffic,
                      "algorithmic_bytes_per_launch": w_bytes, "avg_launch_us": round(kern_s * 1e6, 3),
