@@ -46,7 +46,7 @@ def parse():
     ap.add_argument("--new-tokens", type=int, default=32)
     ap.add_argument("--a8w8", action="store_true", help="int8 weights / per-token int8 activations (M/F/L groups)")
     ap.add_argument("--no-pdl", action="store_true")
-    ap.add_argument("--gemv", default="bulk", choices=["bulk", "registers"],
+    ap.add_argument("--gemv", default="registers", choices=["bulk", "registers"],
                     help="decode GEMV weight streaming: shared-memory bulk copies or register loads")
     ap.add_argument("--prefill-delta", default="chunked", choices=["chunked", "sequential"])
     ap.add_argument("--no-cpu-baseline", action="store_true")

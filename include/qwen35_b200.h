@@ -109,7 +109,7 @@ typedef struct {
 } q35_gemv_desc;
 int q35_gemv(const q35_gemv_desc* d, void* stream);
 
-/* Weight-streaming strategy of the K = 2048 / 6144 decode GEMVs (process-wide, default BULK):
+/* Weight-streaming strategy of the K = 2048 / 6144 decode GEMVs (process-wide, default REGISTERS):
  * BULK stages weights through shared memory with bulk asynchronous copies issued before the
  * programmatic-dependent-launch wait; REGISTERS streams 16-byte loads into registers. */
 enum { Q35_GEMV_BULK = 0, Q35_GEMV_REGISTERS = 1 };

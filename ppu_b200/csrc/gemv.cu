@@ -473,7 +473,7 @@ int launch_any(const GemvParams& p, cudaStream_t s, bool pdl) {
 
 #include "gemv_bulk.cuh"
 
-int g_gemv_variant = Q35_GEMV_BULK;
+int g_gemv_variant = Q35_GEMV_REGISTERS;  // measured faster on B200 (see microbench)
 
 template <int PRO, int EPI, bool INT8>
 int dispatch_k(const GemvParams& p, cudaStream_t s, bool pdl) {

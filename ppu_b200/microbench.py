@@ -1,0 +1,161 @@
+"""Per-kernel microbenchmarks of the hot path on one GPU (CUDA-event timing, cold weights).
+
+``python -m ppu_b200.microbench [--kernels gate_up,in_proj,...] [--reps N]`` prints one JSON line
+per kernel with its average launch time, algorithmic bytes (or FLOPs) and the achieved fraction of
+the measured HBM bandwidth (or bf16 tensor peak). Decode GEMVs rotate over one weight copy per
+layer (1.2 GB for gate/up across 24 layers, far larger than the 126 MB L2) so every launch streams
+from HBM, as in the decode step. Also the small-case target of the ncu captures under profiles/.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+from pathlib import Path
+
+import torch
+
+from . import kernels as K
+from . import lib as L
+
+ROOT = Path(__file__).resolve().parent.parent
+
+
+def _peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"])
+    return 6650.0, 1590.0
+
+
+def _time(fn, reps: int, warm: int = 2) -> float:
+    for _ in range(warm):
+        fn(0)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(reps):
+        fn(i)
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / 1000.0 / reps
+
+
+def run(kernels: list[str], reps: int, layers: int = 24, a8w8: bool = False):
+    dev = torch.device("cuda")
+    hbm, tflops = _peaks()
+    g = torch.Generator(device=dev).manual_seed(0)
+    H, I = 2048, 6144
+    out = []
+
+    def w(rows, k):
+        t = (torch.randn(rows, k, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+        if a8w8:
+            q, s = K.quantize_rows(t)
+            return q, s.reshape(-1).contiguous()
+        return t, None
+
+    x = torch.randn(H, device=dev, generator=g).to(torch.bfloat16)
+    xi = torch.randn(I, device=dev, generator=g).to(torch.bfloat16)
+    nw = (torch.randn(H, device=dev, generator=g) * 0.1).to(torch.bfloat16)
+
+    def report(name, seconds, nbytes=None, flops=None):
+        rec = {"kernel": name, "avg_us": round(seconds * 1e6, 3)}
+        if nbytes is not None:
+            gbs = nbytes / seconds / 1e9
+            rec.update(bytes=nbytes, gbs=round(gbs, 1), hbm_frac=round(gbs / hbm, 4))
+        if flops is not None:
+            tf = flops / seconds / 1e12
+            rec.update(flops=flops, tflops=round(tf, 1), tensor_frac=round(tf / tflops, 4))
+        out.append(rec)
+        print(json.dumps(rec), flush=True)
+
+    def gemv_case(name, rows, k, prologue, epilogue):
+        ws = [w(rows, k) for _ in range(layers)]
+        resid = torch.randn(H, device=dev, generator=g).to(torch.bfloat16)
+        inp = xi if k == I else x
+
+        def fn(i):
+            wt, sc = ws[i % layers]
+            K.fused_gemv(wt, inp if prologue == L.PRO_PLAIN else resid, prologue=prologue, epilogue=epilogue,
+                         norm_weight=nw, w_scale=sc, resid=resid)
+
+        t = _time(fn, reps * layers)
+        esz = 1 if a8w8 else 2
+        report(name, t, nbytes=rows * k * esz + (rows * 4 if a8w8 else 0))
+
+    for name in kernels:
+        if name == "gate_up":
+            gemv_case(name, 2 * I, H, L.PRO_NORM, L.EPI_SWIGLU)
+        elif name == "in_proj":
+            gemv_case(name, 8224, H, L.PRO_NORM, L.EPI_STORE)
+        elif name == "down":
+            gemv_case(name, H, I, L.PRO_PLAIN, L.EPI_RESIDUAL)
+        elif name == "out_proj":
+            gemv_case(name, H, H, L.PRO_PLAIN, L.EPI_RESIDUAL)
+        elif name == "lm_head":
+            e = (torch.randn(248320, H, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+            h = torch.randn(1, H, device=dev, generator=g).to(torch.bfloat16)
+            t = _time(lambda i: K.lm_head_argmax(h, e, norm_weight=nw), reps)
+            report(name, t, nbytes=e.numel() * 2)
+            del e
+        elif name == "attn_decode":
+            max_len, n = 1152, 1056
+            kc = [torch.randn(1, 2, max_len, 256, device=dev, generator=g).to(torch.bfloat16) for _ in range(6)]
+            vc = [torch.randn(1, 2, max_len, 256, device=dev, generator=g).to(torch.bfloat16) for _ in range(6)]
+            packed = torch.randn(1, 5120, device=dev, generator=g).to(torch.bfloat16)
+            qw = torch.zeros(256, device=dev, dtype=torch.bfloat16)
+            inv = torch.ones(32, device=dev)
+            ln = torch.tensor([n], device=dev, dtype=torch.int64)
+            t = _time(lambda i: K.attn_decode(packed, qw, qw, inv, kc[i % 6], vc[i % 6], ln, ln, q_heads=8,
+                                              kv_heads=2, rotary_dim=64), reps * 6)
+            report(name, t, nbytes=2 * 2 * 2 * n * 256)
+        elif name == "delta_decode":
+            packed = torch.randn(1, 8224, device=dev, generator=g).to(torch.bfloat16)
+            cw = (torch.randn(6144, 4, device=dev, generator=g) * 0.5).to(torch.bfloat16)
+            cs = [torch.zeros(1, 6144, 4, device=dev, dtype=torch.bfloat16) for _ in range(18)]
+            st = [torch.zeros(1, 16, 128, 128, device=dev) for _ in range(18)]
+            z16 = torch.zeros(16, device=dev, dtype=torch.bfloat16)
+            gw = torch.ones(128, device=dev, dtype=torch.bfloat16)
+            t = _time(lambda i: K.delta_decode(packed, cw, cs[i % 18], z16, z16, gw, st[i % 18]), reps * 18)
+            report(name, t, nbytes=2 * 16 * 128 * 128 * 4 + 3 * 6144 * 4 * 2)
+        elif name.startswith("gemm_tc"):
+            m = 1024
+            for (n, k, epi, label) in ((8224, H, L.EPI_STORE, "in_proj"), (2 * I, H, L.EPI_SWIGLU, "gate_up"),
+                                       (H, I, L.EPI_RESIDUAL, "down")):
+                a = torch.randn(m, k, device=dev, generator=g).to(torch.bfloat16)
+                wt = (torch.randn(n, k, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+                r = torch.zeros(m, H, device=dev, dtype=torch.bfloat16)
+                t = _time(lambda i: K.gemm(a, wt, epilogue=epi, out=r if epi == L.EPI_RESIDUAL else None, tc=True),
+                          reps)
+                report(f"gemm_tc_{label}", t, flops=2 * m * n * k)
+        elif name == "delta_prefill":
+            Lp = 1024
+            qkv = torch.randn(1, Lp, 6144, device=dev, generator=g).to(torch.bfloat16)
+            packed = torch.randn(1, Lp, 8224, device=dev, generator=g).to(torch.bfloat16)
+            z16 = torch.zeros(16, device=dev, dtype=torch.bfloat16)
+            st = torch.zeros(1, 16, 128, 128, device=dev)
+            t = _time(lambda i: K.delta_chunked_fused(qkv, packed, z16, z16, st), reps)
+            report("delta_chunked_1024", t, flops=16 * 16 * 11_700_000)
+            t = _time(lambda i: K.delta_recurrent_fused(qkv, packed, z16, z16, st), max(1, reps // 4))
+            report("delta_sequential_1024", t)
+        else:
+            raise ValueError(f"unknown kernel {name}")
+    return out
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--kernels", default="gate_up,in_proj,down,out_proj,lm_head,attn_decode,delta_decode,"
+                                         "gemm_tc,delta_prefill")
+    ap.add_argument("--reps", type=int, default=5)
+    ap.add_argument("--a8w8", action="store_true")
+    ap.add_argument("--gemv", default="registers", choices=["bulk", "registers"])
+    args = ap.parse_args()
+    L.call("q35_set_gemv_variant", L.Q35_GEMV_BULK if args.gemv == "bulk" else L.Q35_GEMV_REGISTERS)
+    run(args.kernels.split(","), args.reps, a8w8=args.a8w8)
+
+
+if __name__ == "__main__":
+    main()

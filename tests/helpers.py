@@ -34,6 +34,17 @@ def assert_bf16_close(actual, expected, *, max_ulp=1.0, max_frac=0.02, rel=1e-2,
     assert rel_err(actual, expected) <= rel
 
 
+def assert_swiglu_close(actual, expected, rel=5e-3, abs_rms=2.0 ** -6):
+    """SwiGLU outputs of GEMMs: bf16(silu(g)) * u with g, u BF16-rounded projections. In the
+    negative tail silu(g) ~ g e^g, so a one-ulp difference in g moves the output by ~|g| ulps;
+    compare by relative Frobenius error and by absolute error against the tensor's rms."""
+    assert tuple(actual.shape) == tuple(expected.shape)
+    a, b = actual.float(), expected.float()
+    assert rel_err(a, b) <= rel, rel_err(a, b)
+    rms = float(b.pow(2).mean().sqrt())
+    assert float((a - b).abs().max()) <= abs_rms * rms * 4
+
+
 def gen(seed: int) -> torch.Generator:
     g = torch.Generator()
     g.manual_seed(seed)
