@@ -5,7 +5,9 @@ itself with exact (float64) GEMMs instead of PyTorch's BF16 GEMM (both round onc
 moves the DeltaNet states of the second and third layer by 0.2-0.8 % and the KV cache by ~0.8 %
 after a 96-token prefill; at the full 2B shape (prefill 1024, 32 teacher-forced decode steps) it
 moves logits by up to 0.10-0.15 at every step (p99 ~0.06, several BF16 ulps at |logit| ~ 4) and
-flips the oracle's own greedy top-1 at 3 of 33 steps. Exact equality of every greedy token is
+flips the oracle's own greedy top-1 at 3 of 33 steps. With A8W8 the int8 activation codes amplify
+this: changing only the FP32 summation order of the oracle's RMSNorm moves A8W8 logits by up to
+0.27 (p99 ~0.12) and flips its own top-1 at 6 of 33 steps. Exact equality of every greedy token is
 therefore not a property of the reference either; the tests check:
 
 * teacher-forced top-1 agreement: fed the same tokens, every GPU greedy choice is the oracle's
@@ -31,19 +33,20 @@ pytestmark = pytest.mark.gpu
 
 SMALL = Qwen35Dims(layers=4, vocab=8192)
 LOGIT_NOISE = 0.16  # >= the largest |logit change| of the oracle under a GEMM-order change (0.154)
+LOGIT_NOISE_A8W8 = 0.28  # >= the same for A8W8 under an RMSNorm summation-order change (0.266)
 
 
-def _near_top(tok, top, top_val, tok_val) -> bool:
-    return tok == top or tok_val >= top_val - LOGIT_NOISE
+def _near_top(tok, top, top_val, tok_val, noise=LOGIT_NOISE) -> bool:
+    return tok == top or tok_val >= top_val - noise
 
 
-def _check_stream(oracle: OracleDecoder, prompt, gpu_tokens):
+def _check_stream(oracle: OracleDecoder, prompt, gpu_tokens, noise=LOGIT_NOISE):
     """Teacher-force the oracle with the GPU tokens; returns the number of steps where the GPU
-    picked a near-tie instead of the oracle's top-1 (asserting every step is within TIE_ULPS)."""
+    picked a near-tie instead of the oracle's top-1 (asserting every step is within `noise`)."""
     ref = oracle.teacher_forced_top1(prompt, gpu_tokens)
     ties = 0
     for step, (tok, (top, top_val, tok_val)) in enumerate(zip(gpu_tokens, ref)):
-        assert _near_top(tok, top, top_val, tok_val), (step, tok, top, top_val, tok_val)
+        assert _near_top(tok, top, top_val, tok_val, noise), (step, tok, top, top_val, tok_val)
         ties += tok != top
     return ties
 
@@ -67,7 +70,8 @@ def test_small_decoder_teacher_forced(a8w8):
         top = int(oracle.next_token(h[:, -1]))
         got = int(eng.token)
         lg = ops.linear(h[:, -1], oracle.embed).float()[0]
-        assert _near_top(got, top, float(lg[top]), float(lg[got])), (step, got, top)
+        noise = LOGIT_NOISE_A8W8 if a8w8 else LOGIT_NOISE
+        assert _near_top(got, top, float(lg[top]), float(lg[got]), noise), (step, got, top)
         mismatches += got != top
         tol = 1e-1 if a8w8 else 5e-2
         for s_gpu, s_ref in zip(eng.rec_states, oracle.rec_state):
@@ -125,5 +129,7 @@ def test_full_2b_config4_greedy_stream(a8w8):
     print(f"a8w8={a8w8}: free-running streams identical for {same}/33 tokens")
     print("oracle", want)
     print("gpu   ", got)
-    ties = _check_stream(OracleDecoder(w, dims, a8w8=a8w8, max_cache_len=1152), prompt, got)
-    assert ties <= 6  # the oracle flips its own top-1 at 3 of 33 steps under a GEMM-order change
+    noise = LOGIT_NOISE_A8W8 if a8w8 else LOGIT_NOISE
+    ties = _check_stream(OracleDecoder(w, dims, a8w8=a8w8, max_cache_len=1152), prompt, got, noise)
+    # the oracle flips its own top-1 at 3 (BF16) / 6 (A8W8) of 33 steps under a summation-order change
+    assert ties <= (10 if a8w8 else 6)
