@@ -188,6 +188,20 @@ int q35_gqa_decode_attention(const void* q, const void* cache_k, const void* cac
                              int64_t heads, int64_t kv_heads, int64_t head_dim, int64_t cache_len,
                              void* workspace, size_t workspace_bytes, void* stream);
 
+/* Allocation-free q35_gqa_decode_attention (no counterpart in the reference). For callers that
+ * cannot allocate device memory when they call in (a locked or pool-only allocator, a thread that
+ * must not touch the CUDA allocator, a runtime that passes only inputs and outputs): the scratch
+ * lives in a static device array of q35_gqa_decode_noalloc_max_bytes() bytes (2 MiB) that every
+ * GPU loading this library keeps until exit. Shapes whose scratch exceeds it are rejected with
+ * Q35_EINVAL. The first call on a device looks up the array's device address (make it before any
+ * stream capture); every call clears the ticket words and shares the array, so calls that overlap
+ * on the GPU (other streams, other threads) race with each other. Calls no allocator. */
+size_t q35_gqa_decode_noalloc_max_bytes(void);
+int q35_gqa_decode_attention_noalloc(const void* q, const void* cache_k, const void* cache_v,
+                                     const int64_t* valid_length, float scale, void* out,
+                                     int64_t batch, int64_t heads, int64_t kv_heads, int64_t head_dim,
+                                     int64_t cache_len, void* stream);
+
 /* Fused decode attention layer step (integration.py:298-359 for L == 1): from the packed QGKV
  * projection output [B, 5120] it does Q/K RMSNorm + partial RoPE at position *rope_pos, writes
  * K/V at row *cache_len, attends over rows [0, *cache_len] and multiplies by sigmoid(gate):

@@ -411,3 +411,73 @@ extern "C" int q35_attn_decode(const void* packed, const void* q_weight, const v
                                 batch, q_heads, kv_heads, rotary_dim, max_len, eps, workspace, (cudaStream_t)stream,
                                 false);
 }
+
+// ------------------------------------------------------------------------------------------------
+// Allocation-free variant: scratch in a file-scope device array instead of a caller workspace.
+//
+// For callers that cannot allocate device memory at the point of the call — for example code
+// running under an allocator that is locked or pool-only, a host thread that must not touch the
+// CUDA allocator, or an embedding runtime that hands this library only its inputs and outputs.
+// The scratch (split tickets, per-split maxima/sums and partial outputs) lives in
+// `g_gqa_noalloc_scratch`, kQ35NoAllocScratchBytes bytes that every GPU loading this library
+// holds until the process exits. Host code may not pass the array's name to a kernel (on the host
+// it is only a stand-in symbol): its device address is looked up with cudaGetSymbolAddress once per
+// device, with that device current, by the first call made on that device.
+constexpr size_t kQ35NoAllocScratchBytes = 2u << 20;  // 2 MiB
+
+static __device__ __align__(256) unsigned char g_gqa_noalloc_scratch[kQ35NoAllocScratchBytes];
+
+#include <mutex>
+
+namespace {
+std::mutex g_noalloc_mutex;
+void* g_noalloc_ptr[64] = {};  // device address of the scratch array, per device ordinal
+}  // namespace
+
+extern "C" size_t q35_gqa_decode_noalloc_max_bytes(void) { return kQ35NoAllocScratchBytes; }
+
+extern "C" int q35_gqa_decode_attention_noalloc(const void* q, const void* cache_k, const void* cache_v,
+                                                const int64_t* valid_length, float scale, void* out,
+                                                int64_t batch, int64_t heads, int64_t kv_heads,
+                                                int64_t head_dim, int64_t cache_len, void* stream) {
+  Q35_REQUIRE(q && cache_k && cache_v && valid_length && out, "gqa_decode_attention_noalloc: null pointer");
+  Q35_REQUIRE(head_dim == kD, "gqa_decode_attention_noalloc: head dim %lld unsupported (256)", (long long)head_dim);
+  Q35_REQUIRE(batch >= 1 && batch <= 64 && kv_heads >= 1 && heads % kv_heads == 0 && cache_len >= 1,
+              "gqa_decode_attention_noalloc: head layout does not match cache");
+  const WsLayout w = ws_layout(batch, heads, kv_heads, cache_len);
+  Q35_REQUIRE(w.total <= kQ35NoAllocScratchBytes,
+              "gqa_decode_attention_noalloc: this shape needs %zu bytes of scratch, more than the %zu-byte "
+              "static maximum (use q35_gqa_decode_attention with a workspace)",
+              w.total, kQ35NoAllocScratchBytes);
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
+    return q35_fail(Q35_ECUDA, "gqa_decode_attention_noalloc: no current device");
+  void* scratch = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+    if (!g_noalloc_ptr[dev]) {
+      const cudaError_t e = cudaGetSymbolAddress(&g_noalloc_ptr[dev], g_gqa_noalloc_scratch);
+      if (e != cudaSuccess) {
+        g_noalloc_ptr[dev] = nullptr;
+        return q35_fail(Q35_ECUDA, "gqa_decode_attention_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+      }
+    }
+    scratch = g_noalloc_ptr[dev];
+  }
+  // The ticket words must start at zero; the kernel leaves them zero, but a call cut short by an
+  // error would not, so clear them on every call (a memset, not an allocation).
+  if (cudaMemsetAsync(scratch, 0, w.ml, (cudaStream_t)stream) != cudaSuccess)
+    return q35_fail(Q35_ECUDA, "gqa_decode_attention_noalloc: clearing the tickets failed");
+  DecodeParams p = {};
+  p.q_in = (const bf16*)q;
+  p.cache_k = (bf16*)cache_k;
+  p.cache_v = (bf16*)cache_v;
+  p.len = valid_length;
+  p.out = (bf16*)out;
+  p.Hq = (int)heads;
+  p.Hkv = (int)kv_heads;
+  p.max_len = (int)cache_len;
+  p.S = choose_splits(batch, kv_heads, cache_len);
+  p.scale = scale;
+  return launch_decode<false>(p, batch, (int)(heads / kv_heads), scratch, (cudaStream_t)stream, false);
+}

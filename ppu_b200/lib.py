@@ -79,6 +79,8 @@ _SIGS = {
     "q35_qgkv_norm_rope": (INT, [P, P, P, P, P, P, P, P, P, I64, I64, I64, I64, I64, I64, I64, F32, P]),
     "q35_gqa_decode_workspace_size": (SZ, [I64, I64, I64, I64, I64]),
     "q35_gqa_decode_attention": (INT, [P, P, P, P, F32, P, I64, I64, I64, I64, I64, P, SZ, P]),
+    "q35_gqa_decode_noalloc_max_bytes": (SZ, []),
+    "q35_gqa_decode_attention_noalloc": (INT, [P, P, P, P, F32, P, I64, I64, I64, I64, I64, P]),
     "q35_attn_decode_workspace_size": (SZ, [I64, I64, I64, I64, I64]),
     "q35_attn_decode": (INT, [P, P, P, P, P, P, P, P, P, I64, I64, I64, I64, I64, I64, F32, P, SZ, P]),
     "q35_prefill_attention": (INT, [P, P, P, P, I64, I64, I64, I64, I64, I64, I64, F32, P]),
