@@ -52,7 +52,7 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(DecodeParams p) {
   __shared__ float wm[kWarps][G], wl[kWarps][G];
   __shared__ __align__(16) float wacc[kWarps][G][kD];
   __shared__ float red[kWarps][G + 1];
-  __shared__ float cm[kMaxSplits][G];
+  __shared__ float cm[kMaxSplits][G], cl[kMaxSplits][G];
   __shared__ float cls[G];
   __shared__ unsigned ticket_s;
 
@@ -225,20 +225,22 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(DecodeParams p) {
     const float mi = __ldcg(p.part_ml + 2 * (base + i));
     const float li = __ldcg(p.part_ml + 2 * (base + i) + 1);
     cm[i / G][i % G] = li > 0.f ? mi : -INFINITY;  // empty split: zero weight
+    cl[i / G][i % G] = li;
   }
   __syncthreads();
-  if (threadIdx.x < G) {
-    const int hh = threadIdx.x;
+  if (warp < G) {  // one warp per head: max, weights and normaliser over the S splits
+    const int hh = warp;
     float M = -FLT_MAX;
-    for (int j = 0; j < S; ++j) M = fmaxf(M, cm[j][hh]);
+    for (int j = lane; j < S; j += 32) M = fmaxf(M, cm[j][hh]);
+    M = warp_max(M);
     float Ls = 0.f;
-    for (int j = 0; j < S; ++j) {
-      const float li = __ldcg(p.part_ml + 2 * (base + j * G + hh) + 1);
+    for (int j = lane; j < S; j += 32) {
       const float e = (cm[j][hh] == -INFINITY) ? 0.f : expf(cm[j][hh] - M);
       cm[j][hh] = e;
-      Ls += li * e;
+      Ls += cl[j][hh] * e;
     }
-    cls[hh] = Ls;
+    Ls = warp_sum(Ls);
+    if (lane == 0) cls[hh] = Ls;
   }
   __syncthreads();
   float a8[G][8];

@@ -30,13 +30,20 @@ def _peaks():
 
 
 def _time(fn, reps: int, warm: int = 2) -> float:
+    """Average device time of fn(0..reps-1), launched from one CUDA graph so that host launch
+    overhead (ctypes, argument checks) does not pace the kernels."""
     for _ in range(warm):
         fn(0)
     torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for i in range(reps):
+            fn(i)
+    graph.replay()
+    torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
-    for i in range(reps):
-        fn(i)
+    graph.replay()
     e1.record()
     torch.cuda.synchronize()
     return e0.elapsed_time(e1) / 1000.0 / reps
@@ -151,7 +158,7 @@ def main():
                                          "gemm_tc,delta_prefill")
     ap.add_argument("--reps", type=int, default=5)
     ap.add_argument("--a8w8", action="store_true")
-    ap.add_argument("--gemv", default="registers", choices=["bulk", "registers"])
+    ap.add_argument("--gemv", default="registers", choices=["registers", "bulk"])
     args = ap.parse_args()
     L.call("q35_set_gemv_variant", L.Q35_GEMV_BULK if args.gemv == "bulk" else L.Q35_GEMV_REGISTERS)
     run(args.kernels.split(","), args.reps, a8w8=args.a8w8)

@@ -17,7 +17,7 @@ from oracle import ops as O
 from ppu_b200 import kernels as K
 from ppu_b200 import lib as L
 
-from .helpers import BF16, assert_bf16_close, assert_swiglu_close, randn, rel_err
+from .helpers import BF16, assert_bf16_close, assert_residual_close, assert_swiglu_close, randn, rel_err
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda"
@@ -228,7 +228,7 @@ def test_gemm_epilogues():
     r = randn(130, 2048, seed=5)
     rd = cu(r.clone())
     K.gemm(cu(act), cu(wd), epilogue=L.EPI_RESIDUAL, out=rd)
-    assert_bf16_close(rd.cpu(), (r.float() + O.linear(act, wd).float()).to(BF16), max_ulp=2, max_frac=0.02)
+    assert_residual_close(rd, r, O.linear(act, wd))
 
 
 # ------------------------------------------------------------------ attention

@@ -10,7 +10,7 @@ from oracle import ops as O
 from ppu_b200 import kernels as K
 from ppu_b200 import lib as L
 
-from .helpers import BF16, assert_bf16_close, assert_swiglu_close, randn
+from .helpers import BF16, assert_bf16_close, assert_residual_close, assert_swiglu_close, randn
 
 pytestmark = pytest.mark.gpu
 
@@ -41,7 +41,7 @@ def test_gemm_tc_epilogues():
     K.gemm(cu(act), cu(wd), epilogue=L.EPI_RESIDUAL, out=rd, tc=True)
     torch.cuda.synchronize()
     assert K.tc_error() == 0
-    assert_bf16_close(rd.cpu(), (r.float() + O.linear(act, wd).float()).to(BF16), max_ulp=2, max_frac=0.02)
+    assert_residual_close(rd, r, O.linear(act, wd))
 
 
 @pytest.mark.parametrize("epi", [L.EPI_STORE, L.EPI_SWIGLU, L.EPI_RESIDUAL])
