@@ -49,6 +49,8 @@ def parse():
     ap.add_argument("--gemv", default="registers", choices=["registers", "bulk"],
                     help="decode GEMV weight streaming: shared-memory bulk copies or register loads")
     ap.add_argument("--prefill-delta", default="chunked", choices=["chunked", "sequential"])
+    ap.add_argument("--decode", default="kernels", choices=["kernels", "persistent"],
+                    help="decode step: one persistent cooperative kernel (bf16) or the per-op kernels")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
 
@@ -202,7 +204,8 @@ def main():
     L.call("q35_set_gemv_variant", L.Q35_GEMV_BULK if args.gemv == "bulk" else L.Q35_GEMV_REGISTERS)
     weights = make_weights(dims, seed=0, device=dev)
     eng = Qwen35Engine(weights, dims, a8w8=args.a8w8, max_len=cache_bucket(P, T), max_prefill=P, device=dev,
-                       use_pdl=not args.no_pdl, prefill_chunked=args.prefill_delta == "chunked")
+                       use_pdl=not args.no_pdl, prefill_chunked=args.prefill_delta == "chunked",
+                       persistent=(args.decode == "persistent" and not args.a8w8))
     gate_up_w = [t["gate_up"] for t in eng.layer_tensors]
     post_ln = [t["post_ln"] for t in eng.layer_tensors]
     gate_up_s = [t.get("gate_up_scale") for t in eng.layer_tensors]
@@ -318,7 +321,8 @@ def main():
             "model": "Qwen3.5-2B-shape text decoder (24 layers, 3xGatedDeltaNet:1xGQA, hidden 2048, vocab 248320)",
             "global_batch": world, "seq_len": P, "parallelism": f"request-parallel replicas x{world}",
             "a8w8": args.a8w8, "pdl": not args.no_pdl, "cuda_graph": "1 decode step per replay",
-            "gemv": args.gemv, "prefill_delta": args.prefill_delta, "prefill_gemm": "tcgen05",
+            "decode_step": "persistent" if eng.persistent else "per-op kernels", "gemv": args.gemv,
+            "prefill_delta": args.prefill_delta, "prefill_gemm": "tcgen05",
             "l2": "weights 3.8 GB per step >> 126 MB L2 (no flush needed)",
         },
         "ttft_ms": round(prefill_ms / args.steps, 3),

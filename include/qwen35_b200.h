@@ -322,6 +322,18 @@ int q35_decoder_decode_step(q35_decoder* dec, void* stream);
 /* Number of kernels one decode step launches (for launch accounting). */
 int q35_decoder_kernels_per_step(const q35_decoder* dec);
 
+/* The same greedy decode step as ONE cooperative kernel (graph.py:51-79 in one launch, plus a
+ * 4-byte memset of its barrier counter): one CTA per SM streams its share of every weight matrix
+ * through a shared-memory ring without stopping at op boundaries; dependent ops meet at bounded
+ * grid barriers. bf16 weights and the Qwen3.5-2B shapes only (Q35_ENOTSUP otherwise, with the
+ * reason; the per-op q35_decoder_decode_step covers the rest). Results match the per-op step up
+ * to FP32 summation order. */
+int q35_decoder_decode_step_persistent(q35_decoder* dec, void* stream);
+int q35_decoder_has_persistent(const q35_decoder* dec);
+/* Non-zero when a bounded wait of the persistent step gave up (1 grid barrier, 2 ring slot,
+ * 3 ring data); reading clears it. */
+int q35_decoder_persistent_error(void);
+
 #ifdef __cplusplus
 }
 #endif

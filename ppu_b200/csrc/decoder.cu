@@ -13,6 +13,7 @@
 // by its last CTA: 5 * layers + 1 kernels, all on one stream, optionally chained with
 // programmatic dependent launch so each kernel's weight prefetch overlaps its predecessor.
 #include <cstring>
+#include <string>
 #include <vector>
 
 #include "common.cuh"
@@ -48,6 +49,13 @@ int q35_delta_chunked_launch(const void* qkv, const void* packed, const void* a_
                              float* ws, cudaStream_t s);
 size_t q35_attn_decode_workspace_size(int64_t batch, int64_t q_heads, int64_t kv_heads, int64_t head_dim,
                                       int64_t cache_len);
+struct q35_pk_plan;
+size_t q35_pk_workspace_bytes(const q35_decoder_desc& d);
+const char* q35_pk_unsupported(const q35_decoder_desc& d);
+int q35_pk_create(const q35_decoder_desc& d, const q35_layer_desc* layers, bf16* resid, bf16* proj, bf16* act,
+                  void* ws, q35_pk_plan** out);
+void q35_pk_destroy(q35_pk_plan* plan);
+int q35_pk_launch(const q35_pk_plan* plan, cudaStream_t s);
 
 namespace {
 
@@ -71,6 +79,7 @@ struct Buffers {
   bf16* act;          // SwiGLU output [intermediate]
   void* attn_ws;
   void* lm_ws;
+  void* pk_ws;        // persistent decode step: op table, attention partials, barrier words
   // prefill
   bf16* p_resid;      // [L, H]
   bf16* p_norm;       // [L, H]
@@ -102,6 +111,7 @@ Buffers carve(const q35_decoder_desc& d, void* base, size_t* total) {
   b.mix_out = c.take<bf16>(mixw);
   b.act = c.take<bf16>(d.intermediate);
   b.attn_ws = c.take<char>(q35_attn_decode_workspace_size(1, d.q_heads, d.kv_heads, d.head_dim, d.max_len));
+  b.pk_ws = c.take<char>(q35_pk_workspace_bytes(d));
   b.p_resid = c.take<bf16>(L * d.hidden);
   b.p_norm = c.take<bf16>(L * d.hidden);
   b.p_packed = c.take<bf16>(L * rows_in);
@@ -125,6 +135,8 @@ struct q35_decoder {
   q35_decoder_desc d;
   std::vector<q35_layer_desc> layers;
   Buffers buf;
+  q35_pk_plan* pk = nullptr;  // persistent decode step, when the model fits its built-in shapes
+  std::string pk_why;         // otherwise the reason
 };
 
 extern "C" size_t q35_decoder_workspace_size(const q35_decoder_desc* desc) {
@@ -162,11 +174,30 @@ extern "C" int q35_decoder_create(const q35_decoder_desc* desc, q35_decoder** ou
   dec->d.layers = dec->layers.data();
   size_t total = 0;
   dec->buf = carve(d, d.workspace, &total);
+  const char* why = q35_pk_unsupported(dec->d);
+  if (why[0]) {
+    dec->pk_why = why;
+  } else if (q35_pk_create(dec->d, dec->layers.data(), dec->buf.resid, dec->buf.mix_in_out, dec->buf.act,
+                           dec->buf.pk_ws, &dec->pk) != Q35_OK) {
+    dec->pk_why = q35_last_error();
+    dec->pk = nullptr;
+  }
   *out = dec;
   return Q35_OK;
 }
 
-extern "C" void q35_decoder_destroy(q35_decoder* dec) { delete dec; }
+extern "C" void q35_decoder_destroy(q35_decoder* dec) {
+  if (dec && dec->pk) q35_pk_destroy(dec->pk);
+  delete dec;
+}
+
+extern "C" int q35_decoder_decode_step_persistent(q35_decoder* dec, void* stream) {
+  Q35_REQUIRE(dec, "decode_step_persistent: null decoder");
+  if (!dec->pk) return q35_fail(Q35_ENOTSUP, "persistent decode unavailable: %s", dec->pk_why.c_str());
+  return q35_pk_launch(dec->pk, (cudaStream_t)stream);
+}
+
+extern "C" int q35_decoder_has_persistent(const q35_decoder* dec) { return dec && dec->pk ? 1 : 0; }
 
 extern "C" int q35_decoder_kernels_per_step(const q35_decoder* dec) { return dec ? 5 * dec->d.n_layers + 1 : 0; }
 

@@ -5,7 +5,9 @@ packs the model (integration.py:69-140: [qkv|z|a|b] for DeltaNet, [Q|gate..|K|V]
 [gate; up] for the MLP), optionally quantises the M/F/L projection groups to A8W8 with the CUDA
 quantiser, allocates the static KV cache, DeltaNet conv/recurrent states and one workspace, and
 creates a ``q35_decoder``. Prefill and each greedy decode step are single C calls on the current
-stream; ``capture`` records decode steps into a CUDA graph (qwen35_fused/graph.py).
+stream; ``capture`` records decode steps into a CUDA graph (qwen35_fused/graph.py). The decode
+step is the per-op step (5 kernels per layer + LM head), or with ``persistent=True`` the
+one-kernel persistent step (bf16, 2B shapes).
 """
 
 from __future__ import annotations
@@ -36,7 +38,8 @@ def cache_bucket(input_len: int, max_new_tokens: int) -> int:
 class Qwen35Engine:
     def __init__(self, weights: dict, dims: Qwen35Dims = Qwen35Dims(), *, a8w8: bool = False,
                  max_len: int = 2048, max_prefill: int = 1024, device="cuda", use_pdl: bool = True,
-                 prefill_tc: bool = True, prefill_chunked: bool = True, log_len: int = 4096, release_source: bool = False):
+                 prefill_tc: bool = True, prefill_chunked: bool = True, log_len: int = 4096, release_source: bool = False,
+                 persistent: bool | None = None):
         L.load()
         dev = torch.device(device)
         if dev.type != "cuda":
@@ -144,7 +147,11 @@ class Qwen35Engine:
         handle = C.c_void_p()
         L.check(L.load().q35_decoder_create(C.byref(desc), C.byref(handle)), "q35_decoder_create")
         self.handle = handle
-        self.kernels_per_step = L.load().q35_decoder_kernels_per_step(handle)
+        self.has_persistent = bool(L.load().q35_decoder_has_persistent(handle))
+        if persistent and not self.has_persistent:
+            raise ValueError("persistent decode step unavailable for this model (A8W8, shapes or device)")
+        self.persistent = False if persistent is None else bool(persistent)
+        self.kernels_per_step = 1 if self.persistent else L.load().q35_decoder_kernels_per_step(handle)
         self._graphs: dict[int, torch.cuda.CUDAGraph] = {}
 
     def __del__(self):
@@ -180,7 +187,12 @@ class Qwen35Engine:
 
     def decode_step(self) -> torch.Tensor:
         """One greedy decode step on the current stream (reads/writes ``self.token``)."""
-        L.check(L.load().q35_decoder_decode_step(self.handle, L.stream_of(self.device)), "q35_decoder_decode_step")
+        if self.persistent:
+            L.check(L.load().q35_decoder_decode_step_persistent(self.handle, L.stream_of(self.device)),
+                    "q35_decoder_decode_step_persistent")
+        else:
+            L.check(L.load().q35_decoder_decode_step(self.handle, L.stream_of(self.device)),
+                    "q35_decoder_decode_step")
         return self.token
 
     def capture(self, steps: int = 1) -> torch.cuda.CUDAGraph:

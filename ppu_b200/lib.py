@@ -95,6 +95,9 @@ _SIGS = {
     "q35_decoder_prefill": (INT, [P, P, I64, P]),
     "q35_decoder_decode_step": (INT, [P, P]),
     "q35_decoder_kernels_per_step": (INT, [P]),
+    "q35_decoder_decode_step_persistent": (INT, [P, P]),
+    "q35_decoder_has_persistent": (INT, [P]),
+    "q35_decoder_persistent_error": (INT, []),
 }
 
 EXPORTED = tuple(_SIGS)
