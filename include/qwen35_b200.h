@@ -330,6 +330,13 @@ int q35_decoder_kernels_per_step(const q35_decoder* dec);
  * to FP32 summation order. */
 int q35_decoder_decode_step_persistent(q35_decoder* dec, void* stream);
 int q35_decoder_has_persistent(const q35_decoder* dec);
+/* Step tracing of the persistent step (no counterpart in the reference: a profiling aid). With a
+ * device buffer of >= (ops + 1) * 148 * 2 int64 entries, thread 0 of every CTA writes the
+ * %globaltimer (ns) on arriving at and leaving grid barrier j to [(j * 148 + cta) * 2 + {0, 1}];
+ * row `ops` holds each CTA's step start and end. NULL turns tracing off. `ops` is
+ * q35_decoder_trace_ops() (0 without a persistent step). */
+int q35_decoder_set_trace(q35_decoder* dec, int64_t* trace, int64_t entries);
+int q35_decoder_trace_ops(const q35_decoder* dec);
 /* Non-zero when a bounded wait of the persistent step gave up (1 grid barrier, 2 ring slot,
  * 3 ring data); reading clears it. */
 int q35_decoder_persistent_error(void);

@@ -14,10 +14,12 @@
 //    (atomic counter, acquire polling, bounded wait that sets an error word instead of hanging;
 //    the cooperative launch guarantees co-residency). A GEMV op builds its input vector in shared
 //    memory (plain / RMSNorm / embedding gather + RMSNorm / gated RMSNorm of the DeltaNet output),
-//    then consumes its stages: each warp dot-products a contiguous run of 512-byte chunks against
-//    the vector, reduces once per row run, and parks the sums; one thread per unit adds them in a
-//    fixed order and applies the epilogue (store; store + causal-conv update of that channel;
-//    residual add in place; SwiGLU; running greedy top-1);
+//    then consumes its stages on the tensor cores: ldmatrix reads 8 weight rows x 32 k (rows are
+//    copied into 16-byte-padded slots so the reads hit distinct banks) and m16n8k16 MMAs multiply
+//    them with the vector broadcast into every row of A; warps split (8-row tile, k-range) and park
+//    their partial sums, which one thread per unit adds in a fixed order before the epilogue
+//    (store; store + causal-conv update of that channel; residual add in place; SwiGLU; running
+//    greedy top-1);
 //  * mixers use all CTAs: the DeltaNet step is 128 items (head x 16 value columns, state slice
 //    prefetched before the barrier), attention is split-KV partials over 2 x 74 items and a
 //    combine over 128 (head x 16 dims) items; the conv update rides the in-projection epilogue
@@ -42,9 +44,14 @@ namespace {
 constexpr int kPkCWarps = 16;
 constexpr int kPkCThreads = kPkCWarps * 32;
 constexpr int kPkThreads = kPkCThreads + 32;  // + one producer warp
-constexpr int kPkStages = 4;
-constexpr int kPkStageBytes = 48 * 1024;
-constexpr int kPkChunks = kPkStageBytes / 512;  // 512-byte warp-chunks per stage
+constexpr int kPkStages = 6;
+constexpr int kPkKChunk = 2048;                  // k values of one stage row (4 KB of bf16)
+constexpr int kPkTileRows = 8;                   // weight rows per stage (one MMA N tile)
+constexpr int kPkRowPad = 16;                    // bytes after each row: ldmatrix rows hit distinct banks
+constexpr int kPkRowStride = kPkKChunk * 2 + kPkRowPad;
+constexpr int kPkStageStride = (kPkTileRows * kPkRowStride + 127) / 128 * 128;
+constexpr int kPkGroups = 4;                     // consumer warp groups, one stage each at a time
+constexpr int kPkGroupWarps = kPkCWarps / kPkGroups;  // warps splitting a stage's k range
 constexpr int kPkMaxK = 6144;
 constexpr int kPkSplits = 74;                    // attention splits per KV head
 constexpr int kPkMaxRows = 256;                  // cache rows per attention item
@@ -99,12 +106,14 @@ struct PkParams {
   float* attn_ml;             // [Hkv * kPkSplits * G][2]
   unsigned* bar_counter;      // zeroed before each launch
   unsigned long long* top1;   // zero between launches (the finisher re-zeroes it)
+  int64_t* trace;             // optional: [n_ops + 1][CTAs][2] globaltimer ns (see q35_decoder_set_trace)
 };
 
 struct __align__(16) PkShared {
   uint64_t full[kPkStages];
   uint64_t empty[kPkStages];
-  float slots[2][kPkChunks];
+  uint32_t issued[kPkStages];  // stage number whose copies the producer last armed in each slot
+  float gpart[kPkGroups][2][kPkGroupWarps][kPkTileRows];  // per-warp tile partials, by tile parity
   float red[kPkCWarps * 4];
   int red_i[kPkCWarps];
   int abort;
@@ -129,9 +138,9 @@ struct __align__(16) PkShared {
   } u;
 };
 
-constexpr size_t kPkSmemBytes = (size_t)kPkStages * kPkStageBytes + sizeof(PkShared);
+constexpr size_t kPkSmemBytes = (size_t)kPkStages * kPkStageStride + sizeof(PkShared);
 static_assert(offsetof(PkShared, u) % 16 == 0 && sizeof(PkShared) % 16 == 0, "vector access alignment");
-static_assert((size_t)kPkStages * kPkStageBytes % 128 == 0, "ring stages keep bulk-copy alignment");
+static_assert(kPkStageStride % 128 == 0, "ring stages keep bulk-copy alignment");
 static_assert(kPkSmemBytes <= 227 * 1024, "persistent decode shared memory over budget");
 
 // ------------------------------------------------------------------------------ primitives
@@ -141,6 +150,20 @@ Q35_DEV void cbar() { asm volatile("bar.sync 1, %0;" ::"n"(kPkCThreads) : "memor
 
 // Consumer barrier that also ORs a per-thread flag: every consumer thread gets the same answer,
 // so a decision to stop is taken by all of them at the same barrier.
+// Named barrier of one consumer warp group (ids 2..), with the same OR-reduction.
+Q35_DEV bool gbar_any(int group, bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.or.pred q, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)v), "r"(2 + group), "n"(kPkGroupWarps * 32)
+      : "memory");
+  return r != 0;
+}
+
 Q35_DEV bool cbar_any(bool v) {
   uint32_t r;
   asm volatile(
@@ -171,6 +194,20 @@ Q35_DEV bool mbar_wait(uint64_t* bar, uint32_t parity) {
   }
 }
 
+// Consumers take stages out of order (each warp its own tiles), so a warp may ask for stage s
+// while its slot still holds stage s - kPkStages: wait until the producer has armed stage s in
+// the slot before waiting on the slot's phase parity (which would alias stage s - 2 * kPkStages).
+Q35_DEV bool wait_issued(const uint32_t* issued, uint32_t stage) {
+  const long long t0 = clock64();
+  while (true) {
+    uint32_t v;
+    asm volatile("ld.acquire.cta.shared::cta.u32 %0, [%1];" : "=r"(v) : "r"(smem_u32(issued)) : "memory");
+    if (v == stage) return true;
+    if (clock64() - t0 > kPkWaitBudget) return false;
+    __nanosleep(128);  // most waiting warps are several stages early: stay off the issue ports
+  }
+}
+
 Q35_DEV void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
@@ -180,6 +217,17 @@ Q35_DEV void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar)
                    smem_u32(dst)),
                "l"(src), "r"(bytes), "r"(smem_u32(bar))
                : "memory");
+}
+
+Q35_DEV int64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return (int64_t)t;
+}
+
+// Thread 0 records (arrival, release) of grid barrier `j`; row n_ops holds (start, end) of the step.
+Q35_DEV void trace_mark(const PkParams& p, int j, int which) {
+  if (p.trace && threadIdx.x == 0) p.trace[((int64_t)j * gridDim.x + blockIdx.x) * 2 + which] = globaltimer_ns();
 }
 
 Q35_DEV unsigned ld_acquire(const unsigned* p) {
@@ -196,9 +244,12 @@ Q35_DEV float ldcg_bf(const bf16* p) {
 Q35_DEV bool grid_barrier(const PkParams& p, unsigned target, PkShared& S) {
   cbar();
   bool fail = false;
+  const int j = (int)(target / gridDim.x) - 1;
+  trace_mark(p, j, 0);
   if (threadIdx.x == 0) {
-    __threadfence();
-    atomicAdd(p.bar_counter, 1u);
+    // release: the CTA's writes (ordered before this thread by the consumer barrier) become
+    // visible before the count; acquire on the polled count makes the other CTAs' writes visible
+    asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(p.bar_counter) : "memory");
     const long long t0 = clock64();
     while (ld_acquire(p.bar_counter) < target) {
       if (clock64() - t0 > kPkWaitBudget) {
@@ -206,9 +257,10 @@ Q35_DEV bool grid_barrier(const PkParams& p, unsigned target, PkShared& S) {
         fail = true;
         break;
       }
+      __nanosleep(32);
     }
-    __threadfence();
   }
+  trace_mark(p, j, 1);
   if (cbar_any(fail)) {
     if (threadIdx.x == 0) *(volatile int*)&S.abort = 1;  // tells the producer to stop issuing
     return false;
@@ -237,35 +289,65 @@ Q35_DEV void unit_range(int n, int& u0, int& u1) {
   u1 = (int)((int64_t)(blockIdx.x + 1) * n / gridDim.x);
 }
 
-Q35_DEV int units_per_stage(const PkOp& op) { return kPkStageBytes / (op.rpu * op.k * 2); }
+// A GEMV op's work on one CTA: tiles of 8 weight rows (8 units, or 4 units' gate + up rows for
+// SwiGLU) over K, each tile K / 2048 stages (k-chunks) of 8 x 4 KB.
+struct TilePlan {
+  int u0, u1, upt, ntiles, spt;
+};
+Q35_DEV TilePlan tile_plan(const PkOp& op) {
+  TilePlan t;
+  unit_range(op.n_out, t.u0, t.u1);
+  t.upt = kPkTileRows / op.rpu;
+  t.ntiles = (t.u1 - t.u0 + t.upt - 1) / t.upt;
+  t.spt = op.k / kPkKChunk;
+  return t;
+}
+// Global weight row of stage row r in tile `tile`, or -1 past the CTA's units.
+Q35_DEV int64_t tile_row(const PkOp& op, const TilePlan& tp, int tile, int r) {
+  const int uu = r % tp.upt, half = r / tp.upt;  // half 1 = up rows (SwiGLU)
+  const int unit = tp.u0 + tile * tp.upt + uu;
+  if (unit >= tp.u1) return -1;
+  return (int64_t)half * op.n_out + unit;
+}
 
 // ------------------------------------------------------------------------------ producer
 Q35_DEV void producer(const PkParams& p, PkShared& S, unsigned char* ring) {
   uint32_t st = 0;
   bool stop = false;
   for (int i = 0; i < p.n_ops && !stop && !*(volatile int*)&S.abort; ++i) {
-    const PkOp& op = p.ops[i];
-    if (op.kind != OP_GEMV) continue;
+    if (p.ops[i].kind != OP_GEMV) continue;
+    // the fields this loop needs, in registers (each copy instruction clobbers memory, which
+    // would otherwise reload them from the op table)
+    const int n_out = p.ops[i].n_out, k = p.ops[i].k, rpu = p.ops[i].rpu;
+    const char* w = reinterpret_cast<const char*>(p.ops[i].weight);
     int u0, u1;
-    unit_range(op.n_out, u0, u1);
-    const int su = units_per_stage(op);
-    const int64_t rb = (int64_t)op.k * 2;
-    for (int u = u0; u < u1; u += su, ++st) {
-      const int slot = st % kPkStages;
-      if (!mbar_wait(&S.empty[slot], ((st / kPkStages) & 1) ^ 1)) {
-        atomicCAS(&q35_pk_error_word, 0, 2);
-        stop = true;  // the consumers time out on the stage this would have filled
-        break;
+    unit_range(n_out, u0, u1);
+    const int upt = kPkTileRows / rpu, spt = k / kPkKChunk;
+    const int64_t rb = (int64_t)k * 2;
+    for (int ua = u0; ua < u1 && !stop; ua += upt) {
+      const int nu = min(upt, u1 - ua);
+      const char* gate = w + ua * rb;
+      const char* up = w + ((int64_t)n_out + ua) * rb;
+      for (int j = 0; j < spt; ++j, ++st) {
+        const int slot = st % kPkStages;
+        if (!mbar_wait(&S.empty[slot], ((st / kPkStages) & 1) ^ 1)) {
+          atomicCAS(&q35_pk_error_word, 0, 2);
+          stop = true;  // the consumers time out on the stage this would have filled
+          break;
+        }
+        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(&S.full[slot])),
+                     "r"((uint32_t)(nu * rpu * kPkKChunk * 2))
+                     : "memory");
+        asm volatile("st.release.cta.shared::cta.u32 [%0], %1;" ::"r"(smem_u32(&S.issued[slot])), "r"(st) : "memory");
+        unsigned char* dst = ring + (size_t)slot * kPkStageStride;
+        const int64_t koff = (int64_t)j * kPkKChunk * 2;
+        // stage rows: units' (gate) rows 0..nu-1, then for SwiGLU their up rows at upt..upt+nu-1
+        for (int r = 0; r < nu; ++r)
+          bulk_g2s(dst + r * kPkRowStride, gate + r * rb + koff, kPkKChunk * 2, &S.full[slot]);
+        if (rpu == 2)
+          for (int r = 0; r < nu; ++r)
+            bulk_g2s(dst + (upt + r) * kPkRowStride, up + r * rb + koff, kPkKChunk * 2, &S.full[slot]);
       }
-      const int n = min(su, u1 - u);
-      const uint32_t bytes = (uint32_t)(n * rb);
-      asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(&S.full[slot])),
-                   "r"(bytes * op.rpu)
-                   : "memory");
-      unsigned char* dst = ring + (size_t)slot * kPkStageBytes;
-      const char* w = reinterpret_cast<const char*>(op.weight);
-      bulk_g2s(dst, w + (int64_t)u * rb, bytes, &S.full[slot]);
-      if (op.rpu == 2) bulk_g2s(dst + bytes, w + ((int64_t)op.n_out + u) * rb, bytes, &S.full[slot]);
     }
   }
   // copies still in flight (only after an abort) must land before the CTA's memory goes away
@@ -372,53 +454,112 @@ Q35_DEV void gemv_epilogue(const PkOp& op, int unit, float y0, float y1, float& 
 }
 
 // Returns false on abort. `st` is the ring stage counter shared (by construction) with the producer.
+// Warp group g (4 warps) takes tiles g, g + 4, ...; each warp of the group covers a quarter of
+// every stage's k range: ldmatrix reads 8 weight rows x 32 k and two m16n8k16 MMAs multiply them
+// with the input vector broadcast into every row of A, so column n of D is the partial dot
+// product of tile row n (four accumulator chains). Each warp releases the stage itself; the
+// group meets at its own named barrier, and its first warp adds the four partials in a fixed
+// order and applies the epilogue from lanes 0-3.
 Q35_DEV bool gemv_op(const PkParams& p, const PkOp& op, PkShared& S, const unsigned char* ring, uint32_t& st,
                      float& best_v, int& best_i) {
   build_input(p, op, S);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int wpr = op.k >> 8;  // 512-byte chunks per row
-  int u0, u1;
-  unit_range(op.n_out, u0, u1);
-  const int su = units_per_stage(op);
-  const uint4* xs = reinterpret_cast<const uint4*>(S.u.xs);
-  for (int u = u0; u < u1; u += su, ++st) {
-    const int slot = st % kPkStages;
-    const int n = min(su, u1 - u);
-    bool fail = false;
-    if (!mbar_wait(&S.full[slot], (st / kPkStages) & 1)) {
-      atomicCAS(&q35_pk_error_word, 0, 3);
-      fail = true;
-    }
-    if (cbar_any(fail)) {
-      if (threadIdx.x == 0) *(volatile int*)&S.abort = 1;
-      return false;
-    }
-    const uint4* stage = reinterpret_cast<const uint4*>(ring + (size_t)slot * kPkStageBytes);
-    float* slots = S.slots[st & 1];
-    const int nch = n * op.rpu * wpr;
-    const int c0 = warp * nch / kPkCWarps, c1 = (warp + 1) * nch / kPkCWarps;
-    int wc = c0 % wpr;
-    float acc = 0.f;
-    for (int c = c0; c < c1; ++c) {
-      acc = dot_bf16x8(stage[c * 32 + lane], xs[wc * 32 + lane], acc);
-      float park = 0.f;
-      if (wc == wpr - 1 || c == c1 - 1) {
-        park = warp_sum(acc);
-        acc = 0.f;
+  const int group = warp / kPkGroupWarps, wig = warp % kPkGroupWarps;
+  constexpr int kq = kPkKChunk / kPkGroupWarps;  // k values per warp per stage
+  const TilePlan tp = tile_plan(op);
+  const uint32_t* x32 = reinterpret_cast<const uint32_t*>(S.u.xs);
+  const int c2 = lane & 3;
+  bool fail = false;
+  int par = 0;
+  for (int t = group; t < tp.ntiles; t += kPkGroups, par ^= 1) {
+    // ldmatrix row of this lane: rows past the CTA's units read row 0 (their columns are dropped)
+    const int lr = lane & 7;
+    const int my_row = tile_row(op, tp, t, lr) >= 0 ? lr : 0;
+    if (op.epi == EPI_CONV && wig == 0 && lane == 0) {  // the epilogue's conv lines, ahead of the MMAs
+      const int unit0 = tp.u0 + t * kPkTileRows;
+      if (unit0 < op.conv_ch) {
+        asm volatile("prefetch.global.L1 [%0];" ::"l"(op.conv_state + (int64_t)unit0 * 4));
+        asm volatile("prefetch.global.L1 [%0];" ::"l"(op.conv_w + (int64_t)unit0 * 4));
       }
-      if (lane == 0) slots[c] = park;
-      if (++wc == wpr) wc = 0;
     }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&S.empty[slot]);
-    cbar();
-    for (int t = threadIdx.x; t < n; t += kPkCThreads) {
+    float acc[4][4] = {};
+    for (int j = 0; j < tp.spt && !fail; ++j) {
+      const uint32_t sj = st + (uint32_t)(t * tp.spt + j);
+      const int slot = sj % kPkStages;
+      if (!wait_issued(&S.issued[slot], sj) || !mbar_wait(&S.full[slot], (sj / kPkStages) & 1)) {
+        atomicCAS(&q35_pk_error_word, 0, 3);
+        fail = true;
+        break;
+      }
+      const uint32_t a_base = smem_u32(ring + (size_t)slot * kPkStageStride) + my_row * kPkRowStride +
+                              (lane >> 3) * 16 + wig * kq * 2;
+      const uint32_t* xj = x32 + (j * kPkKChunk + wig * kq) / 2;
+      // software-pipelined by hand (the asm statements keep their order): four ldmatrix loads
+      // in flight, then the eight MMAs that use them
+      for (int k0 = 0; k0 < kq; k0 += 128) {
+        uint32_t b[4][4];
+#pragma unroll
+        for (int h = 0; h < 4; ++h)
+          asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                       : "=r"(b[h][0]), "=r"(b[h][1]), "=r"(b[h][2]), "=r"(b[h][3])
+                       : "r"(a_base + (k0 + 32 * h) * 2));
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          const int kk = (k0 + 32 * h) >> 1;
+          const uint32_t x0 = xj[kk + c2], x1 = xj[kk + 4 + c2], x2 = xj[kk + 8 + c2], x3 = xj[kk + 12 + c2];
+          float* da = acc[2 * (h & 1)];
+          float* db = acc[2 * (h & 1) + 1];
+          asm volatile(
+              "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%4,%5,%5}, {%6,%7}, "
+              "{%0,%1,%2,%3};"
+              : "+f"(da[0]), "+f"(da[1]), "+f"(da[2]), "+f"(da[3])
+              : "r"(x0), "r"(x1), "r"(b[h][0]), "r"(b[h][1]));
+          asm volatile(
+              "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%4,%5,%5}, {%6,%7}, "
+              "{%0,%1,%2,%3};"
+              : "+f"(db[0]), "+f"(db[1]), "+f"(db[2]), "+f"(db[3])
+              : "r"(x2), "r"(x3), "r"(b[h][2]), "r"(b[h][3]));
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&S.empty[slot]);
+    }
+    // lanes 0-3 hold D row 0: tile rows 2 * lane and 2 * lane + 1
+    float* gp = S.gpart[group][par][wig];
+    if (lane < 4) {
+      gp[2 * lane] = (acc[0][0] + acc[1][0]) + (acc[2][0] + acc[3][0]);
+      gp[2 * lane + 1] = (acc[0][1] + acc[1][1]) + (acc[2][1] + acc[3][1]);
+    }
+    if (gbar_any(group, fail)) {
+      fail = true;
+      break;
+    }
+    if (wig == 0) {
       float y0 = 0.f, y1 = 0.f;
-      for (int c = 0; c < wpr; ++c) y0 += slots[t * wpr + c];
-      if (op.rpu == 2)
-        for (int c = 0; c < wpr; ++c) y1 += slots[(n + t) * wpr + c];
-      gemv_epilogue(op, u + t, y0, y1, best_v, best_i);
+      if (lane < 4)
+#pragma unroll
+        for (int w = 0; w < kPkGroupWarps; ++w) {
+          y0 += S.gpart[group][par][w][2 * lane];
+          y1 += S.gpart[group][par][w][2 * lane + 1];
+        }
+      const float up0 = __shfl_down_sync(0xffffffffu, y0, 2), up1 = __shfl_down_sync(0xffffffffu, y1, 2);
+      if (op.rpu == 1) {
+        if (lane < 4) {
+          const int unit0 = tp.u0 + t * kPkTileRows + 2 * lane;
+          if (unit0 < tp.u1) gemv_epilogue(op, unit0, y0, 0.f, best_v, best_i);
+          if (unit0 + 1 < tp.u1) gemv_epilogue(op, unit0 + 1, y1, 0.f, best_v, best_i);
+        }
+      } else if (lane < 2) {  // gate rows 2l, 2l+1 here; up rows 2l+4, 2l+5 from lane l + 2
+        const int unit0 = tp.u0 + t * tp.upt + 2 * lane;
+        if (unit0 < tp.u1) gemv_epilogue(op, unit0, y0, up0, best_v, best_i);
+        if (unit0 + 1 < tp.u1) gemv_epilogue(op, unit0 + 1, y1, up1, best_v, best_i);
+      }
     }
+  }
+  st += (uint32_t)(tp.ntiles * tp.spt);
+  if (cbar_any(fail)) {
+    if (threadIdx.x == 0) *(volatile int*)&S.abort = 1;
+    return false;
   }
   return true;
 }
@@ -505,6 +646,21 @@ Q35_DEV void delta_op(const PkParams& p, const PkOp& op, PkShared& S, float s[4]
 }
 
 // ------------------------------------------------------------------------------ attention
+// Cached K/V rows of this item do not depend on the step: pull them into L2 before the barrier.
+Q35_DEV void attn_prefetch(const PkParams& p, const PkOp& op) {
+  const int g = blockIdx.x / kPkSplits, s = blockIdx.x % kPkSplits;
+  if (g >= p.kv_heads) return;
+  const int64_t len = *p.cache_len;
+  const int n = (int)(len < 0 ? 0 : (len > p.max_len ? p.max_len : len));
+  const int chunk = (n + kPkSplits - 1) / kPkSplits;
+  const int r0 = min(s * chunk, n), r1 = min(r0 + chunk, n);
+  const int lines = (r1 - r0) * 4;  // 128-byte lines per row of 256 bf16
+  for (int i = threadIdx.x; i < 2 * lines; i += kPkCThreads) {
+    const bf16* base = (i < lines ? op.k_cache : op.v_cache) + ((int64_t)g * p.max_len + r0) * 256;
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(base + (i % lines) * 64));
+  }
+}
+
 // Item = (KV head g, split s of the cached rows); the last split also attends the current token.
 Q35_DEV void attn_part_op(const PkParams& p, const PkOp& op, PkShared& S) {
   constexpr int G = 4, D = 256;
@@ -669,13 +825,14 @@ Q35_DEV void attn_combine_op(const PkParams& p, const PkOp& op, PkShared& S) {
 __global__ void __launch_bounds__(kPkThreads, 1) pk_decode_kernel(const __grid_constant__ PkParams p) {
   extern __shared__ __align__(128) unsigned char pk_smem[];
   unsigned char* ring = pk_smem;
-  PkShared& S = *reinterpret_cast<PkShared*>(pk_smem + (size_t)kPkStages * kPkStageBytes);
+  PkShared& S = *reinterpret_cast<PkShared*>(pk_smem + (size_t)kPkStages * kPkStageStride);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     for (int i = 0; i < kPkStages; ++i) {
       asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(&S.full[i])) : "memory");
-      asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(&S.empty[i])), "n"(kPkCWarps)
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(&S.empty[i])), "n"(kPkGroupWarps)
                    : "memory");
+      S.issued[i] = 0xFFFFFFFFu;
     }
     S.abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -686,6 +843,7 @@ __global__ void __launch_bounds__(kPkThreads, 1) pk_decode_kernel(const __grid_c
     return;
   }
 
+  trace_mark(p, p.n_ops, 0);
   uint32_t st = 0;
   unsigned target = 0;
   float best_v = -FLT_MAX;
@@ -695,6 +853,10 @@ __global__ void __launch_bounds__(kPkThreads, 1) pk_decode_kernel(const __grid_c
   for (int i = 0; i < p.n_ops && ok; ++i) {
     const PkOp& op = p.ops[i];
     if (op.kind == OP_DELTA) delta_prefetch(p, op, dstate);  // independent of the ops before it
+    if (op.kind == OP_ATTN_PART) attn_prefetch(p, op);
+    if (op.kind == OP_GEMV && op.norm_w && op.pro != PRO_PLAIN)  // constants: warm L2 before the barrier
+      for (int q = threadIdx.x; q < (op.pro == PRO_GATED ? 2 : op.k / 64); q += kPkCThreads)
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(op.norm_w + 64 * q));
     if (i > 0) {
       target += gridDim.x;
       ok = grid_barrier(p, target, S);
@@ -736,6 +898,7 @@ __global__ void __launch_bounds__(kPkThreads, 1) pk_decode_kernel(const __grid_c
   }
   target += gridDim.x;
   if (!grid_barrier(p, target, S)) return;
+  trace_mark(p, p.n_ops, 1);
   if (blockIdx.x == 0 && threadIdx.x == 0) {
     const unsigned long long key = atomicExch(p.top1, 0ull);
     const int64_t tok = (key == 0ull) ? 0 : (int64_t)(0xFFFFFFFFu - (uint32_t)(key & 0xFFFFFFFFull));
@@ -880,8 +1043,8 @@ int q35_pk_create(const q35_decoder_desc& d, const q35_layer_desc* layers, bf16*
     if (layers[i].kind != 0) aligned = aligned && Q35_ALIGNED(layers[i].k_cache, 16) && Q35_ALIGNED(layers[i].v_cache, 16);
   if (!aligned) return q35_fail(Q35_ENOTSUP, "persistent decode: a buffer is not 16-byte aligned");
   for (const PkOp& op : ops)
-    if (op.kind == OP_GEMV && (!op.weight || op.k % 256 != 0 || op.k > kPkMaxK || op.n_out < kNumSMs ||
-                               (int64_t)op.k * 2 * op.rpu > kPkStageBytes || !Q35_ALIGNED(op.weight, 16)))
+    if (op.kind == OP_GEMV && (!op.weight || op.k % kPkKChunk != 0 || op.k > kPkMaxK || op.n_out < kNumSMs ||
+                               !Q35_ALIGNED(op.weight, 16)))
       return q35_fail(Q35_ENOTSUP, "persistent decode: GEMV shape n=%d k=%d unsupported", op.n_out, op.k);
   if (cudaMemcpy(dev_ops, ops.data(), ops.size() * sizeof(PkOp), cudaMemcpyHostToDevice) != cudaSuccess ||
       cudaMemset(P.top1, 0, 16) != cudaSuccess)
@@ -939,6 +1102,15 @@ int q35_pk_launch(const q35_pk_plan* plan, cudaStream_t s) {
   if (e != cudaSuccess) return q35_fail(Q35_ECUDA, "persistent decode launch: %s", cudaGetErrorString(e));
   return Q35_OK;
 }
+
+int q35_pk_set_trace(q35_pk_plan* plan, int64_t* trace, int64_t entries) {
+  const int64_t need = ((int64_t)plan->params.n_ops + 1) * kNumSMs * 2;
+  Q35_REQUIRE(!trace || entries >= need, "trace buffer needs %lld entries", (long long)need);
+  plan->params.trace = trace;
+  return Q35_OK;
+}
+
+int q35_pk_ops(const q35_pk_plan* plan) { return plan->params.n_ops; }
 
 extern "C" int q35_decoder_persistent_error(void) {
   int v = 0, zero = 0;

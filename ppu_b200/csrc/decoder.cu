@@ -56,6 +56,8 @@ int q35_pk_create(const q35_decoder_desc& d, const q35_layer_desc* layers, bf16*
                   void* ws, q35_pk_plan** out);
 void q35_pk_destroy(q35_pk_plan* plan);
 int q35_pk_launch(const q35_pk_plan* plan, cudaStream_t s);
+int q35_pk_set_trace(q35_pk_plan* plan, int64_t* trace, int64_t entries);
+int q35_pk_ops(const q35_pk_plan* plan);
 
 namespace {
 
@@ -198,6 +200,14 @@ extern "C" int q35_decoder_decode_step_persistent(q35_decoder* dec, void* stream
 }
 
 extern "C" int q35_decoder_has_persistent(const q35_decoder* dec) { return dec && dec->pk ? 1 : 0; }
+
+extern "C" int q35_decoder_set_trace(q35_decoder* dec, int64_t* trace, int64_t entries) {
+  Q35_REQUIRE(dec, "set_trace: null decoder");
+  if (!dec->pk) return q35_fail(Q35_ENOTSUP, "persistent decode unavailable: %s", dec->pk_why.c_str());
+  return q35_pk_set_trace(dec->pk, trace, entries);
+}
+
+extern "C" int q35_decoder_trace_ops(const q35_decoder* dec) { return dec && dec->pk ? q35_pk_ops(dec->pk) : 0; }
 
 extern "C" int q35_decoder_kernels_per_step(const q35_decoder* dec) { return dec ? 5 * dec->d.n_layers + 1 : 0; }
 

@@ -210,6 +210,46 @@ class Qwen35Engine:
         self._graphs[steps] = g
         return g
 
+    def _persistent_op_labels(self) -> list[str]:
+        labels = []
+        for kind in self.dims.layer_types:
+            if kind == "linear_attention":
+                labels += ["in_proj+conv", "delta_step", "out_proj(gated norm)", "gate_up", "down"]
+            else:
+                labels += ["qgkv_proj", "attn_partials", "attn_combine", "o_proj", "gate_up", "down"]
+        return labels + ["lm_head"]
+
+    def trace_step(self) -> dict:
+        """Runs one persistent decode step with barrier tracing (``q35_decoder_set_trace``) and
+        returns, per op, the CTAs' mean / max work time and mean wait at the following grid
+        barrier (microseconds), plus the step's wall time on the device. Advances the decoder by
+        one token like ``decode_step``."""
+        if not self.has_persistent:
+            raise ValueError("persistent decode step unavailable for this model")
+        n_sm = 148
+        n_ops = L.load().q35_decoder_trace_ops(self.handle)
+        buf = torch.zeros((n_ops + 1) * n_sm * 2, device=self.device, dtype=torch.int64)
+        L.check(L.load().q35_decoder_set_trace(self.handle, buf.data_ptr(), buf.numel()), "q35_decoder_set_trace")
+        persistent, self.persistent = self.persistent, True
+        try:
+            self.decode_step()
+            torch.cuda.synchronize(self.device)
+        finally:
+            self.persistent = persistent
+            L.load().q35_decoder_set_trace(self.handle, None, 0)
+        t = buf.view(n_ops + 1, n_sm, 2).double().cpu() / 1000.0
+        start, end = t[n_ops, :, 0], t[n_ops, :, 1]
+        labels = self._persistent_op_labels()
+        ops = []
+        prev = start
+        for j in range(n_ops):
+            work = t[j, :, 0] - prev
+            wait = t[j, :, 1] - t[j, :, 0]
+            ops.append({"op": labels[j] if j < len(labels) else f"op{j}", "work_mean_us": float(work.mean()),
+                        "work_max_us": float(work.max()), "wait_mean_us": float(wait.mean())})
+            prev = t[j, :, 1]
+        return {"step_us": float(end.max() - start.min()), "ops": ops}
+
     # ------------------------------------------------------------------ state
     def snapshot(self) -> dict:
         """Copies of every piece of mutable decoding state (for restoring after warm-up)."""

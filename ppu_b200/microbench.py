@@ -147,6 +147,37 @@ def run(kernels: list[str], reps: int, layers: int = 24, a8w8: bool = False):
             report("delta_chunked_1024", t, flops=16 * 16 * 11_700_000)
             t = _time(lambda i: K.delta_recurrent_fused(qkv, packed, z16, z16, st), max(1, reps // 4))
             report("delta_sequential_1024", t)
+        elif name in ("persistent_trace", "persistent_small"):
+            from .config import Qwen35Dims
+            from .engine import Qwen35Engine
+            from .synthetic import make_prompt, make_weights
+            # persistent_small: 4 layers, vocab 8192 (same kernel and shapes, ~140 MB): the ncu case
+            dims = Qwen35Dims() if name == "persistent_trace" else Qwen35Dims(layers=4, vocab=8192)
+            eng = Qwen35Engine(make_weights(dims, seed=0, device=dev), dims, max_len=1152, max_prefill=1024,
+                               persistent=True)
+            eng.prefill(make_prompt(dims, 1024, seed=1)[0].to(dev))
+            for _ in range(3):
+                eng.decode_step()
+            agg: dict[str, list[float]] = {}
+            steps = max(1, reps)
+            total = 0.0
+            for _ in range(steps):
+                tr = eng.trace_step()
+                total += tr["step_us"]
+                for o in tr["ops"]:
+                    a = agg.setdefault(o["op"], [0, 0.0, 0.0, 0.0])
+                    a[0] += 1
+                    a[1] += o["work_mean_us"]
+                    a[2] += o["work_max_us"]
+                    a[3] += o["wait_mean_us"]
+            for op, (n, wm, wx, bw) in agg.items():
+                rec = {"kernel": "persistent_step", "op": op, "count_per_step": n // steps,
+                       "work_mean_us_per_step": round(wm / steps, 2), "work_max_us_per_step": round(wx / steps, 2),
+                       "barrier_wait_us_per_step": round(bw / steps, 2)}
+                out.append(rec)
+                print(json.dumps(rec), flush=True)
+            print(json.dumps({"kernel": "persistent_step", "step_us": round(total / steps, 2)}), flush=True)
+            del eng
         else:
             raise ValueError(f"unknown kernel {name}")
     return out
