@@ -48,6 +48,7 @@ def parse():
     ap.add_argument("--no-pdl", action="store_true")
     ap.add_argument("--gemv", default="registers", choices=["registers", "bulk"],
                     help="decode GEMV weight streaming: shared-memory bulk copies or register loads")
+    ap.add_argument("--gemv-ctas", type=int, default=0, help="decode GEMV grid cap in CTAs per SM (0: all that fit)")
     ap.add_argument("--prefill-delta", default="chunked", choices=["chunked", "sequential"])
     ap.add_argument("--decode", default="kernels", choices=["kernels", "persistent"],
                     help="decode step: one persistent cooperative kernel (bf16) or the per-op kernels")
@@ -202,6 +203,7 @@ def main():
     dims = Qwen35Dims()
     P, T = args.prompt_len, args.new_tokens
     L.call("q35_set_gemv_variant", L.Q35_GEMV_BULK if args.gemv == "bulk" else L.Q35_GEMV_REGISTERS)
+    L.call("q35_set_gemv_ctas_per_sm", args.gemv_ctas)
     weights = make_weights(dims, seed=0, device=dev)
     eng = Qwen35Engine(weights, dims, a8w8=args.a8w8, max_len=cache_bucket(P, T), max_prefill=P, device=dev,
                        use_pdl=not args.no_pdl, prefill_chunked=args.prefill_delta == "chunked",
@@ -322,6 +324,7 @@ def main():
             "global_batch": world, "seq_len": P, "parallelism": f"request-parallel replicas x{world}",
             "a8w8": args.a8w8, "pdl": not args.no_pdl, "cuda_graph": "1 decode step per replay",
             "decode_step": "persistent" if eng.persistent else "per-op kernels", "gemv": args.gemv,
+            "gemv_ctas_per_sm": args.gemv_ctas or "all that fit",
             "prefill_delta": args.prefill_delta, "prefill_gemm": "tcgen05",
             "l2": "weights 3.8 GB per step >> 126 MB L2 (no flush needed)",
         },

@@ -114,6 +114,10 @@ int q35_gemv(const q35_gemv_desc* d, void* stream);
  * programmatic-dependent-launch wait; REGISTERS streams 16-byte loads into registers. */
 enum { Q35_GEMV_BULK = 0, Q35_GEMV_REGISTERS = 1 };
 int q35_set_gemv_variant(int variant);
+/* Grid cap of the REGISTERS decode GEMVs in CTAs per SM (process-wide; 0 = as many as fit). A cap
+ * leaves registers for the next kernel's CTAs, which then start and issue their weight loads
+ * while this kernel drains (programmatic dependent launch). */
+int q35_set_gemv_ctas_per_sm(int ctas);
 /* Error word of the bulk GEMV (non-zero when a bounded copy wait gave up); reading clears it. */
 int q35_gemv_error(void);
 

@@ -13,6 +13,8 @@
 // current token attended from registers, so nothing waits on the cache write.
 #include <cfloat>
 
+#include <cooperative_groups.h>
+
 #include "common.cuh"
 
 using namespace q35;
@@ -290,6 +292,210 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(DecodeParams p) {
   if (threadIdx.x == 0) atomicExch(&p.tickets[b * Hkv + g], 0u);
 }
 
+// ---------------------------------------------------------------------------------------------
+// Cluster variant of the fused decode mixer (decoder path, caches up to kClusterCTAs * kClRows):
+// one cluster of kClusterCTAs CTAs per (batch, KV head). Each CTA owns a contiguous slice of the
+// cached rows and copies its K/V rows into shared memory with cp.async BEFORE the programmatic-
+// dependent-launch wait: those rows and the row count were written by earlier steps (the kernel
+// before this one is the QGKV projection), so the HBM latency overlaps the projection. After the
+// wait: Q/K RMSNorm + RoPE of the current token, scores (warp per row), per-head softmax over the
+// slice, un-normalised P.V; the last CTA also attends the current token from registers. The
+// partials meet over distributed shared memory: CTA r merges dims [r * D / C, (r + 1) * D / C)
+// of every head from all peers and writes the gated BF16 output. No global scratch, no second
+// pass.
+constexpr int kClusterCTAs = 8;
+constexpr int kClRows = 160;
+constexpr size_t kClSmemBytes = 2ull * kClRows * kD * sizeof(bf16);
+
+Q35_DEV void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
+               : "memory");
+}
+
+template <int G>
+__global__ void __launch_bounds__(kThreads, 1) attn_decode_cluster_kernel(DecodeParams p) {
+  extern __shared__ __align__(16) unsigned char cl_smem[];
+  bf16* Ks = reinterpret_cast<bf16*>(cl_smem);
+  bf16* Vs = Ks + kClRows * kD;
+  __shared__ __align__(16) float qf[G][kD];
+  __shared__ __align__(16) float nrm[G + 1][kD];
+  __shared__ __align__(16) float kn[kD];
+  __shared__ __align__(16) float vn[kD];
+  __shared__ float sc[kClRows + 1][G];
+  __shared__ float red[kWarps][G + 1];
+  __shared__ float inbox[kClusterCTAs][G][kD / kClusterCTAs];  // peers' partial outputs for my dims
+  __shared__ float inml[kClusterCTAs][G][2];                   // peers' (max, sum) per head
+  namespace cg = cooperative_groups;
+  cg::cluster_group cluster = cg::this_cluster();
+  const int rank = (int)cluster.block_rank(), C = (int)cluster.num_blocks();
+  const int g = blockIdx.y, b = blockIdx.z;
+  const int Hq = p.Hq, Hkv = p.Hkv;
+  const int t = threadIdx.x, warp = t >> 5, lane = t & 31, d = t;
+  const int64_t kv_base = ((int64_t)b * Hkv + g) * p.max_len * kD;
+
+  // ---- rows of this CTA, copied before the wait (written by earlier steps)
+  const int64_t len = *p.len;
+  const int n = (int)(len < 0 ? 0 : (len > p.max_len ? p.max_len : len));
+  const int chunk = (n + C - 1) / C;
+  const int r0 = min(rank * chunk, n), r1 = min(r0 + chunk, n), nr = r1 - r0;
+  for (int i = t; i < nr * (kD / 8); i += kThreads) {
+    const int row = i / (kD / 8), c = i % (kD / 8);
+    cp_async16(Ks + row * kD + c * 8, p.cache_k + kv_base + (int64_t)(r0 + row) * kD + c * 8);
+    cp_async16(Vs + row * kD + c * 8, p.cache_v + kv_base + (int64_t)(r0 + row) * kD + c * 8);
+  }
+  asm volatile("cp.async.commit_group;" ::: "memory");
+  // peers write into this CTA's shared memory later: all CTAs of the cluster must have started
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+  pdl_wait();
+  pdl_launch_dependents();
+
+  // ---- Q/K RMSNorm(1+w) and partial RoPE of the current token; its K/V row goes to the cache
+  const int stride = 2 * Hq * kD + 2 * Hkv * kD;
+  const bf16* row = p.packed + (int64_t)b * stride;
+  float x[G + 1];
+#pragma unroll
+  for (int hh = 0; hh < G; ++hh) x[hh] = bf2f(row[(g * G + hh) * 2 * kD + d]);
+  x[G] = bf2f(row[2 * Hq * kD + g * kD + d]);
+  const float v_raw = bf2f(row[2 * Hq * kD + Hkv * kD + g * kD + d]);
+#pragma unroll
+  for (int i = 0; i <= G; ++i) {
+    const float ws = warp_sum(x[i] * x[i]);
+    if (lane == 0) red[warp][i] = ws;
+  }
+  float c = 1.f, sn = 0.f;
+  if (d < p.rot) rope_cs(d, p.rot / 2, (float)(*p.rope_pos), p.inv_freq, c, sn);
+  const float wq = bf2f(p.qw[d]), wk = bf2f(p.kw[d]);
+  __syncthreads();
+#pragma unroll
+  for (int i = 0; i <= G; ++i) {
+    float tot = 0.f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) tot += red[w][i];
+    const float r = rsqrt_ieee(tot / (float)kD + p.eps);
+    nrm[i][d] = rbf(x[i] * r * (1.0f + (i < G ? wq : wk)));
+  }
+  __syncthreads();
+#pragma unroll
+  for (int i = 0; i < G; ++i) qf[i][d] = rope_apply(nrm[i], d, p.rot, c, sn) * p.scale;
+  const float kr = rope_apply(nrm[G], d, p.rot, c, sn);
+  kn[d] = kr;
+  vn[d] = v_raw;
+  if (rank == 0 && len >= 0 && len < p.max_len) {
+    p.cache_k[kv_base + len * kD + d] = f2bf(kr);
+    p.cache_v[kv_base + len * kD + d] = f2bf(v_raw);
+  }
+  asm volatile("cp.async.wait_all;" ::: "memory");
+  __syncthreads();
+
+  // ---- scores: warp per row (two rows per step), lanes hold 8 dims; the last CTA adds the
+  //      current token as row nr
+  const bool last = rank == C - 1;
+  const int rows = nr + (last ? 1 : 0);
+  float q8[G][8];
+#pragma unroll
+  for (int hh = 0; hh < G; ++hh)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) q8[hh][j] = qf[hh][lane * 8 + j];
+  auto key_row = [&](int j, float kf[8]) {
+    if (j < nr) {
+      unpack_bf16x8(*reinterpret_cast<const uint4*>(Ks + j * kD + lane * 8), kf);
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) kf[e] = kn[lane * 8 + e];
+    }
+  };
+  for (int j = warp; j < rows; j += 2 * kWarps) {
+    const int j2 = j + kWarps;
+    const bool two = j2 < rows;
+    float ka[8], kb[8];
+    key_row(j, ka);
+    key_row(two ? j2 : j, kb);
+    float a[G], bsum[G];
+#pragma unroll
+    for (int hh = 0; hh < G; ++hh) {
+      a[hh] = 0.f;
+      bsum[hh] = 0.f;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        a[hh] = fmaf(q8[hh][e], ka[e], a[hh]);
+        bsum[hh] = fmaf(q8[hh][e], kb[e], bsum[hh]);
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+      for (int hh = 0; hh < G; ++hh) {
+        a[hh] += __shfl_xor_sync(0xffffffffu, a[hh], o);
+        bsum[hh] += __shfl_xor_sync(0xffffffffu, bsum[hh], o);
+      }
+    if (lane == 0) {
+#pragma unroll
+      for (int hh = 0; hh < G; ++hh) {
+        sc[j][hh] = a[hh];
+        if (two) sc[j2][hh] = bsum[hh];
+      }
+    }
+  }
+  __syncthreads();
+  asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
+  // ---- per-head max and weights over this CTA's rows; (max, sum) pushed to every peer
+  if (warp < G) {
+    float m = -FLT_MAX;
+    for (int j = lane; j < rows; j += 32) m = fmaxf(m, sc[j][warp]);
+    m = warp_max(m);
+    float l = 0.f;
+    for (int j = lane; j < rows; j += 32) {
+      const float e = expf(sc[j][warp] - m);
+      sc[j][warp] = e;
+      l += e;
+    }
+    l = warp_sum(l);
+    if (lane < C) {
+      float* dst = cluster.map_shared_rank(&inml[rank][warp][0], lane);
+      dst[0] = rows > 0 ? m : -FLT_MAX;
+      dst[1] = rows > 0 ? l : 0.f;
+    }
+  }
+  __syncthreads();
+  // ---- un-normalised P.V (thread = dim, all heads), pushed to the peer that owns the dim
+  {
+    float a[G];
+#pragma unroll
+    for (int hh = 0; hh < G; ++hh) a[hh] = 0.f;
+    for (int j = 0; j < rows; ++j) {
+      const float v = (j < nr) ? bf2f(Vs[j * kD + d]) : vn[d];
+#pragma unroll
+      for (int hh = 0; hh < G; ++hh) a[hh] = fmaf(sc[j][hh], v, a[hh]);
+    }
+    const int dper = kD / kClusterCTAs;
+    const int owner = d / dper;
+#pragma unroll
+    for (int hh = 0; hh < G; ++hh) *cluster.map_shared_rank(&inbox[rank][hh][d % dper], owner) = a[hh];
+  }
+  cluster.sync();  // every push has landed; from here on only this CTA's own shared memory is read
+  // ---- merge the partials of dims [rank * D / C, (rank + 1) * D / C) of every head
+  const int dper = kD / kClusterCTAs;
+  for (int i = t; i < G * dper; i += kThreads) {
+    const int hh = i / dper, di = i % dper, dd = rank * dper + di;
+    float M = -FLT_MAX;
+#pragma unroll
+    for (int r = 0; r < kClusterCTAs; ++r)
+      if (inml[r][hh][1] > 0.f) M = fmaxf(M, inml[r][hh][0]);
+    float L = 0.f, A = 0.f;
+#pragma unroll
+    for (int r = 0; r < kClusterCTAs; ++r) {
+      const float lr = inml[r][hh][1];
+      const float e = lr > 0.f ? expf(inml[r][hh][0] - M) : 0.f;
+      L += lr * e;
+      A += inbox[r][hh][di] * e;
+    }
+    const float o = L > 0.f ? rbf(A / L) : 0.f;
+    const int h = g * G + hh;
+    const float gate = bf2f(row[h * 2 * kD + kD + dd]);
+    p.out[((int64_t)b * Hq + h) * kD + dd] = f2bf(o * rbf(sigmoid_f(gate)));
+  }
+}
+
 int choose_splits(int64_t batch, int64_t kv_heads, int64_t cache_len) {
   int64_t s = (cache_len + kRowsPerSplit - 1) / kRowsPerSplit;  // >= 64 rows per CTA
   const int64_t fill = (2 * kNumSMs + batch * kv_heads - 1) / (batch * kv_heads);
@@ -313,8 +519,35 @@ WsLayout ws_layout(int64_t batch, int64_t heads, int64_t kv_heads, int64_t cache
   return w;
 }
 
+template <int G>
+int launch_cluster(const DecodeParams& p, int64_t batch, cudaStream_t st, bool pdl) {
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(attn_decode_cluster_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kClSmemBytes);
+    attr = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(kClusterCTAs, p.Hkv, (unsigned)batch);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = kClSmemBytes;
+  cfg.stream = st;
+  cudaLaunchAttribute attrs[2];
+  attrs[0].id = cudaLaunchAttributeClusterDimension;
+  attrs[0].val.clusterDim.x = kClusterCTAs;
+  attrs[0].val.clusterDim.y = 1;
+  attrs[0].val.clusterDim.z = 1;
+  attrs[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attrs[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attrs;
+  cfg.numAttrs = pdl ? 2 : 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, attn_decode_cluster_kernel<G>, p);
+  if (e != cudaSuccess) return q35_fail(Q35_ECUDA, "decode attention (cluster) launch: %s", cudaGetErrorString(e));
+  return Q35_OK;
+}
+
 template <bool FUSED>
 int launch_decode(DecodeParams p, int64_t batch, int G, void* ws, cudaStream_t st, bool pdl) {
+  if (FUSED && G == 4 && p.max_len <= kClusterCTAs * kClRows) return launch_cluster<4>(p, batch, st, pdl);
   const WsLayout w = ws_layout(batch, p.Hq, p.Hkv, p.max_len);
   if ((size_t)batch * p.Hkv * sizeof(unsigned) > w.ml) return q35_fail(Q35_ENOTSUP, "decode attention: batch too large");
   char* base = static_cast<char*>(ws);

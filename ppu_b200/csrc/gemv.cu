@@ -447,11 +447,16 @@ int resident_ctas(KernelT kernel, size_t dyn_smem) {
   return per_sm * kNumSMs;
 }
 
+int g_gemv_ctas_per_sm = 0;  // 0: as many as fit; else cap (room for the next kernel's CTAs under PDL)
+
 template <int K, int PRO, int EPI, bool INT8>
 int launch_fast(const GemvParams& p, cudaStream_t s, bool pdl) {
   using Sh = FastShape<K, INT8, (EPI == Q35_EPI_SWIGLU) ? 2 : 1>;
-  static int max_ctas = 0;
-  if (!max_ctas) max_ctas = resident_ctas(gemv_fast_kernel<K, PRO, EPI, INT8>, 0);
+  static int resident = 0;
+  if (!resident) resident = resident_ctas(gemv_fast_kernel<K, PRO, EPI, INT8>, 0);
+  const int max_ctas = g_gemv_ctas_per_sm > 0 && g_gemv_ctas_per_sm * kNumSMs < resident
+                           ? g_gemv_ctas_per_sm * kNumSMs
+                           : resident;
   const int ngroups = (p.n_out + Sh::U - 1) / Sh::U;
   const int grid = choose_grid(ngroups, max_ctas);
   cudaError_t e = q35_launch(gemv_fast_kernel<K, PRO, EPI, INT8>, dim3(grid), dim3(kThreads), 0, s, pdl, p);
@@ -579,6 +584,12 @@ int q35_lm_head_launch(const void* hidden, const void* norm_weight, const void* 
 extern "C" int q35_set_gemv_variant(int variant) {
   Q35_REQUIRE(variant == Q35_GEMV_BULK || variant == Q35_GEMV_REGISTERS, "gemv variant %d unknown", variant);
   g_gemv_variant = variant;
+  return Q35_OK;
+}
+
+extern "C" int q35_set_gemv_ctas_per_sm(int ctas) {
+  Q35_REQUIRE(ctas >= 0 && ctas <= 32, "gemv CTAs per SM %d out of range", ctas);
+  g_gemv_ctas_per_sm = ctas;
   return Q35_OK;
 }
 

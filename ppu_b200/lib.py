@@ -97,6 +97,7 @@ _SIGS = {
     "q35_decoder_kernels_per_step": (INT, [P]),
     "q35_decoder_decode_step_persistent": (INT, [P, P]),
     "q35_decoder_has_persistent": (INT, [P]),
+    "q35_set_gemv_ctas_per_sm": (INT, [C.c_int]),
     "q35_decoder_set_trace": (INT, [P, P, I64]),
     "q35_decoder_trace_ops": (INT, [P]),
     "q35_decoder_persistent_error": (INT, []),

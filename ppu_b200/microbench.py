@@ -115,8 +115,18 @@ def run(kernels: list[str], reps: int, layers: int = 24, a8w8: bool = False):
             qw = torch.zeros(256, device=dev, dtype=torch.bfloat16)
             inv = torch.ones(32, device=dev)
             ln = torch.tensor([n], device=dev, dtype=torch.int64)
-            t = _time(lambda i: K.attn_decode(packed, qw, qw, inv, kc[i % 6], vc[i % 6], ln, ln, q_heads=8,
-                                              kv_heads=2, rotary_dim=64), reps * 6)
+            ws_size = L.load().q35_attn_decode_workspace_size(1, 8, 2, 256, max_len)
+            ws = torch.zeros(ws_size, device=dev, dtype=torch.uint8)
+            o = torch.empty(1, 2048, device=dev, dtype=torch.bfloat16)
+
+            pos0 = torch.zeros(1, device=dev, dtype=torch.int64)
+
+            def attn(i, pos=ln):  # the C entry point with a resident workspace (the wrapper allocates per call)
+                L.call("q35_attn_decode", packed.data_ptr(), qw.data_ptr(), qw.data_ptr(), inv.data_ptr(),
+                       kc[i % 6].data_ptr(), vc[i % 6].data_ptr(), ln.data_ptr(), pos.data_ptr(), o.data_ptr(), 1, 8,
+                       2, 256, 64, max_len, 1e-6, ws.data_ptr(), ws_size, L.stream_of(dev))
+            report("attn_decode_rope_pos0", _time(lambda i: attn(i, pos0), reps * 6), nbytes=2 * 2 * 2 * n * 256)
+            t = _time(attn, reps * 6)
             report(name, t, nbytes=2 * 2 * 2 * n * 256)
         elif name == "delta_decode":
             packed = torch.randn(1, 8224, device=dev, generator=g).to(torch.bfloat16)
