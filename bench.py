@@ -22,7 +22,6 @@ import subprocess
 import sys
 import threading
 import time
-from datetime import timedelta
 from pathlib import Path
 
 import torch
@@ -175,30 +174,19 @@ def main():
     args = parse()
     if args.impl == "reference":
         return run_reference(args)
-    import torch.distributed as dist
-
     from ppu_b200 import kernels as K
+    from ppu_b200 import replicas as R
     from ppu_b200 import lib as L
     from ppu_b200.engine import Qwen35Engine, cache_bucket
 
-    rank = int(os.environ.get("RANK", "0"))
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
+    rank, world, local = R.dist_env()
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    if world > 1:
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
-
-    def barrier():
-        if world > 1:
-            dist.barrier()
+    R.init("nccl", timeout_s=300, device=dev)  # request replicas: no collective on the data path
+    barrier = R.barrier
 
     def max_over_ranks(x: float) -> float:
-        if world == 1:
-            return x
-        t = torch.tensor([x], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t)
+        return R.max_over_ranks(x, dev)
 
     dims = Qwen35Dims()
     P, T = args.prompt_len, args.new_tokens
@@ -218,7 +206,7 @@ def main():
     torch.cuda.empty_cache()
 
     n_req = args.warmup + args.steps
-    prompts = [make_prompt(dims, P, seed=1000 * rank + i)[0].to(dev) for i in range(n_req)]
+    prompts = [make_prompt(dims, P, seed=R.request_seed(rank, i))[0].to(dev) for i in range(n_req)]
     graph = eng.capture(1)
     torch.cuda.synchronize()
 
@@ -249,7 +237,7 @@ def main():
     decode_ms = sum(e[1].elapsed_time(e[2]) for e in evs)
     prefill_ms = sum(e[0].elapsed_time(e[1]) for e in evs)
     total_ms, decode_ms, prefill_ms = (max_over_ranks(x) for x in (total_ms, decode_ms, prefill_ms))
-    value = world * args.steps * T / (decode_ms / 1000.0)
+    value = R.aggregate_rate(args.steps * T, decode_ms / 1000.0, world)
     bytes_tok = dims.weight_bytes_per_token(args.a8w8) + 2 * dims.n_attn * dims.kv_heads * dims.head_dim * 2 * (P + T // 2)
     hbm_peak, tf_peak, peak_kind = peaks()
 
@@ -288,13 +276,13 @@ def main():
     # ---- end to end through the public generate path (host prompt, per-token host reads)
     e2e_tok, e2e_time, e2e_ttft = 0, 0.0, []
     for i in range(2):
-        host_prompt = make_prompt(dims, P, seed=50_000 + 1000 * rank + i)[0]
+        host_prompt = make_prompt(dims, P, seed=50_000 + R.request_seed(rank, i))[0]
         toks, ttft, elapsed = eng.generate(host_prompt, T + 1)
         e2e_tok += len(toks) - 1
         e2e_time += elapsed - ttft
         e2e_ttft.append(ttft)
     e2e_time = max_over_ranks(e2e_time)
-    e2e_value = world * e2e_tok / e2e_time
+    e2e_value = R.aggregate_rate(e2e_tok, e2e_time, world)
 
     cpu = None
     if weights_cpu is not None:
@@ -352,8 +340,8 @@ def main():
         del graph
         eng._graphs.clear()
         torch.cuda.synchronize()
-        dist.barrier()
-        dist.destroy_process_group()
+        R.barrier()
+        R.shutdown()
     return 0
 
 
