@@ -6,7 +6,7 @@
 // ~3 us per launch (launch, first-byte latency, tail) over 121 launches a token. Here the weight
 // stream never stops at op boundaries:
 //  * a producer warp walks the step's GEMV ops and copies this CTA's rows of every weight matrix
-//    (rows [b*n/148, (b+1)*n/148), gate and up rows together for SwiGLU) into a 4-stage x 48 KB
+//    (rows [b*n/148, (b+1)*n/148), gate and up rows together for SwiGLU) into a 6-stage x 32 KB
 //    shared-memory ring with 1-D bulk async copies (cp.async.bulk, no tensor map, no multicast),
 //    each completing on a per-stage mbarrier; it runs ahead across op boundaries, grid barriers and
 //    the mixers, limited only by free ring stages;
@@ -14,12 +14,12 @@
 //    (atomic counter, acquire polling, bounded wait that sets an error word instead of hanging;
 //    the cooperative launch guarantees co-residency). A GEMV op builds its input vector in shared
 //    memory (plain / RMSNorm / embedding gather + RMSNorm / gated RMSNorm of the DeltaNet output),
-//    then consumes its stages on the tensor cores: ldmatrix reads 8 weight rows x 32 k (rows are
-//    copied into 16-byte-padded slots so the reads hit distinct banks) and m16n8k16 MMAs multiply
-//    them with the vector broadcast into every row of A; warps split (8-row tile, k-range) and park
-//    their partial sums, which one thread per unit adds in a fixed order before the epilogue
-//    (store; store + causal-conv update of that channel; residual add in place; SwiGLU; running
-//    greedy top-1);
+//    then consumes its stages (8 weight rows x 2048 k each) with groups of 4 warps: each warp
+//    covers a quarter of the k range with FP32 FMAs on the CUDA cores (vectorised 16-byte reads;
+//    no tensor cores on the decode path), releases the stage itself and reduces per row at the end
+//    of the tile; the group's first warp adds the four partials in a fixed order and applies the
+//    epilogue (store; store + causal-conv update of that channel; residual add in place; SwiGLU;
+//    running greedy top-1);
 //  * mixers use all CTAs: the DeltaNet step is 128 items (head x 16 value columns, state slice
 //    prefetched before the barrier), attention is split-KV partials over 2 x 74 items and a
 //    combine over 128 (head x 16 dims) items; the conv update rides the in-projection epilogue
@@ -46,8 +46,8 @@ constexpr int kPkCThreads = kPkCWarps * 32;
 constexpr int kPkThreads = kPkCThreads + 32;  // + one producer warp
 constexpr int kPkStages = 6;
 constexpr int kPkKChunk = 2048;                  // k values of one stage row (4 KB of bf16)
-constexpr int kPkTileRows = 8;                   // weight rows per stage (one MMA N tile)
-constexpr int kPkRowPad = 16;                    // bytes after each row: ldmatrix rows hit distinct banks
+constexpr int kPkTileRows = 8;                   // weight rows per stage
+constexpr int kPkRowPad = 0;                     // lanes read consecutive 16-byte chunks: no bank padding
 constexpr int kPkRowStride = kPkKChunk * 2 + kPkRowPad;
 constexpr int kPkStageStride = (kPkTileRows * kPkRowStride + 127) / 128 * 128;
 constexpr int kPkGroups = 4;                     // consumer warp groups, one stage each at a time
@@ -454,35 +454,33 @@ Q35_DEV void gemv_epilogue(const PkOp& op, int unit, float y0, float y1, float& 
 }
 
 // Returns false on abort. `st` is the ring stage counter shared (by construction) with the producer.
-// Warp group g (4 warps) takes tiles g, g + 4, ...; each warp of the group covers a quarter of
-// every stage's k range: ldmatrix reads 8 weight rows x 32 k and two m16n8k16 MMAs multiply them
-// with the input vector broadcast into every row of A, so column n of D is the partial dot
-// product of tile row n (four accumulator chains). Each warp releases the stage itself; the
-// group meets at its own named barrier, and its first warp adds the four partials in a fixed
-// order and applies the epilogue from lanes 0-3.
+// Warp group g (4 warps) takes tiles g, g + 4, ...; warp w of the group covers k values
+// [512 w, 512 w + 512) of every stage: lane l dots 16-byte chunks (l and l + 32 of that range) of
+// the tile's 8 rows with the matching input-vector chunks, FP32 FMAs on the CUDA cores. Each warp
+// releases the stage itself; at the end of the tile the warp reduces its 8 row sums, the group
+// meets at its own named barrier, and its first warp adds the four partials in a fixed order and
+// applies the epilogue from lanes 0-7.
 Q35_DEV bool gemv_op(const PkParams& p, const PkOp& op, PkShared& S, const unsigned char* ring, uint32_t& st,
                      float& best_v, int& best_i) {
   build_input(p, op, S);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int group = warp / kPkGroupWarps, wig = warp % kPkGroupWarps;
-  constexpr int kq = kPkKChunk / kPkGroupWarps;  // k values per warp per stage
+  constexpr int kq = kPkKChunk / kPkGroupWarps;  // k values per warp per stage (512)
   const TilePlan tp = tile_plan(op);
-  const uint32_t* x32 = reinterpret_cast<const uint32_t*>(S.u.xs);
-  const int c2 = lane & 3;
+  const uint4* xs = reinterpret_cast<const uint4*>(S.u.xs);
   bool fail = false;
   int par = 0;
   for (int t = group; t < tp.ntiles; t += kPkGroups, par ^= 1) {
-    // ldmatrix row of this lane: rows past the CTA's units read row 0 (their columns are dropped)
-    const int lr = lane & 7;
-    const int my_row = tile_row(op, tp, t, lr) >= 0 ? lr : 0;
-    if (op.epi == EPI_CONV && wig == 0 && lane == 0) {  // the epilogue's conv lines, ahead of the MMAs
+    if (op.epi == EPI_CONV && wig == 0 && lane == 0) {  // the epilogue's conv lines, ahead of the math
       const int unit0 = tp.u0 + t * kPkTileRows;
       if (unit0 < op.conv_ch) {
         asm volatile("prefetch.global.L1 [%0];" ::"l"(op.conv_state + (int64_t)unit0 * 4));
         asm volatile("prefetch.global.L1 [%0];" ::"l"(op.conv_w + (int64_t)unit0 * 4));
       }
     }
-    float acc[4][4] = {};
+    float acc[kPkTileRows];
+#pragma unroll
+    for (int r = 0; r < kPkTileRows; ++r) acc[r] = 0.f;
     for (int j = 0; j < tp.spt && !fail; ++j) {
       const uint32_t sj = st + (uint32_t)(t * tp.spt + j);
       const int slot = sj % kPkStages;
@@ -491,68 +489,43 @@ Q35_DEV bool gemv_op(const PkParams& p, const PkOp& op, PkShared& S, const unsig
         fail = true;
         break;
       }
-      const uint32_t a_base = smem_u32(ring + (size_t)slot * kPkStageStride) + my_row * kPkRowStride +
-                              (lane >> 3) * 16 + wig * kq * 2;
-      const uint32_t* xj = x32 + (j * kPkKChunk + wig * kq) / 2;
-      // software-pipelined by hand (the asm statements keep their order): four ldmatrix loads
-      // in flight, then the eight MMAs that use them
-      for (int k0 = 0; k0 < kq; k0 += 128) {
-        uint32_t b[4][4];
+      // 16-byte chunk index (within a stage row) of this lane's two chunks
+      const int c0 = (wig * kq) / 8 + lane, c1 = c0 + 32;
+      const uint4 xa = xs[(j * kPkKChunk) / 8 + c0], xb = xs[(j * kPkKChunk) / 8 + c1];
+      const unsigned char* base = ring + (size_t)slot * kPkStageStride;
 #pragma unroll
-        for (int h = 0; h < 4; ++h)
-          asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
-                       : "=r"(b[h][0]), "=r"(b[h][1]), "=r"(b[h][2]), "=r"(b[h][3])
-                       : "r"(a_base + (k0 + 32 * h) * 2));
-#pragma unroll
-        for (int h = 0; h < 4; ++h) {
-          const int kk = (k0 + 32 * h) >> 1;
-          const uint32_t x0 = xj[kk + c2], x1 = xj[kk + 4 + c2], x2 = xj[kk + 8 + c2], x3 = xj[kk + 12 + c2];
-          float* da = acc[2 * (h & 1)];
-          float* db = acc[2 * (h & 1) + 1];
-          asm volatile(
-              "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%4,%5,%5}, {%6,%7}, "
-              "{%0,%1,%2,%3};"
-              : "+f"(da[0]), "+f"(da[1]), "+f"(da[2]), "+f"(da[3])
-              : "r"(x0), "r"(x1), "r"(b[h][0]), "r"(b[h][1]));
-          asm volatile(
-              "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%4,%5,%5}, {%6,%7}, "
-              "{%0,%1,%2,%3};"
-              : "+f"(db[0]), "+f"(db[1]), "+f"(db[2]), "+f"(db[3])
-              : "r"(x2), "r"(x3), "r"(b[h][2]), "r"(b[h][3]));
-        }
+      for (int r = 0; r < kPkTileRows; ++r) {
+        const uint4* rowp = reinterpret_cast<const uint4*>(base + r * kPkRowStride);
+        acc[r] = dot_bf16x8(rowp[c1], xb, dot_bf16x8(rowp[c0], xa, acc[r]));
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&S.empty[slot]);
     }
-    // lanes 0-3 hold D row 0: tile rows 2 * lane and 2 * lane + 1
+    // warp sums of the 8 rows (rows past the CTA's units hold stale data and are dropped below)
+#pragma unroll
+    for (int r = 0; r < kPkTileRows; ++r) acc[r] = warp_sum(acc[r]);
     float* gp = S.gpart[group][par][wig];
-    if (lane < 4) {
-      gp[2 * lane] = (acc[0][0] + acc[1][0]) + (acc[2][0] + acc[3][0]);
-      gp[2 * lane + 1] = (acc[0][1] + acc[1][1]) + (acc[2][1] + acc[3][1]);
+    if (lane == 0) {
+#pragma unroll
+      for (int r = 0; r < kPkTileRows; ++r) gp[r] = acc[r];
     }
     if (gbar_any(group, fail)) {
       fail = true;
       break;
     }
-    if (wig == 0) {
-      float y0 = 0.f, y1 = 0.f;
-      if (lane < 4)
+    if (wig == 0 && lane < kPkTileRows) {  // lane r owns tile row r
+      float y = 0.f;
 #pragma unroll
-        for (int w = 0; w < kPkGroupWarps; ++w) {
-          y0 += S.gpart[group][par][w][2 * lane];
-          y1 += S.gpart[group][par][w][2 * lane + 1];
-        }
-      const float up0 = __shfl_down_sync(0xffffffffu, y0, 2), up1 = __shfl_down_sync(0xffffffffu, y1, 2);
+      for (int w = 0; w < kPkGroupWarps; ++w) y += S.gpart[group][par][w][lane];
       if (op.rpu == 1) {
-        if (lane < 4) {
-          const int unit0 = tp.u0 + t * kPkTileRows + 2 * lane;
-          if (unit0 < tp.u1) gemv_epilogue(op, unit0, y0, 0.f, best_v, best_i);
-          if (unit0 + 1 < tp.u1) gemv_epilogue(op, unit0 + 1, y1, 0.f, best_v, best_i);
-        }
-      } else if (lane < 2) {  // gate rows 2l, 2l+1 here; up rows 2l+4, 2l+5 from lane l + 2
-        const int unit0 = tp.u0 + t * tp.upt + 2 * lane;
-        if (unit0 < tp.u1) gemv_epilogue(op, unit0, y0, up0, best_v, best_i);
-        if (unit0 + 1 < tp.u1) gemv_epilogue(op, unit0 + 1, y1, up1, best_v, best_i);
+        const int unit = tp.u0 + t * kPkTileRows + lane;
+        if (unit < tp.u1) gemv_epilogue(op, unit, y, 0.f, best_v, best_i);
+      } else if (lane < tp.upt) {  // gate row `lane`, up row `lane + upt`
+        float up = 0.f;
+#pragma unroll
+        for (int w = 0; w < kPkGroupWarps; ++w) up += S.gpart[group][par][w][lane + tp.upt];
+        const int unit = tp.u0 + t * tp.upt + lane;
+        if (unit < tp.u1) gemv_epilogue(op, unit, y, up, best_v, best_i);
       }
     }
   }
