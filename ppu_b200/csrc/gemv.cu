@@ -110,13 +110,13 @@ Q35_DEV void epilogue(const GemvParams& p, int unit, float y0, float y1) {
 
 // ---------------------------------------------------------------------------------------------
 // Fast path: compile-time K. A warp's unit group is streamed in SEG segments of CHS 16-byte
-// chunks per lane (at most 8 chunks = 32 registers in flight per thread, 16 warps per SM);
-// segment i+1 is loaded before segment i is consumed.
+// chunks per lane (at most 4 chunks = 16 registers per segment buffer), double-buffered: while
+// segment i is consumed, segment i+1 is in flight, and segment i+2 is issued right after.
 template <int K, bool INT8, int RPU>
 struct FastShape {
   static constexpr int ES = INT8 ? 1 : 2;
   static constexpr int CHT = K * ES / 512;                       // chunks per row per lane
-  static constexpr int BUDGET = 8;                               // 16-byte chunks in flight per lane
+  static constexpr int BUDGET = 4;                               // 16-byte chunks per lane per segment buffer
   static constexpr int SEG = (RPU * CHT > BUDGET) ? (RPU * CHT + BUDGET - 1) / BUDGET : 1;
   static constexpr int CHS = CHT / SEG;                          // chunks per segment
   static constexpr int U = (SEG == 1) ? ((BUDGET / (RPU * CHT)) < 1 ? 1 : BUDGET / (RPU * CHT)) : 1;
@@ -142,8 +142,10 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_fast_kernel(GemvParams p) {
   const int n_iter = (g0 < ngroups) ? ((ngroups - 1 - g0) / gstride + 1) * SEG : 0;
   const char* W = static_cast<const char*>(p.weight);
 
-  uint4 wr[U][RPU][CHS];
-  auto load = [&](int it) {
+  // two segment buffers per lane: segment it + 1 is in flight while segment it is consumed, and
+  // segment it + 2 is issued as soon as it's buffer frees up
+  uint4 wa[U][RPU][CHS], wb[U][RPU][CHS];
+  auto load = [&](uint4 (&wr)[U][RPU][CHS], int it) {
     const int grp = g0 + (it / SEG) * gstride, seg = it % SEG;
 #pragma unroll
     for (int u = 0; u < U; ++u) {
@@ -158,7 +160,8 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_fast_kernel(GemvParams p) {
       }
     }
   };
-  if (n_iter > 0) load(0);
+  if (n_iter > 0) load(wa, 0);
+  if (n_iter > 1) load(wb, 1);
   if (PRO != Q35_PRO_PLAIN)  // norm weights are constants: warm L2 while the producer drains
     for (int i = threadIdx.x; i < K / 64; i += kThreads)
       asm volatile("prefetch.global.L2 [%0];" ::"l"(p.norm_w + 64 * i));
@@ -169,7 +172,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_fast_kernel(GemvParams p) {
 
   float accf[U][RPU];
   int acci[U][RPU];
-  for (int it = 0; it < n_iter; ++it) {
+  auto step = [&](uint4 (&wr)[U][RPU][CHS], int it) {
     const int seg = it % SEG;
     const int g = g0 + (it / SEG) * gstride;
     if (seg == 0) {
@@ -194,8 +197,8 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_fast_kernel(GemvParams p) {
             accf[u][r] = dot_bf16x8(wr[u][r][c], reinterpret_cast<const uint4*>(xs)[xi], accf[u][r]);
         }
       }
-    if (it + 1 < n_iter) load(it + 1);
-    if (seg != SEG - 1) continue;
+    if (it + 2 < n_iter) load(wr, it + 2);
+    if (seg != SEG - 1) return;
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       const int unit = g * U + u;
@@ -212,6 +215,10 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_fast_kernel(GemvParams p) {
       }
       if (lane == 0 && unit < n_out) epilogue<EPI, INT8>(p, unit, y[0], RPU > 1 ? y[RPU - 1] : 0.f);
     }
+  };
+  for (int it = 0; it < n_iter; it += 2) {
+    step(wa, it);
+    if (it + 1 < n_iter) step(wb, it + 1);
   }
 }
 
