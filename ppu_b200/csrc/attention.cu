@@ -202,6 +202,223 @@ __global__ void __launch_bounds__(256) prefill_attn_kernel(const bf16* __restric
   }
 }
 
+// ============================================================================ prefill attention, tensor cores
+// FlashAttention-style causal GQA prefill on mma.sync m16n8k16 (bf16 in, FP32 accumulate).
+// CTA = (16 query rows, KV head g): warp w handles query head g * G + w, so each K/V tile in
+// shared memory serves the G heads of the group. Keys stream in tiles of 32 (cp.async, double
+// buffered, rows padded by 16 bytes so ldmatrix hits distinct banks). S = Q K^T from ldmatrix
+// fragments (bf16 products are exact, FP32 accumulation), scaled, causally masked, online softmax
+// in FP32; P.V uses P split into a bf16 high part and a bf16 remainder (two MMAs), which keeps the
+// probabilities to ~16 bits so the result tracks an FP32 softmax.
+constexpr int kFaRows = 16, kFaKeys = 32, kFaStride = kD + 8;
+
+Q35_DEV void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+Q35_DEV void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+Q35_DEV void mma_bf16(float d[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+Q35_DEV uint32_t pack_bf2(float lo, float hi) {
+  const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&v);
+}
+Q35_DEV void cp16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
+               : "memory");
+}
+
+template <int G>
+__global__ void __launch_bounds__(G * 32) prefill_attn_mma_kernel(const bf16* __restrict__ Q, const bf16* __restrict__ K,
+                                                                 const bf16* __restrict__ V, bf16* __restrict__ O,
+                                                                 int Hq, int Hkv, int L, int kv_len, int q_offset,
+                                                                 float scale) {
+  extern __shared__ __align__(16) unsigned char fa_smem[];
+  bf16* Qs = reinterpret_cast<bf16*>(fa_smem);        // [G][16][stride]
+  bf16* Ks = Qs + G * kFaRows * kFaStride;             // [2][32][stride]
+  bf16* Vs = Ks + 2 * kFaKeys * kFaStride;             // [2][32][stride]
+  constexpr int NT = G * 32;
+  const int q0 = blockIdx.x * kFaRows, g = blockIdx.y, b = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int h = g * G + warp;
+  const bf16* Kg = K + ((int64_t)b * Hkv + g) * kv_len * kD;
+  const bf16* Vg = V + ((int64_t)b * Hkv + g) * kv_len * kD;
+  // queries of the G heads (rows past L read as zero)
+  for (int i = threadIdx.x; i < G * kFaRows * (kD / 8); i += NT) {
+    const int hh = i / (kFaRows * (kD / 8)), r = (i / (kD / 8)) % kFaRows, c = (i % (kD / 8)) * 8;
+    bf16* dst = Qs + (hh * kFaRows + r) * kFaStride + c;
+    if (q0 + r < L)
+      cp16(dst, Q + (((int64_t)b * Hq + g * G + hh) * L + q0 + r) * kD + c);
+    else
+      *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
+  }
+  const int kend = min(kv_len, q0 + kFaRows - 1 + q_offset + 1);  // keys any row of the block may see
+  const int ntiles = (kend + kFaKeys - 1) / kFaKeys;
+  auto load_tile = [&](int t, int buf) {
+    const int k0 = t * kFaKeys;
+    for (int i = threadIdx.x; i < kFaKeys * (kD / 8); i += NT) {
+      const int r = i / (kD / 8), c = (i % (kD / 8)) * 8;
+      bf16* kd = Ks + (buf * kFaKeys + r) * kFaStride + c;
+      bf16* vd = Vs + (buf * kFaKeys + r) * kFaStride + c;
+      if (k0 + r < kv_len) {
+        cp16(kd, Kg + (int64_t)(k0 + r) * kD + c);
+        cp16(vd, Vg + (int64_t)(k0 + r) * kD + c);
+      } else {
+        *reinterpret_cast<uint4*>(kd) = make_uint4(0, 0, 0, 0);
+        *reinterpret_cast<uint4*>(vd) = make_uint4(0, 0, 0, 0);
+      }
+    }
+  };
+  if (ntiles > 0) load_tile(0, 0);
+  asm volatile("cp.async.commit_group;" ::: "memory");
+
+  const int gq = lane >> 2, c4 = lane & 3;  // fragment row group / column pair
+  float o[32][4];
+#pragma unroll
+  for (int n = 0; n < 32; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+  float m0 = -FLT_MAX, m1 = -FLT_MAX, l0 = 0.f, l1 = 0.f;  // rows gq and gq + 8
+  const int qi0 = q0 + gq + q_offset, qi1 = qi0 + 8;
+  const uint32_t qbase = (uint32_t)__cvta_generic_to_shared(Qs + (warp * kFaRows + (lane & 15)) * kFaStride) +
+                         (lane >> 4) * 16;
+  for (int t = 0; t < ntiles; ++t) {
+    const int buf = t & 1;
+    if (t + 1 < ntiles) load_tile(t + 1, buf ^ 1);
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    asm volatile("cp.async.wait_group 1;" ::: "memory");
+    __syncthreads();
+    // ---- S = Q K^T for 16 rows x 32 keys
+    float s[4][4];
+#pragma unroll
+    for (int n = 0; n < 4; ++n) s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.f;
+    const uint32_t kbase = (uint32_t)__cvta_generic_to_shared(Ks + (buf * kFaKeys) * kFaStride);
+#pragma unroll 4
+    for (int ks = 0; ks < kD / 16; ++ks) {
+      uint32_t a0, a1, a2, a3;
+      ldsm_x4(qbase + ks * 32, a0, a1, a2, a3);
+#pragma unroll
+      for (int np = 0; np < 2; ++np) {  // key n-tiles 2np, 2np + 1
+        uint32_t b0, b1, b2, b3;
+        const int key = np * 16 + (lane & 7) + ((lane >> 4) << 3);
+        ldsm_x4(kbase + key * kFaStride * 2 + ks * 32 + ((lane >> 3) & 1) * 16, b0, b1, b2, b3);
+        mma_bf16(s[2 * np], a0, a1, a2, a3, b0, b1);
+        mma_bf16(s[2 * np + 1], a0, a1, a2, a3, b2, b3);
+      }
+    }
+    // ---- scale, causal mask, online softmax (rows gq and gq + 8; keys n*8 + 2*c4 + {0,1})
+    const int k0 = t * kFaKeys;
+    float mx0 = -FLT_MAX, mx1 = -FLT_MAX;
+#pragma unroll
+    for (int n = 0; n < 4; ++n)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int kj = k0 + n * 8 + 2 * c4 + e;
+        const bool ok = kj < kv_len;
+        s[n][e] = (ok && kj <= qi0) ? s[n][e] * scale : -FLT_MAX;
+        s[n][2 + e] = (ok && kj <= qi1) ? s[n][2 + e] * scale : -FLT_MAX;
+        mx0 = fmaxf(mx0, s[n][e]);
+        mx1 = fmaxf(mx1, s[n][2 + e]);
+      }
+#pragma unroll
+    for (int off = 1; off < 4; off <<= 1) {
+      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
+    }
+    const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+    const float al0 = (m0 == -FLT_MAX) ? 0.f : expf(m0 - mn0), al1 = (m1 == -FLT_MAX) ? 0.f : expf(m1 - mn1);
+    float rs0 = 0.f, rs1 = 0.f;
+#pragma unroll
+    for (int n = 0; n < 4; ++n)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        s[n][e] = (s[n][e] == -FLT_MAX) ? 0.f : expf(s[n][e] - mn0);
+        s[n][2 + e] = (s[n][2 + e] == -FLT_MAX) ? 0.f : expf(s[n][2 + e] - mn1);
+        rs0 += s[n][e];
+        rs1 += s[n][2 + e];
+      }
+#pragma unroll
+    for (int off = 1; off < 4; off <<= 1) {
+      rs0 += __shfl_xor_sync(0xffffffffu, rs0, off);
+      rs1 += __shfl_xor_sync(0xffffffffu, rs1, off);
+    }
+    l0 = l0 * al0 + rs0;
+    l1 = l1 * al1 + rs1;
+    m0 = mn0;
+    m1 = mn1;
+#pragma unroll
+    for (int n = 0; n < 32; ++n) {
+      o[n][0] *= al0;
+      o[n][1] *= al0;
+      o[n][2] *= al1;
+      o[n][3] *= al1;
+    }
+    // ---- O += P V: P (16 x 32) as two k-steps of 16 keys, high and low bf16 parts
+    const uint32_t vbase = (uint32_t)__cvta_generic_to_shared(Vs + (buf * kFaKeys) * kFaStride);
+#pragma unroll
+    for (int kk = 0; kk < 2; ++kk) {
+      const float* pa = s[2 * kk];
+      const float* pb = s[2 * kk + 1];
+      const uint32_t h0 = pack_bf2(pa[0], pa[1]), h1 = pack_bf2(pa[2], pa[3]);
+      const uint32_t h2 = pack_bf2(pb[0], pb[1]), h3 = pack_bf2(pb[2], pb[3]);
+      auto resid = [](float x, uint32_t packed, int half) {
+        const float r = __uint_as_float(half ? (packed & 0xffff0000u) : (packed << 16));
+        return x - r;
+      };
+      const uint32_t l0p = pack_bf2(resid(pa[0], h0, 0), resid(pa[1], h0, 1));
+      const uint32_t l1p = pack_bf2(resid(pa[2], h1, 0), resid(pa[3], h1, 1));
+      const uint32_t l2p = pack_bf2(resid(pb[0], h2, 0), resid(pb[1], h2, 1));
+      const uint32_t l3p = pack_bf2(resid(pb[2], h3, 0), resid(pb[3], h3, 1));
+      // B fragments of V (keys kk*16 .. +15 x dims): transposed 8x8 loads, two dim n-tiles per x4
+      const int vrow = kk * 16 + (lane & 7) + (((lane >> 3) & 1) << 3);
+#pragma unroll
+      for (int np = 0; np < 16; ++np) {
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4_t(vbase + vrow * kFaStride * 2 + (np * 16 + (lane >> 4) * 8) * 2, b0, b1, b2, b3);
+        mma_bf16(o[2 * np], h0, h1, h2, h3, b0, b1);
+        mma_bf16(o[2 * np], l0p, l1p, l2p, l3p, b0, b1);
+        mma_bf16(o[2 * np + 1], h0, h1, h2, h3, b2, b3);
+        mma_bf16(o[2 * np + 1], l0p, l1p, l2p, l3p, b2, b3);
+      }
+    }
+    __syncthreads();  // this buffer is refilled two tiles later
+  }
+  // ---- normalise and store (rows gq, gq + 8; dims n*8 + 2*c4 + {0,1})
+  const float inv0 = l0 > 0.f ? 1.0f / l0 : 0.f, inv1 = l1 > 0.f ? 1.0f / l1 : 0.f;
+  const int r0 = q0 + gq, r1 = r0 + 8;
+#pragma unroll
+  for (int n = 0; n < 32; ++n) {
+    const int d = n * 8 + 2 * c4;
+    if (r0 < L)
+      *reinterpret_cast<uint32_t*>(O + (((int64_t)b * L + r0) * Hq + h) * kD + d) =
+          pack_bf2(o[n][0] * inv0, o[n][1] * inv0);
+    if (r1 < L)
+      *reinterpret_cast<uint32_t*>(O + (((int64_t)b * L + r1) * Hq + h) * kD + d) =
+          pack_bf2(o[n][2] * inv1, o[n][3] * inv1);
+  }
+}
+
+template <int G>
+int launch_prefill_mma(const void* q, const void* k, const void* v, void* out, int64_t batch, int64_t q_heads,
+                       int64_t kv_heads, int64_t seq_len, int64_t kv_len, int64_t q_offset, float scale,
+                       cudaStream_t stream) {
+  const size_t smem = (size_t)(G * kFaRows + 4 * kFaKeys) * kFaStride * sizeof(bf16);
+  cudaFuncSetAttribute(prefill_attn_mma_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  const dim3 grid((unsigned)((seq_len + kFaRows - 1) / kFaRows), (unsigned)kv_heads, (unsigned)batch);
+  prefill_attn_mma_kernel<G><<<grid, G * 32, smem, stream>>>((const bf16*)q, (const bf16*)k, (const bf16*)v,
+                                                             (bf16*)out, (int)q_heads, (int)kv_heads, (int)seq_len,
+                                                             (int)kv_len, (int)q_offset, scale);
+  return q35_check_launch("prefill_attention");
+}
+
 }  // namespace
 
 // ------------------------------------------------------------------------------------ C ABI
@@ -246,6 +463,15 @@ extern "C" int q35_prefill_attention(const void* q, const void* k, const void* v
                   kv_len >= q_offset + seq_len,
               "prefill_attention: bad shape");
   if (batch * seq_len == 0) return Q35_OK;
+  switch (q_heads / kv_heads) {  // tensor-core path for the group sizes it is built for
+    case 4: return launch_prefill_mma<4>(q, k, v, out, batch, q_heads, kv_heads, seq_len, kv_len, q_offset, scale,
+                                         (cudaStream_t)stream);
+    case 2: return launch_prefill_mma<2>(q, k, v, out, batch, q_heads, kv_heads, seq_len, kv_len, q_offset, scale,
+                                         (cudaStream_t)stream);
+    case 1: return launch_prefill_mma<1>(q, k, v, out, batch, q_heads, kv_heads, seq_len, kv_len, q_offset, scale,
+                                         (cudaStream_t)stream);
+    default: break;
+  }
   const size_t smem = (size_t)(kPQ * kD + kD * kPK + kPK * kD) * sizeof(bf16) + (size_t)kPQ * 65 * sizeof(float);
   cudaFuncSetAttribute(prefill_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   dim3 grid((unsigned)((seq_len + kPQ - 1) / kPQ), (unsigned)q_heads, (unsigned)batch);

@@ -50,6 +50,42 @@ __global__ void conv_prefill_kernel(const bf16* __restrict__ x, const bf16* __re
   (void)total;
 }
 
+// Prefill with a compile-time kernel width: thread = (channel, run of kConvRun timesteps), the
+// last KT inputs held in registers as the window slides (one load per output instead of KT, and
+// no per-element index division). Same tap order and rounding as conv_prefill_kernel.
+constexpr int kConvRun = 32;
+template <int KT>
+__global__ void __launch_bounds__(256) conv_prefill_win_kernel(const bf16* __restrict__ x, const bf16* __restrict__ w,
+                                                               bf16* __restrict__ state, bf16* __restrict__ out, int L,
+                                                               int in_stride, int C) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  const int t0 = blockIdx.y * kConvRun;
+  const int b = blockIdx.z;
+  if (c >= C || t0 >= L) return;
+  const bf16* xb = x + (int64_t)b * L * in_stride + c;
+  float wk[KT], hist[KT];
+#pragma unroll
+  for (int tap = 0; tap < KT; ++tap) wk[tap] = bf2f(w[c * KT + tap]);
+#pragma unroll
+  for (int j = 0; j < KT - 1; ++j) {  // inputs before the run (the sequence starts from a zero history)
+    const int src = t0 - (KT - 1) + j;
+    hist[j] = src >= 0 ? bf2f(xb[(int64_t)src * in_stride]) : 0.f;
+  }
+  const int t1 = min(t0 + kConvRun, L);
+  for (int t = t0; t < t1; ++t) {
+    const bf16 xt = xb[(int64_t)t * in_stride];
+    hist[KT - 1] = bf2f(xt);
+    float acc = 0.f;
+#pragma unroll
+    for (int tap = 0; tap < KT; ++tap) acc += hist[tap] * wk[tap];
+    out[((int64_t)b * L + t) * C + c] = f2bf(silu_f(rbf(acc)));
+    const int sp = t - (L - KT);
+    if (sp >= 0) state[((int64_t)b * C + c) * KT + sp] = xt;
+#pragma unroll
+    for (int j = 0; j < KT - 1; ++j) hist[j] = hist[j + 1];
+  }
+}
+
 __global__ void conv_update_kernel(const bf16* __restrict__ x, const bf16* __restrict__ w, bf16* __restrict__ state,
                                    bf16* __restrict__ out, int batch, int in_stride, int C, int K) {
   const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
@@ -396,6 +432,10 @@ extern "C" int q35_causal_conv1d(const void* x, const void* weight, void* state,
     conv_update_kernel<<<(unsigned)((total + 255) / 256), 256, 0, (cudaStream_t)stream>>>(
         (const bf16*)x, (const bf16*)weight, (bf16*)state, (bf16*)out, (int)batch, (int)in_stride, (int)channels,
         (int)kernel_size);
+  } else if (kernel_size == 4 && seq_len >= 4) {
+    const dim3 grid((unsigned)((channels + 255) / 256), (unsigned)((seq_len + kConvRun - 1) / kConvRun), (unsigned)batch);
+    conv_prefill_win_kernel<4><<<grid, 256, 0, (cudaStream_t)stream>>>(
+        (const bf16*)x, (const bf16*)weight, (bf16*)state, (bf16*)out, (int)seq_len, (int)in_stride, (int)channels);
   } else {
     int64_t blocks = (seq_len * channels + 255) / 256;
     if (blocks > 4 * kNumSMs) blocks = 4 * kNumSMs;

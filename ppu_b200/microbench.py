@@ -157,6 +157,37 @@ def run(kernels: list[str], reps: int, layers: int = 24, a8w8: bool = False):
             report("delta_chunked_1024", t, flops=16 * 16 * 11_700_000)
             t = _time(lambda i: K.delta_recurrent_fused(qkv, packed, z16, z16, st), max(1, reps // 4))
             report("delta_sequential_1024", t)
+        elif name == "prefill_attn":
+            Lp = 1024
+            q = torch.randn(1, 8, Lp, 256, device=dev, generator=g).to(torch.bfloat16)
+            kk = torch.randn(1, 2, Lp, 256, device=dev, generator=g).to(torch.bfloat16)
+            vv = torch.randn(1, 2, Lp, 256, device=dev, generator=g).to(torch.bfloat16)
+            t = _time(lambda i: K.prefill_attention(q, kk, vv, 0.0625), reps)
+            report("prefill_attn_1024", t, flops=4 * 8 * 256 * Lp * Lp // 2)
+        elif name == "conv_prefill":
+            Lp = 1024
+            x = torch.randn(1, Lp, 8224, device=dev, generator=g).to(torch.bfloat16)
+            cw = torch.randn(6144, 4, device=dev, generator=g).to(torch.bfloat16)
+            cs = torch.zeros(1, 6144, 4, device=dev, dtype=torch.bfloat16)
+            t = _time(lambda i: K.causal_conv1d_fused(x, cw, cs), reps)
+            report("conv_prefill_1024", t, nbytes=2 * Lp * 6144 * 2)
+        elif name == "prefill":
+            from .config import Qwen35Dims
+            from .engine import Qwen35Engine
+            from .synthetic import make_prompt, make_weights
+            dims = Qwen35Dims()
+            eng = Qwen35Engine(make_weights(dims, seed=0, device=dev), dims, max_len=1152, max_prefill=1024)
+            ids = make_prompt(dims, 1024, seed=1)[0].to(dev)
+            eng.prefill(ids)
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(max(1, reps)):
+                eng.prefill(ids)
+            e1.record()
+            torch.cuda.synchronize()
+            report("prefill_1024", e0.elapsed_time(e1) / 1000.0 / max(1, reps), flops=2_810_000_000_000)
+            del eng
         elif name in ("persistent_trace", "persistent_small"):
             from .config import Qwen35Dims
             from .engine import Qwen35Engine

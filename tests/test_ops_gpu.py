@@ -277,7 +277,10 @@ def test_prefill_attention(length):
     k = randn(1, 2, length, 256, seed=2)
     v = randn(1, 2, length, 256, seed=3)
     out = K.prefill_attention(cu(q), cu(k), cu(v), 0.0625)
-    assert rel_err(out, O.causal_attention(q, k, v, 0.0625)) < 1e-2
+    err = rel_err(out, O.causal_attention(q, k, v, 0.0625))
+    assert err < 1e-2
+    if length == 1024:  # probabilities kept to ~16 bits: within a few BF16 output roundings of FP32
+        assert err < 3e-3, err
 
 
 # ------------------------------------------------------------------ DeltaNet
