@@ -8,8 +8,8 @@
 //   A_ij = -beta_i (k_i . k_j) exp(c_i - c_j) (i > j); T = (I - A)^-1 by forward substitution;
 //   U = T diag(beta) V;  W = T diag(beta exp(c)) K;  P_ij = (q_i . k_j) exp(c_i - c_j) (i >= j);
 //   Qe = q_hat exp(c);   Kd = k_hat exp(c_last - c);  gl = exp(c_last).
-// Phase B (one CTA per (batch, head, 16 value columns), chunks in order):
-//   Vn = U - W S;  O = Qe S + P Vn;  S <- gl S + Kd^T Vn;  out = bf16(O).
+// Phase B (one CTA per (batch, head, 16 value columns), chunks in order, products on the tensor
+// cores in 3xTF32):  Vn = U - W S;  O = Qe S + P Vn;  S <- gl S + Kd^T Vn;  out = bf16(O).
 // Padded tokens (beyond L) have beta = 0 and g = 0, as the reference's zero padding.
 #include "common.cuh"
 
@@ -205,92 +205,184 @@ struct ScanParams {
   int L, H, NC;
 };
 
+// ---- 3xTF32 tensor-core products (m16n8k8): x = hi + lo with hi, lo TF32; hi*hi + hi*lo + lo*hi
+// keeps ~FP32 accuracy (the dropped lo*lo term is below FP32 rounding of the sum).
+Q35_DEV uint32_t tf32_bits(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return r;
+}
+Q35_DEV void split_tf32(float x, uint32_t& hi, uint32_t& lo) {
+  hi = tf32_bits(x);
+  lo = tf32_bits(x - __uint_as_float(hi));
+}
+Q35_DEV void mma_tf32(float d[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+// d += A[16 x 8] * B[8 x 8] for one k-step; a = {A[g][c], A[g+8][c], A[g][c+4], A[g+8][c+4]},
+// b = {B[c][g], B[c+4][g]} (g = lane / 4, c = lane % 4).
+Q35_DEV void mma3(float d[4], const float a[4], const float b[2]) {
+  uint32_t ah[4], al[4], bh[2], bl[2];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) split_tf32(a[i], ah[i], al[i]);
+  split_tf32(b[0], bh[0], bl[0]);
+  split_tf32(b[1], bh[1], bl[1]);
+  mma_tf32(d, al[0], al[1], al[2], al[3], bh[0], bh[1]);
+  mma_tf32(d, ah[0], ah[1], ah[2], ah[3], bl[0], bl[1]);
+  mma_tf32(d, ah[0], ah[1], ah[2], ah[3], bh[0], bh[1]);
+}
+
+Q35_DEV void cp_async16(float* dst, const float* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
+               : "memory");
+}
+
+constexpr int kPS = 24;   // row stride (floats) of S / Vn tiles: B-fragment loads hit distinct banks
+constexpr int kPP = 68;   // row stride of P
+constexpr int kPK2 = 132; // row stride of Kd (read transposed as the A operand of Kd^T Vn)
+
+// Phase B on the tensor cores: the CTA's 8 warps split every product into 16 x 8 output tiles.
+//   Vn (64 x 16) = U - W S        warp w: rows 16 (w & 3), cols 8 (w >> 2), K = 128
+//   O  (64 x 16) = Qe S + P Vn    same tiles, K = 128 + 64
+//   S' (128 x 16) = gl S + Kd^T Vn  warp w: rows 16 w, both column tiles, K = 64
 __global__ void __launch_bounds__(kThreads, 1) delta_chunk_scan_kernel(ScanParams p) {
   extern __shared__ __align__(16) float sm[];
-  float* W = sm;                  // [64][132]
-  float* Qe = W + kC * kPW;       // [64][132]
-  float* Kd = Qe + kC * kPW;      // [64][128]
-  float* P = Kd + kC * kD;        // [64][64]
-  float* U = P + kC * kC;         // [64][16]
-  float* Vn = U + kC * kVS;       // [64][16]
-  float* S = Vn + kC * kVS;       // [128][16]
+  float* W = sm;                   // [64][132]
+  float* Qe = W + kC * kPW;        // [64][132]
+  float* Kd = Qe + kC * kPW;       // [64][132]
+  float* P = Kd + kC * kPK2;       // [64][68]
+  float* U = P + kC * kPP;         // [64][16]
+  float* Vn = U + kC * kVS;        // [64][24]
+  float* S = Vn + kC * kPS;        // [128][24]
   __shared__ float gl_s;
   const int nvs = kD / kVS;
   const int vs = blockIdx.x % nvs;
   const int h = (blockIdx.x / nvs) % p.H;
   const int b = blockIdx.x / (nvs * p.H);
-  const int tid = threadIdx.x;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, c = lane & 3;
   float* Sg = p.state + ((size_t)(b * p.H + h) * kD) * kD + vs * kVS;
-  for (int i = tid; i < kD * kVS; i += kThreads) S[i] = Sg[(i / kVS) * kD + (i % kVS)];
+  for (int i = tid; i < kD * kVS; i += kThreads) S[(i / kVS) * kPS + (i % kVS)] = Sg[(i / kVS) * kD + (i % kVS)];
+  const int mt = warp & 3, nt = warp >> 2;  // Vn / O tile of this warp
   for (int ch = 0; ch < p.NC; ++ch) {
     const float* rec = p.ws + ((size_t)(b * p.H + h) * p.NC + ch) * ChunkWs::SIZE;
     __syncthreads();
+    // the chunk record: all copies in flight at once (cp.async), one wait
     for (int i = tid; i < kC * kD / 4; i += kThreads) {
       const int r = i / (kD / 4), c4 = (i % (kD / 4)) * 4;
-      *reinterpret_cast<float4*>(W + r * kPW + c4) = *reinterpret_cast<const float4*>(rec + ChunkWs::W + r * kD + c4);
-      *reinterpret_cast<float4*>(Qe + r * kPW + c4) = *reinterpret_cast<const float4*>(rec + ChunkWs::Qe + r * kD + c4);
-      *reinterpret_cast<float4*>(Kd + r * kD + c4) = *reinterpret_cast<const float4*>(rec + ChunkWs::Kd + r * kD + c4);
+      cp_async16(W + r * kPW + c4, rec + ChunkWs::W + r * kD + c4);
+      cp_async16(Qe + r * kPW + c4, rec + ChunkWs::Qe + r * kD + c4);
+      cp_async16(Kd + r * kPK2 + c4, rec + ChunkWs::Kd + r * kD + c4);
     }
-    for (int i = tid; i < kC * kC / 4; i += kThreads)
-      reinterpret_cast<float4*>(P)[i] = reinterpret_cast<const float4*>(rec + ChunkWs::P)[i];
-    for (int i = tid; i < kC * kVS; i += kThreads) U[i] = rec[ChunkWs::U + (i / kVS) * kD + vs * kVS + (i % kVS)];
+    for (int i = tid; i < kC * kC / 4; i += kThreads) {
+      const int r = i / (kC / 4), c4 = (i % (kC / 4)) * 4;
+      cp_async16(P + r * kPP + c4, rec + ChunkWs::P + r * kC + c4);
+    }
+    for (int i = tid; i < kC * kVS / 4; i += kThreads) {
+      const int r = i / (kVS / 4), c4 = (i % (kVS / 4)) * 4;
+      cp_async16(U + r * kVS + c4, rec + ChunkWs::U + r * kD + vs * kVS + c4);
+    }
+    asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
     if (tid == 0) gl_s = rec[ChunkWs::GL];
     __syncthreads();
-    // Vn = U - W S (thread: column e, rows i0..i0+3)
-    const int e = tid % kVS, i0 = (tid / kVS) * 4;
+    const int r0 = mt * 16 + g, n0 = nt * 8;
+    // ---- Vn = U - W S
     {
-      float acc[4] = {0.f, 0.f, 0.f, 0.f};
-      for (int kk = 0; kk < kD; ++kk) {
-        const float sv = S[kk * kVS + e];
+      float d[4] = {0.f, 0.f, 0.f, 0.f}, e[4] = {0.f, 0.f, 0.f, 0.f};  // two chains: even / odd k-steps
+#pragma unroll 4
+      for (int k0 = 0; k0 < kD; k0 += 16) {
 #pragma unroll
-        for (int a = 0; a < 4; ++a) acc[a] = fmaf(W[(i0 + a) * kPW + kk], sv, acc[a]);
+        for (int hh = 0; hh < 2; ++hh) {
+          const int k = k0 + 8 * hh;
+          const float a[4] = {W[r0 * kPW + k + c], W[(r0 + 8) * kPW + k + c], W[r0 * kPW + k + c + 4],
+                              W[(r0 + 8) * kPW + k + c + 4]};
+          const float bb[2] = {S[(k + c) * kPS + n0 + g], S[(k + c + 4) * kPS + n0 + g]};
+          mma3(hh ? e : d, a, bb);
+        }
       }
 #pragma unroll
-      for (int a = 0; a < 4; ++a) Vn[(i0 + a) * kVS + e] = U[(i0 + a) * kVS + e] - acc[a];
+      for (int i = 0; i < 4; ++i) d[i] += e[i];
+      const int col = n0 + 2 * c;
+      Vn[r0 * kPS + col] = U[r0 * kVS + col] - d[0];
+      Vn[r0 * kPS + col + 1] = U[r0 * kVS + col + 1] - d[1];
+      Vn[(r0 + 8) * kPS + col] = U[(r0 + 8) * kVS + col] - d[2];
+      Vn[(r0 + 8) * kPS + col + 1] = U[(r0 + 8) * kVS + col + 1] - d[3];
     }
     __syncthreads();
-    // O = Qe S + P Vn
+    // ---- O = Qe S + P Vn (rows r0, r0 + 8; columns n0 + 2c, +1)
     {
-      float acc[4] = {0.f, 0.f, 0.f, 0.f};
-      for (int kk = 0; kk < kD; ++kk) {
-        const float sv = S[kk * kVS + e];
-#pragma unroll
-        for (int a = 0; a < 4; ++a) acc[a] = fmaf(Qe[(i0 + a) * kPW + kk], sv, acc[a]);
+      float d[4] = {0.f, 0.f, 0.f, 0.f}, e[4] = {0.f, 0.f, 0.f, 0.f};  // Qe S and P Vn in separate chains
+#pragma unroll 4
+      for (int k0 = 0; k0 < kC; k0 += 8) {
+        {
+          const float a[4] = {Qe[r0 * kPW + k0 + c], Qe[(r0 + 8) * kPW + k0 + c], Qe[r0 * kPW + k0 + c + 4],
+                              Qe[(r0 + 8) * kPW + k0 + c + 4]};
+          const float bb[2] = {S[(k0 + c) * kPS + n0 + g], S[(k0 + c + 4) * kPS + n0 + g]};
+          mma3(d, a, bb);
+        }
+        {
+          const int k = kC + k0;
+          const float a[4] = {Qe[r0 * kPW + k + c], Qe[(r0 + 8) * kPW + k + c], Qe[r0 * kPW + k + c + 4],
+                              Qe[(r0 + 8) * kPW + k + c + 4]};
+          const float bb[2] = {S[(k + c) * kPS + n0 + g], S[(k + c + 4) * kPS + n0 + g]};
+          mma3(d, a, bb);
+        }
+        const float a[4] = {P[r0 * kPP + k0 + c], P[(r0 + 8) * kPP + k0 + c], P[r0 * kPP + k0 + c + 4],
+                            P[(r0 + 8) * kPP + k0 + c + 4]};
+        const float bb[2] = {Vn[(k0 + c) * kPS + n0 + g], Vn[(k0 + c + 4) * kPS + n0 + g]};
+        mma3(e, a, bb);
       }
-      for (int j = 0; j < kC; ++j) {
-        const float vn = Vn[j * kVS + e];
 #pragma unroll
-        for (int a = 0; a < 4; ++a) acc[a] = fmaf(P[(i0 + a) * kC + j], vn, acc[a]);
+      for (int i = 0; i < 4; ++i) d[i] += e[i];
+      const int col = vs * kVS + n0 + 2 * c;
+      const int t0 = ch * kC + r0, t1 = t0 + 8;
+      if (t0 < p.L) {
+        bf16* o = p.out + (((int64_t)b * p.L + t0) * p.H + h) * kD + col;
+        o[0] = f2bf(d[0]);
+        o[1] = f2bf(d[1]);
       }
-#pragma unroll
-      for (int a = 0; a < 4; ++a) {
-        const int t = ch * kC + i0 + a;
-        if (t < p.L) p.out[(((int64_t)b * p.L + t) * p.H + h) * kD + vs * kVS + e] = f2bf(acc[a]);
+      if (t1 < p.L) {
+        bf16* o = p.out + (((int64_t)b * p.L + t1) * p.H + h) * kD + col;
+        o[0] = f2bf(d[2]);
+        o[1] = f2bf(d[3]);
       }
     }
-    // S <- gl S + Kd^T Vn (thread: column e, key rows k0..k0+7)
+    // ---- S' = gl S + Kd^T Vn (rows 16 warp + g (+8); columns 8 n + 2c (+1), n = 0, 1)
     {
-      const int k0 = (tid / kVS) * 8;
-      float acc[8];
-#pragma unroll
-      for (int a = 0; a < 8; ++a) acc[a] = 0.f;
-      for (int j = 0; j < kC; ++j) {
-        const float vn = Vn[j * kVS + e];
-#pragma unroll
-        for (int a = 0; a < 8; ++a) acc[a] = fmaf(Kd[j * kD + k0 + a], vn, acc[a]);
+      float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
+      const int m0 = warp * 16 + g;
+#pragma unroll 4
+      for (int k0 = 0; k0 < kC; k0 += 8) {
+        const float a[4] = {Kd[(k0 + c) * kPK2 + m0], Kd[(k0 + c) * kPK2 + m0 + 8], Kd[(k0 + c + 4) * kPK2 + m0],
+                            Kd[(k0 + c + 4) * kPK2 + m0 + 8]};
+        const float b0[2] = {Vn[(k0 + c) * kPS + g], Vn[(k0 + c + 4) * kPS + g]};
+        const float b1[2] = {Vn[(k0 + c) * kPS + 8 + g], Vn[(k0 + c + 4) * kPS + 8 + g]};
+        mma3(d0, a, b0);
+        mma3(d1, a, b1);
       }
       const float gl = gl_s;
-      __syncthreads();  // every thread is done reading S for this chunk
-#pragma unroll
-      for (int a = 0; a < 8; ++a) S[(k0 + a) * kVS + e] = gl * S[(k0 + a) * kVS + e] + acc[a];
+      __syncthreads();  // every warp is done reading S for this chunk
+      const int col = 2 * c;
+      S[m0 * kPS + col] = gl * S[m0 * kPS + col] + d0[0];
+      S[m0 * kPS + col + 1] = gl * S[m0 * kPS + col + 1] + d0[1];
+      S[(m0 + 8) * kPS + col] = gl * S[(m0 + 8) * kPS + col] + d0[2];
+      S[(m0 + 8) * kPS + col + 1] = gl * S[(m0 + 8) * kPS + col + 1] + d0[3];
+      S[m0 * kPS + 8 + col] = gl * S[m0 * kPS + 8 + col] + d1[0];
+      S[m0 * kPS + 8 + col + 1] = gl * S[m0 * kPS + 8 + col + 1] + d1[1];
+      S[(m0 + 8) * kPS + 8 + col] = gl * S[(m0 + 8) * kPS + 8 + col] + d1[2];
+      S[(m0 + 8) * kPS + 8 + col + 1] = gl * S[(m0 + 8) * kPS + 8 + col + 1] + d1[3];
     }
   }
   __syncthreads();
-  for (int i = tid; i < kD * kVS; i += kThreads) Sg[(i / kVS) * kD + (i % kVS)] = S[i];
+  for (int i = tid; i < kD * kVS; i += kThreads) Sg[(i / kVS) * kD + (i % kVS)] = S[(i / kVS) * kPS + (i % kVS)];
 }
 
 constexpr size_t kPrepSmem = (size_t)(3 * kC * kP + 2 * kC * 65) * sizeof(float);
-constexpr size_t kScanSmem = (size_t)(2 * kC * kPW + kC * kD + kC * kC + 2 * kC * kVS + kD * kVS) * sizeof(float);
+constexpr size_t kScanSmem =
+    (size_t)(2 * kC * kPW + kC * kPK2 + kC * kPP + kC * kVS + kC * kPS + kD * kPS) * sizeof(float);
 
 }  // namespace
 

@@ -23,10 +23,9 @@ __device__ int q35_tc_error_word = 0;
 
 namespace {
 
-constexpr int BM = 128, BN = 256, BKB = 128;  // tile rows, tile cols, K bytes per stage
+constexpr int BM = 128, BKB = 128;  // tile rows, K bytes per stage (tile cols: 256, or 128 for narrow N)
 constexpr int kStages = 4;
-constexpr int kABytes = BM * BKB;             // 16 KB
-constexpr int kBBytes = BN * BKB;             // 32 KB
+constexpr int kABytes = BM * BKB;   // 16 KB
 constexpr int kThreads = 128;
 constexpr long long kWaitBudget = 4000000000LL;  // ~2 s at 2 GHz
 
@@ -116,18 +115,19 @@ Q35_DEV void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
 
 Q35_DEV void report(int code) { atomicCAS(&q35_tc_error_word, 0, code); }
 
-template <bool INT8, int EPI>
+template <bool INT8, int EPI, int TBN>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, TcParams p) {
+  constexpr int kBB = TBN * BKB;  // B bytes per stage
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   unsigned char* sA = smem;
   unsigned char* sB = smem + kStages * kABytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + kStages * kBBytes);  // full[S], empty[S], done
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + kStages * kBB);  // full[S], empty[S], done
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kStages + 1);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int m0 = blockIdx.y * BM;
-  const int col0 = blockIdx.x * (EPI == Q35_EPI_SWIGLU ? BN / 2 : BN);  // first output column
+  const int col0 = blockIdx.x * (EPI == Q35_EPI_SWIGLU ? TBN / 2 : TBN);  // first output column
   const int n_k = p.K / (BKB / (INT8 ? 1 : 2));
   const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + kStages), done = smem_u32(bars + 2 * kStages);
 
@@ -141,7 +141,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "r"(BN)
+                 "r"(TBN)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
@@ -157,21 +157,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         report(1);
         break;
       }
-      mbar_expect_tx(full0 + 8 * s, kABytes + kBBytes);
+      mbar_expect_tx(full0 + 8 * s, kABytes + kBB);
       const int kx = kt * (BKB / (INT8 ? 1 : 2));
       tma_load_2d(smem_u32(sA + s * kABytes), &tmA, kx, m0, full0 + 8 * s);
       if (EPI == Q35_EPI_SWIGLU) {
-        tma_load_2d(smem_u32(sB + s * kBBytes), &tmB, kx, col0, full0 + 8 * s);
-        tma_load_2d(smem_u32(sB + s * kBBytes + kBBytes / 2), &tmB, kx, p.N + col0, full0 + 8 * s);
+        tma_load_2d(smem_u32(sB + s * kBB), &tmB, kx, col0, full0 + 8 * s);
+        tma_load_2d(smem_u32(sB + s * kBB + kBB / 2), &tmB, kx, p.N + col0, full0 + 8 * s);
       } else {
-        tma_load_2d(smem_u32(sB + s * kBBytes), &tmB, kx, col0, full0 + 8 * s);
+        tma_load_2d(smem_u32(sB + s * kBB), &tmB, kx, col0, full0 + 8 * s);
       }
     }
   } else if (warp == 1 && lane == 0) {
     // ---------------- MMA issuer
     // instruction descriptor: D fp32 (1) / s32 (2); A, B bf16 (1) / signed int8 (1); K-major;
-    // N = 256 (>> 3 at bit 17), M = 128 (>> 4 at bit 24)
-    const uint32_t idesc = ((INT8 ? 2u : 1u) << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
+    // N = TBN (>> 3 at bit 17), M = 128 (>> 4 at bit 24)
+    const uint32_t idesc = ((INT8 ? 2u : 1u) << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(TBN >> 3) << 17) |
                            ((uint32_t)(BM >> 4) << 24);
     bool ok = true;
     for (int kt = 0; kt < n_k && ok; ++kt) {
@@ -182,7 +182,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      const uint32_t a0 = smem_u32(sA + s * kABytes), b0 = smem_u32(sB + s * kBBytes);
+      const uint32_t a0 = smem_u32(sA + s * kABytes), b0 = smem_u32(sB + s * kBB);
 #pragma unroll
       for (int k = 0; k < BKB / 32; ++k)  // 32 bytes of K per MMA
         mma<INT8>(tmem, smem_desc(a0 + 32 * k), smem_desc(b0 + 32 * k), idesc, (kt > 0 || k > 0) ? 1u : 0u);
@@ -199,11 +199,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int row = m0 + warp * 32 + lane;
   const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
   if (ready) {
-    const int ncols = (EPI == Q35_EPI_SWIGLU) ? BN / 2 : BN;
+    const int ncols = (EPI == Q35_EPI_SWIGLU) ? TBN / 2 : TBN;
     for (int c = 0; c < ncols; c += 32) {
       uint32_t v[32], u[32];
       tmem_ld32(trow + c, v);
-      if (EPI == Q35_EPI_SWIGLU) tmem_ld32(trow + BN / 2 + c, u);
+      if (EPI == Q35_EPI_SWIGLU) tmem_ld32(trow + TBN / 2 + c, u);
       if (row >= p.M) continue;
       const int gc = col0 + c;
       float y[32];
@@ -259,7 +259,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
   if (warp == 1)
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(BN) : "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TBN) : "memory");
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -288,20 +288,30 @@ bool make_map(CUtensorMap* m, const void* ptr, uint64_t rows, uint64_t k, uint32
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-constexpr size_t kSmem = 1024 + (size_t)kStages * (kABytes + kBBytes) + 256;
+constexpr size_t smem_bytes(int bn) { return 1024 + (size_t)kStages * (kABytes + (size_t)bn * BKB) + 256; }
 
-template <bool INT8, int EPI>
-int launch_tc(const void* a, const void* w, const TcParams& p, cudaStream_t s) {
+template <bool INT8, int EPI, int TBN>
+int launch_tc_bn(const void* a, const void* w, const TcParams& p, cudaStream_t s) {
   CUtensorMap ma, mb;
   const uint64_t wrows = (EPI == Q35_EPI_SWIGLU) ? 2 * (uint64_t)p.N : (uint64_t)p.N;
   if (!make_map(&ma, a, p.M, p.K, BM, INT8) ||
-      !make_map(&mb, w, wrows, p.K, EPI == Q35_EPI_SWIGLU ? BN / 2 : BN, INT8))
+      !make_map(&mb, w, wrows, p.K, EPI == Q35_EPI_SWIGLU ? TBN / 2 : TBN, INT8))
     return q35_fail(Q35_ECUDA, "gemm_tc: tensor map encoding failed");
-  cudaFuncSetAttribute(gemm_tc_kernel<INT8, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmem);
-  const int cols_per_tile = (EPI == Q35_EPI_SWIGLU) ? BN / 2 : BN;
+  cudaFuncSetAttribute(gemm_tc_kernel<INT8, EPI, TBN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       (int)smem_bytes(TBN));
+  const int cols_per_tile = (EPI == Q35_EPI_SWIGLU) ? TBN / 2 : TBN;
   dim3 grid((unsigned)((p.N + cols_per_tile - 1) / cols_per_tile), (unsigned)((p.M + BM - 1) / BM));
-  gemm_tc_kernel<INT8, EPI><<<grid, kThreads, kSmem, s>>>(ma, mb, p);
+  gemm_tc_kernel<INT8, EPI, TBN><<<grid, kThreads, smem_bytes(TBN), s>>>(ma, mb, p);
   return q35_check_launch("gemm_tc");
+}
+
+// 256-column tiles unless they leave most SMs idle (e.g. N = 2048 at M = 1024: 64 tiles), then 128.
+template <bool INT8, int EPI>
+int launch_tc(const void* a, const void* w, const TcParams& p, cudaStream_t s) {
+  const int cols256 = (EPI == Q35_EPI_SWIGLU) ? 128 : 256;
+  const int64_t tiles256 = (int64_t)((p.N + cols256 - 1) / cols256) * ((p.M + BM - 1) / BM);
+  if (tiles256 < kNumSMs) return launch_tc_bn<INT8, EPI, 128>(a, w, p, s);
+  return launch_tc_bn<INT8, EPI, 256>(a, w, p, s);
 }
 
 }  // namespace
