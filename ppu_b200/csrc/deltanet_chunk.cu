@@ -54,28 +54,43 @@ __global__ void __launch_bounds__(kThreads, 1) delta_chunk_prep_kernel(PrepParam
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int qkv_stride = 3 * H * kD;
 
-  // ---- load the chunk (bf16 -> fp32), zero padding past L
-  for (int i = tid; i < kC * 3 * (kD / 8); i += kThreads) {
-    const int r = i / (3 * kD / 8), rem = i % (3 * kD / 8);
-    const int which = rem / (kD / 8), col = (rem % (kD / 8)) * 8;
-    const int t = t0 + r;
-    float f[8];
-    if (t < L) {
-      const uint4 u = *reinterpret_cast<const uint4*>(p.qkv + ((int64_t)b * L + t) * qkv_stride + which * H * kD +
-                                                      h * kD + col);
-      unpack_bf16x8(u, f);
-    } else {
+  // ---- load the chunk (bf16 -> fp32), zero padding past L: every load issued before any use
+  constexpr int kLoads = kC * 3 * (kD / 8) / kThreads;  // 12 16-byte loads per thread
+  const float a_log = bf2f(p.a_log[h]), dt_bias = bf2f(p.dt_bias[h]);
+  const int a_off = 4 * H * kD, b_off = a_off + H;
+  __shared__ float araw[kC], braw[kC];
+  {
+    uint4 raw[kLoads];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) f[j] = 0.f;
+    for (int u = 0; u < kLoads; ++u) {
+      const int i = tid + u * kThreads;
+      const int r = i / (3 * kD / 8), rem = i % (3 * kD / 8);
+      const int which = rem / (kD / 8), col = (rem % (kD / 8)) * 8;
+      const int t = t0 + r;
+      raw[u] = (t < L) ? *reinterpret_cast<const uint4*>(p.qkv + ((int64_t)b * L + t) * qkv_stride + which * H * kD +
+                                                         h * kD + col)
+                       : make_uint4(0, 0, 0, 0);
     }
-    float* dst = (which == 0 ? q : which == 1 ? k : v) + r * kP + col;
+    if (tid < 2 * kC) {  // the token's a (tid < 64) or b (64 <= tid < 128) projection
+      const int r = tid % kC, t = t0 + r;
+      float v = 0.f;
+      if (t < L) v = bf2f(p.packed[((int64_t)b * L + t) * p.packed_stride + (tid < kC ? a_off : b_off) + h]);
+      (tid < kC ? araw : braw)[r] = v;
+    }
 #pragma unroll
-    for (int j = 0; j < 8; ++j) dst[j] = f[j];
+    for (int u = 0; u < kLoads; ++u) {
+      const int i = tid + u * kThreads;
+      const int r = i / (3 * kD / 8), rem = i % (3 * kD / 8);
+      const int which = rem / (kD / 8), col = (rem % (kD / 8)) * 8;
+      float f[8];
+      unpack_bf16x8(raw[u], f);
+      float* dst = (which == 0 ? q : which == 1 ? k : v) + r * kP + col;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) dst[j] = f[j];
+    }
   }
   __syncthreads();
   // ---- per-token factors (one warp per token)
-  const float a_log = bf2f(p.a_log[h]), dt_bias = bf2f(p.dt_bias[h]);
-  const int a_off = 4 * H * kD, b_off = a_off + H;
   for (int r = warp; r < kC; r += kThreads / 32) {
     float sq = 0.f, sk = 0.f;
     for (int e = lane; e < kD; e += 32) {
@@ -90,11 +105,10 @@ __global__ void __launch_bounds__(kThreads, 1) delta_chunk_prep_kernel(PrepParam
       const int t = t0 + r;
       float g = 0.f, bt = 0.f;
       if (t < L) {
-        const bf16* pr = p.packed + ((int64_t)b * L + t) * p.packed_stride;
-        const float a = bf2f(pr[a_off + h]) + dt_bias;
+        const float a = araw[r] + dt_bias;
         const float sp = a > 20.0f ? a : log1pf(expf(a));
         g = -expf(a_log) * sp;
-        bt = 1.0f / (1.0f + expf(-bf2f(pr[b_off + h])));
+        bt = 1.0f / (1.0f + expf(-braw[r]));
       }
       c[r] = g;
       beta[r] = bt;
@@ -150,18 +164,45 @@ __global__ void __launch_bounds__(kThreads, 1) delta_chunk_prep_kernel(PrepParam
       }
   }
   __syncthreads();
-  // ---- T = (I - A)^-1, forward substitution row by row (rows < i are final)
-  for (int i = 1; i < kC; ++i) {
-    float nv = 0.f;
-    if (tid < i) {
-      const int j = tid;
-      float s = 0.f;
-      for (int m = j + 1; m < i; ++m) s = fmaf(T[i * 65 + m], T[m * 65 + j], s);
-      nv = T[i * 65 + j] + s;
+  // ---- T = (I - A)^-1 (A strictly lower): T_ij = sum_{j <= m < i} A_im T_mj with T_jj = 1.
+  // Blocked in 16 x 16 blocks: (a) the four diagonal blocks by forward substitution in parallel;
+  // (b) block rows I = 1..3 in order: R_J = sum_{J <= K < I} A_IK T_KJ, then T_IJ = T_II R_J.
+  {
+    constexpr int B = 16;
+    const int blk = tid / 64, lt = tid % 64;
+    for (int r = 1; r < B; ++r) {  // (a) row r of every diagonal block
+      float nv = 0.f;
+      const int i = blk * B + r;
+      if (lt < r) {
+        const int jj = blk * B + lt;
+        float acc = T[i * 65 + jj];
+        for (int m = lt + 1; m < r; ++m) acc = fmaf(T[i * 65 + blk * B + m], T[(blk * B + m) * 65 + jj], acc);
+        nv = acc;
+      }
+      __syncthreads();
+      if (lt < r) T[i * 65 + blk * B + lt] = nv;
+      __syncthreads();
     }
-    __syncthreads();
-    if (tid < i) T[i * 65 + tid] = nv;
-    __syncthreads();
+    float* R = QK + kC * 65;  // [48][16] scratch after QK
+    for (int I = 1; I < kC / B; ++I) {
+      // (b1) R_J for J < I: element (J, r, cc), r = row in the block, cc = column in the block
+      for (int e = tid; e < I * B * B; e += kThreads) {
+        const int J = e / (B * B), r = (e / B) % B, cc = e % B;
+        const int row = I * B + r, col = J * B + cc;
+        float acc = T[row * 65 + col];  // K = J term with T_JJ's unit diagonal
+        for (int m = J * B + cc + 1; m < I * B; ++m) acc = fmaf(T[row * 65 + m], T[m * 65 + col], acc);
+        R[(J * B + r) * B + cc] = acc;
+      }
+      __syncthreads();
+      // (b2) T_IJ = T_II R_J (T_II unit lower triangular, strictly lower part in place)
+      for (int e = tid; e < I * B * B; e += kThreads) {
+        const int J = e / (B * B), r = (e / B) % B, cc = e % B;
+        float acc = R[(J * B + r) * B + cc];
+        for (int m = 0; m < r; ++m) acc = fmaf(T[(I * B + r) * 65 + I * B + m], R[(J * B + m) * B + cc], acc);
+        T[(I * B + r) * 65 + J * B + cc] = acc;
+      }
+      __syncthreads();
+    }
   }
   if (tid < kC) T[tid * 65 + tid] = 1.0f;
   __syncthreads();
@@ -380,7 +421,7 @@ __global__ void __launch_bounds__(kThreads, 1) delta_chunk_scan_kernel(ScanParam
   for (int i = tid; i < kD * kVS; i += kThreads) Sg[(i / kVS) * kD + (i % kVS)] = S[(i / kVS) * kPS + (i % kVS)];
 }
 
-constexpr size_t kPrepSmem = (size_t)(3 * kC * kP + 2 * kC * 65) * sizeof(float);
+constexpr size_t kPrepSmem = (size_t)(3 * kC * kP + 2 * kC * 65 + 48 * 16) * sizeof(float);
 constexpr size_t kScanSmem =
     (size_t)(2 * kC * kPW + kC * kPK2 + kC * kPP + kC * kVS + kC * kPS + kD * kPS) * sizeof(float);
 
