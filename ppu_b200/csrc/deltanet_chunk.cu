@@ -38,13 +38,15 @@ struct PrepParams {
   int L, H, NC, packed_stride;
 };
 
-__global__ void __launch_bounds__(kThreads, 1) delta_chunk_prep_kernel(PrepParams p) {
+// Shared memory is q, k, v only (~99 KB), so two CTAs share an SM: once the QK / KK products are in
+// registers, q is dead (Qe went to the workspace) and its region holds A / T and the solve scratch.
+__global__ void __launch_bounds__(kThreads, 2) delta_chunk_prep_kernel(PrepParams p) {
   extern __shared__ __align__(16) float sm[];
   float* q = sm;                 // [64][129]
   float* k = q + kC * kP;        // [64][129]
   float* v = k + kC * kP;        // [64][129]
-  float* T = v + kC * kP;        // [64][65]  A then T
-  float* QK = T + kC * 65;       // [64][65]
+  float* T = q;                  // [64][65]  A then T, after q is dead
+  float* R = T + kC * 65;        // [48][16]  solve scratch
   __shared__ float c[kC], beta[kC], qs[kC], ks[kC];
   const int ch = blockIdx.x % p.NC;
   const int h = (blockIdx.x / p.NC) % p.H;
@@ -130,6 +132,14 @@ __global__ void __launch_bounds__(kThreads, 1) delta_chunk_prep_kernel(PrepParam
     k[r * kP + e] = k[r * kP + e] * ks[r];
   }
   __syncthreads();
+  float* out = p.ws + ((size_t)(b * H + h) * p.NC + ch) * ChunkWs::SIZE;
+  const float cl = c[kC - 1];
+  for (int i = tid; i < kC * kD; i += kThreads) {
+    const int r = i / kD, e = i % kD;
+    out[ChunkWs::Qe + i] = q[r * kP + e] * expf(c[r]);
+    out[ChunkWs::Kd + i] = k[r * kP + e] * expf(cl - c[r]);
+  }
+  if (tid == 0) out[ChunkWs::GL] = expf(cl);
   // ---- KK and QK (64 x 64): thread (ti, tj) owns a 4 x 4 block
   {
     const int ti = tid / 16, tj = tid % 16;
@@ -154,14 +164,19 @@ __global__ void __launch_bounds__(kThreads, 1) delta_chunk_prep_kernel(PrepParam
           qk[a][bb] = fmaf(qi[a], kj[bb], qk[a][bb]);
         }
     }
+    __syncthreads();  // every thread is done reading q: its region becomes T
 #pragma unroll
-    for (int a = 0; a < 4; ++a)
+    for (int a = 0; a < 4; ++a) {
+      const int i = 4 * ti + a;
+      float pr[4];
 #pragma unroll
       for (int bb = 0; bb < 4; ++bb) {
-        const int i = 4 * ti + a, j = 4 * tj + bb;
+        const int j = 4 * tj + bb;
         T[i * 65 + j] = (j < i) ? -(beta[i] * kk[a][bb]) * expf(c[i] - c[j]) : 0.f;
-        QK[i * 65 + j] = (j <= i) ? qk[a][bb] * expf(c[i] - c[j]) : 0.f;
+        pr[bb] = (j <= i) ? qk[a][bb] * expf(c[i] - c[j]) : 0.f;
       }
+      *reinterpret_cast<float4*>(out + ChunkWs::P + i * kC + 4 * tj) = make_float4(pr[0], pr[1], pr[2], pr[3]);
+    }
   }
   __syncthreads();
   // ---- T = (I - A)^-1 (A strictly lower): T_ij = sum_{j <= m < i} A_im T_mj with T_jj = 1.
@@ -183,7 +198,6 @@ __global__ void __launch_bounds__(kThreads, 1) delta_chunk_prep_kernel(PrepParam
       if (lt < r) T[i * 65 + blk * B + lt] = nv;
       __syncthreads();
     }
-    float* R = QK + kC * 65;  // [48][16] scratch after QK
     for (int I = 1; I < kC / B; ++I) {
       // (b1) R_J for J < I: element (J, r, cc), r = row in the block, cc = column in the block
       for (int e = tid; e < I * B * B; e += kThreads) {
@@ -207,7 +221,6 @@ __global__ void __launch_bounds__(kThreads, 1) delta_chunk_prep_kernel(PrepParam
   if (tid < kC) T[tid * 65 + tid] = 1.0f;
   __syncthreads();
   // ---- U = T diag(beta) V, W = T diag(beta exp(c)) K; thread owns column e and 32 rows
-  float* out = p.ws + ((size_t)(b * H + h) * p.NC + ch) * ChunkWs::SIZE;
   {
     const int e = tid % kD, i0 = (tid / kD) * 32;
     float u[32], w[32];
@@ -229,14 +242,6 @@ __global__ void __launch_bounds__(kThreads, 1) delta_chunk_prep_kernel(PrepParam
       out[ChunkWs::W + (i0 + a) * kD + e] = w[a];
     }
   }
-  const float cl = c[kC - 1];
-  for (int i = tid; i < kC * kD; i += kThreads) {
-    const int r = i / kD, e = i % kD;
-    out[ChunkWs::Qe + i] = q[r * kP + e] * expf(c[r]);
-    out[ChunkWs::Kd + i] = k[r * kP + e] * expf(cl - c[r]);
-  }
-  for (int i = tid; i < kC * kC; i += kThreads) out[ChunkWs::P + i] = QK[(i / kC) * 65 + (i % kC)];
-  if (tid == 0) out[ChunkWs::GL] = expf(cl);
 }
 
 struct ScanParams {
@@ -263,42 +268,58 @@ Q35_DEV void mma_tf32(float d[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
-// d += A[16 x 8] * B[8 x 8] for one k-step; a = {A[g][c], A[g+8][c], A[g][c+4], A[g+8][c+4]},
-// b = {B[c][g], B[c+4][g]} (g = lane / 4, c = lane % 4).
-Q35_DEV void mma3(float d[4], const float a[4], const float b[2]) {
-  uint32_t ah[4], al[4], bh[2], bl[2];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) split_tf32(a[i], ah[i], al[i]);
-  split_tf32(b[0], bh[0], bl[0]);
-  split_tf32(b[1], bh[1], bl[1]);
-  mma_tf32(d, al[0], al[1], al[2], al[3], bh[0], bh[1]);
-  mma_tf32(d, ah[0], ah[1], ah[2], ah[3], bl[0], bl[1]);
-  mma_tf32(d, ah[0], ah[1], ah[2], ah[3], bh[0], bh[1]);
-}
+// Fragments of m16n8k8 (g = lane / 4, c = lane % 4): a = {A[g][c], A[g+8][c], A[g][c+4], A[g+8][c+4]},
+// b = {B[c][g], B[c+4][g]}, d = {D[g][2c], D[g][2c+1], D[g+8][2c], D[g+8][2c+1]}.
 
 Q35_DEV void cp_async16(float* dst, const float* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
                : "memory");
 }
 
-constexpr int kPS = 24;   // row stride (floats) of S / Vn tiles: B-fragment loads hit distinct banks
+constexpr int kPS = 24;   // row stride (words) of the pre-split S / Vn tiles: B-fragment loads hit distinct banks
 constexpr int kPP = 68;   // row stride of P
-constexpr int kPK2 = 132; // row stride of Kd (read transposed as the A operand of Kd^T Vn)
+constexpr int kPK2 = 136; // row stride of Kd (read transposed as the A operand of Kd^T Vn: distinct banks)
 
-// Phase B on the tensor cores: the CTA's 8 warps split every product into 16 x 8 output tiles.
-//   Vn (64 x 16) = U - W S        warp w: rows 16 (w & 3), cols 8 (w >> 2), K = 128
-//   O  (64 x 16) = Qe S + P Vn    same tiles, K = 128 + 64
-//   S' (128 x 16) = gl S + Kd^T Vn  warp w: rows 16 w, both column tiles, K = 64
+// A fragment (16 x 8, row-major at `base` with row stride ld), split into TF32 high / low parts.
+Q35_DEV void load_a_split(const float* base, int ld, int g, int c, uint32_t hi[4], uint32_t lo[4]) {
+  const float a[4] = {base[g * ld + c], base[(g + 8) * ld + c], base[g * ld + c + 4], base[(g + 8) * ld + c + 4]};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) split_tf32(a[i], hi[i], lo[i]);
+}
+// Transposed A fragment: A[m][t] = base[t * ld + m].
+Q35_DEV void load_at_split(const float* base, int ld, int g, int c, uint32_t hi[4], uint32_t lo[4]) {
+  const float a[4] = {base[c * ld + g], base[c * ld + g + 8], base[(c + 4) * ld + g], base[(c + 4) * ld + g + 8]};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) split_tf32(a[i], hi[i], lo[i]);
+}
+// d += A * B[k0 .. k0 + 8][n0 .. n0 + 8] in 3xTF32, B given as pre-split [k][kPS] high / low tiles.
+Q35_DEV void mma3s(float d[4], const uint32_t ah[4], const uint32_t al[4], const uint32_t* Bh, const uint32_t* Bl,
+                   int k0, int n0, int g, int c) {
+  const int i0 = (k0 + c) * kPS + n0 + g, i1 = i0 + 4 * kPS;
+  const uint32_t bh0 = Bh[i0], bh1 = Bh[i1], bl0 = Bl[i0], bl1 = Bl[i1];
+  mma_tf32(d, al[0], al[1], al[2], al[3], bh0, bh1);
+  mma_tf32(d, ah[0], ah[1], ah[2], ah[3], bl0, bl1);
+  mma_tf32(d, ah[0], ah[1], ah[2], ah[3], bh0, bh1);
+}
+
+// Phase B on the tensor cores. Warp w owns the FP32 state tile S[16 w .. 16 w + 16][0 .. 16] in
+// registers across chunks; S and Vn also live in shared memory pre-split into TF32 high / low
+// parts (the B operands), so each value is split once per chunk rather than once per reader.
+//   phase 1: X = [W; Qe] S (128 x 16, K = 128), warp w rows 16 w;  warps 0-3: Vn = U - W S
+//   phase 2: warps 4-7: O = Qe S + P Vn (K = 64);  every warp: S <- gl S + Kd^T Vn on its tile
+// Records arrive in two cp.async groups: {W, Qe, U} for chunk n + 1 is issued once phase 1 of
+// chunk n is done, {P, Kd} once phase 2 is done.
 __global__ void __launch_bounds__(kThreads, 1) delta_chunk_scan_kernel(ScanParams p) {
   extern __shared__ __align__(16) float sm[];
   float* W = sm;                   // [64][132]
   float* Qe = W + kC * kPW;        // [64][132]
-  float* Kd = Qe + kC * kPW;       // [64][132]
+  float* Kd = Qe + kC * kPW;       // [64][136]
   float* P = Kd + kC * kPK2;       // [64][68]
   float* U = P + kC * kPP;         // [64][16]
-  float* Vn = U + kC * kVS;        // [64][24]
-  float* S = Vn + kC * kPS;        // [128][24]
-  __shared__ float gl_s;
+  uint32_t* Vh = reinterpret_cast<uint32_t*>(U + kC * kVS);  // [64][24]
+  uint32_t* Vl = Vh + kC * kPS;    // [64][24]
+  uint32_t* Sh = Vl + kC * kPS;    // [128][24]
+  uint32_t* Sl = Sh + kD * kPS;    // [128][24]
   const int nvs = kD / kVS;
   const int vs = blockIdx.x % nvs;
   const int h = (blockIdx.x / nvs) % p.H;
@@ -306,124 +327,147 @@ __global__ void __launch_bounds__(kThreads, 1) delta_chunk_scan_kernel(ScanParam
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, c = lane & 3;
   float* Sg = p.state + ((size_t)(b * p.H + h) * kD) * kD + vs * kVS;
-  for (int i = tid; i < kD * kVS; i += kThreads) S[(i / kVS) * kPS + (i % kVS)] = Sg[(i / kVS) * kD + (i % kVS)];
-  const int mt = warp & 3, nt = warp >> 2;  // Vn / O tile of this warp
-  for (int ch = 0; ch < p.NC; ++ch) {
-    const float* rec = p.ws + ((size_t)(b * p.H + h) * p.NC + ch) * ChunkWs::SIZE;
-    __syncthreads();
-    // the chunk record: all copies in flight at once (cp.async), one wait
+  auto frag_row = [&](int i) { return warp * 16 + g + (i >= 2 ? 8 : 0); };
+  auto frag_col = [&](int nt, int i) { return nt * 8 + 2 * c + (i & 1); };
+  float s[2][4];  // this warp's state tile: [n-tile][mma fragment]
+#pragma unroll
+  for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) s[nt][i] = Sg[frag_row(i) * kD + frag_col(nt, i)];
+  auto publish_s = [&]() {
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int o = frag_row(i) * kPS + frag_col(nt, i);
+        split_tf32(s[nt][i], Sh[o], Sl[o]);
+      }
+  };
+  publish_s();
+  auto rec_of = [&](int ch) { return p.ws + ((size_t)(b * p.H + h) * p.NC + ch) * ChunkWs::SIZE; };
+  auto issue_g1 = [&](int ch) {  // W, Qe, U
+    const float* rec = rec_of(ch);
     for (int i = tid; i < kC * kD / 4; i += kThreads) {
       const int r = i / (kD / 4), c4 = (i % (kD / 4)) * 4;
       cp_async16(W + r * kPW + c4, rec + ChunkWs::W + r * kD + c4);
       cp_async16(Qe + r * kPW + c4, rec + ChunkWs::Qe + r * kD + c4);
+    }
+    for (int i = tid; i < kC * kVS / 4; i += kThreads) {
+      const int r = i / (kVS / 4), c4 = (i % (kVS / 4)) * 4;
+      cp_async16(U + r * kVS + c4, rec + ChunkWs::U + r * kD + vs * kVS + c4);
+    }
+  };
+  auto issue_g2 = [&](int ch) {  // P, Kd
+    const float* rec = rec_of(ch);
+    for (int i = tid; i < kC * kD / 4; i += kThreads) {
+      const int r = i / (kD / 4), c4 = (i % (kD / 4)) * 4;
       cp_async16(Kd + r * kPK2 + c4, rec + ChunkWs::Kd + r * kD + c4);
     }
     for (int i = tid; i < kC * kC / 4; i += kThreads) {
       const int r = i / (kC / 4), c4 = (i % (kC / 4)) * 4;
       cp_async16(P + r * kPP + c4, rec + ChunkWs::P + r * kC + c4);
     }
-    for (int i = tid; i < kC * kVS / 4; i += kThreads) {
-      const int r = i / (kVS / 4), c4 = (i % (kVS / 4)) * 4;
-      cp_async16(U + r * kVS + c4, rec + ChunkWs::U + r * kD + vs * kVS + c4);
-    }
-    asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
-    if (tid == 0) gl_s = rec[ChunkWs::GL];
-    __syncthreads();
-    const int r0 = mt * 16 + g, n0 = nt * 8;
-    // ---- Vn = U - W S
+  };
+  auto commit = [] { asm volatile("cp.async.commit_group;" ::: "memory"); };
+  if (p.NC > 0) {
+    issue_g1(0);
+    commit();
+    issue_g2(0);
+    commit();
+  }
+  for (int ch = 0; ch < p.NC; ++ch) {
+    const bool more = ch + 1 < p.NC;
+    asm volatile("cp.async.wait_group 1;" ::: "memory");  // pending: G1(ch), G2(ch)
+    __syncthreads();  // W, Qe, U of this chunk and the published S are visible
+    // ---- phase 1: X = [W; Qe] S for rows 16 warp .. + 16 (four chains: n-tile x even / odd k-step)
+    float x[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
     {
-      float d[4] = {0.f, 0.f, 0.f, 0.f}, e[4] = {0.f, 0.f, 0.f, 0.f};  // two chains: even / odd k-steps
-#pragma unroll 4
+      float y[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+      const float* A = warp < 4 ? W + warp * 16 * kPW : Qe + (warp - 4) * 16 * kPW;
+#pragma unroll 2
       for (int k0 = 0; k0 < kD; k0 += 16) {
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh) {
           const int k = k0 + 8 * hh;
-          const float a[4] = {W[r0 * kPW + k + c], W[(r0 + 8) * kPW + k + c], W[r0 * kPW + k + c + 4],
-                              W[(r0 + 8) * kPW + k + c + 4]};
-          const float bb[2] = {S[(k + c) * kPS + n0 + g], S[(k + c + 4) * kPS + n0 + g]};
-          mma3(hh ? e : d, a, bb);
+          uint32_t ah[4], al[4];
+          load_a_split(A + k, kPW, g, c, ah, al);
+          mma3s(hh ? y[0] : x[0], ah, al, Sh, Sl, k, 0, g, c);
+          mma3s(hh ? y[1] : x[1], ah, al, Sh, Sl, k, 8, g, c);
         }
       }
 #pragma unroll
-      for (int i = 0; i < 4; ++i) d[i] += e[i];
-      const int col = n0 + 2 * c;
-      Vn[r0 * kPS + col] = U[r0 * kVS + col] - d[0];
-      Vn[r0 * kPS + col + 1] = U[r0 * kVS + col + 1] - d[1];
-      Vn[(r0 + 8) * kPS + col] = U[(r0 + 8) * kVS + col] - d[2];
-      Vn[(r0 + 8) * kPS + col + 1] = U[(r0 + 8) * kVS + col + 1] - d[3];
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) x[nt][i] += y[nt][i];
     }
-    __syncthreads();
-    // ---- O = Qe S + P Vn (rows r0, r0 + 8; columns n0 + 2c, +1)
-    {
-      float d[4] = {0.f, 0.f, 0.f, 0.f}, e[4] = {0.f, 0.f, 0.f, 0.f};  // Qe S and P Vn in separate chains
+    if (warp < 4) {  // Vn = U - W S (token rows 16 warp + g (+8)), published pre-split
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int r = frag_row(i), col = frag_col(nt, i);
+          split_tf32(U[r * kVS + col] - x[nt][i], Vh[r * kPS + col], Vl[r * kPS + col]);
+        }
+    }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");  // pending: G2(ch)
+    __syncthreads();  // Vn, P, Kd visible; W, Qe, U free
+    if (more) issue_g1(ch + 1);
+    commit();
+    // ---- phase 2a: O = Qe S + P Vn for token rows 16 (warp - 4) .. + 16
+    if (warp >= 4) {
+      const int r = (warp - 4) * 16;
+      float e[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
 #pragma unroll 4
       for (int k0 = 0; k0 < kC; k0 += 8) {
-        {
-          const float a[4] = {Qe[r0 * kPW + k0 + c], Qe[(r0 + 8) * kPW + k0 + c], Qe[r0 * kPW + k0 + c + 4],
-                              Qe[(r0 + 8) * kPW + k0 + c + 4]};
-          const float bb[2] = {S[(k0 + c) * kPS + n0 + g], S[(k0 + c + 4) * kPS + n0 + g]};
-          mma3(d, a, bb);
-        }
-        {
-          const int k = kC + k0;
-          const float a[4] = {Qe[r0 * kPW + k + c], Qe[(r0 + 8) * kPW + k + c], Qe[r0 * kPW + k + c + 4],
-                              Qe[(r0 + 8) * kPW + k + c + 4]};
-          const float bb[2] = {S[(k + c) * kPS + n0 + g], S[(k + c + 4) * kPS + n0 + g]};
-          mma3(d, a, bb);
-        }
-        const float a[4] = {P[r0 * kPP + k0 + c], P[(r0 + 8) * kPP + k0 + c], P[r0 * kPP + k0 + c + 4],
-                            P[(r0 + 8) * kPP + k0 + c + 4]};
-        const float bb[2] = {Vn[(k0 + c) * kPS + n0 + g], Vn[(k0 + c + 4) * kPS + n0 + g]};
-        mma3(e, a, bb);
+        uint32_t ah[4], al[4];
+        load_a_split(P + r * kPP + k0, kPP, g, c, ah, al);
+        mma3s(e[0], ah, al, Vh, Vl, k0, 0, g, c);
+        mma3s(e[1], ah, al, Vh, Vl, k0, 8, g, c);
       }
 #pragma unroll
-      for (int i = 0; i < 4; ++i) d[i] += e[i];
-      const int col = vs * kVS + n0 + 2 * c;
-      const int t0 = ch * kC + r0, t1 = t0 + 8;
-      if (t0 < p.L) {
-        bf16* o = p.out + (((int64_t)b * p.L + t0) * p.H + h) * kD + col;
-        o[0] = f2bf(d[0]);
-        o[1] = f2bf(d[1]);
-      }
-      if (t1 < p.L) {
-        bf16* o = p.out + (((int64_t)b * p.L + t1) * p.H + h) * kD + col;
-        o[0] = f2bf(d[2]);
-        o[1] = f2bf(d[3]);
+      for (int half = 0; half < 2; ++half) {
+        const int t = ch * kC + r + g + 8 * half;
+        if (t < p.L) {
+          bf16* o = p.out + (((int64_t)b * p.L + t) * p.H + h) * kD + vs * kVS;
+#pragma unroll
+          for (int nt = 0; nt < 2; ++nt) {
+            o[nt * 8 + 2 * c] = f2bf(x[nt][2 * half] + e[nt][2 * half]);
+            o[nt * 8 + 2 * c + 1] = f2bf(x[nt][2 * half + 1] + e[nt][2 * half + 1]);
+          }
+        }
       }
     }
-    // ---- S' = gl S + Kd^T Vn (rows 16 warp + g (+8); columns 8 n + 2c (+1), n = 0, 1)
+    // ---- phase 2b: S <- gl S + Kd^T Vn on this warp's tile (rows 16 warp .. + 16)
     {
-      float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
-      const int m0 = warp * 16 + g;
+      float d[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
 #pragma unroll 4
       for (int k0 = 0; k0 < kC; k0 += 8) {
-        const float a[4] = {Kd[(k0 + c) * kPK2 + m0], Kd[(k0 + c) * kPK2 + m0 + 8], Kd[(k0 + c + 4) * kPK2 + m0],
-                            Kd[(k0 + c + 4) * kPK2 + m0 + 8]};
-        const float b0[2] = {Vn[(k0 + c) * kPS + g], Vn[(k0 + c + 4) * kPS + g]};
-        const float b1[2] = {Vn[(k0 + c) * kPS + 8 + g], Vn[(k0 + c + 4) * kPS + 8 + g]};
-        mma3(d0, a, b0);
-        mma3(d1, a, b1);
+        uint32_t ah[4], al[4];
+        load_at_split(Kd + k0 * kPK2 + warp * 16, kPK2, g, c, ah, al);
+        mma3s(d[0], ah, al, Vh, Vl, k0, 0, g, c);
+        mma3s(d[1], ah, al, Vh, Vl, k0, 8, g, c);
       }
-      const float gl = gl_s;
-      __syncthreads();  // every warp is done reading S for this chunk
-      const int col = 2 * c;
-      S[m0 * kPS + col] = gl * S[m0 * kPS + col] + d0[0];
-      S[m0 * kPS + col + 1] = gl * S[m0 * kPS + col + 1] + d0[1];
-      S[(m0 + 8) * kPS + col] = gl * S[(m0 + 8) * kPS + col] + d0[2];
-      S[(m0 + 8) * kPS + col + 1] = gl * S[(m0 + 8) * kPS + col + 1] + d0[3];
-      S[m0 * kPS + 8 + col] = gl * S[m0 * kPS + 8 + col] + d1[0];
-      S[m0 * kPS + 8 + col + 1] = gl * S[m0 * kPS + 8 + col + 1] + d1[1];
-      S[(m0 + 8) * kPS + 8 + col] = gl * S[(m0 + 8) * kPS + 8 + col] + d1[2];
-      S[(m0 + 8) * kPS + 8 + col + 1] = gl * S[(m0 + 8) * kPS + 8 + col + 1] + d1[3];
+      const float gl = rec_of(ch)[ChunkWs::GL];
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) s[nt][i] = gl * s[nt][i] + d[nt][i];
+      publish_s();  // phase 1 readers of Sh / Sl all passed the last barrier
     }
+    __syncthreads();  // P, Kd, Vn free
+    if (more) issue_g2(ch + 1);
+    commit();
   }
-  __syncthreads();
-  for (int i = tid; i < kD * kVS; i += kThreads) Sg[(i / kVS) * kD + (i % kVS)] = S[(i / kVS) * kPS + (i % kVS)];
+#pragma unroll
+  for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) Sg[frag_row(i) * kD + frag_col(nt, i)] = s[nt][i];
 }
 
-constexpr size_t kPrepSmem = (size_t)(3 * kC * kP + 2 * kC * 65 + 48 * 16) * sizeof(float);
+constexpr size_t kPrepSmem = (size_t)(3 * kC * kP) * sizeof(float);
+static_assert(kC * 65 + 48 * 16 <= kC * kP, "T and the solve scratch fit in q's region");
 constexpr size_t kScanSmem =
-    (size_t)(2 * kC * kPW + kC * kPK2 + kC * kPP + kC * kVS + kC * kPS + kD * kPS) * sizeof(float);
+    (size_t)(2 * kC * kPW + kC * kPK2 + kC * kPP + kC * kVS + 2 * kC * kPS + 2 * kD * kPS) * sizeof(float);
 
 }  // namespace
 
