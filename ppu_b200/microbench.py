@@ -139,8 +139,9 @@ def run(kernels: list[str], reps: int, layers: int = 24, a8w8: bool = False):
             report(name, t, nbytes=2 * 16 * 128 * 128 * 4 + 3 * 6144 * 4 * 2)
         elif name.startswith("gemm_tc"):
             m = 1024
-            for (n, k, epi, label) in ((8224, H, L.EPI_STORE, "in_proj"), (2 * I, H, L.EPI_SWIGLU, "gate_up"),
-                                       (H, I, L.EPI_RESIDUAL, "down")):
+            for (n, k, epi, label) in ((8224, H, L.EPI_STORE, "in_proj"), (5120, H, L.EPI_STORE, "qgkv"),
+                                       (2 * I, H, L.EPI_SWIGLU, "gate_up"), (H, I, L.EPI_RESIDUAL, "down"),
+                                       (H, H, L.EPI_RESIDUAL, "out_proj")):
                 a = torch.randn(m, k, device=dev, generator=g).to(torch.bfloat16)
                 wt = (torch.randn(n, k, device=dev, generator=g) * 0.02).to(torch.bfloat16)
                 r = torch.zeros(m, H, device=dev, dtype=torch.bfloat16)
