@@ -1,17 +1,24 @@
 // Prefill projections on the 5th-generation tensor cores (tcgen05 + TMEM + TMA), sm_100a.
 //
 // C[M, N] = A[M, K] . W[N, K]^T with BF16 inputs / FP32 accumulation (kind::f16), or int8 inputs /
-// exact int32 accumulation (kind::i8, A8W8). One CTA computes a 128 x 256 tile:
-//   warp 0 lane 0  TMA producer: A box 128 x 128 B and W box 256 x 128 B per stage (128-byte
-//                  swizzle, K-major), 4-stage ring guarded by full/empty mbarriers;
-//   warp 1 lane 0  MMA issuer: 4 x tcgen05.mma (K = 16 bf16 / 32 int8 each) per stage into a
-//                  128 x 256 FP32/S32 accumulator in TMEM; tcgen05.commit frees the stage;
-//   warps 0-3      epilogue: tcgen05.ld 32 columns at a time from the warp's 32 TMEM lanes,
-//                  dequantise (int8), and store / add to the residual / apply SwiGLU.
-// SwiGLU tiles load W rows [o0, o0+128) (gate) and [N+o0, N+o0+128) (up) as the two halves of
-// the 256-row B tile, so gate and up of an output sit 128 TMEM columns apart.
+// exact int32 accumulation (kind::i8, A8W8). Persistent: one CTA per SM walks the 128 x TBN output
+// tiles (TBN = 256, or 128 when that fills the machine in fewer waves) in M-fastest order, so the
+// CTAs running at once share each weight tile. Warp roles:
+//   warp 0 lane 0  TMA producer: A box 128 x 128 B and W box TBN x 128 B per stage (128-byte
+//                  swizzle, K-major) into a 4-stage ring guarded by full / empty mbarriers
+//                  (6 stages, or L2 prefetches of the weight boxes ahead of their loads, measured
+//                  no faster / 30-50 % slower);
+//   warp 1 lane 0  MMA issuer: 4 x tcgen05.mma (K = 16 bf16 / 32 int8 each) per stage into one of
+//                  two 128 x TBN FP32/S32 TMEM accumulators; tcgen05.commit frees the stage and,
+//                  after a tile's last stage, hands the accumulator to the epilogue;
+//   warps 2-5      epilogue: tcgen05.ld 32 columns at a time from the warp's 32 TMEM lanes,
+//                  dequantise (int8), store / add to the residual / apply SwiGLU, then release the
+//                  accumulator, while the MMA warp already fills the other one.
+// SwiGLU tiles load W rows [o0, o0+TBN/2) (gate) and [N+o0, N+o0+TBN/2) (up) as the two halves of
+// the B tile, so gate and up of an output sit TBN/2 TMEM columns apart.
 // No cluster multicast anywhere (loads are per CTA). Every mbarrier wait is bounded by a clock
-// budget; a wait that gives up records an error code in q35_tc_error and lets the CTA finish.
+// budget; a wait that gives up records an error code in q35_tc_error and raises a CTA-wide abort
+// flag that ends every role's loop.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -24,10 +31,10 @@ __device__ int q35_tc_error_word = 0;
 namespace {
 
 constexpr int BM = 128, BKB = 128;  // tile rows, K bytes per stage (tile cols: 256, or 128 for narrow N)
-constexpr int kStages = 4;
 constexpr int kABytes = BM * BKB;   // 16 KB
-constexpr int kThreads = 128;
+constexpr int kThreads = 192;       // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
 constexpr long long kWaitBudget = 4000000000LL;  // ~2 s at 2 GHz
+constexpr int stages_for(int) { return 4; }
 
 struct TcParams {
   void* out;          // bf16 [M, N] or int32 (RAW)
@@ -39,7 +46,11 @@ struct TcParams {
 
 Q35_DEV uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
-Q35_DEV bool mbar_wait(uint32_t bar, uint32_t parity) {
+Q35_DEV void report(int code);
+
+// Bounded wait for the phase of `parity` to complete. Gives up (false) when another role raised
+// the CTA's abort flag, or after the clock budget, raising the flag and recording `code`.
+Q35_DEV bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag, int code) {
   const long long t0 = clock64();
   while (true) {
     uint32_t ok;
@@ -51,8 +62,17 @@ Q35_DEV bool mbar_wait(uint32_t bar, uint32_t parity) {
         : "r"(bar), "r"(parity)
         : "memory");
     if (ok) return true;
-    if (clock64() - t0 > kWaitBudget) return false;
+    if (*abort_flag) return false;
+    if (clock64() - t0 > kWaitBudget) {
+      *abort_flag = 1;
+      report(code);
+      return false;
+    }
   }
+}
+
+Q35_DEV void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
 
 Q35_DEV void mbar_init(uint32_t bar, uint32_t count) {
@@ -118,30 +138,39 @@ Q35_DEV void report(int code) { atomicCAS(&q35_tc_error_word, 0, code); }
 template <bool INT8, int EPI, int TBN>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, TcParams p) {
+  constexpr int S = stages_for(TBN);
   constexpr int kBB = TBN * BKB;  // B bytes per stage
+  constexpr int kCols = (EPI == Q35_EPI_SWIGLU) ? TBN / 2 : TBN;  // output columns per tile
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   unsigned char* sA = smem;
-  unsigned char* sB = smem + kStages * kABytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + kStages * kBB);  // full[S], empty[S], done
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kStages + 1);
+  unsigned char* sB = smem + S * kABytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + S * kBB);  // full[S], empty[S], tfull[2], tempty[2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 4);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m0 = blockIdx.y * BM;
-  const int col0 = blockIdx.x * (EPI == Q35_EPI_SWIGLU ? TBN / 2 : TBN);  // first output column
-  const int n_k = p.K / (BKB / (INT8 ? 1 : 2));
-  const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + kStages), done = smem_u32(bars + 2 * kStages);
+  const int kstep = BKB / (INT8 ? 1 : 2);  // K elements per stage
+  const int n_k = p.K / kstep;
+  const int num_m = (p.M + BM - 1) / BM;
+  const int ntiles = num_m * ((p.N + kCols - 1) / kCols);
+  const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + S);
+  const uint32_t tfull0 = smem_u32(bars + 2 * S), tempty0 = smem_u32(bars + 2 * S + 2);
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < S; ++s) {
       mbar_init(full0 + 8 * s, 1);
       mbar_init(empty0 + 8 * s, 1);
     }
-    mbar_init(done, 1);
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(tfull0 + 8 * a, 1);
+      mbar_init(tempty0 + 8 * a, 4);  // one arrival per epilogue warp
+    }
+    *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "r"(TBN)
+                 "r"(2 * TBN)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
@@ -149,117 +178,144 @@ __global__ void __launch_bounds__(kThreads, 1)
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0 && lane == 0) {
-    // ---------------- TMA producer
-    for (int kt = 0; kt < n_k; ++kt) {
-      const int s = kt % kStages, r = kt / kStages;
-      if (r > 0 && !mbar_wait(empty0 + 8 * s, (r - 1) & 1)) {
-        report(1);
-        break;
-      }
-      mbar_expect_tx(full0 + 8 * s, kABytes + kBB);
-      const int kx = kt * (BKB / (INT8 ? 1 : 2));
-      tma_load_2d(smem_u32(sA + s * kABytes), &tmA, kx, m0, full0 + 8 * s);
-      if (EPI == Q35_EPI_SWIGLU) {
-        tma_load_2d(smem_u32(sB + s * kBB), &tmB, kx, col0, full0 + 8 * s);
-        tma_load_2d(smem_u32(sB + s * kBB + kBB / 2), &tmB, kx, p.N + col0, full0 + 8 * s);
-      } else {
-        tma_load_2d(smem_u32(sB + s * kBB), &tmB, kx, col0, full0 + 8 * s);
-      }
-    }
-  } else if (warp == 1 && lane == 0) {
-    // ---------------- MMA issuer
-    // instruction descriptor: D fp32 (1) / s32 (2); A, B bf16 (1) / signed int8 (1); K-major;
-    // N = TBN (>> 3 at bit 17), M = 128 (>> 4 at bit 24)
-    const uint32_t idesc = ((INT8 ? 2u : 1u) << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(TBN >> 3) << 17) |
-                           ((uint32_t)(BM >> 4) << 24);
-    bool ok = true;
-    for (int kt = 0; kt < n_k && ok; ++kt) {
-      const int s = kt % kStages, r = kt / kStages;
-      if (!mbar_wait(full0 + 8 * s, r & 1)) {
-        report(2);
-        ok = false;
-        break;
-      }
-      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      const uint32_t a0 = smem_u32(sA + s * kABytes), b0 = smem_u32(sB + s * kBB);
-#pragma unroll
-      for (int k = 0; k < BKB / 32; ++k)  // 32 bytes of K per MMA
-        mma<INT8>(tmem, smem_desc(a0 + 32 * k), smem_desc(b0 + 32 * k), idesc, (kt > 0 || k > 0) ? 1u : 0u);
-      mma_commit(empty0 + 8 * s);
-    }
-    mma_commit(done);
-  }
-  __syncwarp();
-
-  // ---------------- epilogue: warp w owns TMEM lanes / tile rows [32w, 32w + 32)
-  const bool ready = mbar_wait(done, 0);
-  if (!ready) report(3);
-  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-  const int row = m0 + warp * 32 + lane;
-  const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
-  if (ready) {
-    const int ncols = (EPI == Q35_EPI_SWIGLU) ? TBN / 2 : TBN;
-    for (int c = 0; c < ncols; c += 32) {
-      uint32_t v[32], u[32];
-      tmem_ld32(trow + c, v);
-      if (EPI == Q35_EPI_SWIGLU) tmem_ld32(trow + TBN / 2 + c, u);
-      if (row >= p.M) continue;
-      const int gc = col0 + c;
-      float y[32];
-#pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        if (INT8) {
-          const int col = gc + j;
-          y[j] = (col < p.N) ? ((float)(int)v[j] * p.sx[row]) * p.sw[col] : 0.f;
-        } else {
-          y[j] = __uint_as_float(v[j]);
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer
+      int it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
+        const int m0 = (tile % num_m) * BM, c0 = (tile / num_m) * kCols;
+        for (int kt = 0; kt < n_k; ++kt, ++it) {
+          const int s = it % S, r = it / S;
+          if (r > 0 && !mbar_wait(empty0 + 8 * s, (r - 1) & 1, abort_flag, 1)) {
+            ok = false;
+            break;
+          }
+          mbar_expect_tx(full0 + 8 * s, kABytes + kBB);
+          const int kx = kt * kstep;
+          tma_load_2d(smem_u32(sA + s * kABytes), &tmA, kx, m0, full0 + 8 * s);
+          if (EPI == Q35_EPI_SWIGLU) {
+            tma_load_2d(smem_u32(sB + s * kBB), &tmB, kx, c0, full0 + 8 * s);
+            tma_load_2d(smem_u32(sB + s * kBB + kBB / 2), &tmB, kx, p.N + c0, full0 + 8 * s);
+          } else {
+            tma_load_2d(smem_u32(sB + s * kBB), &tmB, kx, c0, full0 + 8 * s);
+          }
         }
       }
-      if (EPI == Q35_EPI_SWIGLU) {
+      // drain: every copy this thread issued has landed before the CTA can exit
+      // (only matters after an abort: otherwise the MMA warp consumed them all)
+      static __shared__ int no_abort;  // a flag nobody raises: these waits end on landing or budget
+      no_abort = 0;
+      for (int j = it - S > 0 ? it - S : 0; j < it; ++j)
+        mbar_wait(full0 + 8 * (j % S), (uint32_t)((j / S) & 1), &no_abort, 5);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- MMA issuer
+      // instruction descriptor: D fp32 (1) / s32 (2); A, B bf16 (1) / signed int8 (1); K-major;
+      // N = TBN (>> 3 at bit 17), M = 128 (>> 4 at bit 24)
+      const uint32_t idesc = ((INT8 ? 2u : 1u) << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(TBN >> 3) << 17) |
+                             ((uint32_t)(BM >> 4) << 24);
+      int it = 0, tc = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++tc) {
+        const int acc = tc & 1, use = tc >> 1;
+        if (use > 0 && !mbar_wait(tempty0 + 8 * acc, (use - 1) & 1, abort_flag, 4)) break;
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t d = tmem + (uint32_t)(acc * TBN);
+        for (int kt = 0; kt < n_k; ++kt, ++it) {
+          const int s = it % S, r = it / S;
+          if (!mbar_wait(full0 + 8 * s, r & 1, abort_flag, 2)) {
+            ok = false;
+            break;
+          }
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          const uint32_t a0 = smem_u32(sA + s * kABytes), b0 = smem_u32(sB + s * kBB);
+#pragma unroll
+          for (int k = 0; k < BKB / 32; ++k)  // 32 bytes of K per MMA
+            mma<INT8>(d, smem_desc(a0 + 32 * k), smem_desc(b0 + 32 * k), idesc, (kt > 0 || k > 0) ? 1u : 0u);
+          mma_commit(empty0 + 8 * s);
+        }
+        if (ok) mma_commit(tfull0 + 8 * acc);
+      }
+    }
+  } else {
+    // ---------------- epilogue: warp w owns TMEM lanes / tile rows [32 (w % 4), 32 (w % 4) + 32)
+    const int q = warp & 3;
+    int tc = 0;
+    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++tc) {
+      const int acc = tc & 1, use = tc >> 1;
+      if (!mbar_wait(tfull0 + 8 * acc, use & 1, abort_flag, 3)) break;
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const int m0 = (tile % num_m) * BM, col0 = (tile / num_m) * kCols;
+      const int row = m0 + q * 32 + lane;
+      const uint32_t trow = tmem + (uint32_t)(acc * TBN) + ((uint32_t)(q * 32) << 16);
+      for (int c = 0; c < kCols; c += 32) {
+        uint32_t v[32], u[32];
+        tmem_ld32(trow + c, v);
+        if (EPI == Q35_EPI_SWIGLU) tmem_ld32(trow + TBN / 2 + c, u);
+        if (row >= p.M) continue;
+        const int gc = col0 + c;
+        if (gc >= p.N) continue;
+        float y[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
-          float up;
           if (INT8) {
             const int col = gc + j;
-            up = (col < p.N) ? ((float)(int)u[j] * p.sx[row]) * p.sw[p.N + col] : 0.f;
+            y[j] = (col < p.N) ? ((float)(int)v[j] * p.sx[row]) * p.sw[col] : 0.f;
           } else {
-            up = __uint_as_float(u[j]);
+            y[j] = __uint_as_float(v[j]);
           }
-          y[j] = rbf(silu_f(rbf(y[j]))) * rbf(up);
+        }
+        if (EPI == Q35_EPI_SWIGLU) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            float up;
+            if (INT8) {
+              const int col = gc + j;
+              up = (col < p.N) ? ((float)(int)u[j] * p.sx[row]) * p.sw[p.N + col] : 0.f;
+            } else {
+              up = __uint_as_float(u[j]);
+            }
+            y[j] = rbf(silu_f(rbf(y[j]))) * rbf(up);
+          }
+        }
+        bf16* dst = (EPI == Q35_EPI_RESIDUAL ? p.resid : static_cast<bf16*>(p.out)) + (int64_t)row * p.N + gc;
+        if (gc + 32 <= p.N) {
+#pragma unroll
+          for (int qq = 0; qq < 4; ++qq) {
+            __align__(16) bf16 o[8];
+            if (EPI == Q35_EPI_RESIDUAL) {
+              const uint4 rv = *reinterpret_cast<const uint4*>(dst + 8 * qq);
+              float rf[8];
+              unpack_bf16x8(rv, rf);
+#pragma unroll
+              for (int j = 0; j < 8; ++j) o[j] = f2bf(rf[j] + rbf(y[8 * qq + j]));
+            } else {
+#pragma unroll
+              for (int j = 0; j < 8; ++j) o[j] = f2bf(y[8 * qq + j]);
+            }
+            *reinterpret_cast<uint4*>(dst + 8 * qq) = *reinterpret_cast<const uint4*>(o);
+          }
+        } else {
+          for (int j = 0; j < 32 && gc + j < p.N; ++j) {
+            if (EPI == Q35_EPI_RESIDUAL)
+              dst[j] = f2bf(bf2f(dst[j]) + rbf(y[j]));
+            else
+              dst[j] = f2bf(y[j]);
+          }
         }
       }
-      bf16* dst = (EPI == Q35_EPI_RESIDUAL ? p.resid : static_cast<bf16*>(p.out)) + (int64_t)row * p.N + gc;
-      if (gc + 32 <= p.N) {
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          __align__(16) bf16 o[8];
-          if (EPI == Q35_EPI_RESIDUAL) {
-            const uint4 rv = *reinterpret_cast<const uint4*>(dst + 8 * q);
-            float rf[8];
-            unpack_bf16x8(rv, rf);
-#pragma unroll
-            for (int j = 0; j < 8; ++j) o[j] = f2bf(rf[j] + rbf(y[8 * q + j]));
-          } else {
-#pragma unroll
-            for (int j = 0; j < 8; ++j) o[j] = f2bf(y[8 * q + j]);
-          }
-          *reinterpret_cast<uint4*>(dst + 8 * q) = *reinterpret_cast<const uint4*>(o);
-        }
-      } else {
-        for (int j = 0; j < 32 && gc + j < p.N; ++j) {
-          if (EPI == Q35_EPI_RESIDUAL)
-            dst[j] = f2bf(bf2f(dst[j]) + rbf(y[j]));
-          else
-            dst[j] = f2bf(y[j]);
-        }
-      }
+      // the accumulator is drained (tcgen05.ld waited): hand it back to the MMA warp
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(tempty0 + 8 * acc);
     }
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
   if (warp == 1)
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TBN) : "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * TBN) : "memory");
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -288,7 +344,7 @@ bool make_map(CUtensorMap* m, const void* ptr, uint64_t rows, uint64_t k, uint32
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-constexpr size_t smem_bytes(int bn) { return 1024 + (size_t)kStages * (kABytes + (size_t)bn * BKB) + 256; }
+constexpr size_t smem_bytes(int bn) { return 1024 + (size_t)stages_for(bn) * (kABytes + (size_t)bn * BKB) + 256; }
 
 template <bool INT8, int EPI, int TBN>
 int launch_tc_bn(const void* a, const void* w, const TcParams& p, cudaStream_t s) {
@@ -300,17 +356,21 @@ int launch_tc_bn(const void* a, const void* w, const TcParams& p, cudaStream_t s
   cudaFuncSetAttribute(gemm_tc_kernel<INT8, EPI, TBN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                        (int)smem_bytes(TBN));
   const int cols_per_tile = (EPI == Q35_EPI_SWIGLU) ? TBN / 2 : TBN;
-  dim3 grid((unsigned)((p.N + cols_per_tile - 1) / cols_per_tile), (unsigned)((p.M + BM - 1) / BM));
+  const int64_t tiles = (int64_t)((p.N + cols_per_tile - 1) / cols_per_tile) * ((p.M + BM - 1) / BM);
+  const unsigned grid = (unsigned)(tiles < kNumSMs ? tiles : kNumSMs);
   gemm_tc_kernel<INT8, EPI, TBN><<<grid, kThreads, smem_bytes(TBN), s>>>(ma, mb, p);
   return q35_check_launch("gemm_tc");
 }
 
-// 256-column tiles unless they leave most SMs idle (e.g. N = 2048 at M = 1024: 64 tiles), then 128.
+// 256-column tiles (about twice the MMA rate per SM of 128-column ones: a 128 x 128 MMA step
+// reads as many shared-memory bytes per FLOP as the SM can supply), unless every 128-column tile
+// fits in one wave on the SMs that 256-column tiles would leave idle (N = 2048 at M = 1024).
 template <bool INT8, int EPI>
 int launch_tc(const void* a, const void* w, const TcParams& p, cudaStream_t s) {
-  const int cols256 = (EPI == Q35_EPI_SWIGLU) ? 128 : 256;
-  const int64_t tiles256 = (int64_t)((p.N + cols256 - 1) / cols256) * ((p.M + BM - 1) / BM);
-  if (tiles256 < kNumSMs) return launch_tc_bn<INT8, EPI, 128>(a, w, p, s);
+  const int64_t mt = (p.M + BM - 1) / BM;
+  const int cols128 = (EPI == Q35_EPI_SWIGLU) ? 64 : 128;
+  const int64_t t128 = (int64_t)((p.N + cols128 - 1) / cols128) * mt;
+  if (t128 <= kNumSMs && mt * 2 <= t128) return launch_tc_bn<INT8, EPI, 128>(a, w, p, s);
   return launch_tc_bn<INT8, EPI, 256>(a, w, p, s);
 }
 

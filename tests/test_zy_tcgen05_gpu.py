@@ -68,3 +68,23 @@ def test_gemm_tc_a8w8_bit_exact(epi):
     torch.cuda.synchronize()
     assert K.tc_error() == 0
     assert torch.equal(got.cpu(), want)
+
+
+def test_gemm_tc_persistent_many_tiles():
+    """Several output tiles per CTA (528 bf16 tiles; 384 A8W8 SwiGLU tiles on 148 CTAs): both TMEM
+    accumulators are reused many times, with a ragged last column tile."""
+    a = randn(2048, 2048, seed=21)
+    w = randn(8224, 2048, seed=22, scale=0.02)
+    out = K.gemm(cu(a), cu(w), tc=True)
+    torch.cuda.synchronize()
+    assert K.tc_error() == 0
+    assert_bf16_close(out.cpu(), O.linear(a, w), max_ulp=2, max_frac=0.02)
+    x = randn(1024, 2048, seed=23)
+    wg = randn(2 * 6144, 2048, seed=24, scale=0.02)
+    qw, sw = OQ.quantize_weight(wg)
+    qx, sx = OQ.quantize_rows(x)
+    want = O.silu_and_mul(OQ.dequantize(OQ.int8_matmul_exact(qx, qw), sx, sw))
+    got = K.gemm_a8w8_tc(cu(qx), cu(sx.reshape(-1)), cu(qw), cu(sw.reshape(-1)), epilogue=L.EPI_SWIGLU)
+    torch.cuda.synchronize()
+    assert K.tc_error() == 0
+    assert torch.equal(got.cpu(), want)
