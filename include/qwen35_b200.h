@@ -157,8 +157,9 @@ int q35_int8_gemm_i32(const int8_t* qx, const int8_t* qw, int32_t* acc, int64_t 
 int q35_gemm_bf16(const void* a, const void* w, void* out, int64_t m, int64_t n, int64_t k,
                   int32_t epilogue, void* stream);
 
-/* The same projection on the 5th-generation tensor cores: TMA-fed 128 x 256 tiles accumulated
- * by tcgen05.mma in TMEM (kind::f16). k must be a multiple of 64, n of 8. */
+/* The same projection on the 5th-generation tensor cores: persistent, TMA-fed output tiles
+ * accumulated by tcgen05.mma in TMEM (kind::f16), by default on pairs of SMs (256-row tiles,
+ * cta_group::2). k must be a multiple of 64, n of 8. */
 int q35_gemm_tc(const void* a, const void* w, void* out, int64_t m, int64_t n, int64_t k,
                 int32_t epilogue, void* stream);
 
@@ -171,6 +172,9 @@ int q35_gemm_tc_a8w8(const int8_t* qa, const float* sx, const int8_t* qw, const 
 /* Error word of the tensor-core kernels: non-zero when a bounded pipeline wait gave up (the
  * kernel then finished without hanging). Reading it synchronises and clears it. */
 int q35_tc_error(void);
+/* Process-wide: 1 (default) runs the tensor-core projections on CTA pairs (thread-block clusters
+ * of 2, tcgen05 cta_group::2, 256-row tiles), 0 on single CTAs (128-row tiles). */
+int q35_set_gemm_tc_pairs(int on);
 
 /* ---------------------------------------------------------------- attention */
 

@@ -11,9 +11,12 @@
 //   warp 1 lane 0  MMA issuer: 4 x tcgen05.mma (K = 16 bf16 / 32 int8 each) per stage into one of
 //                  two 128 x TBN FP32/S32 TMEM accumulators; tcgen05.commit frees the stage and,
 //                  after a tile's last stage, hands the accumulator to the epilogue;
-//   warps 2-5      epilogue: tcgen05.ld 32 columns at a time from the warp's 32 TMEM lanes,
-//                  dequantise (int8), store / add to the residual / apply SwiGLU, then release the
-//                  accumulator, while the MMA warp already fills the other one.
+//   warps 2-9      epilogue, two warps per TMEM lane quarter taking alternate 32-column chunks:
+//                  tcgen05.ld from the warp's 32 TMEM lanes, dequantise (int8), store / add to the
+//                  residual / apply SwiGLU, then release the accumulator, while the MMA warp
+//                  already fills the other one.
+// A second kernel runs the same pipeline on SM pairs (tcgen05 cta_group::2, 256 x 256 tiles); see
+// gemm_tc2_kernel. The launcher picks the kernel and tile width per shape.
 // SwiGLU tiles load W rows [o0, o0+TBN/2) (gate) and [N+o0, N+o0+TBN/2) (up) as the two halves of
 // the B tile, so gate and up of an output sit TBN/2 TMEM columns apart.
 // No cluster multicast anywhere (loads are per CTA). Every mbarrier wait is bounded by a clock
@@ -32,7 +35,8 @@ namespace {
 
 constexpr int BM = 128, BKB = 128;  // tile rows, K bytes per stage (tile cols: 256, or 128 for narrow N)
 constexpr int kABytes = BM * BKB;   // 16 KB
-constexpr int kThreads = 192;       // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
+constexpr int kThreads = 320;       // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue
+constexpr int kEpiWarps = 8;        // two per TMEM lane quarter, alternate 32-column chunks
 constexpr long long kWaitBudget = 4000000000LL;  // ~2 s at 2 GHz
 constexpr int stages_for(int) { return 4; }
 
@@ -135,6 +139,126 @@ Q35_DEV void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
 
 Q35_DEV void report(int code) { atomicCAS(&q35_tc_error_word, 0, code); }
 
+// ---------------------------------------------------------------- CTA-pair (cta_group::2) helpers
+Q35_DEV uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// Address of the same shared-memory object in CTA `rank` of the cluster.
+Q35_DEV uint32_t map_to_rank(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+Q35_DEV void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// TMA load into this CTA's shared memory that completes bytes on an mbarrier of either CTA of the pair.
+Q35_DEV void tma_load_2d_pair(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t cluster_bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+      "[%4];" ::"r"(dst),
+      "l"(map), "r"(x), "r"(y), "r"(cluster_bar)
+      : "memory");
+}
+template <bool INT8>
+Q35_DEV void mma_pair(uint32_t tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
+  if (INT8)
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem),
+        "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
+        : "memory");
+  else
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem),
+        "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+// Arrive (once the pair's MMAs issued so far complete) on the mbarrier at `bar` in both CTAs.
+Q35_DEV void mma_commit_pair(uint32_t bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(bar),
+      "h"((uint16_t)0x3)
+      : "memory");
+}
+Q35_DEV void mbar_arrive_cluster(uint32_t cluster_bar) {
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
+}
+Q35_DEV void mbar_expect_tx_only(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+// Epilogue of one accumulator tile for one thread's output row: the warp takes the 32-column
+// chunks h, h + 2, ... of its TMEM lane quarter. The residual reads of chunk c + 2 are issued
+// before chunk c's TMEM load, so the chunks' memory round trips overlap instead of following one
+// another (with one read round trip per chunk, 8 chunks in a row made the tile's tail several us).
+template <bool INT8, int EPI, int TBN>
+Q35_DEV void epilogue_row(const TcParams& p, uint32_t trow, int row, int col0, int h) {
+  constexpr int kCols = (EPI == Q35_EPI_SWIGLU) ? TBN / 2 : TBN;
+  const bool row_ok = row < p.M;
+  bf16* base = (EPI == Q35_EPI_RESIDUAL ? p.resid : static_cast<bf16*>(p.out)) + (int64_t)(row_ok ? row : 0) * p.N;
+  const float sx = (INT8 && row_ok) ? p.sx[row] : 0.f;
+  uint4 res[4], res_n[4];
+  auto fetch = [&](int c, uint4 (&r)[4]) {
+    const int gc = col0 + c;
+    if (EPI == Q35_EPI_RESIDUAL && row_ok && gc + 32 <= p.N) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) r[i] = *reinterpret_cast<const uint4*>(base + gc + 8 * i);
+    }
+  };
+  if (32 * h < kCols) fetch(32 * h, res);
+  for (int c = 32 * h; c < kCols; c += 64) {
+    if (c + 64 < kCols) fetch(c + 64, res_n);
+    const int gc = col0 + c;
+    uint32_t v[32], u[32];
+    tmem_ld32(trow + c, v);
+    if (EPI == Q35_EPI_SWIGLU) tmem_ld32(trow + TBN / 2 + c, u);
+    if (row_ok && gc < p.N) {
+      float y[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        y[j] = INT8 ? ((gc + j < p.N) ? ((float)(int)v[j] * sx) * __ldg(p.sw + gc + j) : 0.f) : __uint_as_float(v[j]);
+      if (EPI == Q35_EPI_SWIGLU) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const float up =
+              INT8 ? ((gc + j < p.N) ? ((float)(int)u[j] * sx) * __ldg(p.sw + p.N + gc + j) : 0.f) : __uint_as_float(u[j]);
+          y[j] = rbf(silu_f(rbf(y[j]))) * rbf(up);
+        }
+      }
+      bf16* dst = base + gc;
+      if (gc + 32 <= p.N) {
+#pragma unroll
+        for (int qq = 0; qq < 4; ++qq) {
+          __align__(16) bf16 o[8];
+          if (EPI == Q35_EPI_RESIDUAL) {
+            float rf[8];
+            unpack_bf16x8(res[qq], rf);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) o[j] = f2bf(rf[j] + rbf(y[8 * qq + j]));
+          } else {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) o[j] = f2bf(y[8 * qq + j]);
+          }
+          *reinterpret_cast<uint4*>(dst + 8 * qq) = *reinterpret_cast<const uint4*>(o);
+        }
+      } else {
+        for (int j = 0; j < 32 && gc + j < p.N; ++j) {
+          if (EPI == Q35_EPI_RESIDUAL)
+            dst[j] = f2bf(bf2f(dst[j]) + rbf(y[j]));
+          else
+            dst[j] = f2bf(y[j]);
+        }
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) res[i] = res_n[i];
+  }
+}
+
 template <bool INT8, int EPI, int TBN>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, TcParams p) {
@@ -163,7 +287,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(tfull0 + 8 * a, 1);
-      mbar_init(tempty0 + 8 * a, 4);  // one arrival per epilogue warp
+      mbar_init(tempty0 + 8 * a, kEpiWarps);  // one arrival per epilogue warp
     }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -241,71 +365,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ---------------- epilogue: warp w owns TMEM lanes / tile rows [32 (w % 4), 32 (w % 4) + 32)
-    const int q = warp & 3;
+    const int q = warp & 3, h = (warp - 2) >> 2;
     int tc = 0;
     for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++tc) {
       const int acc = tc & 1, use = tc >> 1;
       if (!mbar_wait(tfull0 + 8 * acc, use & 1, abort_flag, 3)) break;
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
       const int m0 = (tile % num_m) * BM, col0 = (tile / num_m) * kCols;
-      const int row = m0 + q * 32 + lane;
       const uint32_t trow = tmem + (uint32_t)(acc * TBN) + ((uint32_t)(q * 32) << 16);
-      for (int c = 0; c < kCols; c += 32) {
-        uint32_t v[32], u[32];
-        tmem_ld32(trow + c, v);
-        if (EPI == Q35_EPI_SWIGLU) tmem_ld32(trow + TBN / 2 + c, u);
-        if (row >= p.M) continue;
-        const int gc = col0 + c;
-        if (gc >= p.N) continue;
-        float y[32];
-#pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          if (INT8) {
-            const int col = gc + j;
-            y[j] = (col < p.N) ? ((float)(int)v[j] * p.sx[row]) * p.sw[col] : 0.f;
-          } else {
-            y[j] = __uint_as_float(v[j]);
-          }
-        }
-        if (EPI == Q35_EPI_SWIGLU) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            float up;
-            if (INT8) {
-              const int col = gc + j;
-              up = (col < p.N) ? ((float)(int)u[j] * p.sx[row]) * p.sw[p.N + col] : 0.f;
-            } else {
-              up = __uint_as_float(u[j]);
-            }
-            y[j] = rbf(silu_f(rbf(y[j]))) * rbf(up);
-          }
-        }
-        bf16* dst = (EPI == Q35_EPI_RESIDUAL ? p.resid : static_cast<bf16*>(p.out)) + (int64_t)row * p.N + gc;
-        if (gc + 32 <= p.N) {
-#pragma unroll
-          for (int qq = 0; qq < 4; ++qq) {
-            __align__(16) bf16 o[8];
-            if (EPI == Q35_EPI_RESIDUAL) {
-              const uint4 rv = *reinterpret_cast<const uint4*>(dst + 8 * qq);
-              float rf[8];
-              unpack_bf16x8(rv, rf);
-#pragma unroll
-              for (int j = 0; j < 8; ++j) o[j] = f2bf(rf[j] + rbf(y[8 * qq + j]));
-            } else {
-#pragma unroll
-              for (int j = 0; j < 8; ++j) o[j] = f2bf(y[8 * qq + j]);
-            }
-            *reinterpret_cast<uint4*>(dst + 8 * qq) = *reinterpret_cast<const uint4*>(o);
-          }
-        } else {
-          for (int j = 0; j < 32 && gc + j < p.N; ++j) {
-            if (EPI == Q35_EPI_RESIDUAL)
-              dst[j] = f2bf(bf2f(dst[j]) + rbf(y[j]));
-            else
-              dst[j] = f2bf(y[j]);
-          }
-        }
-      }
+      epilogue_row<INT8, EPI, TBN>(p, trow, m0 + q * 32 + lane, col0, h);
       // the accumulator is drained (tcgen05.ld waited): hand it back to the MMA warp
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
       __syncwarp();
@@ -316,6 +384,146 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   if (warp == 1)
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * TBN) : "memory");
+}
+
+// ---------------------------------------------------------------- CTA-pair kernel
+// The same persistent pipeline on pairs of SMs (thread-block clusters of 2, tcgen05 cta_group::2):
+// a pair computes a 256 x TBN tile as ONE MMA of M = 256. CTA r of the pair loads its own A rows
+// [128 r, 128 r + 128) and B rows [r TBN/2, (r + 1) TBN/2) and holds output rows 128 r .. in its
+// TMEM; the MMA reads both CTAs' shared memory. Each SM therefore streams half the B bytes per
+// FLOP of the single-CTA kernel. Protocol (rank 0 = leader):
+//   full[s]   leader only: the leader's producer arrives with the pair's total bytes; both CTAs'
+//             loads complete their bytes on it (cta_group::2 TMA, mbarrier mapped to rank 0);
+//   empty[s]  each CTA: the leader's tcgen05.commit arrives on both (multicast commit);
+//   tfull[a]  each CTA: multicast commit after a tile's last MMA;
+//   tempty[a] leader only: the 8 epilogue warps of each CTA arrive (remote arrive from rank 1).
+constexpr int stages_pair(int bn) { return bn == 256 ? 6 : 8; }
+constexpr size_t smem_bytes_pair(int bn) {
+  return 1024 + (size_t)stages_pair(bn) * (kABytes + (size_t)(bn / 2) * BKB) + 256;
+}
+
+template <bool INT8, int EPI, int TBN>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, TcParams p) {
+  constexpr int S = stages_pair(TBN);
+  constexpr int kBB = (TBN / 2) * BKB;  // this CTA's B bytes per stage
+  constexpr int kCols = (EPI == Q35_EPI_SWIGLU) ? TBN / 2 : TBN;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  unsigned char* sA = smem;
+  unsigned char* sB = smem + S * kABytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + S * kBB);  // full[S], empty[S], tfull[2], tempty[2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 4);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+  const int kstep = BKB / (INT8 ? 1 : 2);
+  const int n_k = p.K / kstep;
+  const int num_m = (p.M + 2 * BM - 1) / (2 * BM);
+  const int ntiles = num_m * ((p.N + kCols - 1) / kCols);
+  const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + S);
+  const uint32_t tfull0 = smem_u32(bars + 2 * S), tempty0 = smem_u32(bars + 2 * S + 2);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(full0 + 8 * s, 1);
+      mbar_init(empty0 + 8 * s, 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(tfull0 + 8 * a, 1);
+      mbar_init(tempty0 + 8 * a, 2 * kEpiWarps);  // every epilogue warp of both CTAs
+    }
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(2 * TBN)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  __syncthreads();
+  cluster_sync_all();  // both CTAs' barriers are initialised before any cross-CTA signal
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer (both CTAs)
+      int it = 0;
+      bool ok = true;
+      for (int tile = pair; tile < ntiles && ok; tile += npairs) {
+        const int m0 = (tile % num_m) * 2 * BM + (int)rank * BM, c0 = (tile / num_m) * kCols;
+        for (int kt = 0; kt < n_k; ++kt, ++it) {
+          const int s = it % S, r = it / S;
+          if (r > 0 && !mbar_wait(empty0 + 8 * s, (r - 1) & 1, abort_flag, 11)) {
+            ok = false;
+            break;
+          }
+          if (rank == 0) mbar_expect_tx_only(full0 + 8 * s, 2 * (kABytes + kBB));
+          const uint32_t fbar = map_to_rank(full0 + 8 * s, 0);
+          const int kx = kt * kstep;
+          tma_load_2d_pair(smem_u32(sA + s * kABytes), &tmA, kx, m0, fbar);
+          const int brow = (EPI == Q35_EPI_SWIGLU) ? (rank == 0 ? c0 : p.N + c0) : c0 + (int)rank * (TBN / 2);
+          tma_load_2d_pair(smem_u32(sB + s * kBB), &tmB, kx, brow, fbar);
+        }
+      }
+      (void)ok;
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && rank == 0) {
+      // ---------------- MMA issuer (leader): M = 256 across the pair, N = TBN
+      const uint32_t idesc = ((INT8 ? 2u : 1u) << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(TBN >> 3) << 17) |
+                             ((uint32_t)((2 * BM) >> 4) << 24);
+      int it = 0, tc = 0;
+      bool ok = true;
+      for (int tile = pair; tile < ntiles && ok; tile += npairs, ++tc) {
+        const int acc = tc & 1, use = tc >> 1;
+        if (use > 0 && !mbar_wait(tempty0 + 8 * acc, (use - 1) & 1, abort_flag, 14)) break;
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t d = tmem + (uint32_t)(acc * TBN);
+        for (int kt = 0; kt < n_k; ++kt, ++it) {
+          const int s = it % S, r = it / S;
+          if (!mbar_wait(full0 + 8 * s, r & 1, abort_flag, 12)) {
+            ok = false;
+            break;
+          }
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          const uint32_t a0 = smem_u32(sA + s * kABytes), b0 = smem_u32(sB + s * kBB);
+#pragma unroll
+          for (int k = 0; k < BKB / 32; ++k)
+            mma_pair<INT8>(d, smem_desc(a0 + 32 * k), smem_desc(b0 + 32 * k), idesc, (kt > 0 || k > 0) ? 1u : 0u);
+          mma_commit_pair(empty0 + 8 * s);
+        }
+        if (ok) mma_commit_pair(tfull0 + 8 * acc);
+      }
+    }
+  } else {
+    // ---------------- epilogue (both CTAs): warp w owns TMEM lanes [32 (w % 4), +32) of this CTA
+    const int q = warp & 3, h = (warp - 2) >> 2;
+    const uint32_t tempty_leader = map_to_rank(tempty0, 0);
+    int tc = 0;
+    for (int tile = pair; tile < ntiles; tile += npairs, ++tc) {
+      const int acc = tc & 1, use = tc >> 1;
+      if (!mbar_wait(tfull0 + 8 * acc, use & 1, abort_flag, 13)) break;
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const int m0 = (tile % num_m) * 2 * BM + (int)rank * BM, col0 = (tile / num_m) * kCols;
+      const uint32_t trow = tmem + (uint32_t)(acc * TBN) + ((uint32_t)(q * 32) << 16);
+      epilogue_row<INT8, EPI, TBN>(p, trow, m0 + q * 32 + lane, col0, h);
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(tempty_leader + 8 * acc);
+    }
+  }
+  // Every load, MMA and cross-CTA arrival of the pair is done before either CTA frees TMEM or exits:
+  // the producers' last loads were consumed by the leader's MMAs, whose completion both epilogues
+  // waited for (or the CTA aborted, whose waits are bounded).
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  cluster_sync_all();
+  if (warp == 1)
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * TBN) : "memory");
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -362,15 +570,66 @@ int launch_tc_bn(const void* a, const void* w, const TcParams& p, cudaStream_t s
   return q35_check_launch("gemm_tc");
 }
 
-// 256-column tiles (about twice the MMA rate per SM of 128-column ones: a 128 x 128 MMA step
-// reads as many shared-memory bytes per FLOP as the SM can supply), unless every 128-column tile
-// fits in one wave on the SMs that 256-column tiles would leave idle (N = 2048 at M = 1024).
+int g_tc_pairs = 1;  // process-wide: CTA-pair kernel (1) or single-CTA kernel (0)
+
+template <bool INT8, int EPI>
+int max_active_pairs() {
+  static int max_pairs = 0;  // pairs resident at once (clusters of 2 need both SMs in one GPC)
+  if (max_pairs == 0) {
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = 2;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cfg.gridDim = dim3(kNumSMs);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem_bytes_pair(256);
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    cudaFuncSetAttribute(gemm_tc2_kernel<INT8, EPI, 256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)smem_bytes_pair(256));
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, gemm_tc2_kernel<INT8, EPI, 256>, &cfg) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      n = kNumSMs / 2;
+    }
+    max_pairs = n < kNumSMs / 2 ? n : kNumSMs / 2;
+  }
+  return max_pairs;
+}
+
+// Pair tiles are 256 x 256 (an N = 128 MMA runs at about half the rate of N = 256 on either kernel).
+template <bool INT8, int EPI>
+int launch_tc2(const void* a, const void* w, const TcParams& p, cudaStream_t s) {
+  constexpr int TBN = 256;
+  const int npairs = max_active_pairs<INT8, EPI>();
+  const int cols = (EPI == Q35_EPI_SWIGLU) ? TBN / 2 : TBN;
+  const int64_t tiles = (int64_t)((p.N + cols - 1) / cols) * ((p.M + 2 * BM - 1) / (2 * BM));
+  CUtensorMap ma, mb;
+  const uint64_t wrows = (EPI == Q35_EPI_SWIGLU) ? 2 * (uint64_t)p.N : (uint64_t)p.N;
+  if (!make_map(&ma, a, p.M, p.K, BM, INT8) || !make_map(&mb, w, wrows, p.K, TBN / 2, INT8))
+    return q35_fail(Q35_ECUDA, "gemm_tc: tensor map encoding failed");
+  const int64_t pairs = tiles < npairs ? tiles : npairs;
+  cudaFuncSetAttribute(gemm_tc2_kernel<INT8, EPI, TBN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       (int)smem_bytes_pair(TBN));
+  gemm_tc2_kernel<INT8, EPI, TBN><<<(unsigned)(2 * pairs), kThreads, smem_bytes_pair(TBN), s>>>(ma, mb, p);
+  return q35_check_launch("gemm_tc2");
+}
+
+// Kernel and tile choice (measured at M = 1024 on B200): when single-CTA 128-column tiles fill
+// the machine in one wave while 256-column tiles would leave most SMs idle (N = 2048: 128 vs 64
+// tiles), the single-CTA 128-column kernel (down 41 us, out_proj 19.5 us; pairs: 44.5 / 23.3).
+// Otherwise 256-column tiles, on SM pairs by default (in_proj 35 us, QKV + gate 34, gate/up 47.5;
+// single CTAs: 37.7 / 35.7 / 51.4). Splitting K over more pairs to fill the idle SMs (partial
+// sums through global memory, fixed-order combine) measured slower for every shape and was removed.
 template <bool INT8, int EPI>
 int launch_tc(const void* a, const void* w, const TcParams& p, cudaStream_t s) {
   const int64_t mt = (p.M + BM - 1) / BM;
   const int cols128 = (EPI == Q35_EPI_SWIGLU) ? 64 : 128;
   const int64_t t128 = (int64_t)((p.N + cols128 - 1) / cols128) * mt;
   if (t128 <= kNumSMs && mt * 2 <= t128) return launch_tc_bn<INT8, EPI, 128>(a, w, p, s);
+  if (g_tc_pairs) return launch_tc2<INT8, EPI>(a, w, p, s);
   return launch_tc_bn<INT8, EPI, 256>(a, w, p, s);
 }
 
@@ -386,7 +645,7 @@ int q35_gemm_tc_launch(const void* a, const void* w, void* out, int64_t m, int64
   Q35_REQUIRE(n % 8 == 0, "gemm_tc: n must be a multiple of 8");
   Q35_REQUIRE(!int8 || (sx && sw), "gemm_tc: int8 needs scales");
   Q35_REQUIRE(epi == Q35_EPI_STORE || epi == Q35_EPI_RESIDUAL || epi == Q35_EPI_SWIGLU, "gemm_tc: bad epilogue");
-  TcParams p;
+  TcParams p = {};
   p.out = out;
   p.resid = static_cast<bf16*>(out);
   p.sx = sx;
@@ -416,6 +675,12 @@ extern "C" int q35_gemm_tc(const void* a, const void* w, void* out, int64_t m, i
 extern "C" int q35_gemm_tc_a8w8(const int8_t* qa, const float* sx, const int8_t* qw, const float* sw, void* out,
                                 int64_t m, int64_t n, int64_t k, int32_t epilogue, void* stream) {
   return q35_gemm_tc_launch(qa, qw, out, m, n, k, epilogue, true, sx, sw, (cudaStream_t)stream);
+}
+
+extern "C" int q35_set_gemm_tc_pairs(int on) {
+  Q35_REQUIRE(on == 0 || on == 1, "gemm_tc: pairs must be 0 or 1");
+  g_tc_pairs = on;
+  return Q35_OK;
 }
 
 extern "C" int q35_tc_error(void) {

@@ -193,6 +193,11 @@ def tc_error() -> int:
     return int(L.load().q35_tc_error())
 
 
+def set_gemm_tc_pairs(on: bool) -> None:
+    """Process-wide: tensor-core projections on SM pairs (cta_group::2, default) or single SMs."""
+    L.call("q35_set_gemm_tc_pairs", 1 if on else 0)
+
+
 # ---------------------------------------------------------------------------- A8W8
 def quantize_rows(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
     """Per-row symmetric int8 (explore_runtime_quantization.py:143-155 / vllm per-token)."""

@@ -19,6 +19,14 @@ def cu(t):
     return t.cuda()
 
 
+@pytest.fixture(autouse=True, params=[True, False], ids=["pairs", "single"])
+def sm_pairs(request):
+    """Every case runs on the CTA-pair kernel (the default) and on the single-CTA kernel."""
+    K.set_gemm_tc_pairs(request.param)
+    yield request.param
+    K.set_gemm_tc_pairs(True)
+
+
 @pytest.mark.parametrize("m,n,k", [(128, 256, 128), (1024, 8224, 2048), (77, 2048, 6144), (5, 5120, 2048)])
 def test_gemm_tc_store(m, n, k):
     a = randn(m, k, seed=m + 1)
