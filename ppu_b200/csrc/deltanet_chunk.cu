@@ -2,10 +2,11 @@
 // rule of qwen35_fused/kernels.py:768-851; chunked form of HF torch_chunk_gated_delta_rule,
 // chunk 64, modeling_qwen3_5.py).
 //
-// Phase A (one CTA per (batch, head, 64-token chunk), all chunks in parallel):
+// Phase A (one CTA per (batch, head, 64-token chunk), all chunks in parallel, products on the
+// tensor cores: bf16 for KK / QK, TF32-split left factor for U / W):
 //   q_hat = q * rsqrt(|q|^2 + 1e-6) / sqrt(D), k_hat = k * rsqrt(|k|^2 + 1e-6),
 //   g = -exp(A_log) * softplus(a + dt_bias), beta = sigmoid(b), c = cumsum(g) in the chunk;
-//   A_ij = -beta_i (k_i . k_j) exp(c_i - c_j) (i > j); T = (I - A)^-1 by forward substitution;
+//   A_ij = -beta_i (k_i . k_j) exp(c_i - c_j) (i > j); T = (I - A)^-1 by blocked substitution;
 //   U = T diag(beta) V;  W = T diag(beta exp(c)) K;  P_ij = (q_i . k_j) exp(c_i - c_j) (i >= j);
 //   Qe = q_hat exp(c);   Kd = k_hat exp(c_last - c);  gl = exp(c_last).
 // Phase B (one CTA per (batch, head, 16 value columns), chunks in order, products on the tensor
@@ -21,7 +22,6 @@ constexpr int kC = 64;      // chunk length
 constexpr int kD = 128;     // key / value head dim
 constexpr int kVS = 16;     // value columns per phase-B CTA
 constexpr int kThreads = 256;
-constexpr int kP = 129;     // padded row stride (floats) of the phase-A operand tiles
 constexpr int kPW = 132;    // padded row stride of phase-B W / Qe tiles (16-byte aligned rows)
 
 struct ChunkWs {  // per (b, h, chunk) record in the workspace, FP32
@@ -38,29 +38,64 @@ struct PrepParams {
   int L, H, NC, packed_stride;
 };
 
-// Shared memory is q, k, v only (~99 KB), so two CTAs share an SM: once the QK / KK products are in
-// registers, q is dead (Qe went to the workspace) and its region holds A / T and the solve scratch.
+// ---- tensor-core helpers (mma.sync). Fragments of m16n8k8 TF32 (g = lane / 4, c = lane % 4):
+// a = {A[g][c], A[g+8][c], A[g][c+4], A[g+8][c+4]}, b = {B[c][g], B[c+4][g]},
+// d = {D[g][2c], D[g][2c+1], D[g+8][2c], D[g+8][2c+1]}. m16n8k16 bf16: a holds pairs
+// {A[g][2c..2c+1], A[g+8][2c..], A[g][2c+8..], A[g+8][2c+8..]}, b = {B[2c..2c+1][g], B[2c+8..][g]}.
+Q35_DEV uint32_t tf32_bits(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return r;
+}
+Q35_DEV void split_tf32(float x, uint32_t& hi, uint32_t& lo) {
+  hi = tf32_bits(x);
+  lo = tf32_bits(x - __uint_as_float(hi));
+}
+Q35_DEV void mma_tf32(float d[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+Q35_DEV void mma_bf16(float d[4], const uint32_t a[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+Q35_DEV uint32_t lds32(const bf16* p) { return *reinterpret_cast<const uint32_t*>(p); }
+// a bf16 value as a TF32 operand: its FP32 bit pattern has the low 16 bits zero, so it is exact
+Q35_DEV uint32_t bf16_as_tf32(bf16 x) { return (uint32_t)__bfloat16_as_ushort(x) << 16; }
+
+constexpr int kPB = 136;  // row stride (bf16) of the raw q / k / v tiles: fragment loads hit distinct banks
+constexpr int kTS = 68;   // row stride (floats) of T: A-fragment loads hit distinct banks
+
+// Phase A on the tensor cores. q, k, v stay raw bf16 in shared memory (the normalisations are
+// per-row scales): KK = k k^T and QK = q k^T are exact bf16 products with FP32 accumulation,
+// scaled by the row factors afterwards; U = (T diag(beta)) V and W = (T diag(beta e^c ks)) k take
+// the FP32 left factor split into TF32 high + low parts against the exactly representable bf16
+// right factor (two MMAs per step, FP32-level accuracy). ~73 KB of shared memory: two CTAs per SM.
 __global__ void __launch_bounds__(kThreads, 2) delta_chunk_prep_kernel(PrepParams p) {
-  extern __shared__ __align__(16) float sm[];
-  float* q = sm;                 // [64][129]
-  float* k = q + kC * kP;        // [64][129]
-  float* v = k + kC * kP;        // [64][129]
-  float* T = q;                  // [64][65]  A then T, after q is dead
-  float* R = T + kC * 65;        // [48][16]  solve scratch
-  __shared__ float c[kC], beta[kC], qs[kC], ks[kC];
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  bf16* qb = reinterpret_cast<bf16*>(smem_raw);          // [64][136] raw q
+  bf16* kb = qb + kC * kPB;                              // [64][136] raw k
+  bf16* vb = kb + kC * kPB;                              // [64][136] raw v
+  float* T = reinterpret_cast<float*>(vb + kC * kPB);    // [64][68]  A, then T = (I - A)^-1
+  float* R = T + kC * kTS;                               // [48][16]  solve scratch
+  __shared__ float c[kC], beta[kC], qs[kC], ks[kC], araw[kC], braw[kC], su[kC], sw[kC];
   const int ch = blockIdx.x % p.NC;
   const int h = (blockIdx.x / p.NC) % p.H;
   const int b = blockIdx.x / (p.NC * p.H);
   const int H = p.H, L = p.L;
   const int t0 = ch * kC;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, cq = lane & 3;
   const int qkv_stride = 3 * H * kD;
 
-  // ---- load the chunk (bf16 -> fp32), zero padding past L: every load issued before any use
+  // ---- load the chunk (raw bf16), zero padding past L: every load issued before any use
   constexpr int kLoads = kC * 3 * (kD / 8) / kThreads;  // 12 16-byte loads per thread
   const float a_log = bf2f(p.a_log[h]), dt_bias = bf2f(p.dt_bias[h]);
   const int a_off = 4 * H * kD, b_off = a_off + H;
-  __shared__ float araw[kC], braw[kC];
   {
     uint4 raw[kLoads];
 #pragma unroll
@@ -84,11 +119,8 @@ __global__ void __launch_bounds__(kThreads, 2) delta_chunk_prep_kernel(PrepParam
       const int i = tid + u * kThreads;
       const int r = i / (3 * kD / 8), rem = i % (3 * kD / 8);
       const int which = rem / (kD / 8), col = (rem % (kD / 8)) * 8;
-      float f[8];
-      unpack_bf16x8(raw[u], f);
-      float* dst = (which == 0 ? q : which == 1 ? k : v) + r * kP + col;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) dst[j] = f[j];
+      bf16* dst = (which == 0 ? qb : which == 1 ? kb : vb) + r * kPB + col;
+      *reinterpret_cast<uint4*>(dst) = raw[u];
     }
   }
   __syncthreads();
@@ -96,8 +128,9 @@ __global__ void __launch_bounds__(kThreads, 2) delta_chunk_prep_kernel(PrepParam
   for (int r = warp; r < kC; r += kThreads / 32) {
     float sq = 0.f, sk = 0.f;
     for (int e = lane; e < kD; e += 32) {
-      sq += q[r * kP + e] * q[r * kP + e];
-      sk += k[r * kP + e] * k[r * kP + e];
+      const float qv = bf2f(qb[r * kPB + e]), kv = bf2f(kb[r * kPB + e]);
+      sq += qv * qv;
+      sk += kv * kv;
     }
     sq = warp_sum(sq);
     sk = warp_sum(sk);
@@ -105,14 +138,14 @@ __global__ void __launch_bounds__(kThreads, 2) delta_chunk_prep_kernel(PrepParam
       qs[r] = rsqrt_ieee(sq + 1e-6f);
       ks[r] = rsqrt_ieee(sk + 1e-6f);
       const int t = t0 + r;
-      float g = 0.f, bt = 0.f;
+      float gg = 0.f, bt = 0.f;
       if (t < L) {
         const float a = araw[r] + dt_bias;
         const float sp = a > 20.0f ? a : log1pf(expf(a));
-        g = -expf(a_log) * sp;
+        gg = -expf(a_log) * sp;
         bt = 1.0f / (1.0f + expf(-braw[r]));
       }
-      c[r] = g;
+      c[r] = gg;
       beta[r] = bt;
     }
   }
@@ -124,59 +157,63 @@ __global__ void __launch_bounds__(kThreads, 2) delta_chunk_prep_kernel(PrepParam
       c[r] = acc;
     }
   }
-  // normalise q, k in place: q_hat = (q * q_inv) / sqrt(D) (kernels.py:826-827 association)
+  __syncthreads();
+  // ---- Qe = q_hat e^c, Kd = k_hat e^(c_last - c) with q_hat = (q qs) / sqrt(D) (kernels.py:826-827
+  // association), k_hat = k ks; column scales of the U / W left factors
+  float* out = p.ws + ((size_t)(b * H + h) * p.NC + ch) * ChunkWs::SIZE;
+  const float cl = c[kC - 1];
   const float qscale = 1.0f / sqrtf((float)kD);
   for (int i = tid; i < kC * kD; i += kThreads) {
     const int r = i / kD, e = i % kD;
-    q[r * kP + e] = (q[r * kP + e] * qs[r]) * qscale;
-    k[r * kP + e] = k[r * kP + e] * ks[r];
+    out[ChunkWs::Qe + i] = ((bf2f(qb[r * kPB + e]) * qs[r]) * qscale) * expf(c[r]);
+    out[ChunkWs::Kd + i] = (bf2f(kb[r * kPB + e]) * ks[r]) * expf(cl - c[r]);
   }
-  __syncthreads();
-  float* out = p.ws + ((size_t)(b * H + h) * p.NC + ch) * ChunkWs::SIZE;
-  const float cl = c[kC - 1];
-  for (int i = tid; i < kC * kD; i += kThreads) {
-    const int r = i / kD, e = i % kD;
-    out[ChunkWs::Qe + i] = q[r * kP + e] * expf(c[r]);
-    out[ChunkWs::Kd + i] = k[r * kP + e] * expf(cl - c[r]);
+  if (tid < kC) {
+    su[tid] = beta[tid];
+    sw[tid] = (beta[tid] * expf(c[tid])) * ks[tid];
   }
   if (tid == 0) out[ChunkWs::GL] = expf(cl);
-  // ---- KK and QK (64 x 64): thread (ti, tj) owns a 4 x 4 block
+  // ---- KK = k k^T and QK = q k^T (64 x 64, K = 128) on bf16 mma.sync: warp w computes rows
+  // 16 (w & 3) .. + 16 against key columns 32 (w >> 2) .. + 32 (four 8-column tiles)
   {
-    const int ti = tid / 16, tj = tid % 16;
+    const int mt = warp & 3, nb = (warp >> 2) * 4;
     float kk[4][4], qk[4][4];
 #pragma unroll
-    for (int a = 0; a < 4; ++a)
+    for (int n = 0; n < 4; ++n)
 #pragma unroll
-      for (int bb = 0; bb < 4; ++bb) kk[a][bb] = qk[a][bb] = 0.f;
-    for (int e = 0; e < kD; ++e) {
-      float ki[4], qi[4], kj[4];
+      for (int i = 0; i < 4; ++i) kk[n][i] = qk[n][i] = 0.f;
+#pragma unroll 2
+    for (int k0 = 0; k0 < kD; k0 += 16) {
+      const bf16* ka = kb + (16 * mt + g) * kPB + k0 + 2 * cq;
+      const bf16* qa = qb + (16 * mt + g) * kPB + k0 + 2 * cq;
+      const uint32_t ak[4] = {lds32(ka), lds32(ka + 8 * kPB), lds32(ka + 8), lds32(ka + 8 * kPB + 8)};
+      const uint32_t aq[4] = {lds32(qa), lds32(qa + 8 * kPB), lds32(qa + 8), lds32(qa + 8 * kPB + 8)};
 #pragma unroll
-      for (int a = 0; a < 4; ++a) {
-        ki[a] = k[(4 * ti + a) * kP + e];
-        qi[a] = q[(4 * ti + a) * kP + e];
-        kj[a] = k[(4 * tj + a) * kP + e];
+      for (int n = 0; n < 4; ++n) {
+        const bf16* kbp = kb + (8 * (nb + n) + g) * kPB + k0 + 2 * cq;
+        const uint32_t b0 = lds32(kbp), b1 = lds32(kbp + 8);
+        mma_bf16(kk[n], ak, b0, b1);
+        mma_bf16(qk[n], aq, b0, b1);
       }
+    }
+    // A_ij = -beta_i (k_hat_i . k_hat_j) e^(c_i - c_j) (j < i) into T; P_ij = (q_hat_i . k_hat_j)
+    // e^(c_i - c_j) (j <= i) to the workspace
 #pragma unroll
-      for (int a = 0; a < 4; ++a)
+    for (int n = 0; n < 4; ++n)
 #pragma unroll
-        for (int bb = 0; bb < 4; ++bb) {
-          kk[a][bb] = fmaf(ki[a], kj[bb], kk[a][bb]);
-          qk[a][bb] = fmaf(qi[a], kj[bb], qk[a][bb]);
+      for (int half = 0; half < 2; ++half) {
+        const int i = 16 * mt + g + 8 * half, j = 8 * (nb + n) + 2 * cq;
+        float pv[2];
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int jj = j + e;
+          const float dec = expf(c[i] - c[jj]);
+          const float kkh = (kk[n][2 * half + e] * ks[i]) * ks[jj];
+          T[i * kTS + jj] = (jj < i) ? -(beta[i] * kkh) * dec : 0.f;
+          pv[e] = (jj <= i) ? (((qk[n][2 * half + e] * qs[i]) * qscale) * ks[jj]) * dec : 0.f;
         }
-    }
-    __syncthreads();  // every thread is done reading q: its region becomes T
-#pragma unroll
-    for (int a = 0; a < 4; ++a) {
-      const int i = 4 * ti + a;
-      float pr[4];
-#pragma unroll
-      for (int bb = 0; bb < 4; ++bb) {
-        const int j = 4 * tj + bb;
-        T[i * 65 + j] = (j < i) ? -(beta[i] * kk[a][bb]) * expf(c[i] - c[j]) : 0.f;
-        pr[bb] = (j <= i) ? qk[a][bb] * expf(c[i] - c[j]) : 0.f;
+        *reinterpret_cast<float2*>(out + ChunkWs::P + i * kC + j) = make_float2(pv[0], pv[1]);
       }
-      *reinterpret_cast<float4*>(out + ChunkWs::P + i * kC + 4 * tj) = make_float4(pr[0], pr[1], pr[2], pr[3]);
-    }
   }
   __syncthreads();
   // ---- T = (I - A)^-1 (A strictly lower): T_ij = sum_{j <= m < i} A_im T_mj with T_jj = 1.
@@ -190,12 +227,12 @@ __global__ void __launch_bounds__(kThreads, 2) delta_chunk_prep_kernel(PrepParam
       const int i = blk * B + r;
       if (lt < r) {
         const int jj = blk * B + lt;
-        float acc = T[i * 65 + jj];
-        for (int m = lt + 1; m < r; ++m) acc = fmaf(T[i * 65 + blk * B + m], T[(blk * B + m) * 65 + jj], acc);
+        float acc = T[i * kTS + jj];
+        for (int m = lt + 1; m < r; ++m) acc = fmaf(T[i * kTS + blk * B + m], T[(blk * B + m) * kTS + jj], acc);
         nv = acc;
       }
       __syncthreads();
-      if (lt < r) T[i * 65 + blk * B + lt] = nv;
+      if (lt < r) T[i * kTS + blk * B + lt] = nv;
       __syncthreads();
     }
     for (int I = 1; I < kC / B; ++I) {
@@ -203,8 +240,8 @@ __global__ void __launch_bounds__(kThreads, 2) delta_chunk_prep_kernel(PrepParam
       for (int e = tid; e < I * B * B; e += kThreads) {
         const int J = e / (B * B), r = (e / B) % B, cc = e % B;
         const int row = I * B + r, col = J * B + cc;
-        float acc = T[row * 65 + col];  // K = J term with T_JJ's unit diagonal
-        for (int m = J * B + cc + 1; m < I * B; ++m) acc = fmaf(T[row * 65 + m], T[m * 65 + col], acc);
+        float acc = T[row * kTS + col];  // K = J term with T_JJ's unit diagonal
+        for (int m = J * B + cc + 1; m < I * B; ++m) acc = fmaf(T[row * kTS + m], T[m * kTS + col], acc);
         R[(J * B + r) * B + cc] = acc;
       }
       __syncthreads();
@@ -212,35 +249,55 @@ __global__ void __launch_bounds__(kThreads, 2) delta_chunk_prep_kernel(PrepParam
       for (int e = tid; e < I * B * B; e += kThreads) {
         const int J = e / (B * B), r = (e / B) % B, cc = e % B;
         float acc = R[(J * B + r) * B + cc];
-        for (int m = 0; m < r; ++m) acc = fmaf(T[(I * B + r) * 65 + I * B + m], R[(J * B + m) * B + cc], acc);
-        T[(I * B + r) * 65 + J * B + cc] = acc;
+        for (int m = 0; m < r; ++m) acc = fmaf(T[(I * B + r) * kTS + I * B + m], R[(J * B + m) * B + cc], acc);
+        T[(I * B + r) * kTS + J * B + cc] = acc;
       }
       __syncthreads();
     }
   }
-  if (tid < kC) T[tid * 65 + tid] = 1.0f;
+  if (tid < kC) T[tid * kTS + tid] = 1.0f;
   __syncthreads();
-  // ---- U = T diag(beta) V, W = T diag(beta exp(c)) K; thread owns column e and 32 rows
+  // ---- U = (T diag(beta)) V and W = (T diag(beta e^c ks)) k (64 x 128 each, K = 64 tokens):
+  // warp w computes rows 16 (w & 3) .. + 16 and value / key columns 64 (w >> 2) .. + 64
   {
-    const int e = tid % kD, i0 = (tid / kD) * 32;
-    float u[32], w[32];
+    const int mt = warp & 3, nb = (warp >> 2) * 8;
+    float u[8][4], wv[8][4];
 #pragma unroll
-    for (int a = 0; a < 32; ++a) u[a] = w[a] = 0.f;
-    for (int j = 0; j < kC; ++j) {
-      const float bv = beta[j] * v[j * kP + e];
-      const float bk = (beta[j] * expf(c[j])) * k[j * kP + e];
+    for (int n = 0; n < 8; ++n)
 #pragma unroll
-      for (int a = 0; a < 32; ++a) {
-        const float tij = T[(i0 + a) * 65 + j];
-        u[a] = fmaf(tij, bv, u[a]);
-        w[a] = fmaf(tij, bk, w[a]);
+      for (int i = 0; i < 4; ++i) u[n][i] = wv[n][i] = 0.f;
+    const float* t_lo = T + (16 * mt + g) * kTS;
+    const float* t_hi = t_lo + 8 * kTS;
+#pragma unroll 2
+    for (int j0 = 0; j0 < kC; j0 += 8) {
+      const int ja = j0 + cq, jb = ja + 4;
+      const float ta[4] = {t_lo[ja], t_hi[ja], t_lo[jb], t_hi[jb]};
+      const float sua[2] = {su[ja], su[jb]}, swa[2] = {sw[ja], sw[jb]};
+      uint32_t uh[4], ul[4], wh[4], wl[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        split_tf32(ta[i] * sua[i >> 1], uh[i], ul[i]);
+        split_tf32(ta[i] * swa[i >> 1], wh[i], wl[i]);
+      }
+#pragma unroll
+      for (int n = 0; n < 8; ++n) {
+        const int col = 8 * (nb + n) + g;
+        const uint32_t bv0 = bf16_as_tf32(vb[ja * kPB + col]), bv1 = bf16_as_tf32(vb[jb * kPB + col]);
+        const uint32_t bk0 = bf16_as_tf32(kb[ja * kPB + col]), bk1 = bf16_as_tf32(kb[jb * kPB + col]);
+        mma_tf32(u[n], ul[0], ul[1], ul[2], ul[3], bv0, bv1);
+        mma_tf32(u[n], uh[0], uh[1], uh[2], uh[3], bv0, bv1);
+        mma_tf32(wv[n], wl[0], wl[1], wl[2], wl[3], bk0, bk1);
+        mma_tf32(wv[n], wh[0], wh[1], wh[2], wh[3], bk0, bk1);
       }
     }
 #pragma unroll
-    for (int a = 0; a < 32; ++a) {
-      out[ChunkWs::U + (i0 + a) * kD + e] = u[a];
-      out[ChunkWs::W + (i0 + a) * kD + e] = w[a];
-    }
+    for (int n = 0; n < 8; ++n)
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        const int i = 16 * mt + g + 8 * half, e = 8 * (nb + n) + 2 * cq;
+        *reinterpret_cast<float2*>(out + ChunkWs::U + i * kD + e) = make_float2(u[n][2 * half], u[n][2 * half + 1]);
+        *reinterpret_cast<float2*>(out + ChunkWs::W + i * kD + e) = make_float2(wv[n][2 * half], wv[n][2 * half + 1]);
+      }
   }
 }
 
@@ -251,26 +308,8 @@ struct ScanParams {
   int L, H, NC;
 };
 
-// ---- 3xTF32 tensor-core products (m16n8k8): x = hi + lo with hi, lo TF32; hi*hi + hi*lo + lo*hi
+// ---- 3xTF32 products in the scan (m16n8k8): x = hi + lo with hi, lo TF32; hi*hi + hi*lo + lo*hi
 // keeps ~FP32 accuracy (the dropped lo*lo term is below FP32 rounding of the sum).
-Q35_DEV uint32_t tf32_bits(float x) {
-  uint32_t r;
-  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
-  return r;
-}
-Q35_DEV void split_tf32(float x, uint32_t& hi, uint32_t& lo) {
-  hi = tf32_bits(x);
-  lo = tf32_bits(x - __uint_as_float(hi));
-}
-Q35_DEV void mma_tf32(float d[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
-// Fragments of m16n8k8 (g = lane / 4, c = lane % 4): a = {A[g][c], A[g+8][c], A[g][c+4], A[g+8][c+4]},
-// b = {B[c][g], B[c+4][g]}, d = {D[g][2c], D[g][2c+1], D[g+8][2c], D[g+8][2c+1]}.
-
 Q35_DEV void cp_async16(float* dst, const float* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
                : "memory");
@@ -464,8 +503,8 @@ __global__ void __launch_bounds__(kThreads, 1) delta_chunk_scan_kernel(ScanParam
     for (int i = 0; i < 4; ++i) Sg[frag_row(i) * kD + frag_col(nt, i)] = s[nt][i];
 }
 
-constexpr size_t kPrepSmem = (size_t)(3 * kC * kP) * sizeof(float);
-static_assert(kC * 65 + 48 * 16 <= kC * kP, "T and the solve scratch fit in q's region");
+constexpr size_t kPrepSmem = (size_t)3 * kC * kPB * sizeof(bf16) + (size_t)(kC * kTS + 48 * 16) * sizeof(float);
+static_assert((3 * kC * kPB * sizeof(bf16)) % 16 == 0, "T starts 16-byte aligned");
 constexpr size_t kScanSmem =
     (size_t)(2 * kC * kPW + kC * kPK2 + kC * kPP + kC * kVS + 2 * kC * kPS + 2 * kD * kPS) * sizeof(float);
 
