@@ -239,18 +239,22 @@ Q35_DEV void cp16(void* dst, const void* src) {
 }
 
 template <int G>
-__global__ void __launch_bounds__(G * 32) prefill_attn_mma_kernel(const bf16* __restrict__ Q, const bf16* __restrict__ K,
-                                                                 const bf16* __restrict__ V, bf16* __restrict__ O,
-                                                                 int Hq, int Hkv, int L, int kv_len, int q_offset,
-                                                                 float scale) {
+__global__ void __launch_bounds__(2 * G * 32) prefill_attn_mma_kernel(const bf16* __restrict__ Q, const bf16* __restrict__ K,
+                                                                     const bf16* __restrict__ V, bf16* __restrict__ O,
+                                                                     int Hq, int Hkv, int L, int kv_len, int q_offset,
+                                                                     float scale) {
   extern __shared__ __align__(16) unsigned char fa_smem[];
   bf16* Qs = reinterpret_cast<bf16*>(fa_smem);        // [G][16][stride]
-  bf16* Ks = Qs + G * kFaRows * kFaStride;             // [2][32][stride]
-  bf16* Vs = Ks + 2 * kFaKeys * kFaStride;             // [2][32][stride]
-  constexpr int NT = G * 32;
+  bf16* KVs = Qs + G * kFaRows * kFaStride;            // per key group: K [2][32][stride], V [2][32][stride]
+  constexpr int NG = G * 32;                           // threads of one key group
+  constexpr int NT = 2 * NG;
   const int q0 = blockIdx.x * kFaRows, g = blockIdx.y, b = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int h = g * G + warp;
+  const int kg = warp / G, wq = warp % G;  // key group (even / odd key tiles), query head in the group
+  const int gt = threadIdx.x - kg * NG;    // thread index within the key group
+  const int h = g * G + wq;
+  bf16* Ks = KVs + kg * 4 * kFaKeys * kFaStride;
+  bf16* Vs = Ks + 2 * kFaKeys * kFaStride;
   const bf16* Kg = K + ((int64_t)b * Hkv + g) * kv_len * kD;
   const bf16* Vg = V + ((int64_t)b * Hkv + g) * kv_len * kD;
   // queries of the G heads (rows past L read as zero)
@@ -264,9 +268,9 @@ __global__ void __launch_bounds__(G * 32) prefill_attn_mma_kernel(const bf16* __
   }
   const int kend = min(kv_len, q0 + kFaRows - 1 + q_offset + 1);  // keys any row of the block may see
   const int ntiles = (kend + kFaKeys - 1) / kFaKeys;
-  auto load_tile = [&](int t, int buf) {
+  auto load_tile = [&](int t, int buf) {  // by this key group's threads
     const int k0 = t * kFaKeys;
-    for (int i = threadIdx.x; i < kFaKeys * (kD / 8); i += NT) {
+    for (int i = gt; i < kFaKeys * (kD / 8); i += NG) {
       const int r = i / (kD / 8), c = (i % (kD / 8)) * 8;
       bf16* kd = Ks + (buf * kFaKeys + r) * kFaStride + c;
       bf16* vd = Vs + (buf * kFaKeys + r) * kFaStride + c;
@@ -279,8 +283,11 @@ __global__ void __launch_bounds__(G * 32) prefill_attn_mma_kernel(const bf16* __
       }
     }
   };
-  if (ntiles > 0) load_tile(0, 0);
+  auto group_sync = [&]() { asm volatile("bar.sync %0, %1;" ::"r"(1 + kg), "r"(NG) : "memory"); };
+  if (kg < ntiles) load_tile(kg, 0);
   asm volatile("cp.async.commit_group;" ::: "memory");
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+  __syncthreads();  // the query tile (loaded by both groups) and the first key tiles are in place
 
   const int gq = lane >> 2, c4 = lane & 3;  // fragment row group / column pair
   float o[32][4];
@@ -288,14 +295,15 @@ __global__ void __launch_bounds__(G * 32) prefill_attn_mma_kernel(const bf16* __
   for (int n = 0; n < 32; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
   float m0 = -FLT_MAX, m1 = -FLT_MAX, l0 = 0.f, l1 = 0.f;  // rows gq and gq + 8
   const int qi0 = q0 + gq + q_offset, qi1 = qi0 + 8;
-  const uint32_t qbase = (uint32_t)__cvta_generic_to_shared(Qs + (warp * kFaRows + (lane & 15)) * kFaStride) +
+  const uint32_t qbase = (uint32_t)__cvta_generic_to_shared(Qs + (wq * kFaRows + (lane & 15)) * kFaStride) +
                          (lane >> 4) * 16;
-  for (int t = 0; t < ntiles; ++t) {
-    const int buf = t & 1;
-    if (t + 1 < ntiles) load_tile(t + 1, buf ^ 1);
+  int it = 0;
+  for (int t = kg; t < ntiles; t += 2, ++it) {
+    const int buf = it & 1;
+    if (t + 2 < ntiles) load_tile(t + 2, buf ^ 1);
     asm volatile("cp.async.commit_group;" ::: "memory");
     asm volatile("cp.async.wait_group 1;" ::: "memory");
-    __syncthreads();
+    group_sync();
     // ---- S = Q K^T for 16 rows x 32 keys
     float s[4][4];
 #pragma unroll
@@ -389,9 +397,40 @@ __global__ void __launch_bounds__(G * 32) prefill_attn_mma_kernel(const bf16* __
         mma_bf16(o[2 * np + 1], l0p, l1p, l2p, l3p, b2, b3);
       }
     }
-    __syncthreads();  // this buffer is refilled two tiles later
+    group_sync();  // this buffer is refilled two tiles later
   }
-  // ---- normalise and store (rows gq, gq + 8; dims n*8 + 2*c4 + {0,1})
+  // ---- merge the two key groups' partial softmax states (group 1 parks them in the freed key /
+  // value tiles), then normalise and store (rows gq, gq + 8; dims n*8 + 2*c4 + {0,1})
+  __syncthreads();
+  constexpr int kPart = 4 + 32 * 4 + 1;  // m0 m1 l0 l1, o, pad (odd stride: no bank conflicts)
+  float* pp = reinterpret_cast<float*>(KVs) + (wq * 32 + lane) * kPart;
+  if (kg == 1) {
+    pp[0] = m0;
+    pp[1] = m1;
+    pp[2] = l0;
+    pp[3] = l1;
+#pragma unroll
+    for (int n = 0; n < 32; ++n)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) pp[4 + 4 * n + e] = o[n][e];
+  }
+  __syncthreads();
+  if (kg == 1) return;
+  {
+    const float mb0 = pp[0], mb1 = pp[1], lb0 = pp[2], lb1 = pp[3];
+    const float mn0 = fmaxf(m0, mb0), mn1 = fmaxf(m1, mb1);
+    const float fa0 = (m0 == -FLT_MAX) ? 0.f : expf(m0 - mn0), fb0 = (mb0 == -FLT_MAX) ? 0.f : expf(mb0 - mn0);
+    const float fa1 = (m1 == -FLT_MAX) ? 0.f : expf(m1 - mn1), fb1 = (mb1 == -FLT_MAX) ? 0.f : expf(mb1 - mn1);
+    l0 = l0 * fa0 + lb0 * fb0;
+    l1 = l1 * fa1 + lb1 * fb1;
+#pragma unroll
+    for (int n = 0; n < 32; ++n) {
+      o[n][0] = o[n][0] * fa0 + pp[4 + 4 * n] * fb0;
+      o[n][1] = o[n][1] * fa0 + pp[5 + 4 * n] * fb0;
+      o[n][2] = o[n][2] * fa1 + pp[6 + 4 * n] * fb1;
+      o[n][3] = o[n][3] * fa1 + pp[7 + 4 * n] * fb1;
+    }
+  }
   const float inv0 = l0 > 0.f ? 1.0f / l0 : 0.f, inv1 = l1 > 0.f ? 1.0f / l1 : 0.f;
   const int r0 = q0 + gq, r1 = r0 + 8;
 #pragma unroll
@@ -410,10 +449,13 @@ template <int G>
 int launch_prefill_mma(const void* q, const void* k, const void* v, void* out, int64_t batch, int64_t q_heads,
                        int64_t kv_heads, int64_t seq_len, int64_t kv_len, int64_t q_offset, float scale,
                        cudaStream_t stream) {
-  const size_t smem = (size_t)(G * kFaRows + 4 * kFaKeys) * kFaStride * sizeof(bf16);
+  // query tile + two key groups x two buffers x (K, V) tiles; the merge reuses the key tiles
+  const size_t smem = (size_t)(G * kFaRows + 8 * kFaKeys) * kFaStride * sizeof(bf16);
+  static_assert((size_t)4 * 32 * (4 + 32 * 4 + 1) * sizeof(float) <= (size_t)8 * kFaKeys * kFaStride * sizeof(bf16),
+                "the merge partials fit in the key / value tiles");
   cudaFuncSetAttribute(prefill_attn_mma_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   const dim3 grid((unsigned)((seq_len + kFaRows - 1) / kFaRows), (unsigned)kv_heads, (unsigned)batch);
-  prefill_attn_mma_kernel<G><<<grid, G * 32, smem, stream>>>((const bf16*)q, (const bf16*)k, (const bf16*)v,
+  prefill_attn_mma_kernel<G><<<grid, 2 * G * 32, smem, stream>>>((const bf16*)q, (const bf16*)k, (const bf16*)v,
                                                              (bf16*)out, (int)q_heads, (int)kv_heads, (int)seq_len,
                                                              (int)kv_len, (int)q_offset, scale);
   return q35_check_launch("prefill_attention");

@@ -1,7 +1,8 @@
 // Row norms and elementwise activations (reference: qwen35_fused/kernels.py:24-333).
 //
-// One CTA per row for the 2048-wide norms (the reduction stays on chip); one warp per row for
-// the 128-wide gated norm; vectorised grid-stride loops for the elementwise ops.
+// One CTA per row for the 2048-wide norms (the reduction stays on chip, 16-byte chunks at width
+// 2048); one warp per row for the 128-wide gated norm (8-byte chunks); vectorised grid-stride loops
+// for the elementwise ops.
 #include "common.cuh"
 
 using namespace q35;
@@ -38,6 +39,77 @@ __global__ void __launch_bounds__(kRowThreads) rms_rows_kernel(const bf16* __res
     if (ADD) v = rbf(v + bf2f(ur[c]));
     out[row * width + c] = f2bf(v * r * (1.0f + bf2f(w[c])));
   }
+}
+
+// Width 2048: one 16-byte chunk per thread, x read once and kept in registers; the per-thread
+// partial sums run over 8 consecutive elements, as in the decode GEMVs' RMSNorm prologue, so the
+// prefill and decode norms of a row are bit-identical.
+template <bool ADD>
+__global__ void __launch_bounds__(kRowThreads) rms_rows2048_kernel(const bf16* __restrict__ x,
+                                                                   const bf16* __restrict__ upd,
+                                                                   const bf16* __restrict__ w,
+                                                                   bf16* __restrict__ resid_out,
+                                                                   bf16* __restrict__ out, float eps) {
+  constexpr int kW = 2048;
+  __shared__ float red[kRowThreads / 32];
+  const int64_t base = (int64_t)blockIdx.x * kW + 8 * threadIdx.x;
+  float f[8];
+  unpack_bf16x8(*reinterpret_cast<const uint4*>(x + base), f);
+  if (ADD) {
+    float u[8];
+    unpack_bf16x8(*reinterpret_cast<const uint4*>(upd + base), u);
+    __align__(16) bf16 o[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      f[j] = rbf(f[j] + u[j]);
+      o[j] = f2bf(f[j]);
+    }
+    *reinterpret_cast<uint4*>(resid_out + base) = *reinterpret_cast<const uint4*>(o);
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) ss += f[j] * f[j];
+  const float r = rsqrt_ieee(block_sum<kRowThreads / 32>(ss, red) / (float)kW + eps);
+  float wv[8];
+  unpack_bf16x8(*reinterpret_cast<const uint4*>(w + 8 * threadIdx.x), wv);
+  __align__(16) bf16 o[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) o[j] = f2bf(f[j] * r * (1.0f + wv[j]));
+  *reinterpret_cast<uint4*>(out + base) = *reinterpret_cast<const uint4*>(o);
+}
+
+// Width 128 (the DeltaNet head): one warp per row, four consecutive values per lane in 8-byte
+// loads and stores, x read once.
+__global__ void gated_rms128_kernel(const bf16* __restrict__ x, const bf16* __restrict__ gate,
+                                    const bf16* __restrict__ w, bf16* __restrict__ out, int64_t rows, float eps,
+                                    int gate_group, int64_t gate_stride) {
+  constexpr int kW = 128;
+  const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  auto unpack4 = [](uint2 v, float (&f)[4]) {
+    f[0] = __uint_as_float(v.x << 16);
+    f[1] = __uint_as_float(v.x & 0xFFFF0000u);
+    f[2] = __uint_as_float(v.y << 16);
+    f[3] = __uint_as_float(v.y & 0xFFFF0000u);
+  };
+  float xf[4], gf[4], wf[4];
+  unpack4(*reinterpret_cast<const uint2*>(x + row * kW + 4 * lane), xf);
+  unpack4(*reinterpret_cast<const uint2*>(gate + (row / gate_group) * gate_stride + (row % gate_group) * kW + 4 * lane),
+          gf);
+  unpack4(*reinterpret_cast<const uint2*>(w + 4 * lane), wf);
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) ss += xf[j] * xf[j];
+  const float r = rsqrt_ieee(warp_sum(ss) / (float)kW + eps);
+  __align__(8) bf16 o[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float nrm = rbf(xf[j] * r);
+    const float wt = rbf(nrm * wf[j]);
+    o[j] = f2bf(wt * silu_f(gf[j]));
+  }
+  *reinterpret_cast<uint2*>(out + row * kW + 4 * lane) = *reinterpret_cast<const uint2*>(o);
 }
 
 // One warp per row: bf16(bf16(bf16(norm(x)) * w) * silu(gate)) (kernels.py:115-155).
@@ -121,8 +193,12 @@ extern "C" int q35_rms_norm(const void* x, const void* weight, void* out, int64_
   Q35_REQUIRE(rows >= 0 && width > 0 && width <= 65536, "rms_norm: bad shape rows=%lld width=%lld",
               (long long)rows, (long long)width);
   if (rows == 0) return Q35_OK;
-  rms_rows_kernel<false><<<(unsigned)rows, kRowThreads, 0, (cudaStream_t)stream>>>(
-      (const bf16*)x, nullptr, (const bf16*)weight, nullptr, (bf16*)out, (int)width, eps);
+  if (width == 2048 && Q35_ALIGNED(x, 16) && Q35_ALIGNED(weight, 16) && Q35_ALIGNED(out, 16))
+    rms_rows2048_kernel<false><<<(unsigned)rows, kRowThreads, 0, (cudaStream_t)stream>>>(
+        (const bf16*)x, nullptr, (const bf16*)weight, nullptr, (bf16*)out, eps);
+  else
+    rms_rows_kernel<false><<<(unsigned)rows, kRowThreads, 0, (cudaStream_t)stream>>>(
+        (const bf16*)x, nullptr, (const bf16*)weight, nullptr, (bf16*)out, (int)width, eps);
   return q35_check_launch("rms_norm");
 }
 
@@ -133,23 +209,27 @@ extern "C" int q35_residual_add_rms_norm(const void* residual, const void* updat
               "residual_add_rms_norm: null pointer");
   Q35_REQUIRE(rows >= 0 && width > 0 && width <= 65536, "residual_add_rms_norm: bad shape");
   if (rows == 0) return Q35_OK;
-  rms_rows_kernel<true><<<(unsigned)rows, kRowThreads, 0, (cudaStream_t)stream>>>(
-      (const bf16*)residual, (const bf16*)update, (const bf16*)weight, (bf16*)residual_out,
-      (bf16*)norm_out, (int)width, eps);
+  if (width == 2048 && Q35_ALIGNED(residual, 16) && Q35_ALIGNED(update, 16) && Q35_ALIGNED(weight, 16) &&
+      Q35_ALIGNED(residual_out, 16) && Q35_ALIGNED(norm_out, 16))
+    rms_rows2048_kernel<true><<<(unsigned)rows, kRowThreads, 0, (cudaStream_t)stream>>>(
+        (const bf16*)residual, (const bf16*)update, (const bf16*)weight, (bf16*)residual_out, (bf16*)norm_out,
+        eps);
+  else
+    rms_rows_kernel<true><<<(unsigned)rows, kRowThreads, 0, (cudaStream_t)stream>>>(
+        (const bf16*)residual, (const bf16*)update, (const bf16*)weight, (bf16*)residual_out,
+        (bf16*)norm_out, (int)width, eps);
   return q35_check_launch("residual_add_rms_norm");
 }
+
+int q35_gated_rms_strided_launch(const void* x, const void* gate, int gate_group, int64_t gate_stride,
+                                 const void* weight, void* out, int64_t rows, int64_t width, float eps,
+                                 cudaStream_t stream);
 
 extern "C" int q35_gated_rms_norm(const void* x, const void* gate, const void* weight, void* out,
                                   int64_t rows, int64_t width, float eps, void* stream) {
   Q35_REQUIRE(x && gate && weight && out, "gated_rms_norm: null pointer");
   Q35_REQUIRE(rows >= 0 && width > 0, "gated_rms_norm: bad shape");
-  if (rows == 0) return Q35_OK;
-  const int rows_per_block = 8;
-  gated_rms_kernel<<<(unsigned)((rows + rows_per_block - 1) / rows_per_block), 32 * rows_per_block, 0,
-                     (cudaStream_t)stream>>>((const bf16*)x, (const bf16*)gate,
-                                             (const bf16*)weight, (bf16*)out, rows, (int)width, eps,
-                                             1, width);
-  return q35_check_launch("gated_rms_norm");
+  return q35_gated_rms_strided_launch(x, gate, 1, width, weight, out, rows, width, eps, (cudaStream_t)stream);
 }
 
 int q35_gated_rms_strided_launch(const void* x, const void* gate, int gate_group, int64_t gate_stride,
@@ -157,9 +237,15 @@ int q35_gated_rms_strided_launch(const void* x, const void* gate, int gate_group
                                  cudaStream_t stream) {
   if (rows == 0) return Q35_OK;
   const int rows_per_block = 8;
-  gated_rms_kernel<<<(unsigned)((rows + rows_per_block - 1) / rows_per_block), 32 * rows_per_block, 0,
-                     stream>>>((const bf16*)x, (const bf16*)gate, (const bf16*)weight, (bf16*)out, rows,
-                               (int)width, eps, gate_group, gate_stride);
+  const unsigned blocks = (unsigned)((rows + rows_per_block - 1) / rows_per_block);
+  if (width == 128 && gate_stride % 4 == 0 && Q35_ALIGNED(x, 8) && Q35_ALIGNED(gate, 8) && Q35_ALIGNED(weight, 8) &&
+      Q35_ALIGNED(out, 8))
+    gated_rms128_kernel<<<blocks, 32 * rows_per_block, 0, stream>>>(
+        (const bf16*)x, (const bf16*)gate, (const bf16*)weight, (bf16*)out, rows, eps, gate_group, gate_stride);
+  else
+    gated_rms_kernel<<<blocks, 32 * rows_per_block, 0, stream>>>((const bf16*)x, (const bf16*)gate,
+                                                                 (const bf16*)weight, (bf16*)out, rows,
+                                                                 (int)width, eps, gate_group, gate_stride);
   return q35_check_launch("gated_rms_strided");
 }
 
