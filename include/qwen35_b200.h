@@ -255,6 +255,14 @@ int q35_delta_chunked(const void* qkv, const void* packed, const void* a_log, co
                       float* state, void* out, int64_t batch, int64_t seq_len, int64_t heads,
                       int64_t dim, int64_t packed_stride, void* workspace, size_t workspace_bytes,
                       void* stream);
+/* The same with the causal conv folded in (kernels.py:659 causal_conv1d_fused on the [q k v]
+ * columns of packed, 4 taps, starting from a zero history, then the chunked rule): reads the
+ * raw projection `packed` [B, L, packed_stride] instead of a conv output, writes conv_state
+ * [B, 3*H*D, 4] (the last 4 raw inputs); seq_len >= 4. Workspace as for q35_delta_chunked. */
+int q35_delta_chunked_conv(const void* packed, const void* conv_weight, void* conv_state, const void* a_log,
+                           const void* dt_bias, float* state, void* out, int64_t batch, int64_t seq_len,
+                           int64_t heads, int64_t dim, int64_t packed_stride, void* workspace,
+                           size_t workspace_bytes, void* stream);
 
 /* Fused DeltaNet decode step (integration.py:245-272 for L == 1): conv update + SiLU, q/k L2
  * norm, gated delta step on the fp32 state, gated RMSNorm with z. packed [B, packed_stride]

@@ -46,7 +46,7 @@ int q35_set_counters_launch(int64_t* a, int64_t* b, int64_t value, cudaStream_t 
 size_t q35_delta_chunk_workspace_bytes(int64_t batch, int64_t heads, int64_t max_len);
 int q35_delta_chunked_launch(const void* qkv, const void* packed, const void* a_log, const void* dt_bias, float* state,
                              void* out, int64_t batch, int64_t seq_len, int64_t heads, int64_t packed_stride,
-                             float* ws, cudaStream_t s);
+                             float* ws, cudaStream_t s, const void* conv_weight, void* conv_state);
 size_t q35_attn_decode_workspace_size(int64_t batch, int64_t q_heads, int64_t kv_heads, int64_t head_dim,
                                       int64_t cache_len);
 struct q35_pk_plan;
@@ -344,14 +344,20 @@ extern "C" int q35_decoder_prefill(q35_decoder* dec, const int64_t* ids, int64_t
     Q35_TRY(q35_rms_norm(B.p_resid, L.in_ln, B.p_norm, Lt, H, d.eps, s));
     if (L.kind == 0) {
       Q35_TRY(proj(B.p_norm, H, L.mix_in, L.mix_in_scale, B.p_packed, d.delta_rows, Q35_EPI_STORE));
-      Q35_TRY(q35_causal_conv1d(B.p_packed, L.conv_w, L.conv_state, B.p_conv, 1, Lt, d.delta_rows, conv_dim,
-                                d.conv_kernel, s));
-      if (d.prefill_delta == 0)
-        Q35_TRY(q35_delta_chunked_launch(B.p_conv, B.p_packed, L.a_log, L.dt_bias, L.rec_state, B.p_core, 1, Lt,
-                                         d.lin_heads, d.delta_rows, B.p_chunk, s));
-      else
-        Q35_TRY(q35_delta_recurrent(B.p_conv, B.p_packed, L.a_log, L.dt_bias, L.rec_state, B.p_core, 1, Lt,
-                                    d.lin_heads, d.lin_dk, d.delta_rows, s));
+      if (d.prefill_delta == 0 && d.conv_kernel == 4 && Lt >= 4) {
+        // causal conv folded into the chunk prep (reads the raw [q k v] columns of the projection)
+        Q35_TRY(q35_delta_chunked_launch(nullptr, B.p_packed, L.a_log, L.dt_bias, L.rec_state, B.p_core, 1, Lt,
+                                         d.lin_heads, d.delta_rows, B.p_chunk, s, L.conv_w, L.conv_state));
+      } else {
+        Q35_TRY(q35_causal_conv1d(B.p_packed, L.conv_w, L.conv_state, B.p_conv, 1, Lt, d.delta_rows, conv_dim,
+                                  d.conv_kernel, s));
+        if (d.prefill_delta == 0)
+          Q35_TRY(q35_delta_chunked_launch(B.p_conv, B.p_packed, L.a_log, L.dt_bias, L.rec_state, B.p_core, 1, Lt,
+                                           d.lin_heads, d.delta_rows, B.p_chunk, s, nullptr, nullptr));
+        else
+          Q35_TRY(q35_delta_recurrent(B.p_conv, B.p_packed, L.a_log, L.dt_bias, L.rec_state, B.p_core, 1, Lt,
+                                      d.lin_heads, d.lin_dk, d.delta_rows, s));
+      }
       Q35_TRY(q35_gated_rms_strided_launch(B.p_core, B.p_packed + conv_dim, d.lin_heads, d.delta_rows, L.gnorm,
                                            B.p_mix, Lt * d.lin_heads, d.lin_dv, d.eps, s));
       Q35_TRY(proj(B.p_mix, vdim, L.mix_out, L.mix_out_scale, B.p_resid, H, Q35_EPI_RESIDUAL));

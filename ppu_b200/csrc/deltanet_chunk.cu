@@ -30,13 +30,16 @@ struct ChunkWs {  // per (b, h, chunk) record in the workspace, FP32
 };
 
 struct PrepParams {
-  const bf16* qkv;     // [B, L, 3*H*D] conv output
-  const bf16* packed;  // [B, L, stride] ([qkv | z | a | b])
+  const bf16* qkv;       // [B, L, 3*H*D] conv output (when conv_w is null)
+  const bf16* packed;    // [B, L, stride] ([qkv | z | a | b])
   const bf16* a_log;
   const bf16* dt_bias;
-  float* ws;           // [B, H, NC] x ChunkWs::SIZE
+  const bf16* conv_w;    // [3*H*D, 4] or null: the causal conv (4 taps, zero history) runs in the prep
+  bf16* conv_state;      // [B, 3*H*D, 4] receives the last 4 raw inputs (conv_w set, L >= 4)
+  float* ws;             // [B, H, NC] x ChunkWs::SIZE
   int L, H, NC, packed_stride;
 };
+constexpr int kHalo = 3;  // raw rows before the chunk that the 4-tap conv reads
 
 // ---- tensor-core helpers (mma.sync). Fragments of m16n8k8 TF32 (g = lane / 4, c = lane % 4):
 // a = {A[g][c], A[g+8][c], A[g][c+4], A[g+8][c+4]}, b = {B[c][g], B[c+4][g]},
@@ -77,9 +80,11 @@ constexpr int kTS = 68;   // row stride (floats) of T: A-fragment loads hit dist
 // right factor (two MMAs per step, FP32-level accuracy). ~73 KB of shared memory: two CTAs per SM.
 __global__ void __launch_bounds__(kThreads, 2) delta_chunk_prep_kernel(PrepParams p) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  bf16* qb = reinterpret_cast<bf16*>(smem_raw);          // [64][136] raw q
-  bf16* kb = qb + kC * kPB;                              // [64][136] raw k
-  bf16* vb = kb + kC * kPB;                              // [64][136] raw v
+  // q, k, v tiles [kHalo + 64][136] (bf16) with row 0 of the chunk at kHalo: the halo rows hold the
+  // conv's raw inputs before the chunk when the conv runs here
+  bf16* qb = reinterpret_cast<bf16*>(smem_raw) + kHalo * kPB;
+  bf16* kb = qb + (kHalo + kC) * kPB;
+  bf16* vb = kb + (kHalo + kC) * kPB;
   float* T = reinterpret_cast<float*>(vb + kC * kPB);    // [64][68]  A, then T = (I - A)^-1
   float* R = T + kC * kTS;                               // [48][16]  solve scratch
   __shared__ float c[kC], beta[kC], qs[kC], ks[kC], araw[kC], braw[kC], su[kC], sw[kC];
@@ -96,7 +101,73 @@ __global__ void __launch_bounds__(kThreads, 2) delta_chunk_prep_kernel(PrepParam
   constexpr int kLoads = kC * 3 * (kD / 8) / kThreads;  // 12 16-byte loads per thread
   const float a_log = bf2f(p.a_log[h]), dt_bias = bf2f(p.dt_bias[h]);
   const int a_off = 4 * H * kD, b_off = a_off + H;
-  {
+  if (tid < 2 * kC) {  // the token's a (tid < 64) or b (64 <= tid < 128) projection
+    const int r = tid % kC, t = t0 + r;
+    float v = 0.f;
+    if (t < L) v = bf2f(p.packed[((int64_t)b * L + t) * p.packed_stride + (tid < kC ? a_off : b_off) + h]);
+    (tid < kC ? araw : braw)[r] = v;
+  }
+  if (p.conv_w != nullptr) {
+    // raw projection rows t0 - 3 .. t0 + 63 (zero before 0 and from L on) into tile rows -3 .. 63:
+    // every load issued before any store
+    constexpr int kChunks = (kHalo + kC) * 3 * (kD / 8);
+    constexpr int kCLoads = (kChunks + kThreads - 1) / kThreads;  // 13 16-byte loads per thread
+    uint4 raw[kCLoads];
+#pragma unroll
+    for (int u = 0; u < kCLoads; ++u) {
+      const int i = tid + u * kThreads;
+      const int rr = i / (3 * kD / 8), rem = i % (3 * kD / 8);
+      const int which = rem / (kD / 8), col = (rem % (kD / 8)) * 8;
+      const int t = t0 - kHalo + rr;
+      raw[u] = (i < kChunks && t >= 0 && t < L)
+                   ? *reinterpret_cast<const uint4*>(p.packed + ((int64_t)b * L + t) * p.packed_stride + which * H * kD +
+                                                     h * kD + col)
+                   : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int u = 0; u < kCLoads; ++u) {
+      const int i = tid + u * kThreads;
+      if (i >= kChunks) break;
+      const int rr = i / (3 * kD / 8), rem = i % (3 * kD / 8);
+      const int which = rem / (kD / 8), col = (rem % (kD / 8)) * 8;
+      *reinterpret_cast<uint4*>((which == 0 ? qb : which == 1 ? kb : vb) + (rr - kHalo) * kPB + col) = raw[u];
+    }
+    __syncthreads();
+    // conv state: the chunk holding token L - 1 stores the head's last 4 raw inputs per channel
+    // (causal_conv1d_fused's state update; rows L - 4 - t0 .. L - 1 - t0 lie in [-3, 63])
+    if (ch == p.NC - 1) {
+      for (int i = tid; i < 3 * kD * 4; i += kThreads) {
+        const int c = i / 4, j = i % 4, which = c / kD, cc = c % kD;
+        const bf16* tile = which == 0 ? qb : which == 1 ? kb : vb;
+        p.conv_state[((int64_t)b * 3 * H * kD + which * H * kD + h * kD + cc) * 4 + j] =
+            tile[(L - 4 + j - t0) * kPB + cc];
+      }
+    }
+    __syncthreads();  // the state copy has read the raw rows the conv overwrites
+    // causal conv + SiLU down each column with a 4-tap register window, in place (output row r
+    // replaces raw row r once read); same tap order and rounding as the separate conv, zero past L
+    for (int c = tid; c < 3 * kD; c += kThreads) {
+      const int which = c / kD, cc = c % kD;
+      bf16* colp = (which == 0 ? qb : which == 1 ? kb : vb) + cc;
+      const int chn = which * H * kD + h * kD + cc;
+      float wk[4], hist[4];
+#pragma unroll
+      for (int tap = 0; tap < 4; ++tap) wk[tap] = bf2f(p.conv_w[(int64_t)chn * 4 + tap]);
+#pragma unroll
+      for (int j = 0; j < kHalo; ++j) hist[j] = bf2f(colp[(j - kHalo) * kPB]);
+#pragma unroll 8
+      for (int r = 0; r < kC; ++r) {
+        hist[3] = bf2f(colp[r * kPB]);
+        float acc = 0.f;
+#pragma unroll
+        for (int tap = 0; tap < 4; ++tap) acc += hist[tap] * wk[tap];
+        colp[r * kPB] = (t0 + r < L) ? f2bf(silu_f(rbf(acc))) : f2bf(0.f);
+        hist[0] = hist[1];
+        hist[1] = hist[2];
+        hist[2] = hist[3];
+      }
+    }
+  } else {
     uint4 raw[kLoads];
 #pragma unroll
     for (int u = 0; u < kLoads; ++u) {
@@ -107,12 +178,6 @@ __global__ void __launch_bounds__(kThreads, 2) delta_chunk_prep_kernel(PrepParam
       raw[u] = (t < L) ? *reinterpret_cast<const uint4*>(p.qkv + ((int64_t)b * L + t) * qkv_stride + which * H * kD +
                                                          h * kD + col)
                        : make_uint4(0, 0, 0, 0);
-    }
-    if (tid < 2 * kC) {  // the token's a (tid < 64) or b (64 <= tid < 128) projection
-      const int r = tid % kC, t = t0 + r;
-      float v = 0.f;
-      if (t < L) v = bf2f(p.packed[((int64_t)b * L + t) * p.packed_stride + (tid < kC ? a_off : b_off) + h]);
-      (tid < kC ? araw : braw)[r] = v;
     }
 #pragma unroll
     for (int u = 0; u < kLoads; ++u) {
@@ -503,8 +568,10 @@ __global__ void __launch_bounds__(kThreads, 1) delta_chunk_scan_kernel(ScanParam
     for (int i = 0; i < 4; ++i) Sg[frag_row(i) * kD + frag_col(nt, i)] = s[nt][i];
 }
 
-constexpr size_t kPrepSmem = (size_t)3 * kC * kPB * sizeof(bf16) + (size_t)(kC * kTS + 48 * 16) * sizeof(float);
-static_assert((3 * kC * kPB * sizeof(bf16)) % 16 == 0, "T starts 16-byte aligned");
+constexpr size_t kPrepSmem =
+    (size_t)3 * (kHalo + kC) * kPB * sizeof(bf16) + (size_t)(kC * kTS + 48 * 16) * sizeof(float);
+static_assert((3 * (kHalo + kC) * kPB * sizeof(bf16)) % 16 == 0, "T starts 16-byte aligned");
+static_assert((kHalo * kPB * sizeof(bf16)) % 16 == 0, "tile rows stay 16-byte aligned");
 constexpr size_t kScanSmem =
     (size_t)(2 * kC * kPW + kC * kPK2 + kC * kPP + kC * kVS + 2 * kC * kPS + 2 * kD * kPS) * sizeof(float);
 
@@ -515,10 +582,15 @@ size_t q35_delta_chunk_workspace_bytes(int64_t batch, int64_t heads, int64_t max
   return (size_t)batch * heads * nc * ChunkWs::SIZE * sizeof(float);
 }
 
+// conv_weight / conv_state non-null: `qkv` is ignored and the causal conv (4 taps, zero history,
+// seq_len >= 4) runs inside the prep kernel on the raw [q k v] columns of `packed`, writing the
+// conv state as causal_conv1d_fused does.
 int q35_delta_chunked_launch(const void* qkv, const void* packed, const void* a_log, const void* dt_bias, float* state,
                              void* out, int64_t batch, int64_t seq_len, int64_t heads, int64_t packed_stride,
-                             float* ws, cudaStream_t s) {
+                             float* ws, cudaStream_t s, const void* conv_weight, void* conv_state) {
   if (batch * seq_len == 0) return Q35_OK;
+  Q35_REQUIRE(conv_weight == nullptr || (conv_state != nullptr && seq_len >= 4),
+              "delta_chunked: the fused conv needs a state and at least 4 tokens");
   const int nc = (int)((seq_len + kC - 1) / kC);
   static bool attr = false;
   if (!attr) {
@@ -526,8 +598,9 @@ int q35_delta_chunked_launch(const void* qkv, const void* packed, const void* a_
     cudaFuncSetAttribute(delta_chunk_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kScanSmem);
     attr = true;
   }
-  PrepParams pp{(const bf16*)qkv, (const bf16*)packed, (const bf16*)a_log, (const bf16*)dt_bias, ws, (int)seq_len,
-                (int)heads, nc, (int)packed_stride};
+  PrepParams pp{(const bf16*)qkv,         (const bf16*)packed,    (const bf16*)a_log, (const bf16*)dt_bias,
+                (const bf16*)conv_weight, (bf16*)conv_state,      ws,                  (int)seq_len,
+                (int)heads,               nc,                     (int)packed_stride};
   delta_chunk_prep_kernel<<<(unsigned)(batch * heads * nc), kThreads, kPrepSmem, s>>>(pp);
   int rc = q35_check_launch("delta_chunk_prep");
   if (rc) return rc;
@@ -551,5 +624,22 @@ extern "C" int q35_delta_chunked(const void* qkv, const void* packed, const void
   Q35_REQUIRE(workspace_bytes >= q35_delta_chunk_workspace_bytes(batch, heads, seq_len),
               "delta_chunked: workspace too small");
   return q35_delta_chunked_launch(qkv, packed, a_log, dt_bias, state, out, batch, seq_len, heads, packed_stride,
-                                  static_cast<float*>(workspace), (cudaStream_t)stream);
+                                  static_cast<float*>(workspace), (cudaStream_t)stream, nullptr, nullptr);
+}
+
+extern "C" int q35_delta_chunked_conv(const void* packed, const void* conv_weight, void* conv_state, const void* a_log,
+                                      const void* dt_bias, float* state, void* out, int64_t batch, int64_t seq_len,
+                                      int64_t heads, int64_t dim, int64_t packed_stride, void* workspace,
+                                      size_t workspace_bytes, void* stream) {
+  Q35_REQUIRE(packed && conv_weight && conv_state && a_log && dt_bias && state && out && workspace,
+              "delta_chunked_conv: null pointer");
+  Q35_REQUIRE(dim == kD, "delta_chunked_conv: head dim must be 128");
+  Q35_REQUIRE(batch >= 0 && seq_len >= 4 && heads >= 1 && packed_stride >= 4 * heads * dim + 2 * heads,
+              "delta_chunked_conv: bad shape (seq_len >= 4)");
+  Q35_REQUIRE(Q35_ALIGNED(packed, 16) && packed_stride % 8 == 0 && Q35_ALIGNED(workspace, 16),
+              "delta_chunked_conv: 16-byte alignment");
+  Q35_REQUIRE(workspace_bytes >= q35_delta_chunk_workspace_bytes(batch, heads, seq_len),
+              "delta_chunked_conv: workspace too small");
+  return q35_delta_chunked_launch(nullptr, packed, a_log, dt_bias, state, out, batch, seq_len, heads, packed_stride,
+                                  static_cast<float*>(workspace), (cudaStream_t)stream, conv_weight, conv_state);
 }

@@ -384,6 +384,23 @@ def delta_chunked_fused(qkv, packed_projection, a_log, dt_bias, state):
     return out
 
 
+def delta_chunked_conv_fused(packed_projection, conv_weight, conv_state, a_log, dt_bias, state):
+    """``causal_conv1d_fused`` on the [q k v] columns (4 taps, zero history) followed by
+    ``delta_chunked_fused``, in one prep + scan pair: ``packed_projection [B, L, rows]`` (raw
+    projection) -> ``[B, L, H, D]``; updates ``conv_state`` and ``state`` in place."""
+    batch, seq_len, rows = packed_projection.shape
+    _, heads, dim, _ = state.shape
+    if seq_len < 4 or not packed_projection.is_contiguous() or conv_state.shape[-1] != 4:
+        raise ValueError("delta chunked conv tensors do not match")
+    out = torch.empty((batch, seq_len, heads, dim), device=packed_projection.device, dtype=BF16)
+    size = L.load().q35_delta_chunked_workspace_size(batch, heads, seq_len)
+    ws = torch.empty(max(size, 16), device=packed_projection.device, dtype=torch.uint8)
+    L.call("q35_delta_chunked_conv", L.ptr(packed_projection), L.ptr(conv_weight.contiguous()), L.ptr(conv_state),
+           L.ptr(a_log.contiguous()), L.ptr(dt_bias.contiguous()), L.ptr(state), L.ptr(out), batch, seq_len, heads,
+           dim, rows, L.ptr(ws), size, _s(packed_projection))
+    return out
+
+
 def delta_decode(packed, conv_weight, conv_state, a_log, dt_bias, norm_weight, state, *, eps: float = 1e-6):
     """Whole DeltaNet decode mixer in one kernel: ``packed [B, rows]`` -> ``[B, H*Dv]`` (gated-normed)."""
     batch = packed.shape[0]

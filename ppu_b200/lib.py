@@ -90,6 +90,7 @@ _SIGS = {
     "q35_delta_decode": (INT, [P, P, P, P, P, P, P, P, I64, I64, I64, I64, F32, P]),
     "q35_delta_chunked_workspace_size": (SZ, [I64, I64, I64]),
     "q35_delta_chunked": (INT, [P, P, P, P, P, P, I64, I64, I64, I64, I64, P, SZ, P]),
+    "q35_delta_chunked_conv": (INT, [P, P, P, P, P, P, P, I64, I64, I64, I64, I64, P, SZ, P]),
     "q35_decoder_workspace_size": (SZ, [C.POINTER(DecoderDesc)]),
     "q35_decoder_create": (INT, [C.POINTER(DecoderDesc), C.POINTER(P)]),
     "q35_decoder_destroy": (None, [P]),

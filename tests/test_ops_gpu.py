@@ -329,6 +329,27 @@ def test_delta_prefill_chunked_equivalence():
     assert torch.allclose(std.cpu(), st, rtol=1e-2, atol=1e-3)
 
 
+@pytest.mark.parametrize("length", [4, 70, 1024])
+def test_delta_chunked_conv_matches_separate_conv(length):
+    """The causal conv folded into the chunk prep equals causal_conv1d_fused followed by
+    delta_chunked_fused bit for bit: conv state, recurrent state and outputs (4-token minimum,
+    a partial chunk with its halo from the previous chunk, the full prefill length)."""
+    H, D = 16, 128
+    packed = randn(1, length, 4 * H * D + 2 * H, seed=length)
+    cw = randn(3 * H * D, 4, seed=11, scale=0.5)
+    a_log, dt_bias = randn(H, seed=12, scale=0.5), randn(H, seed=13, scale=0.5)
+    cs1 = torch.zeros(1, 3 * H * D, 4, dtype=BF16, device=DEV)
+    st1 = torch.zeros(1, H, D, D, device=DEV)
+    conv = K.causal_conv1d_fused(cu(packed), cu(cw), cs1)
+    out1 = K.delta_chunked_fused(conv, cu(packed), cu(a_log), cu(dt_bias), st1)
+    cs2 = torch.zeros_like(cs1)
+    st2 = torch.zeros_like(st1)
+    out2 = K.delta_chunked_conv_fused(cu(packed), cu(cw), cs2, cu(a_log), cu(dt_bias), st2)
+    assert torch.equal(cs1, cs2)
+    assert torch.equal(out1, out2)
+    assert torch.equal(st1, st2)
+
+
 def test_delta_decode_fused_matches_oracle():
     """One DeltaNet decode step: conv update + SiLU, q/k L2 norm, state update, gated norm."""
     packed, conv_w, a_log, dt_bias, gnorm = _delta_inputs(1, seed=5)
