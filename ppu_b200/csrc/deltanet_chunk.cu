@@ -396,14 +396,25 @@ Q35_DEV void load_at_split(const float* base, int ld, int g, int c, uint32_t hi[
 #pragma unroll
   for (int i = 0; i < 4; ++i) split_tf32(a[i], hi[i], lo[i]);
 }
-// d += A * B[k0 .. k0 + 8][n0 .. n0 + 8] in 3xTF32, B given as pre-split [k][kPS] high / low tiles.
-Q35_DEV void mma3s(float d[4], const uint32_t ah[4], const uint32_t al[4], const uint32_t* Bh, const uint32_t* Bl,
+// d += A * B[k0 .. k0 + 8][n0 .. n0 + 8] in 3xTF32, B given as pre-split [k][kPS] high / low tiles,
+// with the three terms in three accumulators: the scan's dependent MMA chains
+// are its latency (a chunk step measured ~4x its MMA issue time), so every product keeps
+// independent chains (main hi*hi, corrections lo*hi and hi*lo) that are summed at the end.
+struct Acc3 {
+  float m[4], c1[4], c2[4];
+};
+Q35_DEV void acc3_zero(Acc3& a) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) a.m[i] = a.c1[i] = a.c2[i] = 0.f;
+}
+Q35_DEV float acc3_value(const Acc3& a, int i) { return a.m[i] + (a.c1[i] + a.c2[i]); }
+Q35_DEV void mma3a(Acc3& d, const uint32_t ah[4], const uint32_t al[4], const uint32_t* Bh, const uint32_t* Bl,
                    int k0, int n0, int g, int c) {
   const int i0 = (k0 + c) * kPS + n0 + g, i1 = i0 + 4 * kPS;
   const uint32_t bh0 = Bh[i0], bh1 = Bh[i1], bl0 = Bl[i0], bl1 = Bl[i1];
-  mma_tf32(d, al[0], al[1], al[2], al[3], bh0, bh1);
-  mma_tf32(d, ah[0], ah[1], ah[2], ah[3], bl0, bl1);
-  mma_tf32(d, ah[0], ah[1], ah[2], ah[3], bh0, bh1);
+  mma_tf32(d.c1, al[0], al[1], al[2], al[3], bh0, bh1);
+  mma_tf32(d.c2, ah[0], ah[1], ah[2], ah[3], bl0, bl1);
+  mma_tf32(d.m, ah[0], ah[1], ah[2], ah[3], bh0, bh1);
 }
 
 // Phase B on the tensor cores. Warp w owns the FP32 state tile S[16 w .. 16 w + 16][0 .. 16] in
@@ -483,10 +494,15 @@ __global__ void __launch_bounds__(kThreads, 1) delta_chunk_scan_kernel(ScanParam
     const bool more = ch + 1 < p.NC;
     asm volatile("cp.async.wait_group 1;" ::: "memory");  // pending: G1(ch), G2(ch)
     __syncthreads();  // W, Qe, U of this chunk and the published S are visible
-    // ---- phase 1: X = [W; Qe] S for rows 16 warp .. + 16 (four chains: n-tile x even / odd k-step)
-    float x[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+    // ---- phase 1: X = [W; Qe] S for rows 16 warp .. + 16 (12 chains: n-tile x even / odd k-step
+    // x three terms)
+    float x[2][4];
     {
-      float y[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+      Acc3 xa[2][2];  // [k-step parity][n-tile]
+#pragma unroll
+      for (int q = 0; q < 2; ++q)
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) acc3_zero(xa[q][nt]);
       const float* A = warp < 4 ? W + warp * 16 * kPW : Qe + (warp - 4) * 16 * kPW;
 #pragma unroll 2
       for (int k0 = 0; k0 < kD; k0 += 16) {
@@ -495,14 +511,14 @@ __global__ void __launch_bounds__(kThreads, 1) delta_chunk_scan_kernel(ScanParam
           const int k = k0 + 8 * hh;
           uint32_t ah[4], al[4];
           load_a_split(A + k, kPW, g, c, ah, al);
-          mma3s(hh ? y[0] : x[0], ah, al, Sh, Sl, k, 0, g, c);
-          mma3s(hh ? y[1] : x[1], ah, al, Sh, Sl, k, 8, g, c);
+          mma3a(xa[hh][0], ah, al, Sh, Sl, k, 0, g, c);
+          mma3a(xa[hh][1], ah, al, Sh, Sl, k, 8, g, c);
         }
       }
 #pragma unroll
       for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
-        for (int i = 0; i < 4; ++i) x[nt][i] += y[nt][i];
+        for (int i = 0; i < 4; ++i) x[nt][i] = acc3_value(xa[0][nt], i) + acc3_value(xa[1][nt], i);
     }
     if (warp < 4) {  // Vn = U - W S (token rows 16 warp + g (+8)), published pre-split
 #pragma unroll
@@ -520,13 +536,24 @@ __global__ void __launch_bounds__(kThreads, 1) delta_chunk_scan_kernel(ScanParam
     // ---- phase 2a: O = Qe S + P Vn for token rows 16 (warp - 4) .. + 16
     if (warp >= 4) {
       const int r = (warp - 4) * 16;
-      float e[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-#pragma unroll 4
-      for (int k0 = 0; k0 < kC; k0 += 8) {
-        uint32_t ah[4], al[4];
-        load_a_split(P + r * kPP + k0, kPP, g, c, ah, al);
-        mma3s(e[0], ah, al, Vh, Vl, k0, 0, g, c);
-        mma3s(e[1], ah, al, Vh, Vl, k0, 8, g, c);
+      float e[2][4];
+      {
+        Acc3 ea[2][2];  // [k-step parity][n-tile]
+#pragma unroll
+        for (int q = 0; q < 2; ++q)
+#pragma unroll
+          for (int nt = 0; nt < 2; ++nt) acc3_zero(ea[q][nt]);
+#pragma unroll
+        for (int k0 = 0; k0 < kC; k0 += 8) {
+          uint32_t ah[4], al[4];
+          load_a_split(P + r * kPP + k0, kPP, g, c, ah, al);
+          mma3a(ea[(k0 >> 3) & 1][0], ah, al, Vh, Vl, k0, 0, g, c);
+          mma3a(ea[(k0 >> 3) & 1][1], ah, al, Vh, Vl, k0, 8, g, c);
+        }
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) e[nt][i] = acc3_value(ea[0][nt], i) + acc3_value(ea[1][nt], i);
       }
 #pragma unroll
       for (int half = 0; half < 2; ++half) {
@@ -543,13 +570,24 @@ __global__ void __launch_bounds__(kThreads, 1) delta_chunk_scan_kernel(ScanParam
     }
     // ---- phase 2b: S <- gl S + Kd^T Vn on this warp's tile (rows 16 warp .. + 16)
     {
-      float d[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-#pragma unroll 4
-      for (int k0 = 0; k0 < kC; k0 += 8) {
-        uint32_t ah[4], al[4];
-        load_at_split(Kd + k0 * kPK2 + warp * 16, kPK2, g, c, ah, al);
-        mma3s(d[0], ah, al, Vh, Vl, k0, 0, g, c);
-        mma3s(d[1], ah, al, Vh, Vl, k0, 8, g, c);
+      float d[2][4];
+      {
+        Acc3 da[2][2];  // [k-step parity][n-tile]
+#pragma unroll
+        for (int q = 0; q < 2; ++q)
+#pragma unroll
+          for (int nt = 0; nt < 2; ++nt) acc3_zero(da[q][nt]);
+#pragma unroll
+        for (int k0 = 0; k0 < kC; k0 += 8) {
+          uint32_t ah[4], al[4];
+          load_at_split(Kd + k0 * kPK2 + warp * 16, kPK2, g, c, ah, al);
+          mma3a(da[(k0 >> 3) & 1][0], ah, al, Vh, Vl, k0, 0, g, c);
+          mma3a(da[(k0 >> 3) & 1][1], ah, al, Vh, Vl, k0, 8, g, c);
+        }
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) d[nt][i] = acc3_value(da[0][nt], i) + acc3_value(da[1][nt], i);
       }
       const float gl = rec_of(ch)[ChunkWs::GL];
 #pragma unroll
