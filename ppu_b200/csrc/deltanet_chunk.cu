@@ -435,6 +435,7 @@ __global__ void __launch_bounds__(kThreads, 1) delta_chunk_scan_kernel(ScanParam
   uint32_t* Vl = Vh + kC * kPS;    // [64][24]
   uint32_t* Sh = Vl + kC * kPS;    // [128][24]
   uint32_t* Sl = Sh + kD * kPS;    // [128][24]
+  float* Epart = reinterpret_cast<float*>(Sl + kD * kPS);  // [8 values][4 warps][32 lanes]: half of P Vn
   const int nvs = kD / kVS;
   const int vs = blockIdx.x % nvs;
   const int h = (blockIdx.x / nvs) % p.H;
@@ -492,6 +493,7 @@ __global__ void __launch_bounds__(kThreads, 1) delta_chunk_scan_kernel(ScanParam
   }
   for (int ch = 0; ch < p.NC; ++ch) {
     const bool more = ch + 1 < p.NC;
+    const float gl = rec_of(ch)[ChunkWs::GL];  // issued now, used after phase 2b
     asm volatile("cp.async.wait_group 1;" ::: "memory");  // pending: G1(ch), G2(ch)
     __syncthreads();  // W, Qe, U of this chunk and the published S are visible
     // ---- phase 1: X = [W; Qe] S for rows 16 warp .. + 16 (12 chains: n-tile x even / odd k-step
@@ -533,39 +535,34 @@ __global__ void __launch_bounds__(kThreads, 1) delta_chunk_scan_kernel(ScanParam
     __syncthreads();  // Vn, P, Kd visible; W, Qe, U free
     if (more) issue_g1(ch + 1);
     commit();
-    // ---- phase 2a: O = Qe S + P Vn for token rows 16 (warp - 4) .. + 16
-    if (warp >= 4) {
-      const int r = (warp - 4) * 16;
-      float e[2][4];
-      {
-        Acc3 ea[2][2];  // [k-step parity][n-tile]
+    // ---- phase 2a: O = Qe S + P Vn for token rows 16 (warp & 3) .. + 16: warps 4-7 (which hold
+    // Qe S) take keys 0-31 of P Vn, warps 0-3 keys 32-63 and park their half in shared memory;
+    // warps 4-7 add it and store O after the chunk's last barrier
+    float e[2][4];
+    {
+      const int r = (warp & 3) * 16, kb0 = warp < 4 ? kC / 2 : 0;
+      Acc3 ea[2][2];  // [k-step parity][n-tile]
 #pragma unroll
-        for (int q = 0; q < 2; ++q)
+      for (int q = 0; q < 2; ++q)
 #pragma unroll
-          for (int nt = 0; nt < 2; ++nt) acc3_zero(ea[q][nt]);
+        for (int nt = 0; nt < 2; ++nt) acc3_zero(ea[q][nt]);
 #pragma unroll
-        for (int k0 = 0; k0 < kC; k0 += 8) {
-          uint32_t ah[4], al[4];
-          load_a_split(P + r * kPP + k0, kPP, g, c, ah, al);
-          mma3a(ea[(k0 >> 3) & 1][0], ah, al, Vh, Vl, k0, 0, g, c);
-          mma3a(ea[(k0 >> 3) & 1][1], ah, al, Vh, Vl, k0, 8, g, c);
-        }
+      for (int kk = 0; kk < kC / 2; kk += 8) {
+        const int k0 = kb0 + kk;
+        uint32_t ah[4], al[4];
+        load_a_split(P + r * kPP + k0, kPP, g, c, ah, al);
+        mma3a(ea[(kk >> 3) & 1][0], ah, al, Vh, Vl, k0, 0, g, c);
+        mma3a(ea[(kk >> 3) & 1][1], ah, al, Vh, Vl, k0, 8, g, c);
+      }
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) e[nt][i] = acc3_value(ea[0][nt], i) + acc3_value(ea[1][nt], i);
+      if (warp < 4) {
 #pragma unroll
         for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
-          for (int i = 0; i < 4; ++i) e[nt][i] = acc3_value(ea[0][nt], i) + acc3_value(ea[1][nt], i);
-      }
-#pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        const int t = ch * kC + r + g + 8 * half;
-        if (t < p.L) {
-          bf16* o = p.out + (((int64_t)b * p.L + t) * p.H + h) * kD + vs * kVS;
-#pragma unroll
-          for (int nt = 0; nt < 2; ++nt) {
-            o[nt * 8 + 2 * c] = f2bf(x[nt][2 * half] + e[nt][2 * half]);
-            o[nt * 8 + 2 * c + 1] = f2bf(x[nt][2 * half + 1] + e[nt][2 * half + 1]);
-          }
-        }
+          for (int i = 0; i < 4; ++i) Epart[((nt * 4 + i) * 4 + warp) * 32 + lane] = e[nt][i];
       }
     }
     // ---- phase 2b: S <- gl S + Kd^T Vn on this warp's tile (rows 16 warp .. + 16)
@@ -589,16 +586,32 @@ __global__ void __launch_bounds__(kThreads, 1) delta_chunk_scan_kernel(ScanParam
 #pragma unroll
           for (int i = 0; i < 4; ++i) d[nt][i] = acc3_value(da[0][nt], i) + acc3_value(da[1][nt], i);
       }
-      const float gl = rec_of(ch)[ChunkWs::GL];
 #pragma unroll
       for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
         for (int i = 0; i < 4; ++i) s[nt][i] = gl * s[nt][i] + d[nt][i];
       publish_s();  // phase 1 readers of Sh / Sl all passed the last barrier
     }
-    __syncthreads();  // P, Kd, Vn free
+    __syncthreads();  // P, Kd, Vn free; the parked halves of P Vn are visible
     if (more) issue_g2(ch + 1);
     commit();
+    if (warp >= 4) {
+      const int r = (warp - 4) * 16;
+      auto ep = [&](int j) { return Epart[(j * 4 + (warp - 4)) * 32 + lane]; };
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        const int t = ch * kC + r + g + 8 * half;
+        if (t < p.L) {
+          bf16* o = p.out + (((int64_t)b * p.L + t) * p.H + h) * kD + vs * kVS;
+#pragma unroll
+          for (int nt = 0; nt < 2; ++nt) {
+            const int i0 = 2 * half, i1 = 2 * half + 1;
+            o[nt * 8 + 2 * c] = f2bf(x[nt][i0] + (e[nt][i0] + ep(nt * 4 + i0)));
+            o[nt * 8 + 2 * c + 1] = f2bf(x[nt][i1] + (e[nt][i1] + ep(nt * 4 + i1)));
+          }
+        }
+      }
+    }
   }
 #pragma unroll
   for (int nt = 0; nt < 2; ++nt)
@@ -611,7 +624,8 @@ constexpr size_t kPrepSmem =
 static_assert((3 * (kHalo + kC) * kPB * sizeof(bf16)) % 16 == 0, "T starts 16-byte aligned");
 static_assert((kHalo * kPB * sizeof(bf16)) % 16 == 0, "tile rows stay 16-byte aligned");
 constexpr size_t kScanSmem =
-    (size_t)(2 * kC * kPW + kC * kPK2 + kC * kPP + kC * kVS + 2 * kC * kPS + 2 * kD * kPS) * sizeof(float);
+    (size_t)(2 * kC * kPW + kC * kPK2 + kC * kPP + kC * kVS + 2 * kC * kPS + 2 * kD * kPS + 4 * 32 * 8) *
+    sizeof(float);
 
 }  // namespace
 
