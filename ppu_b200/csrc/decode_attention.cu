@@ -45,14 +45,25 @@ struct DecodeParams {
   float scale, eps;
 };
 
+Q35_DEV void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
+               : "memory");
+}
+
+constexpr int kBlk = 32;     // cache rows per staged block (one per lane in the block softmax)
+constexpr int kStages = 3;   // cp.async ring depth
+constexpr size_t kAttnDynSmem = 2ull * kStages * kBlk * kD * sizeof(bf16);  // K + V stages (96 KB)
+static_assert(kWarps * 4 * kD * sizeof(float) <= kAttnDynSmem, "the combine buffer fits in the stages");
+
 template <int G, bool FUSED>
 __global__ void __launch_bounds__(kThreads) attn_decode_kernel(DecodeParams p) {
+  extern __shared__ __align__(16) unsigned char attn_dsmem[];
   __shared__ __align__(16) float qf[G][kD];
   __shared__ __align__(16) float nrm[FUSED ? G + 1 : 1][kD];
   __shared__ __align__(16) float kn[kD];
   __shared__ __align__(16) float vn[kD];
-  __shared__ float wm[kWarps][G], wl[kWarps][G];
-  __shared__ __align__(16) float wacc[kWarps][G][kD];
+  __shared__ __align__(16) float bsc[kBlk][G];
+  __shared__ float balpha[G];
   __shared__ float red[kWarps][G + 1];
   __shared__ float cm[kMaxSplits][G], cl[kMaxSplits][G];
   __shared__ float cls[G];
@@ -109,112 +120,156 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(DecodeParams p) {
   int n_rows = (int)(len < 0 ? 0 : (len > p.max_len ? p.max_len : len));
   __syncthreads();
 
-  // ---- this CTA's rows of the cache (FP32 online softmax per warp and head)
+  // ---- this CTA's rows of the cache, in blocks of kBlk rows staged through a kStages cp.async
+  // ring; per block: scores (warp per 4 rows, lanes over dims, one butterfly for all 16 dot
+  // products), one online-softmax rescale per head, then P.V with thread = dim for every head
   const int chunk = (n_rows + S - 1) / S;
   const int r0 = s * chunk;
   const int r1 = min(r0 + chunk, n_rows);
-  float m[G], l[G], acc[G][8], q8[G][8];
-#pragma unroll
-  for (int hh = 0; hh < G; ++hh) {
-    m[hh] = -FLT_MAX;
-    l[hh] = 0.f;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      acc[hh][j] = 0.f;
-      q8[hh][j] = qf[hh][lane * 8 + j];
-    }
-  }
-  auto process = [&](const float kf[8], const float vf[8]) {
-    float sc[G];
-#pragma unroll
-    for (int hh = 0; hh < G; ++hh) {
-      float a = 0.f;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) a = fmaf(q8[hh][j], kf[j], a);
-      sc[hh] = warp_sum(a);
-    }
-#pragma unroll
-    for (int hh = 0; hh < G; ++hh) {
-      const float mn = fmaxf(m[hh], sc[hh]);
-      const float alpha = expf(m[hh] - mn);
-      const float pr = expf(sc[hh] - mn);
-      l[hh] = l[hh] * alpha + pr;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) acc[hh][j] = acc[hh][j] * alpha + pr * vf[j];
-      m[hh] = mn;
-    }
-  };
+  const int nr = r1 > r0 ? r1 - r0 : 0;
+  const int nblk = (nr + kBlk - 1) / kBlk;
+  bf16* stage_k = reinterpret_cast<bf16*>(attn_dsmem);                 // [kStages][kBlk][kD]
+  bf16* stage_v = stage_k + kStages * kBlk * kD;                        // [kStages][kBlk][kD]
   const bf16* Kb = p.cache_k + kv_base;
   const bf16* Vb = p.cache_v + kv_base;
-  // Each warp takes rows r0 + warp, r0 + warp + 8, ...; kRowBatch of them are loaded together so
-  // their HBM latencies overlap (the online softmax then consumes them in order).
-  constexpr int kRowBatch = 4;
-  for (int rb = r0 + warp; rb < r1; rb += kWarps * kRowBatch) {
-    uint4 kc[kRowBatch], vc[kRowBatch];
-#pragma unroll
-    for (int i = 0; i < kRowBatch; ++i) {
-      const int r = rb + i * kWarps;
-      kc[i] = vc[i] = make_uint4(0, 0, 0, 0);
-      if (r < r1) {
-        kc[i] = *reinterpret_cast<const uint4*>(Kb + (int64_t)r * kD + lane * 8);
-        vc[i] = *reinterpret_cast<const uint4*>(Vb + (int64_t)r * kD + lane * 8);
+  auto issue_block = [&](int bi) {
+    if (bi < nblk) {
+      const int rb0 = r0 + bi * kBlk, rows_b = min(kBlk, r1 - rb0);
+      bf16* kd = stage_k + (bi % kStages) * kBlk * kD;
+      bf16* vd = stage_v + (bi % kStages) * kBlk * kD;
+      for (int i = threadIdx.x; i < rows_b * (kD / 8); i += kThreads) {
+        const int r = i / (kD / 8), c8 = (i % (kD / 8)) * 8;
+        cp_async16(kd + r * kD + c8, Kb + (int64_t)(rb0 + r) * kD + c8);
+        cp_async16(vd + r * kD + c8, Vb + (int64_t)(rb0 + r) * kD + c8);
       }
     }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  float q8[G][8];
 #pragma unroll
-    for (int i = 0; i < kRowBatch; ++i) {
-      if (rb + i * kWarps >= r1) break;
-      float kf[8], vf[8];
-      unpack_bf16x8(kc[i], kf);
-      unpack_bf16x8(vc[i], vf);
-      process(kf, vf);
-    }
-  }
-  if (FUSED && s == S - 1 && warp == kWarps - 1) {  // the current token, from shared memory
-    float kf[8], vf[8];
+  for (int hh = 0; hh < G; ++hh)
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      kf[j] = kn[lane * 8 + j];
-      vf[j] = vn[lane * 8 + j];
+    for (int j = 0; j < 8; ++j) q8[hh][j] = qf[hh][lane * 8 + j];
+  float m_run = -FLT_MAX, l_run = 0.f;  // warp hh < G: head hh's running max / sum (all lanes)
+  float acc[G];                          // thread d: un-normalised output of every head at dim d
+#pragma unroll
+  for (int hh = 0; hh < G; ++hh) acc[hh] = 0.f;
+  // one block of rows_b rows: K / V from a stage (bf16) or, for the current token, kn / vn (fp32)
+  auto run_block = [&](const bf16* kst, const bf16* vst, int rows_b, bool current) {
+    {  // scores: warp w takes rows w, w + 8, w + 16, w + 24
+      float v[4 * G];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int r = warp + i * kWarps;
+        float kf[8];
+        if (current) {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) kf[e] = (r == 0) ? kn[lane * 8 + e] : 0.f;
+        } else if (r < rows_b) {
+          unpack_bf16x8(*reinterpret_cast<const uint4*>(kst + r * kD + lane * 8), kf);
+        } else {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) kf[e] = 0.f;
+        }
+#pragma unroll
+        for (int hh = 0; hh < G; ++hh) {
+          float a = 0.f;
+#pragma unroll
+          for (int e = 0; e < 8; ++e) a = fmaf(q8[hh][e], kf[e], a);
+          v[i * G + hh] = a;
+        }
+      }
+      // butterfly over the 4 G partial sums: afterwards lane l holds the full sum of value
+      // index idx(l) (lanes l and l ^ 1 agree)
+      int n = 4 * G;
+#pragma unroll
+      for (int o = 16; o >= 2; o >>= 1) {
+        if (n > 1) {
+          const int half = n / 2;
+          const bool upper = (lane & o) != 0;
+#pragma unroll
+          for (int i = 0; i < 2 * G; ++i) {
+            if (i < half) {
+              const float send = upper ? v[i] : v[i + half];
+              const float keep = upper ? v[i + half] : v[i];
+              v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+            }
+          }
+          n = half;
+        } else {
+          v[0] += __shfl_xor_sync(0xffffffffu, v[0], o);
+        }
+      }
+      v[0] += __shfl_xor_sync(0xffffffffu, v[0], 1);
+      // value index held by this lane: bit k of idx comes from lane bit (4 - k) for the levels used
+      int idx = 0;
+      {
+        int nn = 4 * G, bitpos = 4;
+        while (nn > 1) {
+          idx = idx * 2 + ((lane >> bitpos) & 1);
+          nn /= 2;
+          --bitpos;
+        }
+      }
+      // lanes with the low bits beyond the used levels zero write
+      const int used_levels = (G == 4) ? 4 : (G == 2 ? 3 : 2);
+      const bool writer = (lane & ((1 << (5 - used_levels)) - 1)) == 0;
+      if (writer) {
+        const int i = idx / G, hh = idx % G;
+        const int r = warp + i * kWarps;
+        if (r < kBlk) bsc[r][hh] = (r < rows_b) ? v[0] : -FLT_MAX;
+      }
     }
-    process(kf, vf);
+    __syncthreads();
+    if (warp < G) {  // online softmax for head `warp` over the block's rows (lane = row)
+      const float sv = (lane < rows_b) ? bsc[lane][warp] : -FLT_MAX;
+      const float bm = warp_max(sv);
+      const float mn = fmaxf(m_run, bm);
+      const float alpha = (m_run == -FLT_MAX) ? 0.f : expf(m_run - mn);
+      const float pr = (lane < rows_b) ? expf(sv - mn) : 0.f;
+      l_run = l_run * alpha + warp_sum(pr);
+      m_run = mn;
+      bsc[lane][warp] = pr;
+      if (lane == 0) balpha[warp] = alpha;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int hh = 0; hh < G; ++hh) acc[hh] *= balpha[hh];
+    for (int j = 0; j < rows_b; ++j) {
+      const float vv = current ? vn[d] : bf2f(vst[j * kD + d]);
+      if (G == 4) {  // the row's four weights in one 16-byte shared load
+        const float4 w4 = *reinterpret_cast<const float4*>(&bsc[j][0]);
+        acc[0] = fmaf(w4.x, vv, acc[0]);
+        acc[1 % G] = fmaf(w4.y, vv, acc[1 % G]);
+        acc[2 % G] = fmaf(w4.z, vv, acc[2 % G]);
+        acc[3 % G] = fmaf(w4.w, vv, acc[3 % G]);
+      } else {
+#pragma unroll
+        for (int hh = 0; hh < G; ++hh) acc[hh] = fmaf(bsc[j][hh], vv, acc[hh]);
+      }
+    }
+    __syncthreads();  // bsc and this stage are free
+  };
+  for (int i = 0; i < kStages - 1; ++i) issue_block(i);
+  for (int bi = 0; bi < nblk; ++bi) {
+    issue_block(bi + kStages - 1);
+    asm volatile("cp.async.wait_group %0;" ::"n"(kStages - 1) : "memory");
+    __syncthreads();
+    const int st = bi % kStages;
+    run_block(stage_k + st * kBlk * kD, stage_v + st * kBlk * kD, min(kBlk, nr - bi * kBlk), false);
   }
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+  if (FUSED && s == S - 1) run_block(nullptr, nullptr, 1, true);  // the current token
 
-  // ---- merge this CTA's warps into one partial per head
-  if (lane == 0) {
-#pragma unroll
-    for (int hh = 0; hh < G; ++hh) {
-      wm[warp][hh] = m[hh];
-      wl[warp][hh] = l[hh];
-    }
-  }
-#pragma unroll
-  for (int hh = 0; hh < G; ++hh) {
-    float4* dst = reinterpret_cast<float4*>(&wacc[warp][hh][lane * 8]);
-    dst[0] = make_float4(acc[hh][0], acc[hh][1], acc[hh][2], acc[hh][3]);
-    dst[1] = make_float4(acc[hh][4], acc[hh][5], acc[hh][6], acc[hh][7]);
-  }
-  __syncthreads();
+  // ---- this CTA's partial per head: (max, sum) from the softmax warps, the output from every dim
   const int base = ((b * Hkv + g) * S) * G;
-#pragma unroll
-  for (int hh = 0; hh < G; ++hh) {
-    float M = -FLT_MAX;
-#pragma unroll
-    for (int w = 0; w < kWarps; ++w)
-      if (wl[w][hh] > 0.f) M = fmaxf(M, wm[w][hh]);
-    float Ls = 0.f, A = 0.f;
-#pragma unroll
-    for (int w = 0; w < kWarps; ++w) {
-      const float e = (wl[w][hh] > 0.f) ? expf(wm[w][hh] - M) : 0.f;
-      Ls += wl[w][hh] * e;
-      A += wacc[w][hh][d] * e;
-    }
-    const int slot = base + s * G + hh;
-    p.part[(int64_t)slot * kD + d] = A;
-    if (d == 0) {
-      p.part_ml[2 * slot] = M;
-      p.part_ml[2 * slot + 1] = Ls;
-    }
+  if (warp < G && lane == 0) {
+    const int slot = base + s * G + warp;
+    p.part_ml[2 * slot] = m_run;
+    p.part_ml[2 * slot + 1] = l_run;
   }
+#pragma unroll
+  for (int hh = 0; hh < G; ++hh) p.part[(int64_t)(base + s * G + hh) * kD + d] = acc[hh];
   __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) ticket_s = atomicAdd(&p.tickets[b * Hkv + g], 1u);
@@ -222,7 +277,9 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(DecodeParams p) {
   if (ticket_s != (unsigned)(S - 1)) return;
   __threadfence();
 
-  // ---- last CTA: combine the S partials of each head with all warps
+  // ---- last CTA: combine the S partials of each head with all warps (per-warp sums in the
+  // stage memory, free now)
+  float (*wacc)[G][kD] = reinterpret_cast<float (*)[G][kD]>(attn_dsmem);
   for (int i = threadIdx.x; i < S * G; i += kThreads) {
     const float mi = __ldcg(p.part_ml + 2 * (base + i));
     const float li = __ldcg(p.part_ml + 2 * (base + i) + 1);
@@ -306,11 +363,6 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(DecodeParams p) {
 constexpr int kClusterCTAs = 8;
 constexpr int kClRows = 160;
 constexpr size_t kClSmemBytes = 2ull * kClRows * kD * sizeof(bf16);
-
-Q35_DEV void cp_async16(void* dst, const void* src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
-               : "memory");
-}
 
 template <int G>
 __global__ void __launch_bounds__(kThreads, 1) attn_decode_cluster_kernel(DecodeParams p) {
@@ -498,7 +550,9 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_cluster_kernel(Decode
 
 int choose_splits(int64_t batch, int64_t kv_heads, int64_t cache_len) {
   int64_t s = (cache_len + kRowsPerSplit - 1) / kRowsPerSplit;  // >= 64 rows per CTA
-  const int64_t fill = (2 * kNumSMs + batch * kv_heads - 1) / (batch * kv_heads);
+  // one wave of two CTAs per SM: rounding up here left a few CTAs for a second wave (1.03 waves
+  // at 8 x 2 KV heads), doubling the kernel time
+  const int64_t fill = (2 * kNumSMs) / (batch * kv_heads);
   if (s > fill) s = fill;
   if (s > kMaxSplits) s = kMaxSplits;
   return (int)(s < 1 ? 1 : s);
@@ -555,11 +609,22 @@ int launch_decode(DecodeParams p, int64_t batch, int G, void* ws, cudaStream_t s
   p.part_ml = reinterpret_cast<float*>(base + w.ml);
   p.part = reinterpret_cast<float*>(base + w.part);
   dim3 grid(p.S, p.Hkv, (unsigned)batch);
+  static bool attr = false;
+  if (!attr) {  // two CTAs per SM: the full shared-memory carve-out
+    auto set = [](auto kern) {
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kAttnDynSmem);
+      cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, (int)cudaSharedmemCarveoutMaxShared);
+    };
+    set(attn_decode_kernel<1, FUSED>);
+    set(attn_decode_kernel<2, FUSED>);
+    set(attn_decode_kernel<4, FUSED>);
+    attr = true;
+  }
   cudaError_t e;
   switch (G) {
-    case 1: e = q35_launch(attn_decode_kernel<1, FUSED>, grid, dim3(kThreads), 0, st, pdl, p); break;
-    case 2: e = q35_launch(attn_decode_kernel<2, FUSED>, grid, dim3(kThreads), 0, st, pdl, p); break;
-    case 4: e = q35_launch(attn_decode_kernel<4, FUSED>, grid, dim3(kThreads), 0, st, pdl, p); break;
+    case 1: e = q35_launch(attn_decode_kernel<1, FUSED>, grid, dim3(kThreads), kAttnDynSmem, st, pdl, p); break;
+    case 2: e = q35_launch(attn_decode_kernel<2, FUSED>, grid, dim3(kThreads), kAttnDynSmem, st, pdl, p); break;
+    case 4: e = q35_launch(attn_decode_kernel<4, FUSED>, grid, dim3(kThreads), kAttnDynSmem, st, pdl, p); break;
     default: return q35_fail(Q35_ENOTSUP, "decode attention: group size %d unsupported (1, 2, 4)", G);
   }
   if (e != cudaSuccess) return q35_fail(Q35_ECUDA, "decode attention launch: %s", cudaGetErrorString(e));

@@ -245,11 +245,13 @@ def test_gqa_decode_config2(batch, length):
     assert rel_err(out, want) < 1e-2
 
 
-def test_attn_decode_fused_matches_oracle():
+@pytest.mark.parametrize("Lmax,p", [(600, 517), (2000, 1803)], ids=["cluster", "split-kv"])
+def test_attn_decode_fused_matches_oracle(Lmax, p):
     """Whole decode attention mixer: Q/K norm + partial RoPE at the device position, K/V cache
-    write at row cache_len, attention over rows [0, cache_len], sigmoid gate."""
+    write at row cache_len, attention over rows [0, cache_len], sigmoid gate. Caches up to 1280
+    rows take the cluster kernel, longer ones the split-KV kernel (staged blocks, current token
+    from registers, ticketed combine)."""
     torch.manual_seed(0)
-    Lmax, p = 600, 517
     packed = randn(1, 5120, seed=1)
     qw, kw = randn(256, seed=2, scale=0.1), randn(256, seed=3, scale=0.1)
     kc = randn(1, 2, Lmax, 256, seed=4)
