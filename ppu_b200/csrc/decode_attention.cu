@@ -45,6 +45,49 @@ struct DecodeParams {
   float scale, eps;
 };
 
+// Warp reduction of NV per-lane partial sums at once (transpose butterfly: each level halves the
+// values a lane keeps, exchanging the other half with its partner), NV a power of two <= 32:
+// NV - 1 + 5 - log2(NV) shuffles instead of 5 NV. Afterwards the returned value of lane l is the
+// warp total of value index butterfly_index<NV>(l); lanes that differ only in bits below the
+// levels used agree, and butterfly_writer<NV>(l) picks one of them.
+template <int NV>
+Q35_DEV float butterfly_sum(float (&v)[NV], int lane) {
+  int n = NV;
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) {
+    if (n > 1) {
+      const int half = n / 2;
+      const bool upper = (lane & o) != 0;
+#pragma unroll
+      for (int i = 0; i < NV / 2; ++i) {
+        if (i < half) {
+          const float send = upper ? v[i] : v[i + half];
+          const float keep = upper ? v[i + half] : v[i];
+          v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+        }
+      }
+      n = half;
+    } else {
+      v[0] += __shfl_xor_sync(0xffffffffu, v[0], o);
+    }
+  }
+  return v[0];
+}
+template <int NV>
+Q35_DEV int butterfly_index(int lane) {
+  int idx = 0;
+#pragma unroll
+  for (int nn = NV, bit = 4; nn > 1; nn /= 2, --bit) idx = idx * 2 + ((lane >> bit) & 1);
+  return idx;
+}
+template <int NV>
+Q35_DEV bool butterfly_writer(int lane) {
+  int levels = 0;
+#pragma unroll
+  for (int nn = NV; nn > 1; nn /= 2) ++levels;
+  return (lane & ((1 << (5 - levels)) - 1)) == 0;
+}
+
 Q35_DEV void cp_async16(void* dst, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
                : "memory");
@@ -179,41 +222,9 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(DecodeParams p) {
           v[i * G + hh] = a;
         }
       }
-      // butterfly over the 4 G partial sums: afterwards lane l holds the full sum of value
-      // index idx(l) (lanes l and l ^ 1 agree)
-      int n = 4 * G;
-#pragma unroll
-      for (int o = 16; o >= 2; o >>= 1) {
-        if (n > 1) {
-          const int half = n / 2;
-          const bool upper = (lane & o) != 0;
-#pragma unroll
-          for (int i = 0; i < 2 * G; ++i) {
-            if (i < half) {
-              const float send = upper ? v[i] : v[i + half];
-              const float keep = upper ? v[i + half] : v[i];
-              v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
-            }
-          }
-          n = half;
-        } else {
-          v[0] += __shfl_xor_sync(0xffffffffu, v[0], o);
-        }
-      }
-      v[0] += __shfl_xor_sync(0xffffffffu, v[0], 1);
-      // value index held by this lane: bit k of idx comes from lane bit (4 - k) for the levels used
-      int idx = 0;
-      {
-        int nn = 4 * G, bitpos = 4;
-        while (nn > 1) {
-          idx = idx * 2 + ((lane >> bitpos) & 1);
-          nn /= 2;
-          --bitpos;
-        }
-      }
-      // lanes with the low bits beyond the used levels zero write
-      const int used_levels = (G == 4) ? 4 : (G == 2 ? 3 : 2);
-      const bool writer = (lane & ((1 << (5 - used_levels)) - 1)) == 0;
+      butterfly_sum<4 * G>(v, lane);
+      const int idx = butterfly_index<4 * G>(lane);
+      const bool writer = butterfly_writer<4 * G>(lane);
       if (writer) {
         const int i = idx / G, hh = idx % G;
         const int r = warp + i * kWarps;
@@ -361,22 +372,19 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(DecodeParams p) {
 // of every head from all peers and writes the gated BF16 output. No global scratch, no second
 // pass.
 constexpr int kClusterCTAs = 8;
-constexpr int kClRows = 160;                 // cached rows per CTA (caches up to 8 x 160 rows)
-constexpr int kClRowsPad = kClRows + 16;     // + the current token, rounded up to 16-key steps
-constexpr int kClStride = kD + 8;            // padded row (bf16): ldmatrix rows hit distinct banks
-constexpr size_t kClSmemBytes = (2ull * kClRowsPad + 16) * kClStride * sizeof(bf16);  // K, V, Q tiles
-static_assert(kWarps == kClusterCTAs && kD / kClusterCTAs == 32,
-              "warp w's 32 output dims are exactly the dims CTA w merges");
-static_assert(kClSmemBytes + 16 * 1024 <= 227 * 1024, "cluster attention fits one SM's shared memory");
+constexpr int kClRows = 160;
+constexpr size_t kClSmemBytes = 2ull * kClRows * kD * sizeof(bf16);
 
 template <int G>
 __global__ void __launch_bounds__(kThreads, 1) attn_decode_cluster_kernel(DecodeParams p) {
   extern __shared__ __align__(16) unsigned char cl_smem[];
-  bf16* Ks = reinterpret_cast<bf16*>(cl_smem);   // [kClRowsPad][kClStride]
-  bf16* Vs = Ks + kClRowsPad * kClStride;          // [kClRowsPad][kClStride]
-  bf16* Qs = Vs + kClRowsPad * kClStride;          // [16][kClStride]: the G heads, zero rows after
+  bf16* Ks = reinterpret_cast<bf16*>(cl_smem);
+  bf16* Vs = Ks + kClRows * kD;
+  __shared__ __align__(16) float qf[G][kD];
   __shared__ __align__(16) float nrm[G + 1][kD];
-  __shared__ float sc[kClRowsPad][G];
+  __shared__ __align__(16) float kn[kD];
+  __shared__ __align__(16) float vn[kD];
+  __shared__ __align__(16) float sc[kClRows + 1][G];
   __shared__ float red[kWarps][G + 1];
   __shared__ float inbox[kClusterCTAs][G][kD / kClusterCTAs];  // peers' partial outputs for my dims
   __shared__ float inml[kClusterCTAs][G][2];                   // peers' (max, sum) per head
@@ -395,8 +403,8 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_cluster_kernel(Decode
   const int r0 = min(rank * chunk, n), r1 = min(r0 + chunk, n), nr = r1 - r0;
   for (int i = t; i < nr * (kD / 8); i += kThreads) {
     const int row = i / (kD / 8), c = i % (kD / 8);
-    cp_async16(Ks + row * kClStride + c * 8, p.cache_k + kv_base + (int64_t)(r0 + row) * kD + c * 8);
-    cp_async16(Vs + row * kClStride + c * 8, p.cache_v + kv_base + (int64_t)(r0 + row) * kD + c * 8);
+    cp_async16(Ks + row * kD + c * 8, p.cache_k + kv_base + (int64_t)(r0 + row) * kD + c * 8);
+    cp_async16(Vs + row * kD + c * 8, p.cache_v + kv_base + (int64_t)(r0 + row) * kD + c * 8);
   }
   asm volatile("cp.async.commit_group;" ::: "memory");
   // peers write into this CTA's shared memory later: all CTAs of the cluster must have started
@@ -430,53 +438,60 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_cluster_kernel(Decode
     nrm[i][d] = rbf(x[i] * r * (1.0f + (i < G ? wq : wk)));
   }
   __syncthreads();
-  // q = bf16(RoPE(norm(q))) as the reference's qgkv_norm_rope emits it; rows G.. of the tile zero
 #pragma unroll
-  for (int i = 0; i < 16; ++i) Qs[i * kClStride + d] = f2bf(i < G ? rope_apply(nrm[i < G ? i : 0], d, p.rot, c, sn) : 0.f);
+  for (int i = 0; i < G; ++i) qf[i][d] = rope_apply(nrm[i], d, p.rot, c, sn) * p.scale;
   const float kr = rope_apply(nrm[G], d, p.rot, c, sn);
+  kn[d] = kr;
+  vn[d] = v_raw;
   if (rank == 0 && len >= 0 && len < p.max_len) {
     p.cache_k[kv_base + len * kD + d] = f2bf(kr);
     p.cache_v[kv_base + len * kD + d] = f2bf(v_raw);
   }
   asm volatile("cp.async.wait_all;" ::: "memory");
-  // the last CTA attends the current token as row nr (its bf16 cache values); rows up to the next
-  // multiple of 16 are zero so the padded MMA steps add nothing
-  const bool last = rank == C - 1;
-  const int rows = nr + (last ? 1 : 0);
-  const int rows_pad = (rows + 15) & ~15;
-  if (last) {
-    Ks[nr * kClStride + d] = f2bf(kr);
-    Vs[nr * kClStride + d] = f2bf(v_raw);
-  }
-  for (int j = rows; j < rows_pad; ++j) {
-    Ks[j * kClStride + d] = f2bf(0.f);
-    Vs[j * kClStride + d] = f2bf(0.f);
-  }
   __syncthreads();
 
-  // ---- scores S = Q K^T on mma.sync (heads = rows 0..G-1 of the 16-row tile, keys 16 per step of
-  //      a warp: two 8-key n-tiles), scaled; keys past `rows` masked
-  const int gq = lane >> 2, c4 = lane & 3;
-  const uint32_t qaddr = (uint32_t)__cvta_generic_to_shared(Qs + (lane & 15) * kClStride) + (lane >> 4) * 16;
-  const uint32_t kaddr = (uint32_t)__cvta_generic_to_shared(Ks);
-  for (int np = warp; 16 * np < rows; np += kWarps) {
-    float s0[4] = {0.f, 0.f, 0.f, 0.f}, s1[4] = {0.f, 0.f, 0.f, 0.f};
-    const int key = np * 16 + (lane & 7) + ((lane >> 4) << 3);
-#pragma unroll 4
-    for (int ks = 0; ks < kD / 16; ++ks) {
-      uint32_t a0, a1, a2, a3, b0, b1, b2, b3;
-      ldsm_x4(qaddr + ks * 32, a0, a1, a2, a3);
-      ldsm_x4(kaddr + (key * kClStride + ks * 16) * 2 + ((lane >> 3) & 1) * 16, b0, b1, b2, b3);
-      mma_bf16(s0, a0, a1, a2, a3, b0, b1);
-      mma_bf16(s1, a0, a1, a2, a3, b2, b3);
-    }
-    if (gq < G) {
+  // ---- scores: warp per row (four rows per step, one butterfly for their 4 G dot products),
+  //      lanes hold 8 dims; the last CTA adds the current token as row nr
+  const bool last = rank == C - 1;
+  const int rows = nr + (last ? 1 : 0);
+  float q8[G][8];
 #pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const int j0 = np * 16 + 2 * c4 + e, j1 = j0 + 8;
-        sc[j0][gq] = j0 < rows ? s0[e] * p.scale : -FLT_MAX;
-        sc[j1][gq] = j1 < rows ? s1[e] * p.scale : -FLT_MAX;
+  for (int hh = 0; hh < G; ++hh)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) q8[hh][j] = qf[hh][lane * 8 + j];
+  auto key_row = [&](int j, float kf[8]) {
+    if (j < nr) {
+      unpack_bf16x8(*reinterpret_cast<const uint4*>(Ks + j * kD + lane * 8), kf);
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) kf[e] = kn[lane * 8 + e];
+    }
+  };
+  for (int j = warp; j < rows; j += 4 * kWarps) {  // rows j, j + 8, j + 16, j + 24: one butterfly
+    float v[4 * G];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int r = j + i * kWarps;
+      float kf[8];
+      if (r < rows) {
+        key_row(r, kf);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) kf[e] = 0.f;
       }
+#pragma unroll
+      for (int hh = 0; hh < G; ++hh) {
+        float a = 0.f;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) a = fmaf(q8[hh][e], kf[e], a);
+        v[i * G + hh] = a;
+      }
+    }
+    butterfly_sum<4 * G>(v, lane);
+    if (butterfly_writer<4 * G>(lane)) {
+      const int idx = butterfly_index<4 * G>(lane);
+      const int r = j + (idx / G) * kWarps;
+      if (r < rows) sc[r][idx % G] = v[0];
     }
   }
   __syncthreads();
@@ -487,8 +502,8 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_cluster_kernel(Decode
     for (int j = lane; j < rows; j += 32) m = fmaxf(m, sc[j][warp]);
     m = warp_max(m);
     float l = 0.f;
-    for (int j = lane; j < rows_pad; j += 32) {
-      const float e = j < rows ? expf(sc[j][warp] - m) : 0.f;
+    for (int j = lane; j < rows; j += 32) {
+      const float e = expf(sc[j][warp] - m);
       sc[j][warp] = e;
       l += e;
     }
@@ -500,47 +515,28 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_cluster_kernel(Decode
     }
   }
   __syncthreads();
-  // ---- un-normalised O = P V on mma.sync: warp w computes dims [32 w, 32 w + 32) of every head
-  //      (P split into bf16 high and remainder parts), then pushes them to CTA w, which owns those
-  //      dims in the merge
+  // ---- un-normalised P.V (thread = dim, all heads), pushed to the peer that owns the dim
   {
-    float o[4][4];
+    float a[G];
 #pragma unroll
-    for (int n = 0; n < 4; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
-    const uint32_t vaddr = (uint32_t)__cvta_generic_to_shared(Vs);
-    for (int k0 = 0; k0 < rows_pad; k0 += 16) {
-      float pv[4] = {0.f, 0.f, 0.f, 0.f};
-      if (gq < G) {
-        pv[0] = sc[k0 + 2 * c4][gq];
-        pv[1] = sc[k0 + 2 * c4 + 1][gq];
-        pv[2] = sc[k0 + 2 * c4 + 8][gq];
-        pv[3] = sc[k0 + 2 * c4 + 9][gq];
-      }
-      const uint32_t h0 = pack_bf2(pv[0], pv[1]), h2 = pack_bf2(pv[2], pv[3]);
-      auto rem = [](float x, uint32_t packed, int half) {
-        return x - __uint_as_float(half ? (packed & 0xffff0000u) : (packed << 16));
-      };
-      const uint32_t l0 = pack_bf2(rem(pv[0], h0, 0), rem(pv[1], h0, 1));
-      const uint32_t l2 = pack_bf2(rem(pv[2], h2, 0), rem(pv[3], h2, 1));
-      const int vrow = k0 + (lane & 7) + (((lane >> 3) & 1) << 3);
+    for (int hh = 0; hh < G; ++hh) a[hh] = 0.f;
+    for (int j = 0; j < rows; ++j) {
+      const float v = (j < nr) ? bf2f(Vs[j * kD + d]) : vn[d];
+      if (G == 4) {  // the row's four weights in one 16-byte shared load
+        const float4 w4 = *reinterpret_cast<const float4*>(&sc[j][0]);
+        a[0] = fmaf(w4.x, v, a[0]);
+        a[1 % G] = fmaf(w4.y, v, a[1 % G]);
+        a[2 % G] = fmaf(w4.z, v, a[2 % G]);
+        a[3 % G] = fmaf(w4.w, v, a[3 % G]);
+      } else {
 #pragma unroll
-      for (int np = 0; np < 2; ++np) {
-        uint32_t b0, b1, b2, b3;
-        ldsm_x4_t(vaddr + (vrow * kClStride + warp * 32 + np * 16 + (lane >> 4) * 8) * 2, b0, b1, b2, b3);
-        mma_bf16(o[2 * np], h0, 0u, h2, 0u, b0, b1);
-        mma_bf16(o[2 * np], l0, 0u, l2, 0u, b0, b1);
-        mma_bf16(o[2 * np + 1], h0, 0u, h2, 0u, b2, b3);
-        mma_bf16(o[2 * np + 1], l0, 0u, l2, 0u, b2, b3);
+        for (int hh = 0; hh < G; ++hh) a[hh] = fmaf(sc[j][hh], v, a[hh]);
       }
     }
-    if (gq < G) {
-      float* dst = cluster.map_shared_rank(&inbox[rank][gq][0], warp);  // dims 32 w .. of head gq
+    const int dper = kD / kClusterCTAs;
+    const int owner = d / dper;
 #pragma unroll
-      for (int n = 0; n < 4; ++n) {
-        dst[n * 8 + 2 * c4] = o[n][0];
-        dst[n * 8 + 2 * c4 + 1] = o[n][1];
-      }
-    }
+    for (int hh = 0; hh < G; ++hh) *cluster.map_shared_rank(&inbox[rank][hh][d % dper], owner) = a[hh];
   }
   cluster.sync();  // every push has landed; from here on only this CTA's own shared memory is read
   // ---- merge the partials of dims [rank * D / C, (rank + 1) * D / C) of every head
