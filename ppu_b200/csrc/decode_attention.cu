@@ -24,7 +24,7 @@ namespace {
 constexpr int kD = 256;
 constexpr int kThreads = 256;
 constexpr int kWarps = 8;
-constexpr int kMaxSplits = 128;
+constexpr int kMaxSplits = 64;
 constexpr int kRowsPerSplit = 32;
 
 struct DecodeParams {
@@ -563,7 +563,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_cluster_kernel(Decode
 }
 
 int choose_splits(int64_t batch, int64_t kv_heads, int64_t cache_len) {
-  int64_t s = (cache_len + kRowsPerSplit - 1) / kRowsPerSplit;  // >= 64 rows per CTA
+  int64_t s = (cache_len + kRowsPerSplit - 1) / kRowsPerSplit;  // >= one 32-row block per CTA
   // one wave of two CTAs per SM: rounding up here left a few CTAs for a second wave (1.03 waves
   // at 8 x 2 KV heads), doubling the kernel time
   const int64_t fill = (2 * kNumSMs) / (batch * kv_heads);
