@@ -52,6 +52,9 @@ def parse():
     ap.add_argument("--decode", default="kernels", choices=["kernels", "persistent"],
                     help="decode step: one persistent cooperative kernel (bf16) or the per-op kernels")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--lm-shard", action="store_true",
+                    help="N > 1: lock-step decode with the LM head split over the vocabulary (NCCL all_gather of "
+                         "the final residuals + int64 MAX all_reduce of the top-1 keys) instead of full replicas")
     return ap.parse_args()
 
 
@@ -207,7 +210,11 @@ def main():
 
     n_req = args.warmup + args.steps
     prompts = [make_prompt(dims, P, seed=R.request_seed(rank, i))[0].to(dev) for i in range(n_req)]
-    graph = eng.capture(1)
+    sharded = None
+    if args.lm_shard and world > 1:
+        from ppu_b200.vocab_shard import ShardedDecode
+        sharded = ShardedDecode(eng)
+    graph = sharded.capture(1) if sharded else eng.capture(1)
     torch.cuda.synchronize()
 
     def request(i, ev=None):
@@ -277,7 +284,7 @@ def main():
     e2e_tok, e2e_time, e2e_ttft = 0, 0.0, []
     for i in range(2):
         host_prompt = make_prompt(dims, P, seed=50_000 + R.request_seed(rank, i))[0]
-        toks, ttft, elapsed = eng.generate(host_prompt, T + 1)
+        toks, ttft, elapsed = (sharded or eng).generate(host_prompt, T + 1)
         e2e_tok += len(toks) - 1
         e2e_time += elapsed - ttft
         e2e_ttft.append(ttft)
@@ -309,7 +316,10 @@ def main():
         "config": {
             "workload": f"config4: prefill {P} tokens + {T} greedy decode steps, batch 1 (one step = one request)",
             "model": "Qwen3.5-2B-shape text decoder (24 layers, 3xGatedDeltaNet:1xGQA, hidden 2048, vocab 248320)",
-            "global_batch": world, "seq_len": P, "parallelism": f"request-parallel replicas x{world}",
+            "global_batch": world, "seq_len": P,
+            "parallelism": (f"lock-step decode x{world}, LM head vocab-sharded {dims.vocab // world} rows/rank "
+                            "(NCCL all_gather + int64 MAX all_reduce per token)") if sharded
+            else f"request-parallel replicas x{world}",
             "a8w8": args.a8w8, "pdl": not args.no_pdl, "cuda_graph": "1 decode step per replay",
             "decode_step": "persistent" if eng.persistent else "per-op kernels", "gemv": args.gemv,
             "gemv_ctas_per_sm": args.gemv_ctas or "all that fit",
@@ -328,8 +338,9 @@ def main():
                      "peak_kind": peak_kind},
         "e2e": {"value": round(e2e_value, 2), "unit": "tok/s", "h2d_bytes_per_step": P * 8,
                 "d2h_bytes_per_step": (T + 1) * 8, "ttft_ms": round(1000 * statistics.mean(e2e_ttft), 3),
-                "path": "Qwen35Engine.generate (host ids -> H2D, prefill, per-token D2H read, graph replay)"},
-        "gpu_launches": args.steps * (prefill_launches + T * eng.kernels_per_step),
+                "path": ("ShardedDecode.generate" if sharded else "Qwen35Engine.generate")
+                        + " (host ids -> H2D, prefill, per-token D2H read, graph replay)"},
+        "gpu_launches": args.steps * (prefill_launches + T * (eng.kernels_per_step + (1 if sharded else 0))),
         "clocks": clocks.summary(),
     }
     if cpu is not None:
@@ -339,6 +350,8 @@ def main():
     if world > 1:
         del graph
         eng._graphs.clear()
+        if sharded:
+            sharded.release()
         torch.cuda.synchronize()
         R.barrier()
         R.shutdown()

@@ -130,6 +130,23 @@ int q35_lm_head_argmax(const void* hidden, const void* norm_weight, const void* 
                        int64_t* token_out, int64_t batch, int64_t vocab, int64_t hidden_size,
                        float eps, void* workspace, size_t workspace_bytes, void* stream);
 
+/* Vocab-sharded top-1 (no reference counterpart: the multi-GPU split of kernels.py:1093-1185 for
+ * lock-step decode of `batch` requests, one per rank). For each of the `batch` hiddens (rows of
+ * [batch, hidden_size], rms_norm'ed first when norm_weight != NULL) and the shard of rows
+ * [row_offset, row_offset + shard_rows) of the [vocab, hidden_size] table (weight_shard points at
+ * its first row), writes keys_out[b] = ((order(bf16 logit) << 32) | (0xFFFFFFFF - global index))
+ * - 2^63 as int64, INT64_MIN for an empty shard. The maximum of a request's keys over all shards
+ * (an int64 MAX all-reduce) encodes q35_lm_head_argmax's token: logits are bit-identical to it,
+ * and ties go to the lowest index. batch <= 8, hidden_size 2048. Workspace:
+ * q35_lm_shard_workspace_size() bytes, zeroed once; every call leaves it zeroed again. */
+size_t q35_lm_shard_workspace_size(void);
+int q35_lm_head_shard_keys(const void* hidden, int64_t batch, const void* norm_weight,
+                           const void* weight_shard, int64_t row_offset, int64_t shard_rows,
+                           int64_t vocab, int64_t hidden_size, float eps, int64_t* keys_out,
+                           void* workspace, size_t workspace_bytes, void* stream);
+/* tokens_out[b] = the token a reduced key encodes (0 for INT64_MIN), b < n (<= 1024). */
+int q35_lm_keys_to_tokens(const int64_t* keys, int64_t n, int64_t* tokens_out, void* stream);
+
 /* ---------------------------------------------------------------- A8W8 */
 
 /* explore_runtime_quantization.py:143-155 (weights) and :167-172 (activations): per-row
@@ -335,6 +352,15 @@ int q35_decoder_prefill(q35_decoder* dec, const int64_t* ids, int64_t length, vo
 /* One greedy decode step (graph.py:51-79 body): consumes *token, appends to caches, writes the
  * next greedy token to *token (and token_log), advances cache_len / rope_pos. */
 int q35_decoder_decode_step(q35_decoder* dec, void* stream);
+/* The decode step split for a vocab-sharded LM head (lock-step decode across ranks):
+ * q35_decoder_decode_layers runs every layer and leaves the final residual (pre final norm,
+ * [hidden] bf16) at q35_decoder_hidden(dec) without writing a token or advancing the counters;
+ * after the caller has reduced the shard keys of q35_lm_head_shard_keys over ranks,
+ * q35_decoder_finish_step writes the token keys[index] encodes to *token (and token_log) and
+ * advances cache_len / rope_pos, exactly as q35_decoder_decode_step's LM head does. */
+int q35_decoder_decode_layers(q35_decoder* dec, void* stream);
+void* q35_decoder_hidden(const q35_decoder* dec);
+int q35_decoder_finish_step(q35_decoder* dec, const int64_t* keys, int64_t index, void* stream);
 /* Number of kernels one decode step launches (for launch accounting). */
 int q35_decoder_kernels_per_step(const q35_decoder* dec);
 

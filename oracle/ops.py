@@ -359,3 +359,47 @@ def lm_head_argmax(hidden: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
     idx = torch.arange(logits.shape[-1]).expand_as(logits)
     cand = torch.where(logits == best, idx, torch.full_like(idx, logits.shape[-1]))
     return cand.min(dim=-1, keepdim=True).values.to(torch.int64)
+
+
+# --------------------------------------------------------------------------- vocab-sharded LM head
+INT64_MIN = -(1 << 63)
+
+
+def float_order_key(v: float) -> int:
+    """32-bit unsigned key that orders FP32 values like the values themselves (-0 folded to +0):
+    the sign bit set for non-negative values, all bits inverted for negative ones."""
+    import struct
+
+    v = float(v)
+    if v == 0.0:
+        v = 0.0
+    u = struct.unpack("<I", struct.pack("<f", v))[0]
+    return (~u) & 0xFFFFFFFF if u & 0x80000000 else u | 0x80000000
+
+
+def lm_shard_keys(hidden: torch.Tensor, weight_shard: torch.Tensor, row_offset: int) -> torch.Tensor:
+    """Shard keys of the multi-GPU split of kernels.py:1093-1185 (the top-1 over BF16-rounded
+    logits of ``hidden [n, K]`` against rows ``[row_offset, row_offset + rows)``, lowest index on
+    ties), as int64 ``[n]``: ``((order(logit) << 32) | (0xFFFFFFFF - index)) - 2^63``, INT64_MIN for
+    an empty shard. The maximum over shards is the key of the full-vocabulary top-1."""
+    n = hidden.shape[0]
+    if weight_shard.shape[0] == 0:
+        return torch.full((n,), INT64_MIN, dtype=torch.int64)
+    local = lm_head_argmax(hidden, weight_shard).reshape(-1)
+    logits = linear(hidden, weight_shard).float()
+    keys = []
+    for b in range(n):
+        i = int(local[b])
+        v = float(logits[b, i])
+        ukey = (float_order_key(v) << 32) | (0xFFFFFFFF - (row_offset + i))
+        keys.append(ukey - (1 << 63))
+    return torch.tensor(keys, dtype=torch.int64)
+
+
+def lm_keys_to_tokens(keys: torch.Tensor) -> torch.Tensor:
+    """Token ids encoded by reduced shard keys (INT64_MIN, an empty reduction, maps to 0)."""
+    out = []
+    for k in keys.reshape(-1).tolist():
+        u = k + (1 << 63)
+        out.append(0 if u == 0 else 0xFFFFFFFF - (u & 0xFFFFFFFF))
+    return torch.tensor(out, dtype=torch.int64)

@@ -45,48 +45,6 @@ struct DecodeParams {
   float scale, eps;
 };
 
-// Warp reduction of NV per-lane partial sums at once (transpose butterfly: each level halves the
-// values a lane keeps, exchanging the other half with its partner), NV a power of two <= 32:
-// NV - 1 + 5 - log2(NV) shuffles instead of 5 NV. Afterwards the returned value of lane l is the
-// warp total of value index butterfly_index<NV>(l); lanes that differ only in bits below the
-// levels used agree, and butterfly_writer<NV>(l) picks one of them.
-template <int NV>
-Q35_DEV float butterfly_sum(float (&v)[NV], int lane) {
-  int n = NV;
-#pragma unroll
-  for (int o = 16; o >= 1; o >>= 1) {
-    if (n > 1) {
-      const int half = n / 2;
-      const bool upper = (lane & o) != 0;
-#pragma unroll
-      for (int i = 0; i < NV / 2; ++i) {
-        if (i < half) {
-          const float send = upper ? v[i] : v[i + half];
-          const float keep = upper ? v[i + half] : v[i];
-          v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
-        }
-      }
-      n = half;
-    } else {
-      v[0] += __shfl_xor_sync(0xffffffffu, v[0], o);
-    }
-  }
-  return v[0];
-}
-template <int NV>
-Q35_DEV int butterfly_index(int lane) {
-  int idx = 0;
-#pragma unroll
-  for (int nn = NV, bit = 4; nn > 1; nn /= 2, --bit) idx = idx * 2 + ((lane >> bit) & 1);
-  return idx;
-}
-template <int NV>
-Q35_DEV bool butterfly_writer(int lane) {
-  int levels = 0;
-#pragma unroll
-  for (int nn = NV; nn > 1; nn /= 2) ++levels;
-  return (lane & ((1 << (5 - levels)) - 1)) == 0;
-}
 
 Q35_DEV void cp_async16(void* dst, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)

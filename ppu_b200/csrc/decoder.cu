@@ -22,6 +22,8 @@ int q35_gemv_launch(const q35_gemv_desc* d, cudaStream_t s, bool pdl);
 int q35_lm_head_launch(const void* hidden, const void* norm_weight, const void* weight, int64_t* token_out,
                        int64_t vocab, int64_t k, float eps, void* ws, cudaStream_t s, bool pdl,
                        const q35_step_counters* adv);
+int q35_lm_keys_finish_launch(const int64_t* keys, int64_t n, int64_t* tokens, cudaStream_t s, bool pdl,
+                              const q35_step_counters* adv);
 int q35_attn_decode_launch(const void* packed, const void* q_weight, const void* k_weight, const float* inv_freq,
                            void* cache_k, void* cache_v, const int64_t* cache_len, const int64_t* rope_pos,
                            void* out, int64_t batch, int64_t q_heads, int64_t kv_heads, int64_t rotary_dim,
@@ -217,11 +219,11 @@ extern "C" int q35_decoder_kernels_per_step(const q35_decoder* dec) { return dec
     if (_rc) return _rc;    \
   } while (0)
 
-extern "C" int q35_decoder_decode_step(q35_decoder* dec, void* stream) {
-  Q35_REQUIRE(dec, "decode_step: null decoder");
+// The decode step's layers: leaves the final residual in B.resid (pre final norm); the LM head
+// that follows writes the token and advances the step counters.
+static int decode_layers(q35_decoder* dec, cudaStream_t s) {
   const q35_decoder_desc& d = dec->d;
   const Buffers& B = dec->buf;
-  cudaStream_t s = (cudaStream_t)stream;
   const bool pdl = d.use_pdl != 0;
   const bool q8 = d.a8w8 != 0;
   const int qgkv_rows = 2 * d.q_heads * d.head_dim + 2 * d.kv_heads * d.head_dim;
@@ -296,8 +298,32 @@ extern "C" int q35_decoder_decode_step(q35_decoder* dec, void* stream) {
     g.eps = d.eps;
     Q35_TRY(q35_gemv_launch(&g, s, pdl));
   }
+  return Q35_OK;
+}
+
+extern "C" int q35_decoder_decode_step(q35_decoder* dec, void* stream) {
+  Q35_REQUIRE(dec, "decode_step: null decoder");
+  const q35_decoder_desc& d = dec->d;
+  cudaStream_t s = (cudaStream_t)stream;
+  Q35_TRY(decode_layers(dec, s));
   q35_step_counters adv = {d.cache_len, d.rope_pos, d.token_log, d.log_pos, d.log_len};
-  return q35_lm_head_launch(B.resid, d.final_norm, d.embed, d.token, d.vocab, d.hidden, d.eps, B.lm_ws, s, pdl, &adv);
+  return q35_lm_head_launch(dec->buf.resid, d.final_norm, d.embed, d.token, d.vocab, d.hidden, d.eps, dec->buf.lm_ws,
+                            s, d.use_pdl != 0, &adv);
+}
+
+extern "C" int q35_decoder_decode_layers(q35_decoder* dec, void* stream) {
+  Q35_REQUIRE(dec, "decode_layers: null decoder");
+  return decode_layers(dec, (cudaStream_t)stream);
+}
+
+extern "C" void* q35_decoder_hidden(const q35_decoder* dec) { return dec ? dec->buf.resid : nullptr; }
+
+extern "C" int q35_decoder_finish_step(q35_decoder* dec, const int64_t* keys, int64_t index, void* stream) {
+  Q35_REQUIRE(dec && keys, "finish_step: null pointer");
+  Q35_REQUIRE(index >= 0 && index < 1024, "finish_step: key index %lld outside [0, 1024)", (long long)index);
+  const q35_decoder_desc& d = dec->d;
+  q35_step_counters adv = {d.cache_len, d.rope_pos, d.token_log, d.log_pos, d.log_len};
+  return q35_lm_keys_finish_launch(keys + index, 1, d.token, (cudaStream_t)stream, false, &adv);
 }
 
 extern "C" int q35_decoder_prefill(q35_decoder* dec, const int64_t* ids, int64_t length, void* stream) {

@@ -421,6 +421,189 @@ __global__ void __launch_bounds__(kThreads) lm_head_any_kernel(LmParams p) {
 }
 
 // ---------------------------------------------------------------------------------------------
+// Vocab-sharded LM head: the top-1 of N hiddens over one contiguous shard of the tied embedding
+// (rows [row_offset, row_offset + rows)), for lock-step decode of N requests with the vocabulary
+// split across GPUs. Every logit is bit-identical to lm_head_fast_kernel's (same per-lane chunk
+// order, same warp-sum pairing, bf16 rounding as kernels.py:1119-1121), so the reduced shard keys
+// give exactly the single-GPU token. Output per request: a signed 64-bit key
+//   (order(logit) << 32 | (0xFFFFFFFF - global index)) - 2^63
+// whose maximum over ranks (an NCCL all-reduce with MAX on int64) is the largest logit with the
+// lowest index on ties; INT64_MIN when the shard is empty.
+constexpr int kShardMaxBatch = 8;
+
+struct LmShardWorkspace {
+  unsigned long long key[kShardMaxBatch];
+  unsigned int count;
+  unsigned int pad[3];
+};
+
+struct LmShardParams {
+  const bf16* hidden;  // [n, K]: final residuals (norm_w set) or normalised hiddens
+  const bf16* norm_w;
+  const bf16* weight;  // the shard's first row, [rows, K]
+  long long* keys_out;
+  LmShardWorkspace* ws;
+  int n, rows, row_offset;
+  float eps;
+};
+
+template <int NB>
+constexpr size_t lm_shard_smem() {
+  return (size_t)NB * 2048 * 4 + 2048 * 2;  // fp32 planes of NB hiddens + bf16 staging
+}
+
+template <int NB, bool NORM>
+__global__ void __launch_bounds__(kThreads) lm_shard_kernel(LmShardParams p) {
+  constexpr int K = 2048;
+  constexpr int CH = K * 2 / 512;  // 16-byte chunks per lane per row
+  constexpr int U = 2;             // rows per warp iteration
+  constexpr int NV = U * NB;       // dot products reduced together
+  constexpr int NC = K / 8;        // chunks per hidden
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  // Normalised hiddens in fp32, split into two planes (values 0-3 and 4-7 of each 16-byte chunk)
+  // so that a lane's two float4 reads of a chunk are bank-conflict free.
+  float4* xlo = reinterpret_cast<float4*>(smem_raw);
+  float4* xhi = xlo + NB * NC;
+  bf16* xs = reinterpret_cast<bf16*>(xhi + NB * NC);
+  __shared__ float red[kWarps];
+  __shared__ float red_v[kWarps][NV];
+  __shared__ int red_i[kWarps][NV];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int ngroups = (p.rows + U - 1) / U;
+  const int gstride = gridDim.x * kWarps;
+  int g = blockIdx.x * kWarps + warp;
+  const char* W = reinterpret_cast<const char*>(p.weight);
+  uint4 wr[U][CH];
+  auto load_group = [&](int grp) {
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int row = grp * U + u;
+      const char* base = W + (int64_t)row * (K * 2) + lane * 16;
+#pragma unroll
+      for (int c = 0; c < CH; ++c)
+        wr[u][c] = (row < p.rows) ? ld_stream(base + c * 512) : make_uint4(0, 0, 0, 0);
+    }
+  };
+  if (g < ngroups) load_group(g);
+  pdl_wait();
+  pdl_launch_dependents();
+  for (int b = 0; b < NB; ++b) {
+    if (b < p.n) {
+      GemvParams gp = {};
+      gp.input = p.hidden + (int64_t)b * K;
+      gp.norm_w = p.norm_w;
+      gp.eps = p.eps;
+      if (NORM)
+        build_input<Q35_PRO_NORM, false>(gp, K, xs, nullptr, nullptr, red);
+      else
+        build_input<Q35_PRO_PLAIN, false>(gp, K, xs, nullptr, nullptr, red);
+      for (int i = threadIdx.x; i < NC; i += kThreads) {
+        float f[8];
+        unpack_bf16x8(reinterpret_cast<const uint4*>(xs)[i], f);
+        xlo[b * NC + i] = make_float4(f[0], f[1], f[2], f[3]);
+        xhi[b * NC + i] = make_float4(f[4], f[5], f[6], f[7]);
+      }
+    } else {
+      for (int i = threadIdx.x; i < NC; i += kThreads) {
+        xlo[b * NC + i] = make_float4(0.f, 0.f, 0.f, 0.f);
+        xhi[b * NC + i] = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+    __syncthreads();  // the staging row is rewritten for the next hidden
+  }
+  const int my = butterfly_index<NV>(lane);  // the (row u, hidden b) total this lane ends with
+  const int my_u = my / NB;
+  float best_v = -FLT_MAX;
+  int best_i = 0x7fffffff;
+  for (; g < ngroups; g += gstride) {
+    float acc[NV];
+#pragma unroll
+    for (int i = 0; i < NV; ++i) acc[i] = 0.f;
+#pragma unroll
+    for (int c = 0; c < CH; ++c) {
+      float w[U][8];
+#pragma unroll
+      for (int u = 0; u < U; ++u) unpack_bf16x8(wr[u][c], w[u]);
+#pragma unroll
+      for (int b = 0; b < NB; ++b) {
+        const float4 lo = xlo[b * NC + lane + 32 * c], hi = xhi[b * NC + lane + 32 * c];
+        const float x[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+#pragma unroll
+          for (int j = 0; j < 8; ++j) acc[u * NB + b] = fmaf(w[u][j], x[j], acc[u * NB + b]);
+      }
+      // keeps the shared-memory reads of later chunks from being hoisted here (NB x 8 floats per
+      // chunk would otherwise stay live across the whole row and spill)
+      asm volatile("" ::: "memory");
+    }
+    const int gn = g + gstride;
+    if (gn < ngroups) load_group(gn);
+    const float v = rbf(butterfly_sum<NV>(acc, lane));
+    const int row = g * U + my_u;
+    if (row < p.rows && v > best_v) {
+      best_v = v;
+      best_i = row;
+    }
+  }
+  if (butterfly_writer<NV>(lane)) {
+    red_v[warp][my] = best_v;
+    red_i[warp][my] = best_i;
+  }
+  __syncthreads();
+  if (threadIdx.x < p.n) {
+    const int b = threadIdx.x;
+    float bv = -FLT_MAX;
+    int bi = 0x7fffffff;
+    for (int w = 0; w < kWarps; ++w)
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const float v = red_v[w][u * NB + b];
+        const int i = red_i[w][u * NB + b];
+        if (i != 0x7fffffff && (v > bv || (v == bv && i < bi))) {
+          bv = v;
+          bi = i;
+        }
+      }
+    if (bi != 0x7fffffff) atomicMax(&p.ws->key[b], top1_key(bv, p.row_offset + bi));
+    __threadfence();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const unsigned prev = atomicAdd(&p.ws->count, 1u);
+    if (prev == gridDim.x - 1) {
+      __threadfence();
+      for (int b = 0; b < p.n; ++b) {
+        const unsigned long long key = atomicExch(&p.ws->key[b], 0ull);
+        p.keys_out[b] = (long long)(key ^ 0x8000000000000000ull);
+      }
+      atomicExch(&p.ws->count, 0u);
+    }
+  }
+}
+
+// Token of a reduced shard key (the inverse of the packing above; INT64_MIN -> token 0, as the
+// single-GPU head does when no candidate exists), optionally advancing the decoder's counters.
+__global__ void lm_keys_finish_kernel(const long long* keys, int n, int64_t* tokens, q35_step_counters adv) {
+  pdl_wait();
+  pdl_launch_dependents();
+  for (int b = threadIdx.x; b < n; b += blockDim.x) {
+    const unsigned long long key = (unsigned long long)keys[b] ^ 0x8000000000000000ull;
+    tokens[b] = (key == 0ull) ? 0 : (int64_t)(0xFFFFFFFFu - (uint32_t)(key & 0xFFFFFFFFull));
+  }
+  if (threadIdx.x == 0) {
+    if (adv.cache_len) *adv.cache_len += 1;
+    if (adv.rope_pos) *adv.rope_pos += 1;
+    if (adv.token_log && adv.log_pos && adv.log_len > 0) {
+      const int64_t pos = *adv.log_pos;
+      adv.token_log[pos % adv.log_len] = tokens[0];
+      *adv.log_pos = pos + 1;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
 // Grid choice: at most `max_ctas` resident CTAs; among grids of whole-SM multiples pick the one
 // whose last round of unit groups is the fullest (less tail imbalance between warps).
 int choose_grid(int ngroups, int max_ctas) {
@@ -642,4 +825,87 @@ extern "C" int q35_lm_head_argmax(const void* hidden, const void* norm_weight, c
   Q35_REQUIRE(Q35_ALIGNED(weight, 16) && Q35_ALIGNED(hidden, 16), "lm_head_argmax: 16-byte alignment");
   return q35_lm_head_launch(hidden, norm_weight, weight, token_out, vocab, hidden_size, eps, workspace,
                             (cudaStream_t)stream, false, nullptr);
+}
+
+// ---------------------------------------------------------------------------------------------
+// Vocab-sharded LM head entry points.
+namespace {
+template <int NB, bool NORM>
+cudaError_t launch_lm_shard(const LmShardParams& p, cudaStream_t s, bool pdl) {
+  constexpr size_t smem = lm_shard_smem<NB>();
+  static int resident = 0;
+  if (!resident) {
+    cudaFuncSetAttribute(lm_shard_kernel<NB, NORM>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    resident = resident_ctas(lm_shard_kernel<NB, NORM>, smem);
+  }
+  const int ngroups = (p.rows + 1) / 2;  // two rows per warp iteration
+  return q35_launch(lm_shard_kernel<NB, NORM>, dim3(choose_grid(ngroups, resident)), dim3(kThreads), smem, s,
+                    pdl, p);
+}
+
+template <bool NORM>
+cudaError_t dispatch_lm_shard(const LmShardParams& p, cudaStream_t s, bool pdl) {
+  if (p.n <= 1) return launch_lm_shard<1, NORM>(p, s, pdl);
+  if (p.n <= 2) return launch_lm_shard<2, NORM>(p, s, pdl);
+  if (p.n <= 4) return launch_lm_shard<4, NORM>(p, s, pdl);
+  return launch_lm_shard<8, NORM>(p, s, pdl);
+}
+}  // namespace
+
+int q35_lm_shard_launch(const void* hidden, int64_t batch, const void* norm_weight, const void* weight_shard,
+                        int64_t row_offset, int64_t shard_rows, float eps, int64_t* keys_out, void* ws,
+                        cudaStream_t s, bool pdl) {
+  LmShardParams p = {};
+  p.hidden = static_cast<const bf16*>(hidden);
+  p.norm_w = static_cast<const bf16*>(norm_weight);
+  p.weight = static_cast<const bf16*>(weight_shard);
+  p.keys_out = reinterpret_cast<long long*>(keys_out);
+  p.ws = static_cast<LmShardWorkspace*>(ws);
+  p.n = (int)batch;
+  p.rows = (int)shard_rows;
+  p.row_offset = (int)row_offset;
+  p.eps = eps;
+  const cudaError_t e = norm_weight ? dispatch_lm_shard<true>(p, s, pdl) : dispatch_lm_shard<false>(p, s, pdl);
+  if (e != cudaSuccess) return q35_fail(Q35_ECUDA, "lm_head_shard launch: %s", cudaGetErrorString(e));
+  return Q35_OK;
+}
+
+int q35_lm_keys_finish_launch(const int64_t* keys, int64_t n, int64_t* tokens, cudaStream_t s, bool pdl,
+                              const q35_step_counters* adv) {
+  q35_step_counters a = {};
+  if (adv) a = *adv;
+  const cudaError_t e = q35_launch(lm_keys_finish_kernel, dim3(1), dim3(32), 0, s, pdl,
+                                   reinterpret_cast<const long long*>(keys), (int)n, tokens, a);
+  if (e != cudaSuccess) return q35_fail(Q35_ECUDA, "lm_keys_finish launch: %s", cudaGetErrorString(e));
+  return Q35_OK;
+}
+
+extern "C" size_t q35_lm_shard_workspace_size(void) { return sizeof(LmShardWorkspace); }
+
+extern "C" int q35_lm_head_shard_keys(const void* hidden, int64_t batch, const void* norm_weight,
+                                      const void* weight_shard, int64_t row_offset, int64_t shard_rows,
+                                      int64_t vocab, int64_t hidden_size, float eps, int64_t* keys_out,
+                                      void* workspace, size_t workspace_bytes, void* stream) {
+  Q35_REQUIRE(hidden && keys_out && workspace, "lm_head_shard_keys: null pointer");
+  Q35_REQUIRE(batch >= 1 && batch <= kShardMaxBatch, "lm_head_shard_keys: batch %lld outside [1, %d]",
+              (long long)batch, kShardMaxBatch);
+  Q35_REQUIRE(hidden_size == 2048, "lm_head_shard_keys: hidden size %lld unsupported (2048)",
+              (long long)hidden_size);
+  Q35_REQUIRE(vocab > 0 && vocab < (1ll << 31), "lm_head_shard_keys: bad vocab %lld", (long long)vocab);
+  Q35_REQUIRE(row_offset >= 0 && shard_rows >= 0 && row_offset + shard_rows <= vocab,
+              "lm_head_shard_keys: shard [%lld, %lld) outside the vocabulary of %lld", (long long)row_offset,
+              (long long)(row_offset + shard_rows), (long long)vocab);
+  Q35_REQUIRE(shard_rows == 0 || weight_shard, "lm_head_shard_keys: null weight");
+  Q35_REQUIRE(workspace_bytes >= q35_lm_shard_workspace_size(), "lm_head_shard_keys: workspace too small");
+  Q35_REQUIRE(Q35_ALIGNED(hidden, 16) && (shard_rows == 0 || Q35_ALIGNED(weight_shard, 16)) &&
+                  (!norm_weight || Q35_ALIGNED(norm_weight, 16)),
+              "lm_head_shard_keys: 16-byte alignment");
+  return q35_lm_shard_launch(hidden, batch, norm_weight, weight_shard, row_offset, shard_rows, eps, keys_out,
+                             workspace, (cudaStream_t)stream, false);
+}
+
+extern "C" int q35_lm_keys_to_tokens(const int64_t* keys, int64_t n, int64_t* tokens_out, void* stream) {
+  Q35_REQUIRE(keys && tokens_out, "lm_keys_to_tokens: null pointer");
+  Q35_REQUIRE(n >= 1 && n <= 1024, "lm_keys_to_tokens: n %lld outside [1, 1024]", (long long)n);
+  return q35_lm_keys_finish_launch(keys, n, tokens_out, (cudaStream_t)stream, false, nullptr);
 }

@@ -195,6 +195,33 @@ class Qwen35Engine:
                     "q35_decoder_decode_step")
         return self.token
 
+    # ---- the step split for a vocab-sharded LM head (ppu_b200.vocab_shard)
+    def decode_layers(self) -> None:
+        """The decode step's layers only: the final residual lands in ``hidden_view()``; no token
+        is written and the step counters stay put until ``finish_step``."""
+        L.check(L.load().q35_decoder_decode_layers(self.handle, L.stream_of(self.device)),
+                "q35_decoder_decode_layers")
+
+    def hidden_view(self) -> torch.Tensor:
+        """The decoder's final-residual buffer (``[hidden]`` BF16, pre final norm) as a tensor view."""
+        ptr = L.load().q35_decoder_hidden(self.handle)
+        off = (ptr or 0) - self.workspace.data_ptr()
+        nbytes = 2 * self.dims.hidden
+        if ptr is None or off < 0 or off + nbytes > self.workspace.numel():
+            raise RuntimeError("decoder hidden buffer lies outside the engine workspace")
+        return self.workspace[off:off + nbytes].view(BF16)
+
+    def finish_step(self, keys: torch.Tensor, index: int) -> torch.Tensor:
+        """Completes a ``decode_layers`` step from reduced shard keys: the token ``keys[index]``
+        encodes goes to ``self.token`` (and the token log), and the counters advance."""
+        if keys.dtype != torch.int64 or keys.device != self.device or not keys.is_contiguous():
+            raise ValueError("keys must be a contiguous int64 tensor on the engine's device")
+        if not 0 <= index < keys.numel():
+            raise ValueError(f"key index {index} outside [0, {keys.numel()})")
+        L.check(L.load().q35_decoder_finish_step(self.handle, keys.data_ptr(), index, L.stream_of(self.device)),
+                "q35_decoder_finish_step")
+        return self.token
+
     def capture(self, steps: int = 1) -> torch.cuda.CUDAGraph:
         """CUDA graph of ``steps`` consecutive decode steps (graph.py:50-79)."""
         if steps in self._graphs:

@@ -430,9 +430,47 @@ def lm_head_argmax(hidden: torch.Tensor, weight: torch.Tensor, *, block_n: int =
     return out
 
 
+def lm_head_shard_keys(hidden: torch.Tensor, weight_shard: torch.Tensor, row_offset: int, vocab: int, *,
+                       norm_weight: torch.Tensor | None = None, eps: float = 1e-6,
+                       workspace: torch.Tensor | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Top-1 keys of ``hidden [n, 2048]`` (n <= 8) over rows ``[row_offset, row_offset + rows)`` of a
+    ``[vocab, 2048]`` table held as ``weight_shard [rows, 2048]``: int64 ``[n]``, the maximum of which
+    over all shards encodes the token ``lm_head_argmax`` gives (see ``lm_keys_to_tokens``). The
+    multi-GPU split of kernels.py:1093-1185; ``workspace`` (zeroed once, reusable) and ``out`` may be
+    passed to keep the call allocation-free."""
+    if hidden.dim() != 2 or hidden.dtype != BF16 or weight_shard.dtype != BF16:
+        raise ValueError("lm_head_shard_keys expects BF16 hidden [n, K] and a BF16 weight shard")
+    if not hidden.is_cuda or not weight_shard.is_cuda:
+        raise ValueError("fused kernels require a CUDA tensor")
+    if not hidden.is_contiguous() or not weight_shard.is_contiguous():
+        raise ValueError("LM head tensors must be contiguous")
+    n, k = hidden.shape
+    if weight_shard.dim() != 2 or weight_shard.shape[1] != k:
+        raise ValueError("weight shard must be [rows, hidden_size]")
+    size = L.load().q35_lm_shard_workspace_size()
+    if workspace is None:
+        workspace = torch.zeros(size, device=hidden.device, dtype=torch.uint8)
+    if out is None:
+        out = torch.empty(n, device=hidden.device, dtype=torch.int64)
+    L.call("q35_lm_head_shard_keys", L.ptr(hidden), n, L.ptr(norm_weight), L.ptr(weight_shard), row_offset,
+           weight_shard.shape[0], vocab, k, eps, L.ptr(out), L.ptr(workspace), workspace.numel(), _s(hidden))
+    return out
+
+
+def lm_keys_to_tokens(keys: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Token ids encoded by reduced shard keys (int64 ``[n]`` -> int64 ``[n]``)."""
+    if keys.dtype != torch.int64 or not keys.is_cuda or not keys.is_contiguous():
+        raise ValueError("keys must be a contiguous CUDA int64 tensor")
+    if out is None:
+        out = torch.empty_like(keys)
+    L.call("q35_lm_keys_to_tokens", L.ptr(keys), keys.numel(), L.ptr(out), _s(keys))
+    return out
+
+
 __all__ = [
     "rms_norm", "residual_add_rms_norm", "gated_rms_norm", "silu_and_mul", "ppu_swiglu_gemv", "sigmoid_mul",
     "attention_gate_mul", "qgkv_norm_rope", "causal_conv1d_fused", "delta_recurrent_fused",
     "gqa_decode_attention", "lm_head_argmax", "quantize_rows", "int8_gemm", "a8w8_linear", "gemm",
     "fused_gemv", "attn_decode", "prefill_attention", "delta_decode", "delta_chunked_fused",
+    "lm_head_shard_keys", "lm_keys_to_tokens",
 ]

@@ -68,6 +68,9 @@ _SIGS = {
     "q35_gemv_error": (INT, []),
     "q35_lm_head_workspace_size": (SZ, [I64]),
     "q35_lm_head_argmax": (INT, [P, P, P, P, I64, I64, I64, F32, P, SZ, P]),
+    "q35_lm_shard_workspace_size": (SZ, []),
+    "q35_lm_head_shard_keys": (INT, [P, I64, P, P, I64, I64, I64, I64, F32, P, P, SZ, P]),
+    "q35_lm_keys_to_tokens": (INT, [P, I64, P, P]),
     "q35_quantize_rows": (INT, [P, P, P, I64, I64, P]),
     "q35_a8w8_linear_workspace_size": (SZ, [I64, I64]),
     "q35_a8w8_linear": (INT, [P, P, P, P, I64, I64, I64, P, SZ, P]),
@@ -96,6 +99,9 @@ _SIGS = {
     "q35_decoder_destroy": (None, [P]),
     "q35_decoder_prefill": (INT, [P, P, I64, P]),
     "q35_decoder_decode_step": (INT, [P, P]),
+    "q35_decoder_decode_layers": (INT, [P, P]),
+    "q35_decoder_hidden": (P, [P]),
+    "q35_decoder_finish_step": (INT, [P, P, I64, P]),
     "q35_decoder_kernels_per_step": (INT, [P]),
     "q35_decoder_decode_step_persistent": (INT, [P, P]),
     "q35_decoder_has_persistent": (INT, [P]),

@@ -107,6 +107,21 @@ def run(kernels: list[str], reps: int, layers: int = 24, a8w8: bool = False):
             t = _time(lambda i: K.lm_head_argmax(h, e, norm_weight=nw), reps)
             report(name, t, nbytes=e.numel() * 2)
             del e
+        elif name == "lm_shard":
+            # vocab-sharded head of lock-step decode over N ranks: N hiddens against one 1/N shard;
+            # launches rotate over the N shards of the table so no shard is L2-resident
+            e = (torch.randn(248320, H, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+            ws = torch.zeros(64, device=dev, dtype=torch.uint8)
+            keys = torch.empty(8, device=dev, dtype=torch.int64)
+            for world in (2, 4, 8):
+                hs = torch.randn(world, H, device=dev, generator=g).to(torch.bfloat16)
+                rows = 248320 // world
+                shards = [e[r * rows:(r + 1) * rows] for r in range(world)]
+                kv = keys[:world]
+                t = _time(lambda i: K.lm_head_shard_keys(hs, shards[i % world], (i % world) * rows, 248320,
+                                                         norm_weight=nw, workspace=ws, out=kv), reps * world)
+                report(f"lm_shard_n{world}", t, nbytes=rows * H * 2)
+            del e
         elif name == "attn_decode":
             max_len, n = 1152, 1056
             kc = [torch.randn(1, 2, max_len, 256, device=dev, generator=g).to(torch.bfloat16) for _ in range(6)]
