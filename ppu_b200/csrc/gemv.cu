@@ -449,23 +449,97 @@ struct LmShardParams {
 
 template <int NB>
 constexpr size_t lm_shard_smem() {
-  return (size_t)NB * 2048 * 4 + 2048 * 2;  // fp32 planes of NB hiddens + bf16 staging
+  return (size_t)NB * 2048 * 4;  // fp32 copies of NB normalised hiddens
+}
+// Rows a warp streams per iteration: 4 at 8 hiddens halves the shared-memory reads of the hiddens
+// per weight byte, 2 otherwise (two CTAs per SM).
+template <int NB>
+constexpr int lm_shard_rows() {
+  return NB >= 8 ? 4 : 2;
+}
+
+// Shared-memory layout of the normalised hiddens, built for packed FP32 FMAs over hidden pairs:
+// plane q (0..3) of pair p holds, per 16-byte chunk i of the hidden, the float4
+//   {x[2p][8i + 2q], x[2p+1][8i + 2q], x[2p][8i + 2q + 1], x[2p+1][8i + 2q + 1]},
+// so a lane reads its chunk of a pair as four conflict-free 16-byte loads of ready-made operands.
+template <int NB>
+Q35_DEV float* lm_shard_slot(float4* xs, int b, int q, int i) {
+  constexpr int NC = 2048 / 8;
+  return reinterpret_cast<float*>(xs + ((q * (NB / 2) + b / 2) * NC + i)) + (b & 1);
+}
+
+// One warp normalises one hidden: lane l holds chunks l + 32 c (c < 8), i.e. lane l of the eight
+// warps of build_input's block-wide pass. Per-chunk partial sums, the butterfly (the same pairing
+// as those warps' warp_sum) and the in-order sum of the eight warp totals reproduce block_sum
+// bit for bit, so the normalised values equal the single-GPU head's.
+template <int NB, bool NORM>
+Q35_DEV void lm_shard_prologue(const LmShardParams& p, float4* xs, int warp, int lane) {
+  constexpr int K = 2048, NC = K / 8, CPL = NC / 32;
+  const int b = warp;
+  if (b >= NB) return;
+  if (b >= p.n) {
+#pragma unroll 1
+    for (int c = 0; c < CPL; ++c)
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        float* d = lm_shard_slot<NB>(xs, b, q, lane + 32 * c);
+        d[0] = 0.f;
+        d[2] = 0.f;
+      }
+    return;
+  }
+  // the hidden is read twice (the second time from L1 / L2) rather than held in registers next
+  // to the weight rows already in flight
+  const uint4* src = reinterpret_cast<const uint4*>(p.hidden + (int64_t)b * K);
+  float r = 1.0f;
+  if (NORM) {
+    float part[CPL];
+#pragma unroll
+    for (int c = 0; c < CPL; ++c) {
+      float f[8];
+      unpack_bf16x8(src[lane + 32 * c], f);
+      float ss = 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss += f[j] * f[j];
+      part[c] = ss;
+    }
+    const float mine = butterfly_sum<CPL>(part, lane);  // lane 4 i: the total of warp i
+    float t = 0.f;
+#pragma unroll
+    for (int i = 0; i < CPL; ++i) t += __shfl_sync(0xffffffffu, mine, 4 * i);
+    const float var = t / (float)K;
+    r = rsqrt_ieee(var + p.eps);
+  }
+#pragma unroll 1
+  for (int c = 0; c < CPL; ++c) {
+    float f[8];
+    unpack_bf16x8(src[lane + 32 * c], f);
+    if (NORM) {
+      float w[8];
+      unpack_bf16x8(reinterpret_cast<const uint4*>(p.norm_w)[lane + 32 * c], w);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) f[j] = bf2f(f2bf(f[j] * r * (1.0f + w[j])));
+    }
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      float* d = lm_shard_slot<NB>(xs, b, q, lane + 32 * c);
+      d[0] = f[2 * q];
+      d[2] = f[2 * q + 1];
+    }
+  }
 }
 
 template <int NB, bool NORM>
-__global__ void __launch_bounds__(kThreads) lm_shard_kernel(LmShardParams p) {
+__global__ void __launch_bounds__(kThreads, NB >= 8 ? 1 : 2) lm_shard_kernel(LmShardParams p) {
   constexpr int K = 2048;
-  constexpr int CH = K * 2 / 512;  // 16-byte chunks per lane per row
-  constexpr int U = 2;             // rows per warp iteration
-  constexpr int NV = U * NB;       // dot products reduced together
-  constexpr int NC = K / 8;        // chunks per hidden
+  constexpr int CH = K * 2 / 512;          // 16-byte chunks per lane per row
+  constexpr int U = lm_shard_rows<NB>();   // rows per warp iteration
+  constexpr int NP = NB / 2;               // hidden pairs
+  constexpr int NV = U * NB;               // dot products reduced together
+  constexpr int NC = K / 8;                // chunks per hidden
+  static_assert(NB >= 2 && NB % 2 == 0 && NB <= kWarps, "hidden pairs, one warp per hidden in the prologue");
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  // Normalised hiddens in fp32, split into two planes (values 0-3 and 4-7 of each 16-byte chunk)
-  // so that a lane's two float4 reads of a chunk are bank-conflict free.
-  float4* xlo = reinterpret_cast<float4*>(smem_raw);
-  float4* xhi = xlo + NB * NC;
-  bf16* xs = reinterpret_cast<bf16*>(xhi + NB * NC);
-  __shared__ float red[kWarps];
+  float4* xs = reinterpret_cast<float4*>(smem_raw);
   __shared__ float red_v[kWarps][NV];
   __shared__ int red_i[kWarps][NV];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -487,58 +561,61 @@ __global__ void __launch_bounds__(kThreads) lm_shard_kernel(LmShardParams p) {
   if (g < ngroups) load_group(g);
   pdl_wait();
   pdl_launch_dependents();
-  for (int b = 0; b < NB; ++b) {
-    if (b < p.n) {
-      GemvParams gp = {};
-      gp.input = p.hidden + (int64_t)b * K;
-      gp.norm_w = p.norm_w;
-      gp.eps = p.eps;
-      if (NORM)
-        build_input<Q35_PRO_NORM, false>(gp, K, xs, nullptr, nullptr, red);
-      else
-        build_input<Q35_PRO_PLAIN, false>(gp, K, xs, nullptr, nullptr, red);
-      for (int i = threadIdx.x; i < NC; i += kThreads) {
-        float f[8];
-        unpack_bf16x8(reinterpret_cast<const uint4*>(xs)[i], f);
-        xlo[b * NC + i] = make_float4(f[0], f[1], f[2], f[3]);
-        xhi[b * NC + i] = make_float4(f[4], f[5], f[6], f[7]);
-      }
-    } else {
-      for (int i = threadIdx.x; i < NC; i += kThreads) {
-        xlo[b * NC + i] = make_float4(0.f, 0.f, 0.f, 0.f);
-        xhi[b * NC + i] = make_float4(0.f, 0.f, 0.f, 0.f);
-      }
-    }
-    __syncthreads();  // the staging row is rewritten for the next hidden
-  }
+  lm_shard_prologue<NB, NORM>(p, xs, warp, lane);
+  __syncthreads();
   const int my = butterfly_index<NV>(lane);  // the (row u, hidden b) total this lane ends with
   const int my_u = my / NB;
   float best_v = -FLT_MAX;
   int best_i = 0x7fffffff;
   for (; g < ngroups; g += gstride) {
-    float acc[NV];
+    const int gn = g + gstride;
+    float2 acc2[U][NP];  // {row u . hidden 2p, row u . hidden 2p + 1}
 #pragma unroll
-    for (int i = 0; i < NV; ++i) acc[i] = 0.f;
+    for (int u = 0; u < U; ++u)
+#pragma unroll
+      for (int q = 0; q < NP; ++q) acc2[u][q] = make_float2(0.f, 0.f);
 #pragma unroll
     for (int c = 0; c < CH; ++c) {
       float w[U][8];
 #pragma unroll
       for (int u = 0; u < U; ++u) unpack_bf16x8(wr[u][c], w[u]);
+      // rolling prefetch: chunk c of the next group goes into the slot just unpacked, so its
+      // load overlaps the rest of this group's arithmetic (no second register buffer)
 #pragma unroll
-      for (int b = 0; b < NB; ++b) {
-        const float4 lo = xlo[b * NC + lane + 32 * c], hi = xhi[b * NC + lane + 32 * c];
-        const float x[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+      for (int u = 0; u < U; ++u) {
+        const int row = gn * U + u;
+        wr[u][c] = (gn < ngroups && row < p.rows)
+                       ? ld_stream(W + (int64_t)row * (K * 2) + lane * 16 + c * 512)
+                       : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int pr = 0; pr < NP; ++pr) {
+        float2 x[8];  // {hidden 2 pr, hidden 2 pr + 1} at element j of the chunk
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float4 v = xs[(q * NP + pr) * NC + lane + 32 * c];
+          x[2 * q] = make_float2(v.x, v.y);
+          x[2 * q + 1] = make_float2(v.z, v.w);
+        }
+        // per accumulator the same FMA sequence (chunk by chunk, element by element) as the
+        // scalar head; __ffma2_rn rounds each half as one IEEE fma
 #pragma unroll
         for (int u = 0; u < U; ++u)
 #pragma unroll
-          for (int j = 0; j < 8; ++j) acc[u * NB + b] = fmaf(w[u][j], x[j], acc[u * NB + b]);
+          for (int j = 0; j < 8; ++j) acc2[u][pr] = __ffma2_rn(make_float2(w[u][j], w[u][j]), x[j], acc2[u][pr]);
       }
       // keeps the shared-memory reads of later chunks from being hoisted here (NB x 8 floats per
       // chunk would otherwise stay live across the whole row and spill)
       asm volatile("" ::: "memory");
     }
-    const int gn = g + gstride;
-    if (gn < ngroups) load_group(gn);
+    float acc[NV];
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+#pragma unroll
+      for (int q = 0; q < NP; ++q) {
+        acc[u * NB + 2 * q] = acc2[u][q].x;
+        acc[u * NB + 2 * q + 1] = acc2[u][q].y;
+      }
     const float v = rbf(butterfly_sum<NV>(acc, lane));
     const int row = g * U + my_u;
     if (row < p.rows && v > best_v) {
@@ -838,15 +915,15 @@ cudaError_t launch_lm_shard(const LmShardParams& p, cudaStream_t s, bool pdl) {
     cudaFuncSetAttribute(lm_shard_kernel<NB, NORM>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     resident = resident_ctas(lm_shard_kernel<NB, NORM>, smem);
   }
-  const int ngroups = (p.rows + 1) / 2;  // two rows per warp iteration
+  constexpr int U = lm_shard_rows<NB>();
+  const int ngroups = (p.rows + U - 1) / U;  // U rows per warp iteration
   return q35_launch(lm_shard_kernel<NB, NORM>, dim3(choose_grid(ngroups, resident)), dim3(kThreads), smem, s,
                     pdl, p);
 }
 
 template <bool NORM>
 cudaError_t dispatch_lm_shard(const LmShardParams& p, cudaStream_t s, bool pdl) {
-  if (p.n <= 1) return launch_lm_shard<1, NORM>(p, s, pdl);
-  if (p.n <= 2) return launch_lm_shard<2, NORM>(p, s, pdl);
+  if (p.n <= 2) return launch_lm_shard<2, NORM>(p, s, pdl);  // one hidden runs padded to a pair
   if (p.n <= 4) return launch_lm_shard<4, NORM>(p, s, pdl);
   return launch_lm_shard<8, NORM>(p, s, pdl);
 }

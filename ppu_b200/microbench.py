@@ -111,7 +111,7 @@ def run(kernels: list[str], reps: int, layers: int = 24, a8w8: bool = False):
             # vocab-sharded head of lock-step decode over N ranks: N hiddens against one 1/N shard;
             # launches rotate over the N shards of the table so no shard is L2-resident
             e = (torch.randn(248320, H, device=dev, generator=g) * 0.02).to(torch.bfloat16)
-            ws = torch.zeros(64, device=dev, dtype=torch.uint8)
+            ws = torch.zeros(L.load().q35_lm_shard_workspace_size(), device=dev, dtype=torch.uint8)
             keys = torch.empty(8, device=dev, dtype=torch.int64)
             for world in (2, 4, 8):
                 hs = torch.randn(world, H, device=dev, generator=g).to(torch.bfloat16)

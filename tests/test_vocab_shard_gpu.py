@@ -134,7 +134,7 @@ def test_decoder_split_step_matches_decode_step():
     counters = (int(eng.cache_len), int(eng.rope_pos), int(eng.log_pos) - log0)
     eng.restore(snap)
     eng.log_pos.fill_(log0)
-    ws = torch.zeros(64, device=DEV, dtype=torch.uint8)
+    ws = torch.zeros(L.load().q35_lm_shard_workspace_size(), device=DEV, dtype=torch.uint8)
     got = []
     for step in range(12):
         eng.decode_layers()
