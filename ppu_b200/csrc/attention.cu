@@ -65,146 +65,9 @@ __global__ void __launch_bounds__(kD) qgkv_rope_kernel(
   }
 }
 
-// ============================================================================ prefill attention
-// One CTA = 64 queries of one head; 256 threads as a 16 x 16 grid. Scores for a 64 x 64 tile:
-// thread (ty, tx) owns query rows ty*4..+3 and key columns tx*4..+3. Output: rows ty*4..+3,
-// dims tx*16..+15. K is staged transposed so the score loop reads shared memory conflict-free.
-constexpr int kPQ = 64, kPK = 64;
-
-__global__ void __launch_bounds__(256) prefill_attn_kernel(const bf16* __restrict__ Q, const bf16* __restrict__ K,
-                                                          const bf16* __restrict__ V, bf16* __restrict__ O,
-                                                          int Hq, int Hkv, int L, int kv_len, int q_offset,
-                                                          float scale) {
-  extern __shared__ __align__(16) unsigned char smem[];
-  bf16* Qs = reinterpret_cast<bf16*>(smem);                 // [64][256]
-  bf16* Kt = Qs + kPQ * kD;                                 // [256][64] transposed
-  bf16* Vs = Kt + kD * kPK;                                 // [64][256]
-  float* Ps = reinterpret_cast<float*>(Vs + kPK * kD);      // [64][65]
-  const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
-  const int G = Hq / Hkv, kvh = h / G;
-  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
-  const int q0 = qt * kPQ;
-  const bf16* Qg = Q + (((int64_t)b * Hq + h) * L) * kD;
-  const bf16* Kg = K + (((int64_t)b * Hkv + kvh) * kv_len) * kD;
-  const bf16* Vg = V + (((int64_t)b * Hkv + kvh) * kv_len) * kD;
-  for (int i = threadIdx.x; i < kPQ * kD / 8; i += 256) {
-    const int rr = i / (kD / 8), cc = (i % (kD / 8)) * 8;
-    uint4 v = make_uint4(0, 0, 0, 0);
-    if (q0 + rr < L) v = *reinterpret_cast<const uint4*>(Qg + (int64_t)(q0 + rr) * kD + cc);
-    *reinterpret_cast<uint4*>(Qs + rr * kD + cc) = v;
-  }
-  float m[4], l[4], acc[4][16];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    m[i] = -FLT_MAX;
-    l[i] = 0.f;
-#pragma unroll
-    for (int j = 0; j < 16; ++j) acc[i][j] = 0.f;
-  }
-  const int last_q = min(q0 + kPQ, L) - 1 + q_offset;  // highest key any row here may see
-  const int n_kt = last_q / kPK + 1;
-  for (int kt = 0; kt < n_kt; ++kt) {
-    const int k0 = kt * kPK;
-    __syncthreads();
-    for (int i = threadIdx.x; i < kPK * kD / 8; i += 256) {
-      const int rr = i / (kD / 8), cc = (i % (kD / 8)) * 8;
-      uint4 kv = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
-      if (k0 + rr < kv_len) {
-        kv = *reinterpret_cast<const uint4*>(Kg + (int64_t)(k0 + rr) * kD + cc);
-        vv = *reinterpret_cast<const uint4*>(Vg + (int64_t)(k0 + rr) * kD + cc);
-      }
-      const bf16* kp = reinterpret_cast<const bf16*>(&kv);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) Kt[(cc + j) * kPK + rr] = kp[j];
-      *reinterpret_cast<uint4*>(Vs + rr * kD + cc) = vv;
-    }
-    __syncthreads();
-    float sc[4][4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-#pragma unroll
-      for (int j = 0; j < 4; ++j) sc[i][j] = 0.f;
-    for (int dd = 0; dd < kD; dd += 2) {
-      float qv[4][2], kv[2][4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const __nv_bfloat162 q2 = *reinterpret_cast<const __nv_bfloat162*>(Qs + (ty * 4 + i) * kD + dd);
-        qv[i][0] = __low2float(q2);
-        qv[i][1] = __high2float(q2);
-      }
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const uint2 k4 = *reinterpret_cast<const uint2*>(Kt + (dd + e) * kPK + tx * 4);
-        kv[e][0] = __uint_as_float(k4.x << 16);
-        kv[e][1] = __uint_as_float(k4.x & 0xffff0000u);
-        kv[e][2] = __uint_as_float(k4.y << 16);
-        kv[e][3] = __uint_as_float(k4.y & 0xffff0000u);
-      }
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
-#pragma unroll
-        for (int j = 0; j < 4; ++j) sc[i][j] = fmaf(qv[i][0], kv[0][j], fmaf(qv[i][1], kv[1][j], sc[i][j]));
-    }
-    // causal mask + online softmax (row max/sum over the 16 tx lanes of this row group)
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int qi = q0 + ty * 4 + i + q_offset;
-      float mx = -FLT_MAX;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int kj = k0 + tx * 4 + j;
-        sc[i][j] = (kj <= qi && kj < kv_len) ? sc[i][j] * scale : -FLT_MAX;
-        mx = fmaxf(mx, sc[i][j]);
-      }
-#pragma unroll
-      for (int o = 1; o < 16; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-      const float mn = fmaxf(m[i], mx);
-      const float alpha = (m[i] == -FLT_MAX) ? 0.f : expf(m[i] - mn);
-      float rs = 0.f;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float pr = (sc[i][j] == -FLT_MAX) ? 0.f : expf(sc[i][j] - mn);
-        Ps[(ty * 4 + i) * 65 + tx * 4 + j] = pr;
-        rs += pr;
-      }
-#pragma unroll
-      for (int o = 1; o < 16; o <<= 1) rs += __shfl_xor_sync(0xffffffffu, rs, o);
-      l[i] = l[i] * alpha + rs;
-      m[i] = mn;
-#pragma unroll
-      for (int j = 0; j < 16; ++j) acc[i][j] *= alpha;
-    }
-    __syncthreads();
-    for (int c = 0; c < kPK; ++c) {
-      float vv[16];
-      const uint4* vp = reinterpret_cast<const uint4*>(Vs + c * kD + tx * 16);
-      unpack_bf16x8(vp[0], vv);
-      unpack_bf16x8(vp[1], vv + 8);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float pr = Ps[(ty * 4 + i) * 65 + c];
-#pragma unroll
-        for (int j = 0; j < 16; ++j) acc[i][j] = fmaf(pr, vv[j], acc[i][j]);
-      }
-    }
-  }
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int qi = q0 + ty * 4 + i;
-    if (qi >= L) continue;
-    const float inv = l[i] > 0.f ? 1.0f / l[i] : 0.f;
-    __align__(16) bf16 o[16];
-#pragma unroll
-    for (int j = 0; j < 16; ++j) o[j] = f2bf(acc[i][j] * inv);
-    bf16* dst = O + (((int64_t)b * L + qi) * Hq + h) * kD + tx * 16;
-    reinterpret_cast<uint4*>(dst)[0] = reinterpret_cast<const uint4*>(o)[0];
-    reinterpret_cast<uint4*>(dst)[1] = reinterpret_cast<const uint4*>(o)[1];
-  }
-}
-
 // ============================================================================ prefill attention, tensor cores
 // FlashAttention-style causal GQA prefill on mma.sync m16n8k16 (bf16 in, FP32 accumulate).
-// CTA = (16 query rows, KV head g): warp w handles query head g * G + w, so each K/V tile in
+// CTA = (16 query rows, group g of G query heads): warp w handles query head g * G + w, so each K/V tile in
 // shared memory serves the G heads of the group. Keys stream in tiles of 32 (cp.async, double
 // buffered, rows padded by 16 bytes so ldmatrix hits distinct banks). S = Q K^T from ldmatrix
 // fragments (bf16 products are exact, FP32 accumulation), scaled, causally masked, online softmax
@@ -221,7 +84,7 @@ template <int G>
 __global__ void __launch_bounds__(2 * G * 32) prefill_attn_mma_kernel(const bf16* __restrict__ Q, const bf16* __restrict__ K,
                                                                      const bf16* __restrict__ V, bf16* __restrict__ O,
                                                                      int Hq, int Hkv, int L, int kv_len, int q_offset,
-                                                                     float scale) {
+                                                                     float scale, int kv_div) {
   extern __shared__ __align__(16) unsigned char fa_smem[];
   bf16* Qs = reinterpret_cast<bf16*>(fa_smem);        // [G][16][stride]
   bf16* KVs = Qs + G * kFaRows * kFaStride;            // per key group: K [2][32][stride], V [2][32][stride]
@@ -234,8 +97,9 @@ __global__ void __launch_bounds__(2 * G * 32) prefill_attn_mma_kernel(const bf16
   const int h = g * G + wq;
   bf16* Ks = KVs + kg * 4 * kFaKeys * kFaStride;
   bf16* Vs = Ks + 2 * kFaKeys * kFaStride;
-  const bf16* Kg = K + ((int64_t)b * Hkv + g) * kv_len * kD;
-  const bf16* Vg = V + ((int64_t)b * Hkv + g) * kv_len * kD;
+  // blockIdx.y counts groups of G query heads; kv_div of them share one KV head
+  const bf16* Kg = K + ((int64_t)b * Hkv + g / kv_div) * kv_len * kD;
+  const bf16* Vg = V + ((int64_t)b * Hkv + g / kv_div) * kv_len * kD;
   // queries of the G heads (rows past L read as zero)
   for (int i = threadIdx.x; i < G * kFaRows * (kD / 8); i += NT) {
     const int hh = i / (kFaRows * (kD / 8)), r = (i / (kD / 8)) % kFaRows, c = (i % (kD / 8)) * 8;
@@ -428,15 +292,16 @@ template <int G>
 int launch_prefill_mma(const void* q, const void* k, const void* v, void* out, int64_t batch, int64_t q_heads,
                        int64_t kv_heads, int64_t seq_len, int64_t kv_len, int64_t q_offset, float scale,
                        cudaStream_t stream) {
+  const int kv_div = (int)(q_heads / kv_heads / G);  // query-head groups of G per KV head
   // query tile + two key groups x two buffers x (K, V) tiles; the merge reuses the key tiles
   const size_t smem = (size_t)(G * kFaRows + 8 * kFaKeys) * kFaStride * sizeof(bf16);
   static_assert((size_t)4 * 32 * (4 + 32 * 4 + 1) * sizeof(float) <= (size_t)8 * kFaKeys * kFaStride * sizeof(bf16),
                 "the merge partials fit in the key / value tiles");
   cudaFuncSetAttribute(prefill_attn_mma_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  const dim3 grid((unsigned)((seq_len + kFaRows - 1) / kFaRows), (unsigned)kv_heads, (unsigned)batch);
+  const dim3 grid((unsigned)((seq_len + kFaRows - 1) / kFaRows), (unsigned)(kv_heads * kv_div), (unsigned)batch);
   prefill_attn_mma_kernel<G><<<grid, 2 * G * 32, smem, stream>>>((const bf16*)q, (const bf16*)k, (const bf16*)v,
                                                              (bf16*)out, (int)q_heads, (int)kv_heads, (int)seq_len,
-                                                             (int)kv_len, (int)q_offset, scale);
+                                                             (int)kv_len, (int)q_offset, scale, kv_div);
   return q35_check_launch("prefill_attention");
 }
 
@@ -484,20 +349,15 @@ extern "C" int q35_prefill_attention(const void* q, const void* k, const void* v
                   kv_len >= q_offset + seq_len,
               "prefill_attention: bad shape");
   if (batch * seq_len == 0) return Q35_OK;
-  switch (q_heads / kv_heads) {  // tensor-core path for the group sizes it is built for
-    case 4: return launch_prefill_mma<4>(q, k, v, out, batch, q_heads, kv_heads, seq_len, kv_len, q_offset, scale,
-                                         (cudaStream_t)stream);
-    case 2: return launch_prefill_mma<2>(q, k, v, out, batch, q_heads, kv_heads, seq_len, kv_len, q_offset, scale,
-                                         (cudaStream_t)stream);
-    case 1: return launch_prefill_mma<1>(q, k, v, out, batch, q_heads, kv_heads, seq_len, kv_len, q_offset, scale,
-                                         (cudaStream_t)stream);
-    default: break;
-  }
-  const size_t smem = (size_t)(kPQ * kD + kD * kPK + kPK * kD) * sizeof(bf16) + (size_t)kPQ * 65 * sizeof(float);
-  cudaFuncSetAttribute(prefill_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  dim3 grid((unsigned)((seq_len + kPQ - 1) / kPQ), (unsigned)q_heads, (unsigned)batch);
-  prefill_attn_kernel<<<grid, 256, smem, (cudaStream_t)stream>>>((const bf16*)q, (const bf16*)k, (const bf16*)v,
-                                                                 (bf16*)out, (int)q_heads, (int)kv_heads,
-                                                                 (int)seq_len, (int)kv_len, (int)q_offset, scale);
-  return q35_check_launch("prefill_attention");
+  // tensor-core kernel for every group size: a group of G query heads per KV head runs as
+  // G / G' CTA groups of G' = 4, 2 or 1 heads (the largest that divides G), sharing the KV head
+  const int64_t group = q_heads / kv_heads;
+  if (group % 4 == 0)
+    return launch_prefill_mma<4>(q, k, v, out, batch, q_heads, kv_heads, seq_len, kv_len, q_offset, scale,
+                                 (cudaStream_t)stream);
+  if (group % 2 == 0)
+    return launch_prefill_mma<2>(q, k, v, out, batch, q_heads, kv_heads, seq_len, kv_len, q_offset, scale,
+                                 (cudaStream_t)stream);
+  return launch_prefill_mma<1>(q, k, v, out, batch, q_heads, kv_heads, seq_len, kv_len, q_offset, scale,
+                               (cudaStream_t)stream);
 }

@@ -1,8 +1,9 @@
 // Row norms and elementwise activations (reference: qwen35_fused/kernels.py:24-333).
 //
 // One CTA per row for the 2048-wide norms (the reduction stays on chip, 16-byte chunks at width
-// 2048); one warp per row for the 128-wide gated norm (8-byte chunks); vectorised grid-stride loops
-// for the elementwise ops.
+// 2048); one warp per row for the 128-wide gated norm (8-byte chunks) and for the 256-1024-wide
+// norms (16-byte chunks); 16-byte vector loops for the elementwise ops. Scalar kernels cover
+// widths that are not multiples of 8 and unaligned tensors.
 #include "common.cuh"
 
 using namespace q35;
@@ -136,6 +137,134 @@ __global__ void gated_rms_kernel(const bf16* __restrict__ x, const bf16* __restr
   }
 }
 
+// ---- 16-byte vector forms (8 bf16 per thread per step); the scalar kernels above and below
+// remain for widths that are not multiples of 8 or unaligned tensors.
+Q35_DEV uint4 pack_bf16x8(const float (&f)[8]) {
+  return make_uint4(pack_bf2(f[0], f[1]), pack_bf2(f[2], f[3]), pack_bf2(f[4], f[5]), pack_bf2(f[6], f[7]));
+}
+
+// RMSNorm(1+w) of rows of width 256 * CPL, one warp per row, CPL 16-byte chunks per lane.
+template <bool ADD, int CPL>
+__global__ void __launch_bounds__(256) rms_rows_warp_kernel(const bf16* __restrict__ x, const bf16* __restrict__ upd,
+                                                            const bf16* __restrict__ w, bf16* __restrict__ resid_out,
+                                                            bf16* __restrict__ out, int64_t rows, float eps) {
+  constexpr int W = 256 * CPL;
+  const int lane = threadIdx.x & 31;
+  for (int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5); row < rows; row += (int64_t)gridDim.x * 8) {
+    float f[CPL][8];
+    float ss = 0.f;
+#pragma unroll
+    for (int c = 0; c < CPL; ++c) {
+      const int64_t off = row * W + 8 * (lane + 32 * c);
+      unpack_bf16x8(*reinterpret_cast<const uint4*>(x + off), f[c]);
+      if (ADD) {
+        float u[8];
+        unpack_bf16x8(*reinterpret_cast<const uint4*>(upd + off), u);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) f[c][j] = rbf(f[c][j] + u[j]);
+        *reinterpret_cast<uint4*>(resid_out + off) = pack_bf16x8(f[c]);
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss += f[c][j] * f[c][j];
+    }
+    const float r = rsqrt_ieee(warp_sum(ss) / (float)W + eps);
+#pragma unroll
+    for (int c = 0; c < CPL; ++c) {
+      float wv[8], o[8];
+      unpack_bf16x8(*reinterpret_cast<const uint4*>(w + 8 * (lane + 32 * c)), wv);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[j] = f[c][j] * r * (1.0f + wv[j]);
+      *reinterpret_cast<uint4*>(out + row * W + 8 * (lane + 32 * c)) = pack_bf16x8(o);
+    }
+  }
+}
+
+// Gated RMSNorm of rows of width 256 * CPL, one warp per row (same rounding points as
+// gated_rms_kernel).
+template <int CPL>
+__global__ void __launch_bounds__(256) gated_rms_warp_kernel(const bf16* __restrict__ x, const bf16* __restrict__ gate,
+                                                             const bf16* __restrict__ w, bf16* __restrict__ out,
+                                                             int64_t rows, float eps, int gate_group,
+                                                             int64_t gate_stride) {
+  constexpr int W = 256 * CPL;
+  const int lane = threadIdx.x & 31;
+  for (int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5); row < rows; row += (int64_t)gridDim.x * 8) {
+    const bf16* gr = gate + (row / gate_group) * gate_stride + (row % gate_group) * W;
+    float f[CPL][8], g[CPL][8];
+    float ss = 0.f;
+#pragma unroll
+    for (int c = 0; c < CPL; ++c) {
+      unpack_bf16x8(*reinterpret_cast<const uint4*>(x + row * W + 8 * (lane + 32 * c)), f[c]);
+      unpack_bf16x8(*reinterpret_cast<const uint4*>(gr + 8 * (lane + 32 * c)), g[c]);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss += f[c][j] * f[c][j];
+    }
+    const float r = rsqrt_ieee(warp_sum(ss) / (float)W + eps);
+#pragma unroll
+    for (int c = 0; c < CPL; ++c) {
+      float wv[8], o[8];
+      unpack_bf16x8(*reinterpret_cast<const uint4*>(w + 8 * (lane + 32 * c)), wv);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float nrm = rbf(f[c][j] * r);
+        const float wt = rbf(nrm * wv[j]);
+        o[j] = wt * silu_f(g[c][j]);
+      }
+      *reinterpret_cast<uint4*>(out + row * W + 8 * (lane + 32 * c)) = pack_bf16x8(o);
+    }
+  }
+}
+
+// silu(gate) * up over [rows, 2 * width] -> [rows, width], width % 8 == 0; one CTA per row in a
+// row-stride loop, 16-byte chunks.
+__global__ void __launch_bounds__(256) silu_mul_v8_kernel(const bf16* __restrict__ packed, bf16* __restrict__ out,
+                                                          int64_t rows, int width) {
+  const int n8 = width / 8;
+  for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
+    const bf16* pr = packed + r * 2 * width;
+    for (int c = threadIdx.x; c < n8; c += blockDim.x) {
+      float gf[8], uf[8], o[8];
+      unpack_bf16x8(*reinterpret_cast<const uint4*>(pr + 8 * c), gf);
+      unpack_bf16x8(*reinterpret_cast<const uint4*>(pr + width + 8 * c), uf);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[j] = rbf(silu_f(gf[j])) * uf[j];
+      *reinterpret_cast<uint4*>(out + r * width + 8 * c) = pack_bf16x8(o);
+    }
+  }
+}
+
+// x * sigmoid(gate) over n8 16-byte chunks.
+__global__ void __launch_bounds__(256) sigmoid_mul_v8_kernel(const bf16* __restrict__ x, const bf16* __restrict__ gate,
+                                                             bf16* __restrict__ out, int64_t n8) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n8; i += (int64_t)gridDim.x * blockDim.x) {
+    float xf[8], gf[8], o[8];
+    unpack_bf16x8(reinterpret_cast<const uint4*>(x)[i], xf);
+    unpack_bf16x8(reinterpret_cast<const uint4*>(gate)[i], gf);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[j] = xf[j] * rbf(sigmoid_f(gf[j]));
+    reinterpret_cast<uint4*>(out)[i] = pack_bf16x8(o);
+  }
+}
+
+// Attention output gate (the gate block of each head inside the packed QGKV row), 16-byte chunks;
+// head_dim % 8 == 0 so a chunk never straddles two heads.
+__global__ void __launch_bounds__(256) attn_gate_v8_kernel(const bf16* __restrict__ x, const bf16* __restrict__ packed,
+                                                           bf16* __restrict__ out, int64_t rows, int hidden,
+                                                           int64_t stride, int head_dim) {
+  const int n8 = hidden / 8;
+  for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
+    for (int c = threadIdx.x; c < n8; c += blockDim.x) {
+      const int col = 8 * c, h = col / head_dim, d = col - h * head_dim;
+      float xf[8], gf[8], o[8];
+      unpack_bf16x8(*reinterpret_cast<const uint4*>(x + r * hidden + col), xf);
+      unpack_bf16x8(*reinterpret_cast<const uint4*>(packed + r * stride + (int64_t)h * 2 * head_dim + head_dim + d), gf);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[j] = xf[j] * rbf(sigmoid_f(gf[j]));
+      *reinterpret_cast<uint4*>(out + r * hidden + col) = pack_bf16x8(o);
+    }
+  }
+}
+
 __global__ void silu_mul_kernel(const bf16* __restrict__ packed, bf16* __restrict__ out,
                                 int64_t rows, int64_t width) {
   const int64_t total = rows * width;
@@ -185,6 +314,37 @@ int grid_for(int64_t n, int threads) {
   return (int)(g < 1 ? 1 : g);
 }
 
+// Widths the warp-per-row norms cover: 256, 512 or 1024 (1, 2 or 4 chunks per lane).
+bool warp_rows_ok(int64_t width) { return width == 256 || width == 512 || width == 1024; }
+
+unsigned warp_rows_grid(int64_t rows) {
+  const int64_t g = (rows + 7) / 8;  // eight rows (warps) per CTA
+  return (unsigned)(g < 8 * kNumSMs ? g : 8 * kNumSMs);
+}
+
+template <bool ADD>
+void launch_rms_warp(const bf16* x, const bf16* upd, const bf16* w, bf16* resid_out, bf16* out, int64_t rows,
+                     int64_t width, float eps, cudaStream_t s) {
+  const unsigned grid = warp_rows_grid(rows);
+  if (width == 256)
+    rms_rows_warp_kernel<ADD, 1><<<grid, 256, 0, s>>>(x, upd, w, resid_out, out, rows, eps);
+  else if (width == 512)
+    rms_rows_warp_kernel<ADD, 2><<<grid, 256, 0, s>>>(x, upd, w, resid_out, out, rows, eps);
+  else
+    rms_rows_warp_kernel<ADD, 4><<<grid, 256, 0, s>>>(x, upd, w, resid_out, out, rows, eps);
+}
+
+void launch_gated_warp(const bf16* x, const bf16* gate, const bf16* w, bf16* out, int64_t rows, int64_t width,
+                       float eps, int gate_group, int64_t gate_stride, cudaStream_t s) {
+  const unsigned grid = warp_rows_grid(rows);
+  if (width == 256)
+    gated_rms_warp_kernel<1><<<grid, 256, 0, s>>>(x, gate, w, out, rows, eps, gate_group, gate_stride);
+  else if (width == 512)
+    gated_rms_warp_kernel<2><<<grid, 256, 0, s>>>(x, gate, w, out, rows, eps, gate_group, gate_stride);
+  else
+    gated_rms_warp_kernel<4><<<grid, 256, 0, s>>>(x, gate, w, out, rows, eps, gate_group, gate_stride);
+}
+
 }  // namespace
 
 extern "C" int q35_rms_norm(const void* x, const void* weight, void* out, int64_t rows,
@@ -196,6 +356,9 @@ extern "C" int q35_rms_norm(const void* x, const void* weight, void* out, int64_
   if (width == 2048 && Q35_ALIGNED(x, 16) && Q35_ALIGNED(weight, 16) && Q35_ALIGNED(out, 16))
     rms_rows2048_kernel<false><<<(unsigned)rows, kRowThreads, 0, (cudaStream_t)stream>>>(
         (const bf16*)x, nullptr, (const bf16*)weight, nullptr, (bf16*)out, eps);
+  else if (warp_rows_ok(width) && Q35_ALIGNED(x, 16) && Q35_ALIGNED(weight, 16) && Q35_ALIGNED(out, 16))
+    launch_rms_warp<false>((const bf16*)x, nullptr, (const bf16*)weight, nullptr, (bf16*)out, rows, width, eps,
+                           (cudaStream_t)stream);
   else
     rms_rows_kernel<false><<<(unsigned)rows, kRowThreads, 0, (cudaStream_t)stream>>>(
         (const bf16*)x, nullptr, (const bf16*)weight, nullptr, (bf16*)out, (int)width, eps);
@@ -214,6 +377,10 @@ extern "C" int q35_residual_add_rms_norm(const void* residual, const void* updat
     rms_rows2048_kernel<true><<<(unsigned)rows, kRowThreads, 0, (cudaStream_t)stream>>>(
         (const bf16*)residual, (const bf16*)update, (const bf16*)weight, (bf16*)residual_out, (bf16*)norm_out,
         eps);
+  else if (warp_rows_ok(width) && Q35_ALIGNED(residual, 16) && Q35_ALIGNED(update, 16) && Q35_ALIGNED(weight, 16) &&
+           Q35_ALIGNED(residual_out, 16) && Q35_ALIGNED(norm_out, 16))
+    launch_rms_warp<true>((const bf16*)residual, (const bf16*)update, (const bf16*)weight, (bf16*)residual_out,
+                          (bf16*)norm_out, rows, width, eps, (cudaStream_t)stream);
   else
     rms_rows_kernel<true><<<(unsigned)rows, kRowThreads, 0, (cudaStream_t)stream>>>(
         (const bf16*)residual, (const bf16*)update, (const bf16*)weight, (bf16*)residual_out,
@@ -242,6 +409,10 @@ int q35_gated_rms_strided_launch(const void* x, const void* gate, int gate_group
       Q35_ALIGNED(out, 8))
     gated_rms128_kernel<<<blocks, 32 * rows_per_block, 0, stream>>>(
         (const bf16*)x, (const bf16*)gate, (const bf16*)weight, (bf16*)out, rows, eps, gate_group, gate_stride);
+  else if (warp_rows_ok(width) && gate_stride % 8 == 0 && Q35_ALIGNED(x, 16) && Q35_ALIGNED(gate, 16) &&
+           Q35_ALIGNED(weight, 16) && Q35_ALIGNED(out, 16))
+    launch_gated_warp((const bf16*)x, (const bf16*)gate, (const bf16*)weight, (bf16*)out, rows, width, eps,
+                      gate_group, gate_stride, stream);
   else
     gated_rms_kernel<<<blocks, 32 * rows_per_block, 0, stream>>>((const bf16*)x, (const bf16*)gate,
                                                                  (const bf16*)weight, (bf16*)out, rows,
@@ -263,8 +434,12 @@ extern "C" int q35_silu_and_mul(const void* packed, void* out, int64_t rows, int
                                 void* stream) {
   Q35_REQUIRE(packed && out && rows >= 0 && width > 0, "silu_and_mul: bad argument");
   if (rows == 0) return Q35_OK;
-  silu_mul_kernel<<<grid_for(rows * width, 256), 256, 0, (cudaStream_t)stream>>>(
-      (const bf16*)packed, (bf16*)out, rows, width);
+  if (width % 8 == 0 && width <= (1 << 30) && Q35_ALIGNED(packed, 16) && Q35_ALIGNED(out, 16))
+    silu_mul_v8_kernel<<<(unsigned)(rows < 8 * kNumSMs ? rows : 8 * kNumSMs), 256, 0, (cudaStream_t)stream>>>(
+        (const bf16*)packed, (bf16*)out, rows, (int)width);
+  else
+    silu_mul_kernel<<<grid_for(rows * width, 256), 256, 0, (cudaStream_t)stream>>>(
+        (const bf16*)packed, (bf16*)out, rows, width);
   return q35_check_launch("silu_and_mul");
 }
 
@@ -272,8 +447,12 @@ extern "C" int q35_sigmoid_mul(const void* x, const void* gate, void* out, int64
                                void* stream) {
   Q35_REQUIRE(x && gate && out && n >= 0, "sigmoid_mul: bad argument");
   if (n == 0) return Q35_OK;
-  sigmoid_mul_kernel<<<grid_for(n, 256), 256, 0, (cudaStream_t)stream>>>(
-      (const bf16*)x, (const bf16*)gate, (bf16*)out, n);
+  if (n % 8 == 0 && Q35_ALIGNED(x, 16) && Q35_ALIGNED(gate, 16) && Q35_ALIGNED(out, 16))
+    sigmoid_mul_v8_kernel<<<grid_for(n / 8, 256), 256, 0, (cudaStream_t)stream>>>(
+        (const bf16*)x, (const bf16*)gate, (bf16*)out, n / 8);
+  else
+    sigmoid_mul_kernel<<<grid_for(n, 256), 256, 0, (cudaStream_t)stream>>>(
+        (const bf16*)x, (const bf16*)gate, (bf16*)out, n);
   return q35_check_launch("sigmoid_mul");
 }
 
@@ -284,8 +463,13 @@ extern "C" int q35_attention_gate_mul(const void* x, const void* packed, void* o
   Q35_REQUIRE(rows >= 0 && head_dim > 0 && hidden % head_dim == 0 && packed_stride >= 2 * hidden,
               "attention_gate_mul: bad shape");
   if (rows == 0) return Q35_OK;
-  attn_gate_kernel<<<grid_for(rows * hidden, 256), 256, 0, (cudaStream_t)stream>>>(
-      (const bf16*)x, (const bf16*)packed, (bf16*)out, rows, hidden, packed_stride, head_dim);
+  if (hidden % 8 == 0 && head_dim % 8 == 0 && packed_stride % 8 == 0 && hidden <= (1 << 30) &&
+      Q35_ALIGNED(x, 16) && Q35_ALIGNED(packed, 16) && Q35_ALIGNED(out, 16))
+    attn_gate_v8_kernel<<<(unsigned)(rows < 8 * kNumSMs ? rows : 8 * kNumSMs), 256, 0, (cudaStream_t)stream>>>(
+        (const bf16*)x, (const bf16*)packed, (bf16*)out, rows, (int)hidden, packed_stride, (int)head_dim);
+  else
+    attn_gate_kernel<<<grid_for(rows * hidden, 256), 256, 0, (cudaStream_t)stream>>>(
+        (const bf16*)x, (const bf16*)packed, (bf16*)out, rows, hidden, packed_stride, head_dim);
   return q35_check_launch("attention_gate_mul");
 }
 

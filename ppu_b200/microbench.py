@@ -107,6 +107,58 @@ def run(kernels: list[str], reps: int, layers: int = 24, a8w8: bool = False):
             t = _time(lambda i: K.lm_head_argmax(h, e, norm_weight=nw), reps)
             report(name, t, nbytes=e.numel() * 2)
             del e
+        elif name == "api_ops":
+            # the API-level kernels the decoder does not launch (standalone norms and activations,
+            # the reference's sequential DeltaNet scan, the warp-MMA GEMM, generic-K fallbacks), at
+            # prefill-1024 shapes of the 2B model; one launch each per rep, algorithmic bytes = the
+            # tensors each one must read and write once
+            def r(*shape, scale=1.0):
+                return (torch.randn(*shape, device=dev, generator=g) * scale).to(torch.bfloat16)
+
+            M, bf = 1024, 2
+            x2k, u2k, w2k = r(M, H), r(M, H), r(H, scale=0.1)
+            x256, w256 = r(M * 8, 256), r(256, scale=0.1)
+            x128, g128, w128 = r(M * 16, 128), r(M * 16, 128), r(128, scale=0.1)
+            g256 = r(M * 8, 256)
+            packed_mlp = r(M, 2 * I)
+            qgkv = r(M, 5120)
+            conv_x, conv_w = r(1, M, 6144), r(6144, 4, scale=0.5)
+            conv_s = torch.zeros(1, 6144, 4, device=dev, dtype=torch.bfloat16)
+            conv_x1 = r(1, 1, 6144)
+            dq = r(1, M, 6144, scale=0.1)
+            dpack = r(1, M, 8224)
+            dstate = torch.zeros(1, 16, 128, 128, device=dev)
+            a_log, dt_bias = r(16, scale=0.5), r(16, scale=0.5)
+            wg = r(8224, H, scale=0.02)
+            qa, ka, va = r(1, 8, 512, 256), r(1, 1, 512, 256), r(1, 1, 512, 256)
+            w4k, x4k = r(4096, 4096, scale=0.02), r(4096)
+            e1k, h1k, n1k = r(65536, 1024, scale=0.02), r(1, 1024), r(1024, scale=0.1)
+            cases = [
+                ("rms_rows2048_kernel", lambda i: K.rms_norm(x2k, w2k), 2 * M * H * bf),
+                ("rms_rows_warp_kernel<0,1> (width 256)", lambda i: K.rms_norm(x256, w256), 2 * M * 8 * 256 * bf),
+                ("rms_rows2048_kernel<ADD>", lambda i: K.residual_add_rms_norm(x2k, u2k, w2k), 4 * M * H * bf),
+                ("gated_rms128_kernel", lambda i: K.gated_rms_norm(x128, g128, w128), 3 * M * 16 * 128 * bf),
+                ("gated_rms_warp_kernel<1> (width 256)", lambda i: K.gated_rms_norm(x256, g256, w256), 3 * M * 8 * 256 * bf),
+                ("silu_mul_v8_kernel", lambda i: K.silu_and_mul(packed_mlp), 3 * M * I * bf),
+                ("sigmoid_mul_v8_kernel", lambda i: K.sigmoid_mul(x2k, u2k), 3 * M * H * bf),
+                ("attn_gate_v8_kernel", lambda i: K.attention_gate_mul(x2k, qgkv, 256), 3 * M * H * bf),
+                ("conv_prefill_win_kernel<4>", lambda i: K.causal_conv1d_fused(conv_x, conv_w, conv_s),
+                 2 * M * 6144 * bf),
+                ("conv_update_kernel", lambda i: K.causal_conv1d_fused(conv_x1, conv_w, conv_s), 2 * 6144 * bf * 5),
+                ("delta_scan_kernel (sequential, 1024 tokens)",
+                 lambda i: K.delta_recurrent_fused(dq, dpack, a_log, dt_bias, dstate), (3 * 6144 + 2048 + 32 + 2048) * M * bf),
+                ("quant_rows_v8_kernel", lambda i: K.quantize_rows(x2k), M * H * (bf + 1) + M * 4),
+                ("gemv_any_kernel (K 4096)", lambda i: K.fused_gemv(w4k, x4k), w4k.numel() * bf),
+                ("lm_head_any_kernel (K 1024)", lambda i: K.lm_head_argmax(h1k, e1k, norm_weight=n1k), e1k.numel() * bf),
+            ]
+            for kname, fn, nbytes in cases:
+                report(kname, _time(fn, reps), nbytes=nbytes)
+            t = _time(lambda i: K.gemm(x2k, wg), reps)
+            report("gemm_kernel (warp mma.sync, 1024 x 8224 x 2048)", t, flops=2 * M * 8224 * H)
+            t = _time(lambda i: K.prefill_attention(qa, ka, va, 1.0 / 16), reps)
+            report("prefill_attn_mma_kernel<4> (group 8 as 2 x 4 heads, 512 tokens)", t, flops=4 * 8 * 256 * 512 * 512 // 2)
+            keys = torch.full((8,), -5, device=dev, dtype=torch.int64)
+            report("lm_keys_finish_kernel", _time(lambda i: K.lm_keys_to_tokens(keys), reps), nbytes=128)
         elif name == "lm_shard":
             # vocab-sharded head of lock-step decode over N ranks: N hiddens against one 1/N shard;
             # launches rotate over the N shards of the table so no shard is L2-resident

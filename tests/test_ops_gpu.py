@@ -66,6 +66,33 @@ def test_golden_qgkv_and_gate():
     assert_bf16_close(K.attention_gate_mul(cu(c["attn_out"]), cu(c["packed"]), 256).cpu(), c["gated"])
 
 
+# widths that take the 16-byte vector kernels (multiples of 8, warp-per-row norms at 256-1024)
+# and widths that fall back to the scalar kernels
+@pytest.mark.parametrize("rows,width", [(1024, 256), (300, 512), (33, 1024), (64, 2048), (17, 200), (9, 129)])
+def test_norms_vector_and_scalar_paths(rows, width):
+    x, u = randn(rows, width, seed=width), randn(rows, width, seed=width + 1)
+    w = randn(width, seed=width + 2, scale=0.1)
+    assert_bf16_close(K.rms_norm(cu(x), cu(w)).cpu(), O.rms_norm(x, w))
+    r, n = K.residual_add_rms_norm(cu(x), cu(u), cu(w))
+    ro, no = O.residual_add_rms_norm(x, u, w)
+    assert torch.equal(r.cpu(), ro)
+    assert_bf16_close(n.cpu(), no)
+    g = randn(rows, width, seed=width + 3)
+    assert_bf16_close(K.gated_rms_norm(cu(x), cu(g), cu(w)).cpu(), O.gated_rms_norm(x, g, w))
+
+
+@pytest.mark.parametrize("rows,width", [(1024, 6144), (1, 6144), (3, 100)])
+def test_activations_vector_and_scalar_paths(rows, width):
+    packed = randn(rows, 2 * width, seed=width)
+    assert_bf16_close(K.silu_and_mul(cu(packed)).cpu(), O.silu_and_mul(packed))
+    x, gt = randn(rows, width, seed=width + 1), randn(rows, width, seed=width + 2)
+    assert_bf16_close(K.sigmoid_mul(cu(x), cu(gt)).cpu(), O.sigmoid_mul(x, gt))
+    for hidden, hd in ((2048, 256), (96, 12)):  # vector path / head_dim not a multiple of 8
+        att = randn(rows, hidden, seed=hidden)
+        qg = randn(rows, 2 * hidden + 64, seed=hidden + 1)
+        assert_bf16_close(K.attention_gate_mul(cu(att), cu(qg), hd).cpu(), O.attention_gate_mul(att, qg, hd))
+
+
 def test_golden_lm_head_and_tie():
     c = GOLDEN["lm_head"]
     assert torch.equal(K.lm_head_argmax(cu(c["h"]), cu(c["w"])).cpu(), c["out"])
@@ -94,6 +121,22 @@ def test_golden_conv(n):
     assert torch.equal(st.cpu(), c["pstate"])
 
 
+# the sliding-window kernel (full and partial last runs, packed rows wider than the channels) and
+# the generic kernel (L < 4): outputs against the oracle, the conv state bit-exact
+@pytest.mark.parametrize("length,channels,stride", [(1024, 6144, 8224), (37, 6144, 6144), (50, 100, 100),
+                                                    (3, 64, 64)])
+def test_causal_conv_paths(length, channels, stride):
+    x = randn(1, length, stride, seed=length + channels)
+    w = randn(channels, 4, seed=5, scale=0.5)
+    st0 = randn(1, channels, 4, seed=6)
+    st = cu(st0.clone())
+    out = K.causal_conv1d_fused(cu(x), cu(w), st)
+    sto = st0.clone()
+    want = O.causal_conv1d(x, w, sto)
+    assert_bf16_close(out.cpu(), want)
+    assert torch.equal(st.cpu(), sto)
+
+
 def test_golden_delta_recurrent():
     c = GOLDEN["delta"]
     st = cu(c["state0"].clone())
@@ -103,7 +146,7 @@ def test_golden_delta_recurrent():
 
 
 # ------------------------------------------------------------------ A8W8 (bit-exact)
-@pytest.mark.parametrize("rows,width", [(1, 2048), (7, 6144), (64, 2048)])
+@pytest.mark.parametrize("rows,width", [(1, 2048), (7, 6144), (64, 2048), (5, 100), (1024, 2048)])
 def test_quantize_rows_bit_exact(rows, width):
     x = randn(rows, width, seed=rows + width)
     x[0, :5] = 0
@@ -283,6 +326,18 @@ def test_prefill_attention(length):
     assert err < 1e-2
     if length == 1024:  # probabilities kept to ~16 bits: within a few BF16 output roundings of FP32
         assert err < 3e-3, err
+
+
+# every group size runs on the tensor-core kernel: G = 8 as two groups of 4 per KV head, G = 6 as
+# three of 2, G = 3 and 5 as single heads; batch 2 and a query offset into a longer KV
+@pytest.mark.parametrize("hq,hkv,length,kv_extra", [(16, 2, 200, 0), (12, 2, 64, 0), (3, 1, 33, 0),
+                                                   (10, 2, 80, 0), (8, 2, 50, 30)])
+def test_prefill_attention_group_sizes(hq, hkv, length, kv_extra):
+    q = randn(2, hq, length, 256, seed=hq)
+    k = randn(2, hkv, length + kv_extra, 256, seed=hq + 1)
+    v = randn(2, hkv, length + kv_extra, 256, seed=hq + 2)
+    out = K.prefill_attention(cu(q), cu(k), cu(v), 0.0625, q_offset=kv_extra)
+    assert rel_err(out, O.causal_attention(q, k, v, 0.0625, q_offset=kv_extra)) < 1e-2
 
 
 # ------------------------------------------------------------------ DeltaNet
