@@ -110,13 +110,18 @@ Q35_DEV void epilogue(const GemvParams& p, int unit, float y0, float y1) {
 
 // ---------------------------------------------------------------------------------------------
 // Fast path: compile-time K. A warp's unit group is streamed in SEG segments of CHS 16-byte
-// chunks per lane (at most 4 chunks = 16 registers per segment buffer), double-buffered: while
+// chunks per lane (4 or 8 chunks = 16 or 32 registers per segment buffer), double-buffered: while
 // segment i is consumed, segment i+1 is in flight, and segment i+2 is issued right after.
 template <int K, bool INT8, int RPU>
 struct FastShape {
   static constexpr int ES = INT8 ? 1 : 2;
   static constexpr int CHT = K * ES / 512;                       // chunks per row per lane
-  static constexpr int BUDGET = 4;                               // 16-byte chunks per lane per segment buffer
+  // 16-byte chunks per lane per segment buffer. 8 where a unit is long (bf16 K = 6144, int8
+  // K = 6144, int8 gate/up pairs): two wide segments in flight, issued before the PDL wait, start
+  // the stream while the previous kernel drains (bf16 decode 999 -> 1049 tok/s, A8W8 1156 -> 1240);
+  // 4 elsewhere (8 spills the bf16 gate/up pair kernel and slowed it; int8 in/out projections at
+  // 8, two rows per warp group, went 1242 -> 1219 tok/s)
+  static constexpr int BUDGET = (K * ES >= 6144 || (INT8 && RPU == 2)) ? 8 : 4;
   static constexpr int SEG = (RPU * CHT > BUDGET) ? (RPU * CHT + BUDGET - 1) / BUDGET : 1;
   static constexpr int CHS = CHT / SEG;                          // chunks per segment
   static constexpr int U = (SEG == 1) ? ((BUDGET / (RPU * CHT)) < 1 ? 1 : BUDGET / (RPU * CHT)) : 1;
