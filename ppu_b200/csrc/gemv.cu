@@ -127,8 +127,8 @@ struct FastShape {
   static constexpr int U = (SEG == 1) ? ((BUDGET / (RPU * CHT)) < 1 ? 1 : BUDGET / (RPU * CHT)) : 1;
   // bf16: segments 2 .. 2 + PRE - 1 of a warp's stream are copied into shared memory with
   // cp.async before the PDL wait, next to the two register buffers: 4 KB more per warp in flight
-  // while the previous kernel drains, at no register cost (decode 1052 -> 1098 tok/s). Not for
-  // int8, where it measured slower (A8W8 1244 -> 1128 tok/s).
+  // while the previous kernel drains, at no register cost (decode 1052 -> 1098 tok/s; 2 KB per
+  // warp gave 1077, 8 KB 1041). Not for int8, where it measured slower (A8W8 1244 -> 1128).
   static constexpr int SEG_BYTES = U * RPU * CHS * 512;          // one segment of one warp
   static constexpr int PRE = INT8 ? 0 : 4096 / SEG_BYTES;
   static_assert(K * ES % 512 == 0, "K must fill whole warp-wide 16-byte chunks");
