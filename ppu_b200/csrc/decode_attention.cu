@@ -319,7 +319,7 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(DecodeParams p) {
 }
 
 // ---------------------------------------------------------------------------------------------
-// Cluster variant of the fused decode mixer (decoder path, caches up to kClusterCTAs * kClRows):
+// Cluster variant of the fused decode mixer (decoder path, caches up to kClMaxRows rows):
 // one cluster of kClusterCTAs CTAs per (batch, KV head). Each CTA owns a contiguous slice of the
 // cached rows and copies its K/V rows into shared memory with cp.async BEFORE the programmatic-
 // dependent-launch wait: those rows and the row count were written by earlier steps (the kernel
@@ -329,12 +329,20 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(DecodeParams p) {
 // partials meet over distributed shared memory: CTA r merges dims [r * D / C, (r + 1) * D / C)
 // of every head from all peers and writes the gated BF16 output. No global scratch, no second
 // pass.
-constexpr int kClusterCTAs = 8;
-constexpr int kClRows = 160;
-constexpr size_t kClSmemBytes = 2ull * kClRows * kD * sizeof(bf16);
+constexpr int kClMaxRows = 1280;  // cached rows the cluster variant covers (8 CTAs x 160 rows)
+template <int CL>
+constexpr int cl_rows() {
+  return kClMaxRows / CL;
+}
+template <int CL>
+constexpr size_t cl_smem_bytes() {
+  return 2ull * cl_rows<CL>() * kD * sizeof(bf16);
+}
 
-template <int G>
+template <int G, int CL>
 __global__ void __launch_bounds__(kThreads, 1) attn_decode_cluster_kernel(DecodeParams p) {
+  constexpr int kClusterCTAs = CL;
+  constexpr int kClRows = cl_rows<CL>();
   extern __shared__ __align__(16) unsigned char cl_smem[];
   bf16* Ks = reinterpret_cast<bf16*>(cl_smem);
   bf16* Vs = Ks + kClRows * kD;
@@ -545,13 +553,10 @@ WsLayout ws_layout(int64_t batch, int64_t heads, int64_t kv_heads, int64_t cache
   return w;
 }
 
-template <int G>
+template <int G, int CL>
 int launch_cluster(const DecodeParams& p, int64_t batch, cudaStream_t st, bool pdl) {
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(attn_decode_cluster_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kClSmemBytes);
-    attr = true;
-  }
+  constexpr int kClusterCTAs = CL;
+  constexpr size_t kClSmemBytes = cl_smem_bytes<CL>();
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(kClusterCTAs, p.Hkv, (unsigned)batch);
   cfg.blockDim = dim3(kThreads);
@@ -566,14 +571,46 @@ int launch_cluster(const DecodeParams& p, int64_t batch, cudaStream_t st, bool p
   attrs[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attrs;
   cfg.numAttrs = pdl ? 2 : 1;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, attn_decode_cluster_kernel<G>, p);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, attn_decode_cluster_kernel<G, CL>, p);
   if (e != cudaSuccess) return q35_fail(Q35_ECUDA, "decode attention (cluster) launch: %s", cudaGetErrorString(e));
   return Q35_OK;
 }
 
+// Sets the cluster kernels' attributes once; 16-CTA clusters (non-portable) are used when the
+// device can keep one resident, else 8.
+bool cluster16_ok() {
+  static int ok = -1;
+  if (ok < 0) {
+    cudaFuncSetAttribute(attn_decode_cluster_kernel<4, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)cl_smem_bytes<8>());
+    cudaFuncSetAttribute(attn_decode_cluster_kernel<4, 16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)cl_smem_bytes<16>());
+    ok = 0;
+    if (cudaFuncSetAttribute(attn_decode_cluster_kernel<4, 16>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) ==
+        cudaSuccess) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(16, 1, 1);
+      cfg.blockDim = dim3(kThreads);
+      cfg.dynamicSmemBytes = cl_smem_bytes<16>();
+      cudaLaunchAttribute a;
+      a.id = cudaLaunchAttributeClusterDimension;
+      a.val.clusterDim.x = 16;
+      a.val.clusterDim.y = 1;
+      a.val.clusterDim.z = 1;
+      cfg.attrs = &a;
+      cfg.numAttrs = 1;
+      int n = 0;
+      if (cudaOccupancyMaxActiveClusters(&n, attn_decode_cluster_kernel<4, 16>, &cfg) == cudaSuccess && n > 0) ok = 1;
+    }
+    cudaGetLastError();  // a refused query leaves no sticky error
+  }
+  return ok == 1;
+}
+
 template <bool FUSED>
 int launch_decode(DecodeParams p, int64_t batch, int G, void* ws, cudaStream_t st, bool pdl) {
-  if (FUSED && G == 4 && p.max_len <= kClusterCTAs * kClRows) return launch_cluster<4>(p, batch, st, pdl);
+  if (FUSED && G == 4 && p.max_len <= kClMaxRows)
+    return cluster16_ok() ? launch_cluster<4, 16>(p, batch, st, pdl) : launch_cluster<4, 8>(p, batch, st, pdl);
   const WsLayout w = ws_layout(batch, p.Hq, p.Hkv, p.max_len);
   if ((size_t)batch * p.Hkv * sizeof(unsigned) > w.ml) return q35_fail(Q35_ENOTSUP, "decode attention: batch too large");
   char* base = static_cast<char*>(ws);
