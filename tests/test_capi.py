@@ -48,6 +48,32 @@ def test_invalid_arguments_are_rejected_on_host():
     assert lib.q35_gemv(C.byref(d), None) == L.Q35_EINVAL
 
 
+def test_vocab_shard_entry_points_validate_on_host():
+    lib = L.load()
+    ws = lib.q35_lm_shard_workspace_size()
+    assert ws >= 8 * 8 + 4
+    args = dict(hidden=16, batch=2, norm=None, weight=16, row0=0, rows=100, vocab=248320, k=2048, eps=1e-6,
+                keys=16, ws=16, ws_bytes=ws, stream=None)
+
+    def call(**kw):
+        a = {**args, **kw}
+        return lib.q35_lm_head_shard_keys(a["hidden"], a["batch"], a["norm"], a["weight"], a["row0"], a["rows"],
+                                          a["vocab"], a["k"], a["eps"], a["keys"], a["ws"], a["ws_bytes"], a["stream"])
+
+    assert call(hidden=None) == L.Q35_EINVAL
+    assert call(batch=0) == L.Q35_EINVAL and call(batch=9) == L.Q35_EINVAL
+    assert "batch" in L.last_error()
+    assert call(k=1024) == L.Q35_EINVAL and "hidden size" in L.last_error()
+    assert call(row0=248300, rows=100) == L.Q35_EINVAL and "outside the vocabulary" in L.last_error()
+    assert call(ws_bytes=ws - 1) == L.Q35_EINVAL and "workspace" in L.last_error()
+    assert call(hidden=18) == L.Q35_EINVAL and "alignment" in L.last_error()
+    assert lib.q35_lm_keys_to_tokens(None, 1, 16, None) == L.Q35_EINVAL
+    assert lib.q35_lm_keys_to_tokens(16, 0, 16, None) == L.Q35_EINVAL
+    assert lib.q35_decoder_decode_layers(None, None) == L.Q35_EINVAL
+    assert lib.q35_decoder_finish_step(None, 16, 0, None) == L.Q35_EINVAL
+    assert lib.q35_decoder_hidden(None) is None
+
+
 def test_workspace_size_queries():
     lib = L.load()
     assert lib.q35_lm_head_workspace_size(1) >= 12
