@@ -320,7 +320,7 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(DecodeParams p) {
 
 // ---------------------------------------------------------------------------------------------
 // Cluster variant of the fused decode mixer (decoder path, caches up to kClMaxRows rows):
-// one cluster of kClusterCTAs CTAs per (batch, KV head). Each CTA owns a contiguous slice of the
+// one cluster of CL (16, else 8) CTAs per (batch, KV head). Each CTA owns a contiguous slice of the
 // cached rows and copies its K/V rows into shared memory with cp.async BEFORE the programmatic-
 // dependent-launch wait: those rows and the row count were written by earlier steps (the kernel
 // before this one is the QGKV projection), so the HBM latency overlaps the projection. After the
@@ -329,7 +329,7 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(DecodeParams p) {
 // partials meet over distributed shared memory: CTA r merges dims [r * D / C, (r + 1) * D / C)
 // of every head from all peers and writes the gated BF16 output. No global scratch, no second
 // pass.
-constexpr int kClMaxRows = 1280;  // cached rows the cluster variant covers (8 CTAs x 160 rows)
+constexpr int kClMaxRows = 1280;  // cached rows the cluster variant covers (16 x 80 or 8 x 160 per CTA)
 template <int CL>
 constexpr int cl_rows() {
   return kClMaxRows / CL;
