@@ -118,3 +118,8 @@ def test_reduce_keys_single_process_and_dtype_guard():
     assert VS.reduce_keys(k) is k and k.tolist() == [5, -3]
     with pytest.raises(ValueError):
         VS.reduce_keys(torch.zeros(2, dtype=torch.int32))
+
+
+def test_sharded_decode_needs_a_process_group():
+    with pytest.raises(RuntimeError):
+        VS.ShardedDecode(object())
