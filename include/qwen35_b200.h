@@ -149,13 +149,19 @@ int q35_lm_keys_to_tokens(const int64_t* keys, int64_t n, int64_t* tokens_out, v
 
 /* ---------------------------------------------------------------- A8W8 */
 
-/* explore_runtime_quantization.py:143-155 (weights) and :167-172 (activations): per-row
+/* Weight side, explore_runtime_quantization.py:143-155 (PPUA8W8Linear.__init__): per-row
  * symmetric int8, scale = amax|x| / 127 (1 for an all-zero row), q = clamp(rne(x / s), +-127). */
 int q35_quantize_rows(const void* x, int8_t* q, float* scale, int64_t rows, int64_t width,
                       void* stream);
 
+/* Activation side, explore_runtime_quantization.py:167-172 (vllm scaled_int8_quant(x, scale=None,
+ * azp=None, symmetric=True), dynamic per token): scale = amax|x| / 127 (0 for an all-zero row),
+ * q = saturate_int8(rne(x * (127 / amax))) (0 for an all-zero row). */
+int q35_quantize_tokens(const void* x, int8_t* q, float* scale, int64_t rows, int64_t width,
+                        void* stream);
+
 /* explore_runtime_quantization.py:161-181 (PPUA8W8Linear.forward with acext int8_gemm):
- * out = bf16((float(qx @ qw^T) * s_x) * s_w), qx/s_x from q35_quantize_rows(x).
+ * out = bf16((float(qx @ qw^T) * s_x) * s_w), qx/s_x from q35_quantize_tokens(x).
  * Workspace: q35_a8w8_linear_workspace_size(m, k) bytes. */
 size_t q35_a8w8_linear_workspace_size(int64_t m, int64_t k);
 int q35_a8w8_linear(const void* x, const int8_t* qw, const float* w_scale, void* out, int64_t m,
@@ -182,7 +188,7 @@ int q35_gemm_tc(const void* a, const void* w, void* out, int64_t m, int64_t n, i
 
 /* A8W8 prefill projection on tcgen05 (kind::i8, exact int32 accumulation in TMEM) with the
  * dequantisation bf16((float(acc) * sx[m]) * sw[n]) and the epilogue fused (k multiple of 128).
- * qa/sx come from q35_quantize_rows (explore_runtime_quantization.py:161-181). */
+ * qa/sx come from q35_quantize_tokens (explore_runtime_quantization.py:161-181). */
 int q35_gemm_tc_a8w8(const int8_t* qa, const float* sx, const int8_t* qw, const float* sw, void* out,
                      int64_t m, int64_t n, int64_t k, int32_t epilogue, void* stream);
 
@@ -217,8 +223,9 @@ int q35_gqa_decode_attention(const void* q, const void* cache_k, const void* cac
  * cannot allocate device memory when they call in (a locked or pool-only allocator, a thread that
  * must not touch the CUDA allocator, a runtime that passes only inputs and outputs): the scratch
  * lives in a static device array of q35_gqa_decode_noalloc_max_bytes() bytes (2 MiB) that every
- * GPU loading this library keeps until exit. Shapes whose scratch exceeds it are rejected with
- * Q35_EINVAL. The first call on a device looks up the array's device address (make it before any
+ * GPU loading this library keeps until exit. Shapes whose scratch exceeds it, or with more than
+ * 64 (batch x kv_heads) split tickets, are rejected with Q35_EINVAL before anything is queued on
+ * the stream. The first call on a device looks up the array's device address (make it before any
  * stream capture); every call clears the ticket words and shares the array, so calls that overlap
  * on the GPU (other streams, other threads) race with each other. Calls no allocator. */
 size_t q35_gqa_decode_noalloc_max_bytes(void);
@@ -379,6 +386,13 @@ int q35_decoder_has_persistent(const q35_decoder* dec);
  * q35_decoder_trace_ops() (0 without a persistent step). */
 int q35_decoder_set_trace(q35_decoder* dec, int64_t* trace, int64_t entries);
 int q35_decoder_trace_ops(const q35_decoder* dec);
+/* A8W8 parity probe (no counterpart in the reference: a diagnostic). With a device buffer set,
+ * every A8W8 prefill projection appends its input's per-token int8 codes [length x k] and FP32
+ * scales [length] to the buffer, in call order (per layer: in-projection, out-projection, gate/up,
+ * down), as far as the buffer holds; q35_decoder_probe_bytes() gives the bytes the last prefill
+ * needed. NULL / 0 turns it off. */
+int q35_decoder_set_probe(q35_decoder* dec, void* buf, size_t bytes);
+size_t q35_decoder_probe_bytes(const q35_decoder* dec);
 /* Non-zero when a bounded wait of the persistent step gave up (1 grid barrier, 2 ring slot,
  * 3 ring data); reading clears it. */
 int q35_decoder_persistent_error(void);

@@ -7,12 +7,12 @@ Reference: explore_runtime_quantization.py:129-181 (``PPUA8W8Linear``).
 * Weights (:143-155): per output channel ``s_w = amax|W| / 127`` in FP32 (``1`` where the
   row is all zero), ``q_w = clamp(round(W / s_w), -127, 127)`` as int8.
 * Activations (:167-172): dynamic symmetric per-token quantisation through vllm
-  ``scaled_int8_quant(x, scale=None, azp=None, symmetric=True)``. vllm (0.22.0 in this
-  image, compiled) is a third-party dependency whose rounding order the reference does not
-  pin, so this restatement defines it with the weight-side formula per token row:
-  ``s_x = amax|x| / 127`` (``1`` for an all-zero row), ``q_x = clamp(rne(x / s_x), -127, 127)``.
-  Parity of the activation side against vllm is therefore "unpinned"; the CUDA path is
-  checked bit-exactly against this definition.
+  ``scaled_int8_quant(x, scale=None, azp=None, symmetric=True)`` (vllm 0.22.0 in this image;
+  a compiled op). Restated from vllm's published per-token kernel: ``s_x = amax|x| / 127``
+  (``0`` for an all-zero row) and ``q_x = sat_int8(rne(x * (127 / amax)))`` (``0`` for an
+  all-zero row) -- a multiplication by the reciprocal, which rounds differently from the
+  weight side's division at exact half-way values. A GPU test runs vllm's own op on the same
+  rows and compares codes and scales bit for bit.
 * Product (:173-180, acext ``int8_gemm``): exact int32 accumulation of int8 products,
   dequantised as ``bf16((float(acc) * s_x) * s_w)``.
 """
@@ -30,6 +30,18 @@ def quantize_rows(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
     absmax = x32.abs().amax(dim=-1, keepdim=True)
     scale = torch.where(absmax > 0, absmax / 127.0, torch.ones_like(absmax))
     q = torch.round(x32 / scale).clamp_(-127, 127).to(torch.int8)
+    return q, scale
+
+
+def quantize_tokens(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Per-token activation quantisation with vllm ``scaled_int8_quant`` semantics; returns
+    ``(q int8 [.., K], scale fp32 [.., 1])``. Every step is one IEEE float32 operation, as on the
+    GPU: ``amax / 127``, ``127 / amax``, ``x * inv``, round half to even, saturate."""
+    x32 = x.float()
+    absmax = x32.abs().amax(dim=-1, keepdim=True)
+    scale = absmax / 127.0
+    inv = torch.where(absmax > 0, torch.full_like(absmax, 127.0) / absmax, torch.zeros_like(absmax))
+    q = torch.round(x32 * inv).clamp_(-128, 127).to(torch.int8)
     return q, scale
 
 
@@ -52,5 +64,5 @@ def dequantize(acc: torch.Tensor, sx: torch.Tensor, sw: torch.Tensor) -> torch.T
 
 def a8w8_linear(x: torch.Tensor, qw: torch.Tensor, sw: torch.Tensor) -> torch.Tensor:
     """Dynamic-per-token A8W8 linear, explore_runtime_quantization.py:161-181."""
-    qx, sx = quantize_rows(x)
+    qx, sx = quantize_tokens(x)
     return dequantize(int8_matmul_exact(qx, qw), sx, sw)

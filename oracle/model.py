@@ -41,6 +41,7 @@ class OracleDecoder:
         self.a8w8 = a8w8
         self.chunked_prefill = chunked_prefill
         self.max_cache_len = max_cache_len
+        self.probe: list | None = None  # set to a list to record A8W8 input codes (diagnostics)
         self.inv_freq = ops.rope_inv_freq(dims.rotary_dim, dims.rope_theta)
         self.layers = []
         for i, kind in enumerate(dims.layer_types):
@@ -79,9 +80,10 @@ class OracleDecoder:
             return ("q8",) + q8.quantize_weight(w)
         return ("bf16", w)
 
-    @staticmethod
-    def _apply(lin, x):
+    def _apply(self, lin, x):
         if lin[0] == "q8":
+            if self.probe is not None:  # per-token codes and scales of this A8W8 input
+                self.probe.append(q8.quantize_tokens(x.reshape(-1, x.shape[-1])))
             return q8.a8w8_linear(x, lin[1], lin[2])
         return ops.linear(x, lin[1])
 

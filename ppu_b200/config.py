@@ -129,4 +129,8 @@ class FusionConfig:
     vision_graph: bool = False
     vision_graph_max_entries: int = 48
     a8w8: bool = False
+    # The reference's patched forwards hand inputs that are not BF16 CUDA tensors (and padded
+    # batches, which need a 4D mask) back to the Transformers implementation. Off by default
+    # here: such inputs raise ValueError, so nothing silently leaves the B200 kernels.
+    eager_fallback: bool = False
     extra: dict = field(default_factory=dict, compare=False, hash=False)

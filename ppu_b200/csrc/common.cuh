@@ -5,6 +5,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+#include <mutex>
 #include <utility>
 
 #include "qwen35_b200.h"
@@ -142,10 +144,25 @@ Q35_DEV int dot_i8x16(const uint4& a, const uint4& b, int acc) {
   return acc;
 }
 
-// Symmetric int8 quantisation of one value given its row scale: clamp(rne(x / s), -127, 127).
+// Weight side (explore_runtime_quantization.py:143-155, a torch formula): per output row
+// s = amax / 127 (1 for an all-zero row), code = clamp(rne(x / s), -127, 127).
 Q35_DEV int quant_i8(float x, float s) {
   int q = __float2int_rn(__fdiv_rn(x, s));
   return max(-127, min(127, q));
+}
+
+// Activation side: dynamic per-token symmetric quantisation with the semantics of vllm's
+// scaled_int8_quant(x, scale=None, azp=None, symmetric=True), which the reference calls at
+// explore_runtime_quantization.py:167-172. The stored scale is amax / 127 (0 for an all-zero
+// row); each code is x times the reciprocal 127 / amax (0 for an all-zero row), rounded to
+// nearest even and saturated to [-128, 127]. Multiplying by the reciprocal is not the same as
+// dividing by the scale: at exact half-way products (x = amax / 2, or amax with mantissa 127)
+// the two round differently, so the two sides keep their own formulas.
+Q35_DEV float tok_scale(float amax) { return __fdiv_rn(amax, 127.0f); }
+Q35_DEV float tok_inv(float amax) { return amax > 0.f ? __fdiv_rn(127.0f, amax) : 0.f; }
+Q35_DEV int quant_i8_tok(float x, float inv) {
+  const int q = __float2int_rn(__fmul_rn(x, inv));
+  return max(-128, min(127, q));
 }
 
 // Programmatic dependent launch: wait for the producer grid's writes / let the consumer start.
@@ -240,3 +257,35 @@ static inline cudaError_t q35_launch(void (*kernel)(KArgs...), dim3 grid, dim3 b
   cfg.numAttrs = pdl ? 1 : 0;
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
+
+// Host-side set-up that belongs to one device's context: kernel attributes (dynamic shared
+// memory, carve-out, non-portable cluster sizes) and occupancy answers are per device, so a
+// process that drives several GPUs must set and cache them per device ordinal. `get` runs `init`
+// once per device (the first caller on that device, under a mutex; `init` runs with that device
+// current) and afterwards returns the cached value with one acquire load.
+constexpr int kQ35MaxDevices = 64;
+
+template <class T>
+class Q35PerDevice {
+ public:
+  template <class F>
+  T get(F&& init) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kQ35MaxDevices) {
+      cudaGetLastError();
+      return init();  // no cacheable ordinal: set up on every call
+    }
+    if (ready_[dev].load(std::memory_order_acquire)) return val_[dev];
+    std::lock_guard<std::mutex> lock(mu_);
+    if (!ready_[dev].load(std::memory_order_relaxed)) {
+      val_[dev] = init();
+      ready_[dev].store(true, std::memory_order_release);
+    }
+    return val_[dev];
+  }
+
+ private:
+  std::mutex mu_;
+  T val_[kQ35MaxDevices] = {};
+  std::atomic<bool> ready_[kQ35MaxDevices] = {};
+};

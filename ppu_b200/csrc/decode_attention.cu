@@ -579,13 +579,13 @@ int launch_cluster(const DecodeParams& p, int64_t batch, cudaStream_t st, bool p
 // Sets the cluster kernels' attributes once; 16-CTA clusters (non-portable) are used when the
 // device can keep one resident, else 8.
 bool cluster16_ok() {
-  static int ok = -1;
-  if (ok < 0) {
+  static Q35PerDevice<int> ok;
+  return ok.get([] {
     cudaFuncSetAttribute(attn_decode_cluster_kernel<4, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)cl_smem_bytes<8>());
     cudaFuncSetAttribute(attn_decode_cluster_kernel<4, 16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)cl_smem_bytes<16>());
-    ok = 0;
+    int fits = 0;
     if (cudaFuncSetAttribute(attn_decode_cluster_kernel<4, 16>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) ==
         cudaSuccess) {
       cudaLaunchConfig_t cfg = {};
@@ -600,11 +600,11 @@ bool cluster16_ok() {
       cfg.attrs = &a;
       cfg.numAttrs = 1;
       int n = 0;
-      if (cudaOccupancyMaxActiveClusters(&n, attn_decode_cluster_kernel<4, 16>, &cfg) == cudaSuccess && n > 0) ok = 1;
+      if (cudaOccupancyMaxActiveClusters(&n, attn_decode_cluster_kernel<4, 16>, &cfg) == cudaSuccess && n > 0) fits = 1;
     }
     cudaGetLastError();  // a refused query leaves no sticky error
-  }
-  return ok == 1;
+    return fits;
+  }) == 1;
 }
 
 template <bool FUSED>
@@ -618,8 +618,8 @@ int launch_decode(DecodeParams p, int64_t batch, int G, void* ws, cudaStream_t s
   p.part_ml = reinterpret_cast<float*>(base + w.ml);
   p.part = reinterpret_cast<float*>(base + w.part);
   dim3 grid(p.S, p.Hkv, (unsigned)batch);
-  static bool attr = false;
-  if (!attr) {  // two CTAs per SM: the full shared-memory carve-out
+  static Q35PerDevice<bool> attr;
+  attr.get([] {  // two CTAs per SM: the full shared-memory carve-out
     auto set = [](auto kern) {
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kAttnDynSmem);
       cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, (int)cudaSharedmemCarveoutMaxShared);
@@ -627,8 +627,8 @@ int launch_decode(DecodeParams p, int64_t batch, int G, void* ws, cudaStream_t s
     set(attn_decode_kernel<1, FUSED>);
     set(attn_decode_kernel<2, FUSED>);
     set(attn_decode_kernel<4, FUSED>);
-    attr = true;
-  }
+    return true;
+  });
   cudaError_t e;
   switch (G) {
     case 1: e = q35_launch(attn_decode_kernel<1, FUSED>, grid, dim3(kThreads), kAttnDynSmem, st, pdl, p); break;
@@ -758,6 +758,9 @@ extern "C" int q35_gqa_decode_attention_noalloc(const void* q, const void* cache
               "gqa_decode_attention_noalloc: this shape needs %zu bytes of scratch, more than the %zu-byte "
               "static maximum (use q35_gqa_decode_attention with a workspace)",
               w.total, kQ35NoAllocScratchBytes);
+  Q35_REQUIRE((size_t)batch * kv_heads * sizeof(unsigned) <= w.ml,
+              "gqa_decode_attention_noalloc: batch x kv_heads = %lld exceeds the %zu ticket words of the scratch",
+              (long long)(batch * kv_heads), w.ml / sizeof(unsigned));
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
     return q35_fail(Q35_ECUDA, "gqa_decode_attention_noalloc: no current device");

@@ -35,7 +35,8 @@ int q35_gemm_launch(const void* a, const void* w, void* out, int64_t m, int64_t 
                     const float* sx, const float* sw, cudaStream_t s);
 int q35_gemm_tc_launch(const void* a, const void* w, void* out, int64_t m, int64_t n, int64_t k, int epi, bool int8,
                        const float* sx, const float* sw, cudaStream_t s);
-int q35_quantize_rows_launch(const void* x, int8_t* q, float* scale, int64_t rows, int64_t width, cudaStream_t s);
+int q35_quantize_tokens_launch(const void* x, int8_t* q, float* scale, int64_t rows, int64_t width,
+                               cudaStream_t s);
 int q35_qgkv_rope_positions_launch(const void* packed, const void* q_weight, const void* k_weight,
                                    const float* inv_freq, void* q_out, void* k_out, void* v_out,
                                    const int64_t* cache_start, int64_t batch, int64_t seq_len, int64_t q_heads,
@@ -141,7 +142,20 @@ struct q35_decoder {
   Buffers buf;
   q35_pk_plan* pk = nullptr;  // persistent decode step, when the model fits its built-in shapes
   std::string pk_why;         // otherwise the reason
+  char* probe = nullptr;      // A8W8 prefill probe: int8 codes + scales of every projection input
+  size_t probe_bytes = 0;
+  size_t probe_want = 0;      // bytes the last prefill had to record
 };
+
+extern "C" int q35_decoder_set_probe(q35_decoder* dec, void* buf, size_t bytes) {
+  Q35_REQUIRE(dec, "set_probe: null decoder");
+  Q35_REQUIRE(buf || bytes == 0, "set_probe: null buffer with a size");
+  dec->probe = static_cast<char*>(buf);
+  dec->probe_bytes = bytes;
+  return Q35_OK;
+}
+
+extern "C" size_t q35_decoder_probe_bytes(const q35_decoder* dec) { return dec ? dec->probe_want : 0; }
 
 extern "C" size_t q35_decoder_workspace_size(const q35_decoder_desc* desc) {
   if (!desc) return 0;
@@ -339,6 +353,7 @@ extern "C" int q35_decoder_prefill(q35_decoder* dec, const int64_t* ids, int64_t
   const int64_t conv_dim = (int64_t)d.lin_heads * (2 * d.lin_dk + d.lin_dv);
   const int64_t vdim = (int64_t)d.lin_heads * d.lin_dv;
   const int64_t adim = (int64_t)d.q_heads * d.head_dim;
+  dec->probe_want = 0;
 
   // Projection helper: bf16 GEMM, or per-token int8 quantisation + int8 GEMM for A8W8; tcgen05
   // tiles when enabled (K must fill the 128-byte slabs), warp-level MMA otherwise.
@@ -347,8 +362,17 @@ extern "C" int q35_decoder_prefill(q35_decoder* dec, const int64_t* ids, int64_t
     if (!q8)
       return tc ? q35_gemm_tc_launch(x, w, out, Lt, n, k, epi, false, nullptr, nullptr, s)
                 : q35_gemm_launch(x, w, out, Lt, n, k, epi, false, nullptr, nullptr, s);
-    int rc = q35_quantize_rows_launch(x, B.p_q8, B.p_sx, Lt, k, s);
+    int rc = q35_quantize_tokens_launch(x, B.p_q8, B.p_sx, Lt, k, s);
     if (rc) return rc;
+    if (dec->probe) {  // record [codes Lt x k][scales Lt] of this projection's input
+      const size_t codes = (size_t)Lt * k, need = codes + (size_t)Lt * sizeof(float);
+      if (dec->probe_want + need <= dec->probe_bytes &&
+          (cudaMemcpyAsync(dec->probe + dec->probe_want, B.p_q8, codes, cudaMemcpyDeviceToDevice, s) != cudaSuccess ||
+           cudaMemcpyAsync(dec->probe + dec->probe_want + codes, B.p_sx, (size_t)Lt * sizeof(float),
+                           cudaMemcpyDeviceToDevice, s) != cudaSuccess))
+        return q35_fail(Q35_ECUDA, "prefill: probe copy failed");
+      dec->probe_want += need;
+    }
     return tc ? q35_gemm_tc_launch(B.p_q8, w, out, Lt, n, k, epi, true, B.p_sx, sw, s)
               : q35_gemm_launch(B.p_q8, w, out, Lt, n, k, epi, true, B.p_sx, sw, s);
   };

@@ -644,12 +644,12 @@ int q35_delta_chunked_launch(const void* qkv, const void* packed, const void* a_
   Q35_REQUIRE(conv_weight == nullptr || (conv_state != nullptr && seq_len >= 4),
               "delta_chunked: the fused conv needs a state and at least 4 tokens");
   const int nc = (int)((seq_len + kC - 1) / kC);
-  static bool attr = false;
-  if (!attr) {
+  static Q35PerDevice<bool> attr;
+  attr.get([] {
     cudaFuncSetAttribute(delta_chunk_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPrepSmem);
     cudaFuncSetAttribute(delta_chunk_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kScanSmem);
-    attr = true;
-  }
+    return true;
+  });
   PrepParams pp{(const bf16*)qkv,         (const bf16*)packed,    (const bf16*)a_log, (const bf16*)dt_bias,
                 (const bf16*)conv_weight, (bf16*)conv_state,      ws,                  (int)seq_len,
                 (int)heads,               nc,                     (int)packed_stride};

@@ -232,7 +232,15 @@ __global__ void __launch_bounds__(kGemmThreads) gemm_kernel(GemmParams p) {
   }
 }
 
-// Per-row symmetric int8 quantisation (explore_runtime_quantization.py:143-155, 167-172).
+// Per-row symmetric int8 quantisation. TOK = false: the weight-side formula
+// (explore_runtime_quantization.py:143-155); TOK = true: per-token activations with vllm
+// scaled_int8_quant semantics (:167-172). See quant_i8 / quant_i8_tok.
+template <bool TOK>
+Q35_DEV int quant_code(float x, float s, float inv) {
+  return TOK ? quant_i8_tok(x, inv) : quant_i8(x, s);
+}
+
+template <bool TOK>
 __global__ void __launch_bounds__(256) quant_rows_kernel(const bf16* __restrict__ x, int8_t* __restrict__ q,
                                                          float* __restrict__ scale, int width) {
   __shared__ float red[8];
@@ -241,13 +249,15 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(const bf16* __restrict_
   float amax = 0.f;
   for (int c = threadIdx.x; c < width; c += 256) amax = fmaxf(amax, fabsf(bf2f(xr[c])));
   amax = block_max<8>(amax, red);
-  const float s = amax > 0.f ? amax / 127.0f : 1.0f;
-  for (int c = threadIdx.x; c < width; c += 256) q[row * width + c] = (int8_t)quant_i8(bf2f(xr[c]), s);
+  const float s = TOK ? tok_scale(amax) : (amax > 0.f ? amax / 127.0f : 1.0f);
+  const float inv = tok_inv(amax);
+  for (int c = threadIdx.x; c < width; c += 256) q[row * width + c] = (int8_t)quant_code<TOK>(bf2f(xr[c]), s, inv);
   if (threadIdx.x == 0) scale[row] = s;
 }
 
 // Width % 8 == 0, 16-byte aligned input and 8-byte aligned output: 16-byte loads, 8-byte int8
 // stores; the second pass re-reads the row (4-12 KB, still in L1) instead of holding it.
+template <bool TOK>
 __global__ void __launch_bounds__(256) quant_rows_v8_kernel(const bf16* __restrict__ x, int8_t* __restrict__ q,
                                                             float* __restrict__ scale, int width) {
   __shared__ float red[8];
@@ -262,15 +272,16 @@ __global__ void __launch_bounds__(256) quant_rows_v8_kernel(const bf16* __restri
     for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(f[j]));
   }
   amax = block_max<8>(amax, red);
-  const float s = amax > 0.f ? amax / 127.0f : 1.0f;
+  const float s = TOK ? tok_scale(amax) : (amax > 0.f ? amax / 127.0f : 1.0f);
+  const float inv = tok_inv(amax);
   for (int c = threadIdx.x; c < n8; c += 256) {
     float f[8];
     unpack_bf16x8(xr[c], f);
     uint32_t lo = 0, hi = 0;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      lo |= (uint32_t)(quant_i8(f[j], s) & 0xff) << (8 * j);
-      hi |= (uint32_t)(quant_i8(f[4 + j], s) & 0xff) << (8 * j);
+      lo |= (uint32_t)(quant_code<TOK>(f[j], s, inv) & 0xff) << (8 * j);
+      hi |= (uint32_t)(quant_code<TOK>(f[4 + j], s, inv) & 0xff) << (8 * j);
     }
     reinterpret_cast<uint2*>(q + row * width)[c] = make_uint2(lo, hi);
   }
@@ -326,13 +337,23 @@ int q35_gemm_launch(const void* a, const void* w, void* out, int64_t m, int64_t 
   return int8 ? dispatch_gemm<true>(p, epi, s) : dispatch_gemm<false>(p, epi, s);
 }
 
-int q35_quantize_rows_launch(const void* x, int8_t* q, float* scale, int64_t rows, int64_t width, cudaStream_t s) {
+template <bool TOK>
+int quantize_launch(const void* x, int8_t* q, float* scale, int64_t rows, int64_t width, cudaStream_t s) {
   if (rows == 0) return Q35_OK;
   if (width % 8 == 0 && Q35_ALIGNED(x, 16) && Q35_ALIGNED(q, 8))
-    quant_rows_v8_kernel<<<(unsigned)rows, 256, 0, s>>>((const bf16*)x, q, scale, (int)width);
+    quant_rows_v8_kernel<TOK><<<(unsigned)rows, 256, 0, s>>>((const bf16*)x, q, scale, (int)width);
   else
-    quant_rows_kernel<<<(unsigned)rows, 256, 0, s>>>((const bf16*)x, q, scale, (int)width);
-  return q35_check_launch("quantize_rows");
+    quant_rows_kernel<TOK><<<(unsigned)rows, 256, 0, s>>>((const bf16*)x, q, scale, (int)width);
+  return q35_check_launch(TOK ? "quantize_tokens" : "quantize_rows");
+}
+
+int q35_quantize_rows_launch(const void* x, int8_t* q, float* scale, int64_t rows, int64_t width, cudaStream_t s) {
+  return quantize_launch<false>(x, q, scale, rows, width, s);
+}
+
+int q35_quantize_tokens_launch(const void* x, int8_t* q, float* scale, int64_t rows, int64_t width,
+                               cudaStream_t s) {
+  return quantize_launch<true>(x, q, scale, rows, width, s);
 }
 
 extern "C" int q35_gemm_bf16(const void* a, const void* w, void* out, int64_t m, int64_t n, int64_t k,
@@ -347,6 +368,12 @@ extern "C" int q35_quantize_rows(const void* x, int8_t* q, float* scale, int64_t
   return q35_quantize_rows_launch(x, q, scale, rows, width, (cudaStream_t)stream);
 }
 
+extern "C" int q35_quantize_tokens(const void* x, int8_t* q, float* scale, int64_t rows, int64_t width,
+                                   void* stream) {
+  Q35_REQUIRE(x && q && scale && rows >= 0 && width > 0, "quantize_tokens: bad argument");
+  return q35_quantize_tokens_launch(x, q, scale, rows, width, (cudaStream_t)stream);
+}
+
 extern "C" size_t q35_a8w8_linear_workspace_size(int64_t m, int64_t k) {
   return (((size_t)m * k + 255) & ~(size_t)255) + (size_t)m * sizeof(float);
 }
@@ -358,7 +385,7 @@ extern "C" int q35_a8w8_linear(const void* x, const int8_t* qw, const float* w_s
   Q35_REQUIRE(workspace_bytes >= q35_a8w8_linear_workspace_size(m, k), "a8w8_linear: workspace too small");
   int8_t* qx = static_cast<int8_t*>(workspace);
   float* sx = reinterpret_cast<float*>(static_cast<char*>(workspace) + (((size_t)m * k + 255) & ~(size_t)255));
-  int rc = q35_quantize_rows_launch(x, qx, sx, m, k, (cudaStream_t)stream);
+  int rc = q35_quantize_tokens_launch(x, qx, sx, m, k, (cudaStream_t)stream);
   if (rc) return rc;
   return q35_gemm_launch(qx, qw, out, m, n, k, Q35_EPI_STORE, true, sx, w_scale, (cudaStream_t)stream);
 }

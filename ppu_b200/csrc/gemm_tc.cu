@@ -574,8 +574,8 @@ int g_tc_pairs = 1;  // process-wide: CTA-pair kernel (1) or single-CTA kernel (
 
 template <bool INT8, int EPI>
 int max_active_pairs() {
-  static int max_pairs = 0;  // pairs resident at once (clusters of 2 need both SMs in one GPC)
-  if (max_pairs == 0) {
+  static Q35PerDevice<int> max_pairs;  // pairs resident at once (clusters of 2 need both SMs in one GPC)
+  return max_pairs.get([] {
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr;
     attr.id = cudaLaunchAttributeClusterDimension;
@@ -594,9 +594,8 @@ int max_active_pairs() {
       cudaGetLastError();
       n = kNumSMs / 2;
     }
-    max_pairs = n < kNumSMs / 2 ? n : kNumSMs / 2;
-  }
-  return max_pairs;
+    return n < kNumSMs / 2 ? n : kNumSMs / 2;
+  });
 }
 
 // Pair tiles are 256 x 256 (an N = 128 MMA runs at about half the rate of N = 256 on either kernel).

@@ -82,9 +82,9 @@ Q35_DEV void build_input(const GemvParams& p, int k, bf16* xs, int8_t* xq, float
     float amax = 0.f;
     for (int i = threadIdx.x; i < k; i += kThreads) amax = fmaxf(amax, fabsf(bf2f(xs[i])));
     amax = block_max<kWarps>(amax, red);
-    const float s = amax > 0.f ? amax / 127.0f : 1.0f;
-    for (int i = threadIdx.x; i < k; i += kThreads) xq[i] = (int8_t)quant_i8(bf2f(xs[i]), s);
-    if (threadIdx.x == 0) *sx_out = s;
+    const float inv = tok_inv(amax);
+    for (int i = threadIdx.x; i < k; i += kThreads) xq[i] = (int8_t)quant_i8_tok(bf2f(xs[i]), inv);
+    if (threadIdx.x == 0) *sx_out = tok_scale(amax);
   }
   __syncthreads();
 }
@@ -142,7 +142,7 @@ Q35_DEV void build_input_q8(const GemvParams& p, int8_t* xq, float* sx_out, floa
 #pragma unroll
     for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fabsf(f[j][e]));
   amax = block_max<kWarps>(amax, red);
-  const float s = amax > 0.f ? amax / 127.0f : 1.0f;
+  const float inv = tok_inv(amax);
 #pragma unroll
   for (int j = 0; j < CPT; ++j) {
     const int i = threadIdx.x + j * kThreads;
@@ -150,13 +150,13 @@ Q35_DEV void build_input_q8(const GemvParams& p, int8_t* xq, float* sx_out, floa
       uint32_t lo = 0, hi = 0;
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        lo |= (uint32_t)(quant_i8(f[j][e], s) & 0xff) << (8 * e);
-        hi |= (uint32_t)(quant_i8(f[j][4 + e], s) & 0xff) << (8 * e);
+        lo |= (uint32_t)(quant_i8_tok(f[j][e], inv) & 0xff) << (8 * e);
+        hi |= (uint32_t)(quant_i8_tok(f[j][4 + e], inv) & 0xff) << (8 * e);
       }
       reinterpret_cast<uint2*>(xq)[i] = make_uint2(lo, hi);
     }
   }
-  if (threadIdx.x == 0) *sx_out = s;
+  if (threadIdx.x == 0) *sx_out = tok_scale(amax);
   __syncthreads();
 }
 
@@ -850,8 +850,8 @@ int g_gemv_ctas_per_sm = 0;  // 0: as many as fit; else cap (room for the next k
 template <int K, int PRO, int EPI, bool INT8>
 int launch_fast(const GemvParams& p, cudaStream_t s, bool pdl) {
   using Sh = FastShape<K, INT8, (EPI == Q35_EPI_SWIGLU) ? 2 : 1>;
-  static int resident = 0;
-  if (!resident) resident = resident_ctas(gemv_fast_kernel<K, PRO, EPI, INT8>, 0);
+  static Q35PerDevice<int> resident_ctas_of;
+  const int resident = resident_ctas_of.get([] { return resident_ctas(gemv_fast_kernel<K, PRO, EPI, INT8>, 0); });
   const int max_ctas = g_gemv_ctas_per_sm > 0 && g_gemv_ctas_per_sm * kNumSMs < resident
                            ? g_gemv_ctas_per_sm * kNumSMs
                            : resident;
@@ -957,9 +957,9 @@ int q35_lm_head_launch(const void* hidden, const void* norm_weight, const void* 
   p.eps = eps;
   cudaError_t e;
   if (k == 2048) {
-    static int max_norm = 0, max_plain = 0;
-    if (!max_norm) max_norm = resident_ctas(lm_head_fast_kernel<2048, true>, 0);
-    if (!max_plain) max_plain = resident_ctas(lm_head_fast_kernel<2048, false>, 0);
+    static Q35PerDevice<int> resident_norm, resident_plain;
+    const int max_norm = resident_norm.get([] { return resident_ctas(lm_head_fast_kernel<2048, true>, 0); });
+    const int max_plain = resident_plain.get([] { return resident_ctas(lm_head_fast_kernel<2048, false>, 0); });
     const int ngroups = (int)((vocab + 1) / 2);  // two rows per warp iteration at K = 2048
     if (norm_weight)
       e = q35_launch(lm_head_fast_kernel<2048, true>, dim3(choose_grid(ngroups, max_norm)), dim3(kThreads), 0, s,
@@ -1041,11 +1041,11 @@ namespace {
 template <int NB, bool NORM>
 cudaError_t launch_lm_shard(const LmShardParams& p, cudaStream_t s, bool pdl) {
   constexpr size_t smem = lm_shard_smem<NB>();
-  static int resident = 0;
-  if (!resident) {
+  static Q35PerDevice<int> resident_of;
+  const int resident = resident_of.get([] {
     cudaFuncSetAttribute(lm_shard_kernel<NB, NORM>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    resident = resident_ctas(lm_shard_kernel<NB, NORM>, smem);
-  }
+    return resident_ctas(lm_shard_kernel<NB, NORM>, smem);
+  });
   constexpr int U = lm_shard_rows<NB>();
   const int ngroups = (p.rows + U - 1) / U;  // U rows per warp iteration
   return q35_launch(lm_shard_kernel<NB, NORM>, dim3(choose_grid(ngroups, resident)), dim3(kThreads), smem, s,

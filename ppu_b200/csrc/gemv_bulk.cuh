@@ -166,11 +166,11 @@ __global__ void __launch_bounds__(kThreads) gemv_bulk_kernel(GemvParams p) {
 template <int K, int PRO, int EPI, bool INT8>
 int launch_bulk(const GemvParams& p, cudaStream_t s, bool pdl) {
   const size_t smem = (size_t)kBulkStages * kBulkStageBytes;
-  static bool attr = false;
-  if (!attr) {
+  static Q35PerDevice<bool> attr;
+  attr.get([smem] {
     cudaFuncSetAttribute(gemv_bulk_kernel<K, PRO, EPI, INT8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    attr = true;
-  }
+    return true;
+  });
   int grid = kNumSMs;
   if (p.n_out < grid) grid = p.n_out;
   cudaError_t e = q35_launch(gemv_bulk_kernel<K, PRO, EPI, INT8>, dim3(grid), dim3(kThreads), smem, s, pdl, p);

@@ -277,6 +277,38 @@ class Qwen35Engine:
             prev = t[j, :, 1]
         return {"step_us": float(end.max() - start.min()), "ops": ops}
 
+    def prefill_probe(self, ids: torch.Tensor) -> list[tuple[torch.Tensor, torch.Tensor]]:
+        """A8W8 diagnostic: prefills ``ids`` like ``prefill`` and returns, per A8W8 projection in
+        call order (per layer: in-projection, out-projection, gate/up, down), the per-token int8
+        codes ``[L, k]`` and FP32 scales ``[L, 1]`` its input was quantised to."""
+        if not self.a8w8:
+            raise ValueError("prefill_probe needs an A8W8 engine")
+        n = ids.numel()
+        d = self.dims
+        ks = []
+        for kind in d.layer_types:
+            ks += [d.hidden, d.value_dim if kind == "linear_attention" else d.attn_width, d.hidden, d.intermediate]
+        total = sum(n * k + 4 * n for k in ks)
+        buf = torch.zeros(total, device=self.device, dtype=torch.uint8)
+        lib = L.load()
+        L.check(lib.q35_decoder_set_probe(self.handle, buf.data_ptr(), total), "q35_decoder_set_probe")
+        try:
+            self.prefill(ids)
+            torch.cuda.synchronize(self.device)
+        finally:
+            lib.q35_decoder_set_probe(self.handle, None, 0)
+        if lib.q35_decoder_probe_bytes(self.handle) != total:
+            raise RuntimeError("prefill probe: unexpected record size")
+        out, off = [], 0
+        host = buf.cpu()
+        for k in ks:
+            codes = host[off:off + n * k].view(torch.int8).reshape(n, k)
+            off += n * k
+            scale = host[off:off + 4 * n].view(torch.float32).reshape(n, 1)
+            off += 4 * n
+            out.append((codes, scale))
+        return out
+
     # ------------------------------------------------------------------ state
     def snapshot(self) -> dict:
         """Copies of every piece of mutable decoding state (for restoring after warm-up)."""

@@ -22,6 +22,7 @@ token read on the host; throughput is computed by callers as (tokens - 1) / (ela
 from __future__ import annotations
 
 import time
+import zlib
 from dataclasses import dataclass
 from typing import Any
 
@@ -202,16 +203,21 @@ class VLMModel:
                                       "fusion_stats": self._fusion_stats})
 
     def _generate_with_dummy(self, *, prompt, choices, generation_config, sample_id) -> GenerationResult:
-        start = time.perf_counter()
-        usable = [k for k, v in choices.items() if (v or "").strip()]
-        picked = usable[hash(sample_id) % len(usable)] if usable else "A"
-        text = f"Answer: {picked}\nExplanation: dummy backend selected a deterministic option for smoke testing."
-        token_count = max(1, min(generation_config.max_new_tokens, len(text.split())))
-        end = time.perf_counter()
-        return GenerationResult(text=text, token_count=token_count, ttft_seconds=max(end - start, 1e-4),
-                                elapsed_seconds=max(end - start, 2e-4),
+        """Model-free smoke backend: answers with one of the non-empty choices, chosen by a CRC-32
+        of the sample id (stable across processes), so a harness can be exercised without a GPU
+        or checkpoint. The token count is the answer's word count, capped by ``max_new_tokens``."""
+        t0 = time.perf_counter()
+        keys = sorted(k for k, v in choices.items() if str(v or "").strip())
+        key = keys[zlib.crc32(str(sample_id).encode("utf-8")) % len(keys)] if keys else "A"
+        text = f"Answer: {key}\nExplanation: placeholder from the model-free dummy backend."
+        words = len(text.split())
+        t1 = time.perf_counter()
+        # a result must satisfy 0 < ttft < elapsed for the throughput formula; clamp to 1 us / 2 us
+        ttft = max(t1 - t0, 1e-6)
+        return GenerationResult(text=text, token_count=max(1, min(int(generation_config.max_new_tokens), words)),
+                                ttft_seconds=ttft, elapsed_seconds=max(t1 - t0, 2 * ttft),
                                 meta={"backend": "dummy", "reason": getattr(self, "_dummy_reason", "n/a"),
-                                      "prompt_chars": len(str(prompt))})
+                                      "prompt_chars": len(str(prompt)), "choices": len(keys)})
 
 
 def compute_throughput(result: GenerationResult) -> float:

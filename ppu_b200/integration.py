@@ -7,8 +7,9 @@ installed Transformers (5.5) cache API. Same structure as the reference:
   registered as buffers; originals optionally released; A8W8 (``FusionConfig.a8w8``) also keeps
   int8 copies with per-row scales for the M/F/L groups;
 * patched forwards of the RMSNorm / gated RMSNorm modules, MLP, Gated DeltaNet, attention and the
-  text-model loop (integration.py:143-506), each falling back to the original forward when the
-  input is not a BF16 CUDA tensor;
+  text-model loop (integration.py:143-506). Inputs that are not BF16 CUDA tensors, and padded
+  batches, raise ``ValueError`` unless ``FusionConfig(eager_fallback=True)`` asks for the
+  reference's behaviour (the original Transformers forward for them);
 * every operator is a hand-written sm_100a kernel from ``ppu_b200.kernels`` (no F.linear / SDPA on
   the fast path).
 
@@ -131,42 +132,46 @@ def _proj(x: torch.Tensor, weight: torch.Tensor, q8: torch.Tensor | None = None,
     return out.reshape(*lead, out.shape[-1])
 
 
-def _patch_norm_module(module: torch.nn.Module) -> None:
+def _install(module: torch.nn.Module, fast, config: FusionConfig, primary: str) -> bool:
+    """Routes ``module.forward`` through ``fast(self, *args, **kwargs)``. The tensor named
+    ``primary`` (or the first positional argument) must be a BF16 CUDA tensor; otherwise the call
+    raises ``ValueError``, or, with ``config.eager_fallback``, runs the module's original
+    Transformers forward as the reference does (integration.py:51-52). Returns False when the
+    module was patched already."""
     if hasattr(module, "_fused_original_forward"):
-        return
+        return False
     module._fused_original_forward = module.forward
 
-    def forward(self, x):
-        if _is_fast_tensor(x) and x.is_contiguous():
-            return K.rms_norm(x, self.weight, self.eps)
-        return self._fused_original_forward(x)
+    def forward(self, *args, **kwargs):
+        x = args[0] if args else kwargs.get(primary)
+        if x is None and primary == "input_ids":
+            x = kwargs.get("inputs_embeds")
+        if isinstance(x, torch.Tensor) and (x.dtype == torch.long or _is_fast_tensor(x)):
+            if x.dtype != torch.long or x.is_cuda:
+                return fast(self, *args, **kwargs)
+        if config.eager_fallback:
+            return self._fused_original_forward(*args, **kwargs)
+        what = "None" if x is None else f"{tuple(x.shape)} {x.dtype} on {x.device}"
+        raise ValueError(f"{type(self).__name__}: the fused path takes BF16 CUDA tensors, got {what} "
+                         "(FusionConfig(eager_fallback=True) runs the Transformers forward instead)")
 
     module.forward = types.MethodType(forward, module)
+    return True
 
 
-def _patch_gated_norm_module(module: torch.nn.Module) -> None:
-    if hasattr(module, "_fused_original_forward"):
-        return
-    module._fused_original_forward = module.forward
+def _fused_rms_norm(self, x):
+    return K.rms_norm(x.contiguous(), self.weight, self.eps)
 
-    def forward(self, hidden_states, gate=None):
-        if gate is not None and _is_fast_tensor(hidden_states):
-            return K.gated_rms_norm(hidden_states.contiguous(), gate.contiguous(), self.weight,
-                                    self.variance_epsilon)
-        return self._fused_original_forward(hidden_states, gate)
 
-    module.forward = types.MethodType(forward, module)
+def _fused_gated_norm(self, hidden_states, gate=None):
+    if gate is None:  # the reference's gated module is always called with its gate
+        raise ValueError("gated RMSNorm: the fused path needs the gate tensor")
+    return K.gated_rms_norm(hidden_states.contiguous(), gate.contiguous(), self.weight, self.variance_epsilon)
 
 
 def _patch_mlp(module: torch.nn.Module, config: FusionConfig) -> None:
     """integration.py:169-188: decode SwiGLU GEMV, prefill GEMM with the SwiGLU epilogue."""
-    if hasattr(module, "_fused_original_forward"):
-        return
-    module._fused_original_forward = module.forward
-
     def forward(self, x):
-        if not _is_fast_tensor(x):
-            return self._fused_original_forward(x)
         q8 = getattr(self, "_fused_gate_up_q8", None)
         if q8 is not None:
             act = K.silu_and_mul(_proj(x, None, q8, self._fused_gate_up_scale))
@@ -178,7 +183,7 @@ def _patch_mlp(module: torch.nn.Module, config: FusionConfig) -> None:
             act = K.gemm(x.contiguous(), self._fused_gate_up_weight, epilogue=L.EPI_SWIGLU)
         return _proj(act, self.down_proj.weight)
 
-    module.forward = types.MethodType(forward, module)
+    _install(module, forward, config, "x")
 
 
 def _delta_states(module, cache_params, batch: int, device):
@@ -203,14 +208,7 @@ def _delta_states(module, cache_params, batch: int, device):
 
 def _patch_delta(module: torch.nn.Module, config: FusionConfig) -> None:
     """integration.py:220-274."""
-    if hasattr(module, "_fused_original_forward"):
-        return
-    module._fused_original_forward = module.forward
-
     def forward(self, hidden_states, cache_params=None, attention_mask=None, **kwargs):
-        if not _is_fast_tensor(hidden_states):
-            return self._fused_original_forward(hidden_states, cache_params=cache_params,
-                                                attention_mask=attention_mask, **kwargs)
         hidden_states = qwen_impl.apply_mask_to_padding_states(hidden_states, attention_mask)
         batch, seq_len, _ = hidden_states.shape
         packed = _proj(hidden_states, self._fused_in_proj_weight, getattr(self, "_fused_in_proj_q8", None),
@@ -229,19 +227,12 @@ def _patch_delta(module: torch.nn.Module, config: FusionConfig) -> None:
         return _proj(core, self.out_proj.weight, getattr(self, "_fused_out_proj_q8", None),
                      getattr(self, "_fused_out_proj_scale", None))
 
-    module.forward = types.MethodType(forward, module)
+    _install(module, forward, config, "hidden_states")
 
 
 def _patch_attention(module: torch.nn.Module, config: FusionConfig) -> None:
     """integration.py:277-382."""
-    if hasattr(module, "_fused_original_forward"):
-        return
-    module._fused_original_forward = module.forward
-
     def forward(self, hidden_states, position_embeddings, attention_mask, past_key_values=None, **kwargs):
-        if not _is_fast_tensor(hidden_states):
-            return self._fused_original_forward(hidden_states, position_embeddings, attention_mask,
-                                                past_key_values=past_key_values, **kwargs)
         batch, seq_len, _ = hidden_states.shape
         packed = _proj(hidden_states, self._fused_qgkv_weight, getattr(self, "_fused_qgkv_q8", None),
                        getattr(self, "_fused_qgkv_scale", None))
@@ -283,7 +274,10 @@ def _patch_attention(module: torch.nn.Module, config: FusionConfig) -> None:
             if attention_mask is None:
                 attn = K.prefill_attention(q, keys.contiguous(), values.contiguous(), self.scaling,
                                            q_offset=keys.shape[2] - seq_len)
-        if attn is None:  # padded batch: the library attention with the model's 4D mask
+        if attn is None:  # padded batch: the model's 4D mask
+            if not config.eager_fallback:
+                raise ValueError("fused attention: padded batches (a 4D attention mask) need "
+                                 "FusionConfig(eager_fallback=True), which runs Transformers' attention")
             iface = qwen_impl.ALL_ATTENTION_FUNCTIONS.get_interface(cfg._attn_implementation,
                                                                     qwen_impl.eager_attention_forward)
             attn, _ = iface(self, q, keys, values, attention_mask, dropout=0.0, scaling=self.scaling, **kwargs)
@@ -291,15 +285,11 @@ def _patch_attention(module: torch.nn.Module, config: FusionConfig) -> None:
         attn = K.attention_gate_mul(attn.reshape(batch, seq_len, -1).contiguous(), packed, self.head_dim)
         return _proj(attn, self.o_proj.weight, o_q8, o_scale), None
 
-    module.forward = types.MethodType(forward, module)
+    _install(module, forward, config, "hidden_states")
 
 
 def _patch_text_model(text_model: torch.nn.Module, config: FusionConfig) -> None:
     """integration.py:385-506: residual + norm fused between sublayers."""
-    if hasattr(text_model, "_fused_original_forward"):
-        return
-    text_model._fused_original_forward = text_model.forward
-
     def forward(self, input_ids=None, attention_mask=None, position_ids=None, past_key_values=None,
                 inputs_embeds=None, use_cache=None, **kwargs):
         if (input_ids is None) == (inputs_embeds is None):
@@ -307,6 +297,8 @@ def _patch_text_model(text_model: torch.nn.Module, config: FusionConfig) -> None
         if inputs_embeds is None:
             inputs_embeds = self.embed_tokens(input_ids)
         if not _is_fast_tensor(inputs_embeds):
+            if not config.eager_fallback:
+                raise ValueError("fused text model: the embeddings must be BF16 CUDA tensors")
             return self._fused_original_forward(input_ids=None, attention_mask=attention_mask,
                                                 position_ids=position_ids, past_key_values=past_key_values,
                                                 inputs_embeds=inputs_embeds, use_cache=use_cache, **kwargs)
@@ -352,7 +344,7 @@ def _patch_text_model(text_model: torch.nn.Module, config: FusionConfig) -> None
             residual, normalized = K.residual_add_rms_norm(residual, mlp.contiguous(), nxt.weight, nxt.eps)
         return qwen_impl.Qwen3_5ModelOutputWithPast(last_hidden_state=normalized, past_key_values=past_key_values)
 
-    text_model.forward = types.MethodType(forward, text_model)
+    _install(text_model, forward, config, "input_ids")
 
 
 def apply_fusions(model: torch.nn.Module, config: FusionConfig | None = None) -> dict:
@@ -367,19 +359,19 @@ def apply_fusions(model: torch.nn.Module, config: FusionConfig | None = None) ->
     text = _text_model(model)
     for layer in text.layers:
         if config.rms_norm:
-            _patch_norm_module(layer.input_layernorm)
-            _patch_norm_module(layer.post_attention_layernorm)
+            _install(layer.input_layernorm, _fused_rms_norm, config, "hidden_states")
+            _install(layer.post_attention_layernorm, _fused_rms_norm, config, "hidden_states")
         if config.swiglu:
             _patch_mlp(layer.mlp, config)
         if hasattr(layer, "linear_attn") and config.delta:
-            _patch_gated_norm_module(layer.linear_attn.norm)
+            _install(layer.linear_attn.norm, _fused_gated_norm, config, "hidden_states")
             _patch_delta(layer.linear_attn, config)
         if hasattr(layer, "self_attn") and config.attention:
-            _patch_norm_module(layer.self_attn.q_norm)
-            _patch_norm_module(layer.self_attn.k_norm)
+            _install(layer.self_attn.q_norm, _fused_rms_norm, config, "hidden_states")
+            _install(layer.self_attn.k_norm, _fused_rms_norm, config, "hidden_states")
             _patch_attention(layer.self_attn, config)
     if config.rms_norm:
-        _patch_norm_module(text.norm)
+        _install(text.norm, _fused_rms_norm, config, "hidden_states")
     if config.residual_norm:
         _patch_text_model(text, config)
     model._qwen35_fusion_config = config

@@ -200,13 +200,29 @@ def set_gemm_tc_pairs(on: bool) -> None:
 
 # ---------------------------------------------------------------------------- A8W8
 def quantize_rows(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
-    """Per-row symmetric int8 (explore_runtime_quantization.py:143-155 / vllm per-token)."""
+    """Weight-side per-row symmetric int8 (explore_runtime_quantization.py:143-155):
+    ``s = amax/127`` (1 for a zero row), ``q = clamp(rne(x / s), -127, 127)``."""
     rows, width = _rows_and_width(x)
     _need_bf16(x)
     q = torch.empty(x.shape, device=x.device, dtype=torch.int8)
     scale = torch.empty((*x.shape[:-1], 1), device=x.device, dtype=torch.float32)
     L.call("q35_quantize_rows", L.ptr(x), L.ptr(q), L.ptr(scale), rows, width, _s(x))
     return q, scale
+
+
+def scaled_int8_quant(x: torch.Tensor, scale=None, azp=None, symmetric: bool = True):
+    """Activation-side dynamic per-token int8 quantisation, the call the reference makes through
+    vllm (explore_runtime_quantization.py:167-172): returns ``(q int8, scale fp32 [rows, 1], None)``
+    with vllm's semantics (``scale = amax/127``, ``q = sat(rne(x * 127/amax))``, zero rows give
+    zero codes and scale). Only the dynamic symmetric form is provided."""
+    if scale is not None or azp is not None or not symmetric:
+        raise ValueError("scaled_int8_quant: only dynamic symmetric per-token quantisation is supported")
+    rows, width = _rows_and_width(x)
+    _need_bf16(x)
+    q = torch.empty(x.shape, device=x.device, dtype=torch.int8)
+    s = torch.empty((rows, 1), device=x.device, dtype=torch.float32)
+    L.call("q35_quantize_tokens", L.ptr(x), L.ptr(q), L.ptr(s), rows, width, _s(x))
+    return q, s, None
 
 
 def int8_gemm(qx: torch.Tensor, qw: torch.Tensor) -> torch.Tensor:
@@ -470,7 +486,7 @@ def lm_keys_to_tokens(keys: torch.Tensor, out: torch.Tensor | None = None) -> to
 __all__ = [
     "rms_norm", "residual_add_rms_norm", "gated_rms_norm", "silu_and_mul", "ppu_swiglu_gemv", "sigmoid_mul",
     "attention_gate_mul", "qgkv_norm_rope", "causal_conv1d_fused", "delta_recurrent_fused",
-    "gqa_decode_attention", "lm_head_argmax", "quantize_rows", "int8_gemm", "a8w8_linear", "gemm",
+    "gqa_decode_attention", "lm_head_argmax", "quantize_rows", "scaled_int8_quant", "int8_gemm", "a8w8_linear", "gemm",
     "fused_gemv", "attn_decode", "prefill_attention", "delta_decode", "delta_chunked_fused",
     "lm_head_shard_keys", "lm_keys_to_tokens",
 ]

@@ -72,6 +72,7 @@ _SIGS = {
     "q35_lm_head_shard_keys": (INT, [P, I64, P, P, I64, I64, I64, I64, F32, P, P, SZ, P]),
     "q35_lm_keys_to_tokens": (INT, [P, I64, P, P]),
     "q35_quantize_rows": (INT, [P, P, P, I64, I64, P]),
+    "q35_quantize_tokens": (INT, [P, P, P, I64, I64, P]),
     "q35_a8w8_linear_workspace_size": (SZ, [I64, I64]),
     "q35_a8w8_linear": (INT, [P, P, P, P, I64, I64, I64, P, SZ, P]),
     "q35_int8_gemm_i32": (INT, [P, P, P, I64, I64, I64, P]),
@@ -108,6 +109,8 @@ _SIGS = {
     "q35_set_gemv_ctas_per_sm": (INT, [C.c_int]),
     "q35_decoder_set_trace": (INT, [P, P, I64]),
     "q35_decoder_trace_ops": (INT, [P]),
+    "q35_decoder_set_probe": (INT, [P, P, SZ]),
+    "q35_decoder_probe_bytes": (SZ, [P]),
     "q35_decoder_persistent_error": (INT, []),
 }
 

@@ -169,27 +169,60 @@ def test_prefill_state_matches_oracle():
     assert ties == 0 or int(eng.token) != tok_ref
 
 
-@pytest.mark.parametrize("a8w8", [False, True])
-def test_full_2b_config4_greedy_stream(a8w8):
-    """random-init 2B-shape decoder, prefill 1024 uniform-random ids, then
-    32 greedy decode steps with the fused LM-head top-1, batch 1 (CUDA-graph decode)."""
+def test_full_2b_config4_greedy_stream_bf16():
+    """BASELINE config 4 in BF16: random-init 2B-shape decoder, prefill 1024 uniform-random ids,
+    then 32 greedy decode steps with the fused LM-head top-1, batch 1 (CUDA-graph decode). The
+    free-running stream must equal the oracle's, token for token."""
     dims = Qwen35Dims()
     w = make_weights(dims, seed=0)
     prompt = make_prompt(dims, 1024, seed=1)
-    eng = Qwen35Engine(w, dims, a8w8=a8w8, max_len=1152, max_prefill=1024)
+    eng = Qwen35Engine(w, dims, max_len=1152, max_prefill=1024)
     got, ttft, _ = eng.generate(prompt[0], 33, use_graph=True)
-    oracle = OracleDecoder(w, dims, a8w8=a8w8, max_cache_len=1152)
-    want = oracle.generate(prompt, steps=32)
-    same = next((i for i, (a, b) in enumerate(zip(got, want)) if a != b), len(got))
-    print(f"a8w8={a8w8}: free-running streams identical for {same}/33 tokens")
+    want = OracleDecoder(w, dims, max_cache_len=1152).generate(prompt, steps=32)
     print("oracle", want)
     print("gpu   ", got)
-    noise = LOGIT_NOISE_A8W8 if a8w8 else LOGIT_NOISE
-    ties = _check_stream(OracleDecoder(w, dims, a8w8=a8w8, max_cache_len=1152), prompt, got, noise)
-    # The oracle flips its own top-1 at 3 (BF16) / 6 (A8W8) of 33 steps under a single
-    # summation-order change. The A8W8 stream's first token is itself a 0.03-logit near-tie (the
-    # int8 re-quantisation after the first attention layer turns last-bit differences into code
-    # flips; the DeltaNet states then sit 2-11 % from the oracle's by the last layer, identically for
-    # every prefill kernel variant tried), so the A8W8 streams diverge from step 0 and measured 13
-    # near-ties of 33, every one within the 0.28 noise bound asserted above.
-    assert ties <= (16 if a8w8 else 6)
+    assert got == want
+
+
+A8W8_PROJ = ("in", "out", "gate_up", "down")
+# Largest fraction of an A8W8 projection's input codes (config 4 prefill, 1024 x k per layer)
+# that may differ from the oracle's: propagated last-bit BF16 differences (FP32 summation order
+# of norms, scans and softmax) move a code by one step where x * 127/amax sits near a half-way
+# point, at a rate that grows with depth.
+A8W8_MAX_CODE_FLIPS = 0.02
+
+
+def test_full_2b_config4_a8w8_code_flips_and_stream():
+    """BASELINE config 4 with A8W8. Per layer and projection, the per-token int8 codes and scales
+    of the GPU prefill are compared with the oracle's (vllm scaled_int8_quant semantics on both
+    sides): the code-flip rate is reported and bounded, the first layer's codes are compared
+    exactly, and the 33-token stream is checked under teacher forcing against the oracle's top-1."""
+    dims = Qwen35Dims()
+    w = make_weights(dims, seed=0)
+    prompt = make_prompt(dims, 1024, seed=1)
+    eng = Qwen35Engine(w, dims, a8w8=True, max_len=1152, max_prefill=1024)
+    gpu_codes = eng.prefill_probe(prompt[0].cuda())
+    oracle = OracleDecoder(w, dims, a8w8=True, max_cache_len=1152)
+    oracle.probe = []
+    oracle.forward(prompt)
+    ref_codes = oracle.probe
+    assert len(ref_codes) == len(gpu_codes) == 4 * dims.layers
+    worst = 0.0
+    for i, ((qg, sg), (qo, so)) in enumerate(zip(gpu_codes, ref_codes)):
+        flips = float((qg != qo).float().mean())
+        off_by = int((qg.int() - qo.int()).abs().max())
+        scale_rel = float(((sg - so).abs() / so.abs().clamp_min(1e-30)).max())
+        print(f"layer {i // 4:2d} {A8W8_PROJ[i % 4]:>7}: code flips {flips:.5f} (max |dq| {off_by}), "
+              f"max scale rel diff {scale_rel:.2e}")
+        worst = max(worst, flips)
+    # layer 0's in-projection input is RMSNorm(embedding): one norm away from identical inputs
+    assert float((gpu_codes[0][0] != ref_codes[0][0]).float().mean()) < 1e-3
+    assert worst <= A8W8_MAX_CODE_FLIPS, worst
+    got, _, _ = eng.generate(prompt[0], 33, use_graph=True)
+    want = OracleDecoder(w, dims, a8w8=True, max_cache_len=1152).generate(prompt, steps=32)
+    same = next((i for i, (a, b) in enumerate(zip(got, want)) if a != b), len(got))
+    print(f"a8w8: free-running streams identical for {same}/33 tokens")
+    print("oracle", want)
+    print("gpu   ", got)
+    ties = _check_stream(OracleDecoder(w, dims, a8w8=True, max_cache_len=1152), prompt, got, LOGIT_NOISE_A8W8)
+    assert ties <= 16

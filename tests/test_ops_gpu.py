@@ -158,6 +158,21 @@ def test_quantize_rows_bit_exact(rows, width):
     assert torch.equal(s.cpu(), so)
 
 
+@pytest.mark.parametrize("rows,width", [(1, 2048), (7, 6144), (64, 2048), (5, 100), (1024, 2048)])
+def test_quantize_tokens_bit_exact(rows, width):
+    x = randn(rows, width, seed=rows + width + 1)
+    x[0, :5] = 0
+    x[0, 7] = 2.0
+    x[0, 9] = 1.0  # +-amax/2: a half-way product
+    x[0, 10] = -1.0
+    if rows > 1:
+        x[1].zero_()  # all-zero row -> codes 0, scale 0
+    q, s, _ = K.scaled_int8_quant(cu(x))
+    qo, so = OQ.quantize_tokens(x)
+    assert torch.equal(q.cpu(), qo)
+    assert torch.equal(s.cpu(), so)
+
+
 @pytest.mark.parametrize("m,n,k", [(1, 512, 2048), (37, 300, 2048), (128, 256, 6144)])
 def test_int8_gemm_int32_bit_exact(m, n, k):
     g = torch.Generator().manual_seed(m * n + k)

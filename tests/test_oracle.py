@@ -147,7 +147,7 @@ def test_a8w8_linear_is_exact_integer_math():
     x = torch.randn(3, 512, generator=g).bfloat16()
     w = (torch.randn(64, 512, generator=g) * 0.02).bfloat16()
     qw, sw = a8w8.quantize_weight(w)
-    qx, sx = a8w8.quantize_rows(x)
+    qx, sx = a8w8.quantize_tokens(x)
     acc = a8w8.int8_matmul_exact(qx, qw)
     ref = (qx.long()[:, None, :] * qw.long()[None]).sum(-1)
     assert torch.equal(acc.long(), ref)
@@ -155,6 +155,23 @@ def test_a8w8_linear_is_exact_integer_math():
     assert torch.equal(y, ((acc.float() * sx) * sw.T).bfloat16())
     rel = (y.float() - F.linear(x, w).float()).norm() / F.linear(x, w).float().norm()
     assert rel < 0.02
+
+
+def test_activation_quantiser_follows_vllm_semantics():
+    """Activation codes are x * (127/amax) rounded half to even (vllm scaled_int8_quant), not
+    x / (amax/127): with amax = 1.125 the rounded reciprocal puts x = 0.5625 exactly on 63.5 (even
+    code 64), while dividing by the rounded scale lands just below (63); with amax = 1.1875 it is
+    the other way round."""
+    x = torch.zeros(3, 16, dtype=torch.bfloat16)
+    x[0, 0], x[0, 1], x[0, 2] = 1.125, 0.5625, -0.5625
+    x[1, 0], x[1, 1] = 1.1875, 0.59375
+    q, s = a8w8.quantize_tokens(x)
+    assert q[0, :3].tolist() == [127, 64, -64] and q[1, :2].tolist() == [127, 63]
+    assert float(s[0]) == (torch.tensor(1.125) / 127.0).item()
+    assert q[2].abs().sum() == 0 and float(s[2]) == 0.0  # all-zero row: zero codes, zero scale
+    qw, sw = a8w8.quantize_rows(x)
+    assert qw[0, :3].tolist() == [127, 63, -63] and qw[1, :2].tolist() == [127, 64]
+    assert float(sw[2]) == 1.0  # the weight formula's all-zero row
 
 
 def test_linear_rounds_once():

@@ -60,7 +60,7 @@ def test_gemm_tc_a8w8_bit_exact(epi):
     x = randn(m, k, seed=7)
     w = randn(rows, k, seed=8, scale=0.02)
     qw, sw = OQ.quantize_weight(w)
-    qx, sx = OQ.quantize_rows(x)
+    qx, sx = OQ.quantize_tokens(x)
     y = OQ.dequantize(OQ.int8_matmul_exact(qx, qw), sx, sw)
     if epi == L.EPI_SWIGLU:
         want = O.silu_and_mul(y)
@@ -90,7 +90,7 @@ def test_gemm_tc_persistent_many_tiles():
     x = randn(1024, 2048, seed=23)
     wg = randn(2 * 6144, 2048, seed=24, scale=0.02)
     qw, sw = OQ.quantize_weight(wg)
-    qx, sx = OQ.quantize_rows(x)
+    qx, sx = OQ.quantize_tokens(x)
     want = O.silu_and_mul(OQ.dequantize(OQ.int8_matmul_exact(qx, qw), sx, sw))
     got = K.gemm_a8w8_tc(cu(qx), cu(sx.reshape(-1)), cu(qw), cu(sw.reshape(-1)), epilogue=L.EPI_SWIGLU)
     torch.cuda.synchronize()

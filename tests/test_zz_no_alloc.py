@@ -34,12 +34,13 @@ def _noalloc_call(q, k, v, n_valid, out):
                                                       k.shape[2], L.stream_of(q.device))
 
 
-@pytest.mark.parametrize("batch,cache_len", [(1, 1152), (8, 4096)])
-def test_noalloc_matches_workspace_entry_point_on_consecutive_calls(batch, cache_len):
-    g = torch.Generator(device="cuda").manual_seed(batch * 131 + cache_len)
+@pytest.mark.parametrize("batch,cache_len,kv_heads", [(1, 1152, 2), (8, 4096, 2), (2, 2048, 8), (4, 1024, 4)],
+                         ids=["b1-g4", "b8-g4", "b2-g1", "b4-g2"])
+def test_noalloc_matches_workspace_entry_point_on_consecutive_calls(batch, cache_len, kv_heads):
+    g = torch.Generator(device="cuda").manual_seed(batch * 131 + cache_len + kv_heads)
     q = torch.randn(batch, 8, 1, 256, device="cuda", generator=g).to(torch.bfloat16)
-    k = torch.randn(batch, 2, cache_len, 256, device="cuda", generator=g).to(torch.bfloat16)
-    v = torch.randn(batch, 2, cache_len, 256, device="cuda", generator=g).to(torch.bfloat16)
+    k = torch.randn(batch, kv_heads, cache_len, 256, device="cuda", generator=g).to(torch.bfloat16)
+    v = torch.randn(batch, kv_heads, cache_len, 256, device="cuda", generator=g).to(torch.bfloat16)
     for n in (cache_len - 5, 37):  # two calls in a row; the array keeps the previous call's contents
         n_valid = torch.tensor([n], device="cuda", dtype=torch.int64)
         want = torch.empty(batch, 1, 8 * 256, device="cuda", dtype=torch.bfloat16)
@@ -65,3 +66,17 @@ def test_noalloc_rejects_shapes_beyond_its_static_scratch():
                                               C.c_float(0.0625), out.data_ptr(), b, h, kvh, 256, n,
                                               L.stream_of(q.device))
     assert rc == L.Q35_EINVAL and "static maximum" in L.last_error()
+
+
+def test_noalloc_rejects_more_split_tickets_than_its_scratch_holds():
+    lib = L.load()
+    b, h, kvh, n = 33, 2, 2, 64  # 66 (batch x kv_heads) tickets, 64 fit; the scratch itself is small
+    assert lib.q35_gqa_decode_workspace_size(b, h, kvh, 256, n) <= lib.q35_gqa_decode_noalloc_max_bytes()
+    q = torch.zeros(b, h, 1, 256, device="cuda", dtype=torch.bfloat16)
+    kv = torch.zeros(b, kvh, n, 256, device="cuda", dtype=torch.bfloat16)
+    n_valid = torch.ones(1, device="cuda", dtype=torch.int64)
+    out = torch.empty(b, 1, h * 256, device="cuda", dtype=torch.bfloat16)
+    rc = lib.q35_gqa_decode_attention_noalloc(q.data_ptr(), kv.data_ptr(), kv.data_ptr(), n_valid.data_ptr(),
+                                              C.c_float(0.0625), out.data_ptr(), b, h, kvh, 256, n,
+                                              L.stream_of(q.device))
+    assert rc == L.Q35_EINVAL and "ticket" in L.last_error()
