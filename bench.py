@@ -156,8 +156,21 @@ def hf_eager_model(weights_cpu: dict, dims: Qwen35Dims):
                          "partial_rotary_factor": dims.rotary_dim / dims.head_dim,
                          "mrope_section": list(dims.mrope_section), "mrope_interleaved": True})
     cfg._attn_implementation = "eager"
-    with torch.device("meta"):
-        model = hf.Qwen3_5ForCausalLM(cfg)
+    # The torch implementations of the DeltaNet pieces (torch_chunk_gated_delta_rule, the torch
+    # conv update, Qwen3_5RMSNormGated): with a GPU visible, Transformers would pick the Triton
+    # kernels of flash-linear-attention, which cannot run on CPU tensors.
+    fast = ("FusedRMSNormGated", "chunk_gated_delta_rule", "fused_recurrent_gated_delta_rule", "causal_conv1d_fn",
+            "causal_conv1d_update")
+    saved = {name: getattr(hf, name, None) for name in fast + ("is_fast_path_available",)}
+    try:
+        for name in fast:
+            setattr(hf, name, None)
+        hf.is_fast_path_available = False
+        with torch.device("meta"):
+            model = hf.Qwen3_5ForCausalLM(cfg)
+    finally:
+        for name, value in saved.items():
+            setattr(hf, name, value)
     missing, unexpected = model.load_state_dict(weights_cpu, strict=False, assign=True)
     if unexpected or any(not k.startswith("lm_head") for k in missing):
         raise RuntimeError(f"eager model weights: missing {missing}, unexpected {unexpected}")
