@@ -88,7 +88,11 @@ enum {
 enum {
   Q35_EPI_STORE = 0,    /* out[n] = bf16(y_n) */
   Q35_EPI_RESIDUAL = 1, /* resid_out[n] = bf16(resid_out[n] + bf16(y_n)) (in place) */
-  Q35_EPI_SWIGLU = 2    /* rows n and n + n_out are gate/up: out[n] = SwiGLU */
+  Q35_EPI_SWIGLU = 2,   /* rows n and n + n_out are gate/up: out[n] = SwiGLU */
+  /* tensor-core GEMM only (the vision tower's biased linears, q35_gemm_tc_bias): */
+  Q35_EPI_BIAS = 3,           /* out[n] = bf16(y_n + bias[n]) */
+  Q35_EPI_BIAS_GELU_TANH = 4, /* out[n] = bf16(gelu_tanh(bf16(y_n + bias[n]))) */
+  Q35_EPI_BIAS_GELU = 5       /* out[n] = bf16(gelu_erf(bf16(y_n + bias[n]))) */
 };
 typedef struct {
   const void* weight;       /* bf16 [rows, k], or int8 [rows, k] when int8 != 0 */
@@ -185,6 +189,14 @@ int q35_gemm_bf16(const void* a, const void* w, void* out, int64_t m, int64_t n,
  * cta_group::2). k must be a multiple of 64, n of 8. */
 int q35_gemm_tc(const void* a, const void* w, void* out, int64_t m, int64_t n, int64_t k,
                 int32_t epilogue, void* stream);
+
+/* Biased bf16 projection on tcgen05 for the vision tower (HF Qwen3_5Vision* nn.Linear with bias
+ * and the activations that follow them: integration.py:509-736 runs them through F.linear):
+ * out [m,n] = epilogue(A [m,k] @ W [n,k]^T + bias [n]) with epilogue Q35_EPI_BIAS,
+ * Q35_EPI_BIAS_GELU_TANH (gelu_pytorch_tanh, the vision MLP) or Q35_EPI_BIAS_GELU (nn.GELU, the
+ * patch merger). k must be a multiple of 64, n of 8. */
+int q35_gemm_tc_bias(const void* a, const void* w, const void* bias, void* out, int64_t m, int64_t n,
+                     int64_t k, int32_t epilogue, void* stream);
 
 /* A8W8 prefill projection on tcgen05 (kind::i8, exact int32 accumulation in TMEM) with the
  * dequantisation bf16((float(acc) * sx[m]) * sw[n]) and the epilogue fused (k multiple of 128).
@@ -396,6 +408,87 @@ size_t q35_decoder_probe_bytes(const q35_decoder* dec);
 /* Non-zero when a bounded wait of the persistent step gave up (1 grid barrier, 2 ring slot,
  * 3 ring data); reading clears it. */
 int q35_decoder_persistent_error(void);
+
+/* ---------------------------------------------------------------- vision tower */
+
+/* kernels.py:1188-1222 layer_norm: out = LayerNorm(x; weight, bias, eps) over the last dim,
+ * FP32 mean / centred variance, bf16 out. x, out [rows, width] bf16. */
+int q35_layer_norm(const void* x, const void* weight, const void* bias, void* out, int64_t rows,
+                   int64_t width, float eps, void* stream);
+/* kernels.py:1225-1287 residual_add_layer_norm: residual_out = bf16(residual + update);
+ * norm_out = LayerNorm(residual_out). residual_out may alias residual. */
+int q35_residual_add_layer_norm(const void* residual, const void* update, const void* weight,
+                                const void* bias, void* residual_out, void* norm_out, int64_t rows,
+                                int64_t width, float eps, void* stream);
+/* kernels.py:1290-1336 position_embed_add: out[r] = bf16(hidden[r] + bf16(sum_k weights[r,k] *
+ * table[indices[r,k]])) (FP32 accumulation); indices int64 / weights fp32 [rows, neighbors]. */
+int q35_position_embed_add(const void* hidden, const void* table, const int64_t* indices,
+                           const float* weights, void* out, int64_t rows, int64_t width,
+                           int64_t neighbors, void* stream);
+/* kernels.py:336-416 vision_qkv_rope: packed [tokens, 3*heads*dim] -> q, k, v [heads, tokens, dim]
+ * (batch 1) with RoPE on q, k: x*cos + rotate_half(x)*sin in FP32 without fused multiply-adds;
+ * cos / sin fp32 [tokens, dim]. dim 64. */
+int q35_vision_qkv_rope(const void* packed, const float* cos, const float* sin, void* q_out,
+                        void* k_out, void* v_out, int64_t tokens, int64_t heads, int64_t dim,
+                        void* stream);
+/* Bidirectional attention over one image (integration.py:616-700 with cu_seqlens = [0, tokens]):
+ * q, k, v [heads, tokens, dim] bf16 -> out [tokens, heads*dim] bf16, FP32 softmax. dim 64. */
+int q35_vision_attention(const void* q, const void* k, const void* v, void* out, int64_t tokens,
+                         int64_t heads, int64_t dim, float scale, void* stream);
+/* 2-D rotary tables of HF Qwen3_5VisionModel.rot_pos_emb for a grid_h x grid_w patch grid in
+ * merge-block order: cos/sin fp32 [grid_h*grid_w, 64] from inv_freq fp32 [16]. */
+int q35_vision_rope_table(const float* inv_freq, float* cos_out, float* sin_out, int64_t grid_h,
+                          int64_t grid_w, int64_t merge, void* stream);
+/* Processor-side patch extraction (Qwen2-VL image processor order, a single frame repeated over
+ * temporal_patch): pixels fp32 [channels, height, width] (rescaled to [0,1)) -> bf16
+ * [(height/patch)*(width/patch), channels*temporal_patch*patch*patch], normalised (x-mean)/std. */
+int q35_vision_patchify(const float* pixels, void* out, int64_t channels, int64_t height,
+                        int64_t width, int64_t patch, int64_t temporal_patch, int64_t merge,
+                        float mean, float std, void* stream);
+
+/* One ViT block (HF Qwen3_5VisionBlock): pre-norm attention and GELU(tanh) MLP, biased linears. */
+typedef struct {
+  const void* norm1_w; const void* norm1_b;   /* bf16 [width] */
+  const void* qkv_w; const void* qkv_b;       /* [3*width, width], [3*width] */
+  const void* proj_w; const void* proj_b;     /* [width, width], [width] */
+  const void* norm2_w; const void* norm2_b;
+  const void* fc1_w; const void* fc1_b;       /* [intermediate, width] */
+  const void* fc2_w; const void* fc2_b;       /* [width, intermediate] */
+} q35_vit_block_desc;
+
+typedef struct {
+  int32_t depth, width, heads, intermediate;
+  int32_t in_channels, patch, temporal_patch, merge;
+  int32_t out_width;        /* merger output (the text model's hidden size) */
+  int32_t pos_side;         /* learned position table is pos_side x pos_side */
+  int32_t max_patches;      /* largest patch count the workspace is sized for */
+  float eps;                /* LayerNorm epsilon (1e-6) */
+  float pixel_mean, pixel_std;
+  const q35_vit_block_desc* blocks;
+  const void* patch_w;      /* Conv3d weight flattened [width, in_channels*temporal_patch*patch^2] */
+  const void* patch_b;
+  const void* pos_table;    /* [pos_side^2, width] */
+  const float* rope_inv_freq; /* fp32 [16] */
+  const void* merger_norm_w; const void* merger_norm_b;
+  const void* merger_fc1_w; const void* merger_fc1_b;   /* [merge^2*width, merge^2*width] */
+  const void* merger_fc2_w; const void* merger_fc2_b;   /* [out_width, merge^2*width] */
+  void* workspace;
+  size_t workspace_bytes;
+} q35_vit_desc;
+
+typedef struct q35_vit q35_vit;
+size_t q35_vit_workspace_size(const q35_vit_desc* desc);
+int q35_vit_create(const q35_vit_desc* desc, q35_vit** out);
+void q35_vit_destroy(q35_vit* vit);
+/* The vision forward of integration.py:509-736 for one image: patchify, patch embedding (tcgen05
+ * GEMM + bias), bilinear position embedding + norm1, `depth` blocks (8 launches each: QKV GEMM,
+ * QKV RoPE, attention, projection GEMM, residual + norm2, fc1 GEMM + GELU(tanh), fc2 GEMM,
+ * residual + next norm1 / merger norm), then the 2x2 merger (fc1 + GELU, fc2): out bf16
+ * [(height/patch/merge)*(width/patch/merge), out_width]. */
+int q35_vit_encode(q35_vit* vit, const float* pixels, int64_t height, int64_t width, void* out,
+                   void* stream);
+/* Device address of the final patch states [patches, width] of the last encode (pre-merger). */
+void* q35_vit_hidden(const q35_vit* vit);
 
 #ifdef __cplusplus
 }

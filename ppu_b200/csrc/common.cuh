@@ -26,6 +26,14 @@ Q35_DEV float rbf(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 // SiLU / sigmoid exactly as the reference kernels write them (kernels.py:135, 166, 272).
 Q35_DEV float silu_f(float x) { return x / (1.0f + expf(-x)); }
 Q35_DEV float sigmoid_f(float x) { return 1.0f / (1.0f + expf(-x)); }
+// GELU of the vision tower: the tanh form ("gelu_pytorch_tanh", the ViT MLP) and the erf form
+// (nn.GELU(), the patch merger), as torch writes them: 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715
+// x^3))) and 0.5 x (1 + erf(x / sqrt(2))).
+Q35_DEV float gelu_tanh_f(float x) {
+  const float inner = 0.7978845608028654f * (x + 0.044715f * x * x * x);
+  return 0.5f * x * (1.0f + tanhf(inner));
+}
+Q35_DEV float gelu_erf_f(float x) { return 0.5f * x * (1.0f + erff(x * 0.7071067811865476f)); }
 // IEEE square root and division (no approximate rsqrt), closest to torch.rsqrt on the CPU.
 Q35_DEV float rsqrt_ieee(float x) { return 1.0f / sqrtf(x); }
 

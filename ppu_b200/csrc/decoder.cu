@@ -34,7 +34,7 @@ int q35_delta_decode_launch(const void* packed, const void* conv_weight, void* c
 int q35_gemm_launch(const void* a, const void* w, void* out, int64_t m, int64_t n, int64_t k, int epi, bool int8,
                     const float* sx, const float* sw, cudaStream_t s);
 int q35_gemm_tc_launch(const void* a, const void* w, void* out, int64_t m, int64_t n, int64_t k, int epi, bool int8,
-                       const float* sx, const float* sw, cudaStream_t s);
+                       const float* sx, const float* sw, cudaStream_t s, const void* bias = nullptr);
 int q35_quantize_tokens_launch(const void* x, int8_t* q, float* scale, int64_t rows, int64_t width,
                                cudaStream_t s);
 int q35_qgkv_rope_positions_launch(const void* packed, const void* q_weight, const void* k_weight,

@@ -43,6 +43,7 @@ constexpr int stages_for(int) { return 4; }
 struct TcParams {
   void* out;          // bf16 [M, N] or int32 (RAW)
   bf16* resid;        // RESIDUAL: [M, N] updated in place
+  const bf16* bias;   // BIAS*: [N]
   const float* sx;    // int8: [M]
   const float* sw;    // int8: [Nw]
   int M, N, K;        // K in elements
@@ -227,6 +228,15 @@ Q35_DEV void epilogue_row(const TcParams& p, uint32_t trow, int row, int col0, i
           const float up =
               INT8 ? ((gc + j < p.N) ? ((float)(int)u[j] * sx) * __ldg(p.sw + p.N + gc + j) : 0.f) : __uint_as_float(u[j]);
           y[j] = rbf(silu_f(rbf(y[j]))) * rbf(up);
+        }
+      }
+      if (EPI >= Q35_EPI_BIAS) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const float b = (gc + j < p.N) ? bf2f(p.bias[gc + j]) : 0.f;
+          y[j] = y[j] + b;
+          if (EPI == Q35_EPI_BIAS_GELU_TANH) y[j] = gelu_tanh_f(rbf(y[j]));
+          if (EPI == Q35_EPI_BIAS_GELU) y[j] = gelu_erf_f(rbf(y[j]));
         }
       }
       bf16* dst = base + gc;
@@ -636,15 +646,19 @@ int launch_tc(const void* a, const void* w, const TcParams& p, cudaStream_t s) {
 
 // Used by the decoder prefill and q35_gemm_tc: tensor-core projection with fused epilogue.
 int q35_gemm_tc_launch(const void* a, const void* w, void* out, int64_t m, int64_t n, int64_t k, int epi, bool int8,
-                       const float* sx, const float* sw, cudaStream_t s) {
+                       const float* sx, const float* sw, cudaStream_t s, const void* bias = nullptr) {
   Q35_REQUIRE(a && w && out, "gemm_tc: null pointer");
   Q35_REQUIRE(m >= 1 && n >= 1 && k >= 1 && (k * (int8 ? 1 : 2)) % BKB == 0,
               "gemm_tc: k=%lld must fill 128-byte K slabs", (long long)k);
   Q35_REQUIRE(Q35_ALIGNED(a, 16) && Q35_ALIGNED(w, 16) && Q35_ALIGNED(out, 16), "gemm_tc: 16-byte alignment");
   Q35_REQUIRE(n % 8 == 0, "gemm_tc: n must be a multiple of 8");
   Q35_REQUIRE(!int8 || (sx && sw), "gemm_tc: int8 needs scales");
-  Q35_REQUIRE(epi == Q35_EPI_STORE || epi == Q35_EPI_RESIDUAL || epi == Q35_EPI_SWIGLU, "gemm_tc: bad epilogue");
+  Q35_REQUIRE(epi == Q35_EPI_STORE || epi == Q35_EPI_RESIDUAL || epi == Q35_EPI_SWIGLU ||
+                  (!int8 && epi >= Q35_EPI_BIAS && epi <= Q35_EPI_BIAS_GELU && bias),
+              "gemm_tc: bad epilogue %d", epi);
+  Q35_REQUIRE(!bias || Q35_ALIGNED(bias, 16), "gemm_tc: bias must be 16-byte aligned");
   TcParams p = {};
+  p.bias = static_cast<const bf16*>(bias);
   p.out = out;
   p.resid = static_cast<bf16*>(out);
   p.sx = sx;
@@ -662,8 +676,23 @@ int q35_gemm_tc_launch(const void* a, const void* w, void* out, int64_t m, int64
   switch (epi) {
     case Q35_EPI_STORE: return launch_tc<false, Q35_EPI_STORE>(a, w, p, s);
     case Q35_EPI_RESIDUAL: return launch_tc<false, Q35_EPI_RESIDUAL>(a, w, p, s);
+    case Q35_EPI_BIAS: return launch_tc<false, Q35_EPI_BIAS>(a, w, p, s);
+    case Q35_EPI_BIAS_GELU_TANH: return launch_tc<false, Q35_EPI_BIAS_GELU_TANH>(a, w, p, s);
+    case Q35_EPI_BIAS_GELU: return launch_tc<false, Q35_EPI_BIAS_GELU>(a, w, p, s);
     default: return launch_tc<false, Q35_EPI_SWIGLU>(a, w, p, s);
   }
+}
+
+int q35_gemm_tc_bias_launch(const void* a, const void* w, const void* bias, void* out, int64_t m, int64_t n,
+                            int64_t k, int epi, cudaStream_t s) {
+  Q35_REQUIRE(bias, "gemm_tc_bias: null bias");
+  Q35_REQUIRE(epi >= Q35_EPI_BIAS && epi <= Q35_EPI_BIAS_GELU, "gemm_tc_bias: bad epilogue %d", epi);
+  return q35_gemm_tc_launch(a, w, out, m, n, k, epi, false, nullptr, nullptr, s, bias);
+}
+
+extern "C" int q35_gemm_tc_bias(const void* a, const void* w, const void* bias, void* out, int64_t m, int64_t n,
+                                int64_t k, int32_t epilogue, void* stream) {
+  return q35_gemm_tc_bias_launch(a, w, bias, out, m, n, k, epilogue, (cudaStream_t)stream);
 }
 
 extern "C" int q35_gemm_tc(const void* a, const void* w, void* out, int64_t m, int64_t n, int64_t k,

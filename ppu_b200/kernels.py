@@ -483,10 +483,111 @@ def lm_keys_to_tokens(keys: torch.Tensor, out: torch.Tensor | None = None) -> to
     return out
 
 
+# ---------------------------------------------------------------------------- vision tower
+def gemm_bias(a: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, *, epilogue=L.EPI_BIAS, out=None):
+    """Biased projection on tcgen05 (the vision tower's nn.Linear layers): ``epilogue(a @ weight^T +
+    bias)`` with EPI_BIAS, EPI_BIAS_GELU_TANH or EPI_BIAS_GELU; bf16 ``[M, N]``."""
+    _need_bf16(a, weight, bias)
+    m, k = a.reshape(-1, a.shape[-1]).shape
+    n = weight.shape[0]
+    if out is None:
+        out = torch.empty((*a.shape[:-1], n), device=a.device, dtype=BF16)
+    L.call("q35_gemm_tc_bias", L.ptr(a), L.ptr(weight), L.ptr(bias), L.ptr(out), m, n, k, epilogue, _s(a))
+    return out
+
+
+def layer_norm(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
+    """kernels.py:1188-1222: LayerNorm over the last dimension (FP32 statistics, bf16 out)."""
+    rows, width = _rows_and_width(x)
+    _need_bf16(x, weight, bias)
+    out = torch.empty_like(x)
+    L.call("q35_layer_norm", L.ptr(x), L.ptr(weight), L.ptr(bias), L.ptr(out), rows, width, eps, _s(x))
+    return out
+
+
+def residual_add_layer_norm(residual: torch.Tensor, update: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor,
+                            eps: float = 1e-6) -> tuple[torch.Tensor, torch.Tensor]:
+    """kernels.py:1225-1287: ``residual_out = bf16(residual + update)``, ``LayerNorm(residual_out)``."""
+    if residual.shape != update.shape:
+        raise ValueError("vision residual tensors must have identical shape")
+    rows, width = _rows_and_width(residual)
+    _rows_and_width(update)
+    _need_bf16(residual, update, weight, bias)
+    residual_out = torch.empty_like(residual)
+    norm_out = torch.empty_like(residual)
+    L.call("q35_residual_add_layer_norm", L.ptr(residual), L.ptr(update), L.ptr(weight), L.ptr(bias),
+           L.ptr(residual_out), L.ptr(norm_out), rows, width, eps, _s(residual))
+    return residual_out, norm_out
+
+
+def position_embed_add(hidden: torch.Tensor, embedding_table: torch.Tensor, indices: torch.Tensor,
+                       interpolation_weight: torch.Tensor) -> torch.Tensor:
+    """kernels.py:1290-1336: ``hidden + bf16(sum_k w_k * table[idx_k])`` per row (FP32 sum)."""
+    if hidden.ndim != 2 or not hidden.is_contiguous():
+        raise ValueError("vision hidden tensor must be contiguous [rows,width]")
+    rows, width = hidden.shape
+    neighbors = indices.shape[-1]
+    if indices.shape != interpolation_weight.shape or indices.shape[0] != rows:
+        raise ValueError("position interpolation tensors do not match hidden rows")
+    if not hidden.is_cuda:
+        raise ValueError("fused kernels require a CUDA tensor")
+    _need_bf16(hidden, embedding_table)
+    idx = indices.to(device=hidden.device, dtype=torch.int64).contiguous()
+    wts = interpolation_weight.to(device=hidden.device, dtype=torch.float32).contiguous()
+    table = embedding_table.contiguous()
+    out = torch.empty_like(hidden)
+    L.call("q35_position_embed_add", L.ptr(hidden), L.ptr(table), L.ptr(idx), L.ptr(wts), L.ptr(out), rows, width,
+           neighbors, _s(hidden))
+    return out
+
+
+def vision_qkv_rope(packed_qkv: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, *, heads: int,
+                    dim: int) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """kernels.py:336-416: packed Vision QKV ``[tokens, 3*heads*dim]`` to BHLD ``[1, heads, tokens,
+    dim]`` q / k / v with RoPE on q and k, one launch."""
+    if packed_qkv.ndim != 2 or not packed_qkv.is_contiguous():
+        raise ValueError("packed Vision QKV must be contiguous [tokens,3*hidden]")
+    tokens, packed_width = packed_qkv.shape
+    if packed_width != 3 * heads * dim:
+        raise ValueError(f"packed Vision QKV width {packed_width}, expected {3 * heads * dim}")
+    cos = cos.contiguous()
+    sin = sin.contiguous()
+    if cos.shape != (tokens, dim) or sin.shape != cos.shape:
+        raise ValueError(f"Vision RoPE shape {tuple(cos.shape)}, expected {(tokens, dim)}")
+    if not packed_qkv.is_cuda:
+        raise ValueError("fused kernels require a CUDA tensor")
+    _need_bf16(packed_qkv)
+    c32 = cos.to(device=packed_qkv.device, dtype=torch.float32).contiguous()
+    s32 = sin.to(device=packed_qkv.device, dtype=torch.float32).contiguous()
+    q = torch.empty((1, heads, tokens, dim), device=packed_qkv.device, dtype=packed_qkv.dtype)
+    k = torch.empty_like(q)
+    v = torch.empty_like(q)
+    L.call("q35_vision_qkv_rope", L.ptr(packed_qkv), L.ptr(c32), L.ptr(s32), L.ptr(q), L.ptr(k), L.ptr(v), tokens,
+           heads, dim, _s(packed_qkv))
+    return q, k, v
+
+
+def vision_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float) -> torch.Tensor:
+    """Bidirectional attention over one image: ``[1, heads, L, 64]`` q/k/v -> ``[L, heads*64]``
+    (the vision attention of integration.py:616-700 with a single ``cu_seqlens`` segment)."""
+    if q.shape != k.shape or q.shape != v.shape or q.dim() != 4 or q.shape[0] != 1:
+        raise ValueError("vision attention expects q, k, v of one shape [1, heads, tokens, dim]")
+    if not (q.is_contiguous() and k.is_contiguous() and v.is_contiguous()):
+        raise ValueError("fused kernels require contiguous input")
+    if not q.is_cuda:
+        raise ValueError("fused kernels require a CUDA tensor")
+    _need_bf16(q, k, v)
+    _, heads, tokens, dim = q.shape
+    out = torch.empty((tokens, heads * dim), device=q.device, dtype=BF16)
+    L.call("q35_vision_attention", L.ptr(q), L.ptr(k), L.ptr(v), L.ptr(out), tokens, heads, dim, scale, _s(q))
+    return out
+
+
 __all__ = [
     "rms_norm", "residual_add_rms_norm", "gated_rms_norm", "silu_and_mul", "ppu_swiglu_gemv", "sigmoid_mul",
     "attention_gate_mul", "qgkv_norm_rope", "causal_conv1d_fused", "delta_recurrent_fused",
     "gqa_decode_attention", "lm_head_argmax", "quantize_rows", "scaled_int8_quant", "int8_gemm", "a8w8_linear", "gemm",
     "fused_gemv", "attn_decode", "prefill_attention", "delta_decode", "delta_chunked_fused",
     "lm_head_shard_keys", "lm_keys_to_tokens",
+    "gemm_bias", "layer_norm", "residual_add_layer_norm", "position_embed_add", "vision_qkv_rope", "vision_attention",
 ]

@@ -13,6 +13,7 @@ LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libqwen35_b200.so"
 Q35_OK, Q35_EINVAL, Q35_ECUDA, Q35_ETIMEOUT, Q35_ENOTSUP = 0, 1, 2, 3, 4
 PRO_PLAIN, PRO_NORM, PRO_EMBED = 0, 1, 2
 EPI_STORE, EPI_RESIDUAL, EPI_SWIGLU = 0, 1, 2
+EPI_BIAS, EPI_BIAS_GELU_TANH, EPI_BIAS_GELU = 3, 4, 5
 Q35_GEMV_BULK, Q35_GEMV_REGISTERS = 0, 1
 
 P = C.c_void_p
@@ -49,6 +50,25 @@ class DecoderDesc(C.Structure):
         ("layers", C.POINTER(LayerDesc)), ("embed", P), ("final_norm", P), ("inv_freq", P),
         ("token", P), ("cache_len", P), ("rope_pos", P), ("token_log", P), ("log_pos", P),
         ("log_len", I32), ("use_pdl", I32), ("prefill_tc", I32), ("prefill_delta", I32), ("workspace", P), ("workspace_bytes", SZ),
+    ]
+
+
+class VitBlockDesc(C.Structure):
+    _fields_ = [
+        ("norm1_w", P), ("norm1_b", P), ("qkv_w", P), ("qkv_b", P), ("proj_w", P), ("proj_b", P),
+        ("norm2_w", P), ("norm2_b", P), ("fc1_w", P), ("fc1_b", P), ("fc2_w", P), ("fc2_b", P),
+    ]
+
+
+class VitDesc(C.Structure):
+    _fields_ = [
+        ("depth", I32), ("width", I32), ("heads", I32), ("intermediate", I32),
+        ("in_channels", I32), ("patch", I32), ("temporal_patch", I32), ("merge", I32),
+        ("out_width", I32), ("pos_side", I32), ("max_patches", I32), ("eps", F32),
+        ("pixel_mean", F32), ("pixel_std", F32),
+        ("blocks", C.POINTER(VitBlockDesc)), ("patch_w", P), ("patch_b", P), ("pos_table", P), ("rope_inv_freq", P),
+        ("merger_norm_w", P), ("merger_norm_b", P), ("merger_fc1_w", P), ("merger_fc1_b", P),
+        ("merger_fc2_w", P), ("merger_fc2_b", P), ("workspace", P), ("workspace_bytes", SZ),
     ]
 
 
@@ -110,6 +130,19 @@ _SIGS = {
     "q35_decoder_set_trace": (INT, [P, P, I64]),
     "q35_decoder_trace_ops": (INT, [P]),
     "q35_decoder_set_probe": (INT, [P, P, SZ]),
+    "q35_gemm_tc_bias": (INT, [P, P, P, P, I64, I64, I64, I32, P]),
+    "q35_layer_norm": (INT, [P, P, P, P, I64, I64, F32, P]),
+    "q35_residual_add_layer_norm": (INT, [P, P, P, P, P, P, I64, I64, F32, P]),
+    "q35_position_embed_add": (INT, [P, P, P, P, P, I64, I64, I64, P]),
+    "q35_vision_qkv_rope": (INT, [P, P, P, P, P, P, I64, I64, I64, P]),
+    "q35_vision_attention": (INT, [P, P, P, P, I64, I64, I64, F32, P]),
+    "q35_vision_rope_table": (INT, [P, P, P, I64, I64, I64, P]),
+    "q35_vision_patchify": (INT, [P, P, I64, I64, I64, I64, I64, I64, F32, F32, P]),
+    "q35_vit_workspace_size": (SZ, [C.POINTER(VitDesc)]),
+    "q35_vit_create": (INT, [C.POINTER(VitDesc), C.POINTER(P)]),
+    "q35_vit_destroy": (None, [P]),
+    "q35_vit_encode": (INT, [P, P, I64, I64, P, P]),
+    "q35_vit_hidden": (P, [P]),
     "q35_decoder_probe_bytes": (SZ, [P]),
     "q35_decoder_persistent_error": (INT, []),
 }
