@@ -12,40 +12,11 @@ vision model (``tests/golden/make_golden_vision.py``).
 
 from __future__ import annotations
 
-from dataclasses import dataclass
-
 import torch
 
+from ppu_b200.config import VisionDims  # noqa: F401  (shape dataclass shared with the package)
+
 BF16 = torch.bfloat16
-
-
-@dataclass(frozen=True)
-class VisionDims:
-    """Vision tower shape (defaults: BASELINE config 5's ViT: 24 layers, width 1024, 16 heads,
-    patch 16, 2x2 merge to the text model's hidden 2048)."""
-
-    depth: int = 24
-    width: int = 1024
-    heads: int = 16
-    intermediate: int = 4096
-    in_channels: int = 3
-    patch: int = 16
-    temporal_patch: int = 2
-    merge: int = 2
-    out_width: int = 2048
-    pos_side: int = 48  # 48 x 48 = 2304 learned position embeddings
-    eps: float = 1e-6
-    rope_theta: float = 10000.0
-    pixel_mean: float = 0.5
-    pixel_std: float = 0.5
-
-    @property
-    def head_dim(self) -> int:
-        return self.width // self.heads
-
-    @property
-    def patch_features(self) -> int:
-        return self.in_channels * self.temporal_patch * self.patch * self.patch
 
 
 def layer_norm(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:

@@ -134,3 +134,55 @@ class FusionConfig:
     # here: such inputs raise ValueError, so nothing silently leaves the B200 kernels.
     eager_fallback: bool = False
     extra: dict = field(default_factory=dict, compare=False, hash=False)
+
+
+@dataclass(frozen=True)
+class VisionDims:
+    """Vision tower shape (defaults: BASELINE config 5's ViT: 24 layers, width 1024, 16 heads of 64,
+    SwiGLU-free GELU(tanh) MLP 4096, patch 16 over 2 temporal slots, 2 x 2 merge to the text model's
+    hidden 2048, a 48 x 48 learned position table; the Qwen2-VL processor's mean = std = 0.5)."""
+
+    depth: int = 24
+    width: int = 1024
+    heads: int = 16
+    intermediate: int = 4096
+    in_channels: int = 3
+    patch: int = 16
+    temporal_patch: int = 2
+    merge: int = 2
+    out_width: int = 2048
+    pos_side: int = 48
+    eps: float = 1e-6
+    rope_theta: float = 10000.0
+    pixel_mean: float = 0.5
+    pixel_std: float = 0.5
+
+    @property
+    def head_dim(self) -> int:
+        return self.width // self.heads
+
+    @property
+    def patch_features(self) -> int:
+        return self.in_channels * self.temporal_patch * self.patch * self.patch
+
+    def grid(self, height: int, width: int) -> tuple[int, int]:
+        """Patch grid (rows, cols) of an image; both must be multiples of patch x merge."""
+        step = self.patch * self.merge
+        if height % step or width % step:
+            raise ValueError(f"image {height}x{width} is not a multiple of {step}")
+        return height // self.patch, width // self.patch
+
+    def merged_tokens(self, height: int, width: int) -> int:
+        gh, gw = self.grid(height, width)
+        return gh * gw // (self.merge * self.merge)
+
+    def linear_flops(self, height: int, width: int) -> int:
+        """Dense FLOPs of one image: patch embedding, per block QKV / proj / fc1 / fc2 and the
+        bidirectional attention, and the merger."""
+        gh, gw = self.grid(height, width)
+        n = gh * gw
+        w, i = self.width, self.intermediate
+        per_block = 2 * n * (3 * w * w + w * w + 2 * w * i) + 4 * n * n * w
+        mw = w * self.merge * self.merge
+        nm = n // (self.merge * self.merge)
+        return 2 * n * self.patch_features * w + self.depth * per_block + 2 * nm * (mw * mw + mw * self.out_width)

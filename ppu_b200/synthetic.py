@@ -73,3 +73,48 @@ def make_prompt(dims: Qwen35Dims, length: int, seed: int = 1, batch: int = 1) ->
     gen = torch.Generator()
     gen.manual_seed(seed)
     return torch.randint(0, dims.vocab, (batch, length), generator=gen, dtype=torch.int64)
+
+
+def vision_weight_shapes(vd) -> list[tuple[str, tuple[int, ...]]]:
+    """Hugging Face names and shapes of the vision tower (``model.visual.*`` of
+    ``Qwen3_5ForConditionalGeneration``) for a ``VisionDims``-like shape ``vd``."""
+    w, i = vd.width, vd.intermediate
+    mw = w * vd.merge * vd.merge
+    p = "model.visual."
+    out = [(p + "patch_embed.proj.weight", (w, vd.in_channels, vd.temporal_patch, vd.patch, vd.patch)),
+           (p + "patch_embed.proj.bias", (w,)),
+           (p + "pos_embed.weight", (vd.pos_side * vd.pos_side, w))]
+    for b in range(vd.depth):
+        q = f"{p}blocks.{b}."
+        out += [(q + "norm1.weight", (w,)), (q + "norm1.bias", (w,)), (q + "norm2.weight", (w,)),
+                (q + "norm2.bias", (w,)), (q + "attn.qkv.weight", (3 * w, w)), (q + "attn.qkv.bias", (3 * w,)),
+                (q + "attn.proj.weight", (w, w)), (q + "attn.proj.bias", (w,)),
+                (q + "mlp.linear_fc1.weight", (i, w)), (q + "mlp.linear_fc1.bias", (i,)),
+                (q + "mlp.linear_fc2.weight", (w, i)), (q + "mlp.linear_fc2.bias", (w,))]
+    out += [(p + "merger.norm.weight", (w,)), (p + "merger.norm.bias", (w,)),
+            (p + "merger.linear_fc1.weight", (mw, mw)), (p + "merger.linear_fc1.bias", (mw,)),
+            (p + "merger.linear_fc2.weight", (vd.out_width, mw)), (p + "merger.linear_fc2.bias", (vd.out_width,))]
+    return out
+
+
+def make_vision_weights(vd, seed: int = 0, device="cpu", std: float = 0.02,
+                        dtype=torch.bfloat16) -> dict[str, torch.Tensor]:
+    """Random-init vision weights ``{hf_name: tensor}``: ``N(0, std)`` in a fixed name order from one
+    generator, LayerNorm weights ``1 + N(0, std)`` (unit scale, as a LayerNorm starts)."""
+    gen = torch.Generator(device=device)
+    gen.manual_seed(seed)
+    weights: dict[str, torch.Tensor] = {}
+    for name, shape in vision_weight_shapes(vd):
+        t = torch.empty(shape, device=device, dtype=torch.float32)
+        t.normal_(0.0, std, generator=gen)
+        if "norm" in name and name.endswith(".weight"):
+            t += 1.0
+        weights[name] = t.to(dtype)
+    return weights
+
+
+def make_image(height: int, width: int, seed: int = 0, channels: int = 3) -> torch.Tensor:
+    """Uniform [0, 1) pixels ``[channels, height, width]`` fp32 on the CPU (already rescaled)."""
+    gen = torch.Generator()
+    gen.manual_seed(seed)
+    return torch.rand((channels, height, width), generator=gen, dtype=torch.float32)
