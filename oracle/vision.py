@@ -35,9 +35,10 @@ def residual_add_layer_norm(r: torch.Tensor, u: torch.Tensor, w, b, eps: float =
 
 
 def position_embed_add(hidden: torch.Tensor, table: torch.Tensor, idx: torch.Tensor, wts: torch.Tensor):
-    """kernels.py:1290-1336: ``bf16(hidden + bf16(sum_k w_k table[idx_k]))``, FP32 accumulation."""
+    """kernels.py:1290-1336: ``bf16(hidden + bf16(sum_k w_k table[idx_k]))``, FP32 accumulation
+    (roundings to ``hidden.dtype``: none in the FP32 reference mode)."""
     pos = (table[idx].float() * wts.float()[..., None]).sum(-2)
-    return (hidden.float() + pos.to(BF16).float()).to(BF16)
+    return (hidden.float() + pos.to(hidden.dtype).float()).to(hidden.dtype)
 
 
 def linspace(end: float, steps: int) -> torch.Tensor:
@@ -108,8 +109,8 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float) -
 
 
 def linear(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
-    """bf16 nn.Linear with bias: FP32 product + bias, one rounding."""
-    return (x.float() @ w.float().T + b.float()).to(BF16)
+    """nn.Linear with bias: FP32 product + bias, one rounding to ``x.dtype``."""
+    return (x.float() @ w.float().T + b.float()).to(x.dtype)
 
 
 def gelu_tanh(x: torch.Tensor) -> torch.Tensor:
@@ -120,7 +121,7 @@ def gelu(x: torch.Tensor) -> torch.Tensor:
     return torch.nn.functional.gelu(x.float()).to(x.dtype)
 
 
-def patchify(pixels: torch.Tensor, dims: VisionDims) -> torch.Tensor:
+def patchify(pixels: torch.Tensor, dims: VisionDims, dtype=BF16) -> torch.Tensor:
     """Qwen2-VL image processor layout for one image: fp32 [C, H, W] in [0,1) -> normalised bf16
     [(H/P)*(W/P), C*T*P*P], the frame repeated over the temporal patch."""
     C, H, W = pixels.shape
@@ -130,15 +131,18 @@ def patchify(pixels: torch.Tensor, dims: VisionDims) -> torch.Tensor:
     gh, gw = H // P, W // P
     x = x.reshape(1, T, C, gh // M, M, P, gw // M, M, P)
     x = x.permute(0, 3, 6, 4, 7, 2, 1, 5, 8)
-    return x.reshape(gh * gw, C * T * P * P).to(BF16)
+    return x.reshape(gh * gw, C * T * P * P).to(dtype)
 
 
 class VisionOracle:
-    """The reference's vision forward (integration.py:509-575 + merger) on the CPU."""
+    """The reference's vision forward (integration.py:509-575 + merger) on the CPU. With
+    ``dtype=torch.float32`` every bf16 rounding point is skipped (the weights keep their bf16
+    values): the exact forward that measures how far the bf16 forward itself drifts over depth."""
 
-    def __init__(self, weights: dict, dims: VisionDims, prefix: str = "model.visual."):
+    def __init__(self, weights: dict, dims: VisionDims, prefix: str = "model.visual.", dtype=BF16):
         self.d = dims
-        self.w = {k[len(prefix):]: v for k, v in weights.items() if k.startswith(prefix)}
+        self.dtype = dtype
+        self.w = {k[len(prefix):]: v.to(dtype) for k, v in weights.items() if k.startswith(prefix)}
         self.inv_freq = rope_inv_freq(dims.head_dim, dims.rope_theta)
 
     def forward(self, pixels: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
@@ -146,7 +150,7 @@ class VisionOracle:
         d, w = self.d, self.w
         _, H, W = pixels.shape
         gh, gw = H // d.patch, W // d.patch
-        patches = patchify(pixels, d)
+        patches = patchify(pixels, d, self.dtype)
         pw = w["patch_embed.proj.weight"].reshape(d.width, -1)
         hidden = linear(patches, pw, w["patch_embed.proj.bias"])
         idx, wts = interp_indices_weights(gh, gw, d.pos_side, d.merge)
@@ -168,7 +172,7 @@ class VisionOracle:
                 n = f"blocks.{i + 1}.norm1."
                 residual, normed = residual_add_layer_norm(residual, upd, w[n + "weight"], w[n + "bias"], d.eps)
             else:
-                residual = (residual.float() + upd.float()).to(BF16)
+                residual = (residual.float() + upd.float()).to(self.dtype)
         m = layer_norm(residual, w["merger.norm.weight"], w["merger.norm.bias"], d.eps)
         m = m.reshape(-1, d.width * d.merge * d.merge)
         m = gelu(linear(m, w["merger.linear_fc1.weight"], w["merger.linear_fc1.bias"]))
