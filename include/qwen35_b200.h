@@ -356,6 +356,8 @@ typedef struct {
   int32_t use_pdl;        /* launch decode kernels with programmatic dependent launch */
   int32_t prefill_tc;     /* prefill projections on tcgen05 (1) or warp-level MMA (0) */
   int32_t prefill_delta;  /* prefill DeltaNet scan: 0 = chunked WY form, 1 = sequential */
+  int32_t mrope_section[3]; /* interleaved M-RoPE sections (t, h, w) in frequency pairs, e.g.
+                               {11, 11, 10}; used by multimodal prefills with 3-axis positions */
   void* workspace;
   size_t workspace_bytes;
 } q35_decoder_desc;
@@ -368,6 +370,16 @@ void q35_decoder_destroy(q35_decoder* dec);
 /* Prefill `length` token ids (device int64) from an empty cache (evaluation_wrapper.py:354-363):
  * all layers, caches/states filled, greedy first token -> *token; cache_len = rope_pos = length. */
 int q35_decoder_prefill(q35_decoder* dec, const int64_t* ids, int64_t length, void* stream);
+/* Multimodal prefill (the text-model forward of a Qwen3.5 image + text request, integration.py:
+ * 390-504 with inputs_embeds from the vision tower): as q35_decoder_prefill, but the rows
+ * image_rows[i] (device int64 [n_image], each in [0, length)) of the input sequence take
+ * image_embeds[i] (bf16 [n_image, hidden]) instead of the embedding of their id, and the rotary
+ * positions are the 3-axis M-RoPE positions positions3 (device int64 [3, length]: temporal,
+ * height, width; interleaved per mrope_section) instead of 0..length-1. Afterwards
+ * cache_len = length and rope_pos = rope_next (the text position after the prompt, max + 1). */
+int q35_decoder_prefill_mm(q35_decoder* dec, const int64_t* ids, int64_t length, const void* image_embeds,
+                           const int64_t* image_rows, int64_t n_image, const int64_t* positions3,
+                           int64_t rope_next, void* stream);
 /* One greedy decode step (graph.py:51-79 body): consumes *token, appends to caches, writes the
  * next greedy token to *token (and token_log), advances cache_len / rope_pos. */
 int q35_decoder_decode_step(q35_decoder* dec, void* stream);

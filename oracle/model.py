@@ -97,6 +97,7 @@ class OracleDecoder:
                         for _ in range(d.n_attn)]
         self.v_cache = [torch.zeros_like(k) for k in self.k_cache]
         self.length = 0
+        self.rope_delta = 0  # text RoPE position minus cache row (non-zero after an image prompt)
 
     # ------------------------------------------------------------------ mixers
     def _delta(self, j, L, x):
@@ -138,14 +139,25 @@ class OracleDecoder:
         return self._apply(L["o_proj"], out)
 
     # ------------------------------------------------------------------ forward
-    def forward(self, ids: torch.Tensor, positions: torch.Tensor | None = None) -> torch.Tensor:
+    def forward(self, ids: torch.Tensor, positions: torch.Tensor | None = None,
+                image_embeds: torch.Tensor | None = None, image_rows: torch.Tensor | None = None) -> torch.Tensor:
         """Run ``ids [B, n]`` through the decoder, appending to the caches. Returns the final
-        normalised hidden states ``[B, n, H]`` (BF16)."""
+        normalised hidden states ``[B, n, H]`` (BF16).
+
+        Multimodal prompts (batch 1): rows ``image_rows`` of the input take ``image_embeds`` instead
+        of their token embeddings (Transformers' masked_scatter of the image features), and
+        ``positions`` may be the 3-axis M-RoPE positions ``[3, 1, n]``; later calls continue at the
+        text position after their maximum (Transformers' rope deltas)."""
         d = self.d
         b, n = ids.shape
         if positions is None:
-            positions = (torch.arange(n) + self.length)[None].expand(b, n)
+            positions = (torch.arange(n) + self.length + self.rope_delta)[None].expand(b, n)
+        else:
+            self.rope_delta = int(positions.max()) + 1 - (self.length + n)
         residual = self.embed[ids]
+        if image_embeds is not None:
+            residual = residual.clone()
+            residual[0, image_rows] = image_embeds.to(residual.dtype)
         normalized = ops.rms_norm(residual, self.layers[0]["in_ln"], d.eps)
         jd = ja = 0
         for i, L in enumerate(self.layers):

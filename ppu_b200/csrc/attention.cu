@@ -26,7 +26,8 @@ __global__ void __launch_bounds__(kD) qgkv_rope_kernel(
     const bf16* __restrict__ packed, const bf16* __restrict__ qw, const bf16* __restrict__ kw,
     const bf16* __restrict__ cos_t, const bf16* __restrict__ sin_t, const float* __restrict__ inv_freq,
     int64_t pos_base, bf16* __restrict__ q_out, bf16* __restrict__ k_out, bf16* __restrict__ v_out,
-    const int64_t* __restrict__ cache_start, int L, int Hq, int Hkv, int rot, int kv_len, float eps) {
+    const int64_t* __restrict__ cache_start, int L, int Hq, int Hkv, int rot, int kv_len, float eps,
+    const int64_t* __restrict__ pos3 = nullptr, int sec_h = 0, int sec_w = 0) {
   __shared__ float normed[kD];
   __shared__ float red[kD / 32];
   const int bt = blockIdx.x;  // b * L + t
@@ -41,7 +42,13 @@ __global__ void __launch_bounds__(kD) qgkv_rope_kernel(
       c = bf2f(cos_t[(int64_t)bt * rot + d]);
       s = bf2f(sin_t[(int64_t)bt * rot + d]);
     } else {
-      rope_cs(d, rot / 2, (float)(pos_base + start + t), inv_freq, c, s);
+      int64_t pos = pos_base + start + t;
+      if (pos3) {  // interleaved M-RoPE: frequency j takes the height / width axis at j % 3 == 1 / 2
+        const int j = d % (rot / 2);
+        const int axis = (j % 3 == 1 && j < 3 * sec_h) ? 1 : (j % 3 == 2 && j < 3 * sec_w) ? 2 : 0;
+        pos = pos3[(int64_t)axis * L + t];
+      }
+      rope_cs(d, rot / 2, (float)pos, inv_freq, c, s);
     }
   }
   for (int h = 0; h < Hq + Hkv; ++h) {
@@ -328,15 +335,17 @@ extern "C" int q35_qgkv_norm_rope(const void* packed, const void* q_weight, cons
 }
 
 // Prefill variant used by the decoder: RoPE from positions cache_start + t (text tokens).
+// With pos3 (int64 [3, seq_len], batch 1), the positions are 3-axis M-RoPE positions interleaved
+// by (sec_h, sec_w) frequency pairs (Transformers apply_interleaved_mrope).
 int q35_qgkv_rope_positions_launch(const void* packed, const void* q_weight, const void* k_weight,
                                    const float* inv_freq, void* q_out, void* k_out, void* v_out,
                                    const int64_t* cache_start, int64_t batch, int64_t seq_len, int64_t q_heads,
                                    int64_t kv_heads, int64_t rotary_dim, int64_t kv_len, float eps,
-                                   cudaStream_t stream) {
+                                   cudaStream_t stream, const int64_t* pos3, int sec_h, int sec_w) {
   qgkv_rope_kernel<false><<<(unsigned)(batch * seq_len), kD, 0, stream>>>(
       (const bf16*)packed, (const bf16*)q_weight, (const bf16*)k_weight, nullptr, nullptr, inv_freq, 0,
       (bf16*)q_out, (bf16*)k_out, (bf16*)v_out, cache_start, (int)seq_len, (int)q_heads, (int)kv_heads,
-      (int)rotary_dim, (int)kv_len, eps);
+      (int)rotary_dim, (int)kv_len, eps, pos3, sec_h, sec_w);
   return q35_check_launch("qgkv_rope_positions");
 }
 

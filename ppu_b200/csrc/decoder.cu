@@ -41,7 +41,7 @@ int q35_qgkv_rope_positions_launch(const void* packed, const void* q_weight, con
                                    const float* inv_freq, void* q_out, void* k_out, void* v_out,
                                    const int64_t* cache_start, int64_t batch, int64_t seq_len, int64_t q_heads,
                                    int64_t kv_heads, int64_t rotary_dim, int64_t kv_len, float eps,
-                                   cudaStream_t stream);
+                                   cudaStream_t stream, const int64_t* pos3, int sec_h, int sec_w);
 int q35_gated_rms_strided_launch(const void* x, const void* gate, int gate_group, int64_t gate_stride,
                                  const void* weight, void* out, int64_t rows, int64_t width, float eps,
                                  cudaStream_t stream);
@@ -340,13 +340,55 @@ extern "C" int q35_decoder_finish_step(q35_decoder* dec, const int64_t* keys, in
   return q35_lm_keys_finish_launch(keys + index, 1, d.token, (cudaStream_t)stream, false, &adv);
 }
 
+// Multimodal input rows: image_embeds[i] -> resid[rows[i]] (rows outside [0, L) are skipped).
+__global__ void image_rows_kernel(const bf16* __restrict__ embeds, const int64_t* __restrict__ rows,
+                                  bf16* __restrict__ resid, int64_t L, int64_t width) {
+  const int64_t r = rows[blockIdx.x];
+  if (r < 0 || r >= L) return;
+  const uint4* src = reinterpret_cast<const uint4*>(embeds + (int64_t)blockIdx.x * width);
+  uint4* dst = reinterpret_cast<uint4*>(resid + r * width);
+  for (int64_t c = threadIdx.x; c < width / 8; c += blockDim.x) dst[c] = src[c];
+}
+
+struct MmInputs {
+  const void* image_embeds = nullptr;
+  const int64_t* image_rows = nullptr;
+  int64_t n_image = 0;
+  const int64_t* pos3 = nullptr;
+  int64_t rope_next = -1;
+};
+
+static int prefill_impl(q35_decoder* dec, const int64_t* ids, int64_t length, const MmInputs& mm, cudaStream_t s);
+
 extern "C" int q35_decoder_prefill(q35_decoder* dec, const int64_t* ids, int64_t length, void* stream) {
   Q35_REQUIRE(dec && ids, "prefill: null argument");
+  return prefill_impl(dec, ids, length, MmInputs{}, (cudaStream_t)stream);
+}
+
+extern "C" int q35_decoder_prefill_mm(q35_decoder* dec, const int64_t* ids, int64_t length, const void* image_embeds,
+                                      const int64_t* image_rows, int64_t n_image, const int64_t* positions3,
+                                      int64_t rope_next, void* stream) {
+  Q35_REQUIRE(dec && ids, "prefill_mm: null argument");
+  Q35_REQUIRE(n_image >= 0 && n_image <= length && (n_image == 0 || (image_embeds && image_rows)),
+              "prefill_mm: %lld image rows need embeddings and row indices", (long long)n_image);
+  Q35_REQUIRE(!image_embeds || Q35_ALIGNED(image_embeds, 16), "prefill_mm: image embeddings 16-byte aligned");
+  Q35_REQUIRE(!positions3 || dec->d.mrope_section[1] + dec->d.mrope_section[2] > 0,
+              "prefill_mm: 3-axis positions need the decoder's mrope_section");
+  Q35_REQUIRE(rope_next >= 0, "prefill_mm: rope_next must be non-negative");
+  MmInputs mm;
+  mm.image_embeds = image_embeds;
+  mm.image_rows = image_rows;
+  mm.n_image = n_image;
+  mm.pos3 = positions3;
+  mm.rope_next = rope_next;
+  return prefill_impl(dec, ids, length, mm, (cudaStream_t)stream);
+}
+
+static int prefill_impl(q35_decoder* dec, const int64_t* ids, int64_t length, const MmInputs& mm, cudaStream_t s) {
   const q35_decoder_desc& d = dec->d;
   Q35_REQUIRE(length >= 1 && length <= d.max_prefill && length < d.max_len,
               "prefill: length %lld outside [1, %d] (cache %d)", (long long)length, d.max_prefill, d.max_len);
   const Buffers& B = dec->buf;
-  cudaStream_t s = (cudaStream_t)stream;
   const bool q8 = d.a8w8 != 0;
   const int64_t H = d.hidden, I = d.intermediate, Lt = length;
   const int64_t qgkv_rows = 2 * d.q_heads * d.head_dim + 2 * d.kv_heads * d.head_dim;
@@ -389,6 +431,11 @@ extern "C" int q35_decoder_prefill(q35_decoder* dec, const int64_t* ids, int64_t
   }
   Q35_TRY(q35_set_counters_launch(d.cache_len, d.rope_pos, 0, s));
   Q35_TRY(q35_embedding(ids, d.embed, B.p_resid, Lt, d.vocab, H, s));
+  if (mm.n_image > 0) {
+    image_rows_kernel<<<(unsigned)mm.n_image, 128, 0, s>>>((const bf16*)mm.image_embeds, mm.image_rows, B.p_resid,
+                                                         Lt, H);
+    Q35_TRY(q35_check_launch("prefill_mm image rows"));
+  }
   for (int i = 0; i < d.n_layers; ++i) {
     const q35_layer_desc& L = dec->layers[i];
     Q35_TRY(q35_rms_norm(B.p_resid, L.in_ln, B.p_norm, Lt, H, d.eps, s));
@@ -415,7 +462,7 @@ extern "C" int q35_decoder_prefill(q35_decoder* dec, const int64_t* ids, int64_t
       Q35_TRY(proj(B.p_norm, H, L.mix_in, L.mix_in_scale, B.p_packed, qgkv_rows, Q35_EPI_STORE));
       Q35_TRY(q35_qgkv_rope_positions_launch(B.p_packed, L.q_norm, L.k_norm, d.inv_freq, B.p_core, L.k_cache,
                                              L.v_cache, nullptr, 1, Lt, d.q_heads, d.kv_heads, d.rotary_dim,
-                                             d.max_len, d.eps, s));
+                                             d.max_len, d.eps, s, mm.pos3, d.mrope_section[1], d.mrope_section[2]));
       Q35_TRY(q35_prefill_attention(B.p_core, L.k_cache, L.v_cache, B.p_attn, 1, d.q_heads, d.kv_heads, Lt,
                                     d.max_len, 0, d.head_dim, 1.0f / sqrtf((float)d.head_dim), s));
       Q35_TRY(q35_attention_gate_mul(B.p_attn, B.p_packed, B.p_mix, Lt, adim, qgkv_rows, d.head_dim, s));
@@ -427,5 +474,7 @@ extern "C" int q35_decoder_prefill(q35_decoder* dec, const int64_t* ids, int64_t
   }
   Q35_TRY(q35_lm_head_launch(B.p_resid + (Lt - 1) * H, d.final_norm, d.embed, d.token, d.vocab, H, d.eps, B.lm_ws,
                              s, false, nullptr));
-  return q35_set_counters_launch(d.cache_len, d.rope_pos, Lt, s);
+  Q35_TRY(q35_set_counters_launch(d.cache_len, d.rope_pos, Lt, s));
+  if (mm.rope_next >= 0) Q35_TRY(q35_set_counters_launch(d.rope_pos, d.rope_pos, mm.rope_next, s));
+  return Q35_OK;
 }

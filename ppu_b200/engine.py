@@ -140,6 +140,8 @@ class Qwen35Engine:
         desc.use_pdl = int(use_pdl)
         desc.prefill_tc = int(prefill_tc)
         desc.prefill_delta = 0 if prefill_chunked else 1
+        for i, sec in enumerate(d.mrope_section):
+            desc.mrope_section[i] = sec
         size = L.load().q35_decoder_workspace_size(C.byref(desc))
         self.workspace = torch.zeros(size, device=dev, dtype=torch.uint8)
         desc.workspace, desc.workspace_bytes = self.workspace.data_ptr(), size
@@ -183,6 +185,32 @@ class Qwen35Engine:
             raise ValueError(f"prompt of {n} tokens exceeds max_prefill={self.max_prefill}")
         L.check(L.load().q35_decoder_prefill(self.handle, ids.data_ptr(), n, L.stream_of(self.device)),
                 "q35_decoder_prefill")
+        return self.token
+
+    def prefill_multimodal(self, ids: torch.Tensor, image_embeds: torch.Tensor, image_rows: torch.Tensor,
+                           positions3: torch.Tensor, rope_next: int) -> torch.Tensor:
+        """Prefill an image + text prompt from an empty cache: device ids ``[L]`` (the image rows'
+        ids are ignored), ``image_embeds`` bf16 ``[n, hidden]`` placed at rows ``image_rows``
+        (int64 ``[n]``), 3-axis M-RoPE ``positions3`` int64 ``[3, L]``; afterwards the decode
+        steps continue at RoPE position ``rope_next``. The greedy first token lands in
+        ``self.token``."""
+        ids = ids.reshape(-1)
+        n = ids.numel()
+        if not (ids.is_cuda and ids.dtype == torch.int64 and image_rows.dtype == torch.int64
+                and positions3.dtype == torch.int64):
+            raise ValueError("prefill_multimodal expects int64 ids, image rows and positions on the GPU")
+        if n > self.max_prefill:
+            raise ValueError(f"prompt of {n} tokens exceeds max_prefill={self.max_prefill}")
+        if positions3.shape != (3, n) or image_embeds.dim() != 2 or image_embeds.shape[1] != self.dims.hidden:
+            raise ValueError("positions3 must be [3, L] and image_embeds [n, hidden]")
+        if image_rows.numel() != image_embeds.shape[0] or image_embeds.dtype != BF16:
+            raise ValueError("one image row per bf16 image embedding")
+        dev = self.device
+        ids, image_rows = ids.to(dev), image_rows.to(dev).contiguous()
+        image_embeds, positions3 = image_embeds.to(dev).contiguous(), positions3.to(dev).contiguous()
+        L.check(L.load().q35_decoder_prefill_mm(self.handle, ids.data_ptr(), n, image_embeds.data_ptr(),
+                                                image_rows.data_ptr(), image_rows.numel(), positions3.data_ptr(),
+                                                int(rope_next), L.stream_of(dev)), "q35_decoder_prefill_mm")
         return self.token
 
     def decode_step(self) -> torch.Tensor:

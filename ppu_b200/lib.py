@@ -49,7 +49,8 @@ class DecoderDesc(C.Structure):
         ("max_len", I32), ("max_prefill", I32), ("a8w8", I32), ("eps", F32),
         ("layers", C.POINTER(LayerDesc)), ("embed", P), ("final_norm", P), ("inv_freq", P),
         ("token", P), ("cache_len", P), ("rope_pos", P), ("token_log", P), ("log_pos", P),
-        ("log_len", I32), ("use_pdl", I32), ("prefill_tc", I32), ("prefill_delta", I32), ("workspace", P), ("workspace_bytes", SZ),
+        ("log_len", I32), ("use_pdl", I32), ("prefill_tc", I32), ("prefill_delta", I32),
+        ("mrope_section", I32 * 3), ("workspace", P), ("workspace_bytes", SZ),
     ]
 
 
@@ -119,6 +120,7 @@ _SIGS = {
     "q35_decoder_create": (INT, [C.POINTER(DecoderDesc), C.POINTER(P)]),
     "q35_decoder_destroy": (None, [P]),
     "q35_decoder_prefill": (INT, [P, P, I64, P]),
+    "q35_decoder_prefill_mm": (INT, [P, P, I64, P, P, I64, P, I64, P]),
     "q35_decoder_decode_step": (INT, [P, P]),
     "q35_decoder_decode_layers": (INT, [P, P]),
     "q35_decoder_hidden": (P, [P]),
