@@ -65,6 +65,8 @@ def parse():
     ap.add_argument("--lm-shard", action="store_true",
                     help="N > 1: headline on the lock-step vocab-sharded decode instead of full replicas")
     ap.add_argument("--no-lm-shard-leg", action="store_true", help="N > 1: skip the lock-step sub-measurement")
+    ap.add_argument("--mm-requests", type=int, default=256, help="config-5 image + text requests (0: skip)")
+    ap.add_argument("--mm-new-tokens", type=int, default=16)
     return ap.parse_args()
 
 
@@ -352,6 +354,88 @@ def gate_up_roofline(eng, dims, dev, hbm_peak, peak_kind, a8w8: bool):
             "peak_kind": peak_kind}
 
 
+def multimodal_leg(eng, decode_graph, dims, dev, rank, world, args, tf_sust, peak_kind):
+    """``args.mm_requests`` seeded image + text requests spread over the ranks
+    (request i on rank i mod N): a 448 x 448 image through the 24-layer ViT and the 2x2 merger (196
+    tokens), prepended to 300 text tokens, a 496-token multimodal prefill and greedy decode to
+    ``args.mm_new_tokens`` tokens. Device-timed per request (inputs resident in HBM); the vision
+    tower's FLOPs over its time against the sustained bf16 peak; e2e through MultimodalEngine.generate."""
+    from ppu_b200 import replicas as R
+    from ppu_b200.config import VisionDims
+    from ppu_b200.multimodal import MultimodalEngine
+    from ppu_b200.synthetic import make_vision_weights
+    from ppu_b200.vision import VisionEngine
+
+    vd = VisionDims()
+    vw = make_vision_weights(vd, seed=1, device=dev)
+    vis = VisionEngine(vw, vd, max_image=(448, 448), device=dev)
+    del vw
+    n_text, n_new = 300, args.mm_new_tokens
+    mm = MultimodalEngine(None, None, dims, vd, image_hw=(448, 448), max_text=n_text, max_new_tokens=n_new,
+                          text_engine=eng, vision_engine=vis, decode_graph=decode_graph)
+    mine = R.requests_for_rank(args.mm_requests, world, rank)
+
+    def image(i):
+        g = torch.Generator(device=dev)
+        g.manual_seed(100_000 + i)
+        return torch.rand((3, 448, 448), generator=g, device=dev)
+
+    imgs = [image(i) for i in mine]
+    texts = [make_prompt(dims, n_text, seed=200_000 + i)[0].to(dev) for i in mine]
+
+    def request(j, ev=None):
+        if ev:
+            ev[0].record()
+        tokens = mm.encode_image(imgs[j])
+        if ev:
+            ev[1].record()
+        mm.prefill_prompt(tokens, texts[j])
+        if ev:
+            ev[2].record()
+        for _ in range(n_new - 1):
+            mm.decode_step()
+        if ev:
+            ev[3].record()
+
+    for j in range(min(3, len(mine))):
+        request(j)
+    torch.cuda.synchronize()
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in mine]
+    R.barrier()
+    torch.cuda.synchronize()
+    for j in range(len(mine)):
+        request(j, evs[j])
+    torch.cuda.synchronize()
+    R.barrier()
+    total_ms = R.max_over_ranks(evs[0][0].elapsed_time(evs[-1][3]), dev)
+    vis_ms = [e[0].elapsed_time(e[1]) for e in evs]
+    ttft_ms = [e[0].elapsed_time(e[2]) for e in evs]
+    dec_ms = [e[2].elapsed_time(e[3]) for e in evs]
+    mean = lambda xs: R.max_over_ranks(sum(xs) / len(xs), dev)  # noqa: E731
+    v_ms, t_ms, d_ms = mean(vis_ms), mean(ttft_ms), mean(dec_ms)
+    vflops = vd.linear_flops(448, 448)
+    host_img = torch.rand((3, 448, 448), generator=torch.Generator().manual_seed(300_000 + rank))
+    e_tok, e_ttft, e_el = mm.generate(host_img, make_prompt(dims, n_text, seed=310_000 + rank)[0], n_new)
+    e_el = R.max_over_ranks(e_el, dev)
+    return {
+        "workload": f"config5: {args.mm_requests} requests over {world} GPU(s): 448x448 image -> ViT (24 layers, "
+                    f"width 1024) -> 196 tokens + {n_text} text tokens, {n_new} greedy tokens each",
+        "requests_per_s": round(args.mm_requests / (total_ms / 1e3), 2),
+        "tok_per_s": round(args.mm_requests * n_new / (total_ms / 1e3), 1),
+        "ttft_ms_mean": round(t_ms, 3), "vision_ms_mean": round(v_ms, 3),
+        "decode_ms_per_token": round(d_ms / max(n_new - 1, 1), 4),
+        "vision_roofline": {"flops": vflops, "achieved_tflops": round(vflops / (v_ms / 1e3) / 1e12, 1),
+                            "peak_tflops": tf_sust, "frac": round(vflops / (v_ms / 1e3) / 1e12 / tf_sust, 4),
+                            "bound": "tensor", "peak_kind": f"{peak_kind} bf16 sustained"},
+        "decode": "lock-step, LM head vocab-sharded" if decode_graph is not None else "per-rank replicas",
+        "e2e": {"requests_per_s": round(world / e_el, 2), "ttft_ms": round(1000 * e_ttft, 3),
+                "tokens": len(e_tok), "h2d_bytes_per_request": 3 * 448 * 448 * 4 + n_text * 8,
+                "path": "MultimodalEngine.generate (host image + ids -> H2D, ViT graph, prefill, per-token D2H)"},
+        "data": "synthetic: seeded random-init ViT N(0,0.02) (LayerNorm 1+N), uniform [0,1) pixels, "
+                "uniform-random text ids",
+    }
+
+
 def main():
     args = parse()
     if args.impl == "reference":
@@ -506,6 +590,15 @@ def main():
         del gs, cg, kg
         sharded.release()
 
+    # ---- config 5: the multimodal request stream (replicas; at N > 1 also lock-step with the
+    # vocab-sharded LM head)
+    mm = mm_shard = None
+    if args.mm_requests > 0:
+        mm = multimodal_leg(eng, None, dims, dev, rank, world, args, tf_sust, peak_kind)
+        if sharded is not None and head is None:
+            mm_shard = multimodal_leg(eng, sharded.capture(1), dims, dev, rank, world, args, tf_sust, peak_kind)
+            sharded.release()
+
     cpu = None
     if weights_cpu is not None:
         threads = len(os.sched_getaffinity(0))
@@ -569,6 +662,10 @@ def main():
         line["a8w8"] = a8
     if shard is not None:
         line["lm_shard"] = shard
+    if mm is not None:
+        line["multimodal"] = mm
+    if mm_shard is not None:
+        line["multimodal_lm_shard"] = mm_shard
     if cpu is not None:
         line["cpu_baseline"] = cpu
     if rank == 0:

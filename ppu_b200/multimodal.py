@@ -40,23 +40,28 @@ def prompt_layout(vd: VisionDims, image_hw: tuple[int, int], n_text: int):
 
 
 class MultimodalEngine:
-    def __init__(self, text_weights: dict, vision_weights: dict, dims: Qwen35Dims = Qwen35Dims(),
+    def __init__(self, text_weights: dict | None, vision_weights: dict | None, dims: Qwen35Dims = Qwen35Dims(),
                  vd: VisionDims = VisionDims(), *, image_hw=(448, 448), max_text: int = 512, max_new_tokens: int = 16,
-                 a8w8: bool = False, device="cuda"):
+                 a8w8: bool = False, device="cuda", text_engine: Qwen35Engine | None = None,
+                 vision_engine: VisionEngine | None = None, decode_graph=None):
+        """Builds both engines from Hugging Face-named weight dicts, or takes existing ones
+        (``text_engine`` must hold a prompt of ``n_image + max_text`` tokens plus the decode steps;
+        ``decode_graph`` replaces the text engine's captured decode step, e.g. a lock-step graph)."""
         self.dims, self.vd, self.image_hw = dims, vd, tuple(image_hw)
-        self.vision = VisionEngine(vision_weights, vd, max_image=self.image_hw, device=device)
+        self.vision = vision_engine or VisionEngine(vision_weights, vd, max_image=self.image_hw, device=device)
         self.device = self.vision.device
         self.n_img = vd.merged_tokens(*self.image_hw)
         max_prompt = self.n_img + max_text
-        self.text = Qwen35Engine(text_weights, dims, a8w8=a8w8, max_len=cache_bucket(max_prompt, max_new_tokens),
-                                 max_prefill=max_prompt, device=self.device)
+        if text_engine is None:
+            text_engine = Qwen35Engine(text_weights, dims, a8w8=a8w8,
+                                       max_len=cache_bucket(max_prompt, max_new_tokens), max_prefill=max_prompt,
+                                       device=self.device)
+        elif text_engine.max_prefill < max_prompt or text_engine.max_len <= max_prompt + max_new_tokens:
+            raise ValueError("the text engine's cache is too short for the multimodal prompt")
+        self.text = text_engine
         self._vgraph = self.vision.capture(*self.image_hw)
-        self._dgraph = self.text.capture(1)
+        self._dgraph = decode_graph if decode_graph is not None else self.text.capture(1)
         self._layouts: dict[int, tuple[torch.Tensor, torch.Tensor, int]] = {}
-
-    def kernels_per_request(self, n_new: int) -> int:
-        return self.vision.kernels_per_encode() + (1 + 2 + self.dims.layers * 9 + 2) + \
-            (n_new - 1) * self.text.kernels_per_step
 
     def _layout(self, n_text: int):
         if n_text not in self._layouts:
@@ -64,12 +69,21 @@ class MultimodalEngine:
             self._layouts[n_text] = (rows.to(self.device), pos.to(self.device), nxt)
         return self._layouts[n_text]
 
-    def prefill(self, pixels: torch.Tensor, text_ids: torch.Tensor) -> torch.Tensor:
-        """Device pixels fp32 [3, H, W] and text ids int64 [n]: vision graph, then the multimodal
-        prefill; the first greedy token lands in ``text.token``."""
+    def encode_image(self, pixels: torch.Tensor) -> torch.Tensor:
+        """Device pixels fp32 [3, H, W] -> the merged image tokens (the vision graph's output
+        buffer, valid until the next encode)."""
         g, pix, tokens = self._vgraph
         pix.copy_(pixels, non_blocking=True)
         g.replay()
+        return tokens
+
+    def prefill(self, pixels: torch.Tensor, text_ids: torch.Tensor) -> torch.Tensor:
+        """Device pixels fp32 [3, H, W] and text ids int64 [n]: vision graph, then the multimodal
+        prefill; the first greedy token lands in ``text.token``."""
+        return self.prefill_prompt(self.encode_image(pixels), text_ids)
+
+    def prefill_prompt(self, tokens: torch.Tensor, text_ids: torch.Tensor) -> torch.Tensor:
+        """The text model's prefill of [image tokens, text ids] (image first)."""
         n_text = text_ids.numel()
         rows, pos, nxt = self._layout(n_text)
         ids = torch.cat((torch.full((self.n_img,), IMAGE_TOKEN_ID, device=self.device, dtype=torch.int64),
