@@ -499,6 +499,11 @@ void q35_vit_destroy(q35_vit* vit);
  * [(height/patch/merge)*(width/patch/merge), out_width]. */
 int q35_vit_encode(q35_vit* vit, const float* pixels, int64_t height, int64_t width, void* out,
                    void* stream);
+/* The same forward from the processor's patches (Transformers' pixel_values for one image,
+ * fp32 [grid_h*grid_w, in_channels*temporal_patch*patch^2] in merge-block order, the input of
+ * Qwen3_5VisionModel.forward that integration.py:576-637 patches). */
+int q35_vit_encode_patches(q35_vit* vit, const float* patches, int64_t grid_h, int64_t grid_w, void* out,
+                           void* stream);
 /* Device address of the final patch states [patches, width] of the last encode (pre-merger). */
 void* q35_vit_hidden(const q35_vit* vit);
 

@@ -118,7 +118,7 @@ class FusionConfig:
     residual_norm: bool = True
     swiglu: bool = True
     attention: bool = True
-    vision: bool = False
+    vision: bool = True
     release_original_weights: bool = True
     delta_projection_padding: int = 128
     delta_block_v: int = 8

@@ -685,20 +685,58 @@ extern "C" void q35_vit_destroy(q35_vit* v) { delete v; }
     if (_rc) return _rc;  \
   } while (0)
 
+// Processor output (fp32 patches) to the bf16 GEMM operand, 8 values per thread.
+__global__ void patch_cast_kernel(const float* __restrict__ in, bf16* __restrict__ out, int64_t n8) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n8) return;
+  const float4 a = reinterpret_cast<const float4*>(in)[2 * i], b = reinterpret_cast<const float4*>(in)[2 * i + 1];
+  __align__(16) bf16 o[8] = {f2bf(a.x), f2bf(a.y), f2bf(a.z), f2bf(a.w), f2bf(b.x), f2bf(b.y), f2bf(b.z), f2bf(b.w)};
+  reinterpret_cast<uint4*>(out)[i] = *reinterpret_cast<const uint4*>(o);
+}
+
+static int vit_blocks(q35_vit* vit, int64_t gh, int64_t gw, void* out, cudaStream_t s);
+
+extern "C" int q35_vit_encode_patches(q35_vit* vit, const float* patches, int64_t grid_h, int64_t grid_w, void* out,
+                                      void* stream) {
+  Q35_REQUIRE(vit && patches && out, "vit_encode_patches: null argument");
+  const q35_vit_desc& d = vit->d;
+  Q35_REQUIRE(grid_h > 0 && grid_w > 0 && grid_h % d.merge == 0 && grid_w % d.merge == 0,
+              "vit_encode_patches: grid %lldx%lld is not a multiple of the merge size", (long long)grid_h,
+              (long long)grid_w);
+  Q35_REQUIRE(grid_h * grid_w <= d.max_patches, "vit_encode_patches: %lld patches exceed max_patches %d",
+              (long long)(grid_h * grid_w), d.max_patches);
+  Q35_REQUIRE(Q35_ALIGNED(patches, 16), "vit_encode_patches: 16-byte aligned patches");
+  const int64_t F = (int64_t)d.in_channels * d.temporal_patch * d.patch * d.patch;
+  const int64_t n8 = grid_h * grid_w * F / 8;
+  patch_cast_kernel<<<(unsigned)((n8 + 255) / 256), 256, 0, (cudaStream_t)stream>>>(patches, vit->buf.patches, n8);
+  Q35_VTRY(q35_check_launch("vit patch cast"));
+  return vit_blocks(vit, grid_h, grid_w, out, (cudaStream_t)stream);
+}
+
 extern "C" int q35_vit_encode(q35_vit* vit, const float* pixels, int64_t height, int64_t width, void* out,
                               void* stream) {
   Q35_REQUIRE(vit && pixels && out, "vit_encode: null argument");
   const q35_vit_desc& d = vit->d;
   const VitBuffers& B = vit->buf;
-  cudaStream_t s = (cudaStream_t)stream;
   const int64_t P = d.patch, M = d.merge;
   Q35_REQUIRE(height % (P * M) == 0 && width % (P * M) == 0, "vit_encode: image size must be a multiple of %lld",
               (long long)(P * M));
-  const int64_t gh = height / P, gw = width / P, N = gh * gw, W = d.width;
-  Q35_REQUIRE(N <= d.max_patches, "vit_encode: %lld patches exceed max_patches %d", (long long)N, d.max_patches);
-  const int64_t F = (int64_t)d.in_channels * d.temporal_patch * P * P;
+  const int64_t gh = height / P, gw = width / P;
+  Q35_REQUIRE(gh * gw <= d.max_patches, "vit_encode: %lld patches exceed max_patches %d", (long long)(gh * gw),
+              d.max_patches);
   Q35_VTRY(q35_vision_patchify(pixels, B.patches, d.in_channels, height, width, P, d.temporal_patch, M,
                                d.pixel_mean, d.pixel_std, stream));
+  return vit_blocks(vit, gh, gw, out, (cudaStream_t)stream);
+}
+
+// Patch embedding (from vit->buf.patches), position embedding, the blocks and the merger.
+static int vit_blocks(q35_vit* vit, int64_t gh, int64_t gw, void* out, cudaStream_t s) {
+  const q35_vit_desc& d = vit->d;
+  const VitBuffers& B = vit->buf;
+  void* stream = s;
+  const int64_t P = d.patch, M = d.merge;
+  const int64_t N = gh * gw, W = d.width;
+  const int64_t F = (int64_t)d.in_channels * d.temporal_patch * P * P;
   Q35_VTRY(q35_gemm_tc_bias_launch(B.patches, d.patch_w, d.patch_b, B.upd, N, W, F, Q35_EPI_BIAS, s));
   Q35_VTRY(q35_vision_rope_table(d.rope_inv_freq, B.cos_t, B.sin_t, gh, gw, M, stream));
   Q35_VTRY(pos_embed_norm_launch(B.upd, d.pos_table, d.blocks[0].norm1_w, d.blocks[0].norm1_b, B.resid, B.norm, N, W,

@@ -6,8 +6,9 @@ the reference's names, arguments and result fields. Backends:
 * ``"synthetic"``: a seeded random-init Qwen3.5-2B-shape text decoder on the GPU, run by the fully
   fused ``Qwen35Engine`` (5 kernels per layer, CUDA-graph decode). There is no tokenizer or
   checkpoint in this setting, so ``prompt`` may be a list of token ids (or text, mapped byte-wise
-  to ids) and the text of the result lists the generated ids. The image is not used: the vision
-  tower is outside this package.
+  to ids) and the text of the result lists the generated ids. An ``image`` (fp32 ``[3, H, W]``
+  rescaled to [0, 1)) goes through a seeded random-init vision tower (``MultimodalEngine``: ViT
+  graph, image tokens prepended to the prompt, M-RoPE prefill).
 * ``"transformers"``: a local Hugging Face Qwen3.5 checkpoint directory, patched with
   ``integration.apply_fusions``; greedy decode through ``graph.GreedyDecodeGraph`` over length-
   bucketed ``StaticCache`` objects, as the reference does (evaluation_wrapper.py:307-441).
@@ -85,6 +86,7 @@ class VLMModel:
         from .synthetic import make_weights
 
         self._dims = dims or Qwen35Dims()
+        self._seed = seed
         weights = make_weights(self._dims, seed=seed, device=self.device)
         self._engine = Qwen35Engine(weights, self._dims, a8w8=a8w8, max_len=max_len, max_prefill=max_prefill,
                                     device=self.device)
@@ -111,7 +113,7 @@ class VLMModel:
     def generate_with_metrics(self, *, image=None, prompt, choices: dict[str, str] | None = None,
                               generation_config: GenerationConfig, sample_id: str = "") -> GenerationResult:
         if self._backend_name == "synthetic":
-            return self._generate_synthetic(prompt, generation_config)
+            return self._generate_synthetic(prompt, generation_config, image)
         if self._backend_name == "transformers":
             return self._generate_fused_greedy(prompt, generation_config)
         return self._generate_with_dummy(prompt=prompt, choices=choices or {}, generation_config=generation_config,
@@ -126,20 +128,46 @@ class VLMModel:
             return list(self._tokenizer(prompt)["input_ids"])
         return [b % vocab for b in str(prompt).encode("utf-8")] or [0]
 
-    def _generate_synthetic(self, prompt, generation_config: GenerationConfig) -> GenerationResult:
+    def _multimodal(self, image_hw):
+        """The image path of the synthetic backend: a seeded random-init vision tower (config 5's
+        ViT) sharing the text engine, built on the first image of a size."""
+        from .config import VisionDims
+        from .multimodal import MultimodalEngine
+        from .synthetic import make_vision_weights
+        from .vision import VisionEngine
+
+        mm = getattr(self, "_mm", None)
+        if mm is None or mm.image_hw != tuple(image_hw):
+            vd = VisionDims(out_width=self._dims.hidden)
+            vis = VisionEngine(make_vision_weights(vd, seed=self._seed + 1, device=self.device), vd,
+                               max_image=tuple(image_hw), device=self.device)
+            mm = MultimodalEngine(None, None, self._dims, vd, image_hw=tuple(image_hw),
+                                  max_text=self._engine.max_prefill - vd.merged_tokens(*image_hw),
+                                  max_new_tokens=1, text_engine=self._engine, vision_engine=vis,
+                                  decode_graph=self._engine.capture(GRAPH_STEPS))
+            self._mm = mm
+        return mm
+
+    def _generate_synthetic(self, prompt, generation_config: GenerationConfig, image=None) -> GenerationResult:
         import torch
 
         ids = self._prompt_ids(prompt, self._dims.vocab)
         max_new = max(1, int(generation_config.max_new_tokens))
         host = torch.tensor(ids, dtype=torch.int64).pin_memory()
         start = time.perf_counter()
-        tokens, ttft, elapsed = self._engine.generate(host, max_new, use_graph=True, graph_steps=GRAPH_STEPS)
+        if image is not None:
+            # image: fp32 [3, H, W] in [0, 1) (the processor's rescaled pixels), H and W multiples of 32
+            pixels = torch.as_tensor(image, dtype=torch.float32)
+            mm = self._multimodal(pixels.shape[1:])
+            tokens, ttft, elapsed = mm.generate(pixels, host, max_new)
+        else:
+            tokens, ttft, elapsed = self._engine.generate(host, max_new, use_graph=True, graph_steps=GRAPH_STEPS)
         end = time.perf_counter()
         return GenerationResult(
             text=" ".join(str(t) for t in tokens), token_count=len(tokens), ttft_seconds=ttft,
             elapsed_seconds=end - start,
             meta={"backend": "b200-fused-synthetic", "cuda_graph": len(tokens) > 1, "cuda_graph_steps": GRAPH_STEPS,
-                  "prompt_tokens": len(ids), "a8w8": self._engine.a8w8,
+                  "prompt_tokens": len(ids), "a8w8": self._engine.a8w8, "image": image is not None,
                   "kernels_per_decode_step": self._engine.kernels_per_step})
 
     def _generate_fused_greedy(self, prompt, generation_config: GenerationConfig) -> GenerationResult:

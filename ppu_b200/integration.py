@@ -132,7 +132,7 @@ def _proj(x: torch.Tensor, weight: torch.Tensor, q8: torch.Tensor | None = None,
     return out.reshape(*lead, out.shape[-1])
 
 
-def _install(module: torch.nn.Module, fast, config: FusionConfig, primary: str) -> bool:
+def _install(module: torch.nn.Module, fast, config: FusionConfig, primary: str, accept=None) -> bool:
     """Routes ``module.forward`` through ``fast(self, *args, **kwargs)``. The tensor named
     ``primary`` (or the first positional argument) must be a BF16 CUDA tensor; otherwise the call
     raises ``ValueError``, or, with ``config.eager_fallback``, runs the module's original
@@ -146,7 +146,9 @@ def _install(module: torch.nn.Module, fast, config: FusionConfig, primary: str) 
         x = args[0] if args else kwargs.get(primary)
         if x is None and primary == "input_ids":
             x = kwargs.get("inputs_embeds")
-        if isinstance(x, torch.Tensor) and (x.dtype == torch.long or _is_fast_tensor(x)):
+        if accept is not None and isinstance(x, torch.Tensor) and accept(x):
+            return fast(self, *args, **kwargs)
+        if accept is None and isinstance(x, torch.Tensor) and (x.dtype == torch.long or _is_fast_tensor(x)):
             if x.dtype != torch.long or x.is_cuda:
                 return fast(self, *args, **kwargs)
         if config.eager_fallback:
@@ -347,15 +349,66 @@ def _patch_text_model(text_model: torch.nn.Module, config: FusionConfig) -> None
     _install(text_model, forward, config, "input_ids")
 
 
+def _vision_dims(cfg) -> "VisionDims":
+    from .config import VisionDims
+
+    side = int(round(cfg.num_position_embeddings ** 0.5))
+    if side * side != cfg.num_position_embeddings:
+        raise ValueError("the vision position table must be square")
+    return VisionDims(depth=cfg.depth, width=cfg.hidden_size, heads=cfg.num_heads,
+                      intermediate=cfg.intermediate_size, in_channels=cfg.in_channels, patch=cfg.patch_size,
+                      temporal_patch=cfg.temporal_patch_size, merge=cfg.spatial_merge_size,
+                      out_width=cfg.out_hidden_size, pos_side=side)
+
+
+def _patch_vision_model(visual: torch.nn.Module, config: FusionConfig) -> bool:
+    """integration.py:509-637: the vision forward of Qwen3_5VisionModel on this package's ViT
+    runner (q35_vit_encode_patches: tcgen05 projections, fused position embedding + norm, QKV RoPE,
+    attention, residual + norm, merger), one image (one ``grid_thw`` row) at a time, over the
+    module's own weights (no copies). Video grids (t > 1) raise unless ``eager_fallback``."""
+    vcfg = visual.config
+    if vcfg.hidden_act != "gelu_pytorch_tanh" or vcfg.hidden_size // vcfg.num_heads != 64:
+        return False
+    vd = _vision_dims(vcfg)
+    state = {k: v for k, v in visual.state_dict().items() if "inv_freq" not in k}
+
+    def forward(self, hidden_states, grid_thw, **kwargs):
+        from transformers.modeling_outputs import BaseModelOutputWithPooling
+
+        from .vision import VisionEngine
+
+        grids = [tuple(int(v) for v in row) for row in grid_thw.tolist()]
+        if any(t != 1 for t, _, _ in grids):
+            if config.eager_fallback:
+                return self._fused_original_forward(hidden_states, grid_thw, **kwargs)
+            raise ValueError("fused vision tower: video inputs (t > 1) need FusionConfig(eager_fallback=True)")
+        need = max(h * w for _, h, w in grids)
+        eng = getattr(self, "_q35_vit", None)
+        if eng is None or eng.max_patches < need:
+            eng = VisionEngine(state, vd, max_image=(vd.patch * vd.merge, vd.patch * vd.merge),
+                               device=hidden_states.device, prefix="", max_patches=need)
+            self._q35_vit = eng
+        hidden, merged, off = [], [], 0
+        for _, h, w in grids:
+            n = h * w
+            merged.append(eng.encode_patches(hidden_states[off:off + n].float(), h, w))
+            hidden.append(eng.hidden(n).clone())
+            off += n
+        return BaseModelOutputWithPooling(last_hidden_state=torch.cat(hidden), pooler_output=torch.cat(merged))
+
+    return _install(visual, forward, config, "hidden_states", accept=lambda x: x.is_cuda and x.is_floating_point())
+
+
 def apply_fusions(model: torch.nn.Module, config: FusionConfig | None = None) -> dict:
-    """Pack weights and install all enabled inference-only fast paths (integration.py:778-814).
-    Vision patches of the reference are out of scope here (``FusionConfig.vision`` must be False)."""
+    """Pack weights and install all enabled inference-only fast paths (integration.py:778-814),
+    the vision tower's included when the model has one (``FusionConfig.vision``)."""
     config = config or FusionConfig()
     if model.training:
         raise ValueError("apply_fusions requires model.eval()")
-    if config.vision:
-        raise ValueError("the vision-tower fusions are not part of this package")
     stats = _pack_linear_weights(model, config)
+    visual = getattr(getattr(model, "model", None), "visual", None)
+    if config.vision and visual is not None:
+        stats["vision"] = int(_patch_vision_model(visual, config))
     text = _text_model(model)
     for layer in text.layers:
         if config.rms_norm:

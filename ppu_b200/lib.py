@@ -144,6 +144,7 @@ _SIGS = {
     "q35_vit_create": (INT, [C.POINTER(VitDesc), C.POINTER(P)]),
     "q35_vit_destroy": (None, [P]),
     "q35_vit_encode": (INT, [P, P, I64, I64, P, P]),
+    "q35_vit_encode_patches": (INT, [P, P, I64, I64, P, P]),
     "q35_vit_hidden": (P, [P]),
     "q35_decoder_probe_bytes": (SZ, [P]),
     "q35_decoder_persistent_error": (INT, []),

@@ -43,7 +43,7 @@ def vision_positions(vd: VisionDims, height: int, width: int, start: int = 0) ->
 
 class VisionEngine:
     def __init__(self, weights: dict, vd: VisionDims = VisionDims(), *, max_image=(448, 448), device="cuda",
-                 prefix: str = "model.visual."):
+                 prefix: str = "model.visual.", max_patches: int | None = None):
         L.load()
         dev = torch.device(device)
         if dev.type != "cuda":
@@ -74,7 +74,7 @@ class VisionEngine:
             b.fc2_w, b.fc2_b = keep(w(p + "mlp.linear_fc2.weight")), keep(w(p + "mlp.linear_fc2.bias"))
         self.inv_freq = vision_rope_inv_freq(vd.head_dim, vd.rope_theta).to(dev)
         gh, gw = vd.grid(*max_image)
-        self.max_patches = gh * gw
+        self.max_patches = max(gh * gw, max_patches or 0)
         d = L.VitDesc()
         d.depth, d.width, d.heads, d.intermediate = vd.depth, vd.width, vd.heads, vd.intermediate
         d.in_channels, d.patch, d.temporal_patch, d.merge = vd.in_channels, vd.patch, vd.temporal_patch, vd.merge
@@ -120,6 +120,23 @@ class VisionEngine:
             out = torch.empty((n, self.vd.out_width), device=self.device, dtype=BF16)
         L.check(L.load().q35_vit_encode(self.handle, pixels.data_ptr(), h, wd, out.data_ptr(),
                                         L.stream_of(self.device)), "q35_vit_encode")
+        return out
+
+    def encode_patches(self, patches: torch.Tensor, grid_h: int, grid_w: int,
+                       out: torch.Tensor | None = None) -> torch.Tensor:
+        """One image from the processor's patches (fp32 ``[grid_h*grid_w, C*T*P*P]``, the
+        ``pixel_values`` Transformers feeds Qwen3_5VisionModel) -> merged tokens bf16."""
+        n = grid_h * grid_w
+        if patches.shape != (n, self.vd.patch_features) or patches.device != self.device:
+            raise ValueError(f"patches must be [{n}, {self.vd.patch_features}] on the engine's device")
+        if patches.dtype != torch.float32:
+            raise ValueError("patches must be fp32 (the processor's pixel_values)")
+        patches = patches.contiguous()
+        if out is None:
+            m2 = self.vd.merge * self.vd.merge
+            out = torch.empty((n // m2, self.vd.out_width), device=self.device, dtype=BF16)
+        L.check(L.load().q35_vit_encode_patches(self.handle, patches.data_ptr(), grid_h, grid_w, out.data_ptr(),
+                                                L.stream_of(self.device)), "q35_vit_encode_patches")
         return out
 
     def hidden(self, n_patches: int) -> torch.Tensor:

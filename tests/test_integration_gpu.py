@@ -116,3 +116,60 @@ def test_dummy_backend_matches_reference_contract():
     res = vm.generate_with_metrics(image=None, prompt="q", choices={"A": "a", "B": "b"},
                                    generation_config=GenerationConfig(max_new_tokens=8), sample_id="x")
     assert res.meta["backend"] == "dummy" and res.text.startswith("Answer: ")
+
+
+def test_apply_fusions_vision_tower_matches_eager():
+    """integration.py:509-637 drop-in: Transformers' Qwen3_5VisionModel forward replaced by the ViT
+    runner over the module's own weights, against the unpatched eager forward on the GPU."""
+    from pathlib import Path
+
+    from transformers.models.qwen3_5 import modeling_qwen3_5 as hf
+    from transformers.models.qwen3_5.configuration_qwen3_5 import Qwen3_5VisionConfig
+
+    from ppu_b200.config import VisionDims
+    from ppu_b200.integration import _patch_vision_model
+    from ppu_b200.synthetic import make_vision_weights
+
+    from .helpers import rel_err
+
+    g = torch.load(Path(__file__).parent / "golden" / "golden_vision.pt", weights_only=False)
+    c = g["vision_model"]
+    vd = VisionDims(**c["dims"])
+    cfg = Qwen3_5VisionConfig(depth=vd.depth, hidden_size=vd.width, num_heads=vd.heads,
+                              intermediate_size=vd.intermediate, out_hidden_size=vd.out_width,
+                              num_position_embeddings=vd.pos_side ** 2, hidden_act="gelu_pytorch_tanh")
+    cfg._attn_implementation = "eager"
+    visual = hf.Qwen3_5VisionModel(cfg).to(torch.bfloat16)
+    visual.load_state_dict({k[len("model.visual."):]: v for k, v in make_vision_weights(vd, seed=c["seed"]).items()},
+                           strict=False)
+    visual = visual.cuda().eval()
+    visual.rotary_pos_emb.inv_freq = (1.0 / (10000.0 ** (torch.arange(0, 32, 2, dtype=torch.float) / 32))).cuda()
+    pix = g["patchify"]["pixel_values"].cuda().to(torch.bfloat16)
+    grid = g["patchify"]["grid_thw"].cuda()
+    two = torch.cat((pix, pix)), torch.cat((grid, grid))  # two images in one call
+    with torch.inference_mode():
+        want = visual(*two)
+        assert _patch_vision_model(visual, FusionConfig())
+        got = visual(*two)
+    assert got.pooler_output.shape == want.pooler_output.shape == (12, vd.out_width)
+    assert rel_err(got.last_hidden_state, want.last_hidden_state) < 1e-2
+    assert rel_err(got.pooler_output, want.pooler_output) < 1e-2
+    assert torch.equal(got.pooler_output[:6], got.pooler_output[6:])
+
+
+def test_vlmmodel_synthetic_backend_with_an_image():
+    """generate_with_metrics(image=...) on the synthetic backend: the ViT + M-RoPE prefill path;
+    the same request twice gives the same tokens, and the image changes the answer's context."""
+    from ppu_b200.synthetic import make_image
+
+    dims = Qwen35Dims(layers=4, vocab=4096)
+    vm = VLMModel(backend="synthetic", dims=dims, seed=5, max_len=512, max_prefill=256)
+    prompt = make_prompt(dims, 60, seed=7)[0].tolist()
+    img = make_image(64, 96, seed=8)
+    cfg = GenerationConfig(max_new_tokens=10)
+    res = vm.generate_with_metrics(image=img, prompt=prompt, generation_config=cfg)
+    assert res.meta["image"] and res.token_count == 10 and 0 < res.ttft_seconds < res.elapsed_seconds
+    again = vm.generate_with_metrics(image=img, prompt=prompt, generation_config=cfg)
+    assert again.text == res.text
+    text_only = vm.generate_with_metrics(image=None, prompt=prompt, generation_config=cfg)
+    assert not text_only.meta["image"]
