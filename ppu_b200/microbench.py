@@ -290,6 +290,79 @@ def run(kernels: list[str], reps: int, layers: int = 24, a8w8: bool = False):
             torch.cuda.profiler.stop()
             report("prefill_one", 0.0)
             del eng
+        elif name in ("vit", "vit_one"):
+            # config 5's vision tower on one 448 x 448 image (CUDA-graph replay); vit_one: one warm
+            # encode between cudaProfilerStart / Stop, the launch-list target
+            from .config import VisionDims
+            from .synthetic import make_image, make_vision_weights
+            from .vision import VisionEngine
+            vd = VisionDims()
+            eng = VisionEngine(make_vision_weights(vd, seed=1, device=dev), vd, device=dev)
+            graph, pix, _ = eng.capture(448, 448)
+            pix.copy_(make_image(448, 448, seed=2).to(dev))
+            for _ in range(2):
+                graph.replay()
+            torch.cuda.synchronize()
+            if name == "vit_one":
+                torch.cuda.profiler.start()
+                graph.replay()
+                torch.cuda.synchronize()
+                torch.cuda.profiler.stop()
+                report("vit_one", 0.0)
+            else:
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                for _ in range(max(1, reps)):
+                    graph.replay()
+                e1.record()
+                torch.cuda.synchronize()
+                report("vit_448", e0.elapsed_time(e1) / 1000.0 / max(1, reps), flops=vd.linear_flops(448, 448))
+            del eng
+        elif name == "vision_attn":
+            q, k, v = (torch.randn(1, 16, 784, 64, device=dev, generator=g).to(torch.bfloat16) for _ in range(3))
+            o = torch.empty(784, 1024, device=dev, dtype=torch.bfloat16)
+
+            def va(i):
+                L.call("q35_vision_attention", q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), 784, 16, 64,
+                       0.125, L.stream_of(dev))
+            report("vision_attn_784x16", _time(va, reps), flops=4 * 16 * 64 * 784 * 784)
+        elif name == "vision_gemm":
+            for (m, n, k, epi, tag) in ((784, 3072, 1024, L.EPI_BIAS, "qkv"), (784, 4096, 1024, L.EPI_BIAS_GELU_TANH,
+                                        "fc1"), (784, 1024, 4096, L.EPI_BIAS, "fc2"), (784, 1024, 1024, L.EPI_BIAS,
+                                        "proj"), (196, 4096, 4096, L.EPI_BIAS_GELU, "merger_fc1")):
+                a = torch.randn(m, k, device=dev, generator=g).to(torch.bfloat16)
+                ws = [w(n, k) for _ in range(4)]
+                bias = torch.zeros(n, device=dev, dtype=torch.bfloat16)
+                y = torch.empty(m, n, device=dev, dtype=torch.bfloat16)
+
+                def gm(i, a=a, ws=ws, bias=bias, y=y, m=m, n=n, k=k, epi=epi):
+                    L.call("q35_gemm_tc_bias", a.data_ptr(), ws[i % 4].data_ptr(), bias.data_ptr(), y.data_ptr(), m, n,
+                           k, epi, L.stream_of(dev))
+                report(f"vision_gemm_{tag}_{m}x{n}x{k}", _time(gm, reps), flops=2 * m * n * k)
+        elif name in ("mm_request_one",):
+            # one warm config-5 request (ViT graph + 496-token multimodal prefill + 15 decode steps)
+            # between cudaProfilerStart / Stop: the launch-list target
+            from .config import Qwen35Dims, VisionDims
+            from .multimodal import MultimodalEngine
+            from .synthetic import make_image, make_prompt, make_vision_weights, make_weights
+            dims, vd = Qwen35Dims(), VisionDims()
+            mm = MultimodalEngine(make_weights(dims, seed=0, device=dev), make_vision_weights(vd, seed=1, device=dev),
+                                  dims, vd, max_text=300, max_new_tokens=16, device=dev)
+            img, ids = make_image(448, 448, seed=2).to(dev), make_prompt(dims, 300, seed=3)[0].to(dev)
+
+            def req():
+                mm.prefill(img, ids)
+                for _ in range(15):
+                    mm.decode_step()
+            for _ in range(2):
+                req()
+            torch.cuda.synchronize()
+            torch.cuda.profiler.start()
+            req()
+            torch.cuda.synchronize()
+            torch.cuda.profiler.stop()
+            report("mm_request_one", 0.0)
+            del mm
         elif name in ("persistent_trace", "persistent_small"):
             from .config import Qwen35Dims
             from .engine import Qwen35Engine
