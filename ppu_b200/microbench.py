@@ -331,7 +331,7 @@ def run(kernels: list[str], reps: int, layers: int = 24, a8w8: bool = False):
                                         "fc1"), (784, 1024, 4096, L.EPI_BIAS, "fc2"), (784, 1024, 1024, L.EPI_BIAS,
                                         "proj"), (196, 4096, 4096, L.EPI_BIAS_GELU, "merger_fc1")):
                 a = torch.randn(m, k, device=dev, generator=g).to(torch.bfloat16)
-                ws = [w(n, k) for _ in range(4)]
+                ws = [w(n, k)[0] for _ in range(4)]
                 bias = torch.zeros(n, device=dev, dtype=torch.bfloat16)
                 y = torch.empty(m, n, device=dev, dtype=torch.bfloat16)
 
