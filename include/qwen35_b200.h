@@ -358,6 +358,10 @@ typedef struct {
   int32_t prefill_delta;  /* prefill DeltaNet scan: 0 = chunked WY form, 1 = sequential */
   int32_t mrope_section[3]; /* interleaved M-RoPE sections (t, h, w) in frequency pairs, e.g.
                                {11, 11, 10}; used by multimodal prefills with 3-axis positions */
+  int32_t batch;          /* requests decoded in lock step (1..8; 0 means 1). With batch > 1 every
+                             state / cache tensor has a leading batch dimension, token[] holds one
+                             token per request, and all requests share cache_len / rope_pos (equal
+                             prompt lengths); bf16 weights only */
   void* workspace;
   size_t workspace_bytes;
 } q35_decoder_desc;
@@ -379,7 +383,17 @@ int q35_decoder_prefill(q35_decoder* dec, const int64_t* ids, int64_t length, vo
  * cache_len = length and rope_pos = rope_next (the text position after the prompt, max + 1). */
 int q35_decoder_prefill_mm(q35_decoder* dec, const int64_t* ids, int64_t length, const void* image_embeds,
                            const int64_t* image_rows, int64_t n_image, const int64_t* positions3,
-                           int64_t rope_next, void* stream);
+                           int64_t rope_next, int64_t slot, void* stream);
+/* Batched decoders: prefill request slot `slot` (0 <= slot < batch) -- its states, caches and
+ * token[slot]; cache_len / rope_pos are set to `length`, so every slot of a batch is prefilled
+ * with the same length before the batch decodes (evaluation_wrapper.py:338-341 pads a batch to
+ * one cache bucket the same way). q35_decoder_prefill is slot 0. */
+int q35_decoder_prefill_slot(q35_decoder* dec, const int64_t* ids, int64_t length, int64_t slot, void* stream);
+/* The decoder's batched projection (no counterpart in the reference, whose decode is batch 1):
+ * q35_gemv for `batch` <= 8 input vectors [batch, k] / outputs [batch, n_out] at once, the weights
+ * streamed once; bf16, k 2048 (NORM / EMBED + STORE, NORM + SWIGLU, PLAIN + RESIDUAL) or 6144
+ * (PLAIN + RESIDUAL). */
+int q35_gemv_batch(const q35_gemv_desc* desc, int64_t batch, void* stream);
 /* One greedy decode step (graph.py:51-79 body): consumes *token, appends to caches, writes the
  * next greedy token to *token (and token_log), advances cache_len / rope_pos. */
 int q35_decoder_decode_step(q35_decoder* dec, void* stream);

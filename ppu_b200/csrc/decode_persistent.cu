@@ -909,6 +909,7 @@ size_t q35_pk_workspace_bytes(const q35_decoder_desc& d) {
 // Empty when the model fits the persistent kernel's built-in shapes, else the reason.
 const char* q35_pk_unsupported(const q35_decoder_desc& d) {
   if (d.a8w8) return "A8W8 weights use the per-op decode path";
+  if (d.batch > 1) return "batched decoding uses the per-op decode path";
   if (d.hidden != 2048 || d.intermediate != 6144) return "built for hidden 2048 / intermediate 6144";
   if (d.head_dim != 256 || d.q_heads != 8 || d.kv_heads != 2 || d.rotary_dim > 256)
     return "built for 8 query / 2 KV heads of 256";

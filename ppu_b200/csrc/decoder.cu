@@ -19,6 +19,8 @@
 #include "common.cuh"
 
 int q35_gemv_launch(const q35_gemv_desc* d, cudaStream_t s, bool pdl);
+int q35_gemv_batch_launch(const q35_gemv_desc* d, int64_t batch, cudaStream_t s, bool pdl);
+extern "C" size_t q35_lm_shard_workspace_size(void);
 int q35_lm_head_launch(const void* hidden, const void* norm_weight, const void* weight, int64_t* token_out,
                        int64_t vocab, int64_t k, float eps, void* ws, cudaStream_t s, bool pdl,
                        const q35_step_counters* adv);
@@ -84,6 +86,8 @@ struct Buffers {
   bf16* act;          // SwiGLU output [intermediate]
   void* attn_ws;
   void* lm_ws;
+  void* lm_keys_ws;   // batched decode: the shard top-1 workspace (keys reduced over the vocabulary)
+  int64_t* lm_keys;   // batched decode: [batch] reduced keys
   void* pk_ws;        // persistent decode step: op table, attention partials, barrier words
   // prefill
   bf16* p_resid;      // [L, H]
@@ -110,12 +114,15 @@ Buffers carve(const q35_decoder_desc& d, void* base, size_t* total) {
                            : (int64_t)d.q_heads * d.head_dim;
   const int64_t conv_dim = (int64_t)d.lin_heads * (2 * d.lin_dk + d.lin_dv);
   const int64_t L = d.max_prefill;
+  const int64_t nb = d.batch > 1 ? d.batch : 1;
   b.lm_ws = c.take<char>(256);  // LM head ticket + key (must start zeroed)
-  b.resid = c.take<bf16>(d.hidden);
-  b.mix_in_out = c.take<bf16>(rows_in);
-  b.mix_out = c.take<bf16>(mixw);
-  b.act = c.take<bf16>(d.intermediate);
-  b.attn_ws = c.take<char>(q35_attn_decode_workspace_size(1, d.q_heads, d.kv_heads, d.head_dim, d.max_len));
+  b.lm_keys_ws = c.take<char>(q35_lm_shard_workspace_size());  // batched LM head keys (zeroed, left zeroed)
+  b.lm_keys = c.take<int64_t>(8);
+  b.resid = c.take<bf16>(nb * d.hidden);
+  b.mix_in_out = c.take<bf16>(nb * rows_in);
+  b.mix_out = c.take<bf16>(nb * mixw);
+  b.act = c.take<bf16>(nb * d.intermediate);
+  b.attn_ws = c.take<char>(q35_attn_decode_workspace_size(nb, d.q_heads, d.kv_heads, d.head_dim, d.max_len));
   b.pk_ws = c.take<char>(q35_pk_workspace_bytes(d));
   b.p_resid = c.take<bf16>(L * d.hidden);
   b.p_norm = c.take<bf16>(L * d.hidden);
@@ -173,6 +180,9 @@ extern "C" int q35_decoder_create(const q35_decoder_desc* desc, q35_decoder** ou
               "decoder_create: kernels are built for head dims 256 / 128 and conv kernel 4");
   Q35_REQUIRE(d.hidden % 16 == 0 && d.intermediate % 16 == 0 && d.max_len > 0 && d.max_prefill > 0,
               "decoder_create: bad sizes");
+  Q35_REQUIRE(d.batch >= 0 && d.batch <= 8, "decoder_create: batch %d outside [1, 8]", d.batch);
+  Q35_REQUIRE(d.batch <= 1 || (!d.a8w8 && d.hidden == 2048 && d.intermediate % 2 == 0),
+              "decoder_create: batched decode is built for bf16 weights and hidden 2048");
   Q35_REQUIRE(d.workspace && d.workspace_bytes >= q35_decoder_workspace_size(desc),
               "decoder_create: workspace too small (%zu < %zu)", d.workspace_bytes, q35_decoder_workspace_size(desc));
   for (int i = 0; i < d.n_layers; ++i) {
@@ -225,7 +235,9 @@ extern "C" int q35_decoder_set_trace(q35_decoder* dec, int64_t* trace, int64_t e
 
 extern "C" int q35_decoder_trace_ops(const q35_decoder* dec) { return dec && dec->pk ? q35_pk_ops(dec->pk) : 0; }
 
-extern "C" int q35_decoder_kernels_per_step(const q35_decoder* dec) { return dec ? 5 * dec->d.n_layers + 1 : 0; }
+extern "C" int q35_decoder_kernels_per_step(const q35_decoder* dec) {
+  return dec ? 5 * dec->d.n_layers + (dec->d.batch > 1 ? 2 : 1) : 0;
+}
 
 #define Q35_TRY(x)          \
   do {                      \
@@ -240,6 +252,10 @@ static int decode_layers(q35_decoder* dec, cudaStream_t s) {
   const Buffers& B = dec->buf;
   const bool pdl = d.use_pdl != 0;
   const bool q8 = d.a8w8 != 0;
+  const int64_t nb = d.batch > 1 ? d.batch : 1;
+  auto gemv = [&](const q35_gemv_desc* g) -> int {
+    return nb > 1 ? q35_gemv_batch_launch(g, nb, s, pdl) : q35_gemv_launch(g, s, pdl);
+  };
   const int qgkv_rows = 2 * d.q_heads * d.head_dim + 2 * d.kv_heads * d.head_dim;
   for (int i = 0; i < d.n_layers; ++i) {
     const q35_layer_desc& L = dec->layers[i];
@@ -261,14 +277,14 @@ static int decode_layers(q35_decoder* dec, cudaStream_t s) {
     g.epilogue = Q35_EPI_STORE;
     g.int8 = q8;
     g.eps = d.eps;
-    Q35_TRY(q35_gemv_launch(&g, s, pdl));
+    Q35_TRY(gemv(&g));
     // mixer
     if (delta) {
       Q35_TRY(q35_delta_decode_launch(B.mix_in_out, L.conv_w, L.conv_state, L.a_log, L.dt_bias, L.gnorm,
-                                      L.rec_state, B.mix_out, 1, d.lin_heads, d.delta_rows, d.eps, s, pdl));
+                                      L.rec_state, B.mix_out, nb, d.lin_heads, d.delta_rows, d.eps, s, pdl));
     } else {
       Q35_TRY(q35_attn_decode_launch(B.mix_in_out, L.q_norm, L.k_norm, d.inv_freq, L.k_cache, L.v_cache,
-                                     d.cache_len, d.rope_pos, B.mix_out, 1, d.q_heads, d.kv_heads, d.rotary_dim,
+                                     d.cache_len, d.rope_pos, B.mix_out, nb, d.q_heads, d.kv_heads, d.rotary_dim,
                                      d.max_len, d.eps, B.attn_ws, s, pdl));
     }
     // out-projection + residual
@@ -283,7 +299,7 @@ static int decode_layers(q35_decoder* dec, cudaStream_t s) {
     g.epilogue = Q35_EPI_RESIDUAL;
     g.int8 = q8;
     g.eps = d.eps;
-    Q35_TRY(q35_gemv_launch(&g, s, pdl));
+    Q35_TRY(gemv(&g));
     // gate/up + SwiGLU
     g = q35_gemv_desc{};
     g.weight = L.gate_up;
@@ -297,7 +313,7 @@ static int decode_layers(q35_decoder* dec, cudaStream_t s) {
     g.epilogue = Q35_EPI_SWIGLU;
     g.int8 = q8;
     g.eps = d.eps;
-    Q35_TRY(q35_gemv_launch(&g, s, pdl));
+    Q35_TRY(gemv(&g));
     // down + residual
     g = q35_gemv_desc{};
     g.weight = L.down;
@@ -310,7 +326,7 @@ static int decode_layers(q35_decoder* dec, cudaStream_t s) {
     g.epilogue = Q35_EPI_RESIDUAL;
     g.int8 = q8;
     g.eps = d.eps;
-    Q35_TRY(q35_gemv_launch(&g, s, pdl));
+    Q35_TRY(gemv(&g));
   }
   return Q35_OK;
 }
@@ -321,6 +337,11 @@ extern "C" int q35_decoder_decode_step(q35_decoder* dec, void* stream) {
   cudaStream_t s = (cudaStream_t)stream;
   Q35_TRY(decode_layers(dec, s));
   q35_step_counters adv = {d.cache_len, d.rope_pos, d.token_log, d.log_pos, d.log_len};
+  if (d.batch > 1) {  // one pass over the tied table for every request: keys, then tokens + counters
+    Q35_TRY(q35_lm_head_shard_keys(dec->buf.resid, d.batch, d.final_norm, d.embed, 0, d.vocab, d.vocab, d.hidden,
+                                   d.eps, dec->buf.lm_keys, dec->buf.lm_keys_ws, q35_lm_shard_workspace_size(), s));
+    return q35_lm_keys_finish_launch(dec->buf.lm_keys, d.batch, d.token, s, false, &adv);
+  }
   return q35_lm_head_launch(dec->buf.resid, d.final_norm, d.embed, d.token, d.vocab, d.hidden, d.eps, dec->buf.lm_ws,
                             s, d.use_pdl != 0, &adv);
 }
@@ -358,16 +379,23 @@ struct MmInputs {
   int64_t rope_next = -1;
 };
 
-static int prefill_impl(q35_decoder* dec, const int64_t* ids, int64_t length, const MmInputs& mm, cudaStream_t s);
+static int prefill_impl(q35_decoder* dec, const int64_t* ids, int64_t length, const MmInputs& mm, int64_t slot,
+                        cudaStream_t s);
 
 extern "C" int q35_decoder_prefill(q35_decoder* dec, const int64_t* ids, int64_t length, void* stream) {
   Q35_REQUIRE(dec && ids, "prefill: null argument");
-  return prefill_impl(dec, ids, length, MmInputs{}, (cudaStream_t)stream);
+  return prefill_impl(dec, ids, length, MmInputs{}, 0, (cudaStream_t)stream);
+}
+
+extern "C" int q35_decoder_prefill_slot(q35_decoder* dec, const int64_t* ids, int64_t length, int64_t slot,
+                                        void* stream) {
+  Q35_REQUIRE(dec && ids, "prefill_slot: null argument");
+  return prefill_impl(dec, ids, length, MmInputs{}, slot, (cudaStream_t)stream);
 }
 
 extern "C" int q35_decoder_prefill_mm(q35_decoder* dec, const int64_t* ids, int64_t length, const void* image_embeds,
                                       const int64_t* image_rows, int64_t n_image, const int64_t* positions3,
-                                      int64_t rope_next, void* stream) {
+                                      int64_t rope_next, int64_t slot, void* stream) {
   Q35_REQUIRE(dec && ids, "prefill_mm: null argument");
   Q35_REQUIRE(n_image >= 0 && n_image <= length && (n_image == 0 || (image_embeds && image_rows)),
               "prefill_mm: %lld image rows need embeddings and row indices", (long long)n_image);
@@ -381,13 +409,28 @@ extern "C" int q35_decoder_prefill_mm(q35_decoder* dec, const int64_t* ids, int6
   mm.n_image = n_image;
   mm.pos3 = positions3;
   mm.rope_next = rope_next;
-  return prefill_impl(dec, ids, length, mm, (cudaStream_t)stream);
+  return prefill_impl(dec, ids, length, mm, slot, (cudaStream_t)stream);
 }
 
-static int prefill_impl(q35_decoder* dec, const int64_t* ids, int64_t length, const MmInputs& mm, cudaStream_t s) {
+static int prefill_impl(q35_decoder* dec, const int64_t* ids, int64_t length, const MmInputs& mm, int64_t slot,
+                        cudaStream_t s) {
   const q35_decoder_desc& d = dec->d;
   Q35_REQUIRE(length >= 1 && length <= d.max_prefill && length < d.max_len,
               "prefill: length %lld outside [1, %d] (cache %d)", (long long)length, d.max_prefill, d.max_len);
+  Q35_REQUIRE(slot >= 0 && slot < (d.batch > 1 ? d.batch : 1), "prefill: slot %lld outside the batch of %d",
+              (long long)slot, d.batch > 1 ? d.batch : 1);
+  // this slot's states and caches: the layers' tensors have a leading batch dimension
+  const int64_t conv_elems = (int64_t)d.lin_heads * (2 * d.lin_dk + d.lin_dv) * d.conv_kernel;
+  const int64_t rec_elems = (int64_t)d.lin_heads * d.lin_dk * d.lin_dv;
+  const int64_t kv_elems = (int64_t)d.kv_heads * d.max_len * d.head_dim;
+  std::vector<q35_layer_desc> slot_layers(dec->layers);
+  for (q35_layer_desc& L : slot_layers) {
+    if (L.conv_state) L.conv_state = static_cast<bf16*>(L.conv_state) + slot * conv_elems;
+    if (L.rec_state) L.rec_state += slot * rec_elems;
+    if (L.k_cache) L.k_cache = static_cast<bf16*>(L.k_cache) + slot * kv_elems;
+    if (L.v_cache) L.v_cache = static_cast<bf16*>(L.v_cache) + slot * kv_elems;
+  }
+  int64_t* token_out = d.token + slot;
   const Buffers& B = dec->buf;
   const bool q8 = d.a8w8 != 0;
   const int64_t H = d.hidden, I = d.intermediate, Lt = length;
@@ -421,7 +464,7 @@ static int prefill_impl(q35_decoder* dec, const int64_t* ids, int64_t length, co
 
   // fresh cache: zero the recurrent/conv states (the KV rows past `length` are never read)
   for (int i = 0; i < d.n_layers; ++i) {
-    const q35_layer_desc& L = dec->layers[i];
+    const q35_layer_desc& L = slot_layers[i];
     if (L.kind == 0) {
       if (cudaMemsetAsync(L.rec_state, 0, (size_t)d.lin_heads * d.lin_dk * d.lin_dv * sizeof(float), s) !=
               cudaSuccess ||
@@ -437,7 +480,7 @@ static int prefill_impl(q35_decoder* dec, const int64_t* ids, int64_t length, co
     Q35_TRY(q35_check_launch("prefill_mm image rows"));
   }
   for (int i = 0; i < d.n_layers; ++i) {
-    const q35_layer_desc& L = dec->layers[i];
+    const q35_layer_desc& L = slot_layers[i];
     Q35_TRY(q35_rms_norm(B.p_resid, L.in_ln, B.p_norm, Lt, H, d.eps, s));
     if (L.kind == 0) {
       Q35_TRY(proj(B.p_norm, H, L.mix_in, L.mix_in_scale, B.p_packed, d.delta_rows, Q35_EPI_STORE));
@@ -472,7 +515,7 @@ static int prefill_impl(q35_decoder* dec, const int64_t* ids, int64_t length, co
     Q35_TRY(proj(B.p_norm, H, L.gate_up, L.gate_up_scale, B.p_act, I, Q35_EPI_SWIGLU));
     Q35_TRY(proj(B.p_act, I, L.down, L.down_scale, B.p_resid, H, Q35_EPI_RESIDUAL));
   }
-  Q35_TRY(q35_lm_head_launch(B.p_resid + (Lt - 1) * H, d.final_norm, d.embed, d.token, d.vocab, H, d.eps, B.lm_ws,
+  Q35_TRY(q35_lm_head_launch(B.p_resid + (Lt - 1) * H, d.final_norm, d.embed, token_out, d.vocab, H, d.eps, B.lm_ws,
                              s, false, nullptr));
   Q35_TRY(q35_set_counters_launch(d.cache_len, d.rope_pos, Lt, s));
   if (mm.rope_next >= 0) Q35_TRY(q35_set_counters_launch(d.rope_pos, d.rope_pos, mm.rope_next, s));

@@ -39,16 +39,21 @@ class Qwen35Engine:
     def __init__(self, weights: dict, dims: Qwen35Dims = Qwen35Dims(), *, a8w8: bool = False,
                  max_len: int = 2048, max_prefill: int = 1024, device="cuda", use_pdl: bool = True,
                  prefill_tc: bool = True, prefill_chunked: bool = True, log_len: int = 4096, release_source: bool = False,
-                 persistent: bool | None = None):
+                 persistent: bool | None = None, batch: int = 1):
         L.load()
         dev = torch.device(device)
         if dev.type != "cuda":
             raise ValueError("Qwen35Engine runs on a CUDA device only")
         if dev.index is None:
             dev = torch.device("cuda", torch.cuda.current_device())
+        if not 1 <= batch <= 8:
+            raise ValueError("batch must be within [1, 8]")
+        if batch > 1 and a8w8:
+            raise ValueError("batched decoding runs bf16 weights (the A8W8 decode path is batch 1)")
         self.dims = dims
         self.device = dev
         self.a8w8 = a8w8
+        self.batch = batch
         self.max_len = max_len
         self.max_prefill = min(max_prefill, max_len - 1)
         self._keep: list[torch.Tensor] = []
@@ -85,8 +90,8 @@ class Qwen35Engine:
                 T["a_log"] = w(la + "A_log")
                 T["dt_bias"] = w(la + "dt_bias")
                 T["gnorm"] = w(la + "norm.weight")
-                T["conv_state"] = torch.zeros(1, d.conv_dim, d.conv_kernel, device=dev, dtype=BF16)
-                T["rec_state"] = torch.zeros(1, d.lin_heads, d.lin_dk, d.lin_dv, device=dev, dtype=torch.float32)
+                T["conv_state"] = torch.zeros(batch, d.conv_dim, d.conv_kernel, device=dev, dtype=BF16)
+                T["rec_state"] = torch.zeros(batch, d.lin_heads, d.lin_dk, d.lin_dv, device=dev, dtype=torch.float32)
                 self.conv_states.append(T["conv_state"])
                 self.rec_states.append(T["rec_state"])
                 ld.kind = 0
@@ -97,7 +102,7 @@ class Qwen35Engine:
                 T["mix_out"] = w(sa + "o_proj.weight")
                 T["q_norm"] = w(sa + "q_norm.weight")
                 T["k_norm"] = w(sa + "k_norm.weight")
-                T["k_cache"] = torch.zeros(1, d.kv_heads, max_len, d.head_dim, device=dev, dtype=BF16)
+                T["k_cache"] = torch.zeros(batch, d.kv_heads, max_len, d.head_dim, device=dev, dtype=BF16)
                 T["v_cache"] = torch.zeros_like(T["k_cache"])
                 self.k_caches.append(T["k_cache"])
                 self.v_caches.append(T["v_cache"])
@@ -116,7 +121,7 @@ class Qwen35Engine:
         self.embed = w("model.embed_tokens.weight")
         self.final_norm = w("model.norm.weight")
         self.inv_freq = rope_inv_freq(d.rotary_dim, d.rope_theta).to(dev)
-        self.token = torch.zeros(1, device=dev, dtype=torch.int64)
+        self.token = torch.zeros(batch, device=dev, dtype=torch.int64)
         self.cache_len = torch.zeros(1, device=dev, dtype=torch.int64)
         self.rope_pos = torch.zeros(1, device=dev, dtype=torch.int64)
         self.log_len = log_len
@@ -142,6 +147,7 @@ class Qwen35Engine:
         desc.prefill_delta = 0 if prefill_chunked else 1
         for i, sec in enumerate(d.mrope_section):
             desc.mrope_section[i] = sec
+        desc.batch = batch
         size = L.load().q35_decoder_workspace_size(C.byref(desc))
         self.workspace = torch.zeros(size, device=dev, dtype=torch.uint8)
         desc.workspace, desc.workspace_bytes = self.workspace.data_ptr(), size
@@ -172,9 +178,10 @@ class Qwen35Engine:
         return q, s
 
     # ------------------------------------------------------------------ steps
-    def prefill(self, ids: torch.Tensor) -> torch.Tensor:
+    def prefill(self, ids: torch.Tensor, slot: int = 0) -> torch.Tensor:
         """Prefill device token ids ``[L]`` from an empty cache; the greedy first token lands in
-        ``self.token`` (returned, on device)."""
+        ``self.token`` (returned, on device). Batched engines: request slot ``slot``; every slot of a
+        batch is prefilled with the same length before the batch decodes."""
         ids = ids.reshape(-1)
         if not ids.is_cuda or ids.dtype != torch.int64:
             raise ValueError("prefill expects int64 token ids on a CUDA device")
@@ -183,12 +190,12 @@ class Qwen35Engine:
         n = ids.numel()
         if n > self.max_prefill:
             raise ValueError(f"prompt of {n} tokens exceeds max_prefill={self.max_prefill}")
-        L.check(L.load().q35_decoder_prefill(self.handle, ids.data_ptr(), n, L.stream_of(self.device)),
-                "q35_decoder_prefill")
+        L.check(L.load().q35_decoder_prefill_slot(self.handle, ids.data_ptr(), n, int(slot), L.stream_of(self.device)),
+                "q35_decoder_prefill_slot")
         return self.token
 
     def prefill_multimodal(self, ids: torch.Tensor, image_embeds: torch.Tensor, image_rows: torch.Tensor,
-                           positions3: torch.Tensor, rope_next: int) -> torch.Tensor:
+                           positions3: torch.Tensor, rope_next: int, slot: int = 0) -> torch.Tensor:
         """Prefill an image + text prompt from an empty cache: device ids ``[L]`` (the image rows'
         ids are ignored), ``image_embeds`` bf16 ``[n, hidden]`` placed at rows ``image_rows``
         (int64 ``[n]``), 3-axis M-RoPE ``positions3`` int64 ``[3, L]``; afterwards the decode
@@ -210,7 +217,7 @@ class Qwen35Engine:
         image_embeds, positions3 = image_embeds.to(dev).contiguous(), positions3.to(dev).contiguous()
         L.check(L.load().q35_decoder_prefill_mm(self.handle, ids.data_ptr(), n, image_embeds.data_ptr(),
                                                 image_rows.data_ptr(), image_rows.numel(), positions3.data_ptr(),
-                                                int(rope_next), L.stream_of(dev)), "q35_decoder_prefill_mm")
+                                                int(rope_next), int(slot), L.stream_of(dev)), "q35_decoder_prefill_mm")
         return self.token
 
     def decode_step(self) -> torch.Tensor:
@@ -358,6 +365,28 @@ class Qwen35Engine:
         self.rope_pos.copy_(snap["rope_pos"])
 
     # ------------------------------------------------------------------ generation
+    def generate_batch(self, prompts, max_new_tokens: int):
+        """Greedy generation of ``batch`` requests in lock step from host prompts of one length:
+        H2D copies, one prefill per slot, the first tokens read on the host (TTFT), then one
+        graph-replayed batched step per token with a host read of the ``batch`` tokens. Returns
+        ``(tokens per request, ttft_s, elapsed_s)``."""
+        if len(prompts) != self.batch:
+            raise ValueError(f"expected {self.batch} prompts")
+        hosts = [torch.as_tensor(p, dtype=torch.int64).reshape(-1).pin_memory() for p in prompts]
+        if len({h.numel() for h in hosts}) != 1:
+            raise ValueError("the prompts of one batch share a length (one cache position for all)")
+        start = time.perf_counter()
+        for slot, h in enumerate(hosts):
+            self.prefill(h.to(self.device, non_blocking=True), slot)
+        out = [[t] for t in self.token.tolist()]
+        first_at = time.perf_counter()
+        graph = self.capture(1) if max_new_tokens > 1 else None
+        for _ in range(max_new_tokens - 1):
+            graph.replay()
+            for seq, t in zip(out, self.token.tolist()):
+                seq.append(t)
+        return out, first_at - start, time.perf_counter() - start
+
     def generate(self, prompt_ids, max_new_tokens: int, *, eos_ids=(), use_graph: bool = True,
                  graph_steps: int = 1):
         """Greedy generation from host token ids, mirroring evaluation_wrapper.py:307-441:

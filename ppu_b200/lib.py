@@ -50,7 +50,7 @@ class DecoderDesc(C.Structure):
         ("layers", C.POINTER(LayerDesc)), ("embed", P), ("final_norm", P), ("inv_freq", P),
         ("token", P), ("cache_len", P), ("rope_pos", P), ("token_log", P), ("log_pos", P),
         ("log_len", I32), ("use_pdl", I32), ("prefill_tc", I32), ("prefill_delta", I32),
-        ("mrope_section", I32 * 3), ("workspace", P), ("workspace_bytes", SZ),
+        ("mrope_section", I32 * 3), ("batch", I32), ("workspace", P), ("workspace_bytes", SZ),
     ]
 
 
@@ -120,7 +120,9 @@ _SIGS = {
     "q35_decoder_create": (INT, [C.POINTER(DecoderDesc), C.POINTER(P)]),
     "q35_decoder_destroy": (None, [P]),
     "q35_decoder_prefill": (INT, [P, P, I64, P]),
-    "q35_decoder_prefill_mm": (INT, [P, P, I64, P, P, I64, P, I64, P]),
+    "q35_decoder_prefill_mm": (INT, [P, P, I64, P, P, I64, P, I64, I64, P]),
+    "q35_decoder_prefill_slot": (INT, [P, P, I64, I64, P]),
+    "q35_gemv_batch": (INT, [C.POINTER(GemvDesc), I64, P]),
     "q35_decoder_decode_step": (INT, [P, P]),
     "q35_decoder_decode_layers": (INT, [P, P]),
     "q35_decoder_hidden": (P, [P]),

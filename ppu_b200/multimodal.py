@@ -77,18 +77,19 @@ class MultimodalEngine:
         g.replay()
         return tokens
 
-    def prefill(self, pixels: torch.Tensor, text_ids: torch.Tensor) -> torch.Tensor:
+    def prefill(self, pixels: torch.Tensor, text_ids: torch.Tensor, slot: int = 0) -> torch.Tensor:
         """Device pixels fp32 [3, H, W] and text ids int64 [n]: vision graph, then the multimodal
-        prefill; the first greedy token lands in ``text.token``."""
-        return self.prefill_prompt(self.encode_image(pixels), text_ids)
+        prefill (into request slot ``slot`` of a batched text engine); the first greedy token lands
+        in ``text.token[slot]``."""
+        return self.prefill_prompt(self.encode_image(pixels), text_ids, slot)
 
-    def prefill_prompt(self, tokens: torch.Tensor, text_ids: torch.Tensor) -> torch.Tensor:
+    def prefill_prompt(self, tokens: torch.Tensor, text_ids: torch.Tensor, slot: int = 0) -> torch.Tensor:
         """The text model's prefill of [image tokens, text ids] (image first)."""
         n_text = text_ids.numel()
         rows, pos, nxt = self._layout(n_text)
         ids = torch.cat((torch.full((self.n_img,), IMAGE_TOKEN_ID, device=self.device, dtype=torch.int64),
                          text_ids.reshape(-1)))
-        return self.text.prefill_multimodal(ids, tokens, rows, pos, nxt)
+        return self.text.prefill_multimodal(ids, tokens, rows, pos, nxt, slot)
 
     def decode_step(self) -> None:
         self._dgraph.replay()
