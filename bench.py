@@ -67,6 +67,7 @@ def parse():
     ap.add_argument("--no-lm-shard-leg", action="store_true", help="N > 1: skip the lock-step sub-measurement")
     ap.add_argument("--mm-requests", type=int, default=256, help="config-5 image + text requests (0: skip)")
     ap.add_argument("--mm-new-tokens", type=int, default=16)
+    ap.add_argument("--batch", type=int, default=8, help="requests per decode step of the batched legs (1: skip)")
     return ap.parse_args()
 
 
@@ -354,23 +355,29 @@ def gate_up_roofline(eng, dims, dev, hbm_peak, peak_kind, a8w8: bool):
             "peak_kind": peak_kind}
 
 
-def multimodal_leg(eng, decode_graph, dims, dev, rank, world, args, tf_sust, peak_kind):
-    """BASELINE config 5: ``args.mm_requests`` seeded image + text requests spread over the ranks
-    (request i on rank i mod N): a 448 x 448 image through the 24-layer ViT and the 2x2 merger (196
-    tokens), prepended to 300 text tokens, a 496-token multimodal prefill and greedy decode to
-    ``args.mm_new_tokens`` tokens. Device-timed per request (inputs resident in HBM); the vision
-    tower's FLOPs over its time against the sustained bf16 peak; e2e through MultimodalEngine.generate."""
-    from ppu_b200 import replicas as R
+def vision_engine(dev):
     from ppu_b200.config import VisionDims
-    from ppu_b200.multimodal import MultimodalEngine
     from ppu_b200.synthetic import make_vision_weights
     from ppu_b200.vision import VisionEngine
 
     vd = VisionDims()
     vw = make_vision_weights(vd, seed=1, device=dev)
-    vis = VisionEngine(vw, vd, max_image=(448, 448), device=dev)
-    del vw
-    n_text, n_new = 300, args.mm_new_tokens
+    return VisionEngine(vw, vd, max_image=(448, 448), device=dev)
+
+
+def multimodal_leg(eng, vis, decode_graph, dims, dev, rank, world, args, tf_sust, peak_kind):
+    """BASELINE config 5: ``args.mm_requests`` seeded image + text requests spread over the ranks
+    (request i on rank i mod N): a 448 x 448 image through the 24-layer ViT and the 2x2 merger (196
+    tokens), prepended to 300 text tokens, a 496-token multimodal prefill and greedy decode to
+    ``args.mm_new_tokens`` tokens. A batched text engine serves its requests in groups of
+    ``eng.batch`` (each image encoded and prefilled into its slot, then the group decodes in lock
+    step). Device-timed (inputs resident in HBM); the vision tower's FLOPs over its time against the
+    sustained bf16 peak; e2e through MultimodalEngine.generate (batch-1 engines)."""
+    from ppu_b200 import replicas as R
+    from ppu_b200.multimodal import MultimodalEngine
+
+    vd = vis.vd
+    n_text, n_new, nb = 300, args.mm_new_tokens, eng.batch
     mm = MultimodalEngine(None, None, dims, vd, image_hw=(448, 448), max_text=n_text, max_new_tokens=n_new,
                           text_engine=eng, vision_engine=vis, decode_graph=decode_graph)
     mine = R.requests_for_rank(args.mm_requests, world, rank)
@@ -382,58 +389,113 @@ def multimodal_leg(eng, decode_graph, dims, dev, rank, world, args, tf_sust, pea
 
     imgs = [image(i) for i in mine]
     texts = [make_prompt(dims, n_text, seed=200_000 + i)[0].to(dev) for i in mine]
+    groups = [list(range(j, min(j + nb, len(mine)))) for j in range(0, len(mine), nb)]
 
-    def request(j, ev=None):
+    def group(js, ev=None):
         if ev:
-            ev[0].record()
-        tokens = mm.encode_image(imgs[j])
-        if ev:
-            ev[1].record()
-        mm.prefill_prompt(tokens, texts[j])
-        if ev:
-            ev[2].record()
+            ev["start"].record()
+        for slot, j in enumerate(js):
+            tokens = mm.encode_image(imgs[j])
+            if ev:
+                ev["vis"][slot].record()
+            mm.prefill_prompt(tokens, texts[j], slot)
+            if ev:
+                ev["first"][slot].record()
         for _ in range(n_new - 1):
             mm.decode_step()
         if ev:
-            ev[3].record()
+            ev["end"].record()
 
-    for j in range(min(3, len(mine))):
-        request(j)
+    def events(n):
+        e = lambda: torch.cuda.Event(enable_timing=True)  # noqa: E731
+        return {"start": e(), "end": e(), "vis": [e() for _ in range(n)], "first": [e() for _ in range(n)]}
+
+    for js in groups[:min(2, len(groups))]:
+        group(js)
     torch.cuda.synchronize()
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in mine]
+    evs = [events(len(js)) for js in groups]
     R.barrier()
     torch.cuda.synchronize()
-    for j in range(len(mine)):
-        request(j, evs[j])
+    for js, ev in zip(groups, evs):
+        group(js, ev)
     torch.cuda.synchronize()
     R.barrier()
-    total_ms = R.max_over_ranks(evs[0][0].elapsed_time(evs[-1][3]), dev)
-    vis_ms = [e[0].elapsed_time(e[1]) for e in evs]
-    ttft_ms = [e[0].elapsed_time(e[2]) for e in evs]
-    dec_ms = [e[2].elapsed_time(e[3]) for e in evs]
+    total_ms = R.max_over_ranks(evs[0]["start"].elapsed_time(evs[-1]["end"]), dev)
+    vis_ms, ttft_ms, dec_ms = [], [], []
+    for ev in evs:
+        prev = ev["start"]
+        for v, f in zip(ev["vis"], ev["first"]):
+            vis_ms.append(prev.elapsed_time(v))
+            ttft_ms.append(ev["start"].elapsed_time(f))
+            prev = f
+        dec_ms.append(ev["first"][-1].elapsed_time(ev["end"]))
     mean = lambda xs: R.max_over_ranks(sum(xs) / len(xs), dev)  # noqa: E731
     v_ms, t_ms, d_ms = mean(vis_ms), mean(ttft_ms), mean(dec_ms)
     vflops = vd.linear_flops(448, 448)
-    host_img = torch.rand((3, 448, 448), generator=torch.Generator().manual_seed(300_000 + rank))
-    e_tok, e_ttft, e_el = mm.generate(host_img, make_prompt(dims, n_text, seed=310_000 + rank)[0], n_new)
-    e_el = R.max_over_ranks(e_el, dev)
-    return {
+    line = {
         "workload": f"config5: {args.mm_requests} requests over {world} GPU(s): 448x448 image -> ViT (24 layers, "
                     f"width 1024) -> 196 tokens + {n_text} text tokens, {n_new} greedy tokens each",
         "requests_per_s": round(args.mm_requests / (total_ms / 1e3), 2),
         "tok_per_s": round(args.mm_requests * n_new / (total_ms / 1e3), 1),
         "ttft_ms_mean": round(t_ms, 3), "vision_ms_mean": round(v_ms, 3),
-        "decode_ms_per_token": round(d_ms / max(n_new - 1, 1), 4),
+        "decode_ms_per_step": round(d_ms / max(n_new - 1, 1), 4), "requests_per_decode_step": nb,
         "vision_roofline": {"flops": vflops, "achieved_tflops": round(vflops / (v_ms / 1e3) / 1e12, 1),
                             "peak_tflops": tf_sust, "frac": round(vflops / (v_ms / 1e3) / 1e12 / tf_sust, 4),
                             "bound": "tensor", "peak_kind": f"{peak_kind} bf16 sustained"},
-        "decode": "lock-step, LM head vocab-sharded" if decode_graph is not None else "per-rank replicas",
-        "e2e": {"requests_per_s": round(world / e_el, 2), "ttft_ms": round(1000 * e_ttft, 3),
-                "tokens": len(e_tok), "h2d_bytes_per_request": 3 * 448 * 448 * 4 + n_text * 8,
-                "path": "MultimodalEngine.generate (host image + ids -> H2D, ViT graph, prefill, per-token D2H)"},
+        "decode": ("lock-step across ranks, LM head vocab-sharded" if decode_graph is not None
+                   else f"per-rank replicas, {nb} request(s) per decode step"),
         "data": "synthetic: seeded random-init ViT N(0,0.02) (LayerNorm 1+N), uniform [0,1) pixels, "
                 "uniform-random text ids",
     }
+    if nb == 1:
+        host_img = torch.rand((3, 448, 448), generator=torch.Generator().manual_seed(300_000 + rank))
+        e_tok, e_ttft, e_el = mm.generate(host_img, make_prompt(dims, n_text, seed=310_000 + rank)[0], n_new)
+        e_el = R.max_over_ranks(e_el, dev)
+        line["e2e"] = {"requests_per_s": round(world / e_el, 2), "ttft_ms": round(1000 * e_ttft, 3),
+                       "tokens": len(e_tok), "h2d_bytes_per_request": 3 * 448 * 448 * 4 + n_text * 8,
+                       "path": "MultimodalEngine.generate (host image + ids -> H2D, ViT graph, prefill, per-token D2H)"}
+    return line
+
+
+def batched_decode_leg(engB, dims, dev, rank, world, args, hbm_peak, peak_kind):
+    """Config 4's requests ``engB.batch`` at a time: each slot prefilled with its own 1024-token
+    prompt, then ``new_tokens`` lock-step decode steps (CUDA graph); tokens/s over the decode time."""
+    from ppu_b200 import replicas as R
+
+    nb, P, T = engB.batch, args.prompt_len, args.new_tokens
+    n_groups, warm = max(1, min(args.steps, 4)), 1
+    prompts = [make_prompt(dims, P, seed=400_000 + 1000 * rank + i)[0].to(dev) for i in range(nb)]
+    g = engB.capture(1)
+
+    def rnd(ev=None):
+        for slot in range(nb):
+            engB.prefill(prompts[slot], slot)
+        if ev:
+            ev[0].record()
+        for _ in range(T):
+            g.replay()
+        if ev:
+            ev[1].record()
+
+    for _ in range(warm):
+        rnd()
+    torch.cuda.synchronize()
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(n_groups)]
+    R.barrier()
+    for ev in evs:
+        rnd(ev)
+    torch.cuda.synchronize()
+    dec_ms = R.max_over_ranks(sum(e[0].elapsed_time(e[1]) for e in evs), dev)
+    value = R.aggregate_rate(n_groups * T * nb, dec_ms / 1000.0, world)
+    step_ms = dec_ms / (n_groups * T)
+    bytes_step = dims.weight_bytes_per_token() + (nb - 1) * dims.n_delta * 2 * 4 * dims.lin_heads * dims.lin_dk * \
+        dims.lin_dv + nb * 2 * dims.n_attn * dims.kv_heads * dims.head_dim * 2 * (P + T // 2)
+    return {"value": round(value, 2), "unit": "tok/s", "requests_per_step": nb, "rounds": n_groups,
+            "decode_ms_per_step": round(step_ms, 4),
+            "step_hbm": {"bytes_per_step": bytes_step, "achieved_gbs": round(bytes_step / step_ms / 1e6, 1),
+                         "peak_gbs": hbm_peak, "frac": round(bytes_step / step_ms / 1e6 / hbm_peak, 4),
+                         "peak_kind": peak_kind},
+            "workload": f"config4 requests {nb} at a time: prefill {P} per slot, {T} lock-step greedy decode steps"}
 
 
 def main():
@@ -461,6 +523,10 @@ def main():
     eng = Qwen35Engine(weights, dims, a8w8=headline_a8w8, max_len=cache_bucket(P, T), max_prefill=P, device=dev,
                        use_pdl=not args.no_pdl, prefill_chunked=args.prefill_delta == "chunked",
                        persistent=(args.decode == "persistent" and not headline_a8w8))
+    engB = None
+    if args.batch > 1 and not headline_a8w8:
+        engB = Qwen35Engine(weights, dims, max_len=cache_bucket(P, T), max_prefill=P, device=dev, batch=args.batch,
+                            use_pdl=not args.no_pdl, prefill_chunked=args.prefill_delta == "chunked")
     eng8 = None
     if not headline_a8w8 and not args.no_a8w8_leg:
         eng8 = Qwen35Engine(weights, dims, a8w8=True, max_len=cache_bucket(P, T), max_prefill=P, device=dev,
@@ -592,11 +658,15 @@ def main():
 
     # ---- config 5: the multimodal request stream (replicas; at N > 1 also lock-step with the
     # vocab-sharded LM head)
-    mm = mm_shard = None
+    batched = batched_decode_leg(engB, dims, dev, rank, world, args, hbm_peak, peak_kind) if engB else None
+    mm = mm_batched = mm_shard = None
     if args.mm_requests > 0:
-        mm = multimodal_leg(eng, None, dims, dev, rank, world, args, tf_sust, peak_kind)
+        vis = vision_engine(dev)
+        mm = multimodal_leg(eng, vis, None, dims, dev, rank, world, args, tf_sust, peak_kind)
+        if engB is not None:
+            mm_batched = multimodal_leg(engB, vis, None, dims, dev, rank, world, args, tf_sust, peak_kind)
         if sharded is not None and head is None:
-            mm_shard = multimodal_leg(eng, sharded.capture(1), dims, dev, rank, world, args, tf_sust, peak_kind)
+            mm_shard = multimodal_leg(eng, vis, sharded.capture(1), dims, dev, rank, world, args, tf_sust, peak_kind)
             sharded.release()
 
     cpu = None
@@ -662,8 +732,12 @@ def main():
         line["a8w8"] = a8
     if shard is not None:
         line["lm_shard"] = shard
+    if batched is not None:
+        line["decode_batched"] = batched
     if mm is not None:
         line["multimodal"] = mm
+    if mm_batched is not None:
+        line["multimodal_batched"] = mm_batched
     if mm_shard is not None:
         line["multimodal_lm_shard"] = mm_shard
     if cpu is not None:
