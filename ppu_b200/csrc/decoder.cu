@@ -20,6 +20,8 @@
 
 int q35_gemv_launch(const q35_gemv_desc* d, cudaStream_t s, bool pdl);
 int q35_gemv_batch_launch(const q35_gemv_desc* d, int64_t batch, cudaStream_t s, bool pdl);
+int q35_lm_head_batch_launch(const void* hidden, int64_t batch, const void* norm_weight, const void* weight,
+                             int64_t vocab, float eps, int64_t* keys_out, void* workspace, cudaStream_t s, bool pdl);
 extern "C" size_t q35_lm_shard_workspace_size(void);
 int q35_lm_head_launch(const void* hidden, const void* norm_weight, const void* weight, int64_t* token_out,
                        int64_t vocab, int64_t k, float eps, void* ws, cudaStream_t s, bool pdl,
@@ -116,7 +118,7 @@ Buffers carve(const q35_decoder_desc& d, void* base, size_t* total) {
   const int64_t L = d.max_prefill;
   const int64_t nb = d.batch > 1 ? d.batch : 1;
   b.lm_ws = c.take<char>(256);  // LM head ticket + key (must start zeroed)
-  b.lm_keys_ws = c.take<char>(q35_lm_shard_workspace_size());  // batched LM head keys (zeroed, left zeroed)
+  b.lm_keys_ws = c.take<char>(128);  // batched LM head: 8 keys + count (zeroed, left zeroed)
   b.lm_keys = c.take<int64_t>(8);
   b.resid = c.take<bf16>(nb * d.hidden);
   b.mix_in_out = c.take<bf16>(nb * rows_in);
@@ -338,8 +340,8 @@ extern "C" int q35_decoder_decode_step(q35_decoder* dec, void* stream) {
   Q35_TRY(decode_layers(dec, s));
   q35_step_counters adv = {d.cache_len, d.rope_pos, d.token_log, d.log_pos, d.log_len};
   if (d.batch > 1) {  // one pass over the tied table for every request: keys, then tokens + counters
-    Q35_TRY(q35_lm_head_shard_keys(dec->buf.resid, d.batch, d.final_norm, d.embed, 0, d.vocab, d.vocab, d.hidden,
-                                   d.eps, dec->buf.lm_keys, dec->buf.lm_keys_ws, q35_lm_shard_workspace_size(), s));
+    Q35_TRY(q35_lm_head_batch_launch(dec->buf.resid, d.batch, d.final_norm, d.embed, d.vocab, d.eps,
+                                     dec->buf.lm_keys, dec->buf.lm_keys_ws, s, d.use_pdl != 0));
     return q35_lm_keys_finish_launch(dec->buf.lm_keys, d.batch, d.token, s, false, &adv);
   }
   return q35_lm_head_launch(dec->buf.resid, d.final_norm, d.embed, d.token, d.vocab, d.hidden, d.eps, dec->buf.lm_ws,

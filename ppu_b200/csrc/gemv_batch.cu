@@ -1,14 +1,21 @@
-// Batched decode GEMV: one decode step of up to 8 requests in lock step streams each weight
-// matrix once for all of them (the decode projections of integration.py:183-185, 245, 272, 298,
-// 359 with a batch of B in-flight requests instead of one).
+// Batched decode projections: one decode step of up to 8 requests in lock step streams each
+// weight matrix once for all of them (the decode projections of integration.py:183-185, 245, 272,
+// 298, 359 and the LM head top-1 of kernels.py:1093-1185, with a batch of B in-flight requests).
 //
-// y[b, n] = W[n, :] . x_b for b < B, with the batch-1 GEMV's fused prologues (RMSNorm of the
-// residual, or the embedding gather + RMSNorm at layer 0) and epilogues (store, in-place residual
-// add, SwiGLU over gate / up row pairs), computed per request with the same rounding points.
-// The weights stream through registers with a rolling prefetch (chunk c of the next row group is
-// loaded into the slot chunk c of this group just left); the B input vectors sit in shared memory
-// as FP32 pairs so that one packed FMA (__ffma2_rn, one IEEE fma per half) serves two requests.
-// CUDA cores only: at B <= 8 the step is still bound by the weight stream.
+// Y[b, n] = W[n, :] . x_b for b < B as a skinny product on the warp tensor cores: a warp takes 16
+// weight rows x 8 requests (mma.sync m16n8k16, bf16 in, FP32 accumulate), the rows as the M side
+// and the requests as N. Each lane loads 16 contiguous bytes of rows g and g + 8 per 32-column
+// block (fully used 32-byte sectors) and one 16-byte slice of request g's input from shared
+// memory; the 16-column slots of the two MMAs of a block are assigned to those bytes by one
+// permutation of the K order, the same for both operands, so no operand is rearranged. The K range
+// of a 16-row group is split over the CTA's 8 warps and the partial tiles are summed in a fixed
+// order. At batch 8 each weight element feeds 8 products: on the CUDA cores that is issue-bound
+// (8 FMAs per element), on the tensor cores the step stays bound by the weight stream.
+//
+// Prologues as the batch-1 GEMV (input row, RMSNorm(1 + w) of it, or the embedding gather +
+// RMSNorm at layer 0) with its rounding points, per request; epilogues store / in-place residual
+// add / SwiGLU (the warp's 16 rows are 8 gate rows and their 8 up rows) / top-1 keys of the tied
+// LM head (bf16-rounded logits, lowest index on ties, the shard-key encoding).
 #include <cfloat>
 
 #include "common.cuh"
@@ -18,228 +25,260 @@ using namespace q35;
 namespace {
 
 constexpr int kThreads = 256, kWarps = kThreads / 32;
+constexpr int kBlk = 32;        // K columns per block (two MMAs)
+constexpr int kBatch = 8;       // N of the MMA: requests per step
+constexpr int kEpiTop1 = 100;   // epilogue: LM head top-1 keys
 
 struct BatchGemvParams {
-  const bf16* weight;     // [rows, K] (rows = n_out, or 2 n_out for SWIGLU: gate rows, then up rows)
+  const bf16* weight;     // [rows, K] (SWIGLU: gate rows [0, n_out), up rows [n_out, 2 n_out))
   const bf16* input;      // PLAIN / NORM: [n, K]
   const bf16* norm_w;     // NORM / EMBED: [K] (1 + w)
-  const int64_t* token;   // EMBED: [n] token ids
+  const int64_t* token;   // EMBED: [n]
   const bf16* embed;      // EMBED: [vocab, K]
-  bf16* resid;            // RESIDUAL: [n, n_out] updated in place; EMBED: receives the raw rows [n, K]
+  bf16* resid;            // RESIDUAL: [n, n_out] in place; EMBED: receives the raw rows [n, K]
   bf16* out;              // STORE / SWIGLU: [n, n_out]
+  unsigned long long* top1;  // TOP1: workspace keys [8] + count (zero before, zero after)
+  long long* keys_out;    // TOP1: [n] reduced signed keys
   int64_t vocab;
   int n, n_out;
   float eps;
 };
 
-// Plane q (0..3) of pair p holds, per 16-byte chunk i of a vector, the float4
-// {x[2p][8i + 2q], x[2p+1][8i + 2q], x[2p][8i + 2q + 1], x[2p+1][8i + 2q + 1]}.
-template <int K, int NB>
-Q35_DEV float* slot(float4* xs, int b, int q, int i) {
-  return reinterpret_cast<float*>(xs + ((q * (NB / 2) + b / 2) * (K / 8) + i)) + (b & 1);
+template <int K>
+constexpr int xs_stride() {  // bf16 elements per request row in shared memory (+64 bytes: see load)
+  return K + 32;
 }
 
-// Warp b builds vector b: PLAIN copies the input row, NORM / EMBED apply RMSNorm(1 + w) with the
-// batch-1 prologue's rounding (bf16(x * r * (1 + w))).
-template <int K, int NB, int PRO>
-Q35_DEV void build_inputs(const BatchGemvParams& p, float4* xs, int warp, int lane) {
-  constexpr int CPL = K / 8 / 32;  // 16-byte chunks per lane
-  for (int b = warp; b < NB; b += kWarps) {
-    if (b >= p.n) {
-      for (int c = 0; c < CPL; ++c)
+// Warp b builds request b's input row (bf16) in shared memory.
+template <int K, int PRO>
+Q35_DEV void build_inputs(const BatchGemvParams& p, bf16* xs, int warp, int lane) {
+  constexpr int CPL = K / 8 / 32;
+  const int b = warp;
+  uint4* dst = reinterpret_cast<uint4*>(xs + b * xs_stride<K>());
+  if (b >= p.n) {
+    for (int c = 0; c < CPL; ++c) dst[lane + 32 * c] = make_uint4(0, 0, 0, 0);
+    return;
+  }
+  const bf16* row = p.input + (int64_t)b * K;
+  if (PRO == Q35_PRO_EMBED) {
+    int64_t t = p.token[b];
+    t = t < 0 ? 0 : (t >= p.vocab ? p.vocab - 1 : t);
+    row = p.embed + t * (int64_t)K;
+  }
+  const uint4* src = reinterpret_cast<const uint4*>(row);
+  if (PRO == Q35_PRO_PLAIN) {
+    for (int c = 0; c < CPL; ++c) dst[lane + 32 * c] = src[lane + 32 * c];
+    return;
+  }
+  float ss = 0.f;
+  for (int c = 0; c < CPL; ++c) {
+    const uint4 v = src[lane + 32 * c];
+    if (PRO == Q35_PRO_EMBED && blockIdx.x == 0) reinterpret_cast<uint4*>(p.resid + (int64_t)b * K)[lane + 32 * c] = v;
+    float f[8];
+    unpack_bf16x8(v, f);
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          float* d = slot<K, NB>(xs, b, q, lane + 32 * c);
-          d[0] = 0.f;
-          d[2] = 0.f;
-        }
-      continue;
-    }
-    const bf16* row = p.input + (int64_t)b * K;
-    if (PRO == Q35_PRO_EMBED) {
-      int64_t t = p.token[b];
-      t = t < 0 ? 0 : (t >= p.vocab ? p.vocab - 1 : t);
-      row = p.embed + t * (int64_t)K;
-    }
-    const uint4* src = reinterpret_cast<const uint4*>(row);
-    float r = 1.f;
-    if (PRO != Q35_PRO_PLAIN) {
-      float ss = 0.f;
-      for (int c = 0; c < CPL; ++c) {
-        const uint4 v = src[lane + 32 * c];
-        if (PRO == Q35_PRO_EMBED && blockIdx.x == 0) reinterpret_cast<uint4*>(p.resid + (int64_t)b * K)[lane + 32 * c] = v;
-        float f[8];
-        unpack_bf16x8(v, f);
+    for (int j = 0; j < 8; ++j) ss += f[j] * f[j];
+  }
+  const float r = rsqrt_ieee(warp_sum(ss) / (float)K + p.eps);
+  for (int c = 0; c < CPL; ++c) {
+    float f[8], w[8];
+    unpack_bf16x8(src[lane + 32 * c], f);
+    unpack_bf16x8(reinterpret_cast<const uint4*>(p.norm_w)[lane + 32 * c], w);
+    __align__(16) bf16 o[8];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) ss += f[j] * f[j];
-      }
-      r = rsqrt_ieee(warp_sum(ss) / (float)K + p.eps);
-    }
-    for (int c = 0; c < CPL; ++c) {
-      float f[8];
-      unpack_bf16x8(src[lane + 32 * c], f);
-      if (PRO != Q35_PRO_PLAIN) {
-        float w[8];
-        unpack_bf16x8(reinterpret_cast<const uint4*>(p.norm_w)[lane + 32 * c], w);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) f[j] = bf2f(f2bf(f[j] * r * (1.0f + w[j])));
-      }
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        float* d = slot<K, NB>(xs, b, q, lane + 32 * c);
-        d[0] = f[2 * q];
-        d[2] = f[2 * q + 1];
-      }
-    }
+    for (int j = 0; j < 8; ++j) o[j] = f2bf(f[j] * r * (1.0f + w[j]));
+    dst[lane + 32 * c] = *reinterpret_cast<const uint4*>(o);
   }
 }
 
-// Rows a warp streams per group: SWIGLU streams a (gate, up) pair; otherwise 2 rows at K = 2048
-// and 1 at K = 6144 (24 chunks per lane already).
-template <int K, int EPI>
-constexpr int rows_per_group() {
-  return EPI == Q35_EPI_SWIGLU ? 2 : (K <= 2048 ? 2 : 1);
+Q35_DEV unsigned long long top1_key(float v, int idx) {
+  return ((unsigned long long)float_order_key(v) << 32) | (unsigned long long)(0xFFFFFFFFu - (uint32_t)idx);
 }
 
-template <int K, int NB, int PRO, int EPI>
-__global__ void __launch_bounds__(kThreads, 1) gemv_batch_kernel(BatchGemvParams p) {
-  constexpr int CH = K * 2 / 512;              // 16-byte chunks per lane per row
-  constexpr int U = rows_per_group<K, EPI>();  // rows per warp group
-  constexpr int UNITS = EPI == Q35_EPI_SWIGLU ? 1 : U;  // output units per group
-  constexpr int NP = NB / 2;
-  constexpr int NV = U * NB;
-  constexpr int NC = K / 8;
-  static_assert(NB >= 2 && NB % 2 == 0 && NB <= 8, "request pairs, at most 8 requests");
+template <int K, int PRO, int EPI>
+__global__ void __launch_bounds__(kThreads) gemv_batch_kernel(BatchGemvParams p) {
+  constexpr int KW = K / kWarps;       // K columns per warp
+  constexpr int NBK = KW / kBlk;       // blocks per warp
+  constexpr int STAGE = NBK > 8 ? 6 : NBK;  // blocks per register stage
+  constexpr int NST = NBK / STAGE;     // stages per group; more than one: two register buffers
+  constexpr int NBUF = NST > 1 ? 2 : 1;
+  static_assert(KW % kBlk == 0 && NBK % STAGE == 0, "K must split into whole blocks per warp");
+  // an even stage count keeps the buffer of each stage the same from group to group
+  static_assert(NST == 1 || NST % 2 == 0, "stages per group: one, or an even count");
+  constexpr int UNITS = (EPI == Q35_EPI_SWIGLU) ? 8 : 16;  // output units per 16-row group
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  float4* xs = reinterpret_cast<float4*>(smem_raw);
-  __shared__ float tot_s[kWarps][NV];
+  bf16* xs = reinterpret_cast<bf16*>(smem_raw);  // [8][K + 32]
+  __shared__ float4 part[kWarps][32];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
   const int n_out = p.n_out;
   const int ngroups = (n_out + UNITS - 1) / UNITS;
-  const int gstride = gridDim.x * kWarps;
-  int g = blockIdx.x * kWarps + warp;
   const char* W = reinterpret_cast<const char*>(p.weight);
-  auto row_of = [&](int grp, int u) -> int64_t {
-    return EPI == Q35_EPI_SWIGLU ? (int64_t)grp + (int64_t)u * n_out : (int64_t)grp * U + u;
-  };
-  auto unit_ok = [&](int grp, int u) -> bool {
-    return EPI == Q35_EPI_SWIGLU ? grp < n_out : grp * U + u < n_out;
-  };
-  uint4 wr[U][CH];
-  if (g < ngroups) {
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const char* base = W + row_of(g, u) * (K * 2) + lane * 16;
-#pragma unroll
-      for (int c = 0; c < CH; ++c) wr[u][c] = unit_ok(g, u) ? ld_stream(base + c * 512) : make_uint4(0, 0, 0, 0);
+  const int k0 = warp * KW;
+
+  // rows of lane g's two A-fragment rows in group grp (clamped in range; masked at the epilogue)
+  auto rows = [&](int grp, int64_t& r0, int64_t& r1, bool& ok0, bool& ok1) {
+    if (EPI == Q35_EPI_SWIGLU) {
+      const int u = grp * 8 + g;
+      ok0 = ok1 = u < n_out;
+      r0 = ok0 ? u : 0;
+      r1 = ok0 ? (int64_t)u + n_out : 0;
+    } else {
+      const int u0 = grp * 16 + g, u1 = u0 + 8;
+      ok0 = u0 < n_out;
+      ok1 = u1 < n_out;
+      r0 = ok0 ? u0 : 0;
+      r1 = ok1 ? u1 : 0;
     }
+  };
+  uint4 wa[NBUF][STAGE], wb[NBUF][STAGE];
+  auto load = [&](int grp, int stage, int buf) {
+    int64_t r0, r1;
+    bool ok0, ok1;
+    rows(grp, r0, r1, ok0, ok1);
+    const char* b0 = W + r0 * (K * 2) + (k0 + stage * STAGE * kBlk + 8 * t) * 2;
+    const char* b1 = W + r1 * (K * 2) + (k0 + stage * STAGE * kBlk + 8 * t) * 2;
+#pragma unroll
+    for (int i = 0; i < STAGE; ++i) {
+      wa[buf][i] = ok0 ? ld_stream(b0 + i * kBlk * 2) : make_uint4(0, 0, 0, 0);
+      wb[buf][i] = ok1 ? ld_stream(b1 + i * kBlk * 2) : make_uint4(0, 0, 0, 0);
+    }
+  };
+  int grp = blockIdx.x;
+  if (grp < ngroups) {
+    load(grp, 0, 0);
+    if (NST > 1) load(grp, 1, NBUF - 1);
   }
   pdl_wait();
   pdl_launch_dependents();
-  build_inputs<K, NB, PRO>(p, xs, warp, lane);
+  build_inputs<K, PRO>(p, xs, warp, lane);
   __syncthreads();
-  const int my = butterfly_index<NV>(lane);
-  for (; g < ngroups; g += gstride) {
-    const int gn = g + gstride;
-    float2 acc2[U][NP];
+
+  unsigned long long best[2] = {0ull, 0ull};  // TOP1: this lane's best keys for requests 2t, 2t + 1
+  const bf16* xrow = xs + g * xs_stride<K>() + k0 + 8 * t;
+  for (; grp < ngroups; grp += gridDim.x) {
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    // stage st computes from buffer st % NBUF; the buffer is refilled at once with the stage two
+    // ahead (or the next group's first stages), so one stage is always in flight
 #pragma unroll
-    for (int u = 0; u < U; ++u)
+    for (int st = 0; st < NST; ++st) {
+      const int buf = st % NBUF;
 #pragma unroll
-      for (int q = 0; q < NP; ++q) acc2[u][q] = make_float2(0.f, 0.f);
-#pragma unroll
-    for (int c = 0; c < CH; ++c) {
-      float w[U][8];
-#pragma unroll
-      for (int u = 0; u < U; ++u) unpack_bf16x8(wr[u][c], w[u]);
-#pragma unroll
-      for (int u = 0; u < U; ++u)
-        wr[u][c] = (gn < ngroups && unit_ok(gn, u)) ? ld_stream(W + row_of(gn, u) * (K * 2) + lane * 16 + c * 512)
-                                                    : make_uint4(0, 0, 0, 0);
-#pragma unroll
-      for (int pr = 0; pr < NP; ++pr) {
-        float2 x[8];
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const float4 v = xs[(q * NP + pr) * NC + lane + 32 * c];
-          x[2 * q] = make_float2(v.x, v.y);
-          x[2 * q + 1] = make_float2(v.z, v.w);
-        }
-#pragma unroll
-        for (int u = 0; u < U; ++u)
-#pragma unroll
-          for (int j = 0; j < 8; ++j) acc2[u][pr] = __ffma2_rn(make_float2(w[u][j], w[u][j]), x[j], acc2[u][pr]);
+      for (int i = 0; i < STAGE; ++i) {
+        const uint4 x = *reinterpret_cast<const uint4*>(xrow + (st * STAGE + i) * kBlk);
+        mma_bf16(acc, wa[buf][i].x, wb[buf][i].x, wa[buf][i].y, wb[buf][i].y, x.x, x.y);
+        mma_bf16(acc, wa[buf][i].z, wb[buf][i].z, wa[buf][i].w, wb[buf][i].w, x.z, x.w);
       }
-      asm volatile("" ::: "memory");
+      const int nxt = st + NBUF;  // the stage this buffer holds next
+      if (nxt < NST)
+        load(grp, nxt, buf);
+      else if (grp + (int)gridDim.x < ngroups)
+        load(grp + gridDim.x, nxt - NST, buf);
     }
-    float acc[NV];
+    part[warp][lane] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+    __syncthreads();
+    if (warp == 0) {
+      float4 s = part[0][lane];
 #pragma unroll
-    for (int u = 0; u < U; ++u)
-#pragma unroll
-      for (int q = 0; q < NP; ++q) {
-        acc[u * NB + 2 * q] = acc2[u][q].x;
-        acc[u * NB + 2 * q + 1] = acc2[u][q].y;
+      for (int w = 1; w < kWarps; ++w) {
+        const float4 q = part[w][lane];
+        s.x += q.x;
+        s.y += q.y;
+        s.z += q.z;
+        s.w += q.w;
       }
-    const float v = butterfly_sum<NV>(acc, lane);
-    if (butterfly_writer<NV>(lane)) tot_s[warp][my] = v;
-    __syncwarp();
-    // lane (u, b) applies the epilogue of output unit u for request b
-    if (lane < UNITS * NB) {
-      const int u = lane / NB, b = lane % NB;
-      if (b < p.n && unit_ok(g, u)) {
+      // lane (g, t): rows g / g + 8 of the group, requests 2t / 2t + 1
+      const float d[4] = {s.x, s.y, s.z, s.w};
+      int64_t r0, r1;
+      bool ok0, ok1;
+      rows(grp, r0, r1, ok0, ok1);
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int b = 2 * t + e;
+        if (b >= p.n) continue;
         if (EPI == Q35_EPI_SWIGLU) {
-          const float gt = rbf(tot_s[warp][b]), up = rbf(tot_s[warp][NB + b]);
-          p.out[(int64_t)b * n_out + g] = f2bf(rbf(silu_f(gt)) * up);
+          if (ok0) p.out[(int64_t)b * n_out + r0] = f2bf(rbf(silu_f(rbf(d[e]))) * rbf(d[2 + e]));
+        } else if (EPI == kEpiTop1) {
+          if (ok0) {
+            const unsigned long long k = top1_key(rbf(d[e]), (int)r0);
+            best[e] = k > best[e] ? k : best[e];
+          }
+          if (ok1) {
+            const unsigned long long k = top1_key(rbf(d[2 + e]), (int)r1);
+            best[e] = k > best[e] ? k : best[e];
+          }
         } else {
-          const int64_t o = (int64_t)b * n_out + g * U + u;
-          const float y = tot_s[warp][u * NB + b];
-          if (EPI == Q35_EPI_RESIDUAL)
-            p.resid[o] = f2bf(bf2f(p.resid[o]) + rbf(y));
-          else
-            p.out[o] = f2bf(y);
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            if (!(h ? ok1 : ok0)) continue;
+            const int64_t o = (int64_t)b * n_out + (h ? r1 : r0);
+            const float y = d[2 * h + e];
+            if (EPI == Q35_EPI_RESIDUAL)
+              p.resid[o] = f2bf(bf2f(p.resid[o]) + rbf(y));
+            else
+              p.out[o] = f2bf(y);
+          }
         }
       }
     }
-    __syncwarp();
+    __syncthreads();  // part[] is rewritten by the next group
+  }
+  if (EPI == kEpiTop1) {
+    if (warp == 0) {
+      // lanes with the same t hold the same requests: reduce over g (lane bits 2-4)
+#pragma unroll
+      for (int e = 0; e < 2; ++e)
+#pragma unroll
+        for (int o = 4; o < 32; o <<= 1) {
+          const unsigned long long other = __shfl_xor_sync(0xffffffffu, best[e], o);
+          best[e] = other > best[e] ? other : best[e];
+        }
+      if (g == 0) {
+        if (2 * t < p.n && best[0]) atomicMax(p.top1 + 2 * t, best[0]);
+        if (2 * t + 1 < p.n && best[1]) atomicMax(p.top1 + 2 * t + 1, best[1]);
+      }
+      __threadfence();
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      unsigned* count = reinterpret_cast<unsigned*>(p.top1 + kBatch);
+      __threadfence();
+      const unsigned prev = atomicAdd(count, 1u);
+      if (prev == gridDim.x - 1) {
+        __threadfence();
+        for (int b = 0; b < p.n; ++b) {
+          const unsigned long long key = atomicExch(p.top1 + b, 0ull);
+          p.keys_out[b] = (long long)(key ^ 0x8000000000000000ull);
+        }
+        atomicExch(count, 0u);
+      }
+    }
   }
 }
 
-template <int K, int NB, int PRO, int EPI>
-int launch_nb(const BatchGemvParams& p, cudaStream_t s, bool pdl) {
-  constexpr size_t smem = (size_t)NB * K * 4;
+template <int K, int PRO, int EPI>
+int launch(const BatchGemvParams& p, cudaStream_t s, bool pdl) {
+  constexpr size_t smem = (size_t)kBatch * xs_stride<K>() * sizeof(bf16);
   static Q35PerDevice<int> ctas_of;
   const int ctas = ctas_of.get([] {
-    cudaFuncSetAttribute(gemv_batch_kernel<K, NB, PRO, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaFuncSetAttribute(gemv_batch_kernel<K, PRO, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     int per_sm = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemv_batch_kernel<K, NB, PRO, EPI>, kThreads, smem) !=
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemv_batch_kernel<K, PRO, EPI>, kThreads, smem) !=
             cudaSuccess ||
         per_sm < 1)
       per_sm = 1;
     cudaGetLastError();
     return per_sm * kNumSMs;
   });
-  constexpr int UNITS = EPI == Q35_EPI_SWIGLU ? 1 : rows_per_group<K, EPI>();
+  constexpr int UNITS = (EPI == Q35_EPI_SWIGLU) ? 8 : 16;
   const int ngroups = (p.n_out + UNITS - 1) / UNITS;
-  int grid = (ngroups + kWarps - 1) / kWarps;
-  if (grid > ctas) grid = ctas;
-  const cudaError_t e = q35_launch(gemv_batch_kernel<K, NB, PRO, EPI>, dim3(grid), dim3(kThreads), smem, s, pdl, p);
+  const int grid = ngroups < ctas ? ngroups : ctas;
+  const cudaError_t e = q35_launch(gemv_batch_kernel<K, PRO, EPI>, dim3(grid), dim3(kThreads), smem, s, pdl, p);
   if (e != cudaSuccess) return q35_fail(Q35_ECUDA, "batched gemv launch: %s", cudaGetErrorString(e));
   return Q35_OK;
 }
 
-template <int K, int PRO, int EPI>
-int launch_k(const BatchGemvParams& p, cudaStream_t s, bool pdl) {
-  if (p.n <= 2) return launch_nb<K, 2, PRO, EPI>(p, s, pdl);
-  if (p.n <= 4) return launch_nb<K, 4, PRO, EPI>(p, s, pdl);
-  return launch_nb<K, 8, PRO, EPI>(p, s, pdl);
-}
-
-}  // namespace
-
-// The decoder's batched projections (same descriptor as the batch-1 GEMV, `batch` vectors).
-int q35_gemv_batch_launch(const q35_gemv_desc* d, int64_t batch, cudaStream_t s, bool pdl) {
-  Q35_REQUIRE(d && d->weight, "gemv_batch: null descriptor");
-  Q35_REQUIRE(batch >= 1 && batch <= 8, "gemv_batch: batch %lld outside [1, 8]", (long long)batch);
-  Q35_REQUIRE(!d->int8, "gemv_batch: bf16 weights only (the A8W8 decode path is batch 1)");
+BatchGemvParams params_of(const q35_gemv_desc* d, int64_t batch) {
   BatchGemvParams p = {};
   p.weight = static_cast<const bf16*>(d->weight);
   p.input = static_cast<const bf16*>(d->input);
@@ -252,26 +291,54 @@ int q35_gemv_batch_launch(const q35_gemv_desc* d, int64_t batch, cudaStream_t s,
   p.n = (int)batch;
   p.n_out = (int)d->n_out;
   p.eps = d->eps;
+  return p;
+}
+
+}  // namespace
+
+// The decoder's batched projections (same descriptor as the batch-1 GEMV, `batch` vectors).
+int q35_gemv_batch_launch(const q35_gemv_desc* d, int64_t batch, cudaStream_t s, bool pdl) {
+  Q35_REQUIRE(d && d->weight, "gemv_batch: null descriptor");
+  Q35_REQUIRE(batch >= 1 && batch <= kBatch, "gemv_batch: batch %lld outside [1, 8]", (long long)batch);
+  Q35_REQUIRE(!d->int8, "gemv_batch: bf16 weights only (the A8W8 decode path is batch 1)");
+  Q35_REQUIRE(Q35_ALIGNED(d->weight, 16), "gemv_batch: 16-byte aligned weights");
+  const BatchGemvParams p = params_of(d, batch);
   const int pro = d->prologue, epi = d->epilogue;
-  Q35_REQUIRE(pro != Q35_PRO_PLAIN || p.input, "gemv_batch: PLAIN needs an input");
+  Q35_REQUIRE(pro == Q35_PRO_EMBED || p.input, "gemv_batch: PLAIN / NORM need an input");
   Q35_REQUIRE(pro == Q35_PRO_PLAIN || p.norm_w, "gemv_batch: NORM / EMBED need the norm weight");
   Q35_REQUIRE(pro != Q35_PRO_EMBED || (p.token && p.embed && p.resid), "gemv_batch: EMBED needs tokens, table, resid");
-  Q35_REQUIRE(pro != Q35_PRO_NORM || p.input, "gemv_batch: NORM needs an input");
   Q35_REQUIRE(epi == Q35_EPI_RESIDUAL ? p.resid != nullptr : p.out != nullptr, "gemv_batch: missing output");
   if (d->k == 2048) {
-    if (epi == Q35_EPI_SWIGLU) {
-      if (pro == Q35_PRO_NORM) return launch_k<2048, Q35_PRO_NORM, Q35_EPI_SWIGLU>(p, s, pdl);
-    } else if (epi == Q35_EPI_STORE) {
-      if (pro == Q35_PRO_NORM) return launch_k<2048, Q35_PRO_NORM, Q35_EPI_STORE>(p, s, pdl);
-      if (pro == Q35_PRO_EMBED) return launch_k<2048, Q35_PRO_EMBED, Q35_EPI_STORE>(p, s, pdl);
-    } else if (epi == Q35_EPI_RESIDUAL) {
-      if (pro == Q35_PRO_PLAIN) return launch_k<2048, Q35_PRO_PLAIN, Q35_EPI_RESIDUAL>(p, s, pdl);
-    }
+    if (epi == Q35_EPI_SWIGLU && pro == Q35_PRO_NORM) return launch<2048, Q35_PRO_NORM, Q35_EPI_SWIGLU>(p, s, pdl);
+    if (epi == Q35_EPI_STORE && pro == Q35_PRO_NORM) return launch<2048, Q35_PRO_NORM, Q35_EPI_STORE>(p, s, pdl);
+    if (epi == Q35_EPI_STORE && pro == Q35_PRO_EMBED) return launch<2048, Q35_PRO_EMBED, Q35_EPI_STORE>(p, s, pdl);
+    if (epi == Q35_EPI_RESIDUAL && pro == Q35_PRO_PLAIN)
+      return launch<2048, Q35_PRO_PLAIN, Q35_EPI_RESIDUAL>(p, s, pdl);
   } else if (d->k == 6144) {
-    if (epi == Q35_EPI_RESIDUAL && pro == Q35_PRO_PLAIN) return launch_k<6144, Q35_PRO_PLAIN, Q35_EPI_RESIDUAL>(p, s, pdl);
+    if (epi == Q35_EPI_RESIDUAL && pro == Q35_PRO_PLAIN)
+      return launch<6144, Q35_PRO_PLAIN, Q35_EPI_RESIDUAL>(p, s, pdl);
   }
   return q35_fail(Q35_ENOTSUP, "gemv_batch: k=%lld with prologue %d / epilogue %d is not a decoder projection",
                   (long long)d->k, pro, epi);
+}
+
+// Batched LM head: RMSNorm of the `batch` final residuals, logits over the whole tied table, one
+// reduced top-1 key per request in keys_out (the q35_lm_head_shard_keys encoding; workspace of
+// q35_lm_shard_workspace_size() bytes, zero before, left zero).
+int q35_lm_head_batch_launch(const void* hidden, int64_t batch, const void* norm_weight, const void* weight,
+                             int64_t vocab, float eps, int64_t* keys_out, void* workspace, cudaStream_t s, bool pdl) {
+  Q35_REQUIRE(hidden && norm_weight && weight && keys_out && workspace, "lm_head_batch: null pointer");
+  Q35_REQUIRE(batch >= 1 && batch <= kBatch && vocab > 0 && vocab < (1ll << 31), "lm_head_batch: bad shape");
+  BatchGemvParams p = {};
+  p.weight = static_cast<const bf16*>(weight);
+  p.input = static_cast<const bf16*>(hidden);
+  p.norm_w = static_cast<const bf16*>(norm_weight);
+  p.top1 = static_cast<unsigned long long*>(workspace);
+  p.keys_out = reinterpret_cast<long long*>(keys_out);
+  p.n = (int)batch;
+  p.n_out = (int)vocab;
+  p.eps = eps;
+  return launch<2048, Q35_PRO_NORM, kEpiTop1>(p, s, pdl);
 }
 
 extern "C" int q35_gemv_batch(const q35_gemv_desc* desc, int64_t batch, void* stream) {
