@@ -63,8 +63,9 @@ def test_batched_projections_match_the_batch1_projection(batch):
         K.fused_gemv(w_out, act[b, :H].contiguous(), epilogue=L.EPI_RESIDUAL, resid=ro)
         assert_bf16_close(y_in[b].cpu(), want_in.cpu(), max_ulp=1, max_frac=0.02)
         assert rel_err(y_gu[b], want_gu) < 5e-3
-        assert_bf16_close(r_dn[b].cpu(), rd.cpu(), max_ulp=1, max_frac=0.02)
-        assert_bf16_close(r_out[b].cpu(), ro.cpu(), max_ulp=1, max_frac=0.02)
+        # residual adds: one ulp of the update (summation order) plus one of the sum
+        assert_bf16_close(r_dn[b].cpu(), rd.cpu(), max_ulp=2, max_frac=0.02)
+        assert_bf16_close(r_out[b].cpu(), ro.cpu(), max_ulp=2, max_frac=0.02)
 
 
 def test_batched_embedding_prologue():
