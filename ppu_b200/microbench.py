@@ -339,6 +339,26 @@ def run(kernels: list[str], reps: int, layers: int = 24, a8w8: bool = False):
                     L.call("q35_gemm_tc_bias", a.data_ptr(), ws[i % 4].data_ptr(), bias.data_ptr(), y.data_ptr(), m, n,
                            k, epi, L.stream_of(dev))
                 report(f"vision_gemm_{tag}_{m}x{n}x{k}", _time(gm, reps), flops=2 * m * n * k)
+        elif name == "batched_step_one":
+            # one warm decode step of the 2B shape at batch 8 (after 1024-token prefills of every
+            # slot) between cudaProfilerStart / Stop: the launch-list target of the batched path
+            from .config import Qwen35Dims
+            from .engine import Qwen35Engine
+            from .synthetic import make_prompt, make_weights
+            dims = Qwen35Dims()
+            eng = Qwen35Engine(make_weights(dims, seed=0, device=dev), dims, max_len=1152, max_prefill=1024, batch=8)
+            for slot in range(8):
+                eng.prefill(make_prompt(dims, 1024, seed=10 + slot)[0].to(dev), slot)
+            graph = eng.capture(1)
+            for _ in range(3):
+                graph.replay()
+            torch.cuda.synchronize()
+            torch.cuda.profiler.start()
+            graph.replay()
+            torch.cuda.synchronize()
+            torch.cuda.profiler.stop()
+            report("batched_step_one", 0.0)
+            del eng
         elif name in ("mm_request_one",):
             # one warm config-5 request (ViT graph + 496-token multimodal prefill + 15 decode steps)
             # between cudaProfilerStart / Stop: the launch-list target
