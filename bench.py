@@ -355,14 +355,14 @@ def gate_up_roofline(eng, dims, dev, hbm_peak, peak_kind, a8w8: bool):
             "peak_kind": peak_kind}
 
 
-def vision_engine(dev):
+def vision_engine(dev, max_images=1):
     from ppu_b200.config import VisionDims
     from ppu_b200.synthetic import make_vision_weights
     from ppu_b200.vision import VisionEngine
 
     vd = VisionDims()
     vw = make_vision_weights(vd, seed=1, device=dev)
-    return VisionEngine(vw, vd, max_image=(448, 448), device=dev)
+    return VisionEngine(vw, vd, max_image=(448, 448), device=dev, max_patches=max_images * 784)
 
 
 def multimodal_leg(eng, vis, decode_graph, dims, dev, rank, world, args, tf_sust, peak_kind):
@@ -390,17 +390,31 @@ def multimodal_leg(eng, vis, decode_graph, dims, dev, rank, world, args, tf_sust
     imgs = [image(i) for i in mine]
     texts = [make_prompt(dims, n_text, seed=200_000 + i)[0].to(dev) for i in mine]
     groups = [list(range(j, min(j + nb, len(mine)))) for j in range(0, len(mine), nb)]
+    # batched engines: a group's images go through the ViT together and its prompts through one
+    # prefill (inputs stacked once, resident like the single images)
+    together = mm.group_prefill
+    stacked = {g[0]: (torch.stack([imgs[j] for j in g]), torch.stack([texts[j] for j in g])) for g in groups} \
+        if together else {}
 
     def group(js, ev=None):
         if ev:
             ev["start"].record()
-        for slot, j in enumerate(js):
-            tokens = mm.encode_image(imgs[j])
+        if together:
+            pix, ids = stacked[js[0]]
+            tokens = mm.encode_images(pix)
             if ev:
-                ev["vis"][slot].record()
-            mm.prefill_prompt(tokens, texts[j], slot)
+                ev["vis"][0].record()
+            mm.prefill_group(tokens, ids, 0)
             if ev:
-                ev["first"][slot].record()
+                ev["first"][0].record()
+        else:
+            for slot, j in enumerate(js):
+                tokens = mm.encode_image(imgs[j])
+                if ev:
+                    ev["vis"][slot].record()
+                mm.prefill_prompt(tokens, texts[j], slot)
+                if ev:
+                    ev["first"][slot].record()
         for _ in range(n_new - 1):
             mm.decode_step()
         if ev:
@@ -408,6 +422,7 @@ def multimodal_leg(eng, vis, decode_graph, dims, dev, rank, world, args, tf_sust
 
     def events(n):
         e = lambda: torch.cuda.Event(enable_timing=True)  # noqa: E731
+        n = 1 if together else n
         return {"start": e(), "end": e(), "vis": [e() for _ in range(n)], "first": [e() for _ in range(n)]}
 
     for js in groups[:min(2, len(groups))]:
@@ -422,11 +437,15 @@ def multimodal_leg(eng, vis, decode_graph, dims, dev, rank, world, args, tf_sust
     R.barrier()
     total_ms = R.max_over_ranks(evs[0]["start"].elapsed_time(evs[-1]["end"]), dev)
     vis_ms, ttft_ms, dec_ms = [], [], []
-    for ev in evs:
+    for js, ev in zip(groups, evs):
         prev = ev["start"]
         for v, f in zip(ev["vis"], ev["first"]):
-            vis_ms.append(prev.elapsed_time(v))
-            ttft_ms.append(ev["start"].elapsed_time(f))
+            if together:  # one encode of the group's images: its time per image; the group's TTFT
+                vis_ms += [prev.elapsed_time(v) / len(js)] * len(js)
+                ttft_ms += [ev["start"].elapsed_time(f)] * len(js)
+            else:
+                vis_ms.append(prev.elapsed_time(v))
+                ttft_ms.append(ev["start"].elapsed_time(f))
             prev = f
         dec_ms.append(ev["first"][-1].elapsed_time(ev["end"]))
     mean = lambda xs: R.max_over_ranks(sum(xs) / len(xs), dev)  # noqa: E731
@@ -439,6 +458,8 @@ def multimodal_leg(eng, vis, decode_graph, dims, dev, rank, world, args, tf_sust
         "tok_per_s": round(args.mm_requests * n_new / (total_ms / 1e3), 1),
         "ttft_ms_mean": round(t_ms, 3), "vision_ms_mean": round(v_ms, 3),
         "decode_ms_per_step": round(d_ms / max(n_new - 1, 1), 4), "requests_per_decode_step": nb,
+        "prefill": (f"{mm.group_images} images per ViT encode, {nb} prompts per prefill" if together
+                    else "one image per ViT encode, one prompt per prefill"),
         "vision_roofline": {"flops": vflops, "achieved_tflops": round(vflops / (v_ms / 1e3) / 1e12, 1),
                             "peak_tflops": tf_sust, "frac": round(vflops / (v_ms / 1e3) / 1e12 / tf_sust, 4),
                             "bound": "tensor", "peak_kind": f"{peak_kind} bf16 sustained"},
@@ -525,8 +546,11 @@ def main():
                        persistent=(args.decode == "persistent" and not headline_a8w8))
     engB = None
     if args.batch > 1 and not headline_a8w8:
-        engB = Qwen35Engine(weights, dims, max_len=cache_bucket(P, T), max_prefill=P, device=dev, batch=args.batch,
-                            use_pdl=not args.no_pdl, prefill_chunked=args.prefill_delta == "chunked")
+        # its prefill rows also hold a whole group of config-5 prompts (196 image + 300 text tokens)
+        mm_rows = args.batch * (196 + 300) if args.mm_requests > 0 else 0
+        engB = Qwen35Engine(weights, dims, max_len=cache_bucket(P, T), max_prefill=max(P, mm_rows), device=dev,
+                            batch=args.batch, use_pdl=not args.no_pdl,
+                            prefill_chunked=args.prefill_delta == "chunked")
     eng8 = None
     if not headline_a8w8 and not args.no_a8w8_leg:
         eng8 = Qwen35Engine(weights, dims, a8w8=True, max_len=cache_bucket(P, T), max_prefill=P, device=dev,
@@ -661,7 +685,7 @@ def main():
     batched = batched_decode_leg(engB, dims, dev, rank, world, args, hbm_peak, peak_kind) if engB else None
     mm = mm_batched = mm_shard = None
     if args.mm_requests > 0:
-        vis = vision_engine(dev)
+        vis = vision_engine(dev, max_images=engB.batch if engB is not None else 1)
         mm = multimodal_leg(eng, vis, None, dims, dev, rank, world, args, tf_sust, peak_kind)
         if engB is not None:
             mm_batched = multimodal_leg(engB, vis, None, dims, dev, rank, world, args, tf_sust, peak_kind)

@@ -389,6 +389,15 @@ int q35_decoder_prefill_mm(q35_decoder* dec, const int64_t* ids, int64_t length,
  * with the same length before the batch decodes (evaluation_wrapper.py:338-341 pads a batch to
  * one cache bucket the same way). q35_decoder_prefill is slot 0. */
 int q35_decoder_prefill_slot(q35_decoder* dec, const int64_t* ids, int64_t length, int64_t slot, void* stream);
+/* Batched decoders: prefill `nseq` requests of `length` tokens each (ids [nseq * length]) into slots
+ * [slot, slot + nseq) in one pass: the projections, norms and GEMMs take all nseq * length rows,
+ * the DeltaNet scans, causal attention and cache writes run per request, and one LM-head pass
+ * over the tied table gives every request's first token. image_rows index the nseq * length
+ * rows; positions3 (optional) is int64 [3, nseq, length]; rope_next = -1 leaves rope_pos =
+ * length. nseq * length <= max_prefill. */
+int q35_decoder_prefill_batch(q35_decoder* dec, const int64_t* ids, int64_t length, int64_t nseq,
+                              const void* image_embeds, const int64_t* image_rows, int64_t n_image,
+                              const int64_t* positions3, int64_t rope_next, int64_t slot, void* stream);
 /* The decoder's batched projection (no counterpart in the reference, whose decode is batch 1):
  * q35_gemv for `batch` <= 8 input vectors [batch, k] / outputs [batch, n_out] at once, the weights
  * streamed once; bf16, k 2048 (NORM / EMBED + STORE, NORM + SWIGLU, PLAIN + RESIDUAL) or 6144
@@ -513,6 +522,11 @@ void q35_vit_destroy(q35_vit* vit);
  * [(height/patch/merge)*(width/patch/merge), out_width]. */
 int q35_vit_encode(q35_vit* vit, const float* pixels, int64_t height, int64_t width, void* out,
                    void* stream);
+/* The same forward for `images` images of one size, fp32 [images, C, height, width]: every launch
+ * covers the whole batch (the GEMMs take images * patches rows; attention runs per image), out
+ * bf16 [images * merged tokens, out_width] in image order. images * patches <= max_patches. */
+int q35_vit_encode_batch(q35_vit* vit, const float* pixels, int64_t images, int64_t height, int64_t width,
+                         void* out, void* stream);
 /* The same forward from the processor's patches (Transformers' pixel_values for one image,
  * fp32 [grid_h*grid_w, in_channels*temporal_patch*patch^2] in merge-block order, the input of
  * Qwen3_5VisionModel.forward that integration.py:576-637 patches). */

@@ -46,7 +46,7 @@ __global__ void __launch_bounds__(kD) qgkv_rope_kernel(
       if (pos3) {  // interleaved M-RoPE: frequency j takes the height / width axis at j % 3 == 1 / 2
         const int j = d % (rot / 2);
         const int axis = (j % 3 == 1 && j < 3 * sec_h) ? 1 : (j % 3 == 2 && j < 3 * sec_w) ? 2 : 0;
-        pos = pos3[(int64_t)axis * L + t];
+        pos = pos3[((int64_t)axis * (gridDim.x / L) + b) * L + t];  // [3, batch, L]
       }
       rope_cs(d, rot / 2, (float)pos, inv_freq, c, s);
     }
@@ -335,7 +335,7 @@ extern "C" int q35_qgkv_norm_rope(const void* packed, const void* q_weight, cons
 }
 
 // Prefill variant used by the decoder: RoPE from positions cache_start + t (text tokens).
-// With pos3 (int64 [3, seq_len], batch 1), the positions are 3-axis M-RoPE positions interleaved
+// With pos3 (int64 [3, batch, seq_len]), the positions are 3-axis M-RoPE positions interleaved
 // by (sec_h, sec_w) frequency pairs (Transformers apply_interleaved_mrope).
 int q35_qgkv_rope_positions_launch(const void* packed, const void* q_weight, const void* k_weight,
                                    const float* inv_freq, void* q_out, void* k_out, void* v_out,

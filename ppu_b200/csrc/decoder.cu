@@ -138,7 +138,8 @@ Buffers carve(const q35_decoder_desc& d, void* base, size_t* total) {
   if (mixw > qw) qw = mixw;
   b.p_q8 = c.take<int8_t>(L * qw);
   b.p_sx = c.take<float>(L);
-  b.p_chunk = c.take<float>(q35_delta_chunk_workspace_bytes(1, d.lin_heads, L) / sizeof(float));
+  // batched prefill: up to `nb` sequences sharing the L rows, each padded to whole chunks
+  b.p_chunk = c.take<float>(q35_delta_chunk_workspace_bytes(1, d.lin_heads, L + 64 * nb) / sizeof(float));
   *total = c.off + 256;
   return b;
 }
@@ -382,45 +383,61 @@ struct MmInputs {
 };
 
 static int prefill_impl(q35_decoder* dec, const int64_t* ids, int64_t length, const MmInputs& mm, int64_t slot,
-                        cudaStream_t s);
+                        int64_t nseq, cudaStream_t s);
 
 extern "C" int q35_decoder_prefill(q35_decoder* dec, const int64_t* ids, int64_t length, void* stream) {
   Q35_REQUIRE(dec && ids, "prefill: null argument");
-  return prefill_impl(dec, ids, length, MmInputs{}, 0, (cudaStream_t)stream);
+  return prefill_impl(dec, ids, length, MmInputs{}, 0, 1, (cudaStream_t)stream);
 }
 
 extern "C" int q35_decoder_prefill_slot(q35_decoder* dec, const int64_t* ids, int64_t length, int64_t slot,
                                         void* stream) {
   Q35_REQUIRE(dec && ids, "prefill_slot: null argument");
-  return prefill_impl(dec, ids, length, MmInputs{}, slot, (cudaStream_t)stream);
+  return prefill_impl(dec, ids, length, MmInputs{}, slot, 1, (cudaStream_t)stream);
 }
 
-extern "C" int q35_decoder_prefill_mm(q35_decoder* dec, const int64_t* ids, int64_t length, const void* image_embeds,
-                                      const int64_t* image_rows, int64_t n_image, const int64_t* positions3,
-                                      int64_t rope_next, int64_t slot, void* stream) {
-  Q35_REQUIRE(dec && ids, "prefill_mm: null argument");
-  Q35_REQUIRE(n_image >= 0 && n_image <= length && (n_image == 0 || (image_embeds && image_rows)),
-              "prefill_mm: %lld image rows need embeddings and row indices", (long long)n_image);
+extern "C" int q35_decoder_prefill_batch(q35_decoder* dec, const int64_t* ids, int64_t length, int64_t nseq,
+                                         const void* image_embeds, const int64_t* image_rows, int64_t n_image,
+                                         const int64_t* positions3, int64_t rope_next, int64_t slot, void* stream) {
+  Q35_REQUIRE(dec && ids, "prefill_batch: null argument");
+  Q35_REQUIRE(nseq >= 1 && length >= 1 && n_image >= 0 && n_image <= nseq * length &&
+                  (n_image == 0 || (image_embeds && image_rows)),
+              "prefill_batch: %lld sequences of %lld tokens, %lld image rows (embeddings and row indices needed)",
+              (long long)nseq, (long long)length, (long long)n_image);
   Q35_REQUIRE(!image_embeds || Q35_ALIGNED(image_embeds, 16), "prefill_mm: image embeddings 16-byte aligned");
   Q35_REQUIRE(!positions3 || dec->d.mrope_section[1] + dec->d.mrope_section[2] > 0,
               "prefill_mm: 3-axis positions need the decoder's mrope_section");
-  Q35_REQUIRE(rope_next >= 0, "prefill_mm: rope_next must be non-negative");
+  Q35_REQUIRE(rope_next >= -1, "prefill_mm: rope_next must be non-negative (or -1: the prompt length)");
   MmInputs mm;
   mm.image_embeds = image_embeds;
   mm.image_rows = image_rows;
   mm.n_image = n_image;
   mm.pos3 = positions3;
   mm.rope_next = rope_next;
-  return prefill_impl(dec, ids, length, mm, slot, (cudaStream_t)stream);
+  return prefill_impl(dec, ids, length, mm, slot, nseq, (cudaStream_t)stream);
 }
 
+extern "C" int q35_decoder_prefill_mm(q35_decoder* dec, const int64_t* ids, int64_t length, const void* image_embeds,
+                                      const int64_t* image_rows, int64_t n_image, const int64_t* positions3,
+                                      int64_t rope_next, int64_t slot, void* stream) {
+  Q35_REQUIRE(rope_next >= 0, "prefill_mm: rope_next must be non-negative");
+  return q35_decoder_prefill_batch(dec, ids, length, 1, image_embeds, image_rows, n_image, positions3, rope_next, slot,
+                                   stream);
+}
+
+// `nseq` sequences of `length` tokens each (ids [nseq * length]) into request slots
+// [slot, slot + nseq): every projection, norm and GEMM runs over all nseq * length rows at once;
+// the DeltaNet scan, the causal attention and the KV-cache writes run per sequence; the LM head
+// reads each sequence's last row.
 static int prefill_impl(q35_decoder* dec, const int64_t* ids, int64_t length, const MmInputs& mm, int64_t slot,
-                        cudaStream_t s) {
+                        int64_t nseq, cudaStream_t s) {
   const q35_decoder_desc& d = dec->d;
-  Q35_REQUIRE(length >= 1 && length <= d.max_prefill && length < d.max_len,
-              "prefill: length %lld outside [1, %d] (cache %d)", (long long)length, d.max_prefill, d.max_len);
-  Q35_REQUIRE(slot >= 0 && slot < (d.batch > 1 ? d.batch : 1), "prefill: slot %lld outside the batch of %d",
-              (long long)slot, d.batch > 1 ? d.batch : 1);
+  const int64_t nb = d.batch > 1 ? d.batch : 1;
+  Q35_REQUIRE(length >= 1 && nseq >= 1 && nseq * length <= d.max_prefill && length < d.max_len,
+              "prefill: %lld x %lld tokens outside [1, %d] (cache %d)", (long long)nseq, (long long)length,
+              d.max_prefill, d.max_len);
+  Q35_REQUIRE(slot >= 0 && slot + nseq <= nb, "prefill: slots [%lld, %lld) outside the batch of %lld",
+              (long long)slot, (long long)(slot + nseq), (long long)nb);
   // this slot's states and caches: the layers' tensors have a leading batch dimension
   const int64_t conv_elems = (int64_t)d.lin_heads * (2 * d.lin_dk + d.lin_dv) * d.conv_kernel;
   const int64_t rec_elems = (int64_t)d.lin_heads * d.lin_dk * d.lin_dv;
@@ -435,7 +452,7 @@ static int prefill_impl(q35_decoder* dec, const int64_t* ids, int64_t length, co
   int64_t* token_out = d.token + slot;
   const Buffers& B = dec->buf;
   const bool q8 = d.a8w8 != 0;
-  const int64_t H = d.hidden, I = d.intermediate, Lt = length;
+  const int64_t H = d.hidden, I = d.intermediate, Lt = length, R = nseq * length;  // R rows in all
   const int64_t qgkv_rows = 2 * d.q_heads * d.head_dim + 2 * d.kv_heads * d.head_dim;
   const int64_t conv_dim = (int64_t)d.lin_heads * (2 * d.lin_dk + d.lin_dv);
   const int64_t vdim = (int64_t)d.lin_heads * d.lin_dv;
@@ -447,78 +464,86 @@ static int prefill_impl(q35_decoder* dec, const int64_t* ids, int64_t length, co
   auto proj = [&](const bf16* x, int64_t k, const void* w, const float* sw, void* out, int64_t n, int epi) -> int {
     const bool tc = d.prefill_tc && (k * (q8 ? 1 : 2)) % 128 == 0 && n % 8 == 0;
     if (!q8)
-      return tc ? q35_gemm_tc_launch(x, w, out, Lt, n, k, epi, false, nullptr, nullptr, s)
-                : q35_gemm_launch(x, w, out, Lt, n, k, epi, false, nullptr, nullptr, s);
-    int rc = q35_quantize_tokens_launch(x, B.p_q8, B.p_sx, Lt, k, s);
+      return tc ? q35_gemm_tc_launch(x, w, out, R, n, k, epi, false, nullptr, nullptr, s)
+                : q35_gemm_launch(x, w, out, R, n, k, epi, false, nullptr, nullptr, s);
+    int rc = q35_quantize_tokens_launch(x, B.p_q8, B.p_sx, R, k, s);
     if (rc) return rc;
-    if (dec->probe) {  // record [codes Lt x k][scales Lt] of this projection's input
-      const size_t codes = (size_t)Lt * k, need = codes + (size_t)Lt * sizeof(float);
+    if (dec->probe) {  // record [codes R x k][scales R] of this projection's input
+      const size_t codes = (size_t)R * k, need = codes + (size_t)R * sizeof(float);
       if (dec->probe_want + need <= dec->probe_bytes &&
           (cudaMemcpyAsync(dec->probe + dec->probe_want, B.p_q8, codes, cudaMemcpyDeviceToDevice, s) != cudaSuccess ||
-           cudaMemcpyAsync(dec->probe + dec->probe_want + codes, B.p_sx, (size_t)Lt * sizeof(float),
+           cudaMemcpyAsync(dec->probe + dec->probe_want + codes, B.p_sx, (size_t)R * sizeof(float),
                            cudaMemcpyDeviceToDevice, s) != cudaSuccess))
         return q35_fail(Q35_ECUDA, "prefill: probe copy failed");
       dec->probe_want += need;
     }
-    return tc ? q35_gemm_tc_launch(B.p_q8, w, out, Lt, n, k, epi, true, B.p_sx, sw, s)
-              : q35_gemm_launch(B.p_q8, w, out, Lt, n, k, epi, true, B.p_sx, sw, s);
+    return tc ? q35_gemm_tc_launch(B.p_q8, w, out, R, n, k, epi, true, B.p_sx, sw, s)
+              : q35_gemm_launch(B.p_q8, w, out, R, n, k, epi, true, B.p_sx, sw, s);
   };
 
   // fresh cache: zero the recurrent/conv states (the KV rows past `length` are never read)
   for (int i = 0; i < d.n_layers; ++i) {
     const q35_layer_desc& L = slot_layers[i];
     if (L.kind == 0) {
-      if (cudaMemsetAsync(L.rec_state, 0, (size_t)d.lin_heads * d.lin_dk * d.lin_dv * sizeof(float), s) !=
-              cudaSuccess ||
-          cudaMemsetAsync(L.conv_state, 0, (size_t)conv_dim * d.conv_kernel * sizeof(bf16), s) != cudaSuccess)
+      if (cudaMemsetAsync(L.rec_state, 0, (size_t)(nseq * rec_elems) * sizeof(float), s) != cudaSuccess ||
+          cudaMemsetAsync(L.conv_state, 0, (size_t)(nseq * conv_elems) * sizeof(bf16), s) != cudaSuccess)
         return q35_fail(Q35_ECUDA, "prefill: state reset failed");
     }
   }
   Q35_TRY(q35_set_counters_launch(d.cache_len, d.rope_pos, 0, s));
-  Q35_TRY(q35_embedding(ids, d.embed, B.p_resid, Lt, d.vocab, H, s));
+  Q35_TRY(q35_embedding(ids, d.embed, B.p_resid, R, d.vocab, H, s));
   if (mm.n_image > 0) {
     image_rows_kernel<<<(unsigned)mm.n_image, 128, 0, s>>>((const bf16*)mm.image_embeds, mm.image_rows, B.p_resid,
-                                                         Lt, H);
+                                                         R, H);
     Q35_TRY(q35_check_launch("prefill_mm image rows"));
   }
   for (int i = 0; i < d.n_layers; ++i) {
     const q35_layer_desc& L = slot_layers[i];
-    Q35_TRY(q35_rms_norm(B.p_resid, L.in_ln, B.p_norm, Lt, H, d.eps, s));
+    Q35_TRY(q35_rms_norm(B.p_resid, L.in_ln, B.p_norm, R, H, d.eps, s));
     if (L.kind == 0) {
       Q35_TRY(proj(B.p_norm, H, L.mix_in, L.mix_in_scale, B.p_packed, d.delta_rows, Q35_EPI_STORE));
       if (d.prefill_delta == 0 && d.conv_kernel == 4 && Lt >= 4) {
         // causal conv folded into the chunk prep (reads the raw [q k v] columns of the projection)
-        Q35_TRY(q35_delta_chunked_launch(nullptr, B.p_packed, L.a_log, L.dt_bias, L.rec_state, B.p_core, 1, Lt,
+        Q35_TRY(q35_delta_chunked_launch(nullptr, B.p_packed, L.a_log, L.dt_bias, L.rec_state, B.p_core, nseq, Lt,
                                          d.lin_heads, d.delta_rows, B.p_chunk, s, L.conv_w, L.conv_state));
       } else {
-        Q35_TRY(q35_causal_conv1d(B.p_packed, L.conv_w, L.conv_state, B.p_conv, 1, Lt, d.delta_rows, conv_dim,
+        Q35_TRY(q35_causal_conv1d(B.p_packed, L.conv_w, L.conv_state, B.p_conv, nseq, Lt, d.delta_rows, conv_dim,
                                   d.conv_kernel, s));
         if (d.prefill_delta == 0)
-          Q35_TRY(q35_delta_chunked_launch(B.p_conv, B.p_packed, L.a_log, L.dt_bias, L.rec_state, B.p_core, 1, Lt,
-                                           d.lin_heads, d.delta_rows, B.p_chunk, s, nullptr, nullptr));
+          Q35_TRY(q35_delta_chunked_launch(B.p_conv, B.p_packed, L.a_log, L.dt_bias, L.rec_state, B.p_core, nseq,
+                                           Lt, d.lin_heads, d.delta_rows, B.p_chunk, s, nullptr, nullptr));
         else
-          Q35_TRY(q35_delta_recurrent(B.p_conv, B.p_packed, L.a_log, L.dt_bias, L.rec_state, B.p_core, 1, Lt,
+          Q35_TRY(q35_delta_recurrent(B.p_conv, B.p_packed, L.a_log, L.dt_bias, L.rec_state, B.p_core, nseq, Lt,
                                       d.lin_heads, d.lin_dk, d.delta_rows, s));
       }
       Q35_TRY(q35_gated_rms_strided_launch(B.p_core, B.p_packed + conv_dim, d.lin_heads, d.delta_rows, L.gnorm,
-                                           B.p_mix, Lt * d.lin_heads, d.lin_dv, d.eps, s));
+                                           B.p_mix, R * d.lin_heads, d.lin_dv, d.eps, s));
       Q35_TRY(proj(B.p_mix, vdim, L.mix_out, L.mix_out_scale, B.p_resid, H, Q35_EPI_RESIDUAL));
     } else {
       Q35_TRY(proj(B.p_norm, H, L.mix_in, L.mix_in_scale, B.p_packed, qgkv_rows, Q35_EPI_STORE));
       Q35_TRY(q35_qgkv_rope_positions_launch(B.p_packed, L.q_norm, L.k_norm, d.inv_freq, B.p_core, L.k_cache,
-                                             L.v_cache, nullptr, 1, Lt, d.q_heads, d.kv_heads, d.rotary_dim,
+                                             L.v_cache, nullptr, nseq, Lt, d.q_heads, d.kv_heads, d.rotary_dim,
                                              d.max_len, d.eps, s, mm.pos3, d.mrope_section[1], d.mrope_section[2]));
-      Q35_TRY(q35_prefill_attention(B.p_core, L.k_cache, L.v_cache, B.p_attn, 1, d.q_heads, d.kv_heads, Lt,
+      Q35_TRY(q35_prefill_attention(B.p_core, L.k_cache, L.v_cache, B.p_attn, nseq, d.q_heads, d.kv_heads, Lt,
                                     d.max_len, 0, d.head_dim, 1.0f / sqrtf((float)d.head_dim), s));
-      Q35_TRY(q35_attention_gate_mul(B.p_attn, B.p_packed, B.p_mix, Lt, adim, qgkv_rows, d.head_dim, s));
+      Q35_TRY(q35_attention_gate_mul(B.p_attn, B.p_packed, B.p_mix, R, adim, qgkv_rows, d.head_dim, s));
       Q35_TRY(proj(B.p_mix, adim, L.mix_out, L.mix_out_scale, B.p_resid, H, Q35_EPI_RESIDUAL));
     }
-    Q35_TRY(q35_rms_norm(B.p_resid, L.post_ln, B.p_norm, Lt, H, d.eps, s));
+    Q35_TRY(q35_rms_norm(B.p_resid, L.post_ln, B.p_norm, R, H, d.eps, s));
     Q35_TRY(proj(B.p_norm, H, L.gate_up, L.gate_up_scale, B.p_act, I, Q35_EPI_SWIGLU));
     Q35_TRY(proj(B.p_act, I, L.down, L.down_scale, B.p_resid, H, Q35_EPI_RESIDUAL));
   }
-  Q35_TRY(q35_lm_head_launch(B.p_resid + (Lt - 1) * H, d.final_norm, d.embed, token_out, d.vocab, H, d.eps, B.lm_ws,
-                             s, false, nullptr));
+  if (nseq == 1) {
+    Q35_TRY(q35_lm_head_launch(B.p_resid + (Lt - 1) * H, d.final_norm, d.embed, token_out, d.vocab, H, d.eps,
+                               B.lm_ws, s, false, nullptr));
+  } else {  // each sequence's last row -> the decode rows, one pass over the tied table for all
+    if (cudaMemcpy2DAsync(B.resid, (size_t)H * sizeof(bf16), B.p_resid + (Lt - 1) * H, (size_t)(Lt * H) * sizeof(bf16),
+                          (size_t)H * sizeof(bf16), (size_t)nseq, cudaMemcpyDeviceToDevice, s) != cudaSuccess)
+      return q35_fail(Q35_ECUDA, "prefill: last-row gather failed");
+    Q35_TRY(q35_lm_head_batch_launch(B.resid, nseq, d.final_norm, d.embed, d.vocab, d.eps, B.lm_keys, B.lm_keys_ws,
+                                     s, false));
+    Q35_TRY(q35_lm_keys_finish_launch(B.lm_keys, nseq, token_out, s, false, nullptr));
+  }
   Q35_TRY(q35_set_counters_launch(d.cache_len, d.rope_pos, Lt, s));
   if (mm.rope_next >= 0) Q35_TRY(q35_set_counters_launch(d.rope_pos, d.rope_pos, mm.rope_next, s));
   return Q35_OK;

@@ -46,11 +46,12 @@ __global__ void __launch_bounds__(256) patchify_kernel(const float* __restrict__
   const int gw = W / P, bw_n = gw / M;
   const int mw = p % M, mh = (p / M) % M, bw = (p / (M * M)) % bw_n, bh = p / (M * M * bw_n);
   const int y = (bh * M + mh) * P + py, x = (bw * M + mw) * P + px0;
-  const float* src = px + ((int64_t)c * H + y) * W + x;
+  const int64_t img = blockIdx.y;  // images of a batch: [n, C, H, W] -> [n * patches, F]
+  const float* src = px + img * C * H * W + ((int64_t)c * H + y) * W + x;
   __align__(16) bf16 o[8];
 #pragma unroll
   for (int j = 0; j < 8; ++j) o[j] = f2bf((src[j] - mean) * inv_std);
-  *reinterpret_cast<uint4*>(out + flat) = *reinterpret_cast<const uint4*>(o);
+  *reinterpret_cast<uint4*>(out + img * n_patches * F + flat) = *reinterpret_cast<const uint4*>(o);
 }
 
 // Grid position of merge-ordered token p: row = bh * M + mh, column = bw * M + mw.
@@ -197,7 +198,7 @@ __global__ void __launch_bounds__(256) pos_embed_kernel(const bf16* __restrict__
   const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (row >= rows) return;
   int r, c;
-  token_rc(row, gw, M, r, c);
+  token_rc(row % (gh * gw), gw, M, r, c);  // rows of a batch of images: the token within its image
   const float hv = linspace_at(r, gh, side), wv = linspace_at(c, gw, side);
   const int hf = (int)hv, wf = (int)wv;
   const int hc = min(hf + 1, side - 1), wc = min(wf + 1, side - 1);
@@ -253,16 +254,17 @@ __global__ void __launch_bounds__(256) pos_embed_given_kernel(const bf16* __rest
 __global__ void __launch_bounds__(256) qkv_rope_kernel(const bf16* __restrict__ packed, const float* __restrict__ cos_t,
                                                        const float* __restrict__ sin_t, bf16* __restrict__ q_out,
                                                        bf16* __restrict__ k_out, bf16* __restrict__ v_out, int tokens,
-                                                       int heads) {
+                                                       int heads, int per_image) {
   const int gw = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (gw >= tokens * heads) return;
   const int t = gw / heads, h = gw - t * heads;
+  const int img = t / per_image, tt = t - img * per_image;  // tables are per image; q/k/v [n, heads, L, 64]
   const int64_t stride = 3 * (int64_t)heads * kVD;
   const bf16* row = packed + (int64_t)t * stride;
   const int d0 = lane, d1 = lane + 32;
-  const float c0 = cos_t[(int64_t)t * kVD + d0], c1 = cos_t[(int64_t)t * kVD + d1];
-  const float s0 = sin_t[(int64_t)t * kVD + d0], s1 = sin_t[(int64_t)t * kVD + d1];
-  const int64_t o = ((int64_t)h * tokens + t) * kVD;
+  const float c0 = cos_t[(int64_t)tt * kVD + d0], c1 = cos_t[(int64_t)tt * kVD + d1];
+  const float s0 = sin_t[(int64_t)tt * kVD + d0], s1 = sin_t[(int64_t)tt * kVD + d1];
+  const int64_t o = (((int64_t)img * heads + h) * per_image + tt) * kVD;
 #pragma unroll
   for (int which = 0; which < 2; ++which) {
     const bf16* src = row + (int64_t)which * heads * kVD + h * kVD;
@@ -305,12 +307,13 @@ __global__ void __launch_bounds__(kVaThreads) vision_attn_kernel(VisionAttnParam
   __shared__ __align__(16) bf16 vs[2][kVaKeys * kVaStride];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, tq = lane & 3;
-  const int h = blockIdx.y;
+  const int h = blockIdx.y, img = blockIdx.z;  // images of a batch attend within themselves
   const int L = p.L;
   const int r0 = blockIdx.x * kVaRows + warp * 16 + g, r1 = r0 + 8;
-  const bf16* qh = p.q + (int64_t)h * L * kVD;
-  const bf16* kh = p.k + (int64_t)h * L * kVD;
-  const bf16* vh = p.v + (int64_t)h * L * kVD;
+  const int64_t hoff = ((int64_t)img * p.heads + h) * L * kVD;
+  const bf16* qh = p.q + hoff;
+  const bf16* kh = p.k + hoff;
+  const bf16* vh = p.v + hoff;
 
   auto load_tile = [&](int tile, int buf) {
     for (int i = threadIdx.x; i < kVaKeys * 8; i += kVaThreads) {
@@ -437,8 +440,9 @@ __global__ void __launch_bounds__(kVaThreads) vision_attn_kernel(VisionAttnParam
 #pragma unroll
   for (int n = 0; n < 8; ++n) {
     const int c = h * kVD + 8 * n + 2 * tq;
-    if (r0 < L) *reinterpret_cast<uint32_t*>(p.out + (int64_t)r0 * ow + c) = pack_bf2(o[n][0] * i0, o[n][1] * i0);
-    if (r1 < L) *reinterpret_cast<uint32_t*>(p.out + (int64_t)r1 * ow + c) = pack_bf2(o[n][2] * i1, o[n][3] * i1);
+    const int64_t orow = (int64_t)img * L;
+    if (r0 < L) *reinterpret_cast<uint32_t*>(p.out + (orow + r0) * ow + c) = pack_bf2(o[n][0] * i0, o[n][1] * i0);
+    if (r1 < L) *reinterpret_cast<uint32_t*>(p.out + (orow + r1) * ow + c) = pack_bf2(o[n][2] * i1, o[n][3] * i1);
   }
 }
 
@@ -507,11 +511,12 @@ int pos_embed_norm_launch(const void* hidden, const void* table, const void* w, 
 }
 
 int attn_launch(const void* q, const void* k, const void* v, void* out, int64_t L, int64_t heads, float scale,
-                cudaStream_t s) {
-  if (L == 0) return Q35_OK;
+                cudaStream_t s, int64_t images = 1) {
+  if (L == 0 || images == 0) return Q35_OK;
   VisionAttnParams p{(const bf16*)q, (const bf16*)k, (const bf16*)v, (bf16*)out, (int)L, (int)heads,
                      scale * 1.4426950408889634f};
-  vision_attn_kernel<<<dim3((unsigned)((L + kVaRows - 1) / kVaRows), (unsigned)heads), kVaThreads, 0, s>>>(p);
+  vision_attn_kernel<<<dim3((unsigned)((L + kVaRows - 1) / kVaRows), (unsigned)heads, (unsigned)images), kVaThreads, 0,
+                       s>>>(p);
   return q35_check_launch("vision_attention");
 }
 
@@ -590,7 +595,7 @@ extern "C" int q35_vision_qkv_rope(const void* packed, const float* cos, const f
   Q35_REQUIRE(dim == kVD, "vision_qkv_rope: head dim %lld unsupported (64)", (long long)dim);
   if (tokens == 0) return Q35_OK;
   qkv_rope_kernel<<<(unsigned)((tokens * heads + 7) / 8), 256, 0, (cudaStream_t)stream>>>(
-      (const bf16*)packed, cos, sin, (bf16*)q_out, (bf16*)k_out, (bf16*)v_out, (int)tokens, (int)heads);
+      (const bf16*)packed, cos, sin, (bf16*)q_out, (bf16*)k_out, (bf16*)v_out, (int)tokens, (int)heads, (int)tokens);
   return q35_check_launch("vision_qkv_rope");
 }
 
@@ -694,7 +699,7 @@ __global__ void patch_cast_kernel(const float* __restrict__ in, bf16* __restrict
   reinterpret_cast<uint4*>(out)[i] = *reinterpret_cast<const uint4*>(o);
 }
 
-static int vit_blocks(q35_vit* vit, int64_t gh, int64_t gw, void* out, cudaStream_t s);
+static int vit_blocks(q35_vit* vit, int64_t gh, int64_t gw, int64_t images, void* out, cudaStream_t s);
 
 extern "C" int q35_vit_encode_patches(q35_vit* vit, const float* patches, int64_t grid_h, int64_t grid_w, void* out,
                                       void* stream) {
@@ -710,32 +715,40 @@ extern "C" int q35_vit_encode_patches(q35_vit* vit, const float* patches, int64_
   const int64_t n8 = grid_h * grid_w * F / 8;
   patch_cast_kernel<<<(unsigned)((n8 + 255) / 256), 256, 0, (cudaStream_t)stream>>>(patches, vit->buf.patches, n8);
   Q35_VTRY(q35_check_launch("vit patch cast"));
-  return vit_blocks(vit, grid_h, grid_w, out, (cudaStream_t)stream);
+  return vit_blocks(vit, grid_h, grid_w, 1, out, (cudaStream_t)stream);
 }
 
-extern "C" int q35_vit_encode(q35_vit* vit, const float* pixels, int64_t height, int64_t width, void* out,
-                              void* stream) {
-  Q35_REQUIRE(vit && pixels && out, "vit_encode: null argument");
+extern "C" int q35_vit_encode_batch(q35_vit* vit, const float* pixels, int64_t images, int64_t height, int64_t width,
+                                    void* out, void* stream) {
+  Q35_REQUIRE(vit && pixels && out && images >= 1, "vit_encode: null argument or no image");
   const q35_vit_desc& d = vit->d;
   const VitBuffers& B = vit->buf;
   const int64_t P = d.patch, M = d.merge;
   Q35_REQUIRE(height % (P * M) == 0 && width % (P * M) == 0, "vit_encode: image size must be a multiple of %lld",
               (long long)(P * M));
   const int64_t gh = height / P, gw = width / P;
-  Q35_REQUIRE(gh * gw <= d.max_patches, "vit_encode: %lld patches exceed max_patches %d", (long long)(gh * gw),
-              d.max_patches);
-  Q35_VTRY(q35_vision_patchify(pixels, B.patches, d.in_channels, height, width, P, d.temporal_patch, M,
-                               d.pixel_mean, d.pixel_std, stream));
-  return vit_blocks(vit, gh, gw, out, (cudaStream_t)stream);
+  Q35_REQUIRE(images * gh * gw <= d.max_patches, "vit_encode: %lld patches exceed max_patches %d",
+              (long long)(images * gh * gw), d.max_patches);
+  const int64_t groups = gh * gw * d.in_channels * d.temporal_patch * P * P / 8;
+  patchify_kernel<<<dim3((unsigned)((groups + 255) / 256), (unsigned)images), 256, 0, (cudaStream_t)stream>>>(
+      pixels, B.patches, d.in_channels, (int)height, (int)width, (int)P, d.temporal_patch, (int)M, (int)(gh * gw),
+      d.pixel_mean, 1.0f / d.pixel_std);
+  Q35_VTRY(q35_check_launch("vit patchify"));
+  return vit_blocks(vit, gh, gw, images, out, (cudaStream_t)stream);
+}
+
+extern "C" int q35_vit_encode(q35_vit* vit, const float* pixels, int64_t height, int64_t width, void* out,
+                              void* stream) {
+  return q35_vit_encode_batch(vit, pixels, 1, height, width, out, stream);
 }
 
 // Patch embedding (from vit->buf.patches), position embedding, the blocks and the merger.
-static int vit_blocks(q35_vit* vit, int64_t gh, int64_t gw, void* out, cudaStream_t s) {
+static int vit_blocks(q35_vit* vit, int64_t gh, int64_t gw, int64_t images, void* out, cudaStream_t s) {
   const q35_vit_desc& d = vit->d;
   const VitBuffers& B = vit->buf;
   void* stream = s;
   const int64_t P = d.patch, M = d.merge;
-  const int64_t N = gh * gw, W = d.width;
+  const int64_t NI = gh * gw, N = images * NI, W = d.width;  // patches per image, in the batch
   const int64_t F = (int64_t)d.in_channels * d.temporal_patch * P * P;
   Q35_VTRY(q35_gemm_tc_bias_launch(B.patches, d.patch_w, d.patch_b, B.upd, N, W, F, Q35_EPI_BIAS, s));
   Q35_VTRY(q35_vision_rope_table(d.rope_inv_freq, B.cos_t, B.sin_t, gh, gw, M, stream));
@@ -745,8 +758,10 @@ static int vit_blocks(q35_vit* vit, int64_t gh, int64_t gw, void* out, cudaStrea
   for (int i = 0; i < d.depth; ++i) {
     const q35_vit_block_desc& L = vit->blocks[i];
     Q35_VTRY(q35_gemm_tc_bias_launch(B.norm, L.qkv_w, L.qkv_b, B.packed, N, 3 * W, W, Q35_EPI_BIAS, s));
-    Q35_VTRY(q35_vision_qkv_rope(B.packed, B.cos_t, B.sin_t, B.q, B.k, B.v, N, d.heads, kVD, stream));
-    Q35_VTRY(attn_launch(B.q, B.k, B.v, B.attn, N, d.heads, scale, s));
+    qkv_rope_kernel<<<(unsigned)((N * d.heads + 7) / 8), 256, 0, s>>>(B.packed, B.cos_t, B.sin_t, B.q, B.k, B.v, (int)N,
+                                                                      d.heads, (int)NI);
+    Q35_VTRY(q35_check_launch("vit qkv rope"));
+    Q35_VTRY(attn_launch(B.q, B.k, B.v, B.attn, NI, d.heads, scale, s, images));
     Q35_VTRY(q35_gemm_tc_bias_launch(B.attn, L.proj_w, L.proj_b, B.upd, N, W, W, Q35_EPI_BIAS, s));
     Q35_VTRY(ln_launch(B.resid, B.upd, L.norm2_w, L.norm2_b, B.resid, B.norm, N, W, d.eps, s));
     Q35_VTRY(q35_gemm_tc_bias_launch(B.norm, L.fc1_w, L.fc1_b, B.mlp, N, d.intermediate, W,

@@ -55,7 +55,8 @@ class Qwen35Engine:
         self.a8w8 = a8w8
         self.batch = batch
         self.max_len = max_len
-        self.max_prefill = min(max_prefill, max_len - 1)
+        # prefill rows: one prompt shorter than the cache, or (batched) one per slot
+        self.max_prefill = min(max_prefill, (max_len - 1) * batch)
         self._keep: list[torch.Tensor] = []
 
         def w(name):
@@ -188,8 +189,8 @@ class Qwen35Engine:
         if ids.device != self.device:
             ids = ids.to(self.device)
         n = ids.numel()
-        if n > self.max_prefill:
-            raise ValueError(f"prompt of {n} tokens exceeds max_prefill={self.max_prefill}")
+        if n > min(self.max_prefill, self.max_len - 1):
+            raise ValueError(f"prompt of {n} tokens exceeds max_prefill={self.max_prefill} or the cache")
         L.check(L.load().q35_decoder_prefill_slot(self.handle, ids.data_ptr(), n, int(slot), L.stream_of(self.device)),
                 "q35_decoder_prefill_slot")
         return self.token
@@ -206,8 +207,8 @@ class Qwen35Engine:
         if not (ids.is_cuda and ids.dtype == torch.int64 and image_rows.dtype == torch.int64
                 and positions3.dtype == torch.int64):
             raise ValueError("prefill_multimodal expects int64 ids, image rows and positions on the GPU")
-        if n > self.max_prefill:
-            raise ValueError(f"prompt of {n} tokens exceeds max_prefill={self.max_prefill}")
+        if n > min(self.max_prefill, self.max_len - 1):
+            raise ValueError(f"prompt of {n} tokens exceeds max_prefill={self.max_prefill} or the cache")
         if positions3.shape != (3, n) or image_embeds.dim() != 2 or image_embeds.shape[1] != self.dims.hidden:
             raise ValueError("positions3 must be [3, L] and image_embeds [n, hidden]")
         if image_rows.numel() != image_embeds.shape[0] or image_embeds.dtype != BF16:
@@ -218,6 +219,38 @@ class Qwen35Engine:
         L.check(L.load().q35_decoder_prefill_mm(self.handle, ids.data_ptr(), n, image_embeds.data_ptr(),
                                                 image_rows.data_ptr(), image_rows.numel(), positions3.data_ptr(),
                                                 int(rope_next), int(slot), L.stream_of(dev)), "q35_decoder_prefill_mm")
+        return self.token
+
+    def prefill_batch(self, ids: torch.Tensor, *, image_embeds: torch.Tensor | None = None,
+                      image_rows: torch.Tensor | None = None, positions3: torch.Tensor | None = None,
+                      rope_next: int = -1, slot: int = 0) -> torch.Tensor:
+        """Batched engines: prefill ``n`` requests of one length in one pass, device ids
+        ``[n, L]`` into slots ``slot .. slot + n - 1`` (``n * L <= max_prefill``). Optional image
+        rows as in ``prefill_multimodal``, with ``image_rows`` indexing the ``n * L`` rows and
+        ``positions3`` int64 ``[3, n, L]``. The first tokens land in ``self.token[slot:slot + n]``."""
+        if ids.dim() != 2 or not ids.is_cuda or ids.dtype != torch.int64:
+            raise ValueError("prefill_batch expects int64 token ids [n, L] on a CUDA device")
+        nseq, n = ids.shape
+        if nseq * n > self.max_prefill:
+            raise ValueError(f"{nseq} x {n} prompt tokens exceed max_prefill={self.max_prefill}")
+        dev = self.device
+        ids = ids.to(dev).contiguous()
+        emb_p = rows_p = pos_p = None
+        n_img = 0
+        if image_embeds is not None:
+            if image_rows is None or image_rows.numel() != image_embeds.shape[0] or image_embeds.dtype != BF16 \
+                    or image_embeds.dim() != 2 or image_embeds.shape[1] != self.dims.hidden:
+                raise ValueError("one int64 image row per bf16 image embedding [n, hidden]")
+            image_embeds, image_rows = image_embeds.to(dev).contiguous(), image_rows.to(dev).contiguous()
+            emb_p, rows_p, n_img = image_embeds.data_ptr(), image_rows.data_ptr(), image_rows.numel()
+        if positions3 is not None:
+            if positions3.shape != (3, nseq, n) or positions3.dtype != torch.int64:
+                raise ValueError("positions3 must be int64 [3, n, L]")
+            positions3 = positions3.to(dev).contiguous()
+            pos_p = positions3.data_ptr()
+        L.check(L.load().q35_decoder_prefill_batch(self.handle, ids.data_ptr(), n, nseq, emb_p, rows_p, n_img, pos_p,
+                                                   int(rope_next), int(slot), L.stream_of(dev)),
+                "q35_decoder_prefill_batch")
         return self.token
 
     def decode_step(self) -> torch.Tensor:
@@ -367,17 +400,23 @@ class Qwen35Engine:
     # ------------------------------------------------------------------ generation
     def generate_batch(self, prompts, max_new_tokens: int):
         """Greedy generation of ``batch`` requests in lock step from host prompts of one length:
-        H2D copies, one prefill per slot, the first tokens read on the host (TTFT), then one
+        H2D copy, one batched prefill of all requests (one per slot when they exceed
+        ``max_prefill`` together), the first tokens read on the host (TTFT), then one
         graph-replayed batched step per token with a host read of the ``batch`` tokens. Returns
         ``(tokens per request, ttft_s, elapsed_s)``."""
         if len(prompts) != self.batch:
             raise ValueError(f"expected {self.batch} prompts")
-        hosts = [torch.as_tensor(p, dtype=torch.int64).reshape(-1).pin_memory() for p in prompts]
+        hosts = [torch.as_tensor(p, dtype=torch.int64).reshape(-1) for p in prompts]
         if len({h.numel() for h in hosts}) != 1:
             raise ValueError("the prompts of one batch share a length (one cache position for all)")
+        host = torch.stack(hosts).pin_memory()
         start = time.perf_counter()
-        for slot, h in enumerate(hosts):
-            self.prefill(h.to(self.device, non_blocking=True), slot)
+        ids = host.to(self.device, non_blocking=True)
+        if ids.numel() <= self.max_prefill:
+            self.prefill_batch(ids)
+        else:
+            for slot in range(self.batch):
+                self.prefill(ids[slot], slot)
         out = [[t] for t in self.token.tolist()]
         first_at = time.perf_counter()
         graph = self.capture(1) if max_new_tokens > 1 else None

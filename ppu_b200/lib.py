@@ -122,6 +122,7 @@ _SIGS = {
     "q35_decoder_prefill": (INT, [P, P, I64, P]),
     "q35_decoder_prefill_mm": (INT, [P, P, I64, P, P, I64, P, I64, I64, P]),
     "q35_decoder_prefill_slot": (INT, [P, P, I64, I64, P]),
+    "q35_decoder_prefill_batch": (INT, [P, P, I64, I64, P, P, I64, P, I64, I64, P]),
     "q35_gemv_batch": (INT, [C.POINTER(GemvDesc), I64, P]),
     "q35_decoder_decode_step": (INT, [P, P]),
     "q35_decoder_decode_layers": (INT, [P, P]),
@@ -146,6 +147,7 @@ _SIGS = {
     "q35_vit_create": (INT, [C.POINTER(VitDesc), C.POINTER(P)]),
     "q35_vit_destroy": (None, [P]),
     "q35_vit_encode": (INT, [P, P, I64, I64, P, P]),
+    "q35_vit_encode_batch": (INT, [P, P, I64, I64, I64, P, P]),
     "q35_vit_encode_patches": (INT, [P, P, I64, I64, P, P]),
     "q35_vit_hidden": (P, [P]),
     "q35_decoder_probe_bytes": (SZ, [P]),

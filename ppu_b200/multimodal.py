@@ -62,6 +62,13 @@ class MultimodalEngine:
         self._vgraph = self.vision.capture(*self.image_hw)
         self._dgraph = decode_graph if decode_graph is not None else self.text.capture(1)
         self._layouts: dict[int, tuple[torch.Tensor, torch.Tensor, int]] = {}
+        self._group_layouts: dict[tuple[int, int], tuple[torch.Tensor, torch.Tensor, torch.Tensor, int]] = {}
+        # a batched text engine takes a group of requests per prefill; the vision tower takes the
+        # group's images in one encode when its workspace holds them all
+        self.batch = getattr(self.text, "batch", 1)
+        n_patch = vd.merge * vd.merge * self.n_img
+        self.group_images = max(1, min(self.batch, self.vision.max_patches // n_patch))
+        self.group_prefill = self.batch > 1 and self.batch * max_prompt <= self.text.max_prefill
 
     def _layout(self, n_text: int):
         if n_text not in self._layouts:
@@ -90,6 +97,45 @@ class MultimodalEngine:
         ids = torch.cat((torch.full((self.n_img,), IMAGE_TOKEN_ID, device=self.device, dtype=torch.int64),
                          text_ids.reshape(-1)))
         return self.text.prefill_multimodal(ids, tokens, rows, pos, nxt, slot)
+
+    def encode_images(self, pixels: torch.Tensor) -> torch.Tensor:
+        """Device pixels fp32 ``[n, 3, H, W]`` -> merged tokens ``[n * n_image, out_width]`` (image
+        order): one vision-graph replay per ``group_images`` images."""
+        n = pixels.shape[0]
+        outs = []
+        for j in range(0, n, self.group_images):
+            k = min(self.group_images, n - j)
+            if k == 1:
+                outs.append(self.encode_image(pixels[j]).clone() if n > 1 else self.encode_image(pixels[j]))
+                continue
+            g, pix, tokens = self.vision.capture(*self.image_hw, images=k)
+            pix.copy_(pixels[j:j + k], non_blocking=True)
+            g.replay()
+            outs.append(tokens if n <= self.group_images else tokens.clone())
+        return outs[0] if len(outs) == 1 else torch.cat(outs)
+
+    def _group_layout(self, nseq: int, n_text: int):
+        key = (nseq, n_text)
+        if key not in self._group_layouts:
+            rows, pos, nxt = self._layout(n_text)
+            length = self.n_img + n_text
+            all_rows = (rows.view(1, -1) + length * torch.arange(nseq, device=self.device).view(-1, 1)).reshape(-1)
+            pos3 = pos.view(3, 1, length).expand(3, nseq, length).contiguous()
+            img_ids = torch.full((nseq, self.n_img), IMAGE_TOKEN_ID, device=self.device, dtype=torch.int64)
+            self._group_layouts[key] = (all_rows, pos3, img_ids, nxt)
+        return self._group_layouts[key]
+
+    def prefill_group(self, tokens: torch.Tensor, text_ids: torch.Tensor, slot: int = 0) -> torch.Tensor:
+        """Batched text engines: ``n`` requests at once, merged image tokens ``[n * n_image,
+        hidden]`` (``encode_images``) and text ids int64 ``[n, T]`` (one length), prefilled in one
+        pass into slots ``slot .. slot + n - 1``; the first tokens land in ``text.token``."""
+        nseq, n_text = text_ids.shape
+        if not self.group_prefill or slot + nseq > self.batch:
+            raise ValueError("group prefill needs a batched text engine whose max_prefill holds the group")
+        rows, pos3, img_ids, nxt = self._group_layout(nseq, n_text)
+        ids = torch.cat((img_ids, text_ids), 1)
+        return self.text.prefill_batch(ids, image_embeds=tokens, image_rows=rows, positions3=pos3, rope_next=nxt,
+                                       slot=slot)
 
     def decode_step(self) -> None:
         self._dgraph.replay()

@@ -95,7 +95,7 @@ class VisionEngine:
         handle = C.c_void_p()
         L.check(L.load().q35_vit_create(C.byref(d), C.byref(handle)), "q35_vit_create")
         self.handle = handle
-        self._graphs: dict[tuple[int, int], tuple[torch.cuda.CUDAGraph, torch.Tensor, torch.Tensor]] = {}
+        self._graphs: dict[tuple[int, int, int], tuple[torch.cuda.CUDAGraph, torch.Tensor, torch.Tensor]] = {}
 
     def __del__(self):
         h = getattr(self, "handle", None)
@@ -122,6 +122,20 @@ class VisionEngine:
                                         L.stream_of(self.device)), "q35_vit_encode")
         return out
 
+    def encode_batch(self, pixels: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        """Images of one size, fp32 ``[n, C, H, W]`` on this device -> merged tokens bf16
+        ``[n * tokens, out_width]`` (image order), one launch sequence for the whole batch."""
+        if pixels.dim() != 4 or pixels.dtype != torch.float32 or pixels.device != self.device:
+            raise ValueError("pixels must be an fp32 [n, C, H, W] tensor on the engine's device")
+        pixels = pixels.contiguous()
+        n_img, _, h, wd = pixels.shape
+        n = n_img * self.vd.merged_tokens(h, wd)
+        if out is None:
+            out = torch.empty((n, self.vd.out_width), device=self.device, dtype=BF16)
+        L.check(L.load().q35_vit_encode_batch(self.handle, pixels.data_ptr(), n_img, h, wd, out.data_ptr(),
+                                              L.stream_of(self.device)), "q35_vit_encode_batch")
+        return out
+
     def encode_patches(self, patches: torch.Tensor, grid_h: int, grid_w: int,
                        out: torch.Tensor | None = None) -> torch.Tensor:
         """One image from the processor's patches (fp32 ``[grid_h*grid_w, C*T*P*P]``, the
@@ -146,21 +160,25 @@ class VisionEngine:
         nbytes = 2 * n_patches * self.vd.width
         return self.workspace[off:off + nbytes].view(BF16).view(n_patches, self.vd.width)
 
-    def capture(self, height: int, width: int):
-        """CUDA graph of one encode at a fixed image size; returns ``(graph, pixels_in, tokens_out)``:
-        copy an image into ``pixels_in``, replay, read ``tokens_out``."""
-        key = (height, width)
+    def capture(self, height: int, width: int, images: int = 1):
+        """CUDA graph of one encode at a fixed image size (of ``images`` images at once); returns
+        ``(graph, pixels_in, tokens_out)``: copy the image(s) into ``pixels_in`` (``[C, H, W]``, or
+        ``[images, C, H, W]`` when ``images > 1``), replay, read ``tokens_out``."""
+        key = (height, width, images)
         if key in self._graphs:
             return self._graphs[key]
-        pix = torch.zeros((self.vd.in_channels, height, width), device=self.device, dtype=torch.float32)
-        out = torch.empty((self.vd.merged_tokens(height, width), self.vd.out_width), device=self.device, dtype=BF16)
-        self.encode(pix, out)  # warm-up: first-use kernel attributes are set outside the capture
+        shape = (self.vd.in_channels, height, width)
+        pix = torch.zeros(shape if images == 1 else (images, *shape), device=self.device, dtype=torch.float32)
+        out = torch.empty((images * self.vd.merged_tokens(height, width), self.vd.out_width), device=self.device,
+                          dtype=BF16)
+        run = self.encode if images == 1 else self.encode_batch
+        run(pix, out)  # warm-up: first-use kernel attributes are set outside the capture
         torch.cuda.synchronize(self.device)
         side = torch.cuda.Stream(self.device)
         side.wait_stream(torch.cuda.current_stream(self.device))
         g = torch.cuda.CUDAGraph()
         with torch.cuda.stream(side), torch.cuda.graph(g, stream=side):
-            self.encode(pix, out)
+            run(pix, out)
         torch.cuda.current_stream(self.device).wait_stream(side)
         self._graphs[key] = (g, pix, out)
         return self._graphs[key]

@@ -125,3 +125,43 @@ def test_batched_decoder_matches_oracle_per_request():
         alone, _, _ = single.generate(prompts[b], steps)
         agree = next((i for i, (x, y) in enumerate(zip(alone, tokens[b])) if x != y), steps)
         assert agree >= 1
+
+
+def test_batched_prefill_matches_per_slot_prefill():
+    """q35_decoder_prefill_batch (all requests' rows through one set of GEMMs, per-request scans,
+    attention and cache writes) against one prefill per slot: first tokens, DeltaNet states and
+    KV caches agree up to the GEMMs' row-tile summation order."""
+    B, n = 4, 40
+    w = make_weights(SMALL, seed=61)
+    prompts = torch.stack([make_prompt(SMALL, n, seed=70 + b)[0] for b in range(B)])
+    one = Qwen35Engine(w, SMALL, max_len=128, max_prefill=B * n, batch=B)
+    for b in range(B):
+        one.prefill(prompts[b].cuda(), b)
+    torch.cuda.synchronize()
+    ref = {"tok": one.token.clone(), "conv": [t.clone() for t in one.conv_states],
+           "rec": [t.clone() for t in one.rec_states], "k": [t[:, :, :n].clone() for t in one.k_caches]}
+    one.prefill_batch(prompts.cuda())
+    torch.cuda.synchronize()
+    assert int(one.cache_len) == n and int(one.rope_pos) == n
+    for a, b in zip(one.rec_states, ref["rec"]):
+        assert rel_err(a, b) < 1e-3
+    for a, b in zip(one.conv_states, ref["conv"]):
+        assert rel_err(a, b) < 1e-2
+    for a, b in zip(one.k_caches, ref["k"]):
+        assert rel_err(a[:, :, :n], b) < 1e-2
+    # first tokens: equal, or within the logit noise of the oracle's top-1 for that request
+    for b in range(B):
+        got, want = int(one.token[b]), int(ref["tok"][b])
+        if got != want:
+            (top, top_val, tok_val), = OracleDecoder(w, SMALL, max_cache_len=128).teacher_forced_top1(
+                prompts[b][None], [got])
+            assert tok_val >= top_val - LOGIT_NOISE, (b, got, want, top)
+
+
+def test_batched_prefill_rejects_too_many_rows():
+    w = make_weights(SMALL, seed=62)
+    eng = Qwen35Engine(w, SMALL, max_len=128, max_prefill=64, batch=4)
+    with pytest.raises(ValueError, match="max_prefill"):
+        eng.prefill_batch(torch.zeros(4, 20, dtype=torch.int64, device=DEV))
+    with pytest.raises(ValueError, match="slots"):
+        eng.prefill_batch(torch.zeros(2, 20, dtype=torch.int64, device=DEV), slot=3)

@@ -95,3 +95,37 @@ def test_multimodal_engine_generate_matches_oracle_teacher_forced():
         top = int(lg.argmax())
         assert tok == top or float(lg[tok]) >= float(lg[top]) - max(LOGIT_NOISE, bf16_ulp(float(lg[top]))), step
         h = oracle.forward(torch.tensor([[tok]]))[:, -1]
+
+
+def test_multimodal_group_prefill_matches_per_request_prefill():
+    """Config 5 with a batched text engine: the group's images through one ViT encode and its
+    prompts through one prefill (q35_decoder_prefill_batch with per-request image rows and M-RoPE
+    positions) against each request encoded and prefilled alone."""
+    B = 3
+    w = make_weights(SMALL, seed=81)
+    vw = make_vision_weights(TINY_VIT, seed=82)
+    imgs = torch.stack([make_image(224, 224, seed=83 + b) for b in range(B)]).cuda()
+    texts = torch.stack([make_prompt(SMALL, 40, seed=90 + b)[0] for b in range(B)]).cuda()
+    n_img = TINY_VIT.merged_tokens(224, 224)
+    vis = VisionEngine(vw, TINY_VIT, max_image=(224, 224), max_patches=B * 4 * n_img)
+    eng = Qwen35Engine(w, SMALL, max_len=256, max_prefill=B * (n_img + 40), batch=B)
+    mm = MultimodalEngine(None, None, SMALL, TINY_VIT, image_hw=(224, 224), max_text=40, max_new_tokens=4,
+                          text_engine=eng, vision_engine=vis)
+    assert mm.group_prefill and mm.group_images == B
+    tokens = mm.encode_images(imgs)
+    assert tokens.shape == (B * n_img, SMALL.hidden)
+    mm.prefill_group(tokens, texts)
+    torch.cuda.synchronize()
+    group = {"tok": eng.token.clone(), "rec": [t.clone() for t in eng.rec_states],
+             "k": [t[:, :, :n_img + 40].clone() for t in eng.k_caches]}
+    rope_group = int(eng.rope_pos)
+    for b in range(B):
+        mm.prefill(imgs[b], texts[b], b)
+    torch.cuda.synchronize()
+    assert int(eng.rope_pos) == rope_group == prompt_layout(TINY_VIT, (224, 224), 40)[2]
+    for a, b in zip(group["rec"], eng.rec_states):
+        assert rel_err(a, b) < 1e-3
+    for a, b in zip(group["k"], eng.k_caches):
+        assert rel_err(a, b[:, :, :n_img + 40]) < 1e-2
+    agree = sum(int(x) == int(y) for x, y in zip(group["tok"], eng.token))
+    assert agree >= B - 1

@@ -156,3 +156,29 @@ def test_vit_config5_shape_matches_oracle_and_graph_replay():
     graph.replay()
     torch.cuda.synchronize()
     assert torch.equal(out, merged)
+
+
+def test_vit_batch_of_images_matches_one_at_a_time():
+    """q35_vit_encode_batch: three images through one launch sequence (GEMMs over all patches,
+    position embedding / RoPE / attention per image) against three single encodes, and the
+    captured batch graph against the eager batch."""
+    c = G["vision_model"]
+    vd = VisionDims(**c["dims"])
+    w = make_vision_weights(vd, seed=c["seed"])
+    h, wd = c["height"], c["width"]
+    n_patch = vd.grid(h, wd)[0] * vd.grid(h, wd)[1]
+    eng = VisionEngine(w, vd, max_image=(h, wd), max_patches=3 * n_patch)
+    imgs = torch.stack([make_image(h, wd, seed=40 + i) for i in range(3)])
+    batch = eng.encode_batch(cu(imgs)).cpu()
+    m = vd.merged_tokens(h, wd)
+    assert batch.shape == (3 * m, vd.out_width)
+    for i in range(3):
+        alone = eng.encode(cu(imgs[i])).cpu()
+        assert_bf16_close(batch[i * m:(i + 1) * m], alone, max_ulp=2, max_frac=0.02)
+    graph, pix, out = eng.capture(h, wd, images=3)
+    pix.copy_(cu(imgs))
+    graph.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(out.cpu(), batch)
+    with pytest.raises(ValueError, match="max_patches"):
+        eng.encode_batch(cu(torch.stack([imgs[0]] * 4)))
