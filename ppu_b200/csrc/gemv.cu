@@ -160,6 +160,61 @@ Q35_DEV void build_input_q8(const GemvParams& p, int8_t* xq, float* sx_out, floa
   __syncthreads();
 }
 
+// Bf16 prologue at compile-time K: the norm weights arrive in registers, loaded before the PDL
+// wait (they are constants), so the only load after the wait is the input vector itself; each
+// thread keeps its chunks in registers between the sum of squares and the scaling. Values equal
+// build_input's: the same per-thread order of the sum, the same block_sum, the same expression.
+template <int PRO, int K>
+Q35_DEV void build_input_bf16(const GemvParams& p, bf16* xs, float* red, const uint4 (&nwr)[(K / 8 + kThreads - 1) / kThreads]) {
+  constexpr int NV = K / 8, CPT = (NV + kThreads - 1) / kThreads;
+  const bf16* src = p.input;
+  if (PRO == Q35_PRO_EMBED) {
+    int64_t t = *p.token;
+    t = t < 0 ? 0 : (t >= p.vocab ? p.vocab - 1 : t);
+    src = p.embed + t * (int64_t)K;
+  }
+  uint4 v[CPT];
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < CPT; ++j) {
+    const int i = threadIdx.x + j * kThreads;
+    if (i < NV) v[j] = reinterpret_cast<const uint4*>(src)[i];
+  }
+#pragma unroll
+  for (int j = 0; j < CPT; ++j) {
+    const int i = threadIdx.x + j * kThreads;
+    if (i < NV) {
+      if (PRO == Q35_PRO_EMBED && blockIdx.x == 0) reinterpret_cast<uint4*>(p.resid)[i] = v[j];
+      if (PRO == Q35_PRO_PLAIN) {
+        reinterpret_cast<uint4*>(xs)[i] = v[j];
+      } else {
+        float f[8];
+        unpack_bf16x8(v[j], f);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) ss += f[e] * f[e];
+      }
+    }
+  }
+  if (PRO != Q35_PRO_PLAIN) {
+    const float var = block_sum<kWarps>(ss, red) / (float)K;
+    const float r = rsqrt_ieee(var + p.eps);
+#pragma unroll
+    for (int j = 0; j < CPT; ++j) {
+      const int i = threadIdx.x + j * kThreads;
+      if (i < NV) {
+        float f[8], w[8];
+        unpack_bf16x8(v[j], f);
+        unpack_bf16x8(nwr[j], w);
+        __align__(16) bf16 o[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) o[e] = f2bf(f[e] * r * (1.0f + w[e]));
+        reinterpret_cast<uint4*>(xs)[i] = *reinterpret_cast<const uint4*>(o);
+      }
+    }
+  }
+  __syncthreads();
+}
+
 Q35_DEV int warp_sum_i(int v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -283,15 +338,36 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_fast_kernel(GemvParams p) {
   for (int q = 0; q < PRE; ++q)
     if (2 + q < n_iter) stage(2 + q, q);
   asm volatile("cp.async.commit_group;" ::: "memory");
-  if (PRO != Q35_PRO_PLAIN)  // norm weights are constants: warm L2 while the producer drains
-    for (int i = threadIdx.x; i < K / 64; i += kThreads)
-      asm volatile("prefetch.global.L2 [%0];" ::"l"(p.norm_w + 64 * i));
+  constexpr int NCPT = (K / 8 + kThreads - 1) / kThreads;
+  uint4 nwr[NCPT];  // bf16 norm weights: constants, in registers before the wait
+  if (PRO != Q35_PRO_PLAIN) {
+    if (INT8) {  // warm L2 while the producer drains
+      for (int i = threadIdx.x; i < K / 64; i += kThreads)
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(p.norm_w + 64 * i));
+    } else {
+#pragma unroll
+      for (int j = 0; j < NCPT; ++j) {
+        const int i = threadIdx.x + j * kThreads;
+        nwr[j] = i < K / 8 ? reinterpret_cast<const uint4*>(p.norm_w)[i] : make_uint4(0, 0, 0, 0);
+      }
+    }
+  }
   pdl_wait();
   pdl_launch_dependents();
-  if (INT8)
+  // residual epilogue: this warp's first-round residual values, read now (the producers are
+  // done) so that the epilogue's read-modify-write does not wait on L2 at the kernel's tail
+  float rpre[U];
+  if (EPI == Q35_EPI_RESIDUAL && lane == 0) {
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int unit = g0 * U + u;
+      rpre[u] = (g0 < ngroups && unit < n_out) ? bf2f(p.resid[unit]) : 0.f;
+    }
+  }
+  if constexpr (INT8)
     build_input_q8<PRO, K>(p, xq, &sx_s, red);
   else
-    build_input<PRO, false>(p, K, xs, xq, &sx_s, red);
+    build_input_bf16<PRO, K>(p, xs, red, nwr);
   const float sx = INT8 ? sx_s : 1.0f;
 
   float accf[U][RPU];
@@ -344,7 +420,12 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_fast_kernel(GemvParams p) {
           y[r] = warp_sum(accf[u][r]);
         }
       }
-      if (lane == 0 && unit < n_out) epilogue<EPI, INT8>(p, unit, y[0], RPU > 1 ? y[RPU - 1] : 0.f);
+      if (lane == 0 && unit < n_out) {
+        if (EPI == Q35_EPI_RESIDUAL && it < SEG)  // first round: the residual read before the prologue
+          p.resid[unit] = f2bf(rpre[u] + rbf(y[0]));
+        else
+          epilogue<EPI, INT8>(p, unit, y[0], RPU > 1 ? y[RPU - 1] : 0.f);
+      }
     }
   };
   for (int it = 0; it < n_iter; it += 2) {
