@@ -235,8 +235,9 @@ int q35_gqa_decode_attention(const void* q, const void* cache_k, const void* cac
  * cannot allocate device memory when they call in (a locked or pool-only allocator, a thread that
  * must not touch the CUDA allocator, a runtime that passes only inputs and outputs): the scratch
  * lives in a static device array of q35_gqa_decode_noalloc_max_bytes() bytes (2 MiB) that every
- * GPU loading this library keeps until exit. Shapes whose scratch exceeds it, or with more than
- * 64 (batch x kv_heads) split tickets, are rejected with Q35_EINVAL before anything is queued on
+ * GPU loading this library keeps until exit. Shapes whose scratch exceeds it, or that need more
+ * than 256 split-ticket words (batch x kv_heads, plus one per group of 16 splits when a (batch,
+ * KV head) has more than 16), are rejected with Q35_EINVAL before anything is queued on
  * the stream. The first call on a device looks up the array's device address (make it before any
  * stream capture); every call clears the ticket words and shares the array, so calls that overlap
  * on the GPU (other streams, other threads) race with each other. Calls no allocator. */

@@ -24,8 +24,10 @@ namespace {
 constexpr int kD = 256;
 constexpr int kThreads = 256;
 constexpr int kWarps = 8;
-constexpr int kMaxSplits = 64;
+constexpr int kMaxSplits = 148;  // splits per (batch, KV head): two CTAs per SM at batch 1 with two KV heads
 constexpr int kRowsPerSplit = 32;
+constexpr int kGroup = 16;       // splits merged per first-level combine when S > kGroup
+constexpr size_t kTicketBytes = 1024;  // B*Hkv final + B*Hkv*NG group tickets (<= 256 words)
 
 struct DecodeParams {
   const bf16* packed;    // fused: [B, stride] projection output
@@ -40,7 +42,10 @@ struct DecodeParams {
   bf16* out;             // [B, Hq*D]
   float* part;           // [B*Hkv*S*G][D]
   float* part_ml;        // [B*Hkv*S*G][2]
-  unsigned* tickets;     // [B*Hkv]
+  float* group_part;     // [B*Hkv*NG*G][D]: partials of groups of kGroup splits (S > kGroup)
+  float* group_ml;       // [B*Hkv*NG*G][2]
+  unsigned* tickets;     // [B*Hkv] final, then [B*Hkv*NG] per group
+  int n_bg;              // B*Hkv
   int Hq, Hkv, max_len, S, rot;
   float scale, eps;
 };
@@ -51,24 +56,157 @@ Q35_DEV void cp_async16(void* dst, const void* src) {
                : "memory");
 }
 
-constexpr int kBlk = 32;     // cache rows per staged block (one per lane in the block softmax)
-constexpr int kStages = 3;   // cp.async ring depth
-constexpr size_t kAttnDynSmem = 2ull * kStages * kBlk * kD * sizeof(bf16);  // K + V stages (96 KB)
-static_assert(kWarps * 4 * kD * sizeof(float) <= kAttnDynSmem, "the combine buffer fits in the stages");
+// Paired FP32 arithmetic (sm_100 f32x2): two lanes of a 64-bit register per instruction.
+Q35_DEV uint64_t pk2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+Q35_DEV void upk2(uint64_t v, float& lo, float& hi) { asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v)); }
+Q35_DEV uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+Q35_DEV uint64_t mul2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+// 8 bf16 (dims 8 lane .. + 7) as 4 FP32 pairs: a bf16 is the high half of its FP32 pattern
+Q35_DEV void bf16x8_pairs(uint4 u, uint64_t (&p)[4]) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) p[i] = pk2(__uint_as_float(w[i] << 16), __uint_as_float(w[i] & 0xffff0000u));
+}
+Q35_DEV float ex2_approx(float x) {
+  float r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+
+constexpr int kR = 4;    // cache rows per group (one online-softmax rescale per group)
+constexpr int kNS = 3;   // ring stages per warp: 2 groups = 8 KB in flight per warp
+constexpr size_t kAttnDynSmem = (size_t)kWarps * kNS * kR * 2 * kD * sizeof(bf16);  // 96 KB: two CTAs per SM
+static_assert(kWarps * 4 * kD * sizeof(float) + 2 * kMaxSplits * 4 * sizeof(float) <= kAttnDynSmem,
+              "the merge / combine buffers fit in the ring");
+
+// After this CTA's results are written: count it in at `ticket`; true for the last of `n`
+// arrivals (whose later reads then see every earlier CTA's writes).
+template <int G>
+Q35_DEV bool last_arrival(unsigned* ticket, int n) {
+  __shared__ unsigned ticket_s;
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) ticket_s = atomicAdd(ticket, 1u);
+  __syncthreads();
+  if (ticket_s != (unsigned)(n - 1)) return false;
+  __threadfence();
+  return true;
+}
+
+// Merges n partials per head (ml_in [n][G][2], part_in [n][G][kD]; un-normalised outputs with
+// their running max and sum) with all warps. final: normalise, round to BF16 and (fused) apply
+// the sigmoid gate into p.out; else write one partial of the same form to ml_out / part_out.
+// `scratch` (shared memory, >= kWarps * G * kD floats + 2 * kMaxSplits * G floats) is free.
+template <int G, bool FUSED>
+Q35_DEV void merge_partials(const DecodeParams& p, const float* ml_in, const float* part_in, int n, bool final, int b,
+                            int g, float* ml_out, float* part_out, unsigned char* scratch) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, d = threadIdx.x;
+  float (*wacc)[G][kD] = reinterpret_cast<float (*)[G][kD]>(scratch);
+  float (*cm)[G] = reinterpret_cast<float (*)[G]>(scratch + (size_t)kWarps * G * kD * sizeof(float));
+  float (*cl)[G] = cm + kMaxSplits;
+  __shared__ float cls[G], cms[G];
+  for (int i = threadIdx.x; i < n * G; i += kThreads) {
+    const float mi = __ldcg(ml_in + 2 * i);
+    const float li = __ldcg(ml_in + 2 * i + 1);
+    cm[i / G][i % G] = li > 0.f ? mi : -INFINITY;  // empty split: zero weight
+    cl[i / G][i % G] = li;
+  }
+  __syncthreads();
+  if (warp < G) {  // one warp per head: max, weights and normaliser over the n partials
+    const int hh = warp;
+    float M = -FLT_MAX;
+    for (int j = lane; j < n; j += 32) M = fmaxf(M, cm[j][hh]);
+    M = warp_max(M);
+    float Ls = 0.f;
+    for (int j = lane; j < n; j += 32) {
+      const float e = (cm[j][hh] == -INFINITY) ? 0.f : exp2f(cm[j][hh] - M);  // log2-unit maxima
+      cm[j][hh] = e;
+      Ls += cl[j][hh] * e;
+    }
+    Ls = warp_sum(Ls);
+    if (lane == 0) {
+      cls[hh] = Ls;
+      cms[hh] = M;
+    }
+  }
+  __syncthreads();
+  float a8[G][8];
+#pragma unroll
+  for (int hh = 0; hh < G; ++hh)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) a8[hh][j] = 0.f;
+#pragma unroll 2
+  for (int j = warp; j < n; j += kWarps) {
+#pragma unroll
+    for (int hh = 0; hh < G; ++hh) {
+      const float wgt = cm[j][hh];
+      const float4* src = reinterpret_cast<const float4*>(part_in + (int64_t)(j * G + hh) * kD + lane * 8);
+      const float4 u0 = __ldcg(src), u1 = __ldcg(src + 1);
+      a8[hh][0] += wgt * u0.x;
+      a8[hh][1] += wgt * u0.y;
+      a8[hh][2] += wgt * u0.z;
+      a8[hh][3] += wgt * u0.w;
+      a8[hh][4] += wgt * u1.x;
+      a8[hh][5] += wgt * u1.y;
+      a8[hh][6] += wgt * u1.z;
+      a8[hh][7] += wgt * u1.w;
+    }
+  }
+#pragma unroll
+  for (int hh = 0; hh < G; ++hh) {
+    float4* dst = reinterpret_cast<float4*>(&wacc[warp][hh][lane * 8]);
+    dst[0] = make_float4(a8[hh][0], a8[hh][1], a8[hh][2], a8[hh][3]);
+    dst[1] = make_float4(a8[hh][4], a8[hh][5], a8[hh][6], a8[hh][7]);
+  }
+  __syncthreads();
+  const int Hq = p.Hq, Hkv = p.Hkv;
+#pragma unroll
+  for (int hh = 0; hh < G; ++hh) {
+    float A = 0.f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) A += wacc[w][hh][d];
+    if (!final) {
+      part_out[(int64_t)hh * kD + d] = A;
+      if (d == 0) {
+        ml_out[2 * hh] = cls[hh] > 0.f ? cms[hh] : -FLT_MAX;
+        ml_out[2 * hh + 1] = cls[hh];
+      }
+      continue;
+    }
+    const float o = cls[hh] > 0.f ? rbf(A / cls[hh]) : 0.f;
+    const int h = g * G + hh;
+    if (FUSED) {
+      const int stride = 2 * Hq * kD + 2 * Hkv * kD;
+      const float gate = bf2f(p.packed[(int64_t)b * stride + h * 2 * kD + kD + d]);
+      p.out[((int64_t)b * Hq + h) * kD + d] = f2bf(o * rbf(sigmoid_f(gate)));
+    } else {
+      p.out[((int64_t)b * Hq + h) * kD + d] = f2bf(o);
+    }
+  }
+}
 
 template <int G, bool FUSED>
-__global__ void __launch_bounds__(kThreads) attn_decode_kernel(DecodeParams p) {
+__global__ void __launch_bounds__(kThreads, 2) attn_decode_kernel(DecodeParams p) {
   extern __shared__ __align__(16) unsigned char attn_dsmem[];
   __shared__ __align__(16) float qf[G][kD];
   __shared__ __align__(16) float nrm[FUSED ? G + 1 : 1][kD];
   __shared__ __align__(16) float kn[kD];
   __shared__ __align__(16) float vn[kD];
-  __shared__ __align__(16) float bsc[kBlk][G];
-  __shared__ float balpha[G];
+  __shared__ __align__(16) float wsc[kWarps][kR * G < 4 ? 4 : kR * G];  // a warp's group scores
+  __shared__ float wmax[kWarps][G], wsum[kWarps][G];
   __shared__ float red[kWarps][G + 1];
-  __shared__ float cm[kMaxSplits][G], cl[kMaxSplits][G];
-  __shared__ float cls[G];
-  __shared__ unsigned ticket_s;
 
   const int s = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
   const int S = p.S, Hkv = p.Hkv, Hq = p.Hq;
@@ -121,201 +259,216 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(DecodeParams p) {
   int n_rows = (int)(len < 0 ? 0 : (len > p.max_len ? p.max_len : len));
   __syncthreads();
 
-  // ---- this CTA's rows of the cache, in blocks of kBlk rows staged through a kStages cp.async
-  // ring; per block: scores (warp per 4 rows, lanes over dims, one butterfly for all 16 dot
-  // products), one online-softmax rescale per head, then P.V with thread = dim for every head
+  // ---- this CTA's rows of the cache. Every warp streams its own groups of kR rows (group i of
+  // the split goes to warp i mod 8) through a private kNS-stage cp.async ring; each lane copies,
+  // and later reads back, only its own 16-byte chunk (dims 8 lane .. 8 lane + 7) of every K and V
+  // row, so the stream needs no block barrier: cp.async.wait_group orders a lane's own copies.
+  // Per group: the kR x G dot products reduced in one butterfly, one online-softmax rescale per
+  // head, P.V on the lane's 8 dims. The warps' partials merge once at the end.
   const int chunk = (n_rows + S - 1) / S;
   const int r0 = s * chunk;
   const int r1 = min(r0 + chunk, n_rows);
   const int nr = r1 > r0 ? r1 - r0 : 0;
-  const int nblk = (nr + kBlk - 1) / kBlk;
-  bf16* stage_k = reinterpret_cast<bf16*>(attn_dsmem);                 // [kStages][kBlk][kD]
-  bf16* stage_v = stage_k + kStages * kBlk * kD;                        // [kStages][kBlk][kD]
-  const bf16* Kb = p.cache_k + kv_base;
-  const bf16* Vb = p.cache_v + kv_base;
-  auto issue_block = [&](int bi) {
-    if (bi < nblk) {
-      const int rb0 = r0 + bi * kBlk, rows_b = min(kBlk, r1 - rb0);
-      bf16* kd = stage_k + (bi % kStages) * kBlk * kD;
-      bf16* vd = stage_v + (bi % kStages) * kBlk * kD;
-      for (int i = threadIdx.x; i < rows_b * (kD / 8); i += kThreads) {
-        const int r = i / (kD / 8), c8 = (i % (kD / 8)) * 8;
-        cp_async16(kd + r * kD + c8, Kb + (int64_t)(rb0 + r) * kD + c8);
-        cp_async16(vd + r * kD + c8, Vb + (int64_t)(rb0 + r) * kD + c8);
-      }
+  const int ngrp = (nr + kR - 1) / kR;
+  const int nit = warp < ngrp ? (ngrp - 1 - warp) / kWarps + 1 : 0;
+  constexpr int kSlot = kR * 2 * 32;  // uint4 slots of one stage of one warp: [row][K | V][lane]
+  uint4* ring = reinterpret_cast<uint4*>(attn_dsmem) + warp * (kNS * kSlot) + lane;
+  const bf16* Kb = p.cache_k + kv_base + lane * 8;
+  const bf16* Vb = p.cache_v + kv_base + lane * 8;
+  auto issue = [&](int it) {
+    if (it < nit) {
+      const int rg = r0 + (warp + it * kWarps) * kR;
+      uint4* st = ring + (it % kNS) * kSlot;
+#pragma unroll
+      for (int j = 0; j < kR; ++j)
+        if (rg + j < r1) {
+          cp_async16(st + (2 * j) * 32, Kb + (int64_t)(rg + j) * kD);
+          cp_async16(st + (2 * j + 1) * 32, Vb + (int64_t)(rg + j) * kD);
+        }
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
   };
-  float q8[G][8];
+  // scores in log2 units (q scaled by log2 e): the softmax then runs on exp2, one MUFU op each;
+  // the partials' maxima are in the same units (merge_partials uses exp2 as well). The dot
+  // products and P.V run on FP32 pairs (fma.rn.f32x2), half the instructions of scalar FMAs.
+  uint64_t q2[G][4];
 #pragma unroll
   for (int hh = 0; hh < G; ++hh)
 #pragma unroll
-    for (int j = 0; j < 8; ++j) q8[hh][j] = qf[hh][lane * 8 + j];
-  float m_run = -FLT_MAX, l_run = 0.f;  // warp hh < G: head hh's running max / sum (all lanes)
-  float acc[G];                          // thread d: un-normalised output of every head at dim d
+    for (int e = 0; e < 4; ++e)
+      q2[hh][e] = pk2(qf[hh][lane * 8 + 2 * e] * 1.4426950408889634f, qf[hh][lane * 8 + 2 * e + 1] * 1.4426950408889634f);
+  float mw[G], lw[G];  // this warp's running max / sum per head
+  uint64_t aw[G][4];   // and its output at the lane's 8 dims, as pairs
 #pragma unroll
-  for (int hh = 0; hh < G; ++hh) acc[hh] = 0.f;
-  // one block of rows_b rows: K / V from a stage (bf16) or, for the current token, kn / vn (fp32)
-  auto run_block = [&](const bf16* kst, const bf16* vst, int rows_b, bool current) {
-    {  // scores: warp w takes rows w, w + 8, w + 16, w + 24
-      float v[4 * G];
+  for (int hh = 0; hh < G; ++hh) {
+    mw[hh] = -FLT_MAX;
+    lw[hh] = 0.f;
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int r = warp + i * kWarps;
-        float kf[8];
-        if (current) {
+    for (int e = 0; e < 4; ++e) aw[hh][e] = 0ull;
+  }
+  // one group of `nv` rows: from the ring stage `st`, or (current) the new token's kn / vn
+  auto absorb = [&](const uint4* st, int nv, bool current) {
+    float v[kR * G];
 #pragma unroll
-          for (int e = 0; e < 8; ++e) kf[e] = (r == 0) ? kn[lane * 8 + e] : 0.f;
-        } else if (r < rows_b) {
-          unpack_bf16x8(*reinterpret_cast<const uint4*>(kst + r * kD + lane * 8), kf);
-        } else {
+    for (int j = 0; j < kR; ++j) {
+      uint64_t k2[4];
+      if (current) {
 #pragma unroll
-          for (int e = 0; e < 8; ++e) kf[e] = 0.f;
-        }
-#pragma unroll
-        for (int hh = 0; hh < G; ++hh) {
-          float a = 0.f;
-#pragma unroll
-          for (int e = 0; e < 8; ++e) a = fmaf(q8[hh][e], kf[e], a);
-          v[i * G + hh] = a;
-        }
-      }
-      butterfly_sum<4 * G>(v, lane);
-      const int idx = butterfly_index<4 * G>(lane);
-      const bool writer = butterfly_writer<4 * G>(lane);
-      if (writer) {
-        const int i = idx / G, hh = idx % G;
-        const int r = warp + i * kWarps;
-        if (r < kBlk) bsc[r][hh] = (r < rows_b) ? v[0] : -FLT_MAX;
-      }
-    }
-    __syncthreads();
-    if (warp < G) {  // online softmax for head `warp` over the block's rows (lane = row)
-      const float sv = (lane < rows_b) ? bsc[lane][warp] : -FLT_MAX;
-      const float bm = warp_max(sv);
-      const float mn = fmaxf(m_run, bm);
-      const float alpha = (m_run == -FLT_MAX) ? 0.f : expf(m_run - mn);
-      const float pr = (lane < rows_b) ? expf(sv - mn) : 0.f;
-      l_run = l_run * alpha + warp_sum(pr);
-      m_run = mn;
-      bsc[lane][warp] = pr;
-      if (lane == 0) balpha[warp] = alpha;
-    }
-    __syncthreads();
-#pragma unroll
-    for (int hh = 0; hh < G; ++hh) acc[hh] *= balpha[hh];
-    for (int j = 0; j < rows_b; ++j) {
-      const float vv = current ? vn[d] : bf2f(vst[j * kD + d]);
-      if (G == 4) {  // the row's four weights in one 16-byte shared load
-        const float4 w4 = *reinterpret_cast<const float4*>(&bsc[j][0]);
-        acc[0] = fmaf(w4.x, vv, acc[0]);
-        acc[1 % G] = fmaf(w4.y, vv, acc[1 % G]);
-        acc[2 % G] = fmaf(w4.z, vv, acc[2 % G]);
-        acc[3 % G] = fmaf(w4.w, vv, acc[3 % G]);
+        for (int e = 0; e < 4; ++e) k2[e] = (j == 0) ? pk2(kn[lane * 8 + 2 * e], kn[lane * 8 + 2 * e + 1]) : 0ull;
+      } else if (j < nv) {
+        bf16x8_pairs(st[(2 * j) * 32], k2);
       } else {
 #pragma unroll
-        for (int hh = 0; hh < G; ++hh) acc[hh] = fmaf(bsc[j][hh], vv, acc[hh]);
+        for (int e = 0; e < 4; ++e) k2[e] = 0ull;
+      }
+#pragma unroll
+      for (int hh = 0; hh < G; ++hh) {
+        uint64_t a2 = mul2(q2[hh][0], k2[0]);
+#pragma unroll
+        for (int e = 1; e < 4; ++e) a2 = fma2(q2[hh][e], k2[e], a2);
+        float lo, hi;
+        upk2(a2, lo, hi);
+        v[j * G + hh] = lo + hi;
       }
     }
-    __syncthreads();  // bsc and this stage are free
-  };
-  for (int i = 0; i < kStages - 1; ++i) issue_block(i);
-  for (int bi = 0; bi < nblk; ++bi) {
-    issue_block(bi + kStages - 1);
-    asm volatile("cp.async.wait_group %0;" ::"n"(kStages - 1) : "memory");
-    __syncthreads();
-    const int st = bi % kStages;
-    run_block(stage_k + st * kBlk * kD, stage_v + st * kBlk * kD, min(kBlk, nr - bi * kBlk), false);
-  }
-  asm volatile("cp.async.wait_group 0;" ::: "memory");
-  if (FUSED && s == S - 1) run_block(nullptr, nullptr, 1, true);  // the current token
-
-  // ---- this CTA's partial per head: (max, sum) from the softmax warps, the output from every dim
-  const int base = ((b * Hkv + g) * S) * G;
-  if (warp < G && lane == 0) {
-    const int slot = base + s * G + warp;
-    p.part_ml[2 * slot] = m_run;
-    p.part_ml[2 * slot + 1] = l_run;
-  }
+    butterfly_sum<kR * G>(v, lane);
+    if (butterfly_writer<kR * G>(lane)) wsc[warp][butterfly_index<kR * G>(lane)] = v[0];
+    __syncwarp();
+    float sc[kR * G];
 #pragma unroll
-  for (int hh = 0; hh < G; ++hh) p.part[(int64_t)(base + s * G + hh) * kD + d] = acc[hh];
-  __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) ticket_s = atomicAdd(&p.tickets[b * Hkv + g], 1u);
-  __syncthreads();
-  if (ticket_s != (unsigned)(S - 1)) return;
-  __threadfence();
-
-  // ---- last CTA: combine the S partials of each head with all warps (per-warp sums in the
-  // stage memory, free now)
-  float (*wacc)[G][kD] = reinterpret_cast<float (*)[G][kD]>(attn_dsmem);
-  for (int i = threadIdx.x; i < S * G; i += kThreads) {
-    const float mi = __ldcg(p.part_ml + 2 * (base + i));
-    const float li = __ldcg(p.part_ml + 2 * (base + i) + 1);
-    cm[i / G][i % G] = li > 0.f ? mi : -INFINITY;  // empty split: zero weight
-    cl[i / G][i % G] = li;
-  }
-  __syncthreads();
-  if (warp < G) {  // one warp per head: max, weights and normaliser over the S splits
-    const int hh = warp;
-    float M = -FLT_MAX;
-    for (int j = lane; j < S; j += 32) M = fmaxf(M, cm[j][hh]);
-    M = warp_max(M);
-    float Ls = 0.f;
-    for (int j = lane; j < S; j += 32) {
-      const float e = (cm[j][hh] == -INFINITY) ? 0.f : expf(cm[j][hh] - M);
-      cm[j][hh] = e;
-      Ls += cl[j][hh] * e;
+    for (int i = 0; i < kR * G; i += 4) {
+      const float4 t = *reinterpret_cast<const float4*>(&wsc[warp][i]);
+      sc[i] = t.x;
+      sc[i + 1] = t.y;
+      sc[i + 2] = t.z;
+      sc[i + 3] = t.w;
     }
-    Ls = warp_sum(Ls);
-    if (lane == 0) cls[hh] = Ls;
-  }
-  __syncthreads();
-  float a8[G][8];
-#pragma unroll
-  for (int hh = 0; hh < G; ++hh)
-#pragma unroll
-    for (int j = 0; j < 8; ++j) a8[hh][j] = 0.f;
-#pragma unroll 2
-  for (int j = warp; j < S; j += kWarps) {
+    __syncwarp();  // every lane has read the scores before the next group rewrites them
 #pragma unroll
     for (int hh = 0; hh < G; ++hh) {
-      const float wgt = cm[j][hh];
-      const float4* src = reinterpret_cast<const float4*>(p.part + (int64_t)(base + j * G + hh) * kD + lane * 8);
-      const float4 u0 = __ldcg(src), u1 = __ldcg(src + 1);
-      a8[hh][0] += wgt * u0.x;
-      a8[hh][1] += wgt * u0.y;
-      a8[hh][2] += wgt * u0.z;
-      a8[hh][3] += wgt * u0.w;
-      a8[hh][4] += wgt * u1.x;
-      a8[hh][5] += wgt * u1.y;
-      a8[hh][6] += wgt * u1.z;
-      a8[hh][7] += wgt * u1.w;
+      float bm = -FLT_MAX;
+#pragma unroll
+      for (int j = 0; j < kR; ++j)
+        if (j < nv) bm = fmaxf(bm, sc[j * G + hh]);
+      const float mn = fmaxf(mw[hh], bm);
+      if (mn != mw[hh]) {  // a new maximum (uniform across the warp): rescale the running terms
+        const float alpha = (mw[hh] == -FLT_MAX) ? 0.f : ex2_approx(mw[hh] - mn);
+        lw[hh] *= alpha;
+        const uint64_t a2 = pk2(alpha, alpha);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) aw[hh][e] = mul2(aw[hh][e], a2);
+        mw[hh] = mn;
+      }
+#pragma unroll
+      for (int j = 0; j < kR; ++j) {
+        const float pj = (j < nv) ? ex2_approx(sc[j * G + hh] - mn) : 0.f;
+        sc[j * G + hh] = pj;
+        lw[hh] += pj;
+      }
     }
+#pragma unroll
+    for (int j = 0; j < kR; ++j) {
+      if (j >= nv) break;
+      uint64_t v2[4];
+      if (current) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) v2[e] = pk2(vn[lane * 8 + 2 * e], vn[lane * 8 + 2 * e + 1]);
+      } else {
+        bf16x8_pairs(st[(2 * j + 1) * 32], v2);
+      }
+#pragma unroll
+      for (int hh = 0; hh < G; ++hh) {
+        const uint64_t p2 = pk2(sc[j * G + hh], sc[j * G + hh]);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) aw[hh][e] = fma2(v2[e], p2, aw[hh][e]);
+      }
+    }
+  };
+#pragma unroll
+  for (int i = 0; i < kNS - 1; ++i) issue(i);
+  for (int it = 0; it < nit; ++it) {
+    issue(it + kNS - 1);
+    asm volatile("cp.async.wait_group %0;" ::"n"(kNS - 1) : "memory");
+    const int rg = r0 + (warp + it * kWarps) * kR;
+    absorb(ring + (it % kNS) * kSlot, min(kR, r1 - rg), false);
   }
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+  if (FUSED && s == S - 1 && warp == 0) absorb(nullptr, 1, true);  // the current token
+
+  // ---- merge the warps (the ring memory is free once every warp is past its stream)
+  __syncthreads();
+  float* mrg = reinterpret_cast<float*>(attn_dsmem);  // [kWarps][G][kD]
 #pragma unroll
   for (int hh = 0; hh < G; ++hh) {
-    float4* dst = reinterpret_cast<float4*>(&wacc[warp][hh][lane * 8]);
-    dst[0] = make_float4(a8[hh][0], a8[hh][1], a8[hh][2], a8[hh][3]);
-    dst[1] = make_float4(a8[hh][4], a8[hh][5], a8[hh][6], a8[hh][7]);
+    float o[8];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) upk2(aw[hh][e], o[2 * e], o[2 * e + 1]);
+    float4* dst = reinterpret_cast<float4*>(mrg + (warp * G + hh) * kD + lane * 8);
+    dst[0] = make_float4(o[0], o[1], o[2], o[3]);
+    dst[1] = make_float4(o[4], o[5], o[6], o[7]);
+  }
+  if (lane == 0) {
+#pragma unroll
+    for (int hh = 0; hh < G; ++hh) {
+      wmax[warp][hh] = mw[hh];
+      wsum[warp][hh] = lw[hh];
+    }
   }
   __syncthreads();
+  float m_run = -FLT_MAX, l_run = 0.f;  // warp hh < G: head hh's max / sum over the CTA's rows
+  float acc[G];                          // thread d: un-normalised output of every head at dim d
 #pragma unroll
   for (int hh = 0; hh < G; ++hh) {
-    float A = 0.f;
+    float M = -FLT_MAX;
 #pragma unroll
-    for (int w = 0; w < kWarps; ++w) A += wacc[w][hh][d];
-    const float o = cls[hh] > 0.f ? rbf(A / cls[hh]) : 0.f;
-    const int h = g * G + hh;
-    if (FUSED) {
-      const int stride = 2 * Hq * kD + 2 * Hkv * kD;
-      const float gate = bf2f(p.packed[(int64_t)b * stride + h * 2 * kD + kD + d]);
-      p.out[((int64_t)b * Hq + h) * kD + d] = f2bf(o * rbf(sigmoid_f(gate)));
-    } else {
-      p.out[((int64_t)b * Hq + h) * kD + d] = f2bf(o);
+    for (int w = 0; w < kWarps; ++w) M = fmaxf(M, wmax[w][hh]);
+    float A = 0.f, Ls = 0.f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) {
+      const float e = (wmax[w][hh] == -FLT_MAX) ? 0.f : exp2f(wmax[w][hh] - M);
+      A = fmaf(e, mrg[(w * G + hh) * kD + d], A);
+      Ls = fmaf(e, wsum[w][hh], Ls);
+    }
+    acc[hh] = A;
+    if (warp == hh) {
+      m_run = M;
+      l_run = Ls;
     }
   }
-  if (threadIdx.x == 0) atomicExch(&p.tickets[b * Hkv + g], 0u);
+  __syncthreads();  // the merge buffer is read before the last CTA's combine reuses the memory
+
+  // ---- this CTA's partial per head: (max, sum) from the softmax warps, the output from every dim
+  const int bg = b * Hkv + g;
+  const int slot0 = (bg * S + s) * G;
+  if (warp < G && lane == 0) {
+    p.part_ml[2 * (slot0 + warp)] = m_run;
+    p.part_ml[2 * (slot0 + warp) + 1] = l_run;
+  }
+#pragma unroll
+  for (int hh = 0; hh < G; ++hh) p.part[(int64_t)(slot0 + hh) * kD + d] = acc[hh];
+  // ---- combine. S <= kGroup: the last CTA of (batch, KV head), elected by an atomic ticket,
+  // merges the S partials into the output. Otherwise two levels: the last CTA of each group of
+  // kGroup splits merges the group into a group partial, and the last group merger merges the
+  // NG group partials (a single merger over up to 148 partials serialised their reads).
+  const int NG = (S + kGroup - 1) / kGroup;
+  unsigned* tk_final = p.tickets + bg;
+  if (NG > 1) {
+    const int grp = s / kGroup, gsz = min(kGroup, S - grp * kGroup);
+    unsigned* tk = p.tickets + p.n_bg + bg * NG + grp;
+    if (!last_arrival<G>(tk, gsz)) return;
+    merge_partials<G, FUSED>(p, p.part_ml + 2 * (bg * S + grp * kGroup) * G, p.part + (int64_t)(bg * S + grp * kGroup) * G * kD,
+                             gsz, false, b, g, p.group_ml + 2 * (bg * NG + grp) * G,
+                             p.group_part + (int64_t)(bg * NG + grp) * G * kD, attn_dsmem);
+    if (threadIdx.x == 0) atomicExch(tk, 0u);
+    if (!last_arrival<G>(tk_final, NG)) return;
+    merge_partials<G, FUSED>(p, p.group_ml + 2 * bg * NG * G, p.group_part + (int64_t)bg * NG * G * kD, NG, true, b, g,
+                             nullptr, nullptr, attn_dsmem);
+  } else {
+    if (!last_arrival<G>(tk_final, S)) return;
+    merge_partials<G, FUSED>(p, p.part_ml + 2 * bg * S * G, p.part + (int64_t)bg * S * G * kD, S, true, b, g, nullptr,
+                             nullptr, attn_dsmem);
+  }
+  if (threadIdx.x == 0) atomicExch(tk_final, 0u);
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -529,9 +682,8 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_cluster_kernel(Decode
 }
 
 int choose_splits(int64_t batch, int64_t kv_heads, int64_t cache_len) {
-  int64_t s = (cache_len + kRowsPerSplit - 1) / kRowsPerSplit;  // >= one 32-row block per CTA
-  // one wave of two CTAs per SM: rounding up here left a few CTAs for a second wave (1.03 waves
-  // at 8 x 2 KV heads), doubling the kernel time
+  int64_t s = (cache_len + kRowsPerSplit - 1) / kRowsPerSplit;  // >= 32 rows (a group per warp) per CTA
+  // one wave of two CTAs per SM: rounding up would leave a few CTAs for a second wave
   const int64_t fill = (2 * kNumSMs) / (batch * kv_heads);
   if (s > fill) s = fill;
   if (s > kMaxSplits) s = kMaxSplits;
@@ -539,17 +691,24 @@ int choose_splits(int64_t batch, int64_t kv_heads, int64_t cache_len) {
 }
 
 struct WsLayout {
-  size_t tickets, ml, part, total;
+  size_t tickets, ml, part, gml, gpart, total;
+  size_t n_tickets;  // ticket words in use
 };
 
 WsLayout ws_layout(int64_t batch, int64_t heads, int64_t kv_heads, int64_t cache_len) {
   const int S = choose_splits(batch, kv_heads, cache_len);
+  const int NG = (S + kGroup - 1) / kGroup;
   const size_t slots = (size_t)batch * heads * S;
+  const size_t gslots = NG > 1 ? (size_t)batch * heads * NG : 0;
+  auto up = [](size_t x) { return (x + 255) & ~(size_t)255; };
   WsLayout w;
   w.tickets = 0;
-  w.ml = 256;
-  w.part = w.ml + ((slots * 2 * sizeof(float) + 255) & ~(size_t)255);
-  w.total = w.part + slots * kD * sizeof(float);
+  w.n_tickets = (size_t)batch * kv_heads * (NG > 1 ? 1 + NG : 1);
+  w.ml = kTicketBytes;
+  w.part = w.ml + up(slots * 2 * sizeof(float));
+  w.gml = w.part + slots * kD * sizeof(float);
+  w.gpart = w.gml + up(gslots * 2 * sizeof(float));
+  w.total = w.gpart + gslots * kD * sizeof(float);
   return w;
 }
 
@@ -612,11 +771,15 @@ int launch_decode(DecodeParams p, int64_t batch, int G, void* ws, cudaStream_t s
   if (FUSED && G == 4 && p.max_len <= kClMaxRows)
     return cluster16_ok() ? launch_cluster<4, 16>(p, batch, st, pdl) : launch_cluster<4, 8>(p, batch, st, pdl);
   const WsLayout w = ws_layout(batch, p.Hq, p.Hkv, p.max_len);
-  if ((size_t)batch * p.Hkv * sizeof(unsigned) > w.ml) return q35_fail(Q35_ENOTSUP, "decode attention: batch too large");
+  if (w.n_tickets * sizeof(unsigned) > kTicketBytes)
+    return q35_fail(Q35_ENOTSUP, "decode attention: batch x KV heads too large");
   char* base = static_cast<char*>(ws);
   p.tickets = reinterpret_cast<unsigned*>(base + w.tickets);
   p.part_ml = reinterpret_cast<float*>(base + w.ml);
   p.part = reinterpret_cast<float*>(base + w.part);
+  p.group_ml = reinterpret_cast<float*>(base + w.gml);
+  p.group_part = reinterpret_cast<float*>(base + w.gpart);
+  p.n_bg = (int)(batch * p.Hkv);
   dim3 grid(p.S, p.Hkv, (unsigned)batch);
   static Q35PerDevice<bool> attr;
   attr.get([] {  // two CTAs per SM: the full shared-memory carve-out
@@ -758,9 +921,10 @@ extern "C" int q35_gqa_decode_attention_noalloc(const void* q, const void* cache
               "gqa_decode_attention_noalloc: this shape needs %zu bytes of scratch, more than the %zu-byte "
               "static maximum (use q35_gqa_decode_attention with a workspace)",
               w.total, kQ35NoAllocScratchBytes);
-  Q35_REQUIRE((size_t)batch * kv_heads * sizeof(unsigned) <= w.ml,
-              "gqa_decode_attention_noalloc: batch x kv_heads = %lld exceeds the %zu ticket words of the scratch",
-              (long long)(batch * kv_heads), w.ml / sizeof(unsigned));
+  Q35_REQUIRE(w.n_tickets * sizeof(unsigned) <= kTicketBytes,
+              "gqa_decode_attention_noalloc: batch x kv_heads = %lld needs %zu ticket words, more than the %zu of "
+              "the scratch",
+              (long long)(batch * kv_heads), w.n_tickets, kTicketBytes / sizeof(unsigned));
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
     return q35_fail(Q35_ECUDA, "gqa_decode_attention_noalloc: no current device");

@@ -307,7 +307,7 @@ def gqa_decode_attention(q, cache_keys, cache_values, valid_length, scale: float
     n_valid = valid_length.reshape(-1)[:1].to(torch.int64)
     size = L.load().q35_gqa_decode_workspace_size(batch, heads, kv_heads, head_dim, cache_len)
     ws = torch.empty(size, device=q.device, dtype=torch.uint8)
-    ws[:256].zero_()
+    ws[:1024].zero_()  # the split tickets
     out = torch.empty((batch, 1, heads * head_dim), device=q.device, dtype=q.dtype)
     L.call("q35_gqa_decode_attention", L.ptr(q), L.ptr(cache_keys), L.ptr(cache_values), L.ptr(n_valid), scale,
            L.ptr(out), batch, heads, kv_heads, head_dim, cache_len, L.ptr(ws), size, _s(q))
@@ -324,7 +324,7 @@ def attn_decode(packed, q_weight, k_weight, inv_freq, cache_key, cache_value, ca
     max_len = cache_key.shape[2]
     size = L.load().q35_attn_decode_workspace_size(batch, q_heads, kv_heads, dim, max_len)
     ws = torch.empty(size, device=packed.device, dtype=torch.uint8)
-    ws[:256].zero_()
+    ws[:1024].zero_()  # the split tickets
     out = torch.empty((batch, q_heads * dim), device=packed.device, dtype=BF16)
     L.call("q35_attn_decode", L.ptr(packed), L.ptr(q_weight), L.ptr(k_weight), L.ptr(inv_freq), L.ptr(cache_key),
            L.ptr(cache_value), L.ptr(cache_len), L.ptr(rope_pos), L.ptr(out), batch, q_heads, kv_heads, dim,

@@ -195,22 +195,26 @@ def run(kernels: list[str], reps: int, layers: int = 24, a8w8: bool = False):
             report("attn_decode_rope_pos0", _time(lambda i: attn(i, pos0), reps * 6), nbytes=2 * 2 * 2 * n * 256)
             t = _time(attn, reps * 6)
             report(name, t, nbytes=2 * 2 * 2 * n * 256)
-        elif name == "attn_config2":
+        elif name.startswith("attn_config2"):
             # gqa_decode_attention (8 Q / 2 KV heads, D 256) over a full static
-            # cache, K/V ~ N(0,1); enough cache copies rotated that every launch streams from HBM
-            for bsz in (1, 8):
-                for n in (1024, 4096, 16384):
-                    nbytes = 2 * 2 * n * 256 * 2 * bsz  # = 2048 * B * L
-                    copies = max(1, min(64, -(-300_000_000 // nbytes)))
-                    kc = [torch.randn(bsz, 2, n, 256, device=dev, generator=g).to(torch.bfloat16) for _ in range(copies)]
-                    vc = [torch.randn(bsz, 2, n, 256, device=dev, generator=g).to(torch.bfloat16) for _ in range(copies)]
-                    q = torch.randn(bsz, 8, 1, 256, device=dev, generator=g).to(torch.bfloat16)
-                    valid = torch.tensor([n], device=dev, dtype=torch.int64)
-                    t = _time(lambda i: K.gqa_decode_attention(q, kc[i % copies], vc[i % copies], valid, 0.0625),
-                              max(reps, 1) * copies)
-                    report(f"attn_config2_b{bsz}_l{n}", t, nbytes=nbytes)
-                    del kc, vc
-                    torch.cuda.empty_cache()
+            # cache, K/V ~ N(0,1); enough cache copies rotated that every launch streams from HBM.
+            # "attn_config2:B:L" runs one shape (for a profiler capture)
+            shapes = [(b_, n_) for b_ in (1, 8) for n_ in (1024, 4096, 16384)]
+            if ":" in name:
+                _, b_, n_ = name.split(":")
+                shapes = [(int(b_), int(n_))]
+            for bsz, n in shapes:
+                nbytes = 2 * 2 * n * 256 * 2 * bsz  # = 2048 * B * L
+                copies = max(1, min(64, -(-300_000_000 // nbytes)))
+                kc = [torch.randn(bsz, 2, n, 256, device=dev, generator=g).to(torch.bfloat16) for _ in range(copies)]
+                vc = [torch.randn(bsz, 2, n, 256, device=dev, generator=g).to(torch.bfloat16) for _ in range(copies)]
+                q = torch.randn(bsz, 8, 1, 256, device=dev, generator=g).to(torch.bfloat16)
+                valid = torch.tensor([n], device=dev, dtype=torch.int64)
+                t = _time(lambda i: K.gqa_decode_attention(q, kc[i % copies], vc[i % copies], valid, 0.0625),
+                          max(reps, 1) * copies)
+                report(f"attn_config2_b{bsz}_l{n}", t, nbytes=nbytes)
+                del kc, vc
+                torch.cuda.empty_cache()
         elif name == "delta_decode":
             packed = torch.randn(1, 8224, device=dev, generator=g).to(torch.bfloat16)
             cw = (torch.randn(6144, 4, device=dev, generator=g) * 0.5).to(torch.bfloat16)

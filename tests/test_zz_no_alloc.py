@@ -70,7 +70,7 @@ def test_noalloc_rejects_shapes_beyond_its_static_scratch():
 
 def test_noalloc_rejects_more_split_tickets_than_its_scratch_holds():
     lib = L.load()
-    b, h, kvh, n = 33, 2, 2, 64  # 66 (batch x kv_heads) tickets, 64 fit; the scratch itself is small
+    b, h, kvh, n = 64, 5, 5, 64  # 320 (batch x kv_heads) tickets, 256 fit; the scratch itself is small
     assert lib.q35_gqa_decode_workspace_size(b, h, kvh, 256, n) <= lib.q35_gqa_decode_noalloc_max_bytes()
     q = torch.zeros(b, h, 1, 256, device="cuda", dtype=torch.bfloat16)
     kv = torch.zeros(b, kvh, n, 256, device="cuda", dtype=torch.bfloat16)
