@@ -214,9 +214,44 @@ __global__ void __launch_bounds__(kThreads, 2) attn_decode_kernel(DecodeParams p
   const int d = threadIdx.x;  // kThreads == kD
   const int64_t kv_base = ((int64_t)b * Hkv + g) * p.max_len * kD;
 
+  // The cached rows and their count were written by earlier decode steps (the kernel just before
+  // this one only projects the new token), so this CTA's first groups of rows are requested
+  // before the programmatic-dependent-launch wait.
+  const int64_t len = *p.len;
+  const int n_rows = (int)(len < 0 ? 0 : (len > p.max_len ? p.max_len : len));
+  // ---- this CTA's rows of the cache. Every warp streams its own groups of kR rows (group i of
+  // the split goes to warp i mod 8) through a private kNS-stage cp.async ring; each lane copies,
+  // and later reads back, only its own 16-byte chunk (dims 8 lane .. 8 lane + 7) of every K and V
+  // row, so the stream needs no block barrier: cp.async.wait_group orders a lane's own copies.
+  // Per group: the kR x G dot products reduced in one butterfly, one online-softmax rescale per
+  // head, P.V on the lane's 8 dims. The warps' partials merge once at the end.
+  const int chunk = (n_rows + S - 1) / S;
+  const int r0 = s * chunk;
+  const int r1 = min(r0 + chunk, n_rows);
+  const int nr = r1 > r0 ? r1 - r0 : 0;
+  const int ngrp = (nr + kR - 1) / kR;
+  const int nit = warp < ngrp ? (ngrp - 1 - warp) / kWarps + 1 : 0;
+  constexpr int kSlot = kR * 2 * 32;  // uint4 slots of one stage of one warp: [row][K | V][lane]
+  uint4* ring = reinterpret_cast<uint4*>(attn_dsmem) + warp * (kNS * kSlot) + lane;
+  const bf16* Kb = p.cache_k + kv_base + lane * 8;
+  const bf16* Vb = p.cache_v + kv_base + lane * 8;
+  auto issue = [&](int it) {
+    if (it < nit) {
+      const int rg = r0 + (warp + it * kWarps) * kR;
+      uint4* st = ring + (it % kNS) * kSlot;
+#pragma unroll
+      for (int j = 0; j < kR; ++j)
+        if (rg + j < r1) {
+          cp_async16(st + (2 * j) * 32, Kb + (int64_t)(rg + j) * kD);
+          cp_async16(st + (2 * j + 1) * 32, Vb + (int64_t)(rg + j) * kD);
+        }
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+#pragma unroll
+  for (int i = 0; i < kNS - 1; ++i) issue(i);
   pdl_wait();
   pdl_launch_dependents();
-  const int64_t len = *p.len;
   if (FUSED) {
     const int stride = 2 * Hq * kD + 2 * Hkv * kD;
     const bf16* row = p.packed + (int64_t)b * stride;
@@ -256,38 +291,8 @@ __global__ void __launch_bounds__(kThreads, 2) attn_decode_kernel(DecodeParams p
 #pragma unroll
     for (int hh = 0; hh < G; ++hh) qf[hh][d] = bf2f(p.q_in[((int64_t)b * Hq + g * G + hh) * kD + d]) * p.scale;
   }
-  int n_rows = (int)(len < 0 ? 0 : (len > p.max_len ? p.max_len : len));
   __syncthreads();
 
-  // ---- this CTA's rows of the cache. Every warp streams its own groups of kR rows (group i of
-  // the split goes to warp i mod 8) through a private kNS-stage cp.async ring; each lane copies,
-  // and later reads back, only its own 16-byte chunk (dims 8 lane .. 8 lane + 7) of every K and V
-  // row, so the stream needs no block barrier: cp.async.wait_group orders a lane's own copies.
-  // Per group: the kR x G dot products reduced in one butterfly, one online-softmax rescale per
-  // head, P.V on the lane's 8 dims. The warps' partials merge once at the end.
-  const int chunk = (n_rows + S - 1) / S;
-  const int r0 = s * chunk;
-  const int r1 = min(r0 + chunk, n_rows);
-  const int nr = r1 > r0 ? r1 - r0 : 0;
-  const int ngrp = (nr + kR - 1) / kR;
-  const int nit = warp < ngrp ? (ngrp - 1 - warp) / kWarps + 1 : 0;
-  constexpr int kSlot = kR * 2 * 32;  // uint4 slots of one stage of one warp: [row][K | V][lane]
-  uint4* ring = reinterpret_cast<uint4*>(attn_dsmem) + warp * (kNS * kSlot) + lane;
-  const bf16* Kb = p.cache_k + kv_base + lane * 8;
-  const bf16* Vb = p.cache_v + kv_base + lane * 8;
-  auto issue = [&](int it) {
-    if (it < nit) {
-      const int rg = r0 + (warp + it * kWarps) * kR;
-      uint4* st = ring + (it % kNS) * kSlot;
-#pragma unroll
-      for (int j = 0; j < kR; ++j)
-        if (rg + j < r1) {
-          cp_async16(st + (2 * j) * 32, Kb + (int64_t)(rg + j) * kD);
-          cp_async16(st + (2 * j + 1) * 32, Vb + (int64_t)(rg + j) * kD);
-        }
-    }
-    asm volatile("cp.async.commit_group;" ::: "memory");
-  };
   // scores in log2 units (q scaled by log2 e): the softmax then runs on exp2, one MUFU op each;
   // the partials' maxima are in the same units (merge_partials uses exp2 as well). The dot
   // products and P.V run on FP32 pairs (fma.rn.f32x2), half the instructions of scalar FMAs.
@@ -384,8 +389,6 @@ __global__ void __launch_bounds__(kThreads, 2) attn_decode_kernel(DecodeParams p
       }
     }
   };
-#pragma unroll
-  for (int i = 0; i < kNS - 1; ++i) issue(i);
   for (int it = 0; it < nit; ++it) {
     issue(it + kNS - 1);
     asm volatile("cp.async.wait_group %0;" ::"n"(kNS - 1) : "memory");
