@@ -210,6 +210,13 @@ int q35_tc_error(void);
 /* Process-wide: 1 (default) runs the tensor-core projections on CTA pairs (thread-block clusters
  * of 2, tcgen05 cta_group::2, 256-row tiles), 0 on single CTAs (128-row tiles). */
 int q35_set_gemm_tc_pairs(int on);
+/* Process-wide switch (default 0): narrow outputs (N <= 2048, e.g. the out / down projections:
+ * 32 tiles of 256 x 256 for 74 SM pairs at M = 1024) split each tile's K range over two pairs;
+ * the last part to finish sums the parts' raw accumulators in part order (exact for int8) and
+ * runs the epilogue. The split depends on N and K only, so a row's result does not depend on M.
+ * Split launches share one scratch buffer per device: run them on one stream at a time.
+ * 0: never split. */
+int q35_set_gemm_tc_split(int on);
 
 /* ---------------------------------------------------------------- attention */
 
@@ -284,10 +291,14 @@ int q35_delta_recurrent(const void* qkv, const void* packed, const void* a_log,
 
 /* The same recurrence in chunked (WY / UT-transform) form, chunk 64, FP32 throughout — the
  * algorithm of HF torch_chunk_gated_delta_rule — used for prefill: chunk-local factors for all
- * chunks in parallel, then one pass over the chunks per (head, 16 value columns). Same inputs,
+ * chunks in parallel, one pass over the chunks per (head, 16 value columns) for the state, then
+ * the outputs of all chunks in parallel on tcgen05 (3xTF32, TMEM accumulator). Same inputs,
  * outputs and in-place state update as q35_delta_recurrent; workspace from
  * q35_delta_chunked_workspace_size. */
 size_t q35_delta_chunked_workspace_size(int64_t batch, int64_t heads, int64_t seq_len);
+/* Error word of the chunked DeltaNet output kernel (0 = its bounded TMEM wait completed; read and
+ * cleared). */
+int q35_delta_chunk_error(void);
 int q35_delta_chunked(const void* qkv, const void* packed, const void* a_log, const void* dt_bias,
                       float* state, void* out, int64_t batch, int64_t seq_len, int64_t heads,
                       int64_t dim, int64_t packed_stride, void* workspace, size_t workspace_bytes,

@@ -9,12 +9,18 @@
 //   A_ij = -beta_i (k_i . k_j) exp(c_i - c_j) (i > j); T = (I - A)^-1 by blocked substitution;
 //   U = T diag(beta) V;  W = T diag(beta exp(c)) K;  P_ij = (q_i . k_j) exp(c_i - c_j) (i >= j);
 //   Qe = q_hat exp(c);   Kd = k_hat exp(c_last - c);  gl = exp(c_last).
-// Phase B (one CTA per (batch, head, 16 value columns), chunks in order, products on the tensor
-// cores in 3xTF32):  Vn = U - W S;  O = Qe S + P Vn;  S <- gl S + Kd^T Vn;  out = bf16(O).
+// Phase B, the recurrence (one CTA per (batch, head, 16 value columns), chunks in order, products
+// on mma.sync in 3xTF32): keep S_c (the state entering chunk c);  Vn = U - W S;
+// S <- gl S + Kd^T Vn.
+// Phase C, the output (one CTA per (batch, head, chunk, 64 value columns), all chunks at once, on
+// tcgen05 with a TMEM accumulator, 3xTF32): out = bf16(Qe S_c + P Vn).
 // Padded tokens (beyond L) have beta = 0 and g = 0, as the reference's zero padding.
 #include "common.cuh"
+#include "tcgen05.cuh"
 
 using namespace q35;
+
+__device__ int q35_delta_chunk_error_word = 0;
 
 namespace {
 
@@ -25,9 +31,12 @@ constexpr int kThreads = 256;
 constexpr int kPW = 132;    // padded row stride of phase-B W / Qe tiles (16-byte aligned rows)
 
 struct ChunkWs {  // per (b, h, chunk) record in the workspace, FP32
+  // prep: W, U, Qe, Kd [64][128], P [64][64], gl; recurrence: ST = S_c^T [128 value][128 key]
+  // (the state entering the chunk, transposed) and VT = Vn^T [128 value][64 token]
   static constexpr size_t W = 0, U = W + kC * kD, Qe = U + kC * kD, Kd = Qe + kC * kD, P = Kd + kC * kD,
-                          GL = P + kC * kC, SIZE = GL + 4;
+                          GL = P + kC * kC, ST = GL + 4, VT = ST + kD * kD, SIZE = VT + kD * kC;
 };
+static_assert(ChunkWs::ST % 4 == 0 && ChunkWs::VT % 4 == 0 && ChunkWs::SIZE % 4 == 0, "16-byte aligned fields");
 
 struct PrepParams {
   const bf16* qkv;       // [B, L, 3*H*D] conv output (when conv_w is null)
@@ -367,9 +376,8 @@ __global__ void __launch_bounds__(kThreads, 2) delta_chunk_prep_kernel(PrepParam
 }
 
 struct ScanParams {
-  const float* ws;
+  float* ws;      // the chunk records (S_c^T and Vn^T are written here)
   float* state;   // [B, H, D(k), D(v)]
-  bf16* out;      // [B, L, H, D]
   int L, H, NC;
 };
 
@@ -381,7 +389,6 @@ Q35_DEV void cp_async16(float* dst, const float* src) {
 }
 
 constexpr int kPS = 24;   // row stride (words) of the pre-split S / Vn tiles: B-fragment loads hit distinct banks
-constexpr int kPP = 68;   // row stride of P
 constexpr int kPK2 = 136; // row stride of Kd (read transposed as the A operand of Kd^T Vn: distinct banks)
 
 // A fragment (16 x 8, row-major at `base` with row stride ld), split into TF32 high / low parts.
@@ -417,25 +424,23 @@ Q35_DEV void mma3a(Acc3& d, const uint32_t ah[4], const uint32_t al[4], const ui
   mma_tf32(d.m, ah[0], ah[1], ah[2], ah[3], bh0, bh1);
 }
 
-// Phase B on the tensor cores. Warp w owns the FP32 state tile S[16 w .. 16 w + 16][0 .. 16] in
+// Phase B, the recurrence. Warp w owns the FP32 state tile S[16 w .. 16 w + 16][0 .. 16] in
 // registers across chunks; S and Vn also live in shared memory pre-split into TF32 high / low
 // parts (the B operands), so each value is split once per chunk rather than once per reader.
-//   phase 1: X = [W; Qe] S (128 x 16, K = 128), warp w rows 16 w;  warps 0-3: Vn = U - W S
-//   phase 2: warps 4-7: O = Qe S + P Vn (K = 64);  every warp: S <- gl S + Kd^T Vn on its tile
-// Records arrive in two cp.async groups: {W, Qe, U} for chunk n + 1 is issued once phase 1 of
-// chunk n is done, {P, Kd} once phase 2 is done.
+//   chunk c: S_c^T to the record (for phase C); phase 1: X = W S (64 x 16, K = 128), warp w rows
+//   16 (w & 3) .. + 16 of value columns 8 (w >> 2) .. + 8; Vn = U - X, published pre-split and as
+//   Vn^T to the record; phase 2: every warp S <- gl S + Kd^T Vn on its tile.
+// Records arrive in two cp.async groups: {W, U} for chunk n + 1 is issued once phase 1 of chunk n
+// is done, {Kd} once phase 2 is done. The output products (Qe S_c + P Vn) are phase C's.
 __global__ void __launch_bounds__(kThreads, 1) delta_chunk_scan_kernel(ScanParams p) {
   extern __shared__ __align__(16) float sm[];
   float* W = sm;                   // [64][132]
-  float* Qe = W + kC * kPW;        // [64][132]
-  float* Kd = Qe + kC * kPW;       // [64][136]
-  float* P = Kd + kC * kPK2;       // [64][68]
-  float* U = P + kC * kPP;         // [64][16]
+  float* Kd = W + kC * kPW;        // [64][136]
+  float* U = Kd + kC * kPK2;       // [64][16]
   uint32_t* Vh = reinterpret_cast<uint32_t*>(U + kC * kVS);  // [64][24]
   uint32_t* Vl = Vh + kC * kPS;    // [64][24]
   uint32_t* Sh = Vl + kC * kPS;    // [128][24]
   uint32_t* Sl = Sh + kD * kPS;    // [128][24]
-  float* Epart = reinterpret_cast<float*>(Sl + kD * kPS);  // [8 values][4 warps][32 lanes]: half of P Vn
   const int nvs = kD / kVS;
   const int vs = blockIdx.x % nvs;
   const int h = (blockIdx.x / nvs) % p.H;
@@ -461,27 +466,22 @@ __global__ void __launch_bounds__(kThreads, 1) delta_chunk_scan_kernel(ScanParam
   };
   publish_s();
   auto rec_of = [&](int ch) { return p.ws + ((size_t)(b * p.H + h) * p.NC + ch) * ChunkWs::SIZE; };
-  auto issue_g1 = [&](int ch) {  // W, Qe, U
+  auto issue_g1 = [&](int ch) {  // W, U
     const float* rec = rec_of(ch);
     for (int i = tid; i < kC * kD / 4; i += kThreads) {
       const int r = i / (kD / 4), c4 = (i % (kD / 4)) * 4;
       cp_async16(W + r * kPW + c4, rec + ChunkWs::W + r * kD + c4);
-      cp_async16(Qe + r * kPW + c4, rec + ChunkWs::Qe + r * kD + c4);
     }
     for (int i = tid; i < kC * kVS / 4; i += kThreads) {
       const int r = i / (kVS / 4), c4 = (i % (kVS / 4)) * 4;
       cp_async16(U + r * kVS + c4, rec + ChunkWs::U + r * kD + vs * kVS + c4);
     }
   };
-  auto issue_g2 = [&](int ch) {  // P, Kd
+  auto issue_g2 = [&](int ch) {  // Kd
     const float* rec = rec_of(ch);
     for (int i = tid; i < kC * kD / 4; i += kThreads) {
       const int r = i / (kD / 4), c4 = (i % (kD / 4)) * 4;
       cp_async16(Kd + r * kPK2 + c4, rec + ChunkWs::Kd + r * kD + c4);
-    }
-    for (int i = tid; i < kC * kC / 4; i += kThreads) {
-      const int r = i / (kC / 4), c4 = (i % (kC / 4)) * 4;
-      cp_async16(P + r * kPP + c4, rec + ChunkWs::P + r * kC + c4);
     }
   };
   auto commit = [] { asm volatile("cp.async.commit_group;" ::: "memory"); };
@@ -491,81 +491,48 @@ __global__ void __launch_bounds__(kThreads, 1) delta_chunk_scan_kernel(ScanParam
     issue_g2(0);
     commit();
   }
+  const int mt = warp & 3, nt1 = warp >> 2;  // phase-1 tile: token rows 16 mt, value columns 8 nt1
   for (int ch = 0; ch < p.NC; ++ch) {
     const bool more = ch + 1 < p.NC;
-    const float gl = rec_of(ch)[ChunkWs::GL];  // issued now, used after phase 2b
+    float* rec = const_cast<float*>(rec_of(ch));
+    const float gl = rec[ChunkWs::GL];  // issued now, used in phase 2
+    // S_c^T (value column, key row) for phase C, from the registers before this chunk's update
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) rec[ChunkWs::ST + (size_t)(vs * kVS + frag_col(nt, i)) * kD + frag_row(i)] = s[nt][i];
     asm volatile("cp.async.wait_group 1;" ::: "memory");  // pending: G1(ch), G2(ch)
-    __syncthreads();  // W, Qe, U of this chunk and the published S are visible
-    // ---- phase 1: X = [W; Qe] S for rows 16 warp .. + 16 (12 chains: n-tile x even / odd k-step
-    // x three terms)
-    float x[2][4];
+    __syncthreads();  // W, U of this chunk and the published S are visible
+    // ---- phase 1: X = W S for token rows 16 mt .. + 16, value columns 8 nt1 .. + 8 (six chains:
+    // even / odd k-step x three terms)
+    float x[4];
     {
-      Acc3 xa[2][2];  // [k-step parity][n-tile]
+      Acc3 xa[2];
 #pragma unroll
-      for (int q = 0; q < 2; ++q)
-#pragma unroll
-        for (int nt = 0; nt < 2; ++nt) acc3_zero(xa[q][nt]);
-      const float* A = warp < 4 ? W + warp * 16 * kPW : Qe + (warp - 4) * 16 * kPW;
-#pragma unroll 2
-      for (int k0 = 0; k0 < kD; k0 += 16) {
-#pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          const int k = k0 + 8 * hh;
-          uint32_t ah[4], al[4];
-          load_a_split(A + k, kPW, g, c, ah, al);
-          mma3a(xa[hh][0], ah, al, Sh, Sl, k, 0, g, c);
-          mma3a(xa[hh][1], ah, al, Sh, Sl, k, 8, g, c);
-        }
+      for (int q = 0; q < 2; ++q) acc3_zero(xa[q]);
+      const float* A = W + mt * 16 * kPW;
+#pragma unroll 4
+      for (int k = 0; k < kD; k += 8) {
+        uint32_t ah[4], al[4];
+        load_a_split(A + k, kPW, g, c, ah, al);
+        mma3a(xa[(k >> 3) & 1], ah, al, Sh, Sl, k, 8 * nt1, g, c);
       }
 #pragma unroll
-      for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-        for (int i = 0; i < 4; ++i) x[nt][i] = acc3_value(xa[0][nt], i) + acc3_value(xa[1][nt], i);
+      for (int i = 0; i < 4; ++i) x[i] = acc3_value(xa[0], i) + acc3_value(xa[1], i);
     }
-    if (warp < 4) {  // Vn = U - W S (token rows 16 warp + g (+8)), published pre-split
+    // Vn = U - W S, published pre-split for phase 2 and as Vn^T for phase C
 #pragma unroll
-      for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int r = frag_row(i), col = frag_col(nt, i);
-          split_tf32(U[r * kVS + col] - x[nt][i], Vh[r * kPS + col], Vl[r * kPS + col]);
-        }
+    for (int i = 0; i < 4; ++i) {
+      const int r = mt * 16 + g + (i >= 2 ? 8 : 0), col = nt1 * 8 + 2 * c + (i & 1);
+      const float vn = U[r * kVS + col] - x[i];
+      split_tf32(vn, Vh[r * kPS + col], Vl[r * kPS + col]);
+      rec[ChunkWs::VT + (size_t)(vs * kVS + col) * kC + r] = vn;
     }
     asm volatile("cp.async.wait_group 0;" ::: "memory");  // pending: G2(ch)
-    __syncthreads();  // Vn, P, Kd visible; W, Qe, U free
+    __syncthreads();  // Vn, Kd visible; W, U free
     if (more) issue_g1(ch + 1);
     commit();
-    // ---- phase 2a: O = Qe S + P Vn for token rows 16 (warp & 3) .. + 16: warps 4-7 (which hold
-    // Qe S) take keys 0-31 of P Vn, warps 0-3 keys 32-63 and park their half in shared memory;
-    // warps 4-7 add it and store O after the chunk's last barrier
-    float e[2][4];
-    {
-      const int r = (warp & 3) * 16, kb0 = warp < 4 ? kC / 2 : 0;
-      Acc3 ea[2][2];  // [k-step parity][n-tile]
-#pragma unroll
-      for (int q = 0; q < 2; ++q)
-#pragma unroll
-        for (int nt = 0; nt < 2; ++nt) acc3_zero(ea[q][nt]);
-#pragma unroll
-      for (int kk = 0; kk < kC / 2; kk += 8) {
-        const int k0 = kb0 + kk;
-        uint32_t ah[4], al[4];
-        load_a_split(P + r * kPP + k0, kPP, g, c, ah, al);
-        mma3a(ea[(kk >> 3) & 1][0], ah, al, Vh, Vl, k0, 0, g, c);
-        mma3a(ea[(kk >> 3) & 1][1], ah, al, Vh, Vl, k0, 8, g, c);
-      }
-#pragma unroll
-      for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-        for (int i = 0; i < 4; ++i) e[nt][i] = acc3_value(ea[0][nt], i) + acc3_value(ea[1][nt], i);
-      if (warp < 4) {
-#pragma unroll
-        for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-          for (int i = 0; i < 4; ++i) Epart[((nt * 4 + i) * 4 + warp) * 32 + lane] = e[nt][i];
-      }
-    }
-    // ---- phase 2b: S <- gl S + Kd^T Vn on this warp's tile (rows 16 warp .. + 16)
+    // ---- phase 2: S <- gl S + Kd^T Vn on this warp's tile (rows 16 warp .. + 16)
     {
       float d[2][4];
       {
@@ -590,28 +557,11 @@ __global__ void __launch_bounds__(kThreads, 1) delta_chunk_scan_kernel(ScanParam
       for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
         for (int i = 0; i < 4; ++i) s[nt][i] = gl * s[nt][i] + d[nt][i];
-      publish_s();  // phase 1 readers of Sh / Sl all passed the last barrier
     }
-    __syncthreads();  // P, Kd, Vn free; the parked halves of P Vn are visible
+    __syncthreads();  // phase 1 readers of Sh / Sl and phase 2 readers of Vn are done
+    publish_s();
     if (more) issue_g2(ch + 1);
     commit();
-    if (warp >= 4) {
-      const int r = (warp - 4) * 16;
-      auto ep = [&](int j) { return Epart[(j * 4 + (warp - 4)) * 32 + lane]; };
-#pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        const int t = ch * kC + r + g + 8 * half;
-        if (t < p.L) {
-          bf16* o = p.out + (((int64_t)b * p.L + t) * p.H + h) * kD + vs * kVS;
-#pragma unroll
-          for (int nt = 0; nt < 2; ++nt) {
-            const int i0 = 2 * half, i1 = 2 * half + 1;
-            o[nt * 8 + 2 * c] = f2bf(x[nt][i0] + (e[nt][i0] + ep(nt * 4 + i0)));
-            o[nt * 8 + 2 * c + 1] = f2bf(x[nt][i1] + (e[nt][i1] + ep(nt * 4 + i1)));
-          }
-        }
-      }
-    }
   }
 #pragma unroll
   for (int nt = 0; nt < 2; ++nt)
@@ -619,13 +569,143 @@ __global__ void __launch_bounds__(kThreads, 1) delta_chunk_scan_kernel(ScanParam
     for (int i = 0; i < 4; ++i) Sg[frag_row(i) * kD + frag_col(nt, i)] = s[nt][i];
 }
 
+// ---------------------------------------------------------------------------------------------
+// Phase C: out[t, h, v] = bf16((Qe S_c + P Vn)[t, v]) for the chunk's 64 tokens and 64 of the 128
+// value columns, on tcgen05 (kind::tf32, M = 64, N = 64, K = 128 + 64) with the FP32 accumulator
+// in TMEM. 3xTF32: the A = [Qe | P] and B = [S_c ; Vn] operands are staged as TF32 high / low
+// parts (K-major, 128-byte swizzle) and the three products hi.hi, lo.hi and hi.lo accumulate in
+// one TMEM tile, so the result keeps FP32-level accuracy (the dropped lo.lo term is ~2^-22).
+constexpr int kOutThreads = 256;            // staging; warps 0-3 also read one TMEM lane quarter each
+constexpr int kOutBatch = 6;                // 16-byte loads per operand in flight per thread
+constexpr int kOutK = kD + kC;              // 192
+constexpr int kOutSlabs = kOutK / 32;       // 6 slabs of 32 tf32 (128 bytes)
+constexpr int kOutN = 64;                   // value columns per CTA
+constexpr uint32_t kOutSlabBytes = 64 * 128;  // 64 rows of 128 bytes (A: tokens, B: value columns)
+constexpr uint32_t kOutTile = kOutSlabs * kOutSlabBytes;  // 48 KB per operand part
+constexpr size_t kOutSmem = 4 * (size_t)kOutTile + 1024 + 64;
+constexpr long long kOutWaitBudget = 2000000000LL;
+
+struct OutParams {
+  const float* ws;
+  bf16* out;  // [B, L, H, D]
+  int L, H, NC;
+};
+
+__global__ void __launch_bounds__(kOutThreads, 1) delta_chunk_out_kernel(OutParams p) {
+  extern __shared__ __align__(16) unsigned char out_smem_raw[];
+  unsigned char* sm = reinterpret_cast<unsigned char*>(((uintptr_t)out_smem_raw + 1023) & ~(uintptr_t)1023);
+  unsigned char* A_hi = sm;
+  unsigned char* A_lo = sm + kOutTile;
+  unsigned char* B_hi = sm + 2 * kOutTile;
+  unsigned char* B_lo = sm + 3 * kOutTile;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sm + 4 * kOutTile);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 1);
+  const int half = blockIdx.x & 1;
+  const int ch = (blockIdx.x >> 1) % p.NC;
+  const int h = (blockIdx.x / (2 * p.NC)) % p.H;
+  const int b = blockIdx.x / (2 * p.NC * p.H);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const float* rec = p.ws + ((size_t)(b * p.H + h) * p.NC + ch) * ChunkWs::SIZE;
+
+  if (warp == 0) tc::tmem_alloc(tmem_slot, 64);
+  if (tid == 0) {
+    tc::mbar_init(tc::smem_u32(bar), 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  // ---- stage A = [Qe | P] (64 token rows) and B = [S_c^T | Vn^T] (64 value rows of this half),
+  // 16 bytes (4 values along K) per step, split into TF32 high / low parts
+  auto stage = [&](unsigned char* hi, unsigned char* lo, int row, int k4, float4 v) {
+    uint32_t h4[4], l4[4];
+    tc::split_tf32(v.x, h4[0], l4[0]);
+    tc::split_tf32(v.y, h4[1], l4[1]);
+    tc::split_tf32(v.z, h4[2], l4[2]);
+    tc::split_tf32(v.w, h4[3], l4[3]);
+    const uint32_t off = (uint32_t)(k4 / 32) * kOutSlabBytes + tc::sw128_offset(row, (k4 % 32) / 4);
+    *reinterpret_cast<uint4*>(hi + off) = make_uint4(h4[0], h4[1], h4[2], h4[3]);
+    *reinterpret_cast<uint4*>(lo + off) = make_uint4(l4[0], l4[1], l4[2], l4[3]);
+  };
+  // batches of kOutBatch 16-byte loads per operand in flight per thread before any is used
+  constexpr int kItems = 64 * (kOutK / 4);  // 16-byte items per operand
+  static_assert(kItems % (kOutThreads * kOutBatch) == 0, "whole batches");
+  for (int i0 = 0; i0 < kItems; i0 += kOutThreads * kOutBatch) {
+    float4 a[kOutBatch], bv[kOutBatch];
+#pragma unroll
+    for (int u = 0; u < kOutBatch; ++u) {
+      const int i = i0 + u * kOutThreads + tid;
+      const int r = i / (kOutK / 4), k4 = (i % (kOutK / 4)) * 4;
+      const int v = half * kOutN + r;  // B row: value column
+      a[u] = k4 < kD ? __ldcg(reinterpret_cast<const float4*>(rec + ChunkWs::Qe + r * kD + k4))
+                     : __ldcg(reinterpret_cast<const float4*>(rec + ChunkWs::P + r * kC + (k4 - kD)));
+      bv[u] = k4 < kD ? __ldcg(reinterpret_cast<const float4*>(rec + ChunkWs::ST + (size_t)v * kD + k4))
+                      : __ldcg(reinterpret_cast<const float4*>(rec + ChunkWs::VT + (size_t)v * kC + (k4 - kD)));
+    }
+#pragma unroll
+    for (int u = 0; u < kOutBatch; ++u) {
+      const int i = i0 + u * kOutThreads + tid;
+      const int r = i / (kOutK / 4), k4 = (i % (kOutK / 4)) * 4;
+      stage(A_hi, A_lo, r, k4, a[u]);
+      stage(B_hi, B_lo, r, k4, bv[u]);
+    }
+  }
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic-proxy stores -> MMA reads
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = *tmem_slot;
+  if (tid == 0) {
+    const uint32_t idesc = tc::idesc_f32acc(2, 64, kOutN);
+    const uint32_t ah = tc::smem_u32(A_hi), al = tc::smem_u32(A_lo), bh = tc::smem_u32(B_hi), bl = tc::smem_u32(B_lo);
+    const uint32_t as[3] = {ah, al, ah}, bs[3] = {bh, bh, bl};  // hi.hi, lo.hi, hi.lo
+    uint32_t acc = 0;
+#pragma unroll
+    for (int t = 0; t < 3; ++t)
+#pragma unroll
+      for (int sl = 0; sl < kOutSlabs; ++sl)
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          const uint32_t o = sl * kOutSlabBytes + kk * 32;
+          tc::mma_tf32(tmem, tc::desc_sw128(as[t] + o), tc::desc_sw128(bs[t] + o), idesc, acc);
+          acc = 1;
+        }
+    tc::commit(tc::smem_u32(bar));
+  }
+  __syncwarp();
+  if (warp < 4) {  // TMEM lane quarters
+    const bool ok = tc::mbar_wait_bounded(tc::smem_u32(bar), 0, kOutWaitBudget);
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    // M = 64: token row 16 q + i sits in TMEM lane 32 q + i (i < 16) of warp q's lane quarter
+    uint32_t v0[32], v1[32];
+    const uint32_t tq = tmem + ((uint32_t)(warp * 32) << 16);
+    tc::tmem_ld32(tq, v0);
+    tc::tmem_ld32(tq + 32, v1);
+    if (!ok) {
+      if (lane == 0) atomicCAS(&q35_delta_chunk_error_word, 0, 1);
+    } else if (lane < 16) {
+      const int t = ch * kC + warp * 16 + lane;
+      if (t < p.L) {
+        bf16* o = p.out + (((int64_t)b * p.L + t) * p.H + h) * kD + half * kOutN;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          __align__(16) bf16 w8[8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) w8[j] = f2bf(__uint_as_float(v0[8 * q + j]));
+          reinterpret_cast<uint4*>(o)[q] = *reinterpret_cast<const uint4*>(w8);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) w8[j] = f2bf(__uint_as_float(v1[8 * q + j]));
+          reinterpret_cast<uint4*>(o + 32)[q] = *reinterpret_cast<const uint4*>(w8);
+        }
+      }
+    }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == 0) tc::tmem_dealloc(tmem, 64);
+}
+
 constexpr size_t kPrepSmem =
     (size_t)3 * (kHalo + kC) * kPB * sizeof(bf16) + (size_t)(kC * kTS + 48 * 16) * sizeof(float);
 static_assert((3 * (kHalo + kC) * kPB * sizeof(bf16)) % 16 == 0, "T starts 16-byte aligned");
 static_assert((kHalo * kPB * sizeof(bf16)) % 16 == 0, "tile rows stay 16-byte aligned");
-constexpr size_t kScanSmem =
-    (size_t)(2 * kC * kPW + kC * kPK2 + kC * kPP + kC * kVS + 2 * kC * kPS + 2 * kD * kPS + 4 * 32 * 8) *
-    sizeof(float);
+constexpr size_t kScanSmem = (size_t)(kC * kPW + kC * kPK2 + kC * kVS + 2 * kC * kPS + 2 * kD * kPS) * sizeof(float);
 
 }  // namespace
 
@@ -648,6 +728,7 @@ int q35_delta_chunked_launch(const void* qkv, const void* packed, const void* a_
   attr.get([] {
     cudaFuncSetAttribute(delta_chunk_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPrepSmem);
     cudaFuncSetAttribute(delta_chunk_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kScanSmem);
+    cudaFuncSetAttribute(delta_chunk_out_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kOutSmem);
     return true;
   });
   PrepParams pp{(const bf16*)qkv,         (const bf16*)packed,    (const bf16*)a_log, (const bf16*)dt_bias,
@@ -656,9 +737,20 @@ int q35_delta_chunked_launch(const void* qkv, const void* packed, const void* a_
   delta_chunk_prep_kernel<<<(unsigned)(batch * heads * nc), kThreads, kPrepSmem, s>>>(pp);
   int rc = q35_check_launch("delta_chunk_prep");
   if (rc) return rc;
-  ScanParams sp{ws, state, (bf16*)out, (int)seq_len, (int)heads, nc};
+  ScanParams sp{ws, state, (int)seq_len, (int)heads, nc};
   delta_chunk_scan_kernel<<<(unsigned)(batch * heads * (kD / kVS)), kThreads, kScanSmem, s>>>(sp);
-  return q35_check_launch("delta_chunk_scan");
+  rc = q35_check_launch("delta_chunk_scan");
+  if (rc) return rc;
+  OutParams op{ws, (bf16*)out, (int)seq_len, (int)heads, nc};
+  delta_chunk_out_kernel<<<(unsigned)(batch * heads * nc * 2), kOutThreads, kOutSmem, s>>>(op);
+  return q35_check_launch("delta_chunk_out");
+}
+
+extern "C" int q35_delta_chunk_error(void) {
+  int v = 0, zero = 0;
+  if (cudaMemcpyFromSymbol(&v, q35_delta_chunk_error_word, sizeof(int)) != cudaSuccess) return -1;
+  if (v) cudaMemcpyToSymbol(q35_delta_chunk_error_word, &zero, sizeof(int));
+  return v;
 }
 
 extern "C" size_t q35_delta_chunked_workspace_size(int64_t batch, int64_t heads, int64_t seq_len) {

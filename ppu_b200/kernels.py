@@ -189,13 +189,22 @@ def gemm_a8w8_tc(qa, sx, qw, sw, *, epilogue=L.EPI_STORE, out=None) -> torch.Ten
 
 
 def tc_error() -> int:
-    """Error word of the tensor-core kernels (0 = every bounded wait completed)."""
-    return int(L.load().q35_tc_error())
+    """Error word of the tensor-core kernels (0 = every bounded wait completed): the projection
+    GEMMs' code, or 0x100 when the chunked DeltaNet output kernel's wait gave up."""
+    lib = L.load()
+    gemm = int(lib.q35_tc_error())
+    delta = int(lib.q35_delta_chunk_error())
+    return gemm | (0x100 if delta else 0)
 
 
 def set_gemm_tc_pairs(on: bool) -> None:
     """Process-wide: tensor-core projections on SM pairs (cta_group::2, default) or single SMs."""
     L.call("q35_set_gemm_tc_pairs", 1 if on else 0)
+
+
+def set_gemm_tc_split(on: bool) -> None:
+    """Process-wide: split K in two over SM pairs for narrow outputs (N <= 2048; default off)."""
+    L.call("q35_set_gemm_tc_split", 1 if on else 0)
 
 
 # ---------------------------------------------------------------------------- A8W8

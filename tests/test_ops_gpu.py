@@ -454,5 +454,7 @@ def test_delta_chunked_prefill(length):
     want = O.delta_recurrent(qkv, packed, a_log, dt_bias, st)
     std = cu(st0.clone())
     got = K.delta_chunked_fused(cu(qkv), cu(packed), cu(a_log), cu(dt_bias), std)
+    torch.cuda.synchronize()
+    assert K.tc_error() == 0
     assert rel_err(got, want) < 1e-2
     assert torch.allclose(std.cpu(), st, rtol=1e-3, atol=1e-4)
