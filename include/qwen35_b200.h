@@ -210,13 +210,6 @@ int q35_tc_error(void);
 /* Process-wide: 1 (default) runs the tensor-core projections on CTA pairs (thread-block clusters
  * of 2, tcgen05 cta_group::2, 256-row tiles), 0 on single CTAs (128-row tiles). */
 int q35_set_gemm_tc_pairs(int on);
-/* Process-wide switch (default 0): narrow outputs (N <= 2048, e.g. the out / down projections:
- * 32 tiles of 256 x 256 for 74 SM pairs at M = 1024) split each tile's K range over two pairs;
- * the last part to finish sums the parts' raw accumulators in part order (exact for int8) and
- * runs the epilogue. The split depends on N and K only, so a row's result does not depend on M.
- * Split launches share one scratch buffer per device: run them on one stream at a time.
- * 0: never split. */
-int q35_set_gemm_tc_split(int on);
 
 /* ---------------------------------------------------------------- attention */
 

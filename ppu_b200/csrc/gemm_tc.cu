@@ -47,13 +47,6 @@ struct TcParams {
   const float* sx;    // int8: [M]
   const float* sw;    // int8: [Nw]
   int M, N, K;        // K in elements
-  // split K (pair kernel): each tile's K range in two parts run by different pairs; each part
-  // writes its raw accumulator (FP32 / S32 bits) to part[tile][k part][256 rows][TBN], and the
-  // last part to arrive (ticket per tile, CTA and epilogue warp) adds the other part and runs the
-  // epilogue
-  int splits;
-  uint32_t* part;
-  unsigned* tickets;  // [tiles][2 CTAs][8 epilogue warps], zero between launches (the last arrival re-zeroes its word)
 };
 
 Q35_DEV uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -203,24 +196,8 @@ Q35_DEV void mbar_expect_tx_only(uint32_t bar, uint32_t bytes) {
 // chunks h, h + 2, ... of its TMEM lane quarter. The residual reads of chunk c + 2 are issued
 // before chunk c's TMEM load, so the chunks' memory round trips overlap instead of following one
 // another (with one read round trip per chunk, 8 chunks in a row made the tile's tail several us).
-// The raw accumulator row of this thread (all TBN columns of the warp's chunks) to its part slot.
-template <int TBN>
-Q35_DEV void store_part(uint32_t trow, uint32_t* dst, int h) {
-  for (int c = 32 * h; c < TBN; c += 64) {
-    uint32_t v[32];
-    tmem_ld32(trow + c, v);
-    uint4* o = reinterpret_cast<uint4*>(dst + c);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) o[i] = make_uint4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
-  }
-}
-
-// Split K (two parts): `other` holds this row's raw accumulator of the other part; the sum
-// own + other is the same whichever part runs the epilogue (addition commutes exactly). Its
-// chunks are read one chunk ahead, like the residual, so the reads overlap.
 template <bool INT8, int EPI, int TBN>
-Q35_DEV void epilogue_row(const TcParams& p, uint32_t trow, int row, int col0, int h,
-                          const uint32_t* other = nullptr) {
+Q35_DEV void epilogue_row(const TcParams& p, uint32_t trow, int row, int col0, int h) {
   constexpr int kCols = (EPI == Q35_EPI_SWIGLU) ? TBN / 2 : TBN;
   const bool row_ok = row < p.M;
   bf16* base = (EPI == Q35_EPI_RESIDUAL ? p.resid : static_cast<bf16*>(p.out)) + (int64_t)(row_ok ? row : 0) * p.N;
@@ -233,33 +210,13 @@ Q35_DEV void epilogue_row(const TcParams& p, uint32_t trow, int row, int col0, i
       for (int i = 0; i < 4; ++i) r[i] = *reinterpret_cast<const uint4*>(base + gc + 8 * i);
     }
   };
-  uint4 pt[8], pt_n[8];  // split K: the other part's raw accumulator, this chunk and the next
-  auto fetch_part = [&](int c, uint4 (&r)[8]) {
-    const uint4* src = reinterpret_cast<const uint4*>(other + c);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) r[i] = __ldcg(src + i);
-  };
-  if (32 * h < kCols) {
-    fetch(32 * h, res);
-    if (EPI != Q35_EPI_SWIGLU && other) fetch_part(32 * h, pt);
-  }
+  if (32 * h < kCols) fetch(32 * h, res);
   for (int c = 32 * h; c < kCols; c += 64) {
-    if (c + 64 < kCols) {
-      fetch(c + 64, res_n);
-      if (EPI != Q35_EPI_SWIGLU && other) fetch_part(c + 64, pt_n);
-    }
+    if (c + 64 < kCols) fetch(c + 64, res_n);
     const int gc = col0 + c;
     uint32_t v[32], u[32];
     tmem_ld32(trow + c, v);
     if (EPI == Q35_EPI_SWIGLU) tmem_ld32(trow + TBN / 2 + c, u);
-    if (EPI != Q35_EPI_SWIGLU && other) {
-      const uint32_t* o = reinterpret_cast<const uint32_t*>(pt);
-#pragma unroll
-      for (int j = 0; j < 32; ++j)
-        v[j] = INT8 ? (uint32_t)((int)v[j] + (int)o[j]) : __float_as_uint(__uint_as_float(v[j]) + __uint_as_float(o[j]));
-#pragma unroll
-      for (int i = 0; i < 8; ++i) pt[i] = pt_n[i];
-    }
     if (row_ok && gc < p.N) {
       float y[32];
 #pragma unroll
@@ -475,10 +432,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   const int n_k = p.K / kstep;
   const int num_m = (p.M + 2 * BM - 1) / (2 * BM);
   const int ntiles = num_m * ((p.N + kCols - 1) / kCols);
-  const int nsplit = p.splits > 1 ? p.splits : 1;
-  const int nunits = ntiles * nsplit;  // unit u: tile u % ntiles, K part u / ntiles
-  auto k_begin = [&](int u) { return (u / ntiles) * n_k / nsplit; };
-  auto k_end = [&](int u) { return (u / ntiles + 1) * n_k / nsplit; };
   const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + S);
   const uint32_t tfull0 = smem_u32(bars + 2 * S), tempty0 = smem_u32(bars + 2 * S + 2);
 
@@ -510,10 +463,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       // ---------------- TMA producer (both CTAs)
       int it = 0;
       bool ok = true;
-      for (int unit = pair; unit < nunits && ok; unit += npairs) {
-        const int tile = unit % ntiles;
+      for (int tile = pair; tile < ntiles && ok; tile += npairs) {
         const int m0 = (tile % num_m) * 2 * BM + (int)rank * BM, c0 = (tile / num_m) * kCols;
-        for (int kt = k_begin(unit); kt < k_end(unit); ++kt, ++it) {
+        for (int kt = 0; kt < n_k; ++kt, ++it) {
           const int s = it % S, r = it / S;
           if (r > 0 && !mbar_wait(empty0 + 8 * s, (r - 1) & 1, abort_flag, 11)) {
             ok = false;
@@ -536,13 +488,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                              ((uint32_t)((2 * BM) >> 4) << 24);
       int it = 0, tc = 0;
       bool ok = true;
-      for (int unit = pair; unit < nunits && ok; unit += npairs, ++tc) {
+      for (int tile = pair; tile < ntiles && ok; tile += npairs, ++tc) {
         const int acc = tc & 1, use = tc >> 1;
         if (use > 0 && !mbar_wait(tempty0 + 8 * acc, (use - 1) & 1, abort_flag, 14)) break;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         const uint32_t d = tmem + (uint32_t)(acc * TBN);
-        const int kb = k_begin(unit);
-        for (int kt = kb; kt < k_end(unit); ++kt, ++it) {
+        for (int kt = 0; kt < n_k; ++kt, ++it) {
           const int s = it % S, r = it / S;
           if (!mbar_wait(full0 + 8 * s, r & 1, abort_flag, 12)) {
             ok = false;
@@ -552,7 +503,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           const uint32_t a0 = smem_u32(sA + s * kABytes), b0 = smem_u32(sB + s * kBB);
 #pragma unroll
           for (int k = 0; k < BKB / 32; ++k)
-            mma_pair<INT8>(d, smem_desc(a0 + 32 * k), smem_desc(b0 + 32 * k), idesc, (kt > kb || k > 0) ? 1u : 0u);
+            mma_pair<INT8>(d, smem_desc(a0 + 32 * k), smem_desc(b0 + 32 * k), idesc, (kt > 0 || k > 0) ? 1u : 0u);
           mma_commit_pair(empty0 + 8 * s);
         }
         if (ok) mma_commit_pair(tfull0 + 8 * acc);
@@ -563,36 +514,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const int q = warp & 3, h = (warp - 2) >> 2;
     const uint32_t tempty_leader = map_to_rank(tempty0, 0);
     int tc = 0;
-    for (int unit = pair; unit < nunits; unit += npairs, ++tc) {
+    for (int tile = pair; tile < ntiles; tile += npairs, ++tc) {
       const int acc = tc & 1, use = tc >> 1;
       if (!mbar_wait(tfull0 + 8 * acc, use & 1, abort_flag, 13)) break;
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      const int tile = unit % ntiles, ks = unit / ntiles;
       const int m0 = (tile % num_m) * 2 * BM + (int)rank * BM, col0 = (tile / num_m) * kCols;
       const uint32_t trow = tmem + (uint32_t)(acc * TBN) + ((uint32_t)(q * 32) << 16);
-      if (nsplit > 1) {
-        // this part's raw accumulator out (the warp's rows and column chunks), then a ticket per
-        // (tile, CTA, epilogue warp): the warp of the last part in sums every part's values in
-        // index order (the same sum whichever part arrives last) and finishes those columns.
-        // Warps never wait on one another.
-        const int trow_i = (int)rank * BM + q * 32 + lane;  // row within the 256-row tile
-        const int64_t kstride = (int64_t)2 * BM * TBN;
-        uint32_t* my_rows = p.part + ((int64_t)tile * nsplit * 2 * BM + trow_i) * TBN;
-        store_part<TBN>(trow, my_rows + ks * kstride, h);
-        __threadfence();
-        __syncwarp();
-        unsigned* tk = p.tickets + ((int64_t)tile * 2 + rank) * kEpiWarps + (warp - 2);
-        unsigned t = 0;
-        if (lane == 0) t = atomicAdd(tk, 1u);
-        t = __shfl_sync(0xffffffffu, t, 0);
-        if (t == (unsigned)(nsplit - 1)) {
-          __threadfence();
-          epilogue_row<INT8, EPI, TBN>(p, trow, m0 + q * 32 + lane, col0, h, my_rows + (1 - ks) * kstride);
-          if (lane == 0) atomicExch(tk, 0u);
-        }
-      } else {
-        epilogue_row<INT8, EPI, TBN>(p, trow, m0 + q * 32 + lane, col0, h);
-      }
+      epilogue_row<INT8, EPI, TBN>(p, trow, m0 + q * 32 + lane, col0, h);
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(tempty_leader + 8 * acc);
@@ -653,7 +581,6 @@ int launch_tc_bn(const void* a, const void* w, const TcParams& p, cudaStream_t s
 }
 
 int g_tc_pairs = 1;  // process-wide: CTA-pair kernel (1) or single-CTA kernel (0)
-int g_tc_split = 0;  // process-wide: split K over idle pairs when the tiles fill at most half of them
 
 template <bool INT8, int EPI>
 int max_active_pairs() {
@@ -681,50 +608,9 @@ int max_active_pairs() {
   });
 }
 
-// Split-K scratch: raw accumulator parts and per-tile-half tickets, one buffer per device,
-// allocated by the first launch that splits (before any stream capture: the first prefill or
-// vision encode runs eagerly).
-constexpr size_t kSplitPartBytes = 32u << 20;
-constexpr int kSplitTickets = 1024;
-struct SplitScratch {
-  uint32_t* part = nullptr;
-  unsigned* tickets = nullptr;
-};
-SplitScratch split_scratch() {
-  static Q35PerDevice<SplitScratch> ws;
-  return ws.get([] {
-    SplitScratch w;
-    void* p = nullptr;
-    void* t = nullptr;
-    if (cudaMalloc(&p, kSplitPartBytes) == cudaSuccess && cudaMalloc(&t, kSplitTickets * sizeof(unsigned)) == cudaSuccess &&
-        cudaMemset(t, 0, kSplitTickets * sizeof(unsigned)) == cudaSuccess) {
-      w.part = static_cast<uint32_t*>(p);
-      w.tickets = static_cast<unsigned*>(t);
-    } else {
-      cudaGetLastError();
-      if (p) cudaFree(p);
-      if (t) cudaFree(t);
-    }
-    return w;
-  });
-}
-
-// K parts per tile for the pair kernel. Narrow outputs (at most 8 column tiles of 256, e.g. the
-// N = 2048 out / down projections: 32 tiles for 74 pairs at M = 1024) split K in two, each part
-// keeping >= 8 K stages. The choice depends on N and K only, never on M, so a row's result (the
-// parts summed in index order) is the same whatever rows share the launch: one request's
-// prefill and the same request inside a batched prefill give identical projections. Shapes
-// whose parts would not fit the scratch run unsplit.
-int pair_splits(int64_t n_col_tiles, int64_t tiles, int n_k, bool swiglu) {
-  if (swiglu || n_col_tiles > 8 || n_k < 16) return 1;
-  const int sp = 2;
-  if (tiles * sp * 2 * BM * 256 * 4 > (int64_t)kSplitPartBytes || tiles * 2 * kEpiWarps > kSplitTickets) return 1;
-  return sp;
-}
-
 // Pair tiles are 256 x 256 (an N = 128 MMA runs at about half the rate of N = 256 on either kernel).
 template <bool INT8, int EPI>
-int launch_tc2(const void* a, const void* w, TcParams p, cudaStream_t s, int splits = 1) {
+int launch_tc2(const void* a, const void* w, const TcParams& p, cudaStream_t s) {
   constexpr int TBN = 256;
   const int npairs = max_active_pairs<INT8, EPI>();
   const int cols = (EPI == Q35_EPI_SWIGLU) ? TBN / 2 : TBN;
@@ -733,17 +619,7 @@ int launch_tc2(const void* a, const void* w, TcParams p, cudaStream_t s, int spl
   const uint64_t wrows = (EPI == Q35_EPI_SWIGLU) ? 2 * (uint64_t)p.N : (uint64_t)p.N;
   if (!make_map(&ma, a, p.M, p.K, BM, INT8) || !make_map(&mb, w, wrows, p.K, TBN / 2, INT8))
     return q35_fail(Q35_ECUDA, "gemm_tc: tensor map encoding failed");
-  p.splits = 1;
-  if (splits > 1) {
-    const SplitScratch ws = split_scratch();
-    if (ws.part) {
-      p.splits = splits;
-      p.part = ws.part;
-      p.tickets = ws.tickets;
-    }
-  }
-  const int64_t units = tiles * p.splits;
-  const int64_t pairs = units < npairs ? units : npairs;
+  const int64_t pairs = tiles < npairs ? tiles : npairs;
   cudaFuncSetAttribute(gemm_tc2_kernel<INT8, EPI, TBN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                        (int)smem_bytes_pair(TBN));
   gemm_tc2_kernel<INT8, EPI, TBN><<<(unsigned)(2 * pairs), kThreads, smem_bytes_pair(TBN), s>>>(ma, mb, p);
@@ -759,13 +635,6 @@ int launch_tc2(const void* a, const void* w, TcParams p, cudaStream_t s, int spl
 template <bool INT8, int EPI>
 int launch_tc(const void* a, const void* w, const TcParams& p, cudaStream_t s) {
   const int64_t mt = (p.M + BM - 1) / BM;
-  if (g_tc_pairs && g_tc_split) {  // narrow outputs: split K over otherwise idle pairs
-    const int cols256 = (EPI == Q35_EPI_SWIGLU) ? 128 : 256;
-    const int64_t nct = (p.N + cols256 - 1) / cols256;
-    const int sp = pair_splits(nct, nct * ((p.M + 2 * BM - 1) / (2 * BM)), p.K / (BKB / (INT8 ? 1 : 2)),
-                               EPI == Q35_EPI_SWIGLU);
-    if (sp > 1) return launch_tc2<INT8, EPI>(a, w, p, s, sp);
-  }
   const int cols128 = (EPI == Q35_EPI_SWIGLU) ? 64 : 128;
   const int64_t t128 = (int64_t)((p.N + cols128 - 1) / cols128) * mt;
   if (t128 <= kNumSMs && mt * 2 <= t128) return launch_tc_bn<INT8, EPI, 128>(a, w, p, s);
@@ -834,12 +703,6 @@ extern "C" int q35_gemm_tc(const void* a, const void* w, void* out, int64_t m, i
 extern "C" int q35_gemm_tc_a8w8(const int8_t* qa, const float* sx, const int8_t* qw, const float* sw, void* out,
                                 int64_t m, int64_t n, int64_t k, int32_t epilogue, void* stream) {
   return q35_gemm_tc_launch(qa, qw, out, m, n, k, epilogue, true, sx, sw, (cudaStream_t)stream);
-}
-
-extern "C" int q35_set_gemm_tc_split(int on) {
-  Q35_REQUIRE(on == 0 || on == 1, "gemm_tc: split must be 0 or 1");
-  g_tc_split = on;
-  return Q35_OK;
 }
 
 extern "C" int q35_set_gemm_tc_pairs(int on) {

@@ -202,11 +202,6 @@ def set_gemm_tc_pairs(on: bool) -> None:
     L.call("q35_set_gemm_tc_pairs", 1 if on else 0)
 
 
-def set_gemm_tc_split(on: bool) -> None:
-    """Process-wide: split K in two over SM pairs for narrow outputs (N <= 2048; default off)."""
-    L.call("q35_set_gemm_tc_split", 1 if on else 0)
-
-
 # ---------------------------------------------------------------------------- A8W8
 def quantize_rows(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
     """Weight-side per-row symmetric int8 (explore_runtime_quantization.py:143-155):

@@ -102,7 +102,6 @@ _SIGS = {
     "q35_gemm_tc_a8w8": (INT, [P, P, P, P, P, I64, I64, I64, I32, P]),
     "q35_tc_error": (INT, []),
     "q35_set_gemm_tc_pairs": (INT, [C.c_int]),
-    "q35_set_gemm_tc_split": (INT, [C.c_int]),
     "q35_delta_chunk_error": (INT, []),
     "q35_qgkv_norm_rope": (INT, [P, P, P, P, P, P, P, P, P, I64, I64, I64, I64, I64, I64, I64, F32, P]),
     "q35_gqa_decode_workspace_size": (SZ, [I64, I64, I64, I64, I64]),

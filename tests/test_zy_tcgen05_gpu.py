@@ -97,23 +97,3 @@ def test_gemm_tc_persistent_many_tiles():
     assert K.tc_error() == 0
     assert torch.equal(got.cpu(), want)
 
-
-def test_gemm_tc_split_k_rows_do_not_depend_on_m():
-    """With split K on, narrow outputs (N = 2048) split K over two SM pairs; the split depends on N
-    and K only, so each row's result is the same whatever other rows share the launch (a request
-    prefilled alone or inside a batch), and it stays within the bf16 tolerance of the unsplit
-    kernel."""
-    a = randn(600, 6144, seed=31)
-    w = randn(2048, 6144, seed=32, scale=0.02)
-    K.set_gemm_tc_split(True)
-    try:
-        full = K.gemm(cu(a), cu(w), tc=True)
-        part = K.gemm(cu(a[:89].contiguous()), cu(w), tc=True)
-        torch.cuda.synchronize()
-    finally:
-        K.set_gemm_tc_split(False)
-    assert K.tc_error() == 0
-    assert torch.equal(full[:89], part)
-    unsplit = K.gemm(cu(a), cu(w), tc=True)
-    assert_bf16_close(full.cpu(), unsplit.cpu(), max_ulp=2, max_frac=0.02)
-    assert_bf16_close(full.cpu(), O.linear(a, w), max_ulp=2, max_frac=0.02)
