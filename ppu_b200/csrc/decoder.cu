@@ -19,7 +19,8 @@
 #include "common.cuh"
 
 int q35_gemv_launch(const q35_gemv_desc* d, cudaStream_t s, bool pdl);
-int q35_gemv_batch_launch(const q35_gemv_desc* d, int64_t batch, cudaStream_t s, bool pdl);
+int q35_gemv_batch_launch(const q35_gemv_desc* d, int64_t batch, cudaStream_t s, bool pdl, void* split_ws = nullptr);
+size_t q35_gemv_batch_split_bytes(int64_t n_out);
 int q35_lm_head_batch_launch(const void* hidden, int64_t batch, const void* norm_weight, const void* weight,
                              int64_t vocab, float eps, int64_t* keys_out, void* workspace, cudaStream_t s, bool pdl);
 extern "C" size_t q35_lm_shard_workspace_size(void);
@@ -89,6 +90,7 @@ struct Buffers {
   void* attn_ws;
   void* lm_ws;
   void* lm_keys_ws;   // batched decode: the shard top-1 workspace (keys reduced over the vocabulary)
+  void* split_ws;     // batched decode: split-K parts + tickets of the narrow projections (zeroed)
   int64_t* lm_keys;   // batched decode: [batch] reduced keys
   void* pk_ws;        // persistent decode step: op table, attention partials, barrier words
   // prefill
@@ -120,6 +122,7 @@ Buffers carve(const q35_decoder_desc& d, void* base, size_t* total) {
   b.lm_ws = c.take<char>(256);  // LM head ticket + key (must start zeroed)
   b.lm_keys_ws = c.take<char>(128);  // batched LM head: 8 keys + count (zeroed, left zeroed)
   b.lm_keys = c.take<int64_t>(8);
+  b.split_ws = c.take<char>(nb > 1 ? q35_gemv_batch_split_bytes(d.hidden) : 0);
   b.resid = c.take<bf16>(nb * d.hidden);
   b.mix_in_out = c.take<bf16>(nb * rows_in);
   b.mix_out = c.take<bf16>(nb * mixw);
@@ -257,7 +260,7 @@ static int decode_layers(q35_decoder* dec, cudaStream_t s) {
   const bool q8 = d.a8w8 != 0;
   const int64_t nb = d.batch > 1 ? d.batch : 1;
   auto gemv = [&](const q35_gemv_desc* g) -> int {
-    return nb > 1 ? q35_gemv_batch_launch(g, nb, s, pdl) : q35_gemv_launch(g, s, pdl);
+    return nb > 1 ? q35_gemv_batch_launch(g, nb, s, pdl, B.split_ws) : q35_gemv_launch(g, s, pdl);
   };
   const int qgkv_rows = 2 * d.q_heads * d.head_dim + 2 * d.kv_heads * d.head_dim;
   for (int i = 0; i < d.n_layers; ++i) {

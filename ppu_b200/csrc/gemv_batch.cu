@@ -39,6 +39,8 @@ struct BatchGemvParams {
   bf16* out;              // STORE / SWIGLU: [n, n_out]
   unsigned long long* top1;  // TOP1: workspace keys [8] + count (zero before, zero after)
   long long* keys_out;    // TOP1: [n] reduced signed keys
+  float4* part;           // split K: [groups][KSPLIT][32] partial tiles (lane layout of warp 0)
+  unsigned* tickets;      // split K: [groups], zero between launches (the last part re-zeroes it)
   int64_t vocab;
   int n, n_out;
   float eps;
@@ -47,6 +49,29 @@ struct BatchGemvParams {
 template <int K>
 constexpr int xs_stride() {  // bf16 elements per request row in shared memory (+64 bytes: see load)
   return K + 32;
+}
+
+// Largest batch of per-lane 16-byte loads (<= 8) that divides a row's CPL chunks.
+constexpr int load_batch(int cpl) {
+  for (int b = 8; b > 1; --b)
+    if (cpl % b == 0) return b;
+  return 1;
+}
+
+// Split K (PLAIN prologue): columns [k0, k0 + KS) of request b's input into its row of xs.
+template <int KS>
+Q35_DEV void build_input_slice(const BatchGemvParams& p, int k_full, int k0, bf16* xs, int warp, int lane) {
+  constexpr int CPL = KS / 8 / 32;
+  constexpr int BATCH = load_batch(CPL);
+  uint4* dst = reinterpret_cast<uint4*>(xs + warp * xs_stride<KS>());
+  const uint4* src = reinterpret_cast<const uint4*>(p.input + (int64_t)warp * k_full + k0);
+  for (int c0 = 0; c0 < CPL; c0 += BATCH) {
+    uint4 v[BATCH];
+#pragma unroll
+    for (int i = 0; i < BATCH; ++i) v[i] = warp < p.n ? src[lane + 32 * (c0 + i)] : make_uint4(0, 0, 0, 0);
+#pragma unroll
+    for (int i = 0; i < BATCH; ++i) dst[lane + 32 * (c0 + i)] = v[i];
+  }
 }
 
 // Warp b builds request b's input row (bf16) in shared memory.
@@ -66,8 +91,15 @@ Q35_DEV void build_inputs(const BatchGemvParams& p, bf16* xs, int warp, int lane
     row = p.embed + t * (int64_t)K;
   }
   const uint4* src = reinterpret_cast<const uint4*>(row);
-  if (PRO == Q35_PRO_PLAIN) {
-    for (int c = 0; c < CPL; ++c) dst[lane + 32 * c] = src[lane + 32 * c];
+  if (PRO == Q35_PRO_PLAIN) {  // loads in batches of up to 8 per lane, each batch before its stores
+    constexpr int BATCH = load_batch(CPL);
+    for (int c0 = 0; c0 < CPL; c0 += BATCH) {
+      uint4 v[BATCH];
+#pragma unroll
+      for (int i = 0; i < BATCH; ++i) v[i] = src[lane + 32 * (c0 + i)];
+#pragma unroll
+      for (int i = 0; i < BATCH; ++i) dst[lane + 32 * (c0 + i)] = v[i];
+    }
     return;
   }
   float ss = 0.f;
@@ -95,9 +127,15 @@ Q35_DEV unsigned long long top1_key(float v, int idx) {
   return ((unsigned long long)float_order_key(v) << 32) | (unsigned long long)(0xFFFFFFFFu - (uint32_t)idx);
 }
 
-template <int K, int PRO, int EPI>
+// KSPLIT > 1 (PLAIN + RESIDUAL only): the K range of every 16-row group is split over KSPLIT
+// CTAs (CTA i takes part i % KSPLIT of groups i / KSPLIT, i / KSPLIT + gridDim.x / KSPLIT, ...);
+// each part writes its partial tile, and the last part of a group (atomic ticket) sums the parts
+// in part order and applies the residual epilogue, so the result does not depend on arrival order.
+template <int K, int PRO, int EPI, int KSPLIT = 1>
 __global__ void __launch_bounds__(kThreads) gemv_batch_kernel(BatchGemvParams p) {
-  constexpr int KW = K / kWarps;       // K columns per warp
+  static_assert(KSPLIT == 1 || (PRO == Q35_PRO_PLAIN && EPI == Q35_EPI_RESIDUAL), "split K: plain residual only");
+  constexpr int KS = K / KSPLIT;       // K columns of this CTA's part
+  constexpr int KW = KS / kWarps;      // K columns per warp
   constexpr int NBK = KW / kBlk;       // blocks per warp
   constexpr int STAGE = NBK > 8 ? 6 : NBK;  // blocks per register stage
   constexpr int NST = NBK / STAGE;     // stages per group; more than one: two register buffers
@@ -107,14 +145,17 @@ __global__ void __launch_bounds__(kThreads) gemv_batch_kernel(BatchGemvParams p)
   static_assert(NST == 1 || NST % 2 == 0, "stages per group: one, or an even count");
   constexpr int UNITS = (EPI == Q35_EPI_SWIGLU) ? 8 : 16;  // output units per 16-row group
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  bf16* xs = reinterpret_cast<bf16*>(smem_raw);  // [8][K + 32]
+  bf16* xs = reinterpret_cast<bf16*>(smem_raw);  // [8][KS + 32]
   __shared__ float4 part[kWarps][32];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
   const int n_out = p.n_out;
   const int ngroups = (n_out + UNITS - 1) / UNITS;
   const char* W = reinterpret_cast<const char*>(p.weight);
-  const int k0 = warp * KW;
+  const int ks = (int)blockIdx.x % KSPLIT;  // this CTA's part of K
+  const int kbase = ks * KS;
+  const int k0 = kbase + warp * KW;         // weight column of this warp's first block
+  const int gstep = (int)gridDim.x / KSPLIT;
 
   // rows of lane g's two A-fragment rows in group grp (clamped in range; masked at the epilogue)
   auto rows = [&](int grp, int64_t& r0, int64_t& r1, bool& ok0, bool& ok1) {
@@ -144,19 +185,22 @@ __global__ void __launch_bounds__(kThreads) gemv_batch_kernel(BatchGemvParams p)
       wb[buf][i] = ok1 ? ld_stream(b1 + i * kBlk * 2) : make_uint4(0, 0, 0, 0);
     }
   };
-  int grp = blockIdx.x;
+  int grp = (int)blockIdx.x / KSPLIT;
   if (grp < ngroups) {
     load(grp, 0, 0);
     if (NST > 1) load(grp, 1, NBUF - 1);
   }
   pdl_wait();
   pdl_launch_dependents();
-  build_inputs<K, PRO>(p, xs, warp, lane);
+  if constexpr (KSPLIT > 1)
+    build_input_slice<KS>(p, K, kbase, xs, warp, lane);
+  else
+    build_inputs<K, PRO>(p, xs, warp, lane);
   __syncthreads();
 
   unsigned long long best[2] = {0ull, 0ull};  // TOP1: this lane's best keys for requests 2t, 2t + 1
-  const bf16* xrow = xs + g * xs_stride<K>() + k0 + 8 * t;
-  for (; grp < ngroups; grp += gridDim.x) {
+  const bf16* xrow = xs + g * xs_stride<KS>() + (k0 - kbase) + 8 * t;
+  for (; grp < ngroups; grp += gstep) {
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
     // stage st computes from buffer st % NBUF; the buffer is refilled at once with the stage two
     // ahead (or the next group's first stages), so one stage is always in flight
@@ -172,13 +216,15 @@ __global__ void __launch_bounds__(kThreads) gemv_batch_kernel(BatchGemvParams p)
       const int nxt = st + NBUF;  // the stage this buffer holds next
       if (nxt < NST)
         load(grp, nxt, buf);
-      else if (grp + (int)gridDim.x < ngroups)
-        load(grp + gridDim.x, nxt - NST, buf);
+      else if (grp + gstep < ngroups)
+        load(grp + gstep, nxt - NST, buf);
     }
     part[warp][lane] = make_float4(acc[0], acc[1], acc[2], acc[3]);
     __syncthreads();
+    bool finish = true;
+    float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
     if (warp == 0) {
-      float4 s = part[0][lane];
+      s = part[0][lane];
 #pragma unroll
       for (int w = 1; w < kWarps; ++w) {
         const float4 q = part[w][lane];
@@ -187,6 +233,31 @@ __global__ void __launch_bounds__(kThreads) gemv_batch_kernel(BatchGemvParams p)
         s.z += q.z;
         s.w += q.w;
       }
+      if constexpr (KSPLIT > 1) {  // this part's tile out; the group's last part sums them in order
+        float4* gp = p.part + (int64_t)grp * KSPLIT * 32;
+        gp[ks * 32 + lane] = s;
+        __threadfence();
+        __syncwarp();
+        unsigned tk = 0;
+        if (lane == 0) tk = atomicAdd(p.tickets + grp, 1u);
+        tk = __shfl_sync(0xffffffffu, tk, 0);
+        finish = tk == (unsigned)(KSPLIT - 1);
+        if (finish) {
+          __threadfence();
+          s = __ldcg(gp + lane);
+#pragma unroll
+          for (int k = 1; k < KSPLIT; ++k) {
+            const float4 q = __ldcg(gp + k * 32 + lane);
+            s.x += q.x;
+            s.y += q.y;
+            s.z += q.z;
+            s.w += q.w;
+          }
+          if (lane == 0) atomicExch(p.tickets + grp, 0u);
+        }
+      }
+    }
+    if (warp == 0 && finish) {
       // lane (g, t): rows g / g + 8 of the group, requests 2t / 2t + 1
       const float d[4] = {s.x, s.y, s.z, s.w};
       int64_t r0, r1;
@@ -256,15 +327,16 @@ __global__ void __launch_bounds__(kThreads) gemv_batch_kernel(BatchGemvParams p)
   }
 }
 
-template <int K, int PRO, int EPI>
+template <int K, int PRO, int EPI, int KSPLIT = 1>
 int launch(const BatchGemvParams& p, cudaStream_t s, bool pdl) {
-  constexpr size_t smem = (size_t)kBatch * xs_stride<K>() * sizeof(bf16);
+  constexpr size_t smem = (size_t)kBatch * xs_stride<K / KSPLIT>() * sizeof(bf16);
   static Q35PerDevice<int> ctas_of;
   const int ctas = ctas_of.get([] {
-    cudaFuncSetAttribute(gemv_batch_kernel<K, PRO, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaFuncSetAttribute(gemv_batch_kernel<K, PRO, EPI, KSPLIT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)smem);
     int per_sm = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemv_batch_kernel<K, PRO, EPI>, kThreads, smem) !=
-            cudaSuccess ||
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemv_batch_kernel<K, PRO, EPI, KSPLIT>, kThreads,
+                                                      smem) != cudaSuccess ||
         per_sm < 1)
       per_sm = 1;
     cudaGetLastError();
@@ -272,8 +344,10 @@ int launch(const BatchGemvParams& p, cudaStream_t s, bool pdl) {
   });
   constexpr int UNITS = (EPI == Q35_EPI_SWIGLU) ? 8 : 16;
   const int ngroups = (p.n_out + UNITS - 1) / UNITS;
-  const int grid = ngroups < ctas ? ngroups : ctas;
-  const cudaError_t e = q35_launch(gemv_batch_kernel<K, PRO, EPI>, dim3(grid), dim3(kThreads), smem, s, pdl, p);
+  const int items = ngroups * KSPLIT;
+  const int grid = items < ctas ? items : ctas / KSPLIT * KSPLIT;
+  const cudaError_t e =
+      q35_launch(gemv_batch_kernel<K, PRO, EPI, KSPLIT>, dim3(grid), dim3(kThreads), smem, s, pdl, p);
   if (e != cudaSuccess) return q35_fail(Q35_ECUDA, "batched gemv launch: %s", cudaGetErrorString(e));
   return Q35_OK;
 }
@@ -296,8 +370,16 @@ BatchGemvParams params_of(const q35_gemv_desc* d, int64_t batch) {
 
 }  // namespace
 
+// Split-K scratch of the decoder's narrow batched projections (n_out / 16 groups, 2 parts).
+size_t q35_gemv_batch_split_bytes(int64_t n_out) {
+  const size_t groups = (size_t)((n_out + 15) / 16);
+  return groups * 2 * 32 * sizeof(float4) + ((groups * sizeof(unsigned) + 255) & ~(size_t)255);
+}
+
 // The decoder's batched projections (same descriptor as the batch-1 GEMV, `batch` vectors).
-int q35_gemv_batch_launch(const q35_gemv_desc* d, int64_t batch, cudaStream_t s, bool pdl) {
+// `split_ws` (q35_gemv_batch_split_bytes(n_out), tickets zeroed once) lets the narrow plain
+// residual projections (down, out: 128 row groups for 148 SMs) split K over two CTAs.
+int q35_gemv_batch_launch(const q35_gemv_desc* d, int64_t batch, cudaStream_t s, bool pdl, void* split_ws = nullptr) {
   Q35_REQUIRE(d && d->weight, "gemv_batch: null descriptor");
   Q35_REQUIRE(batch >= 1 && batch <= kBatch, "gemv_batch: batch %lld outside [1, 8]", (long long)batch);
   Q35_REQUIRE(!d->int8, "gemv_batch: bf16 weights only (the A8W8 decode path is batch 1)");
@@ -308,15 +390,24 @@ int q35_gemv_batch_launch(const q35_gemv_desc* d, int64_t batch, cudaStream_t s,
   Q35_REQUIRE(pro == Q35_PRO_PLAIN || p.norm_w, "gemv_batch: NORM / EMBED need the norm weight");
   Q35_REQUIRE(pro != Q35_PRO_EMBED || (p.token && p.embed && p.resid), "gemv_batch: EMBED needs tokens, table, resid");
   Q35_REQUIRE(epi == Q35_EPI_RESIDUAL ? p.resid != nullptr : p.out != nullptr, "gemv_batch: missing output");
+  BatchGemvParams ps = p;
+  const bool split = split_ws && epi == Q35_EPI_RESIDUAL && pro == Q35_PRO_PLAIN && (p.n_out + 15) / 16 < kNumSMs;
+  if (split) {
+    const size_t groups = (size_t)((p.n_out + 15) / 16);
+    ps.part = static_cast<float4*>(split_ws);
+    ps.tickets = reinterpret_cast<unsigned*>(static_cast<char*>(split_ws) + groups * 2 * 32 * sizeof(float4));
+  }
   if (d->k == 2048) {
     if (epi == Q35_EPI_SWIGLU && pro == Q35_PRO_NORM) return launch<2048, Q35_PRO_NORM, Q35_EPI_SWIGLU>(p, s, pdl);
     if (epi == Q35_EPI_STORE && pro == Q35_PRO_NORM) return launch<2048, Q35_PRO_NORM, Q35_EPI_STORE>(p, s, pdl);
     if (epi == Q35_EPI_STORE && pro == Q35_PRO_EMBED) return launch<2048, Q35_PRO_EMBED, Q35_EPI_STORE>(p, s, pdl);
     if (epi == Q35_EPI_RESIDUAL && pro == Q35_PRO_PLAIN)
-      return launch<2048, Q35_PRO_PLAIN, Q35_EPI_RESIDUAL>(p, s, pdl);
+      return split ? launch<2048, Q35_PRO_PLAIN, Q35_EPI_RESIDUAL, 2>(ps, s, pdl)
+                   : launch<2048, Q35_PRO_PLAIN, Q35_EPI_RESIDUAL>(p, s, pdl);
   } else if (d->k == 6144) {
     if (epi == Q35_EPI_RESIDUAL && pro == Q35_PRO_PLAIN)
-      return launch<6144, Q35_PRO_PLAIN, Q35_EPI_RESIDUAL>(p, s, pdl);
+      return split ? launch<6144, Q35_PRO_PLAIN, Q35_EPI_RESIDUAL, 2>(ps, s, pdl)
+                   : launch<6144, Q35_PRO_PLAIN, Q35_EPI_RESIDUAL>(p, s, pdl);
   }
   return q35_fail(Q35_ENOTSUP, "gemv_batch: k=%lld with prologue %d / epilogue %d is not a decoder projection",
                   (long long)d->k, pro, epi);
