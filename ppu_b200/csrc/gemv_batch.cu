@@ -377,8 +377,10 @@ size_t q35_gemv_batch_split_bytes(int64_t n_out) {
 }
 
 // The decoder's batched projections (same descriptor as the batch-1 GEMV, `batch` vectors).
-// `split_ws` (q35_gemv_batch_split_bytes(n_out), tickets zeroed once) lets the narrow plain
-// residual projections (down, out: 128 row groups for 148 SMs) split K over two CTAs.
+// `split_ws` (q35_gemv_batch_split_bytes(n_out), tickets zeroed once) lets the down projection
+// (K = 6144, 128 row groups for 148 SMs) split K over two CTAs: batch-8 step 1.68 -> 1.20 ms.
+// Measured and not used: the out-projection (K = 2048) split as well (1.26 ms), four parts for
+// the down projection (1.30 ms).
 int q35_gemv_batch_launch(const q35_gemv_desc* d, int64_t batch, cudaStream_t s, bool pdl, void* split_ws = nullptr) {
   Q35_REQUIRE(d && d->weight, "gemv_batch: null descriptor");
   Q35_REQUIRE(batch >= 1 && batch <= kBatch, "gemv_batch: batch %lld outside [1, 8]", (long long)batch);
@@ -391,7 +393,8 @@ int q35_gemv_batch_launch(const q35_gemv_desc* d, int64_t batch, cudaStream_t s,
   Q35_REQUIRE(pro != Q35_PRO_EMBED || (p.token && p.embed && p.resid), "gemv_batch: EMBED needs tokens, table, resid");
   Q35_REQUIRE(epi == Q35_EPI_RESIDUAL ? p.resid != nullptr : p.out != nullptr, "gemv_batch: missing output");
   BatchGemvParams ps = p;
-  const bool split = split_ws && epi == Q35_EPI_RESIDUAL && pro == Q35_PRO_PLAIN && (p.n_out + 15) / 16 < kNumSMs;
+  const bool split = split_ws && epi == Q35_EPI_RESIDUAL && pro == Q35_PRO_PLAIN && (p.n_out + 15) / 16 < kNumSMs &&
+                     d->k == 6144;
   if (split) {
     const size_t groups = (size_t)((p.n_out + 15) / 16);
     ps.part = static_cast<float4*>(split_ws);
