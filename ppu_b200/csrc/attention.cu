@@ -28,6 +28,8 @@ __global__ void __launch_bounds__(kD) qgkv_rope_kernel(
     int64_t pos_base, bf16* __restrict__ q_out, bf16* __restrict__ k_out, bf16* __restrict__ v_out,
     const int64_t* __restrict__ cache_start, int L, int Hq, int Hkv, int rot, int kv_len, float eps,
     const int64_t* __restrict__ pos3 = nullptr, int sec_h = 0, int sec_w = 0) {
+  pdl_wait();  // programmatic dependent launch: inputs only after the previous kernel
+  pdl_launch_dependents();
   __shared__ float normed[kD];
   __shared__ float red[kD / 32];
   const int bt = blockIdx.x;  // b * L + t
@@ -92,6 +94,8 @@ __global__ void __launch_bounds__(2 * G * 32) prefill_attn_mma_kernel(const bf16
                                                                      const bf16* __restrict__ V, bf16* __restrict__ O,
                                                                      int Hq, int Hkv, int L, int kv_len, int q_offset,
                                                                      float scale, int kv_div) {
+  pdl_wait();  // programmatic dependent launch: inputs only after the previous kernel
+  pdl_launch_dependents();
   extern __shared__ __align__(16) unsigned char fa_smem[];
   bf16* Qs = reinterpret_cast<bf16*>(fa_smem);        // [G][16][stride]
   bf16* KVs = Qs + G * kFaRows * kFaStride;            // per key group: K [2][32][stride], V [2][32][stride]
@@ -298,7 +302,7 @@ __global__ void __launch_bounds__(2 * G * 32) prefill_attn_mma_kernel(const bf16
 template <int G>
 int launch_prefill_mma(const void* q, const void* k, const void* v, void* out, int64_t batch, int64_t q_heads,
                        int64_t kv_heads, int64_t seq_len, int64_t kv_len, int64_t q_offset, float scale,
-                       cudaStream_t stream) {
+                       cudaStream_t stream, bool pdl) {
   const int kv_div = (int)(q_heads / kv_heads / G);  // query-head groups of G per KV head
   // query tile + two key groups x two buffers x (K, V) tiles; the merge reuses the key tiles
   const size_t smem = (size_t)(G * kFaRows + 8 * kFaKeys) * kFaStride * sizeof(bf16);
@@ -306,10 +310,11 @@ int launch_prefill_mma(const void* q, const void* k, const void* v, void* out, i
                 "the merge partials fit in the key / value tiles");
   cudaFuncSetAttribute(prefill_attn_mma_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   const dim3 grid((unsigned)((seq_len + kFaRows - 1) / kFaRows), (unsigned)(kv_heads * kv_div), (unsigned)batch);
-  prefill_attn_mma_kernel<G><<<grid, 2 * G * 32, smem, stream>>>((const bf16*)q, (const bf16*)k, (const bf16*)v,
-                                                             (bf16*)out, (int)q_heads, (int)kv_heads, (int)seq_len,
-                                                             (int)kv_len, (int)q_offset, scale, kv_div);
-  return q35_check_launch("prefill_attention");
+  const cudaError_t e = q35_launch(prefill_attn_mma_kernel<G>, grid, dim3(2 * G * 32), smem, stream, pdl,
+                                   (const bf16*)q, (const bf16*)k, (const bf16*)v, (bf16*)out, (int)q_heads,
+                                   (int)kv_heads, (int)seq_len, (int)kv_len, (int)q_offset, scale, kv_div);
+  if (e != cudaSuccess) return q35_fail(Q35_ECUDA, "prefill_attention launch: %s", cudaGetErrorString(e));
+  return Q35_OK;
 }
 
 }  // namespace
@@ -341,17 +346,32 @@ int q35_qgkv_rope_positions_launch(const void* packed, const void* q_weight, con
                                    const float* inv_freq, void* q_out, void* k_out, void* v_out,
                                    const int64_t* cache_start, int64_t batch, int64_t seq_len, int64_t q_heads,
                                    int64_t kv_heads, int64_t rotary_dim, int64_t kv_len, float eps,
-                                   cudaStream_t stream, const int64_t* pos3, int sec_h, int sec_w) {
-  qgkv_rope_kernel<false><<<(unsigned)(batch * seq_len), kD, 0, stream>>>(
-      (const bf16*)packed, (const bf16*)q_weight, (const bf16*)k_weight, nullptr, nullptr, inv_freq, 0,
+                                   cudaStream_t stream, const int64_t* pos3, int sec_h, int sec_w, bool pdl) {
+  const cudaError_t e = q35_launch(
+      qgkv_rope_kernel<false>, dim3((unsigned)(batch * seq_len)), dim3(kD), 0, stream, pdl, (const bf16*)packed,
+      (const bf16*)q_weight, (const bf16*)k_weight, (const bf16*)nullptr, (const bf16*)nullptr, inv_freq, (int64_t)0,
       (bf16*)q_out, (bf16*)k_out, (bf16*)v_out, cache_start, (int)seq_len, (int)q_heads, (int)kv_heads,
       (int)rotary_dim, (int)kv_len, eps, pos3, sec_h, sec_w);
-  return q35_check_launch("qgkv_rope_positions");
+  if (e != cudaSuccess) return q35_fail(Q35_ECUDA, "qgkv_rope_positions launch: %s", cudaGetErrorString(e));
+  return Q35_OK;
 }
+
+int q35_prefill_attention_launch(const void* q, const void* k, const void* v, void* out, int64_t batch,
+                                 int64_t q_heads, int64_t kv_heads, int64_t seq_len, int64_t kv_len, int64_t q_offset,
+                                 int64_t head_dim, float scale, cudaStream_t stream, bool pdl);
 
 extern "C" int q35_prefill_attention(const void* q, const void* k, const void* v, void* out, int64_t batch,
                                      int64_t q_heads, int64_t kv_heads, int64_t seq_len, int64_t kv_len,
                                      int64_t q_offset, int64_t head_dim, float scale, void* stream) {
+  return q35_prefill_attention_launch(q, k, v, out, batch, q_heads, kv_heads, seq_len, kv_len, q_offset, head_dim,
+                                      scale, (cudaStream_t)stream, false);
+}
+
+// The causal prefill attention of the decoder (optionally chained with programmatic dependent
+// launch): the argument checks and kernel choice of q35_prefill_attention.
+int q35_prefill_attention_launch(const void* q, const void* k, const void* v, void* out, int64_t batch,
+                                 int64_t q_heads, int64_t kv_heads, int64_t seq_len, int64_t kv_len, int64_t q_offset,
+                                 int64_t head_dim, float scale, cudaStream_t stream, bool pdl) {
   Q35_REQUIRE(q && k && v && out, "prefill_attention: null pointer");
   Q35_REQUIRE(head_dim == kD, "prefill_attention: head dim must be 256");
   Q35_REQUIRE(batch >= 0 && seq_len >= 0 && kv_heads >= 1 && q_heads % kv_heads == 0 && q_offset >= 0 &&
@@ -362,11 +382,11 @@ extern "C" int q35_prefill_attention(const void* q, const void* k, const void* v
   // G / G' CTA groups of G' = 4, 2 or 1 heads (the largest that divides G), sharing the KV head
   const int64_t group = q_heads / kv_heads;
   if (group % 4 == 0)
-    return launch_prefill_mma<4>(q, k, v, out, batch, q_heads, kv_heads, seq_len, kv_len, q_offset, scale,
-                                 (cudaStream_t)stream);
+    return launch_prefill_mma<4>(q, k, v, out, batch, q_heads, kv_heads, seq_len, kv_len, q_offset, scale, stream,
+                                 pdl);
   if (group % 2 == 0)
-    return launch_prefill_mma<2>(q, k, v, out, batch, q_heads, kv_heads, seq_len, kv_len, q_offset, scale,
-                                 (cudaStream_t)stream);
-  return launch_prefill_mma<1>(q, k, v, out, batch, q_heads, kv_heads, seq_len, kv_len, q_offset, scale,
-                               (cudaStream_t)stream);
+    return launch_prefill_mma<2>(q, k, v, out, batch, q_heads, kv_heads, seq_len, kv_len, q_offset, scale, stream,
+                                 pdl);
+  return launch_prefill_mma<1>(q, k, v, out, batch, q_heads, kv_heads, seq_len, kv_len, q_offset, scale, stream,
+                               pdl);
 }

@@ -37,24 +37,33 @@ int q35_delta_decode_launch(const void* packed, const void* conv_weight, void* c
                             const void* dt_bias, const void* norm_weight, float* state, void* out, int64_t batch,
                             int64_t heads, int64_t packed_stride, float eps, cudaStream_t stream, bool pdl);
 int q35_gemm_launch(const void* a, const void* w, void* out, int64_t m, int64_t n, int64_t k, int epi, bool int8,
-                    const float* sx, const float* sw, cudaStream_t s);
+                    const float* sx, const float* sw, cudaStream_t s, bool pdl);
 int q35_gemm_tc_launch(const void* a, const void* w, void* out, int64_t m, int64_t n, int64_t k, int epi, bool int8,
-                       const float* sx, const float* sw, cudaStream_t s, const void* bias = nullptr);
+                       const float* sx, const float* sw, cudaStream_t s, const void* bias, bool pdl);
 int q35_quantize_tokens_launch(const void* x, int8_t* q, float* scale, int64_t rows, int64_t width,
-                               cudaStream_t s);
+                               cudaStream_t s, bool pdl);
+int q35_rms_norm_launch(const void* x, const void* weight, void* out, int64_t rows, int64_t width, float eps,
+                        cudaStream_t stream, bool pdl);
+int q35_embedding_launch(const int64_t* ids, const void* table, void* out, int64_t n, int64_t vocab, int64_t width,
+                         cudaStream_t stream, bool pdl);
+int q35_attention_gate_launch(const void* x, const void* packed, void* out, int64_t rows, int64_t hidden,
+                              int64_t packed_stride, int64_t head_dim, cudaStream_t stream, bool pdl);
+int q35_prefill_attention_launch(const void* q, const void* k, const void* v, void* out, int64_t batch,
+                                 int64_t q_heads, int64_t kv_heads, int64_t seq_len, int64_t kv_len, int64_t q_offset,
+                                 int64_t head_dim, float scale, cudaStream_t stream, bool pdl);
 int q35_qgkv_rope_positions_launch(const void* packed, const void* q_weight, const void* k_weight,
                                    const float* inv_freq, void* q_out, void* k_out, void* v_out,
                                    const int64_t* cache_start, int64_t batch, int64_t seq_len, int64_t q_heads,
                                    int64_t kv_heads, int64_t rotary_dim, int64_t kv_len, float eps,
-                                   cudaStream_t stream, const int64_t* pos3, int sec_h, int sec_w);
+                                   cudaStream_t stream, const int64_t* pos3, int sec_h, int sec_w, bool pdl);
 int q35_gated_rms_strided_launch(const void* x, const void* gate, int gate_group, int64_t gate_stride,
                                  const void* weight, void* out, int64_t rows, int64_t width, float eps,
-                                 cudaStream_t stream);
-int q35_set_counters_launch(int64_t* a, int64_t* b, int64_t value, cudaStream_t stream);
+                                 cudaStream_t stream, bool pdl);
+int q35_set_counters_launch(int64_t* a, int64_t* b, int64_t value, cudaStream_t stream, bool pdl);
 size_t q35_delta_chunk_workspace_bytes(int64_t batch, int64_t heads, int64_t max_len);
 int q35_delta_chunked_launch(const void* qkv, const void* packed, const void* a_log, const void* dt_bias, float* state,
                              void* out, int64_t batch, int64_t seq_len, int64_t heads, int64_t packed_stride,
-                             float* ws, cudaStream_t s, const void* conv_weight, void* conv_state);
+                             float* ws, cudaStream_t s, const void* conv_weight, void* conv_state, bool pdl);
 size_t q35_attn_decode_workspace_size(int64_t batch, int64_t q_heads, int64_t kv_heads, int64_t head_dim,
                                       int64_t cache_len);
 struct q35_pk_plan;
@@ -370,6 +379,8 @@ extern "C" int q35_decoder_finish_step(q35_decoder* dec, const int64_t* keys, in
 // Multimodal input rows: image_embeds[i] -> resid[rows[i]] (rows outside [0, L) are skipped).
 __global__ void image_rows_kernel(const bf16* __restrict__ embeds, const int64_t* __restrict__ rows,
                                   bf16* __restrict__ resid, int64_t L, int64_t width) {
+  q35::pdl_wait();  // programmatic dependent launch: inputs only after the previous kernel
+  q35::pdl_launch_dependents();
   const int64_t r = rows[blockIdx.x];
   if (r < 0 || r >= L) return;
   const uint4* src = reinterpret_cast<const uint4*>(embeds + (int64_t)blockIdx.x * width);
@@ -460,6 +471,9 @@ static int prefill_impl(q35_decoder* dec, const int64_t* ids, int64_t length, co
   const int64_t conv_dim = (int64_t)d.lin_heads * (2 * d.lin_dk + d.lin_dv);
   const int64_t vdim = (int64_t)d.lin_heads * d.lin_dv;
   const int64_t adim = (int64_t)d.q_heads * d.head_dim;
+  // Every prefill kernel waits on its predecessor (griddepcontrol.wait) before touching memory,
+  // so chaining them with programmatic dependent launch only overlaps launch and prologue.
+  const bool pdl = d.use_pdl != 0;
   dec->probe_want = 0;
 
   // Projection helper: bf16 GEMM, or per-token int8 quantisation + int8 GEMM for A8W8; tcgen05
@@ -467,9 +481,9 @@ static int prefill_impl(q35_decoder* dec, const int64_t* ids, int64_t length, co
   auto proj = [&](const bf16* x, int64_t k, const void* w, const float* sw, void* out, int64_t n, int epi) -> int {
     const bool tc = d.prefill_tc && (k * (q8 ? 1 : 2)) % 128 == 0 && n % 8 == 0;
     if (!q8)
-      return tc ? q35_gemm_tc_launch(x, w, out, R, n, k, epi, false, nullptr, nullptr, s)
-                : q35_gemm_launch(x, w, out, R, n, k, epi, false, nullptr, nullptr, s);
-    int rc = q35_quantize_tokens_launch(x, B.p_q8, B.p_sx, R, k, s);
+      return tc ? q35_gemm_tc_launch(x, w, out, R, n, k, epi, false, nullptr, nullptr, s, nullptr, pdl)
+                : q35_gemm_launch(x, w, out, R, n, k, epi, false, nullptr, nullptr, s, pdl);
+    int rc = q35_quantize_tokens_launch(x, B.p_q8, B.p_sx, R, k, s, pdl);
     if (rc) return rc;
     if (dec->probe) {  // record [codes R x k][scales R] of this projection's input
       const size_t codes = (size_t)R * k, need = codes + (size_t)R * sizeof(float);
@@ -480,8 +494,8 @@ static int prefill_impl(q35_decoder* dec, const int64_t* ids, int64_t length, co
         return q35_fail(Q35_ECUDA, "prefill: probe copy failed");
       dec->probe_want += need;
     }
-    return tc ? q35_gemm_tc_launch(B.p_q8, w, out, R, n, k, epi, true, B.p_sx, sw, s)
-              : q35_gemm_launch(B.p_q8, w, out, R, n, k, epi, true, B.p_sx, sw, s);
+    return tc ? q35_gemm_tc_launch(B.p_q8, w, out, R, n, k, epi, true, B.p_sx, sw, s, nullptr, pdl)
+              : q35_gemm_launch(B.p_q8, w, out, R, n, k, epi, true, B.p_sx, sw, s, pdl);
   };
 
   // fresh cache: zero the recurrent/conv states (the KV rows past `length` are never read)
@@ -493,52 +507,53 @@ static int prefill_impl(q35_decoder* dec, const int64_t* ids, int64_t length, co
         return q35_fail(Q35_ECUDA, "prefill: state reset failed");
     }
   }
-  Q35_TRY(q35_set_counters_launch(d.cache_len, d.rope_pos, 0, s));
-  Q35_TRY(q35_embedding(ids, d.embed, B.p_resid, R, d.vocab, H, s));
+  Q35_TRY(q35_set_counters_launch(d.cache_len, d.rope_pos, 0, s, false));
+  Q35_TRY(q35_embedding_launch(ids, d.embed, B.p_resid, R, d.vocab, H, s, pdl));
   if (mm.n_image > 0) {
-    image_rows_kernel<<<(unsigned)mm.n_image, 128, 0, s>>>((const bf16*)mm.image_embeds, mm.image_rows, B.p_resid,
-                                                         R, H);
-    Q35_TRY(q35_check_launch("prefill_mm image rows"));
+    const cudaError_t e = q35_launch(image_rows_kernel, dim3((unsigned)mm.n_image), dim3(128), 0, s, pdl,
+                                     (const bf16*)mm.image_embeds, mm.image_rows, B.p_resid, R, H);
+    if (e != cudaSuccess) return q35_fail(Q35_ECUDA, "prefill_mm image rows launch: %s", cudaGetErrorString(e));
   }
   for (int i = 0; i < d.n_layers; ++i) {
     const q35_layer_desc& L = slot_layers[i];
-    Q35_TRY(q35_rms_norm(B.p_resid, L.in_ln, B.p_norm, R, H, d.eps, s));
+    Q35_TRY(q35_rms_norm_launch(B.p_resid, L.in_ln, B.p_norm, R, H, d.eps, s, pdl));
     if (L.kind == 0) {
       Q35_TRY(proj(B.p_norm, H, L.mix_in, L.mix_in_scale, B.p_packed, d.delta_rows, Q35_EPI_STORE));
       if (d.prefill_delta == 0 && d.conv_kernel == 4 && Lt >= 4) {
         // causal conv folded into the chunk prep (reads the raw [q k v] columns of the projection)
         Q35_TRY(q35_delta_chunked_launch(nullptr, B.p_packed, L.a_log, L.dt_bias, L.rec_state, B.p_core, nseq, Lt,
-                                         d.lin_heads, d.delta_rows, B.p_chunk, s, L.conv_w, L.conv_state));
+                                         d.lin_heads, d.delta_rows, B.p_chunk, s, L.conv_w, L.conv_state, pdl));
       } else {
         Q35_TRY(q35_causal_conv1d(B.p_packed, L.conv_w, L.conv_state, B.p_conv, nseq, Lt, d.delta_rows, conv_dim,
                                   d.conv_kernel, s));
         if (d.prefill_delta == 0)
           Q35_TRY(q35_delta_chunked_launch(B.p_conv, B.p_packed, L.a_log, L.dt_bias, L.rec_state, B.p_core, nseq,
-                                           Lt, d.lin_heads, d.delta_rows, B.p_chunk, s, nullptr, nullptr));
+                                           Lt, d.lin_heads, d.delta_rows, B.p_chunk, s, nullptr, nullptr, false));
         else
           Q35_TRY(q35_delta_recurrent(B.p_conv, B.p_packed, L.a_log, L.dt_bias, L.rec_state, B.p_core, nseq, Lt,
                                       d.lin_heads, d.lin_dk, d.delta_rows, s));
       }
       Q35_TRY(q35_gated_rms_strided_launch(B.p_core, B.p_packed + conv_dim, d.lin_heads, d.delta_rows, L.gnorm,
-                                           B.p_mix, R * d.lin_heads, d.lin_dv, d.eps, s));
+                                           B.p_mix, R * d.lin_heads, d.lin_dv, d.eps, s, pdl));
       Q35_TRY(proj(B.p_mix, vdim, L.mix_out, L.mix_out_scale, B.p_resid, H, Q35_EPI_RESIDUAL));
     } else {
       Q35_TRY(proj(B.p_norm, H, L.mix_in, L.mix_in_scale, B.p_packed, qgkv_rows, Q35_EPI_STORE));
       Q35_TRY(q35_qgkv_rope_positions_launch(B.p_packed, L.q_norm, L.k_norm, d.inv_freq, B.p_core, L.k_cache,
                                              L.v_cache, nullptr, nseq, Lt, d.q_heads, d.kv_heads, d.rotary_dim,
-                                             d.max_len, d.eps, s, mm.pos3, d.mrope_section[1], d.mrope_section[2]));
-      Q35_TRY(q35_prefill_attention(B.p_core, L.k_cache, L.v_cache, B.p_attn, nseq, d.q_heads, d.kv_heads, Lt,
-                                    d.max_len, 0, d.head_dim, 1.0f / sqrtf((float)d.head_dim), s));
-      Q35_TRY(q35_attention_gate_mul(B.p_attn, B.p_packed, B.p_mix, R, adim, qgkv_rows, d.head_dim, s));
+                                             d.max_len, d.eps, s, mm.pos3, d.mrope_section[1], d.mrope_section[2],
+                                             pdl));
+      Q35_TRY(q35_prefill_attention_launch(B.p_core, L.k_cache, L.v_cache, B.p_attn, nseq, d.q_heads, d.kv_heads, Lt,
+                                           d.max_len, 0, d.head_dim, 1.0f / sqrtf((float)d.head_dim), s, pdl));
+      Q35_TRY(q35_attention_gate_launch(B.p_attn, B.p_packed, B.p_mix, R, adim, qgkv_rows, d.head_dim, s, pdl));
       Q35_TRY(proj(B.p_mix, adim, L.mix_out, L.mix_out_scale, B.p_resid, H, Q35_EPI_RESIDUAL));
     }
-    Q35_TRY(q35_rms_norm(B.p_resid, L.post_ln, B.p_norm, R, H, d.eps, s));
+    Q35_TRY(q35_rms_norm_launch(B.p_resid, L.post_ln, B.p_norm, R, H, d.eps, s, pdl));
     Q35_TRY(proj(B.p_norm, H, L.gate_up, L.gate_up_scale, B.p_act, I, Q35_EPI_SWIGLU));
     Q35_TRY(proj(B.p_act, I, L.down, L.down_scale, B.p_resid, H, Q35_EPI_RESIDUAL));
   }
   if (nseq == 1) {
     Q35_TRY(q35_lm_head_launch(B.p_resid + (Lt - 1) * H, d.final_norm, d.embed, token_out, d.vocab, H, d.eps,
-                               B.lm_ws, s, false, nullptr));
+                               B.lm_ws, s, pdl, nullptr));
   } else {  // each sequence's last row -> the decode rows, one pass over the tied table for all
     if (cudaMemcpy2DAsync(B.resid, (size_t)H * sizeof(bf16), B.p_resid + (Lt - 1) * H, (size_t)(Lt * H) * sizeof(bf16),
                           (size_t)H * sizeof(bf16), (size_t)nseq, cudaMemcpyDeviceToDevice, s) != cudaSuccess)
@@ -547,7 +562,7 @@ static int prefill_impl(q35_decoder* dec, const int64_t* ids, int64_t length, co
                                      s, false));
     Q35_TRY(q35_lm_keys_finish_launch(B.lm_keys, nseq, token_out, s, false, nullptr));
   }
-  Q35_TRY(q35_set_counters_launch(d.cache_len, d.rope_pos, Lt, s));
-  if (mm.rope_next >= 0) Q35_TRY(q35_set_counters_launch(d.rope_pos, d.rope_pos, mm.rope_next, s));
+  Q35_TRY(q35_set_counters_launch(d.cache_len, d.rope_pos, Lt, s, pdl));
+  if (mm.rope_next >= 0) Q35_TRY(q35_set_counters_launch(d.rope_pos, d.rope_pos, mm.rope_next, s, pdl));
   return Q35_OK;
 }

@@ -88,6 +88,8 @@ constexpr int kTS = 68;   // row stride (floats) of T: A-fragment loads hit dist
 // the FP32 left factor split into TF32 high + low parts against the exactly representable bf16
 // right factor (two MMAs per step, FP32-level accuracy). ~73 KB of shared memory: two CTAs per SM.
 __global__ void __launch_bounds__(kThreads, 2) delta_chunk_prep_kernel(PrepParams p) {
+  pdl_wait();  // programmatic dependent launch: inputs only after the previous kernel
+  pdl_launch_dependents();
   extern __shared__ __align__(16) unsigned char smem_raw[];
   // q, k, v tiles [kHalo + 64][136] (bf16) with row 0 of the chunk at kHalo: the halo rows hold the
   // conv's raw inputs before the chunk when the conv runs here
@@ -430,14 +432,17 @@ Q35_DEV void mma3a(Acc3& d, const uint32_t ah[4], const uint32_t al[4], const ui
 //   chunk c: S_c^T to the record (for phase C); phase 1: X = W S (64 x 16, K = 128), warp w rows
 //   16 (w & 3) .. + 16 of value columns 8 (w >> 2) .. + 8; Vn = U - X, published pre-split and as
 //   Vn^T to the record; phase 2: every warp S <- gl S + Kd^T Vn on its tile.
-// Records arrive in two cp.async groups: {W, U} for chunk n + 1 is issued once phase 1 of chunk n
-// is done, {Kd} once phase 2 is done. The output products (Qe S_c + P Vn) are phase C's.
+// The chunk records {W, U, Kd} are double-buffered: chunk n + 2's cp.async group is issued once
+// chunk n is done with its buffer, a whole chunk step ahead of its use (a record load from L2 or
+// HBM is longer than a chunk's products). The output products (Qe S_c + P Vn) are phase C's.
 __global__ void __launch_bounds__(kThreads, 1) delta_chunk_scan_kernel(ScanParams p) {
+  pdl_wait();  // programmatic dependent launch: inputs only after the previous kernel
+  pdl_launch_dependents();
   extern __shared__ __align__(16) float sm[];
-  float* W = sm;                   // [64][132]
-  float* Kd = W + kC * kPW;        // [64][136]
-  float* U = Kd + kC * kPK2;       // [64][16]
-  uint32_t* Vh = reinterpret_cast<uint32_t*>(U + kC * kVS);  // [64][24]
+  float* Wb = sm;                  // 2 x [64][132]
+  float* Kb = Wb + 2 * kC * kPW;   // 2 x [64][136]
+  float* Ub = Kb + 2 * kC * kPK2;  // 2 x [64][16]
+  uint32_t* Vh = reinterpret_cast<uint32_t*>(Ub + 2 * kC * kVS);  // [64][24]
   uint32_t* Vl = Vh + kC * kPS;    // [64][24]
   uint32_t* Sh = Vl + kC * kPS;    // [128][24]
   uint32_t* Sl = Sh + kD * kPS;    // [128][24]
@@ -466,34 +471,33 @@ __global__ void __launch_bounds__(kThreads, 1) delta_chunk_scan_kernel(ScanParam
   };
   publish_s();
   auto rec_of = [&](int ch) { return p.ws + ((size_t)(b * p.H + h) * p.NC + ch) * ChunkWs::SIZE; };
-  auto issue_g1 = [&](int ch) {  // W, U
+  auto issue = [&](int ch) {  // W, Kd, U of chunk ch into buffer ch % 2
     const float* rec = rec_of(ch);
+    float* W = Wb + (ch & 1) * kC * kPW;
+    float* Kd = Kb + (ch & 1) * kC * kPK2;
+    float* U = Ub + (ch & 1) * kC * kVS;
     for (int i = tid; i < kC * kD / 4; i += kThreads) {
       const int r = i / (kD / 4), c4 = (i % (kD / 4)) * 4;
       cp_async16(W + r * kPW + c4, rec + ChunkWs::W + r * kD + c4);
+      cp_async16(Kd + r * kPK2 + c4, rec + ChunkWs::Kd + r * kD + c4);
     }
     for (int i = tid; i < kC * kVS / 4; i += kThreads) {
       const int r = i / (kVS / 4), c4 = (i % (kVS / 4)) * 4;
       cp_async16(U + r * kVS + c4, rec + ChunkWs::U + r * kD + vs * kVS + c4);
     }
   };
-  auto issue_g2 = [&](int ch) {  // Kd
-    const float* rec = rec_of(ch);
-    for (int i = tid; i < kC * kD / 4; i += kThreads) {
-      const int r = i / (kD / 4), c4 = (i % (kD / 4)) * 4;
-      cp_async16(Kd + r * kPK2 + c4, rec + ChunkWs::Kd + r * kD + c4);
-    }
-  };
+  // one commit group per chunk (empty past the last), so chunk ch's group is complete once at
+  // most one younger group (chunk ch + 1's) is pending
   auto commit = [] { asm volatile("cp.async.commit_group;" ::: "memory"); };
-  if (p.NC > 0) {
-    issue_g1(0);
-    commit();
-    issue_g2(0);
-    commit();
-  }
+  if (p.NC > 0) issue(0);
+  commit();
+  if (p.NC > 1) issue(1);
+  commit();
   const int mt = warp & 3, nt1 = warp >> 2;  // phase-1 tile: token rows 16 mt, value columns 8 nt1
   for (int ch = 0; ch < p.NC; ++ch) {
-    const bool more = ch + 1 < p.NC;
+    const float* W = Wb + (ch & 1) * kC * kPW;
+    const float* Kd = Kb + (ch & 1) * kC * kPK2;
+    const float* U = Ub + (ch & 1) * kC * kVS;
     float* rec = const_cast<float*>(rec_of(ch));
     const float gl = rec[ChunkWs::GL];  // issued now, used in phase 2
     // S_c^T (value column, key row) for phase C, from the registers before this chunk's update
@@ -501,8 +505,8 @@ __global__ void __launch_bounds__(kThreads, 1) delta_chunk_scan_kernel(ScanParam
     for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
       for (int i = 0; i < 4; ++i) rec[ChunkWs::ST + (size_t)(vs * kVS + frag_col(nt, i)) * kD + frag_row(i)] = s[nt][i];
-    asm volatile("cp.async.wait_group 1;" ::: "memory");  // pending: G1(ch), G2(ch)
-    __syncthreads();  // W, U of this chunk and the published S are visible
+    asm volatile("cp.async.wait_group 1;" ::: "memory");  // pending: chunk ch + 1's group
+    __syncthreads();  // this chunk's records and the published S are visible
     // ---- phase 1: X = W S for token rows 16 mt .. + 16, value columns 8 nt1 .. + 8 (six chains:
     // even / odd k-step x three terms)
     float x[4];
@@ -528,10 +532,7 @@ __global__ void __launch_bounds__(kThreads, 1) delta_chunk_scan_kernel(ScanParam
       split_tf32(vn, Vh[r * kPS + col], Vl[r * kPS + col]);
       rec[ChunkWs::VT + (size_t)(vs * kVS + col) * kC + r] = vn;
     }
-    asm volatile("cp.async.wait_group 0;" ::: "memory");  // pending: G2(ch)
-    __syncthreads();  // Vn, Kd visible; W, U free
-    if (more) issue_g1(ch + 1);
-    commit();
+    __syncthreads();  // Vn visible
     // ---- phase 2: S <- gl S + Kd^T Vn on this warp's tile (rows 16 warp .. + 16)
     {
       float d[2][4];
@@ -558,9 +559,9 @@ __global__ void __launch_bounds__(kThreads, 1) delta_chunk_scan_kernel(ScanParam
 #pragma unroll
         for (int i = 0; i < 4; ++i) s[nt][i] = gl * s[nt][i] + d[nt][i];
     }
-    __syncthreads();  // phase 1 readers of Sh / Sl and phase 2 readers of Vn are done
+    __syncthreads();  // readers of Sh / Sl, Vn and this chunk's record buffer are done
     publish_s();
-    if (more) issue_g2(ch + 1);
+    if (ch + 2 < p.NC) issue(ch + 2);
     commit();
   }
 #pragma unroll
@@ -592,6 +593,8 @@ struct OutParams {
 };
 
 __global__ void __launch_bounds__(kOutThreads, 1) delta_chunk_out_kernel(OutParams p) {
+  pdl_wait();  // programmatic dependent launch: inputs only after the previous kernel
+  pdl_launch_dependents();
   extern __shared__ __align__(16) unsigned char out_smem_raw[];
   unsigned char* sm = reinterpret_cast<unsigned char*>(((uintptr_t)out_smem_raw + 1023) & ~(uintptr_t)1023);
   unsigned char* A_hi = sm;
@@ -705,7 +708,9 @@ constexpr size_t kPrepSmem =
     (size_t)3 * (kHalo + kC) * kPB * sizeof(bf16) + (size_t)(kC * kTS + 48 * 16) * sizeof(float);
 static_assert((3 * (kHalo + kC) * kPB * sizeof(bf16)) % 16 == 0, "T starts 16-byte aligned");
 static_assert((kHalo * kPB * sizeof(bf16)) % 16 == 0, "tile rows stay 16-byte aligned");
-constexpr size_t kScanSmem = (size_t)(kC * kPW + kC * kPK2 + kC * kVS + 2 * kC * kPS + 2 * kD * kPS) * sizeof(float);
+constexpr size_t kScanSmem =
+    (size_t)(2 * kC * kPW + 2 * kC * kPK2 + 2 * kC * kVS + 2 * kC * kPS + 2 * kD * kPS) * sizeof(float);
+static_assert(kScanSmem <= 227 * 1024, "scan shared memory");
 
 }  // namespace
 
@@ -719,7 +724,7 @@ size_t q35_delta_chunk_workspace_bytes(int64_t batch, int64_t heads, int64_t max
 // conv state as causal_conv1d_fused does.
 int q35_delta_chunked_launch(const void* qkv, const void* packed, const void* a_log, const void* dt_bias, float* state,
                              void* out, int64_t batch, int64_t seq_len, int64_t heads, int64_t packed_stride,
-                             float* ws, cudaStream_t s, const void* conv_weight, void* conv_state) {
+                             float* ws, cudaStream_t s, const void* conv_weight, void* conv_state, bool pdl) {
   if (batch * seq_len == 0) return Q35_OK;
   Q35_REQUIRE(conv_weight == nullptr || (conv_state != nullptr && seq_len >= 4),
               "delta_chunked: the fused conv needs a state and at least 4 tokens");
@@ -734,16 +739,18 @@ int q35_delta_chunked_launch(const void* qkv, const void* packed, const void* a_
   PrepParams pp{(const bf16*)qkv,         (const bf16*)packed,    (const bf16*)a_log, (const bf16*)dt_bias,
                 (const bf16*)conv_weight, (bf16*)conv_state,      ws,                  (int)seq_len,
                 (int)heads,               nc,                     (int)packed_stride};
-  delta_chunk_prep_kernel<<<(unsigned)(batch * heads * nc), kThreads, kPrepSmem, s>>>(pp);
-  int rc = q35_check_launch("delta_chunk_prep");
-  if (rc) return rc;
+  cudaError_t e =
+      q35_launch(delta_chunk_prep_kernel, dim3((unsigned)(batch * heads * nc)), dim3(kThreads), kPrepSmem, s, pdl, pp);
+  if (e != cudaSuccess) return q35_fail(Q35_ECUDA, "delta_chunk_prep launch: %s", cudaGetErrorString(e));
   ScanParams sp{ws, state, (int)seq_len, (int)heads, nc};
-  delta_chunk_scan_kernel<<<(unsigned)(batch * heads * (kD / kVS)), kThreads, kScanSmem, s>>>(sp);
-  rc = q35_check_launch("delta_chunk_scan");
-  if (rc) return rc;
+  e = q35_launch(delta_chunk_scan_kernel, dim3((unsigned)(batch * heads * (kD / kVS))), dim3(kThreads), kScanSmem, s,
+                 pdl, sp);
+  if (e != cudaSuccess) return q35_fail(Q35_ECUDA, "delta_chunk_scan launch: %s", cudaGetErrorString(e));
   OutParams op{ws, (bf16*)out, (int)seq_len, (int)heads, nc};
-  delta_chunk_out_kernel<<<(unsigned)(batch * heads * nc * 2), kOutThreads, kOutSmem, s>>>(op);
-  return q35_check_launch("delta_chunk_out");
+  e = q35_launch(delta_chunk_out_kernel, dim3((unsigned)(batch * heads * nc * 2)), dim3(kOutThreads), kOutSmem, s,
+                 pdl, op);
+  if (e != cudaSuccess) return q35_fail(Q35_ECUDA, "delta_chunk_out launch: %s", cudaGetErrorString(e));
+  return Q35_OK;
 }
 
 extern "C" int q35_delta_chunk_error(void) {
@@ -768,7 +775,7 @@ extern "C" int q35_delta_chunked(const void* qkv, const void* packed, const void
   Q35_REQUIRE(workspace_bytes >= q35_delta_chunk_workspace_bytes(batch, heads, seq_len),
               "delta_chunked: workspace too small");
   return q35_delta_chunked_launch(qkv, packed, a_log, dt_bias, state, out, batch, seq_len, heads, packed_stride,
-                                  static_cast<float*>(workspace), (cudaStream_t)stream, nullptr, nullptr);
+                                  static_cast<float*>(workspace), (cudaStream_t)stream, nullptr, nullptr, false);
 }
 
 extern "C" int q35_delta_chunked_conv(const void* packed, const void* conv_weight, void* conv_state, const void* a_log,
@@ -785,5 +792,6 @@ extern "C" int q35_delta_chunked_conv(const void* packed, const void* conv_weigh
   Q35_REQUIRE(workspace_bytes >= q35_delta_chunk_workspace_bytes(batch, heads, seq_len),
               "delta_chunked_conv: workspace too small");
   return q35_delta_chunked_launch(nullptr, packed, a_log, dt_bias, state, out, batch, seq_len, heads, packed_stride,
-                                  static_cast<float*>(workspace), (cudaStream_t)stream, conv_weight, conv_state);
+                                  static_cast<float*>(workspace), (cudaStream_t)stream, conv_weight, conv_state,
+                                  false);
 }

@@ -82,6 +82,8 @@ Q35_DEV int w_row_of(int n_tile0, int j, int N) {
 
 template <bool INT8, int EPI>
 __global__ void __launch_bounds__(kGemmThreads) gemm_kernel(GemmParams p) {
+  pdl_wait();  // programmatic dependent launch: inputs only after the previous kernel
+  pdl_launch_dependents();
   extern __shared__ __align__(128) unsigned char smem[];
   unsigned char* As = smem;                           // [stages][BM][kPitch]
   unsigned char* Bs = smem + kStages * BM * kPitch;   // [stages][BN][kPitch]
@@ -243,6 +245,8 @@ Q35_DEV int quant_code(float x, float s, float inv) {
 template <bool TOK>
 __global__ void __launch_bounds__(256) quant_rows_kernel(const bf16* __restrict__ x, int8_t* __restrict__ q,
                                                          float* __restrict__ scale, int width) {
+  pdl_wait();  // programmatic dependent launch: inputs only after the previous kernel
+  pdl_launch_dependents();
   __shared__ float red[8];
   const int64_t row = blockIdx.x;
   const bf16* xr = x + row * width;
@@ -260,6 +264,8 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(const bf16* __restrict_
 template <bool TOK>
 __global__ void __launch_bounds__(256) quant_rows_v8_kernel(const bf16* __restrict__ x, int8_t* __restrict__ q,
                                                             float* __restrict__ scale, int width) {
+  pdl_wait();  // programmatic dependent launch: inputs only after the previous kernel
+  pdl_launch_dependents();
   __shared__ float red[8];
   const int64_t row = blockIdx.x;
   const uint4* xr = reinterpret_cast<const uint4*>(x + row * width);
@@ -291,23 +297,24 @@ __global__ void __launch_bounds__(256) quant_rows_v8_kernel(const bf16* __restri
 size_t gemm_smem() { return (size_t)kStages * (BM + BN) * kPitch; }
 
 template <bool INT8, int EPI>
-int launch_gemm(const GemmParams& p, cudaStream_t s) {
+int launch_gemm(const GemmParams& p, cudaStream_t s, bool pdl) {
   const size_t smem = gemm_smem();
   cudaFuncSetAttribute(gemm_kernel<INT8, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   const int nw_cols = (EPI == Q35_EPI_SWIGLU) ? 2 * p.N : p.N;
   dim3 grid((unsigned)((nw_cols + BN - 1) / BN), (unsigned)((p.M + BM - 1) / BM));
-  gemm_kernel<INT8, EPI><<<grid, kGemmThreads, smem, s>>>(p);
-  return q35_check_launch("gemm");
+  const cudaError_t e = q35_launch(gemm_kernel<INT8, EPI>, grid, dim3(kGemmThreads), smem, s, pdl, p);
+  if (e != cudaSuccess) return q35_fail(Q35_ECUDA, "gemm launch: %s", cudaGetErrorString(e));
+  return Q35_OK;
 }
 
 template <bool INT8>
-int dispatch_gemm(const GemmParams& p, int epi, cudaStream_t s) {
+int dispatch_gemm(const GemmParams& p, int epi, cudaStream_t s, bool pdl) {
   switch (epi) {
-    case Q35_EPI_STORE: return launch_gemm<INT8, Q35_EPI_STORE>(p, s);
-    case Q35_EPI_RESIDUAL: return launch_gemm<INT8, Q35_EPI_RESIDUAL>(p, s);
-    case Q35_EPI_SWIGLU: return launch_gemm<INT8, Q35_EPI_SWIGLU>(p, s);
+    case Q35_EPI_STORE: return launch_gemm<INT8, Q35_EPI_STORE>(p, s, pdl);
+    case Q35_EPI_RESIDUAL: return launch_gemm<INT8, Q35_EPI_RESIDUAL>(p, s, pdl);
+    case Q35_EPI_SWIGLU: return launch_gemm<INT8, Q35_EPI_SWIGLU>(p, s, pdl);
     case EPI_RAW_I32:
-      if (INT8) return launch_gemm<true, EPI_RAW_I32>(p, s);
+      if (INT8) return launch_gemm<true, EPI_RAW_I32>(p, s, pdl);
   }
   return q35_fail(Q35_EINVAL, "gemm: bad epilogue %d", epi);
 }
@@ -315,7 +322,7 @@ int dispatch_gemm(const GemmParams& p, int epi, cudaStream_t s) {
 }  // namespace
 
 int q35_gemm_launch(const void* a, const void* w, void* out, int64_t m, int64_t n, int64_t k, int epi, bool int8,
-                    const float* sx, const float* sw, cudaStream_t s) {
+                    const float* sx, const float* sw, cudaStream_t s, bool pdl) {
   Q35_REQUIRE(a && w && out, "gemm: null pointer");
   Q35_REQUIRE(m >= 0 && n > 0 && k > 0 && (k * (int8 ? 1 : 2)) % BKB == 0,
               "gemm: bad shape m=%lld n=%lld k=%lld (k bytes must be a multiple of 64)", (long long)m, (long long)n,
@@ -334,32 +341,33 @@ int q35_gemm_launch(const void* a, const void* w, void* out, int64_t m, int64_t 
   p.M = (int)m;
   p.N = (int)n;
   p.K = (int)k;
-  return int8 ? dispatch_gemm<true>(p, epi, s) : dispatch_gemm<false>(p, epi, s);
+  return int8 ? dispatch_gemm<true>(p, epi, s, pdl) : dispatch_gemm<false>(p, epi, s, pdl);
 }
 
 template <bool TOK>
-int quantize_launch(const void* x, int8_t* q, float* scale, int64_t rows, int64_t width, cudaStream_t s) {
+int quantize_launch(const void* x, int8_t* q, float* scale, int64_t rows, int64_t width, cudaStream_t s, bool pdl) {
   if (rows == 0) return Q35_OK;
-  if (width % 8 == 0 && Q35_ALIGNED(x, 16) && Q35_ALIGNED(q, 8))
-    quant_rows_v8_kernel<TOK><<<(unsigned)rows, 256, 0, s>>>((const bf16*)x, q, scale, (int)width);
-  else
-    quant_rows_kernel<TOK><<<(unsigned)rows, 256, 0, s>>>((const bf16*)x, q, scale, (int)width);
-  return q35_check_launch(TOK ? "quantize_tokens" : "quantize_rows");
+  const bool v8 = width % 8 == 0 && Q35_ALIGNED(x, 16) && Q35_ALIGNED(q, 8);
+  const cudaError_t e = q35_launch(v8 ? quant_rows_v8_kernel<TOK> : quant_rows_kernel<TOK>, dim3((unsigned)rows),
+                                   dim3(256), 0, s, pdl, (const bf16*)x, q, scale, (int)width);
+  if (e != cudaSuccess)
+    return q35_fail(Q35_ECUDA, "%s launch: %s", TOK ? "quantize_tokens" : "quantize_rows", cudaGetErrorString(e));
+  return Q35_OK;
 }
 
 int q35_quantize_rows_launch(const void* x, int8_t* q, float* scale, int64_t rows, int64_t width, cudaStream_t s) {
-  return quantize_launch<false>(x, q, scale, rows, width, s);
+  return quantize_launch<false>(x, q, scale, rows, width, s, false);
 }
 
 int q35_quantize_tokens_launch(const void* x, int8_t* q, float* scale, int64_t rows, int64_t width,
-                               cudaStream_t s) {
-  return quantize_launch<true>(x, q, scale, rows, width, s);
+                               cudaStream_t s, bool pdl) {
+  return quantize_launch<true>(x, q, scale, rows, width, s, pdl);
 }
 
 extern "C" int q35_gemm_bf16(const void* a, const void* w, void* out, int64_t m, int64_t n, int64_t k,
                              int32_t epilogue, void* stream) {
   Q35_REQUIRE(epilogue >= Q35_EPI_STORE && epilogue <= Q35_EPI_SWIGLU, "gemm_bf16: bad epilogue");
-  return q35_gemm_launch(a, w, out, m, n, k, epilogue, false, nullptr, nullptr, (cudaStream_t)stream);
+  return q35_gemm_launch(a, w, out, m, n, k, epilogue, false, nullptr, nullptr, (cudaStream_t)stream, false);
 }
 
 extern "C" int q35_quantize_rows(const void* x, int8_t* q, float* scale, int64_t rows, int64_t width,
@@ -371,7 +379,7 @@ extern "C" int q35_quantize_rows(const void* x, int8_t* q, float* scale, int64_t
 extern "C" int q35_quantize_tokens(const void* x, int8_t* q, float* scale, int64_t rows, int64_t width,
                                    void* stream) {
   Q35_REQUIRE(x && q && scale && rows >= 0 && width > 0, "quantize_tokens: bad argument");
-  return q35_quantize_tokens_launch(x, q, scale, rows, width, (cudaStream_t)stream);
+  return q35_quantize_tokens_launch(x, q, scale, rows, width, (cudaStream_t)stream, false);
 }
 
 extern "C" size_t q35_a8w8_linear_workspace_size(int64_t m, int64_t k) {
@@ -385,12 +393,12 @@ extern "C" int q35_a8w8_linear(const void* x, const int8_t* qw, const float* w_s
   Q35_REQUIRE(workspace_bytes >= q35_a8w8_linear_workspace_size(m, k), "a8w8_linear: workspace too small");
   int8_t* qx = static_cast<int8_t*>(workspace);
   float* sx = reinterpret_cast<float*>(static_cast<char*>(workspace) + (((size_t)m * k + 255) & ~(size_t)255));
-  int rc = q35_quantize_tokens_launch(x, qx, sx, m, k, (cudaStream_t)stream);
+  int rc = q35_quantize_tokens_launch(x, qx, sx, m, k, (cudaStream_t)stream, false);
   if (rc) return rc;
-  return q35_gemm_launch(qx, qw, out, m, n, k, Q35_EPI_STORE, true, sx, w_scale, (cudaStream_t)stream);
+  return q35_gemm_launch(qx, qw, out, m, n, k, Q35_EPI_STORE, true, sx, w_scale, (cudaStream_t)stream, false);
 }
 
 extern "C" int q35_int8_gemm_i32(const int8_t* qx, const int8_t* qw, int32_t* acc, int64_t m, int64_t n, int64_t k,
                                  void* stream) {
-  return q35_gemm_launch(qx, qw, acc, m, n, k, EPI_RAW_I32, true, nullptr, nullptr, (cudaStream_t)stream);
+  return q35_gemm_launch(qx, qw, acc, m, n, k, EPI_RAW_I32, true, nullptr, nullptr, (cudaStream_t)stream, false);
 }

@@ -311,6 +311,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = *tmem_slot;
+  // programmatic dependent launch: the set-up above overlapped the previous kernel's tail; A,
+  // the residual and the outputs are touched only after it has completed
+  pdl_wait();
+  pdl_launch_dependents();
 
   if (warp == 0) {
     if (lane == 0) {
@@ -457,6 +461,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   cluster_sync_all();  // both CTAs' barriers are initialised before any cross-CTA signal
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = *tmem_slot;
+  pdl_wait();  // as in gemm_tc_kernel: inputs and outputs only after the previous kernel completed
+  pdl_launch_dependents();
 
   if (warp == 0) {
     if (lane == 0) {
@@ -565,7 +571,7 @@ bool make_map(CUtensorMap* m, const void* ptr, uint64_t rows, uint64_t k, uint32
 constexpr size_t smem_bytes(int bn) { return 1024 + (size_t)stages_for(bn) * (kABytes + (size_t)bn * BKB) + 256; }
 
 template <bool INT8, int EPI, int TBN>
-int launch_tc_bn(const void* a, const void* w, const TcParams& p, cudaStream_t s) {
+int launch_tc_bn(const void* a, const void* w, const TcParams& p, cudaStream_t s, bool pdl) {
   CUtensorMap ma, mb;
   const uint64_t wrows = (EPI == Q35_EPI_SWIGLU) ? 2 * (uint64_t)p.N : (uint64_t)p.N;
   if (!make_map(&ma, a, p.M, p.K, BM, INT8) ||
@@ -576,8 +582,10 @@ int launch_tc_bn(const void* a, const void* w, const TcParams& p, cudaStream_t s
   const int cols_per_tile = (EPI == Q35_EPI_SWIGLU) ? TBN / 2 : TBN;
   const int64_t tiles = (int64_t)((p.N + cols_per_tile - 1) / cols_per_tile) * ((p.M + BM - 1) / BM);
   const unsigned grid = (unsigned)(tiles < kNumSMs ? tiles : kNumSMs);
-  gemm_tc_kernel<INT8, EPI, TBN><<<grid, kThreads, smem_bytes(TBN), s>>>(ma, mb, p);
-  return q35_check_launch("gemm_tc");
+  const cudaError_t e = q35_launch(gemm_tc_kernel<INT8, EPI, TBN>, dim3(grid), dim3(kThreads), smem_bytes(TBN), s, pdl,
+                                   ma, mb, p);
+  if (e != cudaSuccess) return q35_fail(Q35_ECUDA, "gemm_tc launch: %s", cudaGetErrorString(e));
+  return Q35_OK;
 }
 
 int g_tc_pairs = 1;  // process-wide: CTA-pair kernel (1) or single-CTA kernel (0)
@@ -610,7 +618,7 @@ int max_active_pairs() {
 
 // Pair tiles are 256 x 256 (an N = 128 MMA runs at about half the rate of N = 256 on either kernel).
 template <bool INT8, int EPI>
-int launch_tc2(const void* a, const void* w, const TcParams& p, cudaStream_t s) {
+int launch_tc2(const void* a, const void* w, const TcParams& p, cudaStream_t s, bool pdl) {
   constexpr int TBN = 256;
   const int npairs = max_active_pairs<INT8, EPI>();
   const int cols = (EPI == Q35_EPI_SWIGLU) ? TBN / 2 : TBN;
@@ -622,8 +630,10 @@ int launch_tc2(const void* a, const void* w, const TcParams& p, cudaStream_t s) 
   const int64_t pairs = tiles < npairs ? tiles : npairs;
   cudaFuncSetAttribute(gemm_tc2_kernel<INT8, EPI, TBN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                        (int)smem_bytes_pair(TBN));
-  gemm_tc2_kernel<INT8, EPI, TBN><<<(unsigned)(2 * pairs), kThreads, smem_bytes_pair(TBN), s>>>(ma, mb, p);
-  return q35_check_launch("gemm_tc2");
+  const cudaError_t e = q35_launch(gemm_tc2_kernel<INT8, EPI, TBN>, dim3((unsigned)(2 * pairs)), dim3(kThreads),
+                                   smem_bytes_pair(TBN), s, pdl, ma, mb, p);
+  if (e != cudaSuccess) return q35_fail(Q35_ECUDA, "gemm_tc2 launch: %s", cudaGetErrorString(e));
+  return Q35_OK;
 }
 
 // Kernel and tile choice (measured at M = 1024 on B200): when single-CTA 128-column tiles fill
@@ -633,20 +643,20 @@ int launch_tc2(const void* a, const void* w, const TcParams& p, cudaStream_t s) 
 // single CTAs: 37.7 / 35.7 / 51.4). Splitting K over more pairs to fill the idle SMs (partial
 // sums through global memory, fixed-order combine) measured slower for every shape and was removed.
 template <bool INT8, int EPI>
-int launch_tc(const void* a, const void* w, const TcParams& p, cudaStream_t s) {
+int launch_tc(const void* a, const void* w, const TcParams& p, cudaStream_t s, bool pdl) {
   const int64_t mt = (p.M + BM - 1) / BM;
   const int cols128 = (EPI == Q35_EPI_SWIGLU) ? 64 : 128;
   const int64_t t128 = (int64_t)((p.N + cols128 - 1) / cols128) * mt;
-  if (t128 <= kNumSMs && mt * 2 <= t128) return launch_tc_bn<INT8, EPI, 128>(a, w, p, s);
-  if (g_tc_pairs) return launch_tc2<INT8, EPI>(a, w, p, s);
-  return launch_tc_bn<INT8, EPI, 256>(a, w, p, s);
+  if (t128 <= kNumSMs && mt * 2 <= t128) return launch_tc_bn<INT8, EPI, 128>(a, w, p, s, pdl);
+  if (g_tc_pairs) return launch_tc2<INT8, EPI>(a, w, p, s, pdl);
+  return launch_tc_bn<INT8, EPI, 256>(a, w, p, s, pdl);
 }
 
 }  // namespace
 
 // Used by the decoder prefill and q35_gemm_tc: tensor-core projection with fused epilogue.
 int q35_gemm_tc_launch(const void* a, const void* w, void* out, int64_t m, int64_t n, int64_t k, int epi, bool int8,
-                       const float* sx, const float* sw, cudaStream_t s, const void* bias = nullptr) {
+                       const float* sx, const float* sw, cudaStream_t s, const void* bias = nullptr, bool pdl = false) {
   Q35_REQUIRE(a && w && out, "gemm_tc: null pointer");
   Q35_REQUIRE(m >= 1 && n >= 1 && k >= 1 && (k * (int8 ? 1 : 2)) % BKB == 0,
               "gemm_tc: k=%lld must fill 128-byte K slabs", (long long)k);
@@ -668,18 +678,18 @@ int q35_gemm_tc_launch(const void* a, const void* w, void* out, int64_t m, int64
   p.K = (int)k;
   if (int8) {
     switch (epi) {
-      case Q35_EPI_STORE: return launch_tc<true, Q35_EPI_STORE>(a, w, p, s);
-      case Q35_EPI_RESIDUAL: return launch_tc<true, Q35_EPI_RESIDUAL>(a, w, p, s);
-      default: return launch_tc<true, Q35_EPI_SWIGLU>(a, w, p, s);
+      case Q35_EPI_STORE: return launch_tc<true, Q35_EPI_STORE>(a, w, p, s, pdl);
+      case Q35_EPI_RESIDUAL: return launch_tc<true, Q35_EPI_RESIDUAL>(a, w, p, s, pdl);
+      default: return launch_tc<true, Q35_EPI_SWIGLU>(a, w, p, s, pdl);
     }
   }
   switch (epi) {
-    case Q35_EPI_STORE: return launch_tc<false, Q35_EPI_STORE>(a, w, p, s);
-    case Q35_EPI_RESIDUAL: return launch_tc<false, Q35_EPI_RESIDUAL>(a, w, p, s);
-    case Q35_EPI_BIAS: return launch_tc<false, Q35_EPI_BIAS>(a, w, p, s);
-    case Q35_EPI_BIAS_GELU_TANH: return launch_tc<false, Q35_EPI_BIAS_GELU_TANH>(a, w, p, s);
-    case Q35_EPI_BIAS_GELU: return launch_tc<false, Q35_EPI_BIAS_GELU>(a, w, p, s);
-    default: return launch_tc<false, Q35_EPI_SWIGLU>(a, w, p, s);
+    case Q35_EPI_STORE: return launch_tc<false, Q35_EPI_STORE>(a, w, p, s, pdl);
+    case Q35_EPI_RESIDUAL: return launch_tc<false, Q35_EPI_RESIDUAL>(a, w, p, s, pdl);
+    case Q35_EPI_BIAS: return launch_tc<false, Q35_EPI_BIAS>(a, w, p, s, pdl);
+    case Q35_EPI_BIAS_GELU_TANH: return launch_tc<false, Q35_EPI_BIAS_GELU_TANH>(a, w, p, s, pdl);
+    case Q35_EPI_BIAS_GELU: return launch_tc<false, Q35_EPI_BIAS_GELU>(a, w, p, s, pdl);
+    default: return launch_tc<false, Q35_EPI_SWIGLU>(a, w, p, s, pdl);
   }
 }
 

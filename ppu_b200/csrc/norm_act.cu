@@ -20,6 +20,8 @@ __global__ void __launch_bounds__(kRowThreads) rms_rows_kernel(const bf16* __res
                                                                bf16* __restrict__ resid_out,
                                                                bf16* __restrict__ out, int width,
                                                                float eps) {
+  pdl_wait();  // programmatic dependent launch: inputs only after the previous kernel
+  pdl_launch_dependents();
   __shared__ float red[kRowThreads / 32];
   const int64_t row = blockIdx.x;
   const bf16* xr = x + row * width;
@@ -51,6 +53,8 @@ __global__ void __launch_bounds__(kRowThreads) rms_rows2048_kernel(const bf16* _
                                                                    const bf16* __restrict__ w,
                                                                    bf16* __restrict__ resid_out,
                                                                    bf16* __restrict__ out, float eps) {
+  pdl_wait();  // programmatic dependent launch: inputs only after the previous kernel
+  pdl_launch_dependents();
   constexpr int kW = 2048;
   __shared__ float red[kRowThreads / 32];
   const int64_t base = (int64_t)blockIdx.x * kW + 8 * threadIdx.x;
@@ -84,6 +88,8 @@ __global__ void __launch_bounds__(kRowThreads) rms_rows2048_kernel(const bf16* _
 __global__ void gated_rms128_kernel(const bf16* __restrict__ x, const bf16* __restrict__ gate,
                                     const bf16* __restrict__ w, bf16* __restrict__ out, int64_t rows, float eps,
                                     int gate_group, int64_t gate_stride) {
+  pdl_wait();  // programmatic dependent launch: inputs only after the previous kernel
+  pdl_launch_dependents();
   constexpr int kW = 128;
   const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
@@ -119,6 +125,8 @@ __global__ void gated_rms128_kernel(const bf16* __restrict__ x, const bf16* __re
 __global__ void gated_rms_kernel(const bf16* __restrict__ x, const bf16* __restrict__ gate,
                                  const bf16* __restrict__ w, bf16* __restrict__ out, int64_t rows,
                                  int width, float eps, int gate_group, int64_t gate_stride) {
+  pdl_wait();  // programmatic dependent launch: inputs only after the previous kernel
+  pdl_launch_dependents();
   const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
@@ -148,6 +156,8 @@ template <bool ADD, int CPL>
 __global__ void __launch_bounds__(256) rms_rows_warp_kernel(const bf16* __restrict__ x, const bf16* __restrict__ upd,
                                                             const bf16* __restrict__ w, bf16* __restrict__ resid_out,
                                                             bf16* __restrict__ out, int64_t rows, float eps) {
+  pdl_wait();  // programmatic dependent launch: inputs only after the previous kernel
+  pdl_launch_dependents();
   constexpr int W = 256 * CPL;
   const int lane = threadIdx.x & 31;
   for (int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5); row < rows; row += (int64_t)gridDim.x * 8) {
@@ -186,6 +196,8 @@ __global__ void __launch_bounds__(256) gated_rms_warp_kernel(const bf16* __restr
                                                              const bf16* __restrict__ w, bf16* __restrict__ out,
                                                              int64_t rows, float eps, int gate_group,
                                                              int64_t gate_stride) {
+  pdl_wait();  // programmatic dependent launch: inputs only after the previous kernel
+  pdl_launch_dependents();
   constexpr int W = 256 * CPL;
   const int lane = threadIdx.x & 31;
   for (int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5); row < rows; row += (int64_t)gridDim.x * 8) {
@@ -251,6 +263,8 @@ __global__ void __launch_bounds__(256) sigmoid_mul_v8_kernel(const bf16* __restr
 __global__ void __launch_bounds__(256) attn_gate_v8_kernel(const bf16* __restrict__ x, const bf16* __restrict__ packed,
                                                            bf16* __restrict__ out, int64_t rows, int hidden,
                                                            int64_t stride, int head_dim) {
+  pdl_wait();  // programmatic dependent launch: inputs only after the previous kernel
+  pdl_launch_dependents();
   const int n8 = hidden / 8;
   for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
     for (int c = threadIdx.x; c < n8; c += blockDim.x) {
@@ -287,6 +301,8 @@ __global__ void sigmoid_mul_kernel(const bf16* __restrict__ x, const bf16* __res
 __global__ void attn_gate_kernel(const bf16* __restrict__ x, const bf16* __restrict__ packed,
                                  bf16* __restrict__ out, int64_t rows, int64_t hidden,
                                  int64_t stride, int64_t head_dim) {
+  pdl_wait();  // programmatic dependent launch: inputs only after the previous kernel
+  pdl_launch_dependents();
   const int64_t total = rows * hidden;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
        i += (int64_t)gridDim.x * blockDim.x) {
@@ -299,6 +315,8 @@ __global__ void attn_gate_kernel(const bf16* __restrict__ x, const bf16* __restr
 
 __global__ void embedding_kernel(const int64_t* __restrict__ ids, const bf16* __restrict__ table,
                                  bf16* __restrict__ out, int64_t n, int64_t vocab, int64_t width) {
+  pdl_wait();  // programmatic dependent launch: inputs only after the previous kernel
+  pdl_launch_dependents();
   const int64_t row = blockIdx.x;
   if (row >= n) return;
   int64_t id = ids[row];
@@ -347,16 +365,28 @@ void launch_gated_warp(const bf16* x, const bf16* gate, const bf16* w, bf16* out
 
 }  // namespace
 
+int q35_rms_norm_launch(const void* x, const void* weight, void* out, int64_t rows, int64_t width, float eps,
+                        cudaStream_t stream, bool pdl);
+
 extern "C" int q35_rms_norm(const void* x, const void* weight, void* out, int64_t rows,
                             int64_t width, float eps, void* stream) {
+  return q35_rms_norm_launch(x, weight, out, rows, width, eps, (cudaStream_t)stream, false);
+}
+
+// q35_rms_norm, optionally chained with programmatic dependent launch (the width-2048 kernel).
+int q35_rms_norm_launch(const void* x, const void* weight, void* out, int64_t rows, int64_t width, float eps,
+                        cudaStream_t stream, bool pdl) {
   Q35_REQUIRE(x && weight && out, "rms_norm: null pointer");
   Q35_REQUIRE(rows >= 0 && width > 0 && width <= 65536, "rms_norm: bad shape rows=%lld width=%lld",
               (long long)rows, (long long)width);
   if (rows == 0) return Q35_OK;
-  if (width == 2048 && Q35_ALIGNED(x, 16) && Q35_ALIGNED(weight, 16) && Q35_ALIGNED(out, 16))
-    rms_rows2048_kernel<false><<<(unsigned)rows, kRowThreads, 0, (cudaStream_t)stream>>>(
-        (const bf16*)x, nullptr, (const bf16*)weight, nullptr, (bf16*)out, eps);
-  else if (warp_rows_ok(width) && Q35_ALIGNED(x, 16) && Q35_ALIGNED(weight, 16) && Q35_ALIGNED(out, 16))
+  if (width == 2048 && Q35_ALIGNED(x, 16) && Q35_ALIGNED(weight, 16) && Q35_ALIGNED(out, 16)) {
+    const cudaError_t e = q35_launch(rms_rows2048_kernel<false>, dim3((unsigned)rows), dim3(kRowThreads), 0, stream,
+                                     pdl, (const bf16*)x, (const bf16*)nullptr, (const bf16*)weight, (bf16*)nullptr,
+                                     (bf16*)out, eps);
+    if (e != cudaSuccess) return q35_fail(Q35_ECUDA, "rms_norm launch: %s", cudaGetErrorString(e));
+    return Q35_OK;
+  } else if (warp_rows_ok(width) && Q35_ALIGNED(x, 16) && Q35_ALIGNED(weight, 16) && Q35_ALIGNED(out, 16))
     launch_rms_warp<false>((const bf16*)x, nullptr, (const bf16*)weight, nullptr, (bf16*)out, rows, width, eps,
                            (cudaStream_t)stream);
   else
@@ -390,7 +420,7 @@ extern "C" int q35_residual_add_rms_norm(const void* residual, const void* updat
 
 int q35_gated_rms_strided_launch(const void* x, const void* gate, int gate_group, int64_t gate_stride,
                                  const void* weight, void* out, int64_t rows, int64_t width, float eps,
-                                 cudaStream_t stream);
+                                 cudaStream_t stream, bool pdl = false);
 
 extern "C" int q35_gated_rms_norm(const void* x, const void* gate, const void* weight, void* out,
                                   int64_t rows, int64_t width, float eps, void* stream) {
@@ -401,15 +431,18 @@ extern "C" int q35_gated_rms_norm(const void* x, const void* gate, const void* w
 
 int q35_gated_rms_strided_launch(const void* x, const void* gate, int gate_group, int64_t gate_stride,
                                  const void* weight, void* out, int64_t rows, int64_t width, float eps,
-                                 cudaStream_t stream) {
+                                 cudaStream_t stream, bool pdl) {
   if (rows == 0) return Q35_OK;
   const int rows_per_block = 8;
   const unsigned blocks = (unsigned)((rows + rows_per_block - 1) / rows_per_block);
   if (width == 128 && gate_stride % 4 == 0 && Q35_ALIGNED(x, 8) && Q35_ALIGNED(gate, 8) && Q35_ALIGNED(weight, 8) &&
-      Q35_ALIGNED(out, 8))
-    gated_rms128_kernel<<<blocks, 32 * rows_per_block, 0, stream>>>(
-        (const bf16*)x, (const bf16*)gate, (const bf16*)weight, (bf16*)out, rows, eps, gate_group, gate_stride);
-  else if (warp_rows_ok(width) && gate_stride % 8 == 0 && Q35_ALIGNED(x, 16) && Q35_ALIGNED(gate, 16) &&
+      Q35_ALIGNED(out, 8)) {
+    const cudaError_t e = q35_launch(gated_rms128_kernel, dim3(blocks), dim3(32 * rows_per_block), 0, stream, pdl,
+                                     (const bf16*)x, (const bf16*)gate, (const bf16*)weight, (bf16*)out, rows, eps,
+                                     gate_group, gate_stride);
+    if (e != cudaSuccess) return q35_fail(Q35_ECUDA, "gated_rms launch: %s", cudaGetErrorString(e));
+    return Q35_OK;
+  } else if (warp_rows_ok(width) && gate_stride % 8 == 0 && Q35_ALIGNED(x, 16) && Q35_ALIGNED(gate, 16) &&
            Q35_ALIGNED(weight, 16) && Q35_ALIGNED(out, 16))
     launch_gated_warp((const bf16*)x, (const bf16*)gate, (const bf16*)weight, (bf16*)out, rows, width, eps,
                       gate_group, gate_stride, stream);
@@ -421,13 +454,16 @@ int q35_gated_rms_strided_launch(const void* x, const void* gate, int gate_group
 }
 
 __global__ void set_counters_kernel(int64_t* a, int64_t* b, int64_t value) {
+  pdl_wait();  // programmatic dependent launch: inputs only after the previous kernel
+  pdl_launch_dependents();
   if (a) *a = value;
   if (b) *b = value;
 }
 
-int q35_set_counters_launch(int64_t* a, int64_t* b, int64_t value, cudaStream_t stream) {
-  set_counters_kernel<<<1, 1, 0, stream>>>(a, b, value);
-  return q35_check_launch("set_counters");
+int q35_set_counters_launch(int64_t* a, int64_t* b, int64_t value, cudaStream_t stream, bool pdl) {
+  const cudaError_t e = q35_launch(set_counters_kernel, dim3(1), dim3(1), 0, stream, pdl, a, b, value);
+  if (e != cudaSuccess) return q35_fail(Q35_ECUDA, "set_counters launch: %s", cudaGetErrorString(e));
+  return Q35_OK;
 }
 
 extern "C" int q35_silu_and_mul(const void* packed, void* out, int64_t rows, int64_t width,
@@ -456,30 +492,49 @@ extern "C" int q35_sigmoid_mul(const void* x, const void* gate, void* out, int64
   return q35_check_launch("sigmoid_mul");
 }
 
+int q35_attention_gate_launch(const void* x, const void* packed, void* out, int64_t rows, int64_t hidden,
+                              int64_t packed_stride, int64_t head_dim, cudaStream_t stream, bool pdl);
+
 extern "C" int q35_attention_gate_mul(const void* x, const void* packed, void* out, int64_t rows,
                                       int64_t hidden, int64_t packed_stride, int64_t head_dim,
                                       void* stream) {
+  return q35_attention_gate_launch(x, packed, out, rows, hidden, packed_stride, head_dim, (cudaStream_t)stream,
+                                   false);
+}
+
+// q35_attention_gate_mul, optionally chained with programmatic dependent launch (16-byte kernel).
+int q35_attention_gate_launch(const void* x, const void* packed, void* out, int64_t rows, int64_t hidden,
+                              int64_t packed_stride, int64_t head_dim, cudaStream_t stream, bool pdl) {
   Q35_REQUIRE(x && packed && out, "attention_gate_mul: null pointer");
   Q35_REQUIRE(rows >= 0 && head_dim > 0 && hidden % head_dim == 0 && packed_stride >= 2 * hidden,
               "attention_gate_mul: bad shape");
   if (rows == 0) return Q35_OK;
   if (hidden % 8 == 0 && head_dim % 8 == 0 && packed_stride % 8 == 0 && hidden <= (1 << 30) &&
-      Q35_ALIGNED(x, 16) && Q35_ALIGNED(packed, 16) && Q35_ALIGNED(out, 16))
-    attn_gate_v8_kernel<<<(unsigned)(rows < 8 * kNumSMs ? rows : 8 * kNumSMs), 256, 0, (cudaStream_t)stream>>>(
-        (const bf16*)x, (const bf16*)packed, (bf16*)out, rows, (int)hidden, packed_stride, (int)head_dim);
-  else
+      Q35_ALIGNED(x, 16) && Q35_ALIGNED(packed, 16) && Q35_ALIGNED(out, 16)) {
+    const cudaError_t e = q35_launch(attn_gate_v8_kernel, dim3((unsigned)(rows < 8 * kNumSMs ? rows : 8 * kNumSMs)),
+                                     dim3(256), 0, stream, pdl, (const bf16*)x, (const bf16*)packed, (bf16*)out, rows,
+                                     (int)hidden, packed_stride, (int)head_dim);
+    if (e != cudaSuccess) return q35_fail(Q35_ECUDA, "attention_gate launch: %s", cudaGetErrorString(e));
+    return Q35_OK;
+  } else
     attn_gate_kernel<<<grid_for(rows * hidden, 256), 256, 0, (cudaStream_t)stream>>>(
         (const bf16*)x, (const bf16*)packed, (bf16*)out, rows, hidden, packed_stride, head_dim);
   return q35_check_launch("attention_gate_mul");
 }
 
-extern "C" int q35_embedding(const int64_t* ids, const void* table, void* out, int64_t n,
-                             int64_t vocab, int64_t width, void* stream) {
+int q35_embedding_launch(const int64_t* ids, const void* table, void* out, int64_t n, int64_t vocab, int64_t width,
+                         cudaStream_t stream, bool pdl) {
   Q35_REQUIRE(ids && table && out && n >= 0 && vocab > 0 && width % 8 == 0,
               "embedding: bad argument");
   Q35_REQUIRE(Q35_ALIGNED(table, 16) && Q35_ALIGNED(out, 16), "embedding: 16-byte alignment");
   if (n == 0) return Q35_OK;
-  embedding_kernel<<<(unsigned)n, 128, 0, (cudaStream_t)stream>>>(ids, (const bf16*)table,
-                                                                 (bf16*)out, n, vocab, width);
-  return q35_check_launch("embedding");
+  const cudaError_t e = q35_launch(embedding_kernel, dim3((unsigned)n), dim3(128), 0, stream, pdl, ids,
+                                   (const bf16*)table, (bf16*)out, n, vocab, width);
+  if (e != cudaSuccess) return q35_fail(Q35_ECUDA, "embedding launch: %s", cudaGetErrorString(e));
+  return Q35_OK;
+}
+
+extern "C" int q35_embedding(const int64_t* ids, const void* table, void* out, int64_t n,
+                             int64_t vocab, int64_t width, void* stream) {
+  return q35_embedding_launch(ids, table, out, n, vocab, width, (cudaStream_t)stream, false);
 }
