@@ -28,14 +28,18 @@ constexpr int kC = 64;      // chunk length
 constexpr int kD = 128;     // key / value head dim
 constexpr int kVS = 16;     // value columns per phase-B CTA
 constexpr int kThreads = 256;
-constexpr int kPW = 132;    // padded row stride of phase-B W / Qe tiles (16-byte aligned rows)
+constexpr int kPW = 132;    // padded row stride of phase-B W tiles (16-byte aligned rows)
+constexpr int kPK2 = 136;   // row stride of Kd (read transposed as the A operand of Kd^T Vn: distinct banks)
 
 struct ChunkWs {  // per (b, h, chunk) record in the workspace, FP32
-  // prep: W, U, Qe, Kd [64][128], P [64][64], gl; recurrence: ST = S_c^T [128 value][128 key]
-  // (the state entering the chunk, transposed) and VT = Vn^T [128 value][64 token]
-  static constexpr size_t W = 0, U = W + kC * kD, Qe = U + kC * kD, Kd = Qe + kC * kD, P = Kd + kC * kD,
+  // prep: W [64][kPW] and Kd [64][kPK2] (the recurrence's shared-memory row strides, so that each
+  // arrives in one bulk copy), U [128 / kVS][64][kVS] (one recurrence CTA's value columns
+  // contiguous), Qe [64][128], P [64][64], gl; recurrence: ST = S_c^T [128 value][128 key] (the
+  // state entering the chunk, transposed) and VT = Vn^T [128 value][64 token]
+  static constexpr size_t W = 0, U = W + kC * kPW, Qe = U + kC * kD, Kd = Qe + kC * kD, P = Kd + kC * kPK2,
                           GL = P + kC * kC, ST = GL + 4, VT = ST + kD * kD, SIZE = VT + kD * kC;
 };
+static_assert(ChunkWs::U % 4 == 0 && ChunkWs::Kd % 4 == 0 && ChunkWs::P % 4 == 0, "16-byte aligned records");
 static_assert(ChunkWs::ST % 4 == 0 && ChunkWs::VT % 4 == 0 && ChunkWs::SIZE % 4 == 0, "16-byte aligned fields");
 
 struct PrepParams {
@@ -98,7 +102,7 @@ __global__ void __launch_bounds__(kThreads, 2) delta_chunk_prep_kernel(PrepParam
   bf16* vb = kb + (kHalo + kC) * kPB;
   float* T = reinterpret_cast<float*>(vb + kC * kPB);    // [64][68]  A, then T = (I - A)^-1
   float* R = T + kC * kTS;                               // [48][16]  solve scratch
-  __shared__ float c[kC], beta[kC], qs[kC], ks[kC], araw[kC], braw[kC], su[kC], sw[kC];
+  __shared__ float c[kC], beta[kC], qs[kC], ks[kC], araw[kC], braw[kC], su[kC], sw[kC], ec[kC], ed[kC];
   const int ch = blockIdx.x % p.NC;
   const int h = (blockIdx.x / p.NC) % p.H;
   const int b = blockIdx.x / (p.NC * p.H);
@@ -156,26 +160,41 @@ __global__ void __launch_bounds__(kThreads, 2) delta_chunk_prep_kernel(PrepParam
     }
     __syncthreads();  // the state copy has read the raw rows the conv overwrites
     // causal conv + SiLU down each column with a 4-tap register window, in place (output row r
-    // replaces raw row r once read); same tap order and rounding as the separate conv, zero past L
-    for (int c = tid; c < 3 * kD; c += kThreads) {
-      const int which = c / kD, cc = c % kD;
-      bf16* colp = (which == 0 ? qb : which == 1 ? kb : vb) + cc;
-      const int chn = which * H * kD + h * kD + cc;
-      float wk[4], hist[4];
+    // replaces raw row r once read); same tap order and rounding as the separate conv, zero past L.
+    // Work unit: (column, quarter of the chunk's rows), six per thread run interleaved; each unit
+    // reads its three rows of history before the barrier, so the in-place writes cannot race.
+    {
+      constexpr int kQ = 4, kRows = kC / kQ, kTasks = 3 * kD * kQ / kThreads;
+      static_assert(3 * kD * kQ == kTasks * kThreads, "whole units per thread");
+      float wk[kTasks][4], hist[kTasks][4];
+      int off[kTasks], rlim[kTasks];
 #pragma unroll
-      for (int tap = 0; tap < 4; ++tap) wk[tap] = bf2f(p.conv_w[(int64_t)chn * 4 + tap]);
+      for (int k = 0; k < kTasks; ++k) {
+        const int task = tid + k * kThreads, cidx = task % (3 * kD), qtr = task / (3 * kD);
+        const int which = cidx / kD, cc = cidx % kD;
+        off[k] = which * (int)((kHalo + kC) * kPB) + qtr * kRows * kPB + cc;  // from qb (tiles are contiguous)
+        rlim[k] = L - t0 - qtr * kRows;
+        const int chn = which * H * kD + h * kD + cc;
 #pragma unroll
-      for (int j = 0; j < kHalo; ++j) hist[j] = bf2f(colp[(j - kHalo) * kPB]);
-#pragma unroll 8
-      for (int r = 0; r < kC; ++r) {
-        hist[3] = bf2f(colp[r * kPB]);
-        float acc = 0.f;
+        for (int tap = 0; tap < 4; ++tap) wk[k][tap] = bf2f(p.conv_w[(int64_t)chn * 4 + tap]);
 #pragma unroll
-        for (int tap = 0; tap < 4; ++tap) acc += hist[tap] * wk[tap];
-        colp[r * kPB] = (t0 + r < L) ? f2bf(silu_f(rbf(acc))) : f2bf(0.f);
-        hist[0] = hist[1];
-        hist[1] = hist[2];
-        hist[2] = hist[3];
+        for (int j = 0; j < kHalo; ++j) hist[k][j] = bf2f(qb[off[k] + (j - kHalo) * kPB]);
+      }
+      __syncthreads();  // all history rows read
+#pragma unroll 2
+      for (int r = 0; r < kRows; ++r) {
+#pragma unroll
+        for (int k = 0; k < kTasks; ++k) {
+          bf16* cp = qb + off[k] + r * kPB;
+          hist[k][3] = bf2f(*cp);
+          float acc = 0.f;
+#pragma unroll
+          for (int tap = 0; tap < 4; ++tap) acc += hist[k][tap] * wk[k][tap];
+          *cp = (r < rlim[k]) ? f2bf(silu_f(rbf(acc))) : f2bf(0.f);
+          hist[k][0] = hist[k][1];
+          hist[k][1] = hist[k][2];
+          hist[k][2] = hist[k][3];
+        }
       }
     }
   } else {
@@ -200,36 +219,62 @@ __global__ void __launch_bounds__(kThreads, 2) delta_chunk_prep_kernel(PrepParam
     }
   }
   __syncthreads();
-  // ---- per-token factors (one warp per token)
-  for (int r = warp; r < kC; r += kThreads / 32) {
-    float sq = 0.f, sk = 0.f;
-    for (int e = lane; e < kD; e += 32) {
-      const float qv = bf2f(qb[r * kPB + e]), kv = bf2f(kb[r * kPB + e]);
-      sq += qv * qv;
-      sk += kv * kv;
+  // ---- per-token factors. Squared norms: warp w sums tokens 8w .. 8w + 8 (interleaved, each in
+  // the order of one warp per token: lane-strided partial sums, then the butterfly); the gates:
+  // thread r < 64 for token r
+  {
+    float sq[8], sk[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int r = warp * 8 + j;
+      float a = 0.f, bb = 0.f;
+#pragma unroll
+      for (int e = lane; e < kD; e += 32) {
+        const float qv = bf2f(qb[r * kPB + e]), kv = bf2f(kb[r * kPB + e]);
+        a += qv * qv;
+        bb += kv * kv;
+      }
+      sq[j] = a;
+      sk[j] = bb;
     }
-    sq = warp_sum(sq);
-    sk = warp_sum(sk);
-    if (lane == 0) {
-      qs[r] = rsqrt_ieee(sq + 1e-6f);
-      ks[r] = rsqrt_ieee(sk + 1e-6f);
-      const int t = t0 + r;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      sq[j] = warp_sum(sq[j]);
+      sk[j] = warp_sum(sk[j]);
+    }
+    if (lane < 8) {
+      float mq = sq[0], mk = sk[0];
+#pragma unroll
+      for (int j = 1; j < 8; ++j)
+        if (lane == j) {
+          mq = sq[j];
+          mk = sk[j];
+        }
+      qs[warp * 8 + lane] = rsqrt_ieee(mq + 1e-6f);
+      ks[warp * 8 + lane] = rsqrt_ieee(mk + 1e-6f);
+    }
+    if (tid < kC) {
+      const int t = t0 + tid;
       float gg = 0.f, bt = 0.f;
       if (t < L) {
-        const float a = araw[r] + dt_bias;
+        const float a = araw[tid] + dt_bias;
         const float sp = a > 20.0f ? a : log1pf(expf(a));
         gg = -expf(a_log) * sp;
-        bt = 1.0f / (1.0f + expf(-braw[r]));
+        bt = 1.0f / (1.0f + expf(-braw[tid]));
       }
-      c[r] = gg;
-      beta[r] = bt;
+      c[tid] = gg;
+      beta[tid] = bt;
     }
   }
   __syncthreads();
-  if (tid == 0) {  // cumulative log decay, in token order
+  if (tid == 0) {  // cumulative log decay, in token order (values in registers: one dependent add each)
+    float v[kC];
+#pragma unroll
+    for (int r = 0; r < kC; ++r) v[r] = c[r];
     float acc = 0.f;
+#pragma unroll
     for (int r = 0; r < kC; ++r) {
-      acc += c[r];
+      acc += v[r];
       c[r] = acc;
     }
   }
@@ -239,14 +284,19 @@ __global__ void __launch_bounds__(kThreads, 2) delta_chunk_prep_kernel(PrepParam
   float* out = p.ws + ((size_t)(b * H + h) * p.NC + ch) * ChunkWs::SIZE;
   const float cl = c[kC - 1];
   const float qscale = 1.0f / sqrtf((float)kD);
+  if (tid < kC) {  // the row exponentials once per token
+    ec[tid] = expf(c[tid]);
+    ed[tid] = expf(cl - c[tid]);
+  }
+  __syncthreads();
   for (int i = tid; i < kC * kD; i += kThreads) {
     const int r = i / kD, e = i % kD;
-    out[ChunkWs::Qe + i] = ((bf2f(qb[r * kPB + e]) * qs[r]) * qscale) * expf(c[r]);
-    out[ChunkWs::Kd + i] = (bf2f(kb[r * kPB + e]) * ks[r]) * expf(cl - c[r]);
+    out[ChunkWs::Qe + i] = ((bf2f(qb[r * kPB + e]) * qs[r]) * qscale) * ec[r];
+    out[ChunkWs::Kd + r * kPK2 + e] = (bf2f(kb[r * kPB + e]) * ks[r]) * ed[r];
   }
   if (tid < kC) {
     su[tid] = beta[tid];
-    sw[tid] = (beta[tid] * expf(c[tid])) * ks[tid];
+    sw[tid] = (beta[tid] * ec[tid]) * ks[tid];
   }
   if (tid == 0) out[ChunkWs::GL] = expf(cl);
   // ---- KK = k k^T and QK = q k^T (64 x 64, K = 128) on bf16 mma.sync: warp w computes rows
@@ -292,40 +342,71 @@ __global__ void __launch_bounds__(kThreads, 2) delta_chunk_prep_kernel(PrepParam
       }
   }
   __syncthreads();
-  // ---- T = (I - A)^-1 (A strictly lower): T_ij = sum_{j <= m < i} A_im T_mj with T_jj = 1.
-  // Blocked in 16 x 16 blocks: (a) the four diagonal blocks by forward substitution in parallel;
-  // (b) block rows I = 1..3 in order: R_J = sum_{J <= K < I} A_IK T_KJ, then T_IJ = T_II R_J.
+  // ---- T = (I - A)^-1 (A strictly lower), in 16 x 16 blocks. The blocks below the diagonal
+  // band are overwritten by T as it is formed, so their A values are first copied into q's tile
+  // (q is no longer read: Qe and QK are done).
+  // (a) Diagonal blocks T_II by forward substitution, one half-warp per block, lane = column:
+  //     T_rj = A_rj + sum_{j < m < r} A_rm T_mj, m ascending, the column kept in registers.
+  // (b) Off-diagonal blocks T_IJ = T_II (A_IJ T_JJ + sum_{J < K < I} A_IK T_KJ), by diagonals:
+  //     I - J = 1 (three blocks at once), 2 (two), 3 (one); each diagonal is two 16 x 16 x 16k
+  //     products (X = sum_K A_IK T_KJ into the scratch R, then T_IJ = T_II X), one output element
+  //     per thread with the reduction unrolled.
   {
     constexpr int B = 16;
-    const int blk = tid / 64, lt = tid % 64;
-    for (int r = 1; r < B; ++r) {  // (a) row r of every diagonal block
-      float nv = 0.f;
-      const int i = blk * B + r;
-      if (lt < r) {
-        const int jj = blk * B + lt;
-        float acc = T[i * kTS + jj];
-        for (int m = lt + 1; m < r; ++m) acc = fmaf(T[i * kTS + blk * B + m], T[(blk * B + m) * kTS + jj], acc);
-        nv = acc;
-      }
-      __syncthreads();
-      if (lt < r) T[i * kTS + blk * B + lt] = nv;
-      __syncthreads();
+    float* Ac = reinterpret_cast<float*>(smem_raw);  // [64][kTS]: A rows 16 .. 63, columns < the row's block
+    for (int e = tid; e < 6 * B * B; e += kThreads) {
+      const int blk = e / (B * B), r = (e / B) % B, cc = e % B;
+      const int I = blk < 1 ? 1 : blk < 3 ? 2 : 3, J = blk - (I * (I - 1)) / 2;  // (1,0) (2,0) (2,1) (3,0) (3,1) (3,2)
+      Ac[(I * B + r) * kTS + J * B + cc] = T[(I * B + r) * kTS + J * B + cc];
     }
-    for (int I = 1; I < kC / B; ++I) {
-      // (b1) R_J for J < I: element (J, r, cc), r = row in the block, cc = column in the block
-      for (int e = tid; e < I * B * B; e += kThreads) {
-        const int J = e / (B * B), r = (e / B) % B, cc = e % B;
-        const int row = I * B + r, col = J * B + cc;
-        float acc = T[row * kTS + col];  // K = J term with T_JJ's unit diagonal
-        for (int m = J * B + cc + 1; m < I * B; ++m) acc = fmaf(T[row * kTS + m], T[m * kTS + col], acc);
-        R[(J * B + r) * B + cc] = acc;
+    if (warp < 2) {
+      const int blk = warp * 2 + (lane >> 4), lt = lane & 15;
+      float* Tb = T + blk * B * kTS + blk * B;  // the block's top-left corner
+      float col[B];
+#pragma unroll
+      for (int r = 0; r < B; ++r) col[r] = 0.f;
+#pragma unroll
+      for (int r = 1; r < B; ++r) {
+        float acc = Tb[r * kTS + lt];
+#pragma unroll
+        for (int m = 1; m < r; ++m)
+          if (m > lt) acc = fmaf(Tb[r * kTS + m], col[m], acc);
+        col[r] = acc;
+      }
+#pragma unroll
+      for (int r = 1; r < B; ++r)
+        if (r > lt) Tb[r * kTS + lt] = col[r];
+    }
+    __syncthreads();  // the diagonal blocks and the copy of A are complete
+#pragma unroll 1
+    for (int dg = 1; dg < kC / B; ++dg) {
+      const int nblk = kC / B - dg;  // blocks (I, J = I - dg), I = dg .. 3
+      // X_IJ = A_IJ T_JJ + sum_{J < K < I} A_IK T_KJ = sum_{J <= K < I} A_IK T_KJ (T_JJ unit diagonal)
+      for (int e = tid; e < nblk * B * B; e += kThreads) {
+        const int q = e / (B * B), r = (e / B) % B, cc = e % B;
+        const int I = dg + q, J = q;
+        const float* arow = Ac + (I * B + r) * kTS;
+        float acc = 0.f;
+        for (int K = J; K < I; ++K) {
+#pragma unroll
+          for (int m = 0; m < B; ++m) {
+            const float tv = (K == J) ? (m == cc ? 1.f : (m > cc ? T[(K * B + m) * kTS + J * B + cc] : 0.f))
+                                      : T[(K * B + m) * kTS + J * B + cc];
+            acc = fmaf(arow[K * B + m], tv, acc);
+          }
+        }
+        R[(q * B + r) * B + cc] = acc;
       }
       __syncthreads();
-      // (b2) T_IJ = T_II R_J (T_II unit lower triangular, strictly lower part in place)
-      for (int e = tid; e < I * B * B; e += kThreads) {
-        const int J = e / (B * B), r = (e / B) % B, cc = e % B;
-        float acc = R[(J * B + r) * B + cc];
-        for (int m = 0; m < r; ++m) acc = fmaf(T[(I * B + r) * kTS + I * B + m], R[(J * B + m) * B + cc], acc);
+      // T_IJ = T_II X (T_II unit lower triangular)
+      for (int e = tid; e < nblk * B * B; e += kThreads) {
+        const int q = e / (B * B), r = (e / B) % B, cc = e % B;
+        const int I = dg + q, J = q;
+        const float* trow = T + (I * B + r) * kTS + I * B;
+        float acc = R[(q * B + r) * B + cc];
+#pragma unroll
+        for (int m = 0; m < B; ++m)
+          if (m < r) acc = fmaf(trow[m], R[(q * B + m) * B + cc], acc);
         T[(I * B + r) * kTS + J * B + cc] = acc;
       }
       __syncthreads();
@@ -371,8 +452,9 @@ __global__ void __launch_bounds__(kThreads, 2) delta_chunk_prep_kernel(PrepParam
 #pragma unroll
       for (int half = 0; half < 2; ++half) {
         const int i = 16 * mt + g + 8 * half, e = 8 * (nb + n) + 2 * cq;
-        *reinterpret_cast<float2*>(out + ChunkWs::U + i * kD + e) = make_float2(u[n][2 * half], u[n][2 * half + 1]);
-        *reinterpret_cast<float2*>(out + ChunkWs::W + i * kD + e) = make_float2(wv[n][2 * half], wv[n][2 * half + 1]);
+        *reinterpret_cast<float2*>(out + ChunkWs::U + ((e / kVS) * kC + i) * kVS + e % kVS) =
+            make_float2(u[n][2 * half], u[n][2 * half + 1]);
+        *reinterpret_cast<float2*>(out + ChunkWs::W + i * kPW + e) = make_float2(wv[n][2 * half], wv[n][2 * half + 1]);
       }
   }
 }
@@ -385,13 +467,7 @@ struct ScanParams {
 
 // ---- 3xTF32 products in the scan (m16n8k8): x = hi + lo with hi, lo TF32; hi*hi + hi*lo + lo*hi
 // keeps ~FP32 accuracy (the dropped lo*lo term is below FP32 rounding of the sum).
-Q35_DEV void cp_async16(float* dst, const float* src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
-               : "memory");
-}
-
 constexpr int kPS = 24;   // row stride (words) of the pre-split S / Vn tiles: B-fragment loads hit distinct banks
-constexpr int kPK2 = 136; // row stride of Kd (read transposed as the A operand of Kd^T Vn: distinct banks)
 
 // A fragment (16 x 8, row-major at `base` with row stride ld), split into TF32 high / low parts.
 Q35_DEV void load_a_split(const float* base, int ld, int g, int c, uint32_t hi[4], uint32_t lo[4]) {
@@ -432,9 +508,13 @@ Q35_DEV void mma3a(Acc3& d, const uint32_t ah[4], const uint32_t al[4], const ui
 //   chunk c: S_c^T to the record (for phase C); phase 1: X = W S (64 x 16, K = 128), warp w rows
 //   16 (w & 3) .. + 16 of value columns 8 (w >> 2) .. + 8; Vn = U - X, published pre-split and as
 //   Vn^T to the record; phase 2: every warp S <- gl S + Kd^T Vn on its tile.
-// The chunk records {W, U, Kd} are double-buffered: chunk n + 2's cp.async group is issued once
-// chunk n is done with its buffer, a whole chunk step ahead of its use (a record load from L2 or
-// HBM is longer than a chunk's products). The output products (Qe S_c + P Vn) are phase C's.
+// The chunk records {W, U, Kd} are double-buffered: chunk n + 2's rows are requested as bulk
+// copies on the buffer's mbarrier once chunk n is done with it, a whole chunk step ahead of their
+// use (a record load from L2 or HBM is longer than a chunk's products). The output products
+// (Qe S_c + P Vn) are phase C's.
+constexpr long long kScanWaitBudget = 2000000000LL;
+constexpr uint32_t kScanW = kC * kPW * sizeof(float), kScanK = kC * kPK2 * sizeof(float),
+                   kScanU = kC * kVS * sizeof(float), kScanRecBytes = kScanW + kScanK + kScanU;
 __global__ void __launch_bounds__(kThreads, 1) delta_chunk_scan_kernel(ScanParams p) {
   pdl_wait();  // programmatic dependent launch: inputs only after the previous kernel
   pdl_launch_dependents();
@@ -471,28 +551,29 @@ __global__ void __launch_bounds__(kThreads, 1) delta_chunk_scan_kernel(ScanParam
   };
   publish_s();
   auto rec_of = [&](int ch) { return p.ws + ((size_t)(b * p.H + h) * p.NC + ch) * ChunkWs::SIZE; };
-  auto issue = [&](int ch) {  // W, Kd, U of chunk ch into buffer ch % 2
+  __shared__ __align__(8) uint64_t rec_bar[2];
+  __shared__ int wait_failed;
+  // W, Kd and this CTA's U columns of chunk ch into buffer ch % 2: three bulk copies (the prep
+  // writes them in these shared-memory layouts), issued by thread 0 after arming the barrier
+  auto issue = [&](int ch) {
+    if (tid != 0) return;
     const float* rec = rec_of(ch);
-    float* W = Wb + (ch & 1) * kC * kPW;
-    float* Kd = Kb + (ch & 1) * kC * kPK2;
-    float* U = Ub + (ch & 1) * kC * kVS;
-    for (int i = tid; i < kC * kD / 4; i += kThreads) {
-      const int r = i / (kD / 4), c4 = (i % (kD / 4)) * 4;
-      cp_async16(W + r * kPW + c4, rec + ChunkWs::W + r * kD + c4);
-      cp_async16(Kd + r * kPK2 + c4, rec + ChunkWs::Kd + r * kD + c4);
-    }
-    for (int i = tid; i < kC * kVS / 4; i += kThreads) {
-      const int r = i / (kVS / 4), c4 = (i % (kVS / 4)) * 4;
-      cp_async16(U + r * kVS + c4, rec + ChunkWs::U + r * kD + vs * kVS + c4);
-    }
+    const int buf = ch & 1;
+    const uint32_t bar = tc::smem_u32(&rec_bar[buf]);
+    tc::mbar_expect_tx(bar, kScanRecBytes);
+    tc::bulk_g2s(tc::smem_u32(Wb + buf * kC * kPW), rec + ChunkWs::W, kScanW, bar);
+    tc::bulk_g2s(tc::smem_u32(Kb + buf * kC * kPK2), rec + ChunkWs::Kd, kScanK, bar);
+    tc::bulk_g2s(tc::smem_u32(Ub + buf * kC * kVS), rec + ChunkWs::U + vs * kC * kVS, kScanU, bar);
   };
-  // one commit group per chunk (empty past the last), so chunk ch's group is complete once at
-  // most one younger group (chunk ch + 1's) is pending
-  auto commit = [] { asm volatile("cp.async.commit_group;" ::: "memory"); };
+  if (tid == 0) {
+    tc::mbar_init(tc::smem_u32(&rec_bar[0]), 1);
+    tc::mbar_init(tc::smem_u32(&rec_bar[1]), 1);
+    wait_failed = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
   if (p.NC > 0) issue(0);
-  commit();
   if (p.NC > 1) issue(1);
-  commit();
   const int mt = warp & 3, nt1 = warp >> 2;  // phase-1 tile: token rows 16 mt, value columns 8 nt1
   for (int ch = 0; ch < p.NC; ++ch) {
     const float* W = Wb + (ch & 1) * kC * kPW;
@@ -505,8 +586,20 @@ __global__ void __launch_bounds__(kThreads, 1) delta_chunk_scan_kernel(ScanParam
     for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
       for (int i = 0; i < 4; ++i) rec[ChunkWs::ST + (size_t)(vs * kVS + frag_col(nt, i)) * kD + frag_row(i)] = s[nt][i];
-    asm volatile("cp.async.wait_group 1;" ::: "memory");  // pending: chunk ch + 1's group
-    __syncthreads();  // this chunk's records and the published S are visible
+    // this chunk's records: thread 0 waits with a budget and shares the outcome, then every
+    // thread observes the completed phase itself (instant), which orders its reads after the copies
+    const uint32_t bar = tc::smem_u32(&rec_bar[ch & 1]), parity = (uint32_t)(ch >> 1) & 1u;
+    if (tid == 0 && !tc::mbar_wait_bounded(bar, parity, kScanWaitBudget)) {
+      wait_failed = 1;
+      atomicCAS(&q35_delta_chunk_error_word, 0, 2);
+    }
+    __syncthreads();  // the published S is visible; the wait's outcome is known
+    if (wait_failed) {  // uniform: the recurrence stops and the error word is set
+      if (tid == 0 && ch + 1 < p.NC)  // the other buffer's copies, with a budget, before exiting
+        tc::mbar_wait_bounded(tc::smem_u32(&rec_bar[(ch + 1) & 1]), (uint32_t)((ch + 1) >> 1) & 1u, kScanWaitBudget);
+      return;
+    }
+    tc::mbar_wait_bounded(bar, parity, kScanWaitBudget);
     // ---- phase 1: X = W S for token rows 16 mt .. + 16, value columns 8 nt1 .. + 8 (six chains:
     // even / odd k-step x three terms)
     float x[4];
@@ -562,7 +655,6 @@ __global__ void __launch_bounds__(kThreads, 1) delta_chunk_scan_kernel(ScanParam
     __syncthreads();  // readers of Sh / Sl, Vn and this chunk's record buffer are done
     publish_s();
     if (ch + 2 < p.NC) issue(ch + 2);
-    commit();
   }
 #pragma unroll
   for (int nt = 0; nt < 2; ++nt)
@@ -708,6 +800,8 @@ constexpr size_t kPrepSmem =
     (size_t)3 * (kHalo + kC) * kPB * sizeof(bf16) + (size_t)(kC * kTS + 48 * 16) * sizeof(float);
 static_assert((3 * (kHalo + kC) * kPB * sizeof(bf16)) % 16 == 0, "T starts 16-byte aligned");
 static_assert((kHalo * kPB * sizeof(bf16)) % 16 == 0, "tile rows stay 16-byte aligned");
+static_assert((size_t)kC * kTS * sizeof(float) <= (size_t)(kHalo + kC) * kPB * sizeof(bf16),
+              "the solve's copy of A fits in q's tile");
 constexpr size_t kScanSmem =
     (size_t)(2 * kC * kPW + 2 * kC * kPK2 + 2 * kC * kVS + 2 * kC * kPS + 2 * kD * kPS) * sizeof(float);
 static_assert(kScanSmem <= 227 * 1024, "scan shared memory");

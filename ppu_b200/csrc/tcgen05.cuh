@@ -81,6 +81,19 @@ Q35_DEV bool mbar_wait_bounded(uint32_t bar, uint32_t parity, long long budget) 
   }
 }
 
+// Arrive on the mbarrier and add `bytes` to the transaction count the phase waits for.
+Q35_DEV void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+// Bulk (non-tensor) copy global -> this CTA's shared memory, completing `bytes` on the mbarrier.
+// Both addresses 16-byte aligned, `bytes` a multiple of 16.
+Q35_DEV void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "l"(src), "r"(bytes), "r"(bar)
+               : "memory");
+}
+
 // TMEM columns for one warp (the whole warp must call both).
 Q35_DEV void tmem_alloc(uint32_t* slot, uint32_t cols) {
   asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)), "r"(cols)
