@@ -668,13 +668,16 @@ __global__ void __launch_bounds__(kThreads, 1) delta_chunk_scan_kernel(ScanParam
 // in TMEM. 3xTF32: the A = [Qe | P] and B = [S_c ; Vn] operands are staged as TF32 high / low
 // parts (K-major, 128-byte swizzle) and the three products hi.hi, lo.hi and hi.lo accumulate in
 // one TMEM tile, so the result keeps FP32-level accuracy (the dropped lo.lo term is ~2^-22).
+// K runs in two halves of 96 through one 96 KB staging area (two CTAs per SM): the second half's
+// loads are in flight while the first half's MMAs run.
 constexpr int kOutThreads = 256;            // staging; warps 0-3 also read one TMEM lane quarter each
 constexpr int kOutBatch = 6;                // 16-byte loads per operand in flight per thread
 constexpr int kOutK = kD + kC;              // 192
-constexpr int kOutSlabs = kOutK / 32;       // 6 slabs of 32 tf32 (128 bytes)
+constexpr int kOutKH = kOutK / 2;           // 96: K per half
+constexpr int kOutSlabs = kOutKH / 32;      // 3 slabs of 32 tf32 (128 bytes) per half
 constexpr int kOutN = 64;                   // value columns per CTA
 constexpr uint32_t kOutSlabBytes = 64 * 128;  // 64 rows of 128 bytes (A: tokens, B: value columns)
-constexpr uint32_t kOutTile = kOutSlabs * kOutSlabBytes;  // 48 KB per operand part
+constexpr uint32_t kOutTile = kOutSlabs * kOutSlabBytes;  // 24 KB per operand part
 constexpr size_t kOutSmem = 4 * (size_t)kOutTile + 1024 + 64;
 constexpr long long kOutWaitBudget = 2000000000LL;
 
@@ -684,7 +687,7 @@ struct OutParams {
   int L, H, NC;
 };
 
-__global__ void __launch_bounds__(kOutThreads, 1) delta_chunk_out_kernel(OutParams p) {
+__global__ void __launch_bounds__(kOutThreads, 2) delta_chunk_out_kernel(OutParams p) {
   pdl_wait();  // programmatic dependent launch: inputs only after the previous kernel
   pdl_launch_dependents();
   extern __shared__ __align__(16) unsigned char out_smem_raw[];
@@ -719,38 +722,37 @@ __global__ void __launch_bounds__(kOutThreads, 1) delta_chunk_out_kernel(OutPara
     *reinterpret_cast<uint4*>(hi + off) = make_uint4(h4[0], h4[1], h4[2], h4[3]);
     *reinterpret_cast<uint4*>(lo + off) = make_uint4(l4[0], l4[1], l4[2], l4[3]);
   };
-  // batches of kOutBatch 16-byte loads per operand in flight per thread before any is used
-  constexpr int kItems = 64 * (kOutK / 4);  // 16-byte items per operand
-  static_assert(kItems % (kOutThreads * kOutBatch) == 0, "whole batches");
-  for (int i0 = 0; i0 < kItems; i0 += kOutThreads * kOutBatch) {
-    float4 a[kOutBatch], bv[kOutBatch];
+  // one batch of kOutBatch 16-byte loads per operand per thread covers a half of K
+  constexpr int kItems = 64 * (kOutKH / 4);  // 16-byte items per operand per half
+  static_assert(kItems == kOutThreads * kOutBatch, "one batch per half");
+  float4 a[kOutBatch], bv[kOutBatch];
+  auto load_half = [&](int kh) {
 #pragma unroll
     for (int u = 0; u < kOutBatch; ++u) {
-      const int i = i0 + u * kOutThreads + tid;
-      const int r = i / (kOutK / 4), k4 = (i % (kOutK / 4)) * 4;
+      const int i = u * kOutThreads + tid;
+      const int r = i / (kOutKH / 4), k4 = kh * kOutKH + (i % (kOutKH / 4)) * 4;
       const int v = half * kOutN + r;  // B row: value column
       a[u] = k4 < kD ? __ldcg(reinterpret_cast<const float4*>(rec + ChunkWs::Qe + r * kD + k4))
                      : __ldcg(reinterpret_cast<const float4*>(rec + ChunkWs::P + r * kC + (k4 - kD)));
       bv[u] = k4 < kD ? __ldcg(reinterpret_cast<const float4*>(rec + ChunkWs::ST + (size_t)v * kD + k4))
                       : __ldcg(reinterpret_cast<const float4*>(rec + ChunkWs::VT + (size_t)v * kC + (k4 - kD)));
     }
+  };
+  auto stage_half = [&]() {
 #pragma unroll
     for (int u = 0; u < kOutBatch; ++u) {
-      const int i = i0 + u * kOutThreads + tid;
-      const int r = i / (kOutK / 4), k4 = (i % (kOutK / 4)) * 4;
+      const int i = u * kOutThreads + tid;
+      const int r = i / (kOutKH / 4), k4 = (i % (kOutKH / 4)) * 4;  // K offset within the half
       stage(A_hi, A_lo, r, k4, a[u]);
       stage(B_hi, B_lo, r, k4, bv[u]);
     }
-  }
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic-proxy stores -> MMA reads
-  __syncthreads();
-  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-  const uint32_t tmem = *tmem_slot;
-  if (tid == 0) {
-    const uint32_t idesc = tc::idesc_f32acc(2, 64, kOutN);
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic-proxy stores -> MMA reads
+  };
+  const uint32_t idesc = tc::idesc_f32acc(2, 64, kOutN);
+  auto mma_half = [&](uint32_t tmem_acc, bool first) {
     const uint32_t ah = tc::smem_u32(A_hi), al = tc::smem_u32(A_lo), bh = tc::smem_u32(B_hi), bl = tc::smem_u32(B_lo);
     const uint32_t as[3] = {ah, al, ah}, bs[3] = {bh, bh, bl};  // hi.hi, lo.hi, hi.lo
-    uint32_t acc = 0;
+    uint32_t acc = first ? 0u : 1u;
 #pragma unroll
     for (int t = 0; t < 3; ++t)
 #pragma unroll
@@ -758,14 +760,28 @@ __global__ void __launch_bounds__(kOutThreads, 1) delta_chunk_out_kernel(OutPara
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {
           const uint32_t o = sl * kOutSlabBytes + kk * 32;
-          tc::mma_tf32(tmem, tc::desc_sw128(as[t] + o), tc::desc_sw128(bs[t] + o), idesc, acc);
+          tc::mma_tf32(tmem_acc, tc::desc_sw128(as[t] + o), tc::desc_sw128(bs[t] + o), idesc, acc);
           acc = 1;
         }
     tc::commit(tc::smem_u32(bar));
-  }
+  };
+  load_half(0);
+  stage_half();
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = *tmem_slot;
+  if (tid == 0) mma_half(tmem, true);
+  load_half(1);  // in flight while the first half's MMAs read the staging area
+  // every thread waits for those MMAs before overwriting their operands
+  bool ok = tc::mbar_wait_bounded(tc::smem_u32(bar), 0, kOutWaitBudget);
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  stage_half();
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  if (tid == 0) mma_half(tmem, false);
   __syncwarp();
   if (warp < 4) {  // TMEM lane quarters
-    const bool ok = tc::mbar_wait_bounded(tc::smem_u32(bar), 0, kOutWaitBudget);
+    ok = tc::mbar_wait_bounded(tc::smem_u32(bar), 1, kOutWaitBudget) && ok;
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     // M = 64: token row 16 q + i sits in TMEM lane 32 q + i (i < 16) of warp q's lane quarter
     uint32_t v0[32], v1[32];
