@@ -161,36 +161,46 @@ __global__ void __launch_bounds__(kThreads, 2) delta_chunk_prep_kernel(PrepParam
     __syncthreads();  // the state copy has read the raw rows the conv overwrites
     // causal conv + SiLU down each column with a 4-tap register window, in place (output row r
     // replaces raw row r once read); same tap order and rounding as the separate conv, zero past L.
-    // Work unit: (column, quarter of the chunk's rows), six per thread run interleaved; each unit
-    // reads its three rows of history before the barrier, so the in-place writes cannot race.
+    // Work unit: (two adjacent columns, quarter of the chunk's rows), three per thread run
+    // interleaved, the two columns on paired FP32 FMAs (each half one IEEE fma, as the scalar
+    // form); each unit reads its three rows of history before the barrier, so the in-place writes
+    // cannot race.
     {
-      constexpr int kQ = 4, kRows = kC / kQ, kTasks = 3 * kD * kQ / kThreads;
-      static_assert(3 * kD * kQ == kTasks * kThreads, "whole units per thread");
-      float wk[kTasks][4], hist[kTasks][4];
+      constexpr int kQ = 4, kRows = kC / kQ, kPairs = 3 * kD / 2, kTasks = kPairs * kQ / kThreads;
+      static_assert(kPairs * kQ == kTasks * kThreads, "whole units per thread");
+      float2 wk[kTasks][4], hist[kTasks][4];
       int off[kTasks], rlim[kTasks];
+      auto ld_pair = [&](int o) {
+        const uint32_t u = *reinterpret_cast<const uint32_t*>(qb + o);
+        return make_float2(__uint_as_float(u << 16), __uint_as_float(u & 0xffff0000u));
+      };
 #pragma unroll
       for (int k = 0; k < kTasks; ++k) {
-        const int task = tid + k * kThreads, cidx = task % (3 * kD), qtr = task / (3 * kD);
-        const int which = cidx / kD, cc = cidx % kD;
+        const int task = tid + k * kThreads, pidx = task % kPairs, qtr = task / kPairs;
+        const int which = pidx / (kD / 2), cc = (pidx % (kD / 2)) * 2;
         off[k] = which * (int)((kHalo + kC) * kPB) + qtr * kRows * kPB + cc;  // from qb (tiles are contiguous)
         rlim[k] = L - t0 - qtr * kRows;
         const int chn = which * H * kD + h * kD + cc;
 #pragma unroll
-        for (int tap = 0; tap < 4; ++tap) wk[k][tap] = bf2f(p.conv_w[(int64_t)chn * 4 + tap]);
+        for (int tap = 0; tap < 4; ++tap)
+          wk[k][tap] = make_float2(bf2f(p.conv_w[(int64_t)chn * 4 + tap]), bf2f(p.conv_w[(int64_t)(chn + 1) * 4 + tap]));
 #pragma unroll
-        for (int j = 0; j < kHalo; ++j) hist[k][j] = bf2f(qb[off[k] + (j - kHalo) * kPB]);
+        for (int j = 0; j < kHalo; ++j) hist[k][j] = ld_pair(off[k] + (j - kHalo) * kPB);
       }
       __syncthreads();  // all history rows read
 #pragma unroll 2
       for (int r = 0; r < kRows; ++r) {
 #pragma unroll
         for (int k = 0; k < kTasks; ++k) {
-          bf16* cp = qb + off[k] + r * kPB;
-          hist[k][3] = bf2f(*cp);
-          float acc = 0.f;
+          const int o = off[k] + r * kPB;
+          hist[k][3] = ld_pair(o);
+          float2 acc = make_float2(0.f, 0.f);
 #pragma unroll
-          for (int tap = 0; tap < 4; ++tap) acc += hist[k][tap] * wk[k][tap];
-          *cp = (r < rlim[k]) ? f2bf(silu_f(rbf(acc))) : f2bf(0.f);
+          for (int tap = 0; tap < 4; ++tap) acc = __ffma2_rn(hist[k][tap], wk[k][tap], acc);
+          const float2 y = __bfloat1622float2(__floats2bfloat162_rn(acc.x, acc.y));  // rbf of both
+          const __nv_bfloat162 v = (r < rlim[k]) ? __floats2bfloat162_rn(silu_f(y.x), silu_f(y.y))
+                                                 : __floats2bfloat162_rn(0.f, 0.f);
+          *reinterpret_cast<__nv_bfloat162*>(qb + o) = v;
           hist[k][0] = hist[k][1];
           hist[k][1] = hist[k][2];
           hist[k][2] = hist[k][3];
