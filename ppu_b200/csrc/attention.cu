@@ -27,7 +27,8 @@ __global__ void __launch_bounds__(kD) qgkv_rope_kernel(
     const bf16* __restrict__ cos_t, const bf16* __restrict__ sin_t, const float* __restrict__ inv_freq,
     int64_t pos_base, bf16* __restrict__ q_out, bf16* __restrict__ k_out, bf16* __restrict__ v_out,
     const int64_t* __restrict__ cache_start, int L, int Hq, int Hkv, int rot, int kv_len, float eps,
-    const int64_t* __restrict__ pos3 = nullptr, int sec_h = 0, int sec_w = 0) {
+    const int64_t* __restrict__ pos3 = nullptr, int sec_h = 0, int sec_w = 0, bf16* __restrict__ vt_out = nullptr,
+    int vt_stride = 0) {
   pdl_wait();  // programmatic dependent launch: inputs only after the previous kernel
   pdl_launch_dependents();
   __shared__ float normed[kD];
@@ -68,7 +69,10 @@ __global__ void __launch_bounds__(kD) qgkv_rope_kernel(
       const int kh = h - Hq;
       const int64_t o = (((int64_t)b * Hkv + kh) * kv_len + start + t) * kD + d;
       k_out[o] = f2bf(y);
-      v_out[o] = row[2 * Hq * kD + Hkv * kD + kh * kD + d];
+      const bf16 vv = row[2 * Hq * kD + Hkv * kD + kh * kD + d];
+      v_out[o] = vv;
+      // V^T [b][kv head][dim][key] for the tcgen05 prefill attention (its K-major B operand)
+      if (vt_out != nullptr && start + t < vt_stride) vt_out[(((int64_t)b * Hkv + kh) * kD + d) * vt_stride + start + t] = vv;
     }
     __syncthreads();
   }
@@ -341,17 +345,19 @@ extern "C" int q35_qgkv_norm_rope(const void* packed, const void* q_weight, cons
 
 // Prefill variant used by the decoder: RoPE from positions cache_start + t (text tokens).
 // With pos3 (int64 [3, batch, seq_len]), the positions are 3-axis M-RoPE positions interleaved
-// by (sec_h, sec_w) frequency pairs (Transformers apply_interleaved_mrope).
+// by (sec_h, sec_w) frequency pairs (Transformers apply_interleaved_mrope). With vt_out, V is also
+// written transposed: vt_out [batch, kv_heads, 256, vt_stride].
 int q35_qgkv_rope_positions_launch(const void* packed, const void* q_weight, const void* k_weight,
                                    const float* inv_freq, void* q_out, void* k_out, void* v_out,
                                    const int64_t* cache_start, int64_t batch, int64_t seq_len, int64_t q_heads,
                                    int64_t kv_heads, int64_t rotary_dim, int64_t kv_len, float eps,
-                                   cudaStream_t stream, const int64_t* pos3, int sec_h, int sec_w, bool pdl) {
+                                   cudaStream_t stream, const int64_t* pos3, int sec_h, int sec_w, bool pdl,
+                                   void* vt_out, int64_t vt_stride) {
   const cudaError_t e = q35_launch(
       qgkv_rope_kernel<false>, dim3((unsigned)(batch * seq_len)), dim3(kD), 0, stream, pdl, (const bf16*)packed,
       (const bf16*)q_weight, (const bf16*)k_weight, (const bf16*)nullptr, (const bf16*)nullptr, inv_freq, (int64_t)0,
       (bf16*)q_out, (bf16*)k_out, (bf16*)v_out, cache_start, (int)seq_len, (int)q_heads, (int)kv_heads,
-      (int)rotary_dim, (int)kv_len, eps, pos3, sec_h, sec_w);
+      (int)rotary_dim, (int)kv_len, eps, pos3, sec_h, sec_w, (bf16*)vt_out, (int)vt_stride);
   if (e != cudaSuccess) return q35_fail(Q35_ECUDA, "qgkv_rope_positions launch: %s", cudaGetErrorString(e));
   return Q35_OK;
 }

@@ -55,7 +55,11 @@ int q35_qgkv_rope_positions_launch(const void* packed, const void* q_weight, con
                                    const float* inv_freq, void* q_out, void* k_out, void* v_out,
                                    const int64_t* cache_start, int64_t batch, int64_t seq_len, int64_t q_heads,
                                    int64_t kv_heads, int64_t rotary_dim, int64_t kv_len, float eps,
-                                   cudaStream_t stream, const int64_t* pos3, int sec_h, int sec_w, bool pdl);
+                                   cudaStream_t stream, const int64_t* pos3, int sec_h, int sec_w, bool pdl,
+                                   void* vt_out, int64_t vt_stride);
+int q35_prefill_attention_tc_launch(const void* q, const void* k, const void* vt, void* out, int64_t batch,
+                                    int64_t q_heads, int64_t kv_heads, int64_t seq_len, int64_t kv_len,
+                                    int64_t vt_stride, float scale, cudaStream_t stream, bool pdl);
 int q35_gated_rms_strided_launch(const void* x, const void* gate, int gate_group, int64_t gate_stride,
                                  const void* weight, void* out, int64_t rows, int64_t width, float eps,
                                  cudaStream_t stream, bool pdl);
@@ -114,6 +118,8 @@ struct Buffers {
   int8_t* p_q8;       // [L, max(H, I, mix width)]
   float* p_sx;        // [L]
   float* p_chunk;     // chunked DeltaNet factors for one layer
+  bf16* p_vt;         // V^T [seq][kv heads][head dim][keys padded to 64] (tcgen05 prefill attention;
+                      // the workspace starts zeroed, so padding columns are finite)
 };
 
 Buffers carve(const q35_decoder_desc& d, void* base, size_t* total) {
@@ -152,6 +158,7 @@ Buffers carve(const q35_decoder_desc& d, void* base, size_t* total) {
   b.p_sx = c.take<float>(L);
   // batched prefill: up to `nb` sequences sharing the L rows, each padded to whole chunks
   b.p_chunk = c.take<float>(q35_delta_chunk_workspace_bytes(1, d.lin_heads, L + 64 * nb) / sizeof(float));
+  b.p_vt = c.take<bf16>((size_t)d.kv_heads * d.head_dim * (L + 64 * nb));
   *total = c.off + 256;
   return b;
 }
@@ -538,12 +545,21 @@ static int prefill_impl(q35_decoder* dec, const int64_t* ids, int64_t length, co
       Q35_TRY(proj(B.p_mix, vdim, L.mix_out, L.mix_out_scale, B.p_resid, H, Q35_EPI_RESIDUAL));
     } else {
       Q35_TRY(proj(B.p_norm, H, L.mix_in, L.mix_in_scale, B.p_packed, qgkv_rows, Q35_EPI_STORE));
+      // tcgen05 attention (4 query heads per KV head, head dim 256) reads V transposed, written by
+      // the norm + RoPE kernel beside the cache rows; else the warp-MMA kernel reads the cache
+      const bool tc_attn = d.prefill_tc && d.q_heads == 4 * d.kv_heads && d.head_dim == 256;
+      const int64_t vt_stride = (Lt + 63) / 64 * 64;
+      const float scale = 1.0f / sqrtf((float)d.head_dim);
       Q35_TRY(q35_qgkv_rope_positions_launch(B.p_packed, L.q_norm, L.k_norm, d.inv_freq, B.p_core, L.k_cache,
                                              L.v_cache, nullptr, nseq, Lt, d.q_heads, d.kv_heads, d.rotary_dim,
                                              d.max_len, d.eps, s, mm.pos3, d.mrope_section[1], d.mrope_section[2],
-                                             pdl));
-      Q35_TRY(q35_prefill_attention_launch(B.p_core, L.k_cache, L.v_cache, B.p_attn, nseq, d.q_heads, d.kv_heads, Lt,
-                                           d.max_len, 0, d.head_dim, 1.0f / sqrtf((float)d.head_dim), s, pdl));
+                                             pdl, tc_attn ? B.p_vt : nullptr, vt_stride));
+      if (tc_attn)
+        Q35_TRY(q35_prefill_attention_tc_launch(B.p_core, L.k_cache, B.p_vt, B.p_attn, nseq, d.q_heads, d.kv_heads, Lt,
+                                                d.max_len, vt_stride, scale, s, pdl));
+      else
+        Q35_TRY(q35_prefill_attention_launch(B.p_core, L.k_cache, L.v_cache, B.p_attn, nseq, d.q_heads, d.kv_heads,
+                                             Lt, d.max_len, 0, d.head_dim, scale, s, pdl));
       Q35_TRY(q35_attention_gate_launch(B.p_attn, B.p_packed, B.p_mix, R, adim, qgkv_rows, d.head_dim, s, pdl));
       Q35_TRY(proj(B.p_mix, adim, L.mix_out, L.mix_out_scale, B.p_resid, H, Q35_EPI_RESIDUAL));
     }

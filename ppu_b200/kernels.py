@@ -190,11 +190,13 @@ def gemm_a8w8_tc(qa, sx, qw, sw, *, epilogue=L.EPI_STORE, out=None) -> torch.Ten
 
 def tc_error() -> int:
     """Error word of the tensor-core kernels (0 = every bounded wait completed): the projection
-    GEMMs' code, or 0x100 when the chunked DeltaNet output kernel's wait gave up."""
+    GEMMs' code, | 0x100 when a chunked DeltaNet kernel's wait gave up, | 0x200 when the tcgen05
+    prefill attention's did."""
     lib = L.load()
     gemm = int(lib.q35_tc_error())
     delta = int(lib.q35_delta_chunk_error())
-    return gemm | (0x100 if delta else 0)
+    attn = int(lib.q35_prefill_attention_tc_error())
+    return gemm | (0x100 if delta else 0) | (0x200 if attn else 0)
 
 
 def set_gemm_tc_pairs(on: bool) -> None:
@@ -342,6 +344,20 @@ def prefill_attention(q, k, v, scale: float, q_offset: int = 0) -> torch.Tensor:
     out = torch.empty((b, length, hq * dim), device=q.device, dtype=BF16)
     L.call("q35_prefill_attention", L.ptr(q), L.ptr(k), L.ptr(v), L.ptr(out), b, hq, k.shape[1], length,
            k.shape[2], q_offset, dim, scale, _s(q))
+    return out
+
+
+def prefill_attention_tc(q, k, v, scale: float, kv_len: int | None = None) -> torch.Tensor:
+    """The decoder's tcgen05 causal attention: ``q [B,Hq,L,256]`` (Hq = 4 Hkv) over the first L
+    rows of ``k/v [B,Hkv,S,256]`` (queries at rows 0 .. L-1) -> ``[B, L, Hq*256]``. V is passed to
+    the kernel transposed, padded with zeros to a multiple of 64 keys, as the decoder writes it."""
+    b, hq, length, dim = q.shape
+    stride = (length + 63) // 64 * 64
+    vt = torch.zeros((b, v.shape[1], dim, stride), device=v.device, dtype=BF16)
+    vt[..., :length] = v[:, :, :length].transpose(-1, -2)
+    out = torch.empty((b, length, hq * dim), device=q.device, dtype=BF16)
+    L.call("q35_prefill_attention_tc", L.ptr(q), L.ptr(k), L.ptr(vt), L.ptr(out), b, hq, k.shape[1], length,
+           k.shape[2] if kv_len is None else kv_len, stride, scale, _s(q))
     return out
 
 

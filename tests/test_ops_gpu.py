@@ -355,6 +355,23 @@ def test_prefill_attention_group_sizes(hq, hkv, length, kv_extra):
     assert rel_err(out, O.causal_attention(q, k, v, 0.0625, q_offset=kv_extra)) < 1e-2
 
 
+# the decoder's tcgen05 attention (4 query heads per KV head): ragged lengths around the 32-query
+# blocks and 64-key tiles, batch 2, cache rows past L holding other values (masked), full 1024
+@pytest.mark.parametrize("batch,length,extra", [(1, 1, 0), (1, 17, 5), (2, 64, 64), (1, 100, 28), (2, 333, 3),
+                                                (1, 1024, 0)])
+def test_prefill_attention_tc(batch, length, extra):
+    q = randn(batch, 8, length, 256, seed=length)
+    k = randn(batch, 2, length + extra, 256, seed=length + 1)
+    v = randn(batch, 2, length + extra, 256, seed=length + 2)
+    out = K.prefill_attention_tc(cu(q), cu(k), cu(v), 0.0625)
+    assert K.tc_error() == 0
+    want = O.causal_attention(q, k[:, :, :length], v[:, :, :length], 0.0625)
+    err = rel_err(out, want)
+    assert err < 3e-3, err  # probabilities kept to ~16 bits, as the warp-MMA kernel
+    ref = K.prefill_attention(cu(q), cu(k[:, :, :length].contiguous()), cu(v[:, :, :length].contiguous()), 0.0625)
+    assert rel_err(out, ref.cpu()) < 3e-3
+
+
 # ------------------------------------------------------------------ DeltaNet
 def _delta_inputs(L_, seed=0):
     """16 heads x 128, conv K=4, alpha = exp(-softplus(N(0,1))),
