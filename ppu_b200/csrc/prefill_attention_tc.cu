@@ -19,8 +19,11 @@
 //                        load / store of the row) when a warp's reference maximum moved
 // V is read transposed (V^T [dim][key], written by the Q/K-norm + RoPE kernel next to the cache
 // rows) so that both MMA operands are K-major with the 128-byte swizzle. Operands arrive by
-// cp.async: Q once, K and V^T double-buffered a tile ahead. One thread issues the MMAs; every wait
-// on an mbarrier is bounded and a timeout sets q35_attn_tc_error_word.
+// cp.async: Q once, K and V^T double-buffered a tile ahead. Warps 0-7 load and run the softmax; a
+// ninth warp only issues the MMAs (an issuing thread stalls about as long as its MMAs run, which
+// would hold back its own softmax row), handed off through two mbarriers the 256 softmax threads
+// arrive on (operands ready for S, for P.V). Every wait is bounded; a timeout sets
+// q35_attn_tc_error_word.
 #include <cfloat>
 
 #include "common.cuh"
@@ -37,7 +40,8 @@ constexpr int kAG = 4;           // query heads stacked per KV head
 constexpr int kAQ = 32;          // queries per head in a tile
 constexpr int kAM = kAG * kAQ;   // 128 MMA rows
 constexpr int kAK = 64;          // keys per tile
-constexpr int kAThreads = 256;   // two threads per row r = tid % 128 (TMEM lane r): key / O column halves
+constexpr int kASoft = 256;      // softmax threads: two per row r = tid % 128 (TMEM lane r), key / O column halves
+constexpr int kAThreads = kASoft + 32;  // + the MMA warp
 constexpr uint32_t kQBytes = 4 * kAM * 128;  // Q: 4 slabs (64 dims) x 128 rows x 128 B
 constexpr uint32_t kKBytes = 4 * kAK * 128;  // K tile: 4 slabs x 64 keys x 128 B
 constexpr uint32_t kVBytes = kAD * 128;      // V^T tile: 256 dim rows x 64 keys (128 B)
@@ -79,8 +83,8 @@ __global__ void __launch_bounds__(kAThreads, 1) prefill_attn_tc_kernel(AttnTcPar
   extern __shared__ __align__(16) unsigned char attn_smem_raw[];
   unsigned char* sm = reinterpret_cast<unsigned char*>(((uintptr_t)attn_smem_raw + 1023) & ~(uintptr_t)1023);
   const uint32_t sQ = tc::smem_u32(sm), sK = sQ + kOffK, sV = sQ + kOffV, sP = sQ + kOffP;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + kOffBar);  // S[0], S[1], PV
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + kOffBar);  // S[0], S[1], PV, ready-S, ready-PV
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 5);
   const int qb = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5;
   const int q0 = qb * kAQ;
@@ -90,16 +94,19 @@ __global__ void __launch_bounds__(kAThreads, 1) prefill_attn_tc_kernel(AttnTcPar
   const bf16* kbase = p.k + ((int64_t)b * p.Hkv + g) * p.kv_len * kAD;
   const bf16* vbase = p.vt + ((int64_t)b * p.Hkv + g) * kAD * p.vt_stride;
 
-  if (warp == 0) tc::tmem_alloc(tmem_slot, kTmemCols);
+  const bool mma_warp = warp == kASoft / 32;
+  if (mma_warp) tc::tmem_alloc(tmem_slot, kTmemCols);
   if (tid == 0) {
 #pragma unroll
     for (int i = 0; i < 3; ++i) tc::mbar_init(tc::smem_u32(&bars[i]), 1);
+    tc::mbar_init(tc::smem_u32(&bars[3]), kASoft);
+    tc::mbar_init(tc::smem_u32(&bars[4]), kASoft);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
 
   // ---- operand loads (every thread): 16-byte chunks into their 128-byte-swizzled positions
   auto load_q = [&]() {  // 128 rows x 32 chunks
-    for (int i = tid; i < kAM * (kAD / 8); i += kAThreads) {
+    for (int i = tid; i < kAM * (kAD / 8); i += kASoft) {
       const int r = i >> 5, c = i & 31;
       const int qi = q0 + (r & (kAQ - 1)), hh = g * kAG + (r >> 5);
       const bool ok = qi < L;
@@ -108,7 +115,7 @@ __global__ void __launch_bounds__(kAThreads, 1) prefill_attn_tc_kernel(AttnTcPar
     }
   };
   auto load_k = [&](int t, int buf) {  // 64 keys x 32 chunks
-    for (int i = tid; i < kAK * (kAD / 8); i += kAThreads) {
+    for (int i = tid; i < kAK * (kAD / 8); i += kASoft) {
       const int r = i >> 5, c = i & 31, key = t * kAK + r;
       const bool ok = key < p.kv_len;
       const bf16* src = kbase + (int64_t)(ok ? key : 0) * kAD + c * 8;
@@ -116,7 +123,7 @@ __global__ void __launch_bounds__(kAThreads, 1) prefill_attn_tc_kernel(AttnTcPar
     }
   };
   auto load_v = [&](int t, int buf) {  // 256 dim rows x 8 chunks of 8 keys
-    for (int i = tid; i < kAD * (kAK / 8); i += kAThreads) {
+    for (int i = tid; i < kAD * (kAK / 8); i += kASoft) {
       const int d = i >> 3, c = i & 7, key = t * kAK + c * 8;
       const bool ok = key + 8 <= p.vt_stride;
       const bf16* src = vbase + (int64_t)d * p.vt_stride + (ok ? key : 0);
@@ -157,6 +164,32 @@ __global__ void __launch_bounds__(kAThreads, 1) prefill_attn_tc_kernel(AttnTcPar
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   };
 
+  __syncthreads();  // barriers initialised, TMEM allocated
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = *tmem_slot;
+  // arrive (release) once this thread's operand writes are complete and its TMEM accesses done
+  auto ready = [&](int i) {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(tc::smem_u32(&bars[i])) : "memory");
+  };
+
+  if (mma_warp) {
+    // ---- MMA issue: S_0, then per tile S_{t+1} (operands ready) and P.V_t (P and V_t ready)
+    if ((tid & 31) == 0) {
+      wait_bar(3, 0);
+      issue_s(tmem, 0);
+      for (int t = 0; t < nt; ++t) {
+        if (t + 1 < nt) {
+          wait_bar(3, (uint32_t)(t + 1) & 1u);
+          issue_s(tmem, t + 1);
+        }
+        wait_bar(4, (uint32_t)t & 1u);
+        issue_pv(tmem, t);
+      }
+    }
+    __syncwarp();
+  } else {
   // prologue: {Q, K_0}, {K_1}, {V_0}
   load_q();
   load_k(0, 0);
@@ -166,16 +199,13 @@ __global__ void __launch_bounds__(kAThreads, 1) prefill_attn_tc_kernel(AttnTcPar
   load_v(0, 0);
   commit();
   asm volatile("cp.async.wait_group 2;" ::: "memory");
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-  __syncthreads();
-  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-  const uint32_t tmem = *tmem_slot;
+  ready(3);  // S_0's operands
   const uint32_t trow = tmem + ((uint32_t)((warp & 3) * 32) << 16);  // this warp's TMEM lane quarter
-  if (tid == 0) issue_s(tmem, 0);
 
   const int row = tid & (kAM - 1), half = tid >> 7;  // row r = head 4 g + r / 32, query q0 + r % 32
   const int qi = q0 + (row & (kAQ - 1));
-  // per-tile row maxima, then (after the last tile's barriers) the row sums of the two halves
+  // per-tile row maxima, then (after the last tile) the row sums of the two halves; only the two
+  // threads of a row touch its entries
   __shared__ float xmax[2][kAM];
   float(&xsum)[2][kAM] = xmax;
   // warps w and w + 4 hold the two halves of the same 32 rows
@@ -187,13 +217,9 @@ __global__ void __launch_bounds__(kAThreads, 1) prefill_attn_tc_kernel(AttnTcPar
     uint32_t sv[32];
     tc::tmem_ld32_async(trow + (uint32_t)((t & 1) * kAK + half * 32), sv);
     tc::tmem_wait_ld();
-    // (b) K_{t+1} present (pending: V_t's group) -> S_{t+1} runs during this tile's softmax
+    // (b) K_{t+1} present (pending: V_t's group): S_{t+1} may run during this tile's softmax
     asm volatile("cp.async.wait_group 1;" ::: "memory");
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-    __syncthreads();
-    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    if (tid == 0 && t + 1 < nt) issue_s(tmem, t + 1);
+    ready(3);
     // (c) K_{t+2} into the buffer S_t has finished reading
     if (t + 2 < nt) load_k(t + 2, t & 1);
     commit();
@@ -215,6 +241,7 @@ __global__ void __launch_bounds__(kAThreads, 1) prefill_attn_tc_kernel(AttnTcPar
     xmax[half][row] = mx[0];
     pair_sync();
     const float mt = fmaxf(mx[0], xmax[half ^ 1][row]);
+    pair_sync();  // both halves have read before either writes the next tile's maximum
     // the reference maximum moves only past a margin of 8 (and on the first finite score); both
     // threads of the row take the same decision
     const float m_new = (mt > m_run + 8.f) ? mt : m_run;
@@ -269,13 +296,9 @@ __global__ void __launch_bounds__(kAThreads, 1) prefill_attn_tc_kernel(AttnTcPar
                    "r"(pl[4 * c + 1]), "r"(pl[4 * c + 2]), "r"(pl[4 * c + 3])
                    : "memory");
     }
-    // (i) V_t present (pending: K_{t+2}, V_{t+1}) -> O += P V_t
+    // (i) V_t present (pending: K_{t+2}, V_{t+1}): P.V_t may run
     asm volatile("cp.async.wait_group 2;" ::: "memory");
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-    __syncthreads();
-    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    if (tid == 0) issue_pv(tmem, t);
+    ready(4);
   }
   // ---- epilogue: O / l for rows of real queries
   if (nt > 0) wait_bar(2, (uint32_t)(nt - 1) & 1u);
@@ -301,9 +324,10 @@ __global__ void __launch_bounds__(kAThreads, 1) prefill_attn_tc_kernel(AttnTcPar
       }
     }
   }
+  }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
-  if (warp == 0) tc::tmem_dealloc(tmem, kTmemCols);
+  if (mma_warp) tc::tmem_dealloc(tmem, kTmemCols);
 }
 
 }  // namespace
