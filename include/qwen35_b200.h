@@ -271,7 +271,8 @@ int q35_prefill_attention(const void* q, const void* k, const void* v, void* out
  * the cache): q [B,Hq,L,256], k [B,Hkv,kv_len,256], vt = V transposed [B,Hkv,256,vt_stride] with
  * vt_stride a multiple of 64 >= L whose columns past L hold finite values -> out [B, L, Hq*256].
  * FP32 softmax; P enters the P.V product as a bf16 high part plus a bf16 remainder.
- * q35_prefill_attention_tc_error returns (and clears) the kernel's bounded-wait error word. */
+ * q35_prefill_attention_tc_error returns (and clears) the kernel's bounded-wait error word: 0, or
+ * 1 + the shared-memory barrier slot whose wait gave up first. */
 int q35_prefill_attention_tc(const void* q, const void* k, const void* vt, void* out, int64_t batch,
                              int64_t q_heads, int64_t kv_heads, int64_t seq_len, int64_t kv_len,
                              int64_t vt_stride, float scale, void* stream);

@@ -18,12 +18,15 @@
 //                        warp-MMA kernel does; O lives in TMEM and is rescaled in place (TMEM
 //                        load / store of the row) when a warp's reference maximum moved
 // V is read transposed (V^T [dim][key], written by the Q/K-norm + RoPE kernel next to the cache
-// rows) so that both MMA operands are K-major with the 128-byte swizzle. Operands arrive by
-// cp.async: Q once, K and V^T double-buffered a tile ahead. Warps 0-7 load and run the softmax; a
-// ninth warp only issues the MMAs (an issuing thread stalls about as long as its MMAs run, which
-// would hold back its own softmax row), handed off through two mbarriers the 256 softmax threads
-// arrive on (operands ready for S, for P.V). Every wait is bounded; a timeout sets
+// rows) so that both MMA operands are K-major with the 128-byte swizzle. Warps 0-7 run the
+// softmax; a ninth warp brings the operands in by TMA (Q once, K and V^T tiles double-buffered)
+// and issues the MMAs (an issuing thread stalls about as long as its MMAs run, which would hold
+// back a softmax row), handed off through mbarriers: TMA arrivals, MMA commits, and two barriers
+// the 256 softmax threads arrive on (S read, P written). Every wait is bounded; a timeout sets
 // q35_attn_tc_error_word.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include <cfloat>
 
 #include "common.cuh"
@@ -48,24 +51,27 @@ constexpr uint32_t kVBytes = kAD * 128;      // V^T tile: 256 dim rows x 64 keys
 constexpr uint32_t kPBytes = kAM * 128;      // P part: 128 rows x 64 keys (128 B)
 constexpr uint32_t kOffK = kQBytes, kOffV = kOffK + 2 * kKBytes, kOffP = kOffV + 2 * kVBytes;
 constexpr uint32_t kOffBar = kOffP + 2 * kPBytes;
-constexpr size_t kAttnTcSmem = kOffBar + 64 + 1024;  // barriers + TMEM slot, 1024-byte alignment slack
+constexpr size_t kAttnTcSmem = kOffBar + 96 + 1024;  // barriers + TMEM slot, 1024-byte alignment slack
 static_assert(kAttnTcSmem + 2 * kAM * sizeof(float) <= 232448, "dynamic + static shared memory of one CTA");
 constexpr uint32_t kTmemCols = 512;                 // S buffers at columns 0 / 64, O at 256
 constexpr uint32_t kColO = 256;
 constexpr long long kAttnWaitBudget = 2000000000LL;
 
 struct AttnTcParams {
-  const bf16* q;   // [B, Hq, L, 256]
-  const bf16* k;   // [B, Hkv, kv_len, 256]
-  const bf16* vt;  // [B, Hkv, 256, vt_stride]: V transposed; columns L .. vt_stride - 1 finite
-  bf16* out;       // [B, L, Hq, 256]
+  bf16* out;  // [B, L, Hq, 256]
   int Hq, Hkv, L, kv_len, vt_stride;
   float scale_log2;  // softmax scale x log2(e)
 };
+// barrier slots in shared memory
+// ready-S is one barrier per S buffer: the MMA warp can fall a tile behind the softmax, and a
+// single barrier would then have advanced past the phase it waits for
+enum { kBarQ = 0, kBarK = 1, kBarV = 3, kBarS = 5, kBarPV = 7, kBarRdyS = 8, kBarRdyPV = 10, kBars = 11 };
 
-Q35_DEV void cp16z(uint32_t dst, const void* src, bool valid) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(valid ? 16 : 0)
-               : "memory");
+Q35_DEV void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+      "l"(map), "r"(x), "r"(y), "r"(bar)
+      : "memory");
 }
 Q35_DEV float ex2(float x) {
   float y;
@@ -77,257 +83,274 @@ Q35_DEV uint32_t pack_bf16(float lo, float hi) {
   return *reinterpret_cast<const uint32_t*>(&v);
 }
 
-__global__ void __launch_bounds__(kAThreads, 1) prefill_attn_tc_kernel(AttnTcParams p) {
+__global__ void __launch_bounds__(kAThreads, 1)
+    prefill_attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                           const __grid_constant__ CUtensorMap tmV, AttnTcParams p) {
   pdl_wait();  // programmatic dependent launch: inputs only after the previous kernel
   pdl_launch_dependents();
   extern __shared__ __align__(16) unsigned char attn_smem_raw[];
   unsigned char* sm = reinterpret_cast<unsigned char*>(((uintptr_t)attn_smem_raw + 1023) & ~(uintptr_t)1023);
   const uint32_t sQ = tc::smem_u32(sm), sK = sQ + kOffK, sV = sQ + kOffV, sP = sQ + kOffP;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + kOffBar);  // S[0], S[1], PV, ready-S, ready-PV
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 5);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + kOffBar);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kBars);
+  auto bar = [&](int i) { return tc::smem_u32(&bars[i]); };
   const int qb = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5;
   const int q0 = qb * kAQ;
   const int L = p.L;
   const int nkeys = min(q0 + kAQ, L);  // keys any row of the block may see (causal)
   const int nt = (nkeys + kAK - 1) / kAK;
-  const bf16* kbase = p.k + ((int64_t)b * p.Hkv + g) * p.kv_len * kAD;
-  const bf16* vbase = p.vt + ((int64_t)b * p.Hkv + g) * kAD * p.vt_stride;
 
   const bool mma_warp = warp == kASoft / 32;
   if (mma_warp) tc::tmem_alloc(tmem_slot, kTmemCols);
   if (tid == 0) {
 #pragma unroll
-    for (int i = 0; i < 3; ++i) tc::mbar_init(tc::smem_u32(&bars[i]), 1);
-    tc::mbar_init(tc::smem_u32(&bars[3]), kASoft);
-    tc::mbar_init(tc::smem_u32(&bars[4]), kASoft);
+    for (int i = 0; i < kBarRdyS; ++i) tc::mbar_init(bar(i), 1);
+    tc::mbar_init(bar(kBarRdyS), kASoft);
+    tc::mbar_init(bar(kBarRdyS + 1), kASoft);
+    tc::mbar_init(bar(kBarRdyPV), kASoft);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-
-  // ---- operand loads (every thread): 16-byte chunks into their 128-byte-swizzled positions
-  auto load_q = [&]() {  // 128 rows x 32 chunks
-    for (int i = tid; i < kAM * (kAD / 8); i += kASoft) {
-      const int r = i >> 5, c = i & 31;
-      const int qi = q0 + (r & (kAQ - 1)), hh = g * kAG + (r >> 5);
-      const bool ok = qi < L;
-      const bf16* src = p.q + (((int64_t)b * p.Hq + hh) * L + (ok ? qi : 0)) * kAD + c * 8;
-      cp16z(sQ + (c >> 3) * (kAM * 128) + tc::sw128_offset(r, c & 7), src, ok);
-    }
-  };
-  auto load_k = [&](int t, int buf) {  // 64 keys x 32 chunks
-    for (int i = tid; i < kAK * (kAD / 8); i += kASoft) {
-      const int r = i >> 5, c = i & 31, key = t * kAK + r;
-      const bool ok = key < p.kv_len;
-      const bf16* src = kbase + (int64_t)(ok ? key : 0) * kAD + c * 8;
-      cp16z(sK + buf * kKBytes + (c >> 3) * (kAK * 128) + tc::sw128_offset(r, c & 7), src, ok);
-    }
-  };
-  auto load_v = [&](int t, int buf) {  // 256 dim rows x 8 chunks of 8 keys
-    for (int i = tid; i < kAD * (kAK / 8); i += kASoft) {
-      const int d = i >> 3, c = i & 7, key = t * kAK + c * 8;
-      const bool ok = key + 8 <= p.vt_stride;
-      const bf16* src = vbase + (int64_t)d * p.vt_stride + (ok ? key : 0);
-      cp16z(sV + buf * kVBytes + tc::sw128_offset(d, c), src, ok);
-    }
-  };
-  auto commit = [] { asm volatile("cp.async.commit_group;" ::: "memory"); };
-
-  const uint32_t idesc_s = tc::idesc_f32acc(1, kAM, kAK);  // bf16 x bf16 -> FP32, M 128, N 64
-  const uint32_t idesc_o = tc::idesc_f32acc(1, kAM, kAD);  // M 128, N 256
-  auto issue_s = [&](uint32_t tmem, int t) {  // S[t & 1] = Q K_t^T
-    const uint32_t d = tmem + (uint32_t)((t & 1) * kAK);
-    const uint32_t kb = sK + (t & 1) * kKBytes;
-#pragma unroll
-    for (int s = 0; s < 4; ++s)
-#pragma unroll
-      for (int kk = 0; kk < 4; ++kk)
-        tc::mma_bf16(d, tc::desc_sw128(sQ + s * (kAM * 128) + kk * 32), tc::desc_sw128(kb + s * (kAK * 128) + kk * 32),
-                     idesc_s, (s | kk) ? 1u : 0u);
-    tc::commit(tc::smem_u32(&bars[t & 1]));
-  };
-  auto issue_pv = [&](uint32_t tmem, int t) {  // O += P_hi V_t + P_lo V_t
-    const uint32_t vb = sV + (t & 1) * kVBytes;
-#pragma unroll
-    for (int kk = 0; kk < 4; ++kk)
-#pragma unroll
-      for (int part = 0; part < 2; ++part)
-        tc::mma_bf16(tmem + kColO, tc::desc_sw128(sP + part * kPBytes + kk * 32), tc::desc_sw128(vb + kk * 32), idesc_o,
-                     (t > 0 || kk > 0 || part > 0) ? 1u : 0u);
-    tc::commit(tc::smem_u32(&bars[2]));
-  };
   bool ok = true;
   auto wait_bar = [&](int i, uint32_t parity) {
-    if (ok && !tc::mbar_wait_bounded(tc::smem_u32(&bars[i]), parity, kAttnWaitBudget)) {
+    if (ok && !tc::mbar_wait_bounded(bar(i), parity, kAttnWaitBudget)) {
       ok = false;
-      atomicCAS(&q35_attn_tc_error_word, 0, 1);
+      atomicCAS(&q35_attn_tc_error_word, 0, 1 + i);  // 1 + the barrier slot that timed out
     }
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   };
-
   __syncthreads();  // barriers initialised, TMEM allocated
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = *tmem_slot;
-  // arrive (release) once this thread's operand writes are complete and its TMEM accesses done
-  auto ready = [&](int i) {
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(tc::smem_u32(&bars[i])) : "memory");
-  };
 
   if (mma_warp) {
-    // ---- MMA issue: S_0, then per tile S_{t+1} (operands ready) and P.V_t (P and V_t ready)
     if ((tid & 31) == 0) {
-      wait_bar(3, 0);
-      issue_s(tmem, 0);
+      const uint32_t idesc_s = tc::idesc_f32acc(1, kAM, kAK);  // bf16 x bf16 -> FP32, M 128, N 64
+      const uint32_t idesc_o = tc::idesc_f32acc(1, kAM, kAD);  // M 128, N 256
+      const int krow0 = (b * p.Hkv + g) * p.kv_len, vrow0 = (b * p.Hkv + g) * kAD;
+      auto load_k = [&](int t) {  // 4 boxes of 64 keys x 64 dims into buffer t & 1
+        const int i = t & 1;
+        tc::mbar_expect_tx(bar(kBarK + i), kKBytes);
+#pragma unroll
+        for (int sl = 0; sl < 4; ++sl)
+          tma_load_2d(sK + i * kKBytes + sl * (kAK * 128), &tmK, sl * 64, krow0 + t * kAK, bar(kBarK + i));
+      };
+      auto load_v = [&](int t) {  // one box of 256 dims x 64 keys into buffer t & 1
+        const int i = t & 1;
+        tc::mbar_expect_tx(bar(kBarV + i), kVBytes);
+        tma_load_2d(sV + i * kVBytes, &tmV, t * kAK, vrow0, bar(kBarV + i));
+      };
+      auto issue_s = [&](int t) {  // S[t & 1] = Q K_t^T
+        const uint32_t d = tmem + (uint32_t)((t & 1) * kAK);
+        const uint32_t kb = sK + (t & 1) * kKBytes;
+#pragma unroll
+        for (int sl = 0; sl < 4; ++sl)
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            tc::mma_bf16(d, tc::desc_sw128(sQ + sl * (kAM * 128) + kk * 32),
+                         tc::desc_sw128(kb + sl * (kAK * 128) + kk * 32), idesc_s, (sl | kk) ? 1u : 0u);
+        tc::commit(bar(kBarS + (t & 1)));
+      };
+      auto issue_pv = [&](int t) {  // O += P_hi V_t + P_lo V_t
+        const uint32_t vb = sV + (t & 1) * kVBytes;
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+#pragma unroll
+          for (int part = 0; part < 2; ++part)
+            tc::mma_bf16(tmem + kColO, tc::desc_sw128(sP + part * kPBytes + kk * 32), tc::desc_sw128(vb + kk * 32),
+                         idesc_o, (t > 0 || kk > 0 || part > 0) ? 1u : 0u);
+        tc::commit(bar(kBarPV));
+      };
+      // Q: 4 heads x 4 dim slabs of 32 query rows
+      tc::mbar_expect_tx(bar(kBarQ), kQBytes);
+#pragma unroll
+      for (int hd = 0; hd < kAG; ++hd)
+#pragma unroll
+        for (int sl = 0; sl < 4; ++sl)
+          tma_load_2d(sQ + sl * (kAM * 128) + hd * (kAQ * 128), &tmQ, sl * 64, (b * p.Hq + g * kAG + hd) * L + q0,
+                      bar(kBarQ));
+      load_k(0);
+      if (nt > 1) load_k(1);
+      load_v(0);
+      if (nt > 1) load_v(1);
+      wait_bar(kBarQ, 0);
+      wait_bar(kBarK, 0);
+      issue_s(0);
       for (int t = 0; t < nt; ++t) {
-        if (t + 1 < nt) {
-          wait_bar(3, (uint32_t)(t + 1) & 1u);
-          issue_s(tmem, t + 1);
+        if (t + 1 < nt) {  // S_{t+1}: K_{t+1} arrived and the softmax has read S_{t-1} from its buffer
+          wait_bar(kBarK + ((t + 1) & 1), (uint32_t)((t + 1) >> 1) & 1u);
+          if (t >= 1) wait_bar(kBarRdyS + ((t - 1) & 1), (uint32_t)((t - 1) >> 1) & 1u);
+          issue_s(t + 1);
         }
-        wait_bar(4, (uint32_t)t & 1u);
-        issue_pv(tmem, t);
+        if (t + 2 < nt) {  // K_{t+2} into the buffer S_t has finished reading
+          wait_bar(kBarS + (t & 1), (uint32_t)(t >> 1) & 1u);
+          load_k(t + 2);
+        }
+        if (t >= 1 && t + 1 < nt) {  // V_{t+1} into the buffer P.V_{t-1} has finished reading
+          wait_bar(kBarPV, (uint32_t)(t - 1) & 1u);
+          load_v(t + 1);
+        }
+        wait_bar(kBarV + (t & 1), (uint32_t)(t >> 1) & 1u);  // V_t
+        wait_bar(kBarRdyPV, (uint32_t)t & 1u);               // P_t written, O rescaled
+        issue_pv(t);
       }
     }
     __syncwarp();
   } else {
-  // prologue: {Q, K_0}, {K_1}, {V_0}
-  load_q();
-  load_k(0, 0);
-  commit();
-  if (nt > 1) load_k(1, 1);
-  commit();
-  load_v(0, 0);
-  commit();
-  asm volatile("cp.async.wait_group 2;" ::: "memory");
-  ready(3);  // S_0's operands
-  const uint32_t trow = tmem + ((uint32_t)((warp & 3) * 32) << 16);  // this warp's TMEM lane quarter
-
-  const int row = tid & (kAM - 1), half = tid >> 7;  // row r = head 4 g + r / 32, query q0 + r % 32
-  const int qi = q0 + (row & (kAQ - 1));
-  // per-tile row maxima, then (after the last tile) the row sums of the two halves; only the two
-  // threads of a row touch its entries
-  __shared__ float xmax[2][kAM];
-  float(&xsum)[2][kAM] = xmax;
-  // warps w and w + 4 hold the two halves of the same 32 rows
-  auto pair_sync = [&] { asm volatile("bar.sync %0, 64;" ::"r"(1 + (warp & 3)) : "memory"); };
-  float m_run = -INFINITY, l_run = 0.f;
-  for (int t = 0; t < nt; ++t) {
-    // (a) S_t -> registers (frees its TMEM buffer for S_{t+2})
-    wait_bar(t & 1, (uint32_t)(t >> 1) & 1u);
-    uint32_t sv[32];
-    tc::tmem_ld32_async(trow + (uint32_t)((t & 1) * kAK + half * 32), sv);
-    tc::tmem_wait_ld();
-    // (b) K_{t+1} present (pending: V_t's group): S_{t+1} may run during this tile's softmax
-    asm volatile("cp.async.wait_group 1;" ::: "memory");
-    ready(3);
-    // (c) K_{t+2} into the buffer S_t has finished reading
-    if (t + 2 < nt) load_k(t + 2, t & 1);
-    commit();
-    // (d) softmax of this row over the tile's 64 keys: this thread's 32, the partner's maximum
-    const int k0 = t * kAK + half * 32;
-    float x[32];
-#pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      const int key = k0 + j;
-      x[j] = (key <= qi && key < L) ? __uint_as_float(sv[j]) * p.scale_log2 : -INFINITY;
+    const uint32_t trow = tmem + ((uint32_t)((warp & 3) * 32) << 16);  // this warp's TMEM lane quarter
+    const int row = tid & (kAM - 1), half = tid >> 7;  // row r = head 4 g + r / 32, query q0 + r % 32
+    const int qi = q0 + (row & (kAQ - 1));
+    // per-tile row maxima, then (after the last tile) the row sums of the two halves; only the two
+    // threads of a row touch its entries
+    __shared__ float xmax[2][kAM];
+    float(&xsum)[2][kAM] = xmax;
+    // warps w and w + 4 hold the two halves of the same 32 rows
+    auto pair_sync = [&] { asm volatile("bar.sync %0, 64;" ::"r"(1 + (warp & 3)) : "memory"); };
+    // arrive (release) once this thread's shared-memory writes and TMEM accesses are done
+    auto ready = [&](int i) {
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar(i)) : "memory");
+    };
+    float m_run = -INFINITY, l_run = 0.f;
+    for (int t = 0; t < nt; ++t) {
+      // (a) S_t -> registers; its TMEM buffer is then free for S_{t+2}
+      wait_bar(kBarS + (t & 1), (uint32_t)(t >> 1) & 1u);
+      uint32_t sv[32];
+      tc::tmem_ld32_async(trow + (uint32_t)((t & 1) * kAK + half * 32), sv);
+      tc::tmem_wait_ld();
+      ready(kBarRdyS + (t & 1));
+      // (d) softmax of this row over the tile's 64 keys: this thread's 32, the partner's maximum
+      const int k0 = t * kAK + half * 32;
+      float x[32];
+  #pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const int key = k0 + j;
+        x[j] = (key <= qi && key < L) ? __uint_as_float(sv[j]) * p.scale_log2 : -INFINITY;
+      }
+      float mx[16];
+  #pragma unroll
+      for (int j = 0; j < 16; ++j) mx[j] = fmaxf(x[j], x[j + 16]);
+  #pragma unroll
+      for (int w = 8; w > 0; w >>= 1)
+  #pragma unroll
+        for (int j = 0; j < w; ++j) mx[j] = fmaxf(mx[j], mx[j + w]);
+      xmax[half][row] = mx[0];
+      pair_sync();
+      const float mt = fmaxf(mx[0], xmax[half ^ 1][row]);
+      pair_sync();  // both halves have read before either writes the next tile's maximum
+      // the reference maximum moves only past a margin of 8 (and on the first finite score); both
+      // threads of the row take the same decision
+      const float m_new = (mt > m_run + 8.f) ? mt : m_run;
+      const float alpha = (m_new == m_run) ? 1.f : ex2(m_run - m_new);
+      uint32_t ph[16], pl[16];
+      float ps[16];
+  #pragma unroll
+      for (int j = 0; j < 32; j += 2) {
+        const float p0 = (x[j] == -INFINITY) ? 0.f : ex2(x[j] - m_new);
+        const float p1 = (x[j + 1] == -INFINITY) ? 0.f : ex2(x[j + 1] - m_new);
+        ps[j / 2] = p0 + p1;
+        const uint32_t hi = pack_bf16(p0, p1);
+        ph[j / 2] = hi;
+        pl[j / 2] = pack_bf16(p0 - __uint_as_float(hi << 16), p1 - __uint_as_float(hi & 0xffff0000u));
+      }
+  #pragma unroll
+      for (int w = 8; w > 0; w >>= 1)
+  #pragma unroll
+        for (int j = 0; j < w; ++j) ps[j] += ps[j + w];
+      l_run = l_run * alpha + ps[0];  // this thread's half of the row sum
+      m_run = m_new;
+      // (e) PV_{t-1} done: O is stable, P is free
+      if (t > 0) wait_bar(kBarPV, (uint32_t)(t - 1) & 1u);
+      // (g) rescale O rows whose maximum moved (whole warps: TMEM access is warp-collective)
+      if (t > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+  #pragma unroll 1
+        for (int c = half * (kAD / 2); c < (half + 1) * (kAD / 2); c += 64) {
+          uint32_t o[2][32];
+          tc::tmem_ld32_async(trow + kColO + c, o[0]);
+          tc::tmem_ld32_async(trow + kColO + c + 32, o[1]);
+          tc::tmem_wait_ld();
+  #pragma unroll
+          for (int h = 0; h < 2; ++h)
+  #pragma unroll
+            for (int j = 0; j < 32; ++j) o[h][j] = __float_as_uint(__uint_as_float(o[h][j]) * alpha);
+          tc::tmem_st32(trow + kColO + c, o[0]);
+          tc::tmem_st32(trow + kColO + c + 32, o[1]);
+        }
+        tc::tmem_wait_st();
+      }
+      // (h) P high / low parts: row `row`, this thread's 4 chunks of 8 keys
+  #pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const uint32_t off = tc::sw128_offset(row, half * 4 + c);
+        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(sP + off), "r"(ph[4 * c]), "r"(ph[4 * c + 1]),
+                     "r"(ph[4 * c + 2]), "r"(ph[4 * c + 3])
+                     : "memory");
+        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(sP + kPBytes + off), "r"(pl[4 * c]),
+                     "r"(pl[4 * c + 1]), "r"(pl[4 * c + 2]), "r"(pl[4 * c + 3])
+                     : "memory");
+      }
+      // (i) P.V_t may run
+      ready(kBarRdyPV);
     }
-    float mx[16];
-#pragma unroll
-    for (int j = 0; j < 16; ++j) mx[j] = fmaxf(x[j], x[j + 16]);
-#pragma unroll
-    for (int w = 8; w > 0; w >>= 1)
-#pragma unroll
-      for (int j = 0; j < w; ++j) mx[j] = fmaxf(mx[j], mx[j + w]);
-    xmax[half][row] = mx[0];
+    // ---- epilogue: O / l for rows of real queries
+    if (nt > 0) wait_bar(kBarPV, (uint32_t)(nt - 1) & 1u);
+    xsum[half][row] = l_run;
     pair_sync();
-    const float mt = fmaxf(mx[0], xmax[half ^ 1][row]);
-    pair_sync();  // both halves have read before either writes the next tile's maximum
-    // the reference maximum moves only past a margin of 8 (and on the first finite score); both
-    // threads of the row take the same decision
-    const float m_new = (mt > m_run + 8.f) ? mt : m_run;
-    const float alpha = (m_new == m_run) ? 1.f : ex2(m_run - m_new);
-    uint32_t ph[16], pl[16];
-    float ps[16];
-#pragma unroll
-    for (int j = 0; j < 32; j += 2) {
-      const float p0 = (x[j] == -INFINITY) ? 0.f : ex2(x[j] - m_new);
-      const float p1 = (x[j + 1] == -INFINITY) ? 0.f : ex2(x[j + 1] - m_new);
-      ps[j / 2] = p0 + p1;
-      const uint32_t hi = pack_bf16(p0, p1);
-      ph[j / 2] = hi;
-      pl[j / 2] = pack_bf16(p0 - __uint_as_float(hi << 16), p1 - __uint_as_float(hi & 0xffff0000u));
-    }
-#pragma unroll
-    for (int w = 8; w > 0; w >>= 1)
-#pragma unroll
-      for (int j = 0; j < w; ++j) ps[j] += ps[j + w];
-    l_run = l_run * alpha + ps[0];  // this thread's half of the row sum
-    m_run = m_new;
-    // (e) PV_{t-1} done: O is stable, P and V_{t-1}'s buffer are free
-    if (t > 0) wait_bar(2, (uint32_t)(t - 1) & 1u);
-    // (f) V_{t+1} into the freed buffer
-    if (t + 1 < nt) load_v(t + 1, (t + 1) & 1);
-    commit();
-    // (g) rescale O rows whose maximum moved (whole warps: TMEM access is warp-collective)
-    if (t > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
-#pragma unroll 1
-      for (int c = half * (kAD / 2); c < (half + 1) * (kAD / 2); c += 64) {
-        uint32_t o[2][32];
-        tc::tmem_ld32_async(trow + kColO + c, o[0]);
-        tc::tmem_ld32_async(trow + kColO + c + 32, o[1]);
-        tc::tmem_wait_ld();
-#pragma unroll
-        for (int h = 0; h < 2; ++h)
-#pragma unroll
-          for (int j = 0; j < 32; ++j) o[h][j] = __float_as_uint(__uint_as_float(o[h][j]) * alpha);
-        tc::tmem_st32(trow + kColO + c, o[0]);
-        tc::tmem_st32(trow + kColO + c + 32, o[1]);
-      }
-      tc::tmem_wait_st();
-    }
-    // (h) P high / low parts: row `row`, this thread's 4 chunks of 8 keys
-#pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      const uint32_t off = tc::sw128_offset(row, half * 4 + c);
-      asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(sP + off), "r"(ph[4 * c]), "r"(ph[4 * c + 1]),
-                   "r"(ph[4 * c + 2]), "r"(ph[4 * c + 3])
-                   : "memory");
-      asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(sP + kPBytes + off), "r"(pl[4 * c]),
-                   "r"(pl[4 * c + 1]), "r"(pl[4 * c + 2]), "r"(pl[4 * c + 3])
-                   : "memory");
-    }
-    // (i) V_t present (pending: K_{t+2}, V_{t+1}): P.V_t may run
-    asm volatile("cp.async.wait_group 2;" ::: "memory");
-    ready(4);
-  }
-  // ---- epilogue: O / l for rows of real queries
-  if (nt > 0) wait_bar(2, (uint32_t)(nt - 1) & 1u);
-  xsum[half][row] = l_run;
-  pair_sync();
-  const float l_row = half ? xsum[0][row] + l_run : l_run + xsum[1][row];  // same order in both threads
-  const float inv = l_row > 0.f ? 1.0f / l_row : 0.f;
-  const int hh = g * kAG + (row >> 5);
-#pragma unroll 1
-  for (int c = half * (kAD / 2); c < (half + 1) * (kAD / 2); c += 32) {
-    uint32_t o[32];
-    tc::tmem_ld32(trow + kColO + c, o);
-    if (ok && qi < L) {
-      bf16* dst = p.out + (((int64_t)b * L + qi) * p.Hq + hh) * kAD + c;
-#pragma unroll
-      for (int j = 0; j < 32; j += 8) {
-        uint4 v;
-        v.x = pack_bf16(__uint_as_float(o[j]) * inv, __uint_as_float(o[j + 1]) * inv);
-        v.y = pack_bf16(__uint_as_float(o[j + 2]) * inv, __uint_as_float(o[j + 3]) * inv);
-        v.z = pack_bf16(__uint_as_float(o[j + 4]) * inv, __uint_as_float(o[j + 5]) * inv);
-        v.w = pack_bf16(__uint_as_float(o[j + 6]) * inv, __uint_as_float(o[j + 7]) * inv);
-        *reinterpret_cast<uint4*>(dst + j) = v;
+    const float l_row = half ? xsum[0][row] + l_run : l_run + xsum[1][row];  // same order in both threads
+    const float inv = l_row > 0.f ? 1.0f / l_row : 0.f;
+    const int hh = g * kAG + (row >> 5);
+  #pragma unroll 1
+    for (int c = half * (kAD / 2); c < (half + 1) * (kAD / 2); c += 32) {
+      uint32_t o[32];
+      tc::tmem_ld32(trow + kColO + c, o);
+      if (ok && qi < L) {
+        bf16* dst = p.out + (((int64_t)b * L + qi) * p.Hq + hh) * kAD + c;
+  #pragma unroll
+        for (int j = 0; j < 32; j += 8) {
+          uint4 v;
+          v.x = pack_bf16(__uint_as_float(o[j]) * inv, __uint_as_float(o[j + 1]) * inv);
+          v.y = pack_bf16(__uint_as_float(o[j + 2]) * inv, __uint_as_float(o[j + 3]) * inv);
+          v.z = pack_bf16(__uint_as_float(o[j + 4]) * inv, __uint_as_float(o[j + 5]) * inv);
+          v.w = pack_bf16(__uint_as_float(o[j + 6]) * inv, __uint_as_float(o[j + 7]) * inv);
+          *reinterpret_cast<uint4*>(dst + j) = v;
+        }
       }
     }
-  }
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
   if (mma_warp) tc::tmem_dealloc(tmem, kTmemCols);
+}
+
+}  // namespace
+
+namespace {
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult qr;
+    void* f = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &qr) == cudaSuccess &&
+        qr == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+  }
+  return fn;
+}
+
+// 2-D bf16 map over rows x cols (row-major), boxes of 64 columns (128 bytes) x box_rows, 128-byte
+// swizzle; reads past the tensor fill with zeros.
+bool make_map_bf16(CUtensorMap* m, const void* ptr, uint64_t rows, uint64_t cols, uint32_t box_rows) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {cols * 2};
+  cuuint32_t box[2] = {64, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 }  // namespace
@@ -352,10 +375,18 @@ int q35_prefill_attention_tc_launch(const void* q, const void* k, const void* vt
     cudaFuncSetAttribute(prefill_attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kAttnTcSmem);
     return true;
   });
-  AttnTcParams prm{(const bf16*)q, (const bf16*)k, (const bf16*)vt, (bf16*)out, (int)q_heads, (int)kv_heads,
-                   (int)seq_len, (int)kv_len, (int)vt_stride, scale * 1.4426950408889634f};
+  // TMA maps (bf16, 128-byte swizzle, boxes of 64 elements along the row): q rows [B*Hq*L] boxes
+  // of 32 rows, k rows [B*Hkv*kv_len] boxes of 64 keys, V^T rows [B*Hkv*256] boxes of 256 dims x 64 keys
+  CUtensorMap mq, mk, mv;
+  if (!make_map_bf16(&mq, q, (uint64_t)batch * q_heads * seq_len, kAD, 32) ||
+      !make_map_bf16(&mk, k, (uint64_t)batch * kv_heads * kv_len, kAD, kAK) ||
+      !make_map_bf16(&mv, vt, (uint64_t)batch * kv_heads * kAD, (uint64_t)vt_stride, kAD))
+    return q35_fail(Q35_ECUDA, "prefill_attention_tc: tensor map encoding failed");
+  AttnTcParams prm{(bf16*)out, (int)q_heads, (int)kv_heads, (int)seq_len, (int)kv_len, (int)vt_stride,
+                   scale * 1.4426950408889634f};
   const dim3 grid((unsigned)((seq_len + kAQ - 1) / kAQ), (unsigned)kv_heads, (unsigned)batch);
-  const cudaError_t e = q35_launch(prefill_attn_tc_kernel, grid, dim3(kAThreads), kAttnTcSmem, stream, pdl, prm);
+  const cudaError_t e =
+      q35_launch(prefill_attn_tc_kernel, grid, dim3(kAThreads), kAttnTcSmem, stream, pdl, mq, mk, mv, prm);
   if (e != cudaSuccess) return q35_fail(Q35_ECUDA, "prefill_attention_tc launch: %s", cudaGetErrorString(e));
   return Q35_OK;
 }
