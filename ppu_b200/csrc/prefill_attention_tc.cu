@@ -19,11 +19,12 @@
 //                        load / store of the row) when a warp's reference maximum moved
 // V is read transposed (V^T [dim][key], written by the Q/K-norm + RoPE kernel next to the cache
 // rows) so that both MMA operands are K-major with the 128-byte swizzle. Warps 0-7 run the
-// softmax; a ninth warp brings the operands in by TMA (Q once, K and V^T tiles double-buffered)
-// and issues the MMAs (an issuing thread stalls about as long as its MMAs run, which would hold
-// back a softmax row), handed off through mbarriers: TMA arrivals, MMA commits, and two barriers
-// the 256 softmax threads arrive on (S read, P written). Every wait is bounded; a timeout sets
-// q35_attn_tc_error_word.
+// softmax; warp 8 issues the MMAs (an issuing thread stalls about as long as its MMAs run, which
+// would hold back a softmax row); warp 9 brings the operands in by TMA (Q once, K and V^T tiles
+// double-buffered). They hand off through mbarriers: TMA arrivals, MMA commits, and barriers the
+// 256 softmax threads arrive on (S read, P written); wherever one side can run a tile ahead of
+// its waiter the barrier is per buffer, so no wait can see a later phase of the same parity.
+// Every wait is bounded; a timeout sets q35_attn_tc_error_word.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -44,14 +45,14 @@ constexpr int kAQ = 32;          // queries per head in a tile
 constexpr int kAM = kAG * kAQ;   // 128 MMA rows
 constexpr int kAK = 64;          // keys per tile
 constexpr int kASoft = 256;      // softmax threads: two per row r = tid % 128 (TMEM lane r), key / O column halves
-constexpr int kAThreads = kASoft + 32;  // + the MMA warp
+constexpr int kAThreads = kASoft + 64;  // + the MMA warp + the TMA warp
 constexpr uint32_t kQBytes = 4 * kAM * 128;  // Q: 4 slabs (64 dims) x 128 rows x 128 B
 constexpr uint32_t kKBytes = 4 * kAK * 128;  // K tile: 4 slabs x 64 keys x 128 B
 constexpr uint32_t kVBytes = kAD * 128;      // V^T tile: 256 dim rows x 64 keys (128 B)
 constexpr uint32_t kPBytes = kAM * 128;      // P part: 128 rows x 64 keys (128 B)
 constexpr uint32_t kOffK = kQBytes, kOffV = kOffK + 2 * kKBytes, kOffP = kOffV + 2 * kVBytes;
 constexpr uint32_t kOffBar = kOffP + 2 * kPBytes;
-constexpr size_t kAttnTcSmem = kOffBar + 96 + 1024;  // barriers + TMEM slot, 1024-byte alignment slack
+constexpr size_t kAttnTcSmem = kOffBar + 128 + 1024;  // barriers + TMEM slot, 1024-byte alignment slack
 static_assert(kAttnTcSmem + 2 * kAM * sizeof(float) <= 232448, "dynamic + static shared memory of one CTA");
 constexpr uint32_t kTmemCols = 512;                 // S buffers at columns 0 / 64, O at 256
 constexpr uint32_t kColO = 256;
@@ -63,9 +64,9 @@ struct AttnTcParams {
   float scale_log2;  // softmax scale x log2(e)
 };
 // barrier slots in shared memory
-// ready-S is one barrier per S buffer: the MMA warp can fall a tile behind the softmax, and a
-// single barrier would then have advanced past the phase it waits for
-enum { kBarQ = 0, kBarK = 1, kBarV = 3, kBarS = 5, kBarPV = 7, kBarRdyS = 8, kBarRdyPV = 10, kBars = 11 };
+// barrier slots: TMA arrivals (Q, K[2], V[2]), MMA commits (S[2], P.V, V buffer free[2]), softmax
+// arrivals (S[2] read, P written)
+enum { kBarQ = 0, kBarK = 1, kBarV = 3, kBarS = 5, kBarPV = 7, kBarVFree = 8, kBarRdyS = 10, kBarRdyPV = 12, kBars = 13 };
 
 Q35_DEV void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
   asm volatile(
@@ -101,11 +102,13 @@ __global__ void __launch_bounds__(kAThreads, 1)
   const int nkeys = min(q0 + kAQ, L);  // keys any row of the block may see (causal)
   const int nt = (nkeys + kAK - 1) / kAK;
 
-  const bool mma_warp = warp == kASoft / 32;
+  const bool mma_warp = warp == kASoft / 32, tma_warp = warp == kASoft / 32 + 1;
   if (mma_warp) tc::tmem_alloc(tmem_slot, kTmemCols);
   if (tid == 0) {
 #pragma unroll
     for (int i = 0; i < kBarRdyS; ++i) tc::mbar_init(bar(i), 1);
+    tc::mbar_init(bar(kBarVFree), 1);
+    tc::mbar_init(bar(kBarVFree + 1), 1);
     tc::mbar_init(bar(kBarRdyS), kASoft);
     tc::mbar_init(bar(kBarRdyS + 1), kASoft);
     tc::mbar_init(bar(kBarRdyPV), kASoft);
@@ -113,7 +116,7 @@ __global__ void __launch_bounds__(kAThreads, 1)
   }
   bool ok = true;
   auto wait_bar = [&](int i, uint32_t parity) {
-    if (ok && !tc::mbar_wait_bounded(bar(i), parity, kAttnWaitBudget)) {
+    if (ok && !tc::mbar_test(bar(i), parity) && !tc::mbar_wait_bounded(bar(i), parity, kAttnWaitBudget)) {
       ok = false;
       atomicCAS(&q35_attn_tc_error_word, 0, 1 + i);  // 1 + the barrier slot that timed out
     }
@@ -123,7 +126,7 @@ __global__ void __launch_bounds__(kAThreads, 1)
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = *tmem_slot;
 
-  if (mma_warp) {
+  if (mma_warp || tma_warp) {
     if ((tid & 31) == 0) {
       const uint32_t idesc_s = tc::idesc_f32acc(1, kAM, kAK);  // bf16 x bf16 -> FP32, M 128, N 64
       const uint32_t idesc_o = tc::idesc_f32acc(1, kAM, kAD);  // M 128, N 256
@@ -160,39 +163,44 @@ __global__ void __launch_bounds__(kAThreads, 1)
             tc::mma_bf16(tmem + kColO, tc::desc_sw128(sP + part * kPBytes + kk * 32), tc::desc_sw128(vb + kk * 32),
                          idesc_o, (t > 0 || kk > 0 || part > 0) ? 1u : 0u);
         tc::commit(bar(kBarPV));
+        tc::commit(bar(kBarVFree + (t & 1)));
       };
-      // Q: 4 heads x 4 dim slabs of 32 query rows
-      tc::mbar_expect_tx(bar(kBarQ), kQBytes);
+      if (tma_warp) {
+        // Q: 4 heads x 4 dim slabs of 32 query rows; K_0, K_1, V_0, V_1; then each buffer again
+        // once the MMA that read it has completed
+        tc::mbar_expect_tx(bar(kBarQ), kQBytes);
 #pragma unroll
-      for (int hd = 0; hd < kAG; ++hd)
+        for (int hd = 0; hd < kAG; ++hd)
 #pragma unroll
-        for (int sl = 0; sl < 4; ++sl)
-          tma_load_2d(sQ + sl * (kAM * 128) + hd * (kAQ * 128), &tmQ, sl * 64, (b * p.Hq + g * kAG + hd) * L + q0,
-                      bar(kBarQ));
-      load_k(0);
-      if (nt > 1) load_k(1);
-      load_v(0);
-      if (nt > 1) load_v(1);
-      wait_bar(kBarQ, 0);
-      wait_bar(kBarK, 0);
-      issue_s(0);
-      for (int t = 0; t < nt; ++t) {
-        if (t + 1 < nt) {  // S_{t+1}: K_{t+1} arrived and the softmax has read S_{t-1} from its buffer
-          wait_bar(kBarK + ((t + 1) & 1), (uint32_t)((t + 1) >> 1) & 1u);
-          if (t >= 1) wait_bar(kBarRdyS + ((t - 1) & 1), (uint32_t)((t - 1) >> 1) & 1u);
-          issue_s(t + 1);
+          for (int sl = 0; sl < 4; ++sl)
+            tma_load_2d(sQ + sl * (kAM * 128) + hd * (kAQ * 128), &tmQ, sl * 64, (b * p.Hq + g * kAG + hd) * L + q0,
+                        bar(kBarQ));
+        load_k(0);
+        load_v(0);
+        if (nt > 1) {
+          load_k(1);
+          load_v(1);
         }
-        if (t + 2 < nt) {  // K_{t+2} into the buffer S_t has finished reading
-          wait_bar(kBarS + (t & 1), (uint32_t)(t >> 1) & 1u);
+        for (int t = 0; t + 2 < nt; ++t) {
+          wait_bar(kBarS + (t & 1), (uint32_t)(t >> 1) & 1u);  // S_t read K_t's buffer
           load_k(t + 2);
+          wait_bar(kBarVFree + (t & 1), (uint32_t)(t >> 1) & 1u);  // P.V_t read V_t's buffer
+          load_v(t + 2);
         }
-        if (t >= 1 && t + 1 < nt) {  // V_{t+1} into the buffer P.V_{t-1} has finished reading
-          wait_bar(kBarPV, (uint32_t)(t - 1) & 1u);
-          load_v(t + 1);
+      } else {
+        wait_bar(kBarQ, 0);
+        wait_bar(kBarK, 0);
+        issue_s(0);
+        for (int t = 0; t < nt; ++t) {
+          if (t + 1 < nt) {  // S_{t+1}: K_{t+1} arrived and the softmax has read S_{t-1} from its buffer
+            wait_bar(kBarK + ((t + 1) & 1), (uint32_t)((t + 1) >> 1) & 1u);
+            if (t >= 1) wait_bar(kBarRdyS + ((t - 1) & 1), (uint32_t)((t - 1) >> 1) & 1u);
+            issue_s(t + 1);
+          }
+          wait_bar(kBarV + (t & 1), (uint32_t)(t >> 1) & 1u);  // V_t
+          wait_bar(kBarRdyPV, (uint32_t)t & 1u);               // P_t written, O rescaled
+          issue_pv(t);
         }
-        wait_bar(kBarV + (t & 1), (uint32_t)(t >> 1) & 1u);  // V_t
-        wait_bar(kBarRdyPV, (uint32_t)t & 1u);               // P_t written, O rescaled
-        issue_pv(t);
       }
     }
     __syncwarp();

@@ -63,6 +63,19 @@ Q35_DEV void mbar_init(uint32_t bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
 }
 
+// One non-blocking test of phase `parity` (true once that phase has completed).
+Q35_DEV bool mbar_test(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // Bounded wait for phase `parity` of the mbarrier: false after ~`budget` clocks (the caller
 // records an error and skips the work instead of hanging).
 Q35_DEV bool mbar_wait_bounded(uint32_t bar, uint32_t parity, long long budget) {
