@@ -34,7 +34,11 @@ pytestmark = pytest.mark.gpu
 
 SMALL = Qwen35Dims(layers=4, vocab=8192)
 LOGIT_NOISE = 0.16  # >= the largest |logit change| of the oracle under a GEMM-order change (0.154)
-LOGIT_NOISE_A8W8 = 0.28  # >= the same for A8W8 under an RMSNorm summation-order change (0.266)
+# A8W8: the largest teacher-forced gaps of the oracle against itself (tests/calibrate_logit_noise.py
+# and the RMSNorm order change) are 0.266 (RMSNorm summation order), 0.094 (attention as two
+# merged key halves) and 0.109 (the reference's two DeltaNet prefill algorithms); the GPU path
+# differs from the oracle by the first two at once, so the bound is their sum
+LOGIT_NOISE_A8W8 = 0.37
 
 
 def _near_top(tok, top, top_val, tok_val, noise=LOGIT_NOISE) -> bool:
