@@ -270,12 +270,16 @@ int q35_prefill_attention(const void* q, const void* k, const void* v, void* out
  * integration.py:360-372 for 4 query heads per KV head, head dim 256, queries at rows 0 .. L-1 of
  * the cache): q [B,Hq,L,256], k [B,Hkv,kv_len,256], vt = V transposed [B,Hkv,256,vt_stride] with
  * vt_stride a multiple of 64 >= L whose columns past L hold finite values -> out [B, L, Hq*256].
- * FP32 softmax; P enters the P.V product as a bf16 high part plus a bf16 remainder.
+ * FP32 softmax; P enters the P.V product as a bf16 high part plus a bf16 remainder. The
+ * workspace (256-byte aligned, zeroed before first use; the kernel leaves it zeroed) holds the
+ * partials of query blocks whose keys are split over two CTAs.
  * q35_prefill_attention_tc_error returns (and clears) the kernel's bounded-wait error word: 0, or
  * 1 + the shared-memory barrier slot whose wait gave up first. */
+size_t q35_prefill_attention_tc_workspace_size(int64_t batch, int64_t kv_heads, int64_t seq_len);
 int q35_prefill_attention_tc(const void* q, const void* k, const void* vt, void* out, int64_t batch,
                              int64_t q_heads, int64_t kv_heads, int64_t seq_len, int64_t kv_len,
-                             int64_t vt_stride, float scale, void* stream);
+                             int64_t vt_stride, float scale, void* workspace, size_t workspace_bytes,
+                             void* stream);
 int q35_prefill_attention_tc_error(void);
 
 /* ---------------------------------------------------------------- Gated DeltaNet */

@@ -59,7 +59,9 @@ int q35_qgkv_rope_positions_launch(const void* packed, const void* q_weight, con
                                    void* vt_out, int64_t vt_stride);
 int q35_prefill_attention_tc_launch(const void* q, const void* k, const void* vt, void* out, int64_t batch,
                                     int64_t q_heads, int64_t kv_heads, int64_t seq_len, int64_t kv_len,
-                                    int64_t vt_stride, float scale, cudaStream_t stream, bool pdl);
+                                    int64_t vt_stride, float scale, void* ws, size_t ws_bytes, cudaStream_t stream,
+                                    bool pdl);
+size_t q35_prefill_attention_tc_ws_bytes(int64_t batch, int64_t kv_heads, int64_t seq_len);
 int q35_gated_rms_strided_launch(const void* x, const void* gate, int gate_group, int64_t gate_stride,
                                  const void* weight, void* out, int64_t rows, int64_t width, float eps,
                                  cudaStream_t stream, bool pdl);
@@ -120,6 +122,8 @@ struct Buffers {
   float* p_chunk;     // chunked DeltaNet factors for one layer
   bf16* p_vt;         // V^T [seq][kv heads][head dim][keys padded to 64] (tcgen05 prefill attention;
                       // the workspace starts zeroed, so padding columns are finite)
+  void* p_attn_ws;    // its key-split partials and tickets (zeroed, left zeroed)
+  size_t p_attn_ws_bytes;
 };
 
 Buffers carve(const q35_decoder_desc& d, void* base, size_t* total) {
@@ -159,6 +163,10 @@ Buffers carve(const q35_decoder_desc& d, void* base, size_t* total) {
   // batched prefill: up to `nb` sequences sharing the L rows, each padded to whole chunks
   b.p_chunk = c.take<float>(q35_delta_chunk_workspace_bytes(1, d.lin_heads, L + 64 * nb) / sizeof(float));
   b.p_vt = c.take<bf16>((size_t)d.kv_heads * d.head_dim * (L + 64 * nb));
+  // the key-split workspace for nb sequences whose lengths add up to L: bounded by L / 32 + nb
+  // query blocks (the size function counts ceil(L / 32) blocks per sequence)
+  b.p_attn_ws_bytes = q35_prefill_attention_tc_ws_bytes(1, d.kv_heads, L + 32 * nb);
+  b.p_attn_ws = c.take<char>(b.p_attn_ws_bytes);
   *total = c.off + 256;
   return b;
 }
@@ -556,7 +564,7 @@ static int prefill_impl(q35_decoder* dec, const int64_t* ids, int64_t length, co
                                              pdl, tc_attn ? B.p_vt : nullptr, vt_stride));
       if (tc_attn)
         Q35_TRY(q35_prefill_attention_tc_launch(B.p_core, L.k_cache, B.p_vt, B.p_attn, nseq, d.q_heads, d.kv_heads, Lt,
-                                                d.max_len, vt_stride, scale, s, pdl));
+                                                d.max_len, vt_stride, scale, B.p_attn_ws, B.p_attn_ws_bytes, s, pdl));
       else
         Q35_TRY(q35_prefill_attention_launch(B.p_core, L.k_cache, L.v_cache, B.p_attn, nseq, d.q_heads, d.kv_heads,
                                              Lt, d.max_len, 0, d.head_dim, scale, s, pdl));

@@ -62,6 +62,12 @@ struct AttnTcParams {
   bf16* out;  // [B, L, Hq, 256]
   int Hq, Hkv, L, kv_len, vt_stride;
   float scale_log2;  // softmax scale x log2(e)
+  // key split: a block with more than `half_tiles` key tiles runs as two CTAs (tiles below /
+  // from half_tiles) whose partial O, maximum and sum meet in part / ml; the later one merges
+  int nqb, half_tiles;
+  float* part;        // [B * Hkv][nqb][2][256 dims][128 rows] (a warp's 32 rows are contiguous)
+  float* ml;          // [B * Hkv][nqb][2][128 rows][2]
+  unsigned* tickets;  // [B * Hkv][nqb], zero at rest (the merger resets its word)
 };
 // barrier slots in shared memory
 // barrier slots: TMA arrivals (Q, K[2], V[2]), MMA commits (S[2], P.V, V buffer free[2]), softmax
@@ -95,12 +101,16 @@ __global__ void __launch_bounds__(kAThreads, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + kOffBar);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kBars);
   auto bar = [&](int i) { return tc::smem_u32(&bars[i]); };
-  const int qb = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
+  const int qb = blockIdx.x % p.nqb, split = blockIdx.x / p.nqb, g = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5;
   const int q0 = qb * kAQ;
   const int L = p.L;
   const int nkeys = min(q0 + kAQ, L);  // keys any row of the block may see (causal)
-  const int nt = (nkeys + kAK - 1) / kAK;
+  const int nt_all = (nkeys + kAK - 1) / kAK;
+  const bool two = nt_all > p.half_tiles;  // this block runs as two CTAs
+  if (split == 1 && !two) return;        // (whole CTA: before any barrier or TMEM)
+  const int t0 = split ? p.half_tiles : 0;                    // first key tile of this CTA
+  const int nt = (two && split == 0) ? p.half_tiles : nt_all - t0;  // its tile count
 
   const bool mma_warp = warp == kASoft / 32, tma_warp = warp == kASoft / 32 + 1;
   if (mma_warp) tc::tmem_alloc(tmem_slot, kTmemCols);
@@ -136,12 +146,12 @@ __global__ void __launch_bounds__(kAThreads, 1)
         tc::mbar_expect_tx(bar(kBarK + i), kKBytes);
 #pragma unroll
         for (int sl = 0; sl < 4; ++sl)
-          tma_load_2d(sK + i * kKBytes + sl * (kAK * 128), &tmK, sl * 64, krow0 + t * kAK, bar(kBarK + i));
+          tma_load_2d(sK + i * kKBytes + sl * (kAK * 128), &tmK, sl * 64, krow0 + (t0 + t) * kAK, bar(kBarK + i));
       };
       auto load_v = [&](int t) {  // one box of 256 dims x 64 keys into buffer t & 1
         const int i = t & 1;
         tc::mbar_expect_tx(bar(kBarV + i), kVBytes);
-        tma_load_2d(sV + i * kVBytes, &tmV, t * kAK, vrow0, bar(kBarV + i));
+        tma_load_2d(sV + i * kVBytes, &tmV, (t0 + t) * kAK, vrow0, bar(kBarV + i));
       };
       auto issue_s = [&](int t) {  // S[t & 1] = Q K_t^T
         const uint32_t d = tmem + (uint32_t)((t & 1) * kAK);
@@ -229,7 +239,7 @@ __global__ void __launch_bounds__(kAThreads, 1)
       tc::tmem_wait_ld();
       ready(kBarRdyS + (t & 1));
       // (d) softmax of this row over the tile's 64 keys: this thread's 32, the partner's maximum
-      const int k0 = t * kAK + half * 32;
+      const int k0 = (t0 + t) * kAK + half * 32;
       float x[32];
   #pragma unroll
       for (int j = 0; j < 32; ++j) {
@@ -306,23 +316,66 @@ __global__ void __launch_bounds__(kAThreads, 1)
     xsum[half][row] = l_run;
     pair_sync();
     const float l_row = half ? xsum[0][row] + l_run : l_run + xsum[1][row];  // same order in both threads
-    const float inv = l_row > 0.f ? 1.0f / l_row : 0.f;
     const int hh = g * kAG + (row >> 5);
-  #pragma unroll 1
-    for (int c = half * (kAD / 2); c < (half + 1) * (kAD / 2); c += 32) {
-      uint32_t o[32];
-      tc::tmem_ld32(trow + kColO + c, o);
-      if (ok && qi < L) {
-        bf16* dst = p.out + (((int64_t)b * L + qi) * p.Hq + hh) * kAD + c;
+    auto store_row = [&](int c, const float* o32, float scale) {  // 32 dims of this row, bf16
+      if (!(ok && qi < L)) return;
+      bf16* dst = p.out + (((int64_t)b * L + qi) * p.Hq + hh) * kAD + c;
   #pragma unroll
-        for (int j = 0; j < 32; j += 8) {
-          uint4 v;
-          v.x = pack_bf16(__uint_as_float(o[j]) * inv, __uint_as_float(o[j + 1]) * inv);
-          v.y = pack_bf16(__uint_as_float(o[j + 2]) * inv, __uint_as_float(o[j + 3]) * inv);
-          v.z = pack_bf16(__uint_as_float(o[j + 4]) * inv, __uint_as_float(o[j + 5]) * inv);
-          v.w = pack_bf16(__uint_as_float(o[j + 6]) * inv, __uint_as_float(o[j + 7]) * inv);
-          *reinterpret_cast<uint4*>(dst + j) = v;
+      for (int j = 0; j < 32; j += 8) {
+        uint4 v;
+        v.x = pack_bf16(o32[j] * scale, o32[j + 1] * scale);
+        v.y = pack_bf16(o32[j + 2] * scale, o32[j + 3] * scale);
+        v.z = pack_bf16(o32[j + 4] * scale, o32[j + 5] * scale);
+        v.w = pack_bf16(o32[j + 6] * scale, o32[j + 7] * scale);
+        *reinterpret_cast<uint4*>(dst + j) = v;
+      }
+    };
+    if (!two) {
+      const float inv = l_row > 0.f ? 1.0f / l_row : 0.f;
+  #pragma unroll 1
+      for (int c = half * (kAD / 2); c < (half + 1) * (kAD / 2); c += 32) {
+        uint32_t o[32];
+        tc::tmem_ld32(trow + kColO + c, o);
+        store_row(c, reinterpret_cast<const float*>(o), inv);
+      }
+    } else {
+      // this part's un-normalised O (its own reference maximum), maximum and sum to global
+      const int64_t slot = ((int64_t)(b * p.Hkv + g) * p.nqb + qb) * 2;
+      float* my = p.part + (slot + split) * kAD * kAM + row;
+  #pragma unroll 1
+      for (int c = half * (kAD / 2); c < (half + 1) * (kAD / 2); c += 32) {
+        uint32_t o[32];
+        tc::tmem_ld32(trow + kColO + c, o);
+  #pragma unroll
+        for (int j = 0; j < 32; ++j) my[(c + j) * kAM] = __uint_as_float(o[j]);
+      }
+      if (half == 0) {
+        p.ml[((slot + split) * kAM + row) * 2] = m_run;
+        p.ml[((slot + split) * kAM + row) * 2 + 1] = l_row;
+      }
+      // the second of the two CTAs to finish merges both parts in split order
+      __shared__ unsigned arrival;
+      __threadfence();
+      asm volatile("bar.sync 5, %0;" ::"n"(kASoft) : "memory");
+      if (tid == 0) arrival = atomicAdd(&p.tickets[slot / 2], 1u);
+      asm volatile("bar.sync 5, %0;" ::"n"(kASoft) : "memory");
+      if (arrival == 1) {
+        __threadfence();
+        const float* pa = p.part + slot * kAD * kAM + row;
+        const float* pb = p.part + (slot + 1) * kAD * kAM + row;
+        const float ma = __ldcg(p.ml + (slot * kAM + row) * 2), la = __ldcg(p.ml + (slot * kAM + row) * 2 + 1);
+        const float mb = __ldcg(p.ml + ((slot + 1) * kAM + row) * 2), lb = __ldcg(p.ml + ((slot + 1) * kAM + row) * 2 + 1);
+        const float m = fmaxf(ma, mb), wa = ex2(ma - m), wb = ex2(mb - m);
+        const float l = la * wa + lb * wb;
+        const float inv = l > 0.f ? 1.0f / l : 0.f;
+  #pragma unroll 1
+        for (int c = half * (kAD / 2); c < (half + 1) * (kAD / 2); c += 32) {
+          float o[32];
+  #pragma unroll
+          for (int j = 0; j < 32; ++j) o[j] = __ldcg(pa + (c + j) * kAM) * wa + __ldcg(pb + (c + j) * kAM) * wb;
+          store_row(c, o, inv);
         }
+        if (tid == 0) p.tickets[slot / 2] = 0u;  // rest state for the next launch
       }
     }
   }
@@ -363,12 +416,42 @@ bool make_map_bf16(CUtensorMap* m, const void* ptr, uint64_t rows, uint64_t cols
 
 }  // namespace
 
+namespace {
+
+// Key split: blocks with more than half the longest block's key tiles run as two CTAs, when the
+// longest block has at least 4 tiles (256 keys).
+int half_tiles_for(int64_t seq_len) {
+  const int ntmax = (int)((seq_len + kAK - 1) / kAK);
+  return ntmax >= 4 ? (ntmax + 1) / 2 : ntmax;
+}
+
+struct TcWs {
+  size_t tickets, ml, part, total;
+};
+TcWs tc_ws_layout(int64_t batch, int64_t kv_heads, int64_t seq_len) {
+  const int64_t slots = batch * kv_heads * ((seq_len + kAQ - 1) / kAQ);
+  TcWs w;
+  w.tickets = 0;
+  w.ml = (slots * sizeof(unsigned) + 255) & ~(size_t)255;
+  w.part = (w.ml + (size_t)slots * 2 * kAM * 2 * sizeof(float) + 255) & ~(size_t)255;
+  w.total = w.part + (size_t)slots * 2 * kAM * kAD * sizeof(float);
+  return w;
+}
+
+}  // namespace
+
+size_t q35_prefill_attention_tc_ws_bytes(int64_t batch, int64_t kv_heads, int64_t seq_len) {
+  return tc_ws_layout(batch, kv_heads, seq_len).total;
+}
+
 // The decoder's causal prefill attention on tcgen05. q [B, Hq, L, 256], k the cache
 // [B, Hkv, kv_len, 256], vt = V^T [B, Hkv, 256, vt_stride] with vt_stride a multiple of 64 that
-// is >= L (columns past L hold finite values), out [B, L, Hq, 256]; Hq = 4 Hkv.
+// is >= L (columns past L hold finite values), out [B, L, Hq, 256]; Hq = 4 Hkv. `ws` (zeroed
+// before first use, left zeroed) holds the key-split partials.
 int q35_prefill_attention_tc_launch(const void* q, const void* k, const void* vt, void* out, int64_t batch,
                                     int64_t q_heads, int64_t kv_heads, int64_t seq_len, int64_t kv_len,
-                                    int64_t vt_stride, float scale, cudaStream_t stream, bool pdl) {
+                                    int64_t vt_stride, float scale, void* ws, size_t ws_bytes, cudaStream_t stream,
+                                    bool pdl) {
   Q35_REQUIRE(q && k && vt && out, "prefill_attention_tc: null pointer");
   Q35_REQUIRE(q_heads == kAG * kv_heads, "prefill_attention_tc: %lld query heads for %lld KV heads (needs 4 per KV head)",
               (long long)q_heads, (long long)kv_heads);
@@ -378,6 +461,9 @@ int q35_prefill_attention_tc_launch(const void* q, const void* k, const void* vt
   Q35_REQUIRE(Q35_ALIGNED(q, 16) && Q35_ALIGNED(k, 16) && Q35_ALIGNED(vt, 16) && Q35_ALIGNED(out, 16),
               "prefill_attention_tc: 16-byte alignment");
   if (batch * seq_len == 0) return Q35_OK;
+  const TcWs w = tc_ws_layout(batch, kv_heads, seq_len);
+  Q35_REQUIRE(ws && Q35_ALIGNED(ws, 256) && ws_bytes >= w.total,
+              "prefill_attention_tc: workspace of %zu bytes (256-byte aligned) needed", w.total);
   static Q35PerDevice<bool> attr;
   attr.get([] {
     cudaFuncSetAttribute(prefill_attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kAttnTcSmem);
@@ -390,20 +476,38 @@ int q35_prefill_attention_tc_launch(const void* q, const void* k, const void* vt
       !make_map_bf16(&mk, k, (uint64_t)batch * kv_heads * kv_len, kAD, kAK) ||
       !make_map_bf16(&mv, vt, (uint64_t)batch * kv_heads * kAD, (uint64_t)vt_stride, kAD))
     return q35_fail(Q35_ECUDA, "prefill_attention_tc: tensor map encoding failed");
-  AttnTcParams prm{(bf16*)out, (int)q_heads, (int)kv_heads, (int)seq_len, (int)kv_len, (int)vt_stride,
-                   scale * 1.4426950408889634f};
-  const dim3 grid((unsigned)((seq_len + kAQ - 1) / kAQ), (unsigned)kv_heads, (unsigned)batch);
+  const int nqb = (int)((seq_len + kAQ - 1) / kAQ), half_tiles = half_tiles_for(seq_len);
+  const int ntmax = (int)((seq_len + kAK - 1) / kAK);
+  char* base = static_cast<char*>(ws);
+  AttnTcParams prm{(bf16*)out,
+                   (int)q_heads,
+                   (int)kv_heads,
+                   (int)seq_len,
+                   (int)kv_len,
+                   (int)vt_stride,
+                   scale * 1.4426950408889634f,
+                   nqb,
+                   half_tiles,
+                   reinterpret_cast<float*>(base + w.part),
+                   reinterpret_cast<float*>(base + w.ml),
+                   reinterpret_cast<unsigned*>(base + w.tickets)};
+  const dim3 grid((unsigned)(nqb * (ntmax > half_tiles ? 2 : 1)), (unsigned)kv_heads, (unsigned)batch);
   const cudaError_t e =
       q35_launch(prefill_attn_tc_kernel, grid, dim3(kAThreads), kAttnTcSmem, stream, pdl, mq, mk, mv, prm);
   if (e != cudaSuccess) return q35_fail(Q35_ECUDA, "prefill_attention_tc launch: %s", cudaGetErrorString(e));
   return Q35_OK;
 }
 
+extern "C" size_t q35_prefill_attention_tc_workspace_size(int64_t batch, int64_t kv_heads, int64_t seq_len) {
+  return q35_prefill_attention_tc_ws_bytes(batch, kv_heads, seq_len);
+}
+
 extern "C" int q35_prefill_attention_tc(const void* q, const void* k, const void* vt, void* out, int64_t batch,
                                         int64_t q_heads, int64_t kv_heads, int64_t seq_len, int64_t kv_len,
-                                        int64_t vt_stride, float scale, void* stream) {
+                                        int64_t vt_stride, float scale, void* workspace, size_t workspace_bytes,
+                                        void* stream) {
   return q35_prefill_attention_tc_launch(q, k, vt, out, batch, q_heads, kv_heads, seq_len, kv_len, vt_stride, scale,
-                                         (cudaStream_t)stream, false);
+                                         workspace, workspace_bytes, (cudaStream_t)stream, false);
 }
 
 extern "C" int q35_prefill_attention_tc_error(void) {

@@ -356,8 +356,10 @@ def prefill_attention_tc(q, k, v, scale: float, kv_len: int | None = None) -> to
     vt = torch.zeros((b, v.shape[1], dim, stride), device=v.device, dtype=BF16)
     vt[..., :length] = v[:, :, :length].transpose(-1, -2)
     out = torch.empty((b, length, hq * dim), device=q.device, dtype=BF16)
+    nbytes = int(L.load().q35_prefill_attention_tc_workspace_size(b, k.shape[1], length))
+    ws = torch.zeros(nbytes, device=q.device, dtype=torch.uint8)
     L.call("q35_prefill_attention_tc", L.ptr(q), L.ptr(k), L.ptr(vt), L.ptr(out), b, hq, k.shape[1], length,
-           k.shape[2] if kv_len is None else kv_len, stride, scale, _s(q))
+           k.shape[2] if kv_len is None else kv_len, stride, scale, L.ptr(ws), nbytes, _s(q))
     return out
 
 

@@ -111,7 +111,8 @@ _SIGS = {
     "q35_attn_decode_workspace_size": (SZ, [I64, I64, I64, I64, I64]),
     "q35_attn_decode": (INT, [P, P, P, P, P, P, P, P, P, I64, I64, I64, I64, I64, I64, F32, P, SZ, P]),
     "q35_prefill_attention": (INT, [P, P, P, P, I64, I64, I64, I64, I64, I64, I64, F32, P]),
-    "q35_prefill_attention_tc": (INT, [P, P, P, P, I64, I64, I64, I64, I64, I64, F32, P]),
+    "q35_prefill_attention_tc": (INT, [P, P, P, P, I64, I64, I64, I64, I64, I64, F32, P, SZ, P]),
+    "q35_prefill_attention_tc_workspace_size": (SZ, [I64, I64, I64]),
     "q35_prefill_attention_tc_error": (INT, []),
     "q35_causal_conv1d": (INT, [P, P, P, P, I64, I64, I64, I64, I64, P]),
     "q35_delta_recurrent": (INT, [P, P, P, P, P, P, I64, I64, I64, I64, I64, P]),

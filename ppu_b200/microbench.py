@@ -255,8 +255,10 @@ def run(kernels: list[str], reps: int, layers: int = 24, a8w8: bool = False):
             # the decoder's tcgen05 kernel, V^T prepared once (the decoder writes it with the cache)
             vt = vv.transpose(-1, -2).contiguous()
             o_tc = torch.empty(1, Lp, 8 * 256, device=dev, dtype=torch.bfloat16)
+            nws = int(L.load().q35_prefill_attention_tc_workspace_size(1, 2, Lp))
+            ws_tc = torch.zeros(nws, device=dev, dtype=torch.uint8)
             t = _time(lambda i: L.call("q35_prefill_attention_tc", L.ptr(q), L.ptr(kk), L.ptr(vt), L.ptr(o_tc), 1, 8, 2,
-                                       Lp, Lp, Lp, 0.0625, L.stream_of(dev)), reps)
+                                       Lp, Lp, Lp, 0.0625, L.ptr(ws_tc), nws, L.stream_of(dev)), reps)
             report("prefill_attn_tc_1024", t, flops=4 * 8 * 256 * Lp * Lp // 2)
         elif name == "conv_prefill":
             Lp = 1024

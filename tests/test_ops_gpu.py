@@ -373,6 +373,31 @@ def test_prefill_attention_tc(batch, length, extra):
     assert rel_err(out, ref.cpu()) < 3e-3
 
 
+def test_prefill_attention_tc_workspace_reuse():
+    """Blocks whose keys are split over two CTAs merge through the workspace; its ticket words
+    return to zero, so back-to-back calls on one workspace give identical outputs."""
+    length = 700
+    q = cu(randn(1, 8, length, 256, seed=71))
+    k = cu(randn(1, 2, length, 256, seed=72))
+    v = cu(randn(1, 2, length, 256, seed=73))
+    stride = (length + 63) // 64 * 64
+    vt = torch.zeros((1, 2, 256, stride), device=DEV, dtype=BF16)
+    vt[..., :length] = v.transpose(-1, -2)
+    nbytes = int(L.load().q35_prefill_attention_tc_workspace_size(1, 2, length))
+    ws = torch.zeros(nbytes, device=DEV, dtype=torch.uint8)
+    outs = []
+    for _ in range(2):
+        out = torch.empty((1, length, 8 * 256), device=DEV, dtype=BF16)
+        L.call("q35_prefill_attention_tc", L.ptr(q), L.ptr(k), L.ptr(vt), L.ptr(out), 1, 8, 2, length, length, stride,
+               0.0625, L.ptr(ws), nbytes, 0)
+        torch.cuda.synchronize()
+        outs.append(out)
+        assert int(L.load().q35_prefill_attention_tc_error()) == 0
+    assert torch.equal(outs[0], outs[1])
+    assert int(ws[: 2 * 22 * 4].view(torch.int32).abs().sum()) == 0  # the 2 x 22 ticket words
+    assert rel_err(outs[0], O.causal_attention(q.cpu(), k.cpu(), v.cpu(), 0.0625)) < 3e-3
+
+
 # ------------------------------------------------------------------ DeltaNet
 def _delta_inputs(L_, seed=0):
     """16 heads x 128, conv K=4, alpha = exp(-softplus(N(0,1))),
