@@ -78,6 +78,79 @@ __global__ void __launch_bounds__(kD) qgkv_rope_kernel(
   }
 }
 
+// Prefill form of the decoder (positions, not tables; rotary_dim 64, Qwen3.5's): one warp per
+// (token, head), lane l holding dims l + 32 i (i < 8), so the norm's sum is formed exactly as
+// block_sum forms it in qgkv_rope_kernel (a butterfly over each 32-dim group, the 8 group sums in
+// order) and the RoPE partner of dim d (d +- 32) sits in the same lane: no barrier, and the
+// outputs are bit-identical to the one-CTA-per-token kernel.
+__global__ void __launch_bounds__(256) qgkv_rope_warp_kernel(
+    const bf16* __restrict__ packed, const bf16* __restrict__ qw, const bf16* __restrict__ kw,
+    const float* __restrict__ inv_freq, bf16* __restrict__ q_out, bf16* __restrict__ k_out, bf16* __restrict__ v_out,
+    const int64_t* __restrict__ cache_start, int batch, int L, int Hq, int Hkv, int rot, int kv_len, float eps,
+    const int64_t* __restrict__ pos3, int sec_h, int sec_w, bf16* __restrict__ vt_out, int vt_stride) {
+  pdl_wait();  // programmatic dependent launch: inputs only after the previous kernel
+  pdl_launch_dependents();
+  constexpr int NG = kD / 32;  // dims per lane
+  const int lane = threadIdx.x & 31;
+  const int64_t pair = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int heads = Hq + Hkv;
+  if (pair >= (int64_t)batch * L * heads) return;
+  const int h = (int)(pair % heads);
+  const int bt = (int)(pair / heads), b = bt / L, t = bt - b * L;
+  const bool is_q = h < Hq;
+  const int stride = 2 * Hq * kD + 2 * Hkv * kD;
+  const bf16* row = packed + (int64_t)bt * stride;
+  const int off = is_q ? h * 2 * kD : 2 * Hq * kD + (h - Hq) * kD;
+  const int64_t start = cache_start ? *cache_start : 0;
+  float x[NG], wv[NG];
+#pragma unroll
+  for (int i = 0; i < NG; ++i) {
+    x[i] = bf2f(row[off + lane + 32 * i]);
+    wv[i] = bf2f(is_q ? qw[lane + 32 * i] : kw[lane + 32 * i]);
+  }
+  float var = 0.f;
+#pragma unroll
+  for (int i = 0; i < NG; ++i) var += warp_sum(x[i] * x[i]);
+  var /= (float)kD;
+  float nrm[NG];
+#pragma unroll
+  for (int i = 0; i < NG; ++i) nrm[i] = rbf(x[i] * rsqrt_ieee(var + eps) * (1.0f + wv[i]));
+  constexpr int half = 32;  // rot / 2
+  float y[NG];
+#pragma unroll
+  for (int i = 0; i < NG; ++i) y[i] = nrm[i];
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {  // dims lane (partner lane + 32, negated) and lane + 32 (partner lane)
+    const int d = lane + 32 * i;
+    int64_t pos = start + t;
+    if (pos3) {  // interleaved M-RoPE: frequency j takes the height / width axis at j % 3 == 1 / 2
+      const int j = d % half;
+      const int axis = (j % 3 == 1 && j < 3 * sec_h) ? 1 : (j % 3 == 2 && j < 3 * sec_w) ? 2 : 0;
+      pos = pos3[((int64_t)axis * batch + b) * L + t];  // [3, batch, L]
+    }
+    float c, sn;
+    rope_cs(d, half, (float)pos, inv_freq, c, sn);
+    const float partner = i == 0 ? -nrm[1] : nrm[0];
+    y[i] = rbf(rbf(nrm[i] * c) + rbf(partner * sn));
+  }
+  if (is_q) {
+    bf16* o = q_out + (((int64_t)b * Hq + h) * L + t) * kD + lane;
+#pragma unroll
+    for (int i = 0; i < NG; ++i) o[32 * i] = f2bf(y[i]);
+  } else if (start + t >= 0 && start + t < kv_len) {  // device-side start: never write past the cache
+    const int kh = h - Hq;
+    const int64_t o = (((int64_t)b * Hkv + kh) * kv_len + start + t) * kD + lane;
+#pragma unroll
+    for (int i = 0; i < NG; ++i) {
+      k_out[o + 32 * i] = f2bf(y[i]);
+      const bf16 vv = row[2 * Hq * kD + Hkv * kD + kh * kD + lane + 32 * i];
+      v_out[o + 32 * i] = vv;
+      if (vt_out != nullptr && start + t < vt_stride)
+        vt_out[(((int64_t)b * Hkv + kh) * kD + lane + 32 * i) * vt_stride + start + t] = vv;
+    }
+  }
+}
+
 // ============================================================================ prefill attention, tensor cores
 // FlashAttention-style causal GQA prefill on mma.sync m16n8k16 (bf16 in, FP32 accumulate).
 // CTA = (16 query rows, group g of G query heads): warp w handles query head g * G + w, so each K/V tile in
@@ -347,12 +420,27 @@ extern "C" int q35_qgkv_norm_rope(const void* packed, const void* q_weight, cons
 // With pos3 (int64 [3, batch, seq_len]), the positions are 3-axis M-RoPE positions interleaved
 // by (sec_h, sec_w) frequency pairs (Transformers apply_interleaved_mrope). With vt_out, V is also
 // written transposed: vt_out [batch, kv_heads, 256, vt_stride].
+namespace {
+// the warp kernel is built for rotary_dim 64 (RoPE partners 32 dims apart, in one lane)
+bool rot_ok_for_warp_kernel(int64_t rot) { return rot == 64; }
+}  // namespace
+
 int q35_qgkv_rope_positions_launch(const void* packed, const void* q_weight, const void* k_weight,
                                    const float* inv_freq, void* q_out, void* k_out, void* v_out,
                                    const int64_t* cache_start, int64_t batch, int64_t seq_len, int64_t q_heads,
                                    int64_t kv_heads, int64_t rotary_dim, int64_t kv_len, float eps,
                                    cudaStream_t stream, const int64_t* pos3, int sec_h, int sec_w, bool pdl,
                                    void* vt_out, int64_t vt_stride) {
+  if (rot_ok_for_warp_kernel(rotary_dim)) {
+    const int64_t pairs = batch * seq_len * (q_heads + kv_heads);
+    const cudaError_t e = q35_launch(
+        qgkv_rope_warp_kernel, dim3((unsigned)((pairs + 7) / 8)), dim3(256), 0, stream, pdl, (const bf16*)packed,
+        (const bf16*)q_weight, (const bf16*)k_weight, inv_freq, (bf16*)q_out, (bf16*)k_out, (bf16*)v_out, cache_start,
+        (int)batch, (int)seq_len, (int)q_heads, (int)kv_heads, (int)rotary_dim, (int)kv_len, eps, pos3, sec_h, sec_w,
+        (bf16*)vt_out, (int)vt_stride);
+    if (e != cudaSuccess) return q35_fail(Q35_ECUDA, "qgkv_rope_positions launch: %s", cudaGetErrorString(e));
+    return Q35_OK;
+  }
   const cudaError_t e = q35_launch(
       qgkv_rope_kernel<false>, dim3((unsigned)(batch * seq_len)), dim3(kD), 0, stream, pdl, (const bf16*)packed,
       (const bf16*)q_weight, (const bf16*)k_weight, (const bf16*)nullptr, (const bf16*)nullptr, inv_freq, (int64_t)0,
