@@ -85,51 +85,38 @@ __global__ void __launch_bounds__(kRowThreads) rms_rows2048_kernel(const bf16* _
 
 // Width 128 (the DeltaNet head): one warp per row, four consecutive values per lane in 8-byte
 // loads and stores, x read once.
-constexpr int kGatedRows = 4;  // rows per warp of the width-128 gated RMSNorm
 __global__ void gated_rms128_kernel(const bf16* __restrict__ x, const bf16* __restrict__ gate,
                                     const bf16* __restrict__ w, bf16* __restrict__ out, int64_t rows, float eps,
                                     int gate_group, int64_t gate_stride) {
   pdl_wait();  // programmatic dependent launch: inputs only after the previous kernel
   pdl_launch_dependents();
   constexpr int kW = 128;
-  // kGatedRows rows per warp, every row's loads issued before the first is used
-  const int64_t row0 = ((int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * kGatedRows;
+  const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
-  if (row0 >= rows) return;
+  if (row >= rows) return;
   auto unpack4 = [](uint2 v, float (&f)[4]) {
     f[0] = __uint_as_float(v.x << 16);
     f[1] = __uint_as_float(v.x & 0xFFFF0000u);
     f[2] = __uint_as_float(v.y << 16);
     f[3] = __uint_as_float(v.y & 0xFFFF0000u);
   };
-  uint2 xv[kGatedRows], gv[kGatedRows];
-#pragma unroll
-  for (int i = 0; i < kGatedRows; ++i) {
-    const int64_t row = row0 + i < rows ? row0 + i : row0;
-    xv[i] = *reinterpret_cast<const uint2*>(x + row * kW + 4 * lane);
-    gv[i] = *reinterpret_cast<const uint2*>(gate + (row / gate_group) * gate_stride + (row % gate_group) * kW + 4 * lane);
-  }
-  float wf[4];
+  float xf[4], gf[4], wf[4];
+  unpack4(*reinterpret_cast<const uint2*>(x + row * kW + 4 * lane), xf);
+  unpack4(*reinterpret_cast<const uint2*>(gate + (row / gate_group) * gate_stride + (row % gate_group) * kW + 4 * lane),
+          gf);
   unpack4(*reinterpret_cast<const uint2*>(w + 4 * lane), wf);
+  float ss = 0.f;
 #pragma unroll
-  for (int i = 0; i < kGatedRows; ++i) {
-    const int64_t row = row0 + i;
-    float xf[4], gf[4];
-    unpack4(xv[i], xf);
-    unpack4(gv[i], gf);
-    float ss = 0.f;
+  for (int j = 0; j < 4; ++j) ss += xf[j] * xf[j];
+  const float r = rsqrt_ieee(warp_sum(ss) / (float)kW + eps);
+  __align__(8) bf16 o[4];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) ss += xf[j] * xf[j];
-    const float r = rsqrt_ieee(warp_sum(ss) / (float)kW + eps);
-    __align__(8) bf16 o[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float nrm = rbf(xf[j] * r);
-      const float wt = rbf(nrm * wf[j]);
-      o[j] = f2bf(wt * silu_f(gf[j]));
-    }
-    if (row < rows) *reinterpret_cast<uint2*>(out + row * kW + 4 * lane) = *reinterpret_cast<const uint2*>(o);
+  for (int j = 0; j < 4; ++j) {
+    const float nrm = rbf(xf[j] * r);
+    const float wt = rbf(nrm * wf[j]);
+    o[j] = f2bf(wt * silu_f(gf[j]));
   }
+  *reinterpret_cast<uint2*>(out + row * kW + 4 * lane) = *reinterpret_cast<const uint2*>(o);
 }
 
 // One warp per row: bf16(bf16(bf16(norm(x)) * w) * silu(gate)) (kernels.py:115-155).
@@ -450,8 +437,7 @@ int q35_gated_rms_strided_launch(const void* x, const void* gate, int gate_group
   const unsigned blocks = (unsigned)((rows + rows_per_block - 1) / rows_per_block);
   if (width == 128 && gate_stride % 4 == 0 && Q35_ALIGNED(x, 8) && Q35_ALIGNED(gate, 8) && Q35_ALIGNED(weight, 8) &&
       Q35_ALIGNED(out, 8)) {
-    const unsigned blocks128 = (unsigned)((rows + rows_per_block * kGatedRows - 1) / (rows_per_block * kGatedRows));
-    const cudaError_t e = q35_launch(gated_rms128_kernel, dim3(blocks128), dim3(32 * rows_per_block), 0, stream, pdl,
+    const cudaError_t e = q35_launch(gated_rms128_kernel, dim3(blocks), dim3(32 * rows_per_block), 0, stream, pdl,
                                      (const bf16*)x, (const bf16*)gate, (const bf16*)weight, (bf16*)out, rows, eps,
                                      gate_group, gate_stride);
     if (e != cudaSuccess) return q35_fail(Q35_ECUDA, "gated_rms launch: %s", cudaGetErrorString(e));
