@@ -678,16 +678,17 @@ __global__ void __launch_bounds__(kThreads, 1) delta_chunk_scan_kernel(ScanParam
 // in TMEM. 3xTF32: the A = [Qe | P] and B = [S_c ; Vn] operands are staged as TF32 high / low
 // parts (K-major, 128-byte swizzle) and the three products hi.hi, lo.hi and hi.lo accumulate in
 // one TMEM tile, so the result keeps FP32-level accuracy (the dropped lo.lo term is ~2^-22).
-// K runs in two halves of 96 through one 96 KB staging area (two CTAs per SM): the second half's
-// loads are in flight while the first half's MMAs run.
+// K runs in three parts of 64 through one 64 KB staging area (three CTAs per SM): each part's loads
+// are in flight while the previous part's MMAs run.
 constexpr int kOutThreads = 256;            // staging; warps 0-3 also read one TMEM lane quarter each
-constexpr int kOutBatch = 6;                // 16-byte loads per operand in flight per thread
+constexpr int kOutParts = 3;                // K in three parts through one staging area
+constexpr int kOutBatch = 4;                // 16-byte loads per operand in flight per thread
 constexpr int kOutK = kD + kC;              // 192
-constexpr int kOutKH = kOutK / 2;           // 96: K per half
-constexpr int kOutSlabs = kOutKH / 32;      // 3 slabs of 32 tf32 (128 bytes) per half
+constexpr int kOutKH = kOutK / kOutParts;   // 64: K per part
+constexpr int kOutSlabs = kOutKH / 32;      // 2 slabs of 32 tf32 (128 bytes) per part
 constexpr int kOutN = 64;                   // value columns per CTA
 constexpr uint32_t kOutSlabBytes = 64 * 128;  // 64 rows of 128 bytes (A: tokens, B: value columns)
-constexpr uint32_t kOutTile = kOutSlabs * kOutSlabBytes;  // 24 KB per operand part
+constexpr uint32_t kOutTile = kOutSlabs * kOutSlabBytes;  // 16 KB per operand part
 constexpr size_t kOutSmem = 4 * (size_t)kOutTile + 1024 + 64;
 constexpr long long kOutWaitBudget = 2000000000LL;
 
@@ -697,7 +698,7 @@ struct OutParams {
   int L, H, NC;
 };
 
-__global__ void __launch_bounds__(kOutThreads, 2) delta_chunk_out_kernel(OutParams p) {
+__global__ void __launch_bounds__(kOutThreads, 3) delta_chunk_out_kernel(OutParams p) {
   pdl_wait();  // programmatic dependent launch: inputs only after the previous kernel
   pdl_launch_dependents();
   extern __shared__ __align__(16) unsigned char out_smem_raw[];
@@ -732,9 +733,9 @@ __global__ void __launch_bounds__(kOutThreads, 2) delta_chunk_out_kernel(OutPara
     *reinterpret_cast<uint4*>(hi + off) = make_uint4(h4[0], h4[1], h4[2], h4[3]);
     *reinterpret_cast<uint4*>(lo + off) = make_uint4(l4[0], l4[1], l4[2], l4[3]);
   };
-  // one batch of kOutBatch 16-byte loads per operand per thread covers a half of K
-  constexpr int kItems = 64 * (kOutKH / 4);  // 16-byte items per operand per half
-  static_assert(kItems == kOutThreads * kOutBatch, "one batch per half");
+  // one batch of kOutBatch 16-byte loads per operand per thread covers a part of K
+  constexpr int kItems = 64 * (kOutKH / 4);  // 16-byte items per operand per part
+  static_assert(kItems == kOutThreads * kOutBatch, "one batch per part");
   float4 a[kOutBatch], bv[kOutBatch];
   auto load_half = [&](int kh) {
 #pragma unroll
@@ -752,7 +753,7 @@ __global__ void __launch_bounds__(kOutThreads, 2) delta_chunk_out_kernel(OutPara
 #pragma unroll
     for (int u = 0; u < kOutBatch; ++u) {
       const int i = u * kOutThreads + tid;
-      const int r = i / (kOutKH / 4), k4 = (i % (kOutKH / 4)) * 4;  // K offset within the half
+      const int r = i / (kOutKH / 4), k4 = (i % (kOutKH / 4)) * 4;  // K offset within the part
       stage(A_hi, A_lo, r, k4, a[u]);
       stage(B_hi, B_lo, r, k4, bv[u]);
     }
@@ -781,17 +782,21 @@ __global__ void __launch_bounds__(kOutThreads, 2) delta_chunk_out_kernel(OutPara
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = *tmem_slot;
   if (tid == 0) mma_half(tmem, true);
-  load_half(1);  // in flight while the first half's MMAs read the staging area
-  // every thread waits for those MMAs before overwriting their operands
-  bool ok = tc::mbar_wait_bounded(tc::smem_u32(bar), 0, kOutWaitBudget);
-  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-  stage_half();
-  __syncthreads();
-  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-  if (tid == 0) mma_half(tmem, false);
+  bool ok = true;
+#pragma unroll 1
+  for (int part = 1; part < kOutParts; ++part) {
+    load_half(part);  // in flight while the previous part's MMAs read the staging area
+    // every thread waits for those MMAs before overwriting their operands
+    ok = tc::mbar_wait_bounded(tc::smem_u32(bar), (uint32_t)(part - 1) & 1u, kOutWaitBudget) && ok;
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    stage_half();
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    if (tid == 0) mma_half(tmem, false);
+  }
   __syncwarp();
   if (warp < 4) {  // TMEM lane quarters
-    ok = tc::mbar_wait_bounded(tc::smem_u32(bar), 1, kOutWaitBudget) && ok;
+    ok = tc::mbar_wait_bounded(tc::smem_u32(bar), (uint32_t)(kOutParts - 1) & 1u, kOutWaitBudget) && ok;
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     // M = 64: token row 16 q + i sits in TMEM lane 32 q + i (i < 16) of warp q's lane quarter
     uint32_t v0[32], v1[32];
