@@ -302,13 +302,6 @@ Q35_DEV TilePlan tile_plan(const PkOp& op) {
   t.spt = op.k / kPkKChunk;
   return t;
 }
-// Global weight row of stage row r in tile `tile`, or -1 past the CTA's units.
-Q35_DEV int64_t tile_row(const PkOp& op, const TilePlan& tp, int tile, int r) {
-  const int uu = r % tp.upt, half = r / tp.upt;  // half 1 = up rows (SwiGLU)
-  const int unit = tp.u0 + tile * tp.upt + uu;
-  if (unit >= tp.u1) return -1;
-  return (int64_t)half * op.n_out + unit;
-}
 
 // ------------------------------------------------------------------------------ producer
 Q35_DEV void producer(const PkParams& p, PkShared& S, unsigned char* ring) {
