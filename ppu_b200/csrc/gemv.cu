@@ -96,7 +96,8 @@ Q35_DEV void build_input(const GemvParams& p, int k, bf16* xs, int8_t* xq, float
 // beyond block_max. Values, scale and codes equal build_input's: the same expressions in the
 // same order per element, and the maximum does not depend on the order it is taken in.
 template <int PRO, int K>
-Q35_DEV void build_input_q8(const GemvParams& p, int8_t* xq, float* sx_out, float* red) {
+Q35_DEV void build_input_q8(const GemvParams& p, int8_t* xq, float* sx_out, float* red,
+                            const uint4 (&nwr)[(K / 8 + kThreads - 1) / kThreads]) {
   constexpr int NV = K / 8, CPT = (NV + kThreads - 1) / kThreads;
   const bf16* src = p.input;
   if (PRO == Q35_PRO_EMBED) {
@@ -130,7 +131,7 @@ Q35_DEV void build_input_q8(const GemvParams& p, int8_t* xq, float* sx_out, floa
       const int i = threadIdx.x + j * kThreads;
       if (i < NV) {
         float w[8];
-        unpack_bf16x8(reinterpret_cast<const uint4*>(p.norm_w)[i], w);
+        unpack_bf16x8(nwr[j], w);
 #pragma unroll
         for (int e = 0; e < 8; ++e) f[j][e] = bf2f(f2bf(f[j][e] * r * (1.0f + w[e])));
       }
@@ -339,18 +340,24 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_fast_kernel(GemvParams p) {
     if (2 + q < n_iter) stage(2 + q, q);
   asm volatile("cp.async.commit_group;" ::: "memory");
   constexpr int NCPT = (K / 8 + kThreads - 1) / kThreads;
-  uint4 nwr[NCPT];  // bf16 norm weights: constants, in registers before the wait
+  uint4 nwr[NCPT];  // norm weights: constants, in registers before the wait
   if (PRO != Q35_PRO_PLAIN) {
-    if (INT8) {  // warm L2 while the producer drains
-      for (int i = threadIdx.x; i < K / 64; i += kThreads)
-        asm volatile("prefetch.global.L2 [%0];" ::"l"(p.norm_w + 64 * i));
-    } else {
 #pragma unroll
-      for (int j = 0; j < NCPT; ++j) {
-        const int i = threadIdx.x + j * kThreads;
-        nwr[j] = i < K / 8 ? reinterpret_cast<const uint4*>(p.norm_w)[i] : make_uint4(0, 0, 0, 0);
-      }
+    for (int j = 0; j < NCPT; ++j) {
+      const int i = threadIdx.x + j * kThreads;
+      nwr[j] = i < K / 8 ? reinterpret_cast<const uint4*>(p.norm_w)[i] : make_uint4(0, 0, 0, 0);
     }
+  }
+  // int8: the per-row weight scales (constants) of the warp's first SROUNDS rounds, read before
+  // the wait, one per lane: lane (round * U + u) * RPU + r holds row (unit u, r) of that round.
+  // Read at the tail instead, each scale was a dependent load from HBM (the token's weight
+  // stream evicts it from L2) after the warp's last dot product.
+  constexpr int SPR = U * RPU, SROUNDS = 32 / SPR;
+  float wsc = 0.f;
+  if (INT8) {
+    const int rnd = lane / SPR, u = (lane % SPR) / RPU, r = lane % RPU;
+    const int grp = g0 + rnd * gstride, unit = grp * U + u;
+    if (rnd < SROUNDS && grp < ngroups && unit < n_out) wsc = p.w_scale[unit + (int64_t)r * n_out];
   }
   pdl_wait();
   pdl_launch_dependents();
@@ -365,7 +372,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_fast_kernel(GemvParams p) {
     }
   }
   if constexpr (INT8)
-    build_input_q8<PRO, K>(p, xq, &sx_s, red);
+    build_input_q8<PRO, K>(p, xq, &sx_s, red, nwr);
   else
     build_input_bf16<PRO, K>(p, xs, red, nwr);
   const float sx = INT8 ? sx_s : 1.0f;
@@ -415,7 +422,10 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_fast_kernel(GemvParams p) {
         if (INT8) {
           const int tot = warp_sum_i(acci[u][r]);
           const int64_t row = unit + (int64_t)r * n_out;
-          y[r] = ((float)tot * sx) * ((unit < n_out) ? p.w_scale[row] : 0.f);
+          const int rnd = it / SEG;  // warp-uniform
+          const float sc = rnd < SROUNDS ? __shfl_sync(0xffffffffu, wsc, (rnd * U + u) * RPU + r)
+                                         : ((unit < n_out) ? p.w_scale[row] : 0.f);
+          y[r] = ((float)tot * sx) * sc;
         } else {
           y[r] = warp_sum(accf[u][r]);
         }
