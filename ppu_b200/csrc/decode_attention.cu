@@ -531,6 +531,11 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_cluster_kernel(Decode
   asm volatile("cp.async.commit_group;" ::: "memory");
   // peers write into this CTA's shared memory later: all CTAs of the cluster must have started
   asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+  // RoPE angle and norm weights before the wait (the position counter is advanced at the end of
+  // the previous token; the weights are constants)
+  float c = 1.f, sn = 0.f;
+  if (d < p.rot) rope_cs(d, p.rot / 2, (float)(*p.rope_pos), p.inv_freq, c, sn);
+  const float wq = bf2f(p.qw[d]), wk = bf2f(p.kw[d]);
   pdl_wait();
   pdl_launch_dependents();
 
@@ -547,9 +552,6 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_cluster_kernel(Decode
     const float ws = warp_sum(x[i] * x[i]);
     if (lane == 0) red[warp][i] = ws;
   }
-  float c = 1.f, sn = 0.f;
-  if (d < p.rot) rope_cs(d, p.rot / 2, (float)(*p.rope_pos), p.inv_freq, c, sn);
-  const float wq = bf2f(p.qw[d]), wk = bf2f(p.kw[d]);
   __syncthreads();
 #pragma unroll
   for (int i = 0; i <= G; ++i) {

@@ -567,6 +567,15 @@ __global__ void __launch_bounds__(kThreads) lm_head_fast_kernel(LmParams p) {
     }
   };
   if (g < ngroups) load_group(g);
+  constexpr int NCPT = (K / 8 + kThreads - 1) / kThreads;
+  uint4 nwr[NCPT];  // final-norm weights: constants, in registers before the wait
+  if (NORM) {
+#pragma unroll
+    for (int j = 0; j < NCPT; ++j) {
+      const int i = threadIdx.x + j * kThreads;
+      nwr[j] = i < K / 8 ? reinterpret_cast<const uint4*>(p.norm_w)[i] : make_uint4(0, 0, 0, 0);
+    }
+  }
   pdl_wait();
   pdl_launch_dependents();
   {
@@ -575,9 +584,9 @@ __global__ void __launch_bounds__(kThreads) lm_head_fast_kernel(LmParams p) {
     gp.norm_w = p.norm_w;
     gp.eps = p.eps;
     if (NORM)
-      build_input<Q35_PRO_NORM, false>(gp, K, xs, nullptr, nullptr, red);
+      build_input_bf16<Q35_PRO_NORM, K>(gp, xs, red, nwr);
     else
-      build_input<Q35_PRO_PLAIN, false>(gp, K, xs, nullptr, nullptr, red);
+      build_input_bf16<Q35_PRO_PLAIN, K>(gp, xs, red, nwr);
   }
   float best_v = -FLT_MAX;
   int best_i = 0x7fffffff;
