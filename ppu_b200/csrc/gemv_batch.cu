@@ -74,9 +74,10 @@ Q35_DEV void build_input_slice(const BatchGemvParams& p, int k_full, int k0, bf1
   }
 }
 
-// Warp b builds request b's input row (bf16) in shared memory.
+// Warp b builds request b's input row (bf16) in shared memory. `nws`: the norm weights, already
+// in shared memory (copied before the PDL wait: they are constants).
 template <int K, int PRO>
-Q35_DEV void build_inputs(const BatchGemvParams& p, bf16* xs, int warp, int lane) {
+Q35_DEV void build_inputs(const BatchGemvParams& p, bf16* xs, const uint4* nws, int warp, int lane) {
   constexpr int CPL = K / 8 / 32;
   const int b = warp;
   uint4* dst = reinterpret_cast<uint4*>(xs + b * xs_stride<K>());
@@ -115,12 +116,17 @@ Q35_DEV void build_inputs(const BatchGemvParams& p, bf16* xs, int warp, int lane
   for (int c = 0; c < CPL; ++c) {
     float f[8], w[8];
     unpack_bf16x8(src[lane + 32 * c], f);
-    unpack_bf16x8(reinterpret_cast<const uint4*>(p.norm_w)[lane + 32 * c], w);
+    unpack_bf16x8(nws[lane + 32 * c], w);
     __align__(16) bf16 o[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) o[j] = f2bf(f[j] * r * (1.0f + w[j]));
     dst[lane + 32 * c] = *reinterpret_cast<const uint4*>(o);
   }
+}
+
+Q35_DEV void cp_async16(void* smem, const void* gmem) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(smem)), "l"(gmem)
+               : "memory");
 }
 
 Q35_DEV unsigned long long top1_key(float v, int idx) {
@@ -186,16 +192,44 @@ __global__ void __launch_bounds__(kThreads) gemv_batch_kernel(BatchGemvParams p)
     }
   };
   int grp = (int)blockIdx.x / KSPLIT;
+  const int grp0 = grp;
   if (grp < ngroups) {
     load(grp, 0, 0);
     if (NST > 1) load(grp, 1, NBUF - 1);
   }
+  // norm weights (constants) copied into shared memory before the wait: read after the sum of
+  // squares, they would be a dependent load from HBM (the step's weight stream evicts them)
+  constexpr bool kNormed = PRO == Q35_PRO_NORM || PRO == Q35_PRO_EMBED;
+  __shared__ __align__(16) uint4 nws[kNormed ? K / 8 : 1];
+  if constexpr (kNormed) {
+    for (int i = threadIdx.x; i < K / 8; i += kThreads) cp_async16(&nws[i], p.norm_w + 8 * i);
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  }
   pdl_wait();
   pdl_launch_dependents();
+  // residual epilogue: warp 0's values for its first group, read now (the producers are done) so
+  // that the epilogue's read-modify-write does not wait on L2 at the kernel's tail
+  float rp[2][2] = {{0.f, 0.f}, {0.f, 0.f}};  // [row h][request 2t + e]
+  if (EPI == Q35_EPI_RESIDUAL && warp == 0 && grp0 < ngroups) {
+    int64_t r0, r1;
+    bool ok0, ok1;
+    rows(grp0, r0, r1, ok0, ok1);
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int b = 2 * t + e;
+        if (b < p.n && (h ? ok1 : ok0)) rp[h][e] = bf2f(p.resid[(int64_t)b * n_out + (h ? r1 : r0)]);
+      }
+  }
+  if constexpr (kNormed) {
+    asm volatile("cp.async.wait_all;" ::: "memory");
+    __syncthreads();
+  }
   if constexpr (KSPLIT > 1)
     build_input_slice<KS>(p, K, kbase, xs, warp, lane);
   else
-    build_inputs<K, PRO>(p, xs, warp, lane);
+    build_inputs<K, PRO>(p, xs, nws, warp, lane);
   __syncthreads();
 
   unsigned long long best[2] = {0ull, 0ull};  // TOP1: this lane's best keys for requests 2t, 2t + 1
@@ -285,7 +319,7 @@ __global__ void __launch_bounds__(kThreads) gemv_batch_kernel(BatchGemvParams p)
             const int64_t o = (int64_t)b * n_out + (h ? r1 : r0);
             const float y = d[2 * h + e];
             if (EPI == Q35_EPI_RESIDUAL)
-              p.resid[o] = f2bf(bf2f(p.resid[o]) + rbf(y));
+              p.resid[o] = f2bf((grp == grp0 ? rp[h][e] : bf2f(p.resid[o])) + rbf(y));
             else
               p.out[o] = f2bf(y);
           }
