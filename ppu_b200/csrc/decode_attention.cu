@@ -547,6 +547,10 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_cluster_kernel(Decode
   for (int hh = 0; hh < G; ++hh) x[hh] = bf2f(row[(g * G + hh) * 2 * kD + d]);
   x[G] = bf2f(row[2 * Hq * kD + g * kD + d]);
   const float v_raw = bf2f(row[2 * Hq * kD + Hkv * kD + g * kD + d]);
+  // the output gate of this thread's first merge item (dims of this rank, below), loaded with the
+  // rest of the row: read after the cluster barrier it would be one more round trip to L2
+  constexpr int kDper = kD / kClusterCTAs;
+  const float gate0 = t < G * kDper ? bf2f(row[(g * G + t / kDper) * 2 * kD + kD + rank * kDper + t % kDper]) : 0.f;
 #pragma unroll
   for (int i = 0; i <= G; ++i) {
     const float ws = warp_sum(x[i] * x[i]);
@@ -681,7 +685,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_cluster_kernel(Decode
     }
     const float o = L > 0.f ? rbf(A / L) : 0.f;
     const int h = g * G + hh;
-    const float gate = bf2f(row[h * 2 * kD + kD + dd]);
+    const float gate = i == t ? gate0 : bf2f(row[h * 2 * kD + kD + dd]);
     p.out[((int64_t)b * Hq + h) * kD + dd] = f2bf(o * rbf(sigmoid_f(gate)));
   }
 }

@@ -318,8 +318,16 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kDecThreads)
   pdl_launch_dependents();
 
   const bf16* row = p.packed + (int64_t)b * p.packed_stride;
+  // packed row layout (integration.py:81-93): [q | k | v] (3*H*D) | z (H*D) | a (H) | b (H).
+  // Every value this thread needs from the row is loaded here, at once: a load after one of the
+  // barriers below would be one more dependent round trip to L2.
+  const int z_off = 3 * H * kD, a_off = 4 * H * kD, b_off = 4 * H * kD + H;
+  const bf16 a_raw = row[a_off + h], b_raw = row[b_off + h];
+  const bf16 z_raw = warp == 0 ? row[z_off + h * kD + v0 + lane] : bf16();
+  const bf16 xq_raw = row[cqk];
+  const bf16 xv_raw = t < kVS ? row[cv] : bf16();
   // ---- causal conv update + SiLU (kernels.py:622-656), rounded to BF16 (conv output dtype)
-  const float xq = bf2f(row[cqk]);
+  const float xq = bf2f(xq_raw);
   float acc = sq[1] * wq[0];
   acc += sq[2] * wq[1];
   acc += sq[3] * wq[2];
@@ -327,7 +335,7 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kDecThreads)
   const float cqk_out = rbf(silu_f(rbf(acc)));
   float xv = 0.f;
   if (t < kVS) {
-    xv = bf2f(row[cv]);
+    xv = bf2f(xv_raw);
     float av = sv[1] * wv[0];
     av += sv[2] * wv[1];
     av += sv[3] * wv[2];
@@ -350,9 +358,7 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kDecThreads)
       khat[t - kD] = cqk_out * inv;
   }
   float alpha, beta;
-  // packed row layout (integration.py:81-93): [q | k | v] (3*H*D) | z (H*D) | a (H) | b (H)
-  const int z_off = 3 * H * kD, a_off = 4 * H * kD, b_off = 4 * H * kD + H;
-  delta_gates(bf2f(row[a_off + h]), bf2f(row[b_off + h]), a_log, dt_bias, alpha, beta);
+  delta_gates(bf2f(a_raw), bf2f(b_raw), a_log, dt_bias, alpha, beta);
   __syncthreads();
 
   // ---- state update: s = alpha*s; mem = s^T k; d = beta (v - mem); s += k d^T; o = s^T q
@@ -397,19 +403,19 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kDecThreads)
     stq[0] = f2bf(sq[1]);
     stq[1] = f2bf(sq[2]);
     stq[2] = f2bf(sq[3]);
-    stq[3] = row[cqk];
+    stq[3] = xq_raw;
   }
   if (t < kVS) {
     stv[0] = f2bf(sv[1]);
     stv[1] = f2bf(sv[2]);
     stv[2] = f2bf(sv[3]);
-    stv[3] = row[cv];
+    stv[3] = xv_raw;
   }
   if (warp == 0) {
     const float rstd = rsqrt_ieee(tot / (float)kD + p.eps);
     const float nrm = rbf(o * rstd);
     const float wt = rbf(nrm * gw);
-    const float z = bf2f(row[z_off + h * kD + v0 + lane]);
+    const float z = bf2f(z_raw);
     p.out[(int64_t)b * H * kD + h * kD + v0 + lane] = f2bf(wt * silu_f(z));
   }
   cluster.sync();  // keep this CTA's shared memory alive until the peers have read cl_part
