@@ -507,7 +507,23 @@ Q35_DEV unsigned long long top1_key(float v, int idx) {
   return ((unsigned long long)float_order_key(v) << 32) | (unsigned long long)(0xFFFFFFFFu - (uint32_t)idx);
 }
 
-Q35_DEV void lm_finish(const LmParams& p, float best_v, int best_i, float* red_v, int* red_i) {
+// The step counters the finish advances, read by thread 0 before the PDL wait: only the previous
+// step's finish (or the host, before the step) writes them, so the finish stores instead of three
+// dependent read-modify-writes at the step's tail.
+struct LmCounters {
+  int64_t len = 0, pos = 0, log_pos = 0;
+};
+Q35_DEV LmCounters lm_counters_preload(const LmParams& p) {
+  LmCounters c;
+  if (threadIdx.x == 0) {
+    if (p.adv.cache_len) c.len = *p.adv.cache_len;
+    if (p.adv.rope_pos) c.pos = *p.adv.rope_pos;
+    if (p.adv.token_log && p.adv.log_pos && p.adv.log_len > 0) c.log_pos = *p.adv.log_pos;
+  }
+  return c;
+}
+
+Q35_DEV void lm_finish(const LmParams& p, float best_v, int best_i, float* red_v, int* red_i, const LmCounters& pre) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (lane == 0) {
     red_v[warp] = best_v;
@@ -531,12 +547,11 @@ Q35_DEV void lm_finish(const LmParams& p, float best_v, int best_i, float* red_v
       atomicExch(&p.ws->count, 0u);
       const int64_t tok = (key == 0ull) ? 0 : (int64_t)(0xFFFFFFFFu - (uint32_t)(key & 0xFFFFFFFFull));
       p.token_out[0] = tok;
-      if (p.adv.cache_len) *p.adv.cache_len += 1;
-      if (p.adv.rope_pos) *p.adv.rope_pos += 1;
+      if (p.adv.cache_len) *p.adv.cache_len = pre.len + 1;
+      if (p.adv.rope_pos) *p.adv.rope_pos = pre.pos + 1;
       if (p.adv.token_log && p.adv.log_pos && p.adv.log_len > 0) {
-        const int64_t pos = *p.adv.log_pos;
-        p.adv.token_log[pos % p.adv.log_len] = tok;
-        *p.adv.log_pos = pos + 1;
+        p.adv.token_log[pre.log_pos % p.adv.log_len] = tok;
+        *p.adv.log_pos = pre.log_pos + 1;
       }
     }
   }
@@ -567,6 +582,7 @@ __global__ void __launch_bounds__(kThreads) lm_head_fast_kernel(LmParams p) {
     }
   };
   if (g < ngroups) load_group(g);
+  const LmCounters pre = lm_counters_preload(p);
   constexpr int NCPT = (K / 8 + kThreads - 1) / kThreads;
   uint4 nwr[NCPT];  // final-norm weights: constants, in registers before the wait
   if (NORM) {
@@ -612,7 +628,7 @@ __global__ void __launch_bounds__(kThreads) lm_head_fast_kernel(LmParams p) {
       }
     }
   }
-  lm_finish(p, best_v, best_i, red_v, red_i);
+  lm_finish(p, best_v, best_i, red_v, red_i, pre);
 }
 
 template <bool NORM>
@@ -623,6 +639,7 @@ __global__ void __launch_bounds__(kThreads) lm_head_any_kernel(LmParams p) {
   __shared__ int red_i[kWarps];
   bf16* xs = reinterpret_cast<bf16*>(smem_raw);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const LmCounters pre = lm_counters_preload(p);
   pdl_wait();
   pdl_launch_dependents();
   {
@@ -648,7 +665,7 @@ __global__ void __launch_bounds__(kThreads) lm_head_any_kernel(LmParams p) {
       best_i = row;
     }
   }
-  lm_finish(p, best_v, best_i, red_v, red_i);
+  lm_finish(p, best_v, best_i, red_v, red_i, pre);
 }
 
 // ---------------------------------------------------------------------------------------------

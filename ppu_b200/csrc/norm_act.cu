@@ -53,9 +53,11 @@ __global__ void __launch_bounds__(kRowThreads) rms_rows2048_kernel(const bf16* _
                                                                    const bf16* __restrict__ w,
                                                                    bf16* __restrict__ resid_out,
                                                                    bf16* __restrict__ out, float eps) {
+  constexpr int kW = 2048;
+  // the norm weights are constants: loaded before the wait, not after the block reduction
+  const uint4 wraw = *reinterpret_cast<const uint4*>(w + 8 * threadIdx.x);
   pdl_wait();  // programmatic dependent launch: inputs only after the previous kernel
   pdl_launch_dependents();
-  constexpr int kW = 2048;
   __shared__ float red[kRowThreads / 32];
   const int64_t base = (int64_t)blockIdx.x * kW + 8 * threadIdx.x;
   float f[8];
@@ -76,7 +78,7 @@ __global__ void __launch_bounds__(kRowThreads) rms_rows2048_kernel(const bf16* _
   for (int j = 0; j < 8; ++j) ss += f[j] * f[j];
   const float r = rsqrt_ieee(block_sum<kRowThreads / 32>(ss, red) / (float)kW + eps);
   float wv[8];
-  unpack_bf16x8(*reinterpret_cast<const uint4*>(w + 8 * threadIdx.x), wv);
+  unpack_bf16x8(wraw, wv);
   __align__(16) bf16 o[8];
 #pragma unroll
   for (int j = 0; j < 8; ++j) o[j] = f2bf(f[j] * r * (1.0f + wv[j]));
