@@ -283,7 +283,7 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kDecThreads)
   __shared__ float vconv[kVS];
   __shared__ float red1[kDecThreads / 32][kVS], red2[kDecThreads / 32][kVS];
   __shared__ float nred[kDecThreads / 32];
-  __shared__ float cl_part;
+  __shared__ float cl_parts[kCluster];  // the gated norm's partial sums, pushed by every CTA
   cg::cluster_group cluster = cg::this_cluster();
   const int rank = (int)cluster.block_rank();
   const int bh = blockIdx.x / kCluster;
@@ -313,6 +313,8 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kDecThreads)
   }
   const float a_log = bf2f(p.a_log[h]), dt_bias = bf2f(p.dt_bias[h]);
   const float gw = bf2f(p.norm_w[v0 + lane]);
+  // the peers write into this CTA's shared memory later: all CTAs of the cluster must have started
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
 
   pdl_wait();
   pdl_launch_dependents();
@@ -389,15 +391,18 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kDecThreads)
   for (int w = 0; w < kDecThreads / 32; ++w) o += red2[w][lane];
   o = rbf(o);  // the recurrent output is materialised in BF16 (kernels.py:849, 884)
 
-  // ---- gated RMSNorm over the head's 128 values: partial sums exchanged across the cluster
+  // ---- gated RMSNorm over the head's 128 values: each CTA pushes its partial sum into slot
+  // `rank` of every CTA of the cluster, and after one cluster barrier reads only its own shared
+  // memory (so no second barrier has to keep it alive for the peers' reads)
+  asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
   if (warp == 0) {
     const float ps = warp_sum(o * o);
-    if (lane == 0) cl_part = ps;
+    if (lane < kCluster) *cluster.map_shared_rank(&cl_parts[rank], lane) = ps;
   }
   cluster.sync();
   float tot = 0.f;
 #pragma unroll
-  for (int r = 0; r < kCluster; ++r) tot += *cluster.map_shared_rank(&cl_part, r);
+  for (int r = 0; r < kCluster; ++r) tot += cl_parts[r];
   // conv state writes: every CTA of the cluster has read the old state before cluster.sync()
   if ((t < kD ? t : t - kD) / kVS == rank) {
     stq[0] = f2bf(sq[1]);
@@ -418,7 +423,6 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kDecThreads)
     const float z = bf2f(z_raw);
     p.out[(int64_t)b * H * kD + h * kD + v0 + lane] = f2bf(wt * silu_f(z));
   }
-  cluster.sync();  // keep this CTA's shared memory alive until the peers have read cl_part
   (void)xv;
 }
 
