@@ -35,7 +35,8 @@ int q35_attn_decode_launch(const void* packed, const void* q_weight, const void*
                            int64_t max_len, float eps, void* workspace, cudaStream_t stream, bool pdl);
 int q35_delta_decode_launch(const void* packed, const void* conv_weight, void* conv_state, const void* a_log,
                             const void* dt_bias, const void* norm_weight, float* state, void* out, int64_t batch,
-                            int64_t heads, int64_t packed_stride, float eps, cudaStream_t stream, bool pdl);
+                            int64_t heads, int64_t packed_stride, float eps, cudaStream_t stream, bool pdl,
+                            bool qk_regs);
 int q35_gemm_launch(const void* a, const void* w, void* out, int64_t m, int64_t n, int64_t k, int epi, bool int8,
                     const float* sx, const float* sw, cudaStream_t s, bool pdl);
 int q35_gemm_tc_launch(const void* a, const void* w, void* out, int64_t m, int64_t n, int64_t k, int epi, bool int8,
@@ -311,7 +312,7 @@ static int decode_layers(q35_decoder* dec, cudaStream_t s) {
     // mixer
     if (delta) {
       Q35_TRY(q35_delta_decode_launch(B.mix_in_out, L.conv_w, L.conv_state, L.a_log, L.dt_bias, L.gnorm,
-                                      L.rec_state, B.mix_out, nb, d.lin_heads, d.delta_rows, d.eps, s, pdl));
+                                      L.rec_state, B.mix_out, nb, d.lin_heads, d.delta_rows, d.eps, s, pdl, q8));
     } else {
       Q35_TRY(q35_attn_decode_launch(B.mix_in_out, L.q_norm, L.k_norm, d.inv_freq, L.k_cache, L.v_cache,
                                      d.cache_len, d.rope_pos, B.mix_out, nb, d.q_heads, d.kv_heads, d.rotary_dim,
