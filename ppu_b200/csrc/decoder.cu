@@ -26,7 +26,7 @@ int q35_lm_head_batch_launch(const void* hidden, int64_t batch, const void* norm
 extern "C" size_t q35_lm_shard_workspace_size(void);
 int q35_lm_head_launch(const void* hidden, const void* norm_weight, const void* weight, int64_t* token_out,
                        int64_t vocab, int64_t k, float eps, void* ws, cudaStream_t s, bool pdl,
-                       const q35_step_counters* adv);
+                       const q35_step_counters* adv, bool ring);
 int q35_lm_keys_finish_launch(const int64_t* keys, int64_t n, int64_t* tokens, cudaStream_t s, bool pdl,
                               const q35_step_counters* adv);
 int q35_attn_decode_launch(const void* packed, const void* q_weight, const void* k_weight, const float* inv_freq,
@@ -374,7 +374,7 @@ extern "C" int q35_decoder_decode_step(q35_decoder* dec, void* stream) {
     return q35_lm_keys_finish_launch(dec->buf.lm_keys, d.batch, d.token, s, false, &adv);
   }
   return q35_lm_head_launch(dec->buf.resid, d.final_norm, d.embed, d.token, d.vocab, d.hidden, d.eps, dec->buf.lm_ws,
-                            s, d.use_pdl != 0, &adv);
+                            s, d.use_pdl != 0, &adv, d.a8w8 == 0);
 }
 
 extern "C" int q35_decoder_decode_layers(q35_decoder* dec, void* stream) {
@@ -578,7 +578,7 @@ static int prefill_impl(q35_decoder* dec, const int64_t* ids, int64_t length, co
   }
   if (nseq == 1) {
     Q35_TRY(q35_lm_head_launch(B.p_resid + (Lt - 1) * H, d.final_norm, d.embed, token_out, d.vocab, H, d.eps,
-                               B.lm_ws, s, pdl, nullptr));
+                               B.lm_ws, s, pdl, nullptr, d.a8w8 == 0));
   } else {  // each sequence's last row -> the decode rows, one pass over the tied table for all
     if (cudaMemcpy2DAsync(B.resid, (size_t)H * sizeof(bf16), B.p_resid + (Lt - 1) * H, (size_t)(Lt * H) * sizeof(bf16),
                           (size_t)H * sizeof(bf16), (size_t)nseq, cudaMemcpyDeviceToDevice, s) != cudaSuccess)
